@@ -1,0 +1,76 @@
+"""Loads libheliocuda.so (built in-tree) and declares its C ABI for ctypes.
+
+There is no CPU fallback: if the library or a CUDA device is missing, the
+calls raise.  The declarations mirror include/heliocuda.h one for one.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import re
+from pathlib import Path
+
+PKG = Path(__file__).resolve().parent
+LIB_PATH = PKG / "libheliocuda.so"
+HEADERS = sorted((PKG.parent / "include").glob("*.h"))
+
+_sz = C.c_size_t
+_vp = C.c_void_p
+_i = C.c_int
+
+# name -> (restype, argtypes)
+SIGNATURES = {
+    "hpc_last_error": (C.c_char_p, []),
+    "hpc_version": (_i, []),
+    "hpc_device_init": (_i, [_i]),
+    "hpc_device_error": (_i, []),
+    "hpc_weight_upload": (_i, [_i, _vp, _sz, _sz, _sz, C.POINTER(_vp)]),
+    "hpc_weight_upload_device": (_i, [_i, _vp, _sz, _sz, _sz, _vp, C.POINTER(_vp)]),
+    "hpc_weight_release": (_i, [_vp]),
+    "hpc_weight_info": (_i, [_vp, C.POINTER(_i), C.POINTER(_sz), C.POINTER(_sz), C.POINTER(_sz)]),
+    "hpc_weight_dequantize": (_i, [_vp, _vp, _sz, _vp]),
+    "hpc_quantize_q8_k": (_i, [_vp, _sz, _sz, _sz, _vp, _vp, _vp, _vp]),
+    "hpc_matmul_quantized_prepared_f32": (_i, [_vp, _vp, _sz, _sz, _sz, _sz, _vp, _sz, _vp]),
+    "hpc_matmul_quantized_prepared_multi_f32": (_i, [_sz, _vp, _sz, _sz, _sz, C.POINTER(_vp), C.POINTER(_vp),
+                                                     C.POINTER(_sz), _vp]),
+    "hpc_matmul_quantized_f32": (_i, [_i, _vp, _sz, _vp, _sz, _sz, _sz, _sz, _vp, _sz]),
+    "hpc_q8_workspace_bytes": (_i, [_sz, _sz, C.POINTER(_sz)]),
+    "hpc_q8_quantize": (_i, [_vp, _sz, _sz, _sz, _vp, _sz, _vp]),
+    "hpc_matmul_q8": (_i, [_sz, C.POINTER(_vp), _vp, _sz, _sz, _sz, C.POINTER(_vp), C.POINTER(_sz), _vp]),
+    "hpc_lm_head_topk": (_i, [_vp, _vp, _sz, _sz, _sz, _sz, C.c_int32, C.c_float, _vp, _vp, _vp]),
+    "hpc_lm_head_candidates_bytes": (_i, [_vp, _sz, _sz, C.POINTER(_sz)]),
+    "hpc_lm_head_topk_q8": (_i, [_vp, _vp, _sz, _sz, _sz, _sz, C.c_int32, _vp, _sz, C.c_float, _vp, _vp, _vp, _vp]),
+    "hpc_topk_merge_keys": (_i, [_vp, _sz, _sz, _sz, C.c_float, _vp, _vp, _vp]),
+}
+
+_lib = None
+
+
+class LibraryMissing(RuntimeError):
+    pass
+
+
+def header_symbols() -> list[str]:
+    """Every function the public headers declare."""
+    names = []
+    for h in HEADERS:
+        text = re.sub(r"/\*.*?\*/", "", h.read_text(), flags=re.S)
+        names += re.findall(r"\b(hpc_[a-z0-9_]+)\s*\(", text)
+    return sorted(set(names))
+
+
+def lib() -> C.CDLL:
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise LibraryMissing(f"{LIB_PATH} is not built; run `python -m heliopause_b200.build`")
+        L = C.CDLL(str(LIB_PATH))
+        for name, (res, args) in SIGNATURES.items():
+            f = getattr(L, name)
+            f.restype = res
+            f.argtypes = args
+        _lib = L
+    return _lib
+
+
+def last_error() -> str:
+    return lib().hpc_last_error().decode(errors="replace")

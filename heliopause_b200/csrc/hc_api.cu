@@ -1,0 +1,515 @@
+// hc_api.cu -- the C ABI declared in include/heliocuda.h.
+//
+// Validation order and status codes follow the WASM drivers they replace
+// (packages/engine/wasm-kernels/src/lib.rs:41-426): the input/output length
+// check comes first (ERR_SHAPE), then the type/row-size check (ERR_TYPE),
+// then the weight length (ERR_SHAPE).  A resident handle carries its own
+// shape, so "weight length" becomes "handle shape equals (input_size,
+// row_count)".
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/heliocuda.h"
+#include "hc_common.cuh"
+#include "hc_kernels.cuh"
+#include "hc_lmhead.cuh"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+constexpr uint32_t kWeightMagic = 0x48504357u;  // "HPCW"
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(HPC_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+#define HPC_CK(call, what)                       \
+  do {                                           \
+    cudaError_t e_ = (call);                     \
+    if (e_ != cudaSuccess) return cuda_fail(e_, what); \
+  } while (0)
+
+bool supported_type(int t) { return t == HPC_TYPE_Q4_K || t == HPC_TYPE_Q6_K; }
+
+// lib.rs:1551-1561 quantized_row_bytes for every reference type id.
+bool row_bytes(int type, size_t k, size_t* out) {
+  switch (type) {
+    case HPC_TYPE_Q4_K: if (k % 256) return false; *out = k / 256 * 144; return true;
+    case HPC_TYPE_Q5_K: if (k % 256) return false; *out = k / 256 * 176; return true;
+    case HPC_TYPE_Q6_K: if (k % 256) return false; *out = k / 256 * 210; return true;
+    case HPC_TYPE_IQ4_XS: if (k % 256) return false; *out = k / 256 * 136; return true;
+    case HPC_TYPE_Q8_0: if (k % 32) return false; *out = k / 32 * 34; return true;
+    case HPC_TYPE_Q4_0: if (k % 32) return false; *out = k / 32 * 18; return true;
+    default: return false;
+  }
+}
+
+bool mul_overflows(size_t a, size_t b, size_t* out) {
+  if (a != 0 && b > SIZE_MAX / a) return true;
+  *out = a * b;
+  return false;
+}
+
+}  // namespace
+
+struct hpc_weight_s {
+  uint32_t magic;
+  int type;
+  int device;
+  size_t input_size;
+  size_t row_count;
+  size_t rows_pad;
+  int nb;
+  uint8_t* d_data;
+  size_t bytes;
+};
+
+static bool valid(const hpc_weight_s* h) { return h && h->magic == kWeightMagic && h->d_data; }
+
+// One status word per device for bounded-wait timeouts inside kernels.
+static __device__ int g_status_word;
+
+namespace hc {
+int* device_status_word() {
+  static std::mutex mu;
+  static int* ptrs[64] = {nullptr};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!ptrs[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_status_word) == cudaSuccess) ptrs[dev] = static_cast<int*>(p);
+  }
+  return ptrs[dev];
+}
+}  // namespace hc
+
+extern "C" {
+
+const char* hpc_last_error(void) { return g_last_error.c_str(); }
+
+int hpc_version(void) { return (1 << 16) | 0; }
+
+int hpc_device_error(void) {
+  int* w = hc::device_status_word();
+  if (!w) return fail(HPC_ERR_CUDA, "no device status word");
+  int v = 0;
+  HPC_CK(cudaMemcpy(&v, w, sizeof v, cudaMemcpyDeviceToHost), "read device status");
+  if (v == 0) return HPC_OK;
+  const int zero = 0;
+  HPC_CK(cudaMemcpy(w, &zero, sizeof zero, cudaMemcpyHostToDevice), "clear device status");
+  return fail(HPC_ERR_TIMEOUT, "a kernel wait timed out on the device (code %d)", v);
+}
+
+int hpc_device_init(int device) {
+  int n = 0;
+  HPC_CK(cudaGetDeviceCount(&n), "cudaGetDeviceCount");
+  if (device < 0 || device >= n) return fail(HPC_ERR_ARG, "device %d out of range (%d devices)", device, n);
+  HPC_CK(cudaSetDevice(device), "cudaSetDevice");
+  cudaDeviceProp prop;
+  HPC_CK(cudaGetDeviceProperties(&prop, device), "cudaGetDeviceProperties");
+  if (prop.major != 10) return fail(HPC_ERR_CUDA, "device %d is sm_%d%d; this library is built for sm_100a", device,
+                                    prop.major, prop.minor);
+  return HPC_OK;
+}
+
+static int upload_common(int type_id, const void* src, bool src_on_device, size_t byte_len, size_t input_size,
+                         size_t row_count, cudaStream_t stream, hpc_weight* out_handle) {
+  if (!out_handle) return fail(HPC_ERR_ARG, "null out_handle");
+  *out_handle = nullptr;
+  size_t rb;
+  if (!row_bytes(type_id, input_size, &rb)) return fail(HPC_ERR_TYPE, "weight upload: unsupported type %d / input size %zu", type_id, input_size);
+  if (!supported_type(type_id)) return fail(HPC_ERR_TYPE, "weight upload: type %d is not resident on the GPU (Q4_K and Q6_K only)", type_id);
+  size_t want;
+  if (input_size == 0 || row_count == 0 || mul_overflows(rb, row_count, &want) || byte_len != want)
+    return fail(HPC_ERR_SHAPE, "weight upload shape mismatch: %zu bytes for %zu rows of %zu", byte_len, row_count, input_size);
+  if (!src) return fail(HPC_ERR_ARG, "null weight bytes");
+  if (row_count > (size_t(1) << 30) || input_size > (size_t(1) << 24))
+    return fail(HPC_ERR_SHAPE, "weight upload: shape too large");
+  int dev = 0;
+  HPC_CK(cudaGetDevice(&dev), "cudaGetDevice");
+  const int nb = int(input_size / 256);
+  const size_t rows_pad = (row_count + hc::TILE - 1) / hc::TILE * hc::TILE;
+  const size_t bytes = rows_pad / hc::TILE * size_t(nb) * hc::tile_block_bytes(type_id);
+  uint8_t* d_data = nullptr;
+  uint8_t* d_raw = nullptr;
+  HPC_CK(cudaMalloc(&d_data, bytes), "cudaMalloc(weight)");
+  const uint8_t* raw = static_cast<const uint8_t*>(src);
+  cudaError_t e = cudaSuccess;
+  if (!src_on_device) {
+    e = cudaMalloc(&d_raw, byte_len);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(d_raw, src, byte_len, cudaMemcpyHostToDevice, stream);
+    raw = d_raw;
+  }
+  if (e == cudaSuccess) e = hc::launch_repack(type_id, raw, d_data, int(row_count), int(rows_pad), nb, stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+  if (d_raw) cudaFree(d_raw);
+  if (e != cudaSuccess) {
+    cudaFree(d_data);
+    return cuda_fail(e, "weight upload/repack");
+  }
+  auto* h = new hpc_weight_s;
+  h->magic = kWeightMagic;
+  h->type = type_id;
+  h->device = dev;
+  h->input_size = input_size;
+  h->row_count = row_count;
+  h->rows_pad = rows_pad;
+  h->nb = nb;
+  h->d_data = d_data;
+  h->bytes = bytes;
+  *out_handle = h;
+  return HPC_OK;
+}
+
+int hpc_weight_upload(int type_id, const uint8_t* host_bytes, size_t byte_len, size_t input_size, size_t row_count,
+                      hpc_weight* out_handle) {
+  return upload_common(type_id, host_bytes, false, byte_len, input_size, row_count, 0, out_handle);
+}
+
+int hpc_weight_upload_device(int type_id, const void* d_bytes, size_t byte_len, size_t input_size, size_t row_count,
+                             void* stream, hpc_weight* out_handle) {
+  return upload_common(type_id, d_bytes, true, byte_len, input_size, row_count, static_cast<cudaStream_t>(stream),
+                       out_handle);
+}
+
+int hpc_weight_release(hpc_weight h) {
+  if (!valid(h)) return fail(HPC_ERR_ARG, "invalid weight handle");
+  cudaError_t e = cudaFree(h->d_data);
+  h->magic = 0;
+  h->d_data = nullptr;
+  delete h;
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFree(weight)");
+  return HPC_OK;
+}
+
+int hpc_weight_info(hpc_weight h, int* type_id, size_t* input_size, size_t* row_count, size_t* device_bytes) {
+  if (!valid(h)) return fail(HPC_ERR_ARG, "invalid weight handle");
+  if (type_id) *type_id = h->type;
+  if (input_size) *input_size = h->input_size;
+  if (row_count) *row_count = h->row_count;
+  if (device_bytes) *device_bytes = h->bytes;
+  return HPC_OK;
+}
+
+int hpc_weight_dequantize(hpc_weight h, float* d_out, size_t out_len, void* stream) {
+  if (!valid(h)) return fail(HPC_ERR_ARG, "invalid weight handle");
+  if (out_len != h->input_size * h->row_count) return fail(HPC_ERR_SHAPE, "dequantize output length %zu", out_len);
+  if (!d_out) return fail(HPC_ERR_ARG, "null output");
+  HPC_CK(hc::launch_dequant(h->type, h->d_data, d_out, int(h->row_count), h->nb, static_cast<cudaStream_t>(stream)),
+         "dequantize launch");
+  return HPC_OK;
+}
+
+int hpc_quantize_q8_k(const float* d_in, size_t in_len, size_t input_size, size_t column_count, float* d_d,
+                      int8_t* d_qs, int16_t* d_bsums, void* stream) {
+  if (input_size == 0 || input_size % 256 || in_len != input_size * column_count)
+    return fail(HPC_ERR_SHAPE, "quantize_q8_k shape mismatch");
+  if (column_count == 0) return HPC_OK;
+  if (!d_in || !d_d || !d_qs || !d_bsums) return fail(HPC_ERR_ARG, "null pointer");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int K = int(input_size), cols = int(column_count);
+  void* ws = nullptr;
+  HPC_CK(cudaMallocAsync(&ws, hc::q8buf_bytes(K, cols), st), "cudaMallocAsync(q8)");
+  hc::Q8Buf q = hc::q8buf_carve(ws, K, cols);
+  cudaError_t e = hc::launch_q8k_quantize(d_in, K, cols, q, d_qs, d_bsums, d_d, st);
+  cudaFreeAsync(ws, st);
+  if (e != cudaSuccess) return cuda_fail(e, "quantize_q8_k launch");
+  return HPC_OK;
+}
+
+// GEMV launches over an already-quantized workspace: one launch per group of
+// up to 8 columns, covering all segments.
+static int launch_gemv_ws(const hc::Q8Buf& q, int K, int cols, const hc::GemvSeg* segs, int nseg, int total_tiles,
+                          cudaStream_t st) {
+  hc::GemvParams p;
+  memset(&p, 0, sizeof p);
+  for (int i = 0; i < nseg; ++i) p.seg[i] = segs[i];
+  p.nseg = nseg;
+  p.K = K;
+  p.nb = K / 256;
+  p.total_tiles = total_tiles;
+  hc::gemv_plan(p);
+  p.q = q;
+  for (int c0 = 0; c0 < cols; c0 += 8) {
+    p.col0 = c0;
+    p.ncols = cols - c0 < 8 ? cols - c0 : 8;
+    HPC_CK(hc::launch_gemv(p, st), "gemv launch");
+  }
+  return HPC_OK;
+}
+
+// Shared by the single and multi entry points: quantize once into a
+// stream-ordered scratch allocation, then the GEMV launches.
+static int run_gemv(const float* d_in, int K, int cols, const hc::GemvSeg* segs, int nseg, int total_tiles,
+                    cudaStream_t st) {
+  if (cols == 0) return HPC_OK;
+  void* ws = nullptr;
+  HPC_CK(cudaMallocAsync(&ws, hc::q8buf_bytes(K, cols), st), "cudaMallocAsync(q8)");
+  hc::Q8Buf q = hc::q8buf_carve(ws, K, cols);
+  cudaError_t e = hc::launch_q8k_quantize(d_in, K, cols, q, nullptr, nullptr, nullptr, st);
+  int rc = e == cudaSuccess ? launch_gemv_ws(q, K, cols, segs, nseg, total_tiles, st) : cuda_fail(e, "quantize launch");
+  cudaError_t e2 = cudaFreeAsync(ws, st);
+  if (rc != HPC_OK) return rc;
+  if (e2 != cudaSuccess) return cuda_fail(e2, "cudaFreeAsync(q8)");
+  return HPC_OK;
+}
+
+// Validates `count` handles against (input_size, column_count) and fills the
+// segment table; returns the total tile count through *tiles.
+static int build_segments(size_t count, const hpc_weight* handles, float* const* d_outs, const size_t* out_lens,
+                          size_t input_size, size_t column_count, hc::GemvSeg* segs, int* tiles_out) {
+  int dev = 0;
+  HPC_CK(cudaGetDevice(&dev), "cudaGetDevice");
+  int tiles = 0;
+  for (size_t i = 0; i < count; ++i) {
+    const hpc_weight h = handles[i];
+    if (!valid(h)) return fail(HPC_ERR_ARG, "invalid weight handle %zu", i);
+    size_t rb;
+    if (!row_bytes(h->type, input_size, &rb)) return fail(HPC_ERR_TYPE, "unsupported type %d", h->type);
+    if (h->input_size != input_size || out_lens[i] != h->row_count * column_count)
+      return fail(HPC_ERR_SHAPE, "matmul: spec %zu shape mismatch", i);
+    if (h->device != dev) return fail(HPC_ERR_ARG, "handle %zu lives on device %d, current device is %d", i, h->device, dev);
+    if (column_count > 0 && !d_outs[i]) return fail(HPC_ERR_ARG, "null output %zu", i);
+    segs[i].w = h->d_data;
+    segs[i].out = d_outs[i];
+    segs[i].type = h->type;
+    segs[i].rows = int(h->row_count);
+    segs[i].tile_begin = tiles;
+    segs[i].pad = 0;
+    tiles += int(h->rows_pad / hc::TILE);
+  }
+  *tiles_out = tiles;
+  return HPC_OK;
+}
+
+int hpc_matmul_quantized_prepared_f32(hpc_weight h, const float* d_in, size_t in_len, size_t input_size,
+                                      size_t row_count, size_t column_count, float* d_out, size_t out_len,
+                                      void* stream) {
+  if (in_len != input_size * column_count || out_len != row_count * column_count)
+    return fail(HPC_ERR_SHAPE, "matmul shape mismatch: input %zu output %zu", in_len, out_len);
+  if (!valid(h)) return fail(HPC_ERR_ARG, "invalid weight handle");
+  size_t rb;
+  if (!row_bytes(h->type, input_size, &rb)) return fail(HPC_ERR_TYPE, "unsupported type %d for input size %zu", h->type, input_size);
+  if (h->input_size != input_size || h->row_count != row_count)
+    return fail(HPC_ERR_SHAPE, "handle shape mismatch: %zux%zu vs %zux%zu", h->input_size, h->row_count, input_size, row_count);
+  if (column_count > 0 && (!d_in || !d_out)) return fail(HPC_ERR_ARG, "null pointer");
+  if (column_count > (size_t(1) << 20)) return fail(HPC_ERR_SHAPE, "too many columns");
+  hc::GemvSeg s;
+  int tiles = 0;
+  int rc = build_segments(1, &h, &d_out, &out_len, input_size, column_count, &s, &tiles);
+  if (rc != HPC_OK) return rc;
+  return run_gemv(d_in, int(input_size), int(column_count), &s, 1, tiles, static_cast<cudaStream_t>(stream));
+}
+
+int hpc_matmul_quantized_prepared_multi_f32(size_t count, const float* d_in, size_t in_len, size_t input_size,
+                                            size_t column_count, const hpc_weight* handles, float* const* d_outs,
+                                            const size_t* out_lens, void* stream) {
+  if (count == 0 || count > size_t(hc::GEMV_MAXSEG) || in_len != input_size * column_count)
+    return fail(HPC_ERR_SHAPE, "multi matmul: count %zu / input length %zu", count, in_len);
+  if (!handles || !d_outs || !out_lens) return fail(HPC_ERR_ARG, "null pointer");
+  if (column_count > (size_t(1) << 20)) return fail(HPC_ERR_SHAPE, "too many columns");
+  hc::GemvSeg segs[hc::GEMV_MAXSEG];
+  int tiles = 0;
+  int rc = build_segments(count, handles, d_outs, out_lens, input_size, column_count, segs, &tiles);
+  if (rc != HPC_OK) return rc;
+  if (column_count > 0 && !d_in) return fail(HPC_ERR_ARG, "null input");
+  return run_gemv(d_in, int(input_size), int(column_count), segs, int(count), tiles, static_cast<cudaStream_t>(stream));
+}
+
+int hpc_matmul_quantized_f32(int type_id, const uint8_t* host_weight, size_t weight_len, const float* host_in,
+                             size_t in_len, size_t input_size, size_t row_count, size_t column_count, float* host_out,
+                             size_t out_len) {
+  if (in_len != input_size * column_count || out_len != row_count * column_count)
+    return fail(HPC_ERR_SHAPE, "matmul shape mismatch");
+  size_t rb;
+  if (!row_bytes(type_id, input_size, &rb)) return fail(HPC_ERR_TYPE, "unsupported type %d", type_id);
+  if (weight_len != rb * row_count) return fail(HPC_ERR_SHAPE, "weight length %zu", weight_len);
+  if (column_count == 0 || row_count == 0) return HPC_OK;
+  if (!host_in || !host_out) return fail(HPC_ERR_ARG, "null pointer");
+  hpc_weight h = nullptr;
+  int rc = hpc_weight_upload(type_id, host_weight, weight_len, input_size, row_count, &h);
+  if (rc != HPC_OK) return rc;
+  float* d_in = nullptr;
+  float* d_out = nullptr;
+  cudaError_t e = cudaMalloc(&d_in, in_len * sizeof(float));
+  if (e == cudaSuccess) e = cudaMalloc(&d_out, out_len * sizeof(float));
+  if (e == cudaSuccess) e = cudaMemcpy(d_in, host_in, in_len * sizeof(float), cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) {
+    rc = hpc_matmul_quantized_prepared_f32(h, d_in, in_len, input_size, row_count, column_count, d_out, out_len, nullptr);
+    if (rc == HPC_OK) e = cudaMemcpy(host_out, d_out, out_len * sizeof(float), cudaMemcpyDeviceToHost);
+  }
+  cudaFree(d_in);
+  cudaFree(d_out);
+  hpc_weight_release(h);
+  if (rc != HPC_OK) return rc;
+  if (e != cudaSuccess) return cuda_fail(e, "one-shot matmul");
+  return HPC_OK;
+}
+
+int hpc_q8_workspace_bytes(size_t input_size, size_t column_count, size_t* out_bytes) {
+  if (!out_bytes) return fail(HPC_ERR_ARG, "null out_bytes");
+  if (input_size == 0 || input_size % 256 || column_count > (size_t(1) << 20))
+    return fail(HPC_ERR_SHAPE, "workspace shape %zu x %zu", input_size, column_count);
+  *out_bytes = hc::q8buf_bytes(int(input_size), int(column_count));
+  return HPC_OK;
+}
+
+int hpc_q8_quantize(const float* d_in, size_t in_len, size_t input_size, size_t column_count, void* d_workspace,
+                    size_t workspace_bytes, void* stream) {
+  if (input_size == 0 || input_size % 256 || in_len != input_size * column_count || column_count > (size_t(1) << 20))
+    return fail(HPC_ERR_SHAPE, "q8 quantize shape mismatch");
+  if (column_count == 0) return HPC_OK;
+  if (!d_in || !d_workspace) return fail(HPC_ERR_ARG, "null pointer");
+  if (workspace_bytes < hc::q8buf_bytes(int(input_size), int(column_count)))
+    return fail(HPC_ERR_SHAPE, "workspace too small: %zu bytes", workspace_bytes);
+  hc::Q8Buf q = hc::q8buf_carve(d_workspace, int(input_size), int(column_count));
+  HPC_CK(hc::launch_q8k_quantize(d_in, int(input_size), int(column_count), q, nullptr, nullptr, nullptr,
+                                 static_cast<cudaStream_t>(stream)), "quantize launch");
+  return HPC_OK;
+}
+
+int hpc_matmul_q8(size_t count, const hpc_weight* handles, const void* d_workspace, size_t workspace_bytes,
+                  size_t input_size, size_t column_count, float* const* d_outs, const size_t* out_lens, void* stream) {
+  if (count == 0 || count > size_t(hc::GEMV_MAXSEG)) return fail(HPC_ERR_SHAPE, "matmul_q8: count %zu", count);
+  if (!handles || !d_outs || !out_lens) return fail(HPC_ERR_ARG, "null pointer");
+  if (input_size == 0 || input_size % 256 || column_count > (size_t(1) << 20))
+    return fail(HPC_ERR_SHAPE, "matmul_q8 shape");
+  if (column_count > 0 && !d_workspace) return fail(HPC_ERR_ARG, "null workspace");
+  if (workspace_bytes < hc::q8buf_bytes(int(input_size), int(column_count)))
+    return fail(HPC_ERR_SHAPE, "workspace too small: %zu bytes", workspace_bytes);
+  hc::GemvSeg segs[hc::GEMV_MAXSEG];
+  int tiles = 0;
+  int rc = build_segments(count, handles, d_outs, out_lens, input_size, column_count, segs, &tiles);
+  if (rc != HPC_OK) return rc;
+  if (column_count == 0) return HPC_OK;
+  hc::Q8Buf q = hc::q8buf_carve(const_cast<void*>(d_workspace), int(input_size), int(column_count));
+  return launch_gemv_ws(q, int(input_size), int(column_count), segs, int(count), tiles,
+                        static_cast<cudaStream_t>(stream));
+}
+
+static int lm_head_check(hpc_weight h, size_t input_size, size_t column_count, size_t k) {
+  if (!valid(h)) return fail(HPC_ERR_ARG, "invalid weight handle");
+  if (h->input_size != input_size) return fail(HPC_ERR_SHAPE, "LM head input size %zu vs %zu", h->input_size, input_size);
+  if (k < 1 || k > size_t(hc::TOPK_MAX) || k > h->row_count)
+    return fail(HPC_ERR_SHAPE, "top-k %zu outside 1..min(64, rows)", k);
+  if (column_count > (size_t(1) << 20)) return fail(HPC_ERR_SHAPE, "too many columns");
+  int dev = 0;
+  HPC_CK(cudaGetDevice(&dev), "cudaGetDevice");
+  if (dev != h->device) return fail(HPC_ERR_ARG, "handle lives on device %d, current device is %d", h->device, dev);
+  return HPC_OK;
+}
+
+static size_t cand_bytes_for(hpc_weight h, size_t cols, size_t k) {
+  const int tiles = int(h->rows_pad / hc::TILE);
+  return size_t(hc::lmhead_grid(tiles)) * hc::LMHEAD_LISTS * k * cols * sizeof(uint64_t);
+}
+
+int hpc_lm_head_candidates_bytes(hpc_weight h, size_t column_count, size_t k, size_t* out_bytes) {
+  if (!out_bytes) return fail(HPC_ERR_ARG, "null out_bytes");
+  int rc = lm_head_check(h, h ? h->input_size : 0, column_count, k);
+  if (rc != HPC_OK) return rc;
+  *out_bytes = cand_bytes_for(h, column_count, k);
+  return HPC_OK;
+}
+
+int hpc_lm_head_topk_q8(hpc_weight h, const void* d_workspace, size_t workspace_bytes, size_t input_size,
+                        size_t column_count, size_t k, int32_t id_offset, void* d_candidates, size_t candidates_bytes,
+                        float softcap, int32_t* d_ids, float* d_vals, uint64_t* d_keys, void* stream) {
+  int rc = lm_head_check(h, input_size, column_count, k);
+  if (rc != HPC_OK) return rc;
+  if (column_count == 0) return HPC_OK;
+  if (!d_workspace || !d_candidates || !d_ids || !d_vals) return fail(HPC_ERR_ARG, "null pointer");
+  if (workspace_bytes < hc::q8buf_bytes(int(input_size), int(column_count)))
+    return fail(HPC_ERR_SHAPE, "workspace too small: %zu bytes", workspace_bytes);
+  if (candidates_bytes < cand_bytes_for(h, column_count, k))
+    return fail(HPC_ERR_SHAPE, "candidate buffer too small: %zu bytes", candidates_bytes);
+  if (id_offset < 0 || size_t(id_offset) + h->row_count > size_t(INT32_MAX)) return fail(HPC_ERR_SHAPE, "id offset");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int tiles = int(h->rows_pad / hc::TILE);
+  const int grid = hc::lmhead_grid(tiles);
+  hc::LmHeadParams P;
+  memset(&P, 0, sizeof P);
+  P.g.seg[0].w = h->d_data;
+  P.g.seg[0].out = nullptr;
+  P.g.seg[0].type = h->type;
+  P.g.seg[0].rows = int(h->row_count);
+  P.g.nseg = 1;
+  P.g.K = int(input_size);
+  P.g.nb = int(input_size / 256);
+  P.g.split = 1;
+  P.g.split_log2 = 0;
+  P.g.bps = P.g.nb;
+  P.g.bulk = 0;
+  P.g.err = hc::device_status_word();
+  P.g.total_tiles = tiles;
+  P.g.q = hc::q8buf_carve(const_cast<void*>(d_workspace), int(input_size), int(column_count));
+  P.k = int(k);
+  P.id_offset = id_offset;
+  P.cand = static_cast<uint64_t*>(d_candidates);
+  P.cand_col_stride = size_t(grid) * hc::LMHEAD_LISTS * k;
+  const int cols = int(column_count);
+  for (int c0 = 0; c0 < cols; c0 += 8) {
+    P.g.col0 = c0;
+    P.g.ncols = cols - c0 < 8 ? cols - c0 : 8;
+    HPC_CK(hc::launch_lmhead_topk(P, grid, st), "lm head launch");
+  }
+  const int n = grid * hc::LMHEAD_LISTS * int(k);
+  HPC_CK(hc::launch_topk_merge(P.cand, n, P.cand_col_stride, int(k), k, cols, int(k), softcap, d_ids, d_vals, d_keys,
+                               st),
+         "top-k merge launch");
+  return HPC_OK;
+}
+
+int hpc_lm_head_topk(hpc_weight h, const float* d_hidden, size_t hidden_len, size_t input_size, size_t column_count,
+                     size_t k, int32_t id_offset, float softcap, int32_t* d_ids, float* d_vals, void* stream) {
+  if (hidden_len != input_size * column_count) return fail(HPC_ERR_SHAPE, "hidden length %zu", hidden_len);
+  int rc = lm_head_check(h, input_size, column_count, k);
+  if (rc != HPC_OK) return rc;
+  if (column_count == 0) return HPC_OK;
+  if (!d_hidden || !d_ids || !d_vals) return fail(HPC_ERR_ARG, "null pointer");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const size_t qb = hc::q8buf_bytes(int(input_size), int(column_count));
+  const size_t cb = cand_bytes_for(h, column_count, k);
+  void* ws = nullptr;
+  HPC_CK(cudaMallocAsync(&ws, qb + cb, st), "cudaMallocAsync(lm head scratch)");
+  hc::Q8Buf q = hc::q8buf_carve(ws, int(input_size), int(column_count));
+  cudaError_t e = hc::launch_q8k_quantize(d_hidden, int(input_size), int(column_count), q, nullptr, nullptr, nullptr, st);
+  rc = e == cudaSuccess ? hpc_lm_head_topk_q8(h, ws, qb, input_size, column_count, k, id_offset,
+                                              static_cast<char*>(ws) + qb, cb, softcap, d_ids, d_vals, nullptr, stream)
+                        : cuda_fail(e, "quantize launch");
+  cudaError_t e2 = cudaFreeAsync(ws, st);
+  if (rc != HPC_OK) return rc;
+  if (e2 != cudaSuccess) return cuda_fail(e2, "cudaFreeAsync(lm head scratch)");
+  return HPC_OK;
+}
+
+int hpc_topk_merge_keys(const uint64_t* d_keys, size_t group_count, size_t column_count, size_t k, float softcap,
+                        int32_t* d_ids, float* d_vals, void* stream) {
+  if (k < 1 || k > size_t(hc::TOPK_MAX) || group_count == 0 || group_count > 4096 || column_count > (size_t(1) << 20))
+    return fail(HPC_ERR_SHAPE, "merge shape: groups %zu columns %zu k %zu", group_count, column_count, k);
+  if (column_count == 0) return HPC_OK;
+  if (!d_keys || !d_ids || !d_vals) return fail(HPC_ERR_ARG, "null pointer");
+  const int n = int(group_count * k);
+  HPC_CK(hc::launch_topk_merge(d_keys, n, k, int(k), column_count * k, int(column_count), int(k), softcap, d_ids,
+                               d_vals, nullptr, static_cast<cudaStream_t>(stream)),
+         "top-k merge launch");
+  return HPC_OK;
+}
+
+}  // extern "C"

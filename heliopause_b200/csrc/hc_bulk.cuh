@@ -1,0 +1,65 @@
+// hc_bulk.cuh -- one-shot bulk prefetch of weight units into shared memory.
+//
+// cp.async.bulk (no multicast) copies a CTA's weight units from HBM into
+// shared memory with completion on one mbarrier.  The copies are issued
+// before griddepcontrol.wait, so under programmatic dependent launch the
+// whole weight fetch of a small GEMV overlaps the previous kernel.  The wait
+// is bounded: after ~2 s of %globaltimer it records a timeout in the
+// device status word and returns false, so a broken launch cannot hang.
+#pragma once
+#include <cstdint>
+
+#include "hc_common.cuh"
+
+namespace hc {
+
+constexpr int DEVICE_ERR_TIMEOUT = 1;
+constexpr unsigned long long WAIT_LIMIT_NS = 2000000000ull;  // 2 s
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("{ .reg .b64 st; mbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1; }" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_wait_parity(uint64_t* bar, uint32_t parity, int* err) {
+  const unsigned long long t0 = [] {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+  }();
+  while (true) {
+    uint32_t ok;
+    asm volatile(
+        "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    if (ok) return true;
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    if (t - t0 > WAIT_LIMIT_NS) {
+      if (err) atomicExch(err, DEVICE_ERR_TIMEOUT);
+      return false;
+    }
+  }
+}
+
+// dst, src, bytes: multiples of 16.
+__device__ __forceinline__ void bulk_copy_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+}  // namespace hc

@@ -1,0 +1,297 @@
+// hc_gemv.cu -- Q4_K / Q6_K x Q8_K small-M matmul (M = 1..8 per launch).
+//
+// Replaces the per-row loop of hp_matmul_quantized_prepared_f32 /
+// _multi_f32 (packages/engine/wasm-kernels/src/lib.rs:225-426) and the block
+// dots vec_dot_q4_k_q8_k_prepared (lib.rs:2117-2172) and
+// vec_dot_q6_k_q8_k_prepared (lib.rs:1924-1968).
+//
+// Decomposition (B200, HBM-bound):
+//   * unit = one 256-element block of one 32-row tile: a contiguous 4,608 B
+//     (Q4_K) / 6,720 B (Q6_K) region read as 9 / 13 warp-wide 512-byte loads
+//     (lane = row, so no cross-lane reduction inside a block);
+//   * item = (tile, K part): the K range of every tile is split into `split`
+//     parts so the launch has enough warps (~2,000) to keep HBM busy; a warp
+//     streams its item's units through a two-deep register buffer;
+//   * split 1  : persistent grid, each warp walks whole tiles;
+//     split 2/4: the parts of a tile live in one CTA and are summed in shared
+//                memory in part order;
+//     split 8-32: a cluster of split/4 CTAs per tile, summed through
+//                distributed shared memory in rank order;
+//     so every result is deterministic;
+//   * programmatic dependent launch: each warp loads its first weight unit
+//     before griddepcontrol.wait, the activation slice (written by the
+//     previous kernel) is staged into shared memory after it.
+//
+// Integer block sums are exact (dp4a / dp2a on the same int8 operands as the
+// reference); the f32 combine of the per-block terms runs in a different
+// order than the reference's 8-lane accumulators, so outputs agree to f32
+// rounding.
+#include <cooperative_groups.h>
+
+#include "hc_common.cuh"
+#include "hc_bulk.cuh"
+#include "hc_gemv_body.cuh"
+#include "hc_kernels.cuh"
+
+namespace cg = cooperative_groups;
+
+namespace hc {
+
+template <int NC>
+struct GemvFlush {
+  const GemvParams* p;
+  float (*red)[NC][32];
+  int warp, lane;
+  __device__ __forceinline__ void operator()(int item, const float (&v)[NC]) {
+    if (p->split == 1) {
+      const int tile = item;
+      const GemvSeg& sg = p->seg[seg_of(*p, tile)];
+      const int row = (tile - sg.tile_begin) * TILE + lane;
+      if (row < sg.rows) {
+#pragma unroll
+        for (int c = 0; c < NC; ++c)
+          if (c < p->ncols) sg.out[size_t(p->col0 + c) * sg.rows + row] = v[c];
+      }
+    } else {
+#pragma unroll
+      for (int c = 0; c < NC; ++c) red[warp][c][lane] = v[c];
+    }
+  }
+};
+
+template <int NC>
+__device__ __forceinline__ void store_tile(const GemvParams& p, int tile, const float (&v)[NC], int lane) {
+  const GemvSeg& sg = p.seg[seg_of(p, tile)];
+  const int row = (tile - sg.tile_begin) * TILE + lane;
+  if (row < sg.rows) {
+#pragma unroll
+    for (int c = 0; c < NC; ++c)
+      if (c < p.ncols) sg.out[size_t(p.col0 + c) * sg.rows + row] = v[c];
+  }
+}
+
+template <int NC>
+__global__ void __launch_bounds__(GEMV_THREADS, GEMV_CTAS_PER_SM) gemv_kernel(const __grid_constant__ GemvParams p) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  __shared__ float red[GEMV_WARPS_PER_CTA][NC][32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#if __CUDA_ARCH__ >= 900
+  asm volatile("griddepcontrol.launch_dependents;");
+#endif
+  const int nitems = p.total_tiles * p.split;
+  int item0, istride, kb0 = 0, nblk = p.nb;
+  if (p.split == 1) {  // warps walk whole tiles (persistent unless bulk)
+    item0 = blockIdx.x * GEMV_WARPS_PER_CTA + warp;
+    istride = p.bulk ? nitems : gridDim.x * GEMV_WARPS_PER_CTA;
+  } else if (p.split <= GEMV_WARPS_PER_CTA) {  // one item per warp, a tile's parts in one CTA
+    item0 = blockIdx.x * GEMV_WARPS_PER_CTA + warp;
+    istride = nitems;
+  } else {  // one tile per cluster, rank r owns parts [4r, 4r + 4)
+    const int csize = p.split / GEMV_WARPS_PER_CTA;
+    const int tile = blockIdx.x / csize, rank = blockIdx.x % csize;
+    item0 = tile * p.split + rank * GEMV_WARPS_PER_CTA + warp;
+    istride = nitems;
+    kb0 = rank * GEMV_WARPS_PER_CTA * p.bps;
+    nblk = GEMV_WARPS_PER_CTA * p.bps;
+  }
+
+  bool need_a, need_b;
+  gemv_planes(p, &need_a, &need_b);
+  uint8_t* act_a = need_a ? smem : nullptr;
+  uint8_t* act_b = need_b ? smem + (need_a ? size_t(p.ncols) * nblk * Q8A_REC : 0) : nullptr;
+  const ActSlice act{act_a, act_b, nblk, kb0};
+  GemvFlush<NC> flush{&p, red, warp, lane};
+
+  if (p.bulk) {
+    // Bulk mode (one item per warp): copy every unit of the CTA into shared
+    // memory before waiting for the previous kernel, then compute from there.
+    __shared__ __align__(8) uint64_t bar;
+    uint8_t* units = smem + (gemv_smem_bytes(p, nblk) + 15) / 16 * 16;  // after the activation slice
+    const int ub_max = unit_bytes(TYPE_Q6_K);
+    if (threadIdx.x == 0) {
+      mbar_init(&bar, 1);
+      uint32_t total = 0;
+      for (int w = 0; w < GEMV_WARPS_PER_CTA; ++w) {
+        const int it = item0 - warp + w;
+        if (it >= nitems) break;
+        for (int jj = 0; jj < p.bps; ++jj) {
+          int t;
+          unit_addr(p, it, jj, &t);
+          total += uint32_t(unit_bytes(t));
+        }
+      }
+      mbar_expect_tx(&bar, total);
+      for (int w = 0; w < GEMV_WARPS_PER_CTA; ++w) {
+        const int it = item0 - warp + w;
+        if (it >= nitems) break;
+        for (int jj = 0; jj < p.bps; ++jj) {
+          int t;
+          const uint8_t* src = unit_addr(p, it, jj, &t);
+          bulk_copy_g2s(units + size_t(w * p.bps + jj) * ub_max, src, uint32_t(unit_bytes(t)), &bar);
+        }
+      }
+    }
+#if __CUDA_ARCH__ >= 900
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+#endif
+    stage_activations(p, act_a, act_b, kb0, nblk);
+    __syncthreads();
+    const bool ok = mbar_wait_parity(&bar, 0, p.err);
+    if (item0 < nitems) {
+      float acc[NC];
+#pragma unroll
+      for (int c = 0; c < NC; ++c) acc[c] = 0.0f;
+      if (ok) {
+        int t;
+        unit_addr(p, item0, 0, &t);
+        for (int jj = 0; jj < p.bps; ++jj) {
+          UnitRegs r;
+          load_unit_smem(r, units + size_t(warp * p.bps + jj) * ub_max, t, lane);
+          unit_compute<NC>(r, t, (item0 & (p.split - 1)) * p.bps + jj - kb0, p.ncols, act, acc);
+        }
+      }
+      flush(item0, acc);
+    }
+  } else {
+    UnitRegs buf[2];
+    int first_type = TYPE_Q4_K;
+    if (item0 < nitems) load_unit(buf[0], unit_addr(p, item0, 0, &first_type), first_type, lane);
+#if __CUDA_ARCH__ >= 900
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+#endif
+    stage_activations(p, act_a, act_b, kb0, nblk);
+    __syncthreads();
+    stream_items<NC>(p, act, item0, istride, nitems, lane, buf[0], first_type, flush);
+  }
+  if (p.split == 1) return;
+
+  __syncthreads();
+  if (p.split <= GEMV_WARPS_PER_CTA) {
+    // warps holding part 0 of a tile sum the tile's parts in part order
+    if (item0 < nitems && item0 % p.split == 0) {
+      float v[NC];
+#pragma unroll
+      for (int c = 0; c < NC; ++c) {
+        v[c] = red[warp][c][lane];
+        for (int k = 1; k < p.split; ++k) v[c] += red[warp + k][c][lane];
+      }
+      store_tile<NC>(p, item0 / p.split, v, lane);
+    }
+    return;
+  }
+  // cluster split: CTA partial (warp order), then rank 0 sums ranks in order
+  if (warp == 0) {
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+      float v = red[0][c][lane];
+#pragma unroll
+      for (int w = 1; w < GEMV_WARPS_PER_CTA; ++w) v += red[w][c][lane];
+      red[0][c][lane] = v;
+    }
+  }
+  cg::cluster_group cl = cg::this_cluster();
+  cl.sync();
+  const int csize = p.split / GEMV_WARPS_PER_CTA;
+  if (blockIdx.x % csize == 0 && warp == 0) {
+    float v[NC];
+#pragma unroll
+    for (int c = 0; c < NC; ++c) v[c] = 0.0f;
+    for (int r = 0; r < csize; ++r) {
+      const float* remote = cl.map_shared_rank(&red[0][0][0], r);
+#pragma unroll
+      for (int c = 0; c < NC; ++c) v[c] += remote[c * 32 + lane];
+    }
+    store_tile<NC>(p, blockIdx.x / csize, v, lane);
+  }
+  cl.sync();  // keep every CTA's shared memory alive until rank 0 has read it
+}
+
+int sm_count() {
+  static int sms = 0;
+  if (!sms) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (sms <= 0) sms = 148;
+  }
+  return sms;
+}
+
+int persistent_grid(int items, int cap) {
+  const int warps_cap = cap * GEMV_WARPS_PER_CTA;
+  const int per = (items + warps_cap - 1) / warps_cap;                   // items per warp
+  const int warps = (items + per - 1) / per;                             // warps needed
+  return (warps + GEMV_WARPS_PER_CTA - 1) / GEMV_WARPS_PER_CTA;
+}
+
+void gemv_plan(GemvParams& p) {
+  // Split K as far as the launch still fits in one wave of resident CTAs
+  // (GEMV_CTAS_PER_SM per SM, one item per warp); parts stay >= 1 block and
+  // the cluster form is used up to 8 CTAs (split 32).
+  const int cap_warps = sm_count() * GEMV_CTAS_PER_SM * GEMV_WARPS_PER_CTA;
+  int s = 1, lg = 0;
+  while (s < 32 && p.nb % (s * 2) == 0 && p.total_tiles * s * 2 <= cap_warps) {
+    s *= 2;
+    ++lg;
+  }
+  p.split = s;
+  p.split_log2 = lg;
+  p.bps = p.nb / s;
+  // Launches that fit in one wave stage all their units in shared memory.
+  const size_t unit_smem = size_t(GEMV_WARPS_PER_CTA) * p.bps * unit_bytes(TYPE_Q6_K);
+  p.bulk = (p.split > 1 || p.total_tiles <= cap_warps) && unit_smem <= size_t(GEMV_BULK_MAX_UNITS_SMEM);
+  if (p.split == 1 && p.bulk) {
+    // one item per warp in bulk mode: make the grid non-persistent
+    p.bulk = p.total_tiles <= cap_warps;
+  }
+  p.err = device_status_word();
+}
+
+int gemv_grid(const GemvParams& p) {
+  const int items = p.total_tiles * p.split;
+  if (p.split == 1 && !p.bulk) return persistent_grid(items, sm_count() * GEMV_CTAS_PER_SM);
+  return (items + GEMV_WARPS_PER_CTA - 1) / GEMV_WARPS_PER_CTA;
+}
+
+template <int NC>
+static cudaError_t launch_nc(const GemvParams& p, cudaStream_t stream) {
+  const int nblk = p.split > GEMV_WARPS_PER_CTA ? GEMV_WARPS_PER_CTA * p.bps : p.nb;
+  size_t smem = (gemv_smem_bytes(p, nblk) + 15) / 16 * 16;
+  if (p.bulk) smem += size_t(GEMV_WARPS_PER_CTA) * p.bps * unit_bytes(TYPE_Q6_K);
+  if (smem > size_t(GEMV_MAX_SMEM)) return cudaErrorInvalidValue;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(gemv_kernel<NC>, cudaFuncAttributeMaxDynamicSharedMemorySize, GEMV_MAX_SMEM);
+    if (e != cudaSuccess) return e;
+    attr_set = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(gemv_grid(p)));
+  cfg.blockDim = dim3(GEMV_THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[na].val.programmaticStreamSerializationAllowed = 1;
+  ++na;
+  if (p.split > GEMV_WARPS_PER_CTA) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = unsigned(p.split / GEMV_WARPS_PER_CTA);
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  return cudaLaunchKernelEx(&cfg, gemv_kernel<NC>, p);
+}
+
+cudaError_t launch_gemv(const GemvParams& p, cudaStream_t stream) {
+  if (p.ncols <= 1) return launch_nc<1>(p, stream);
+  if (p.ncols <= 2) return launch_nc<2>(p, stream);
+  if (p.ncols <= 4) return launch_nc<4>(p, stream);
+  return launch_nc<8>(p, stream);
+}
+
+}  // namespace hc

@@ -1,0 +1,271 @@
+// hc_gemv_body.cuh -- the streaming core shared by the GEMV and LM-head
+// kernels: per-block Q4_K / Q6_K x Q8_K dot products for one 32-row tile
+// (lane = row) computed from registers, and the register double buffer that
+// keeps two units (one 256-element block of one tile each) in flight per warp.
+//
+// Block math follows vec_dot_q4_k_q8_k_prepared (lib.rs:2117-2172) and
+// vec_dot_q6_k_q8_k_prepared (lib.rs:1924-1968): exact int32 block sums
+//   Q4_K: sum_g sc[g] * dot(q4, q8)_g  and  sum_g mn[g] * bsum32[g]
+//   Q6_K: sum_s sc[s] * dot(q6 - 32, q8)_s
+// combined per block as (d*d8)*isum - (dmin*d8)*msum in f32.
+//
+// Work decomposition (see hc_gemv.cu): an "item" is (tile, K part); the K
+// range of a tile is split into p.split parts, item i = (i / split, i % split).
+// A warp walks its items and streams their units through the double buffer,
+// so the loads of the next unit (possibly of the next item) are in flight
+// while the current one is computed.
+#pragma once
+#include "hc_common.cuh"
+#include "hc_kernels.cuh"
+#include "hc_unpack.cuh"
+
+namespace hc {
+
+constexpr int UNIT_CHUNKS = Q6K_CHUNKS;  // register buffer sized for the larger type
+
+// Activation records staged in shared memory (hc_common.cuh planes): record of
+// (local column c, local block j) at act + (c*nblk + j)*rec.
+struct ActSlice {
+  const uint8_t* a;  // plane A records (Q4_K)
+  const uint8_t* b;  // plane B records (Q6_K)
+  int nblk;          // blocks per column in the slice
+  int kb0;           // first block of the slice
+};
+
+struct UnitRegs {
+  uint4 c[UNIT_CHUNKS];
+  uint32_t d;  // Q6_K d bits
+};
+
+// Streaming loads: evict-first, no L1 allocation (weights are read once).
+__device__ __forceinline__ void load_unit(UnitRegs& r, const uint8_t* unit, int type, int lane) {
+  const uint4* p = reinterpret_cast<const uint4*>(unit) + lane;
+  if (type == TYPE_Q4_K) {
+#pragma unroll
+    for (int k = 0; k < Q4K_CHUNKS; ++k) r.c[k] = __ldcs(p + k * TILE);
+  } else {
+#pragma unroll
+    for (int k = 0; k < Q6K_CHUNKS; ++k) r.c[k] = __ldcs(p + k * TILE);
+    r.d = __ldcs(reinterpret_cast<const unsigned short*>(unit + Q6K_DPLANE_OFFSET) + lane);
+  }
+}
+
+template <int NC>
+__device__ __forceinline__ void q4k_regs(const UnitRegs& r, int j, int ncols, const ActSlice& act, float (&acc)[NC]) {
+  const Q4KHeader hd = q4k_header(r.c[0]);
+  int isum[NC];
+#pragma unroll
+  for (int col = 0; col < NC; ++col) isum[col] = 0;
+#pragma unroll
+  for (int pp = 0; pp < 4; ++pp) {
+    const uint4 u0 = r.c[1 + 2 * pp], u1 = r.c[2 + 2 * pp];
+    const uint32_t w[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+    const int s0 = hd.sc(2 * pp), s1 = hd.sc(2 * pp + 1);
+#pragma unroll
+    for (int col = 0; col < NC; ++col) {
+      if (col < ncols) {
+        const uint8_t* rec = act.a + (col * act.nblk + j) * Q8A_REC + 64 * pp;
+        const uint4 a0 = *reinterpret_cast<const uint4*>(rec), a1 = *reinterpret_cast<const uint4*>(rec + 16);
+        const uint4 a2 = *reinterpret_cast<const uint4*>(rec + 32), a3 = *reinterpret_cast<const uint4*>(rec + 48);
+        const uint32_t al[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+        const uint32_t ah[8] = {a2.x, a2.y, a2.z, a2.w, a3.x, a3.y, a3.z, a3.w};
+        int tl = 0, th = 0;
+#pragma unroll
+        for (int l = 0; l < 8; ++l) {
+          tl = dp4a(w[l] & 0x0f0f0f0fu, al[l], tl);
+          th = dp4a((w[l] >> 4) & 0x0f0f0f0fu, ah[l], th);
+        }
+        isum[col] += s0 * tl + s1 * th;
+      }
+    }
+  }
+#pragma unroll
+  for (int col = 0; col < NC; ++col) {
+    if (col < ncols) {
+      const uint8_t* rec = act.a + (col * act.nblk + j) * Q8A_REC;
+      const uint4 bs = *reinterpret_cast<const uint4*>(rec + Q8A_BS);
+      int ms = __dp2a_lo(int(bs.x), int(hd.mn_lo), 0);
+      ms = __dp2a_hi(int(bs.y), int(hd.mn_lo), ms);
+      ms = __dp2a_lo(int(bs.z), int(hd.mn_hi), ms);
+      ms = __dp2a_hi(int(bs.w), int(hd.mn_hi), ms);
+      const float d8 = *reinterpret_cast<const float*>(rec + Q8A_D);
+      acc[col] += __fmul_rn(hd.d, d8) * float(isum[col]) - __fmul_rn(hd.dmin, d8) * float(ms);
+    }
+  }
+}
+
+template <int NC>
+__device__ __forceinline__ void q6k_regs(const UnitRegs& r, int j, int ncols, const ActSlice& act, float (&acc)[NC]) {
+  const float dw = f16_bits_to_f32(r.d);
+  const uint32_t scw[4] = {r.c[12].x, r.c[12].y, r.c[12].z, r.c[12].w};
+  int isum[NC];
+#pragma unroll
+  for (int col = 0; col < NC; ++col) isum[col] = 0;
+#pragma unroll
+  for (int s = 0; s < 8; ++s) {
+    const uint32_t nw[4] = {r.c[s].x, r.c[s].y, r.c[s].z, r.c[s].w};
+    const uint4 hv = r.c[8 + (s >> 1)];
+    const uint32_t hw[4] = {hv.x, hv.y, hv.z, hv.w};
+    uint32_t ua[4], ub[4];
+#pragma unroll
+    for (int jj = 0; jj < 4; ++jj) q6k_unpack(nw[jj], hw[2 * (s & 1) + (jj >> 1)], jj & 1, ua[jj], ub[jj]);
+    const int sa = int(int8_t((scw[s >> 2] >> (8 * (s & 3))) & 0xff));
+    const int sb = int(int8_t((scw[(s + 8) >> 2] >> (8 * ((s + 8) & 3))) & 0xff));
+#pragma unroll
+    for (int col = 0; col < NC; ++col) {
+      if (col < ncols) {
+        const uint8_t* rec = act.b + (col * act.nblk + j) * Q8B_REC;
+        const uint4 A = *reinterpret_cast<const uint4*>(rec + 16 * s);
+        const uint4 B = *reinterpret_cast<const uint4*>(rec + 16 * (s + 8));
+        int ta = dp4a(ua[0], A.x, 0);
+        ta = dp4a(ua[1], A.y, ta);
+        ta = dp4a(ua[2], A.z, ta);
+        ta = dp4a(ua[3], A.w, ta);
+        int tb = dp4a(ub[0], B.x, 0);
+        tb = dp4a(ub[1], B.y, tb);
+        tb = dp4a(ub[2], B.z, tb);
+        tb = dp4a(ub[3], B.w, tb);
+        isum[col] += sa * ta + sb * tb;
+      }
+    }
+  }
+#pragma unroll
+  for (int col = 0; col < NC; ++col) {
+    if (col < ncols) {
+      // The 6-bit values were used unsigned (0..63); subtract 32 * sum(sc * bsum16).
+      const uint8_t* rec = act.b + (col * act.nblk + j) * Q8B_REC;
+      const uint4 b0 = *reinterpret_cast<const uint4*>(rec + Q8B_BS);
+      const uint4 b1 = *reinterpret_cast<const uint4*>(rec + Q8B_BS + 16);
+      int corr = __dp2a_lo(int(b0.x), int(scw[0]), 0);
+      corr = __dp2a_hi(int(b0.y), int(scw[0]), corr);
+      corr = __dp2a_lo(int(b0.z), int(scw[1]), corr);
+      corr = __dp2a_hi(int(b0.w), int(scw[1]), corr);
+      corr = __dp2a_lo(int(b1.x), int(scw[2]), corr);
+      corr = __dp2a_hi(int(b1.y), int(scw[2]), corr);
+      corr = __dp2a_lo(int(b1.z), int(scw[3]), corr);
+      corr = __dp2a_hi(int(b1.w), int(scw[3]), corr);
+      const float d8 = *reinterpret_cast<const float*>(rec + Q8B_D);
+      acc[col] += __fmul_rn(dw, d8) * float(isum[col] - 32 * corr);
+    }
+  }
+}
+
+// Loads one unit that was staged in shared memory into registers.
+__device__ __forceinline__ void load_unit_smem(UnitRegs& r, const uint8_t* unit, int type, int lane) {
+  const uint4* p = reinterpret_cast<const uint4*>(unit) + lane;
+  if (type == TYPE_Q4_K) {
+#pragma unroll
+    for (int k = 0; k < Q4K_CHUNKS; ++k) r.c[k] = p[k * TILE];
+  } else {
+#pragma unroll
+    for (int k = 0; k < Q6K_CHUNKS; ++k) r.c[k] = p[k * TILE];
+    r.d = reinterpret_cast<const uint16_t*>(unit + Q6K_DPLANE_OFFSET)[lane];
+  }
+}
+
+template <int NC>
+__device__ __forceinline__ void unit_compute(const UnitRegs& r, int type, int j, int ncols, const ActSlice& act,
+                                             float (&acc)[NC]) {
+  if (type == TYPE_Q4_K) q4k_regs<NC>(r, j, ncols, act, acc);
+  else q6k_regs<NC>(r, j, ncols, act, acc);
+}
+
+__device__ __forceinline__ int seg_of(const GemvParams& p, int tile_g) {
+  int si = 0;
+#pragma unroll
+  for (int i = 1; i < GEMV_MAXSEG; ++i)
+    if (i < p.nseg && tile_g >= p.seg[i].tile_begin) si = i;
+  return si;
+}
+
+// Position of one unit in a warp's stream.
+struct UnitPos {
+  int item;  // global item index
+  int j;     // block offset inside the item's K part
+};
+
+// Address and type of unit j of an item.
+__device__ __forceinline__ const uint8_t* unit_addr(const GemvParams& p, int item, int j, int* type) {
+  const int tile = item >> p.split_log2, part = item & (p.split - 1);
+  const GemvSeg& sg = p.seg[seg_of(p, tile)];
+  *type = sg.type;
+  const int ub = unit_bytes(sg.type);
+  const int b = part * p.bps + j;
+  return sg.w + (size_t(tile - sg.tile_begin) * p.nb + b) * ub;
+}
+
+// Streams the items item0, item0 + istride, ... (< nitems) of one warp: every
+// unit is loaded one step ahead (double buffer), `flush(item, acc)` receives
+// each finished item's row sums.  buf[0] must already hold the first unit
+// (loaded by the caller before it waited for the previous kernel: PDL).
+template <int NC, class Flush>
+__device__ __forceinline__ void stream_items(const GemvParams& p, const ActSlice& act, int item0, int istride,
+                                             int nitems, int lane, UnitRegs& buf0, int first_type, Flush& flush) {
+  if (item0 >= nitems) return;
+  UnitRegs buf1;
+  int t0 = first_type, t1 = first_type;
+  int item = item0, j = 0;
+  float acc[NC];
+#pragma unroll
+  for (int c = 0; c < NC; ++c) acc[c] = 0.0f;
+  // One step: prefetch the unit after (item, j) into `nxt`, compute `cur`.
+  // The two buffers alternate by name (no dynamic indexing, so they stay in
+  // registers).
+  auto step = [&](UnitRegs& cur, int tcur, UnitRegs& nxt, int& tnxt) -> bool {
+    int nitem = item, nj = j + 1;
+    if (nj == p.bps) {
+      nitem = item + istride;
+      nj = 0;
+    }
+    const bool has_next = nitem < nitems;
+    if (has_next) load_unit(nxt, unit_addr(p, nitem, nj, &tnxt), tnxt, lane);
+    unit_compute<NC>(cur, tcur, (item & (p.split - 1)) * p.bps + j - act.kb0, p.ncols, act, acc);
+    if (nj == 0) {
+      flush(item, acc);
+#pragma unroll
+      for (int c = 0; c < NC; ++c) acc[c] = 0.0f;
+    }
+    item = nitem;
+    j = nj;
+    return has_next;
+  };
+  while (step(buf0, t0, buf1, t1) && step(buf1, t1, buf0, t0)) {
+  }
+}
+
+// Cooperative copy of the activation slice for blocks [kb0, kb0 + nblk) of
+// columns [col0, col0 + ncols) into shared memory (plane A then plane B).
+__device__ __forceinline__ void stage_activations(const GemvParams& p, uint8_t* dst_a, uint8_t* dst_b, int kb0,
+                                                  int nblk) {
+  const int nthreads = blockDim.x;
+  for (int c = 0; c < p.ncols; ++c) {
+    const size_t rec0 = size_t(p.col0 + c) * p.nb + kb0;
+    if (dst_a) {
+      const uint4* s = reinterpret_cast<const uint4*>(p.q.a + rec0 * Q8A_REC);
+      uint4* d = reinterpret_cast<uint4*>(dst_a + size_t(c) * nblk * Q8A_REC);
+      for (int i = threadIdx.x; i < nblk * Q8A_REC / 16; i += nthreads) d[i] = __ldg(s + i);
+    }
+    if (dst_b) {
+      const uint4* s = reinterpret_cast<const uint4*>(p.q.b + rec0 * Q8B_REC);
+      uint4* d = reinterpret_cast<uint4*>(dst_b + size_t(c) * nblk * Q8B_REC);
+      for (int i = threadIdx.x; i < nblk * Q8B_REC / 16; i += nthreads) d[i] = __ldg(s + i);
+    }
+  }
+}
+
+__host__ __device__ inline void gemv_planes(const GemvParams& p, bool* need_a, bool* need_b) {
+  *need_a = *need_b = false;
+  for (int i = 0; i < p.nseg; ++i) {
+    if (p.seg[i].type == TYPE_Q4_K) *need_a = true;
+    else *need_b = true;
+  }
+}
+
+// Dynamic shared memory of a launch: the activation slice of one CTA.
+__host__ __device__ inline size_t gemv_smem_bytes(const GemvParams& p, int nblk) {
+  bool a, b;
+  gemv_planes(p, &a, &b);
+  return size_t(p.ncols) * nblk * ((a ? Q8A_REC : 0) + (b ? Q8B_REC : 0));
+}
+
+}  // namespace hc

@@ -1,0 +1,61 @@
+// hc_kernels.cuh -- launchers shared between the kernel files and the C ABI.
+#pragma once
+#include "hc_common.cuh"
+
+namespace hc {
+
+constexpr int GEMV_WARPS = 4;  // warps per CTA; each warp owns whole blocks
+constexpr int GEMV_BPW = 2;    // blocks per warp per round (loads issued together)
+constexpr int GEMV_MAXSEG = 8; // weights sharing one input in one launch
+
+struct GemvSeg {
+  const uint8_t* w;  // tile layout
+  float* out;        // out[col * rows + row]
+  int type;
+  int rows;
+  int tile_begin;    // first global tile index of this segment
+  int pad;
+};
+
+struct GemvParams {
+  GemvSeg seg[GEMV_MAXSEG];
+  int nseg;
+  int K, nb;        // input size and 256-blocks per row
+  int split;        // K parts per tile (1, 2, 4, or 8..32 = a cluster of split/4 CTAs)
+  int split_log2;   // log2(split)
+  int bps;          // blocks per part = nb / split
+  int col0, ncols;  // this launch covers columns [col0, col0 + ncols), ncols <= 8
+  int total_tiles;  // over all segments
+  int bulk;         // 1: each CTA copies all of its units into shared memory up front
+  int* err;         // device status word (bounded-wait timeouts)
+  Q8Buf q;
+};
+
+// Device status word of the current device (hc_api.cu).
+int* device_status_word();
+
+constexpr int GEMV_WARPS_PER_CTA = 4;
+constexpr int GEMV_THREADS = GEMV_WARPS_PER_CTA * 32;
+constexpr int GEMV_CTAS_PER_SM = 3;
+constexpr int GEMV_MAX_SMEM = 200 * 1024;
+constexpr int GEMV_BULK_MAX_UNITS_SMEM = 112 * 1024;  // unit bytes a bulk-mode CTA may stage
+
+__host__ __device__ inline int unit_bytes(int type) { return int(tile_block_bytes(type)); }
+
+cudaError_t launch_q8k_quantize(const float* x, int K, int cols, const Q8Buf& q, int8_t* nat_qs, int16_t* nat_bs32,
+                                float* nat_d, cudaStream_t stream);
+cudaError_t launch_repack(int type, const uint8_t* src, uint8_t* dst, int rows, int rows_pad, int nb,
+                          cudaStream_t stream);
+cudaError_t launch_dequant(int type, const uint8_t* w, float* out, int rows, int nb, cudaStream_t stream);
+
+// Picks the K split for a launch; fills p.split and p.bps.
+void gemv_plan(GemvParams& p);
+// Grid size of a launch planned by gemv_plan.
+int gemv_grid(const GemvParams& p);
+int sm_count();
+// Persistent grid over `items` items, one warp per item at a time: the fewest
+// CTAs (<= cap) that give every warp the same number of items.
+int persistent_grid(int items, int cap);
+cudaError_t launch_gemv(const GemvParams& p, cudaStream_t stream);
+
+}  // namespace hc

@@ -1,0 +1,194 @@
+// hc_repack.cu -- GGUF block layout -> row-tile layout (see hc_common.cuh),
+// and the inverse dequantization used to prove the repack bit-exact.
+//
+// Dequantization follows dequantize_q4_k (lib.rs:1630-1664):
+//   y = (d*sc)*q - dmin*m
+// and dequantize_q6_k (lib.rs:1709-1744):
+//   y = (d*sc)*(q-32)
+// with every product and difference rounded on its own (__fmul_rn/__fsub_rn),
+// as the Rust code never fuses them.
+#include "hc_common.cuh"
+#include "hc_kernels.cuh"
+#include "hc_unpack.cuh"
+
+namespace hc {
+
+// ---- repack: one thread per (row, block) -----------------------------------
+
+__global__ void repack_q4k_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, int rows,
+                                  int rows_pad, int nb) {
+  const size_t t = blockIdx.x * size_t(blockDim.x) + threadIdx.x;
+  if (t >= size_t(rows_pad) * nb) return;
+  const int row = int(t / nb), b = int(t % nb);
+  const int tile = row / TILE, lane = row % TILE;
+  uint8_t blk[144];
+  if (row < rows) {
+    const uint8_t* s = src + (size_t(row) * nb + b) * 144;
+    for (int i = 0; i < 144; ++i) blk[i] = s[i];
+  } else {
+    for (int i = 0; i < 144; ++i) blk[i] = 0;
+  }
+  uint8_t* out = dst + (size_t(tile) * nb + b) * Q4K_TILE_BLOCK_BYTES + size_t(lane) * 16;
+  uint32_t w[4];
+  for (int k = 0; k < 4; ++k) w[k] = blk[4 * k] | (blk[4 * k + 1] << 8) | (blk[4 * k + 2] << 16) | (uint32_t(blk[4 * k + 3]) << 24);
+  *reinterpret_cast<uint4*>(out) = make_uint4(w[0], w[1], w[2], w[3]);
+  const uint8_t* qs = blk + 16;
+  for (int c = 0; c < 8; ++c) {
+    const int p = c >> 1;
+    for (int k = 0; k < 4; ++k) {
+      const int l = 4 * (c & 1) + k;
+      const int o = 32 * p + l;
+      w[k] = qs[o] | (qs[o + 8] << 8) | (qs[o + 16] << 16) | (uint32_t(qs[o + 24]) << 24);
+    }
+    *reinterpret_cast<uint4*>(out + size_t(1 + c) * 16 * TILE) = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
+__device__ __forceinline__ uint32_t q6_value(const uint8_t* blk, int e) {
+  const int h = e >> 7, r = e & 127;
+  const uint8_t lq = blk[64 * h + (r & 63)];
+  const uint32_t lo = (r < 64) ? (lq & 0x0f) : (lq >> 4);
+  const uint32_t hi = (blk[128 + 32 * h + (r & 31)] >> (2 * (r >> 5))) & 3;
+  return lo | (hi << 4);
+}
+
+__device__ __forceinline__ int q6_elem(int s, int j, int i) {
+  const int off[4] = {0, 8, 1, 9};
+  return 16 * s + 2 * j + off[i];
+}
+
+__global__ void repack_q6k_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, int rows,
+                                  int rows_pad, int nb) {
+  const size_t t = blockIdx.x * size_t(blockDim.x) + threadIdx.x;
+  if (t >= size_t(rows_pad) * nb) return;
+  const int row = int(t / nb), b = int(t % nb);
+  const int tile = row / TILE, lane = row % TILE;
+  uint8_t blk[210];
+  if (row < rows) {
+    const uint8_t* s = src + (size_t(row) * nb + b) * 210;
+    for (int i = 0; i < 210; ++i) blk[i] = s[i];
+  } else {
+    for (int i = 0; i < 210; ++i) blk[i] = 0;
+  }
+  uint8_t* base = dst + (size_t(tile) * nb + b) * Q6K_TILE_BLOCK_BYTES;
+  uint8_t* out = base + size_t(lane) * 16;
+  // nibble words
+  for (int s = 0; s < 8; ++s) {
+    uint32_t w[4];
+    for (int j = 0; j < 4; ++j) {
+      uint32_t word = 0;
+      for (int i = 0; i < 4; ++i) {
+        const uint32_t a = q6_value(blk, q6_elem(s, j, i)) & 15;
+        const uint32_t c = q6_value(blk, q6_elem(s + 8, j, i)) & 15;
+        word |= (a | (c << 4)) << (8 * i);
+      }
+      w[j] = word;
+    }
+    *reinterpret_cast<uint4*>(out + size_t(s) * 16 * TILE) = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+  // high-bit words: h = 2s + jj -> chunk 8 + h/4, word h%4
+  for (int c = 0; c < 4; ++c) {
+    uint32_t w[4];
+    for (int k = 0; k < 4; ++k) {
+      const int h = 4 * c + k, s = h >> 1, jj = h & 1;
+      uint32_t word = 0;
+      for (int i = 0; i < 4; ++i) {
+        const uint32_t b0 = q6_value(blk, q6_elem(s, 2 * jj, i)) >> 4;
+        const uint32_t b1 = q6_value(blk, q6_elem(s, 2 * jj + 1, i)) >> 4;
+        const uint32_t b2 = q6_value(blk, q6_elem(s + 8, 2 * jj, i)) >> 4;
+        const uint32_t b3 = q6_value(blk, q6_elem(s + 8, 2 * jj + 1, i)) >> 4;
+        word |= (b0 | (b1 << 2) | (b2 << 4) | (b3 << 6)) << (8 * i);
+      }
+      w[k] = word;
+    }
+    *reinterpret_cast<uint4*>(out + size_t(8 + c) * 16 * TILE) = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+  {
+    uint32_t w[4];
+    for (int k = 0; k < 4; ++k)
+      w[k] = blk[192 + 4 * k] | (blk[193 + 4 * k] << 8) | (blk[194 + 4 * k] << 16) | (uint32_t(blk[195 + 4 * k]) << 24);
+    *reinterpret_cast<uint4*>(out + size_t(12) * 16 * TILE) = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+  *reinterpret_cast<uint16_t*>(base + Q6K_DPLANE_OFFSET + size_t(lane) * 2) = uint16_t(blk[208] | (blk[209] << 8));
+}
+
+// ---- dequantize from the tile layout: one thread per (row, block) -----------
+
+__global__ void dequant_q4k_kernel(const uint8_t* __restrict__ w, float* __restrict__ out, int rows, int nb) {
+  const size_t t = blockIdx.x * size_t(blockDim.x) + threadIdx.x;
+  if (t >= size_t(rows) * nb) return;
+  const int row = int(t / nb), b = int(t % nb);
+  const uint4* c = reinterpret_cast<const uint4*>(w + (size_t(row / TILE) * nb + b) * Q4K_TILE_BLOCK_BYTES) + (row % TILE);
+  Q4KHeader hd = q4k_header(c[0]);
+  float* o = out + size_t(row) * nb * QK + size_t(b) * QK;
+  for (int ch = 0; ch < 8; ++ch) {
+    const uint4 v = c[size_t(1 + ch) * TILE];
+    const uint32_t words[4] = {v.x, v.y, v.z, v.w};
+    const int p = ch >> 1;
+    const float d1 = __fmul_rn(hd.d, float(hd.sc(2 * p))), d2 = __fmul_rn(hd.d, float(hd.sc(2 * p + 1)));
+    const float m1 = __fmul_rn(hd.dmin, float(hd.mn(2 * p))), m2 = __fmul_rn(hd.dmin, float(hd.mn(2 * p + 1)));
+    for (int k = 0; k < 4; ++k) {
+      const int l = 4 * (ch & 1) + k;
+      for (int i = 0; i < 4; ++i) {
+        const uint32_t byte = (words[k] >> (8 * i)) & 0xff;
+        const int j = l + 8 * i;  // position inside the 32-byte pair
+        o[64 * p + j] = __fsub_rn(__fmul_rn(d1, float(byte & 15)), m1);
+        o[64 * p + 32 + j] = __fsub_rn(__fmul_rn(d2, float(byte >> 4)), m2);
+      }
+    }
+  }
+}
+
+__global__ void dequant_q6k_kernel(const uint8_t* __restrict__ w, float* __restrict__ out, int rows, int nb) {
+  const size_t t = blockIdx.x * size_t(blockDim.x) + threadIdx.x;
+  if (t >= size_t(rows) * nb) return;
+  const int row = int(t / nb), b = int(t % nb);
+  const uint8_t* base = w + (size_t(row / TILE) * nb + b) * Q6K_TILE_BLOCK_BYTES;
+  const uint4* c = reinterpret_cast<const uint4*>(base) + (row % TILE);
+  const float d = f16_bits_to_f32(reinterpret_cast<const uint16_t*>(base + Q6K_DPLANE_OFFSET)[row % TILE]);
+  const uint4 scv = c[12 * TILE];
+  const uint32_t scw[4] = {scv.x, scv.y, scv.z, scv.w};
+  float* o = out + size_t(row) * nb * QK + size_t(b) * QK;
+  for (int s = 0; s < 8; ++s) {
+    const uint4 nv = c[size_t(s) * TILE];
+    const uint32_t nw[4] = {nv.x, nv.y, nv.z, nv.w};
+    const uint4 hv = c[size_t(8 + (s >> 1)) * TILE];
+    const uint32_t hw4[4] = {hv.x, hv.y, hv.z, hv.w};
+    const int sa = int(int8_t((scw[s >> 2] >> (8 * (s & 3))) & 0xff));
+    const int sb = int(int8_t((scw[(s + 8) >> 2] >> (8 * ((s + 8) & 3))) & 0xff));
+    const float da = __fmul_rn(d, float(sa)), db = __fmul_rn(d, float(sb));
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t hw = hw4[2 * (s & 1) + (j >> 1)];
+      uint32_t ua, ub;
+      q6k_unpack(nw[j], hw, j & 1, ua, ub);
+      const int off[4] = {0, 8, 1, 9};
+      for (int i = 0; i < 4; ++i) {
+        const int qa = int((ua >> (8 * i)) & 0xff) - 32;
+        const int qb = int((ub >> (8 * i)) & 0xff) - 32;
+        o[16 * s + 2 * j + off[i]] = __fmul_rn(da, float(qa));
+        o[16 * (s + 8) + 2 * j + off[i]] = __fmul_rn(db, float(qb));
+      }
+    }
+  }
+}
+
+cudaError_t launch_repack(int type, const uint8_t* src, uint8_t* dst, int rows, int rows_pad, int nb,
+                          cudaStream_t stream) {
+  const size_t n = size_t(rows_pad) * nb;
+  const int threads = 128;
+  const unsigned blocks = unsigned((n + threads - 1) / threads);
+  if (type == TYPE_Q4_K) repack_q4k_kernel<<<blocks, threads, 0, stream>>>(src, dst, rows, rows_pad, nb);
+  else repack_q6k_kernel<<<blocks, threads, 0, stream>>>(src, dst, rows, rows_pad, nb);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_dequant(int type, const uint8_t* w, float* out, int rows, int nb, cudaStream_t stream) {
+  const size_t n = size_t(rows) * nb;
+  const int threads = 128;
+  const unsigned blocks = unsigned((n + threads - 1) / threads);
+  if (type == TYPE_Q4_K) dequant_q4k_kernel<<<blocks, threads, 0, stream>>>(w, out, rows, nb);
+  else dequant_q6k_kernel<<<blocks, threads, 0, stream>>>(w, out, rows, nb);
+  return cudaGetLastError();
+}
+
+}  // namespace hc

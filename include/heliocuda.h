@@ -1,0 +1,178 @@
+/*
+ * heliocuda.h -- C ABI of the B200 (sm_100a) runner for the Heliopause decode
+ * hot path: Q4_K/Q6_K dequant-fused GEMV and small-M matmul, the Q6_K LM head
+ * with on-GPU top-k, and the pieces of the decode step around them.
+ *
+ * Conventions
+ *   - Plain C types only.  `stream` is a cudaStream_t passed as void*
+ *     (NULL = the legacy default stream).  Device pointers are marked d_*.
+ *   - Lengths are element counts (bytes for weight buffers), exactly as in
+ *     the WASM exports these functions replace.
+ *   - Matrices follow the reference layout: a weight has `row_count` output
+ *     rows of `input_size` elements; activations are `column_count` columns of
+ *     `input_size` floats (x[col*input_size + i]); outputs are
+ *     out[col*row_count + row].
+ *   - Every call returns a status code.  0..3 are the reference's codes
+ *     (packages/engine/wasm-kernels/src/lib.rs:7-10); 4..7 are added for the
+ *     GPU.  hpc_last_error() gives a message for the calling thread.
+ *   - Calls are stream-ordered and do not synchronize unless noted.
+ *   - The library never falls back to the CPU: without a usable device every
+ *     call returns HPC_ERR_CUDA.
+ */
+#ifndef HELIOCUDA_H
+#define HELIOCUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define HPC_OK 0
+#define HPC_ERR_SHAPE 1   /* lib.rs:8  ERR_SHAPE */
+#define HPC_ERR_HEADS 2   /* lib.rs:9  ERR_HEADS */
+#define HPC_ERR_TYPE 3    /* lib.rs:10 ERR_TYPE  */
+#define HPC_ERR_CUDA 4    /* CUDA runtime or launch failure */
+#define HPC_ERR_TIMEOUT 5 /* a bounded device wait gave up */
+#define HPC_ERR_NCCL 6    /* collective failure */
+#define HPC_ERR_ARG 7     /* null pointer / invalid handle */
+
+/* Type ids: lib.rs:12-17 and quantizedTypeId (runner/wasm/wasm-kernels.ts:1908-1923). */
+#define HPC_TYPE_Q4_K 1
+#define HPC_TYPE_Q5_K 2
+#define HPC_TYPE_Q6_K 3
+#define HPC_TYPE_IQ4_XS 4
+#define HPC_TYPE_Q8_0 5
+#define HPC_TYPE_Q4_0 6
+
+/* Opaque resident weight (HBM).  Replaces WasmQuantizedWeightHandle
+ * (runner/wasm/wasm-kernels.ts:387-397): it owns the uploaded bytes, already
+ * repacked into the coalesced tile layout the kernels read. */
+typedef struct hpc_weight_s *hpc_weight;
+
+/* Message of the last failing call on this thread ("" if none). */
+const char *hpc_last_error(void);
+
+/* ABI version (major << 16 | minor). */
+int hpc_version(void);
+
+/* Reads and clears the current device's status word: HPC_ERR_TIMEOUT if a
+ * kernel's bounded wait gave up since the last call, else HPC_OK.
+ * Synchronizes with the device. */
+int hpc_device_error(void);
+
+/* Select the device for subsequent calls on this thread and check it is an
+ * sm_100 part.  Replaces prefillWasmExports() instantiation
+ * (runner/wasm/wasm-kernels.ts:416-426). */
+int hpc_device_init(int device);
+
+/* Upload a GGUF-layout weight (host bytes) and repack it in HBM.  Only Q4_K
+ * and Q6_K are resident on the GPU; other type ids return HPC_ERR_TYPE.
+ * Replaces createWasmQuantizedWeightHandle (wasm-kernels.ts:520-574), which
+ * copies the bytes and runs hp_prepare_quantized_scales_f32 (lib.rs:157-222).
+ * Synchronous. */
+int hpc_weight_upload(int type_id, const uint8_t *host_bytes, size_t byte_len, size_t input_size,
+                      size_t row_count, hpc_weight *out_handle);
+
+/* Same, from GGUF-layout bytes already in device memory (not modified). */
+int hpc_weight_upload_device(int type_id, const void *d_bytes, size_t byte_len, size_t input_size,
+                             size_t row_count, void *stream, hpc_weight *out_handle);
+
+/* Replaces releaseWasmQuantizedWeightHandle (wasm-kernels.ts:576-584). */
+int hpc_weight_release(hpc_weight handle);
+
+/* Shape and residency of a handle (any out pointer may be NULL). */
+int hpc_weight_info(hpc_weight handle, int *type_id, size_t *input_size, size_t *row_count,
+                    size_t *device_bytes);
+
+/* Dequantize the resident weight to f32 [row_count][input_size], bit-exact
+ * to dequantize_q4_k / dequantize_q6_k (lib.rs:1630-1664, 1709-1744). */
+int hpc_weight_dequantize(hpc_weight handle, float *d_out, size_t out_len, void *stream);
+
+/* Q8_K activation quantization of `column_count` columns, bit-exact to
+ * quantize_q8_k (lib.rs:1774-1811): d_d[col*(K/256)], d_qs[col*K] (natural
+ * element order), d_bsums[col*(K/32)]. */
+int hpc_quantize_q8_k(const float *d_in, size_t in_len, size_t input_size, size_t column_count, float *d_d,
+                      int8_t *d_qs, int16_t *d_bsums, void *stream);
+
+/* Resident GEMV / small-M matmul with Q8_K activations.
+ * Replaces hp_matmul_quantized_prepared_f32 (lib.rs:225-298) as called by
+ * matMulQuantizedWasmResident (wasm-kernels.ts:593-646); same validation
+ * order and codes.  column_count may be any value >= 1 (processed 8 columns
+ * per pass). */
+int hpc_matmul_quantized_prepared_f32(hpc_weight handle, const float *d_in, size_t in_len, size_t input_size,
+                                      size_t row_count, size_t column_count, float *d_out, size_t out_len,
+                                      void *stream);
+
+/* Several resident weights sharing one input, in ONE launch; the input is
+ * quantized once.  Replaces hp_matmul_quantized_prepared_multi_f32
+ * (lib.rs:302-426) via matMulQuantizedWasmResidentMulti
+ * (wasm-kernels.ts:648-749); count is 1..8 here (the reference caps at 4). */
+int hpc_matmul_quantized_prepared_multi_f32(size_t count, const float *d_in, size_t in_len, size_t input_size,
+                                            size_t column_count, const hpc_weight *handles, float *const *d_outs,
+                                            const size_t *out_lens, void *stream);
+
+/* One-shot matmul on HOST buffers: upload, repack, quantize, multiply,
+ * download, release.  Replaces hp_matmul_quantized_f32 (lib.rs:41-100) as
+ * called by matMulQuantizedWasm (wasm-kernels.ts:416-466).  Synchronous. */
+int hpc_matmul_quantized_f32(int type_id, const uint8_t *host_weight, size_t weight_len, const float *host_in,
+                             size_t in_len, size_t input_size, size_t row_count, size_t column_count,
+                             float *host_out, size_t out_len);
+
+/* ---- caller-provided scratch ("workspace") variants ----------------------
+ * The activation is quantized once into a workspace the caller allocates
+ * (no allocation inside the call, so these can be captured in a CUDA graph),
+ * then any number of resident weights consume it.  They split
+ * matMulQuantizedWasmResident(Multi) into its two phases: quantize_q8_k
+ * (lib.rs:1774) and the per-row dots (lib.rs:264-296). */
+
+/* Workspace bytes for `column_count` columns of `input_size`. */
+int hpc_q8_workspace_bytes(size_t input_size, size_t column_count, size_t *out_bytes);
+
+/* Quantize f32 columns into the workspace (Q8_K, bit-exact to lib.rs:1774). */
+int hpc_q8_quantize(const float *d_in, size_t in_len, size_t input_size, size_t column_count, void *d_workspace,
+                    size_t workspace_bytes, void *stream);
+
+/* Multiply `count` (1..8) resident weights against a quantized workspace in
+ * one launch per 8 columns; outputs as hpc_matmul_quantized_prepared_multi_f32. */
+int hpc_matmul_q8(size_t count, const hpc_weight *handles, const void *d_workspace, size_t workspace_bytes,
+                  size_t input_size, size_t column_count, float *const *d_outs, const size_t *out_lens, void *stream);
+
+/* ---- LM head with on-GPU top-k --------------------------------------------
+ * Ordering everywhere: value descending, then vocabulary id ascending
+ * (topK, runtime.ts:514-527; betterValue in TOPK_CHUNK_CANDIDATES_WGSL,
+ * runner/webgpu/shaders.ts:1591-1650).  k is 1..64 (TOPK_MAX,
+ * runner/webgpu/dispatch.ts:906).  Values are the raw logits, or
+ * fround(tanh(v/cap)*cap) when softcap > 0, applied after selection as
+ * mergeTopCandidates does (runner/webgpu/segment-runner.ts:3773-3794). */
+
+/* Fused Q6_K/Q4_K LM head + top-k on f32 hidden columns (already normed):
+ * ids/vals are [column_count][k].  Replaces dispatchOutputTopK
+ * (runner/webgpu/segment-runner.ts:3208-3248) and the WASM forwardOutput
+ * logits + topK (runner/wasm/layers.ts:381-416).  id_offset is the vocabulary
+ * id of the handle's row 0 (row-sharded heads). */
+int hpc_lm_head_topk(hpc_weight lm_head, const float *d_hidden, size_t hidden_len, size_t input_size,
+                     size_t column_count, size_t k, int32_t id_offset, float softcap, int32_t *d_ids, float *d_vals,
+                     void *stream);
+
+/* Candidate-buffer bytes for hpc_lm_head_topk_q8. */
+int hpc_lm_head_candidates_bytes(hpc_weight lm_head, size_t column_count, size_t k, size_t *out_bytes);
+
+/* Same on a quantized workspace (hpc_q8_quantize), with a caller-provided
+ * candidate buffer; also writes the selected 64-bit keys
+ * (orderable(value) << 32 | 0xFFFFFFFF - id) when d_keys != NULL, which is
+ * what a row-sharded head all-gathers before hpc_topk_merge_keys. */
+int hpc_lm_head_topk_q8(hpc_weight lm_head, const void *d_workspace, size_t workspace_bytes, size_t input_size,
+                        size_t column_count, size_t k, int32_t id_offset, void *d_candidates, size_t candidates_bytes,
+                        float softcap, int32_t *d_ids, float *d_vals, uint64_t *d_keys, void *stream);
+
+/* Merge gathered keys laid out [group_count][column_count][k] into the
+ * global top-k per column (the cross-GPU merge of a row-sharded LM head). */
+int hpc_topk_merge_keys(const uint64_t *d_keys, size_t group_count, size_t column_count, size_t k, float softcap,
+                        int32_t *d_ids, float *d_vals, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* HELIOCUDA_H */
