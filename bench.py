@@ -7,6 +7,11 @@ runs its own replica/shard and the reported time is the max over ranks.
 
 Workloads (a "step" is one pass of the hot path over one batch of synthetic
 input, inputs resident in HBM when the timed region starts):
+  decode-config3 (default) one decode token of the BASELINE config-3 model
+                 (35 layers, hidden 2048, Q4_K_M mix, fp32 KV at context 4096,
+                 Q6_K LM head 2048 -> 262,144 with top-40): 3.357 GB of weights
+                 and KV per token, far above the 126 MB L2, so every step
+                 streams from HBM.  Also reports the M=5 batched verify.
   gemv-config1   one Q4_K GEMV, K=2048 -> N=16384, M=1 (BASELINE config 1);
                  rotates 8 weight copies (151 MB > 126 MB L2) so every step
                  streams its weights from HBM.
@@ -60,7 +65,7 @@ class ClockSampler:
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
-                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                          "--format=csv,noheader,nounits", "-lms", "20"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
@@ -157,6 +162,27 @@ class GemvConfig1:
     def units_per_step(self) -> float:
         return self.algo_bytes / 1e9  # GB per step
 
+    def kernel_launch_count(self) -> int:
+        return self.launches_per_step
+
+    def roofline(self, peak_gbs: float) -> dict:
+        C, L, hk, torch = self.C, self.L, self.hk, self.torch
+        launches = []
+        for h in self.handles:
+            def f(h=h):
+                hs = (C.c_void_p * 1)(h.handle)
+                outs = (C.c_void_p * 1)(self.out.data_ptr())
+                lens = (C.c_size_t * 1)(self.out.numel())
+                hk.assert_cuda_ok(L.hpc_matmul_q8(1, hs, C.c_void_p(self.ws.data_ptr()), self.ws_bytes, self.K,
+                                                  self.M, outs, lens,
+                                                  C.c_void_p(torch.cuda.current_stream().cuda_stream)), "gemv")
+            launches.append(f)
+        ms = graph_launch_times(launches * 2)
+        achieved = self.algo_bytes / (ms / 1e3) / 1e9
+        return {"bound": "hbm", "achieved": achieved, "peak": peak_gbs, "unit": "GB/s", "frac": achieved / peak_gbs,
+                "traffic": None, "kernel": "gemv_kernel<1> (Q4_K 2048 -> 16384, M=1)",
+                "algorithmic_bytes_per_launch": self.algo_bytes, "launch_ms": ms}
+
     unit = "GB/s"
     dtype = "u8"
 
@@ -184,7 +210,196 @@ class GemvConfig1:
                                           f"rows split over {threads} threads like the WASM pool)"}
 
 
-WORKLOADS = {"gemv-config1": GemvConfig1}
+def graph_launch_times(launches, reps: int = 3) -> float:
+    """Average device time (ms) of each callable in `launches`, measured with
+    external CUDA events captured around every launch inside one CUDA graph
+    (so the times exclude host launch overhead)."""
+    import torch
+    n = len(launches)
+    evs = [(torch.cuda.Event(enable_timing=True, external=True), torch.cuda.Event(enable_timing=True, external=True))
+           for _ in range(n)]
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s):
+        for f in launches:
+            f()
+        torch.cuda.synchronize()
+        with torch.cuda.graph(g, stream=s):
+            for (a, b), f in zip(evs, launches):
+                a.record()
+                f()
+                b.record()
+    torch.cuda.current_stream().wait_stream(s)
+    times = []
+    for _ in range(reps):
+        g.replay()
+        torch.cuda.synchronize()
+        times.append(statistics.mean(a.elapsed_time(b) for a, b in evs))
+    del g
+    return min(times)
+
+
+class DecodeConfig3:
+    """one decode token at position 4095 (KV context 4096)."""
+    name = "decode-config3"
+    unit = "tok/s"
+    dtype = "u8/int32 (Q4_K/Q6_K x Q8_K), f32 decoder math"
+    position = 4095
+    k = 40
+
+    def __init__(self):
+        import torch
+
+        from heliopause_b200 import synthetic as syn
+        from heliopause_b200.model import CONFIG3, W_GATE, W_UP, CudaDecoderModel
+        self.torch, self.syn = torch, syn
+        self.shape = CONFIG3
+        self.model = CudaDecoderModel(CONFIG3, max_tokens=8, top_k=64)
+        self.model.load_gpu_synthetic(seed=1)
+        self.model.fill_kv_random(self.position, seed=3)
+        self.ids = torch.tensor([12345], dtype=torch.int32, device="cuda")
+        self.pos = torch.tensor([self.position], dtype=torch.int32, device="cuda")
+        self.vids = torch.tensor([12345, 7, 70000, 99, 4242], dtype=torch.int32, device="cuda")
+        self.vpos = torch.tensor([self.position - 4 + i for i in range(5)], dtype=torch.int32, device="cuda")
+        self.step_bytes = CONFIG3.weight_bytes() + CONFIG3.kv_read_bytes(self.position)
+        self.launches_per_step = None
+        self.W_GATE, self.W_UP = W_GATE, W_UP
+        torch.cuda.synchronize()
+
+    def step(self, ev=None):
+        self.model.forward(self.ids, self.pos, self.k)
+
+    def verify_step(self):
+        self.model.forward(self.vids, self.vpos, self.k)
+
+    def e2e_step(self, host_ids):
+        """Public API with host buffers: token id in, top-k ids/values out."""
+        ids, vals = self.model.forward(host_ids, [self.position], self.k)
+        ids.cpu()
+        vals.cpu()
+
+    def units_per_step(self) -> float:
+        return 1.0
+
+    def kernel_launch_count(self) -> int:
+        s = self.shape
+        per_layer = 10  # norm, QKV, qk/rope/kv, attention, combine, O, norm, gate/up, geglu, down
+        return 2 + s.layers * per_layer + 1 + 2  # rope table + embed ... final norm + LM head + merge
+
+    def roofline(self, peak_gbs: float) -> dict:
+        """Dominant kernel: the gate/up GEMV (39% of the step's bytes), timed
+        per launch over the model's 35 layers in one CUDA graph."""
+        import ctypes as C
+
+        from heliopause_b200 import _lib
+        from heliopause_b200 import kernels as hk
+        torch = self.torch
+        L = _lib.lib()
+        s = self.shape
+        nbytes = C.c_size_t()
+        L.hpc_q8_workspace_bytes(s.hidden, 1, C.byref(nbytes))
+        ws = torch.zeros(nbytes.value, dtype=torch.uint8, device="cuda")
+        x = torch.randn(s.hidden, device="cuda")
+        hk.assert_cuda_ok(L.hpc_q8_quantize(C.c_void_p(x.data_ptr()), s.hidden, s.hidden, 1, C.c_void_p(ws.data_ptr()),
+                                            nbytes.value, C.c_void_p(torch.cuda.current_stream().cuda_stream)), "q8")
+        g = torch.empty(s.ffn, device="cuda")
+        u = torch.empty(s.ffn, device="cuda")
+        launches = []
+        for layer in range(s.layers):
+            hg = self.model.weight_handles[(layer, self.W_GATE)]
+            hu = self.model.weight_handles[(layer, self.W_UP)]
+
+            def f(hg=hg, hu=hu):
+                hs = (C.c_void_p * 2)(hg.handle, hu.handle)
+                outs = (C.c_void_p * 2)(g.data_ptr(), u.data_ptr())
+                lens = (C.c_size_t * 2)(s.ffn, s.ffn)
+                hk.assert_cuda_ok(L.hpc_matmul_q8(2, hs, C.c_void_p(ws.data_ptr()), nbytes.value, s.hidden, 1, outs,
+                                                  lens, C.c_void_p(torch.cuda.current_stream().cuda_stream)), "gemv")
+            launches.append(f)
+        ms = graph_launch_times(launches)
+        algo = 2 * self.syn.row_bytes(self.syn.Q4_K, s.hidden) * s.ffn + 4 * s.hidden + 8 * s.ffn
+        achieved = algo / (ms / 1e3) / 1e9
+        return {"bound": "hbm", "achieved": achieved, "peak": peak_gbs, "unit": "GB/s", "frac": achieved / peak_gbs,
+                "traffic": None, "kernel": "gemv_kernel<1> (ffn gate+up, 2048 -> 2x16384 Q4_K, M=1)",
+                "algorithmic_bytes_per_launch": algo, "launch_ms": ms}
+
+    def config(self) -> dict:
+        s = self.shape
+        return {"workload": "decode one token, E4B-shaped Q4_K_M decoder (BASELINE config 3)",
+                "layers": s.layers, "hidden": s.hidden, "heads": s.heads, "kv_heads": s.kv_heads,
+                "head_dim": s.head_dim, "ffn": s.ffn, "vocab": s.vocab, "kv_layers": s.kv_layers,
+                "context": s.context, "position": self.position, "top_k": self.k, "kv_dtype": "f32",
+                "bytes_per_token": self.step_bytes,
+                "l2": f"inputs larger than L2: {self.step_bytes / 1e9:.2f} GB of weights+KV streamed per step"}
+
+    @classmethod
+    def cpu_sampler(cls, threads: int):
+        return CpuDecodeSample(threads, cls.position, cls.k)
+
+    def cpu_baseline(self, budget_s: float, threads: int) -> dict:
+        return cpu_baseline_from(self.cpu_sampler(threads), budget_s)
+
+
+class CpuDecodeSample:
+    """The C restatement of the WASM decode path on the host cores: a bounded
+    sample of 2 full decoder layers at context 4096 (one writing KV) plus the
+    262,144-row LM head and top-40, scaled to the model's 35 layers."""
+
+    def __init__(self, threads: int, position: int, k: int):
+        from heliopause_b200.model import CONFIG3, SyntheticWeights
+        from oracle.decoder_oracle import OracleDecoder
+        self.s = CONFIG3
+        self.threads, self.position, self.k = threads, position, k
+        self.w = SyntheticWeights(CONFIG3, seed=1)
+        self.ref = OracleDecoder(CONFIG3, self.w, threads=threads)
+        kc, vc = self.w.kv(0, position)
+        self.ref.set_kv(0, kc, vc)
+        self.ref.set_kv(1, kc.copy(), vc.copy())
+        self.x0 = self.ref.embed([12345])
+        self.ref._lm_head()
+        self.ref._weight(0, 0)
+
+    def run(self) -> tuple[float, float]:
+        """Seconds for (2 layers, LM head + top-k)."""
+        from oracle import oracle as o
+        s = self.s
+        t0 = time.perf_counter()
+        x = self.x0
+        for layer in (0, 1):
+            x = self.ref.layer(layer, x, [self.position])
+        t_layers = time.perf_counter() - t0
+        data, scales = self.ref._lm_head()
+        norm = o.rms_norm_rows(x, self.w.output_norm(), s.rms_eps)
+        t1 = time.perf_counter()
+        logits = o.matmul_prepared(o.Q6_K, data, scales, norm, s.hidden, s.vocab, 1, threads=self.threads)
+        o.topk(logits, self.k)
+        return t_layers, time.perf_counter() - t1
+
+    def per_token(self, t_layers: float, t_head: float) -> float:
+        return t_layers / 2 * self.s.layers + t_head
+
+    def describe(self, t_layers: float, t_head: float) -> str:
+        return (f"2 decoder layers at context {self.s.context} ({t_layers:.2f} s) + LM head/top-{self.k} "
+                f"({t_head:.2f} s) of the C restatement of the WASM path on {self.threads} threads, "
+                f"scaled to {self.s.layers} layers")
+
+
+def cpu_baseline_from(sampler, budget_s: float) -> dict:
+    sampler.run()  # warm
+    t0 = time.perf_counter()
+    runs = []
+    while True:
+        runs.append(sampler.run())
+        if time.perf_counter() - t0 >= budget_s:
+            break
+    tl = statistics.median(r[0] for r in runs)
+    th = statistics.median(r[1] for r in runs)
+    return {"value": 1.0 / sampler.per_token(tl, th), "unit": "tok/s", "cores": sampler.threads, "kind": "port",
+            "sample": f"{len(runs)} x (" + sampler.describe(tl, th) + ")"}
+
+
+WORKLOADS = {"decode-config3": DecodeConfig3, "gemv-config1": GemvConfig1}
 
 
 # ------------------------------------------------------------------- main ---
@@ -197,46 +412,58 @@ def _dist():
 
 
 def run_reference(args, world, rank):
-    """CPU reference arm (rank 0 only)."""
+    """CPU reference arm (rank 0 only): the C restatement of the reference's
+    WASM path (the reference itself cannot run here) on all host threads."""
     if rank != 0:
         return
-    wl_cls = WORKLOADS[args.workload]
-    threads = os.cpu_count() or 1
-    try:
-        threads = len(os.sched_getaffinity(0))
-    except AttributeError:
-        pass
-    wl = wl_cls.__new__(wl_cls)
-    import heliopause_b200.synthetic as syn
-    wl.syn = syn
-    wl.w_bytes = syn.row_bytes(syn.Q4_K, wl.K) * wl.N
-    wl.algo_bytes = wl.w_bytes + 4 * wl.K * wl.M + 4 * wl.N * wl.M
-    budget = max(2.0, 60.0 / max(1, args.steps + args.warmup))
-    for _ in range(args.warmup):
-        wl.cpu_baseline(0.0, threads)
-    vals = []
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        vals.append(wl.cpu_baseline(budget, threads))
-    elapsed = time.perf_counter() - t0
-    v = statistics.median(x["value"] for x in vals)
-    cb = dict(vals[-1])
-    cb["value"] = v
-    line = {"metric": METRIC, "value": v, "unit": wl.unit, "impl": "reference", "n_gpus": args.gpus,
+    threads = len(os.sched_getaffinity(0))
+    if args.workload == "decode-config3":
+        sampler = DecodeConfig3.cpu_sampler(threads)
+        for _ in range(args.warmup):
+            sampler.run()
+        t0 = time.perf_counter()
+        runs = [sampler.run() for _ in range(args.steps)]
+        elapsed = time.perf_counter() - t0
+        tl = statistics.median(r[0] for r in runs)
+        th = statistics.median(r[1] for r in runs)
+        v = 1.0 / sampler.per_token(tl, th)
+        cfg = {"workload": "decode one token, E4B-shaped Q4_K_M decoder (BASELINE config 3)", "context": 4096,
+               "position": DecodeConfig3.position, "top_k": DecodeConfig3.k}
+        cb = {"value": v, "unit": "tok/s", "cores": threads, "kind": "port",
+              "sample": "each step: " + sampler.describe(tl, th)}
+        unit, dtype = "tok/s", DecodeConfig3.dtype
+    else:
+        wl = GemvConfig1.__new__(GemvConfig1)
+        import heliopause_b200.synthetic as syn
+        wl.syn = syn
+        wl.w_bytes = syn.row_bytes(syn.Q4_K, wl.K) * wl.N
+        wl.algo_bytes = wl.w_bytes + 4 * wl.K * wl.M + 4 * wl.N * wl.M
+        budget = max(1.0, 60.0 / max(1, args.steps + args.warmup))
+        for _ in range(args.warmup):
+            wl.cpu_baseline(0.0, threads)
+        t0 = time.perf_counter()
+        vals = [wl.cpu_baseline(budget, threads) for _ in range(args.steps)]
+        elapsed = time.perf_counter() - t0
+        v = statistics.median(x["value"] for x in vals)
+        cb = dict(vals[-1])
+        cb["value"] = v
+        cfg = wl.config()
+        unit, dtype = wl.unit, wl.dtype
+    line = {"metric": METRIC, "value": v, "unit": unit, "impl": "reference", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": elapsed * 1e3 / max(1, args.steps),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": wl.dtype,
-            "data": "synthetic (seeded PCG64, BASELINE distributions)", "config": wl.config(),
-            "cpu_baseline": cb, "e2e": {"value": v, "unit": wl.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": dtype,
+            "data": "synthetic (seeded, BASELINE distributions)", "config": cfg, "cpu_baseline": cb,
+            "e2e": {"value": v, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="gemv-config1")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="decode-config3")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
@@ -263,50 +490,59 @@ def main():
         if world > 1:
             dist.barrier()
 
-    for _ in range(args.warmup):
-        wl.step()
-    torch.cuda.synchronize()
-    barrier()
-    torch.cuda.synchronize()
-
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
-    with ClockSampler(local) as clk:
-        start.record()
-        for i in range(args.steps):
-            wl.step(kev[i])
-        end.record()
+    def timed(fn, steps):
+        for _ in range(args.warmup):
+            fn()
         torch.cuda.synchronize()
-    barrier()
-    torch.cuda.synchronize()
-    ms = start.elapsed_time(end) / args.steps
-    kern_ms = statistics.mean(a.elapsed_time(b) for a, b in kev)
-    t = torch.tensor([ms, kern_ms], device="cuda", dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms, kern_ms = float(t[0]), float(t[1])
+        barrier()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(steps):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        t = torch.tensor([a.elapsed_time(b) / steps], device="cuda", dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t[0])
+
+    with ClockSampler(local) as clk:
+        ms = timed(wl.step, args.steps)
     value = wl.units_per_step() * world / (ms / 1e3)
 
-    # end to end through the public API with host buffers (pinned input)
-    host_x = torch.from_numpy(wl.syn.activations(wl.M, wl.K, seed=7)).pin_memory()
+    verify = None
+    if hasattr(wl, "verify_step"):
+        vms = timed(wl.verify_step, max(5, args.steps // 2))
+        verify = {"m": 5, "ms_per_step": vms, "positions_per_s": 5 * world / (vms / 1e3),
+                  "note": "one batched forward over 5 positions (MTP verify width), top-40 per position"}
+
+    # end to end through the public API with host buffers
+    if args.workload == "decode-config3":
+        host_in = torch.tensor([12345], dtype=torch.int32).pin_memory()
+        h2d, d2h = 8, 8 * wl.k
+    else:
+        host_in = torch.from_numpy(wl.syn.activations(wl.M, wl.K, seed=7)).pin_memory()
+        h2d, d2h = 4 * wl.K * wl.M, 4 * wl.N * wl.M
     for _ in range(3):
-        wl.e2e_step(host_x)
+        wl.e2e_step(host_in)
     torch.cuda.synchronize()
     barrier()
     t0 = time.perf_counter()
-    for _ in range(args.steps):
-        wl.e2e_step(host_x)
+    n_e2e = max(5, args.steps // 2)
+    for _ in range(n_e2e):
+        wl.e2e_step(host_in)
     torch.cuda.synchronize()
-    e2e_s = torch.tensor([(time.perf_counter() - t0) / args.steps], device="cuda", dtype=torch.float64)
+    e2e_s = torch.tensor([(time.perf_counter() - t0) / n_e2e], device="cuda", dtype=torch.float64)
     if world > 1:
         dist.all_reduce(e2e_s, op=dist.ReduceOp.MAX)
     e2e_value = wl.units_per_step() * world / float(e2e_s[0])
 
     peaks = _peaks()
-    achieved = wl.algo_bytes / (kern_ms / 1e3) / 1e9
-    roofline = {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                "frac": achieved / peaks["hbm_gbs"], "traffic": None,
-                "kernel": "gemv_kernel<1>", "peak_source": peaks["source"]}
+    roofline = wl.roofline(peaks["hbm_gbs"])
+    roofline["peak_source"] = peaks["source"]
     prof = ROOT / "profiles" / "traffic.json"
     if prof.exists():
         tr = json.loads(prof.read_text()).get(wl.name)
@@ -321,11 +557,16 @@ def main():
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": wl.unit, "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-                "vs_baseline": None, "dtype": wl.dtype, "data": "synthetic (seeded PCG64, BASELINE distributions)",
+                "vs_baseline": None, "dtype": wl.dtype, "data": "synthetic (seeded, BASELINE distributions)",
                 "config": wl.config(), "roofline": roofline, "cpu_baseline": cpu,
-                "e2e": {"value": e2e_value, "unit": wl.unit, "h2d_bytes_per_step": 4 * wl.K * wl.M,
-                        "d2h_bytes_per_step": 4 * wl.N * wl.M},
-                "gpu_launches": wl.launches_per_step * args.steps, "clocks": clk.summary()}
+                "e2e": {"value": e2e_value, "unit": wl.unit, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+                "gpu_launches": wl.kernel_launch_count() * args.steps, "clocks": clk.summary()}
+        if hasattr(wl, "step_bytes"):
+            line["step_hbm"] = {"bytes_per_step": wl.step_bytes,
+                                "achieved_gbs": wl.step_bytes / (ms / 1e3) / 1e9,
+                                "frac_of_peak": wl.step_bytes / (ms / 1e3) / 1e9 / peaks["hbm_gbs"]}
+        if verify:
+            line["verify"] = verify
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()

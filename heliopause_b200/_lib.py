@@ -40,7 +40,22 @@ SIGNATURES = {
     "hpc_lm_head_candidates_bytes": (_i, [_vp, _sz, _sz, C.POINTER(_sz)]),
     "hpc_lm_head_topk_q8": (_i, [_vp, _vp, _sz, _sz, _sz, _sz, C.c_int32, _vp, _sz, C.c_float, _vp, _vp, _vp, _vp]),
     "hpc_topk_merge_keys": (_i, [_vp, _sz, _sz, _sz, C.c_float, _vp, _vp, _vp]),
+    "hpc_model_create": (_i, [_vp, C.POINTER(_vp)]),
+    "hpc_model_release": (_i, [_vp]),
+    "hpc_model_set_weight": (_i, [_vp, _i, _i, _vp]),
+    "hpc_model_set_norm": (_i, [_vp, _i, _i, _vp, _sz]),
+    "hpc_model_set_lm_head": (_i, [_vp, _vp]),
+    "hpc_model_kv": (_i, [_vp, _i, C.POINTER(_vp), C.POINTER(_vp)]),
+    "hpc_model_forward": (_i, [_vp, _vp, _vp, _sz, _sz, _vp, _vp, _vp, _vp]),
 }
+
+
+class ModelConfig(C.Structure):
+    """hpc_model_config (include/heliocuda.h)."""
+    _fields_ = [("hidden", C.c_int), ("heads", C.c_int), ("kv_heads", C.c_int), ("head_dim", C.c_int),
+                ("ffn", C.c_int), ("vocab", C.c_int), ("layers", C.c_int), ("kv_layers", C.c_int),
+                ("context", C.c_int), ("max_tokens", C.c_int), ("top_k", C.c_int), ("rms_eps", C.c_double),
+                ("rope_theta", C.c_double), ("final_logit_softcap", C.c_float)]
 
 _lib = None
 

@@ -15,16 +15,13 @@
 
 #include "../../include/heliocuda.h"
 #include "hc_common.cuh"
+#include "hc_internal.h"
 #include "hc_kernels.cuh"
 #include "hc_lmhead.cuh"
 
-namespace {
-
 thread_local std::string g_last_error;
 
-constexpr uint32_t kWeightMagic = 0x48504357u;  // "HPCW"
-
-int fail(int code, const char* fmt, ...) {
+int hpc_fail(int code, const char* fmt, ...) {
   char buf[512];
   va_list ap;
   va_start(ap, fmt);
@@ -34,15 +31,14 @@ int fail(int code, const char* fmt, ...) {
   return code;
 }
 
-int cuda_fail(cudaError_t e, const char* what) {
-  return fail(HPC_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+int hpc_cuda_fail(cudaError_t e, const char* what) {
+  return hpc_fail(HPC_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
 }
 
-#define HPC_CK(call, what)                       \
-  do {                                           \
-    cudaError_t e_ = (call);                     \
-    if (e_ != cudaSuccess) return cuda_fail(e_, what); \
-  } while (0)
+namespace {
+
+int (*const fail)(int, const char*, ...) = hpc_fail;
+int (*const cuda_fail)(cudaError_t, const char*) = hpc_cuda_fail;
 
 bool supported_type(int t) { return t == HPC_TYPE_Q4_K || t == HPC_TYPE_Q6_K; }
 
@@ -67,19 +63,7 @@ bool mul_overflows(size_t a, size_t b, size_t* out) {
 
 }  // namespace
 
-struct hpc_weight_s {
-  uint32_t magic;
-  int type;
-  int device;
-  size_t input_size;
-  size_t row_count;
-  size_t rows_pad;
-  int nb;
-  uint8_t* d_data;
-  size_t bytes;
-};
-
-static bool valid(const hpc_weight_s* h) { return h && h->magic == kWeightMagic && h->d_data; }
+static bool valid(const hpc_weight_s* h) { return hpc_weight_valid(h); }
 
 // One status word per device for bounded-wait timeouts inside kernels.
 static __device__ int g_status_word;

@@ -1,0 +1,564 @@
+// hc_decode.cu -- the per-layer decoder math around the quantized matmuls.
+//
+// Restates forwardAttentionLayer / forwardFfn / forwardOutput of the WASM
+// provider (packages/engine/src/runner/wasm/layers.ts:161-473) as CUDA
+// kernels.  The reference computes in JavaScript numbers (f64) and rounds to
+// f32 at stores and Math.fround; the kernels keep those rounding points:
+//   * RMSNorm (layers.ts:871-885): f64 sum of squares, f64 scale
+//     1/sqrt(ss/n + eps), product x*scale*w in f64, stored as f32;
+//   * RoPE NeoX (layers.ts:990-1033): theta chain fround(theta*base^(-2/n)),
+//     cos/sin in f64, each product rounded to f32;
+//   * attention (lib.rs:539-654 via layers.ts:304-334): query rounded to f16
+//     with the Rust codec, scale 1, causal mask, f64 exp; the output is cast
+//     through the TS f16 codec (castF16Rows, layers.ts:982-988);
+//   * GEGLU (layers.ts:450-456, gelu 1062-1076): tanh-GELU with f16 round
+//     trips of its input and output, product rounded to f32.
+// Parallel reductions (sums of squares, dot products, softmax across KV
+// chunks) run in a different order than the reference's sequential loops, so
+// results agree to f32/f64 rounding, not bit for bit.
+//
+// Every kernel is launched with programmatic dependent launch: it signals its
+// dependents early and waits (griddepcontrol.wait) before touching memory the
+// previous kernel writes.
+#include <cmath>
+#include <utility>
+
+#include <cuda_fp16.h>
+
+#include "hc_common.cuh"
+#include "hc_decode.cuh"
+#include "hc_q8.cuh"
+#include "hc_unpack.cuh"
+
+namespace hc {
+
+__device__ __forceinline__ void pdl_trigger() {
+#if __CUDA_ARCH__ >= 900
+  asm volatile("griddepcontrol.launch_dependents;");
+#endif
+}
+__device__ __forceinline__ void pdl_wait() {
+#if __CUDA_ARCH__ >= 900
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+#endif
+}
+
+// ---- f16 codecs ---------------------------------------------------------------
+
+// quant.ts:632-669 float32ToFloat16 (the TS codec used by layers.ts): round
+// to nearest even, |x| >= 65504 clamps to 65504, |x| < 2^-24 flushes to zero.
+__device__ __forceinline__ float round_f16_ts(float x) {
+  const float a = fabsf(x);
+  if (x != x) return x;
+  if (a >= 65504.0f) return a == INFINITY ? x : copysignf(65504.0f, x);
+  if (a < 5.9604644775390625e-8f) return copysignf(0.0f, x);
+  return __half2float(__float2half_rn(x));
+}
+
+// lib.rs:2534-2568 float32_to_float16 (the Rust codec used for the attention
+// query, lib.rs:590-597): the dropped bits round half UP, overflow clamps to
+// 0x7bff, NaN -> 0x7e00.  Returns the f16 value widened back to f32.
+__device__ __forceinline__ float round_f16_rust(float v) {
+  const uint32_t bits = __float_as_uint(v);
+  const uint32_t sign = (bits >> 16) & 0x8000u;
+  const int exp = int((bits >> 23) & 0xff);
+  const uint32_t mant = bits & 0x7fffffu;
+  uint32_t h;
+  if (exp == 0xff) {
+    h = mant == 0 ? (sign | 0x7c00u) : 0x7e00u;
+  } else {
+    const int he = exp - 127 + 15;
+    if (he >= 31) {
+      h = sign | 0x7bffu;
+    } else if (he <= 0) {
+      if (he < -10) {
+        h = sign;
+      } else {
+        const uint32_t m = mant | 0x800000u;
+        const uint32_t shift = uint32_t(14 - he);
+        h = sign | ((m + (1u << (shift - 1))) >> shift);
+      }
+    } else {
+      const uint32_t rm = mant + 0x1000u;
+      if (rm & 0x800000u) {
+        const int re = he + 1;
+        h = re >= 31 ? (sign | 0x7bffu) : (sign | uint32_t(re << 10));
+      } else {
+        h = sign | uint32_t(he << 10) | (rm >> 13);
+      }
+    }
+  }
+  return f16_bits_to_f32(h);
+}
+
+// ---- block reductions -----------------------------------------------------------
+
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+  return v;
+}
+
+// Sum over a CTA of `warps` warps (all threads call it).
+__device__ __forceinline__ double block_sum_d(double v, double* scratch, int warps) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  v = warp_sum_d(v);
+  __syncthreads();
+  if (lane == 0) scratch[warp] = v;
+  __syncthreads();
+  double t = 0.0;
+  for (int w = 0; w < warps; ++w) t += scratch[w];
+  return t;
+}
+
+// ---- RoPE table -------------------------------------------------------------------
+
+// cos/sin of the NeoX RoPE angles for each token (layers.ts:1012-1030):
+// theta_0 = position, theta_{i+1} = fround(theta_i * base^(-2/ndims)); the
+// chain is serial (one thread), the cos/sin are parallel.  One CTA per token.
+__global__ void rope_table_kernel(const int32_t* __restrict__ pos, int half, double theta_scale,
+                                  double* __restrict__ cos_t, double* __restrict__ sin_t) {
+  __shared__ double theta[512];
+  pdl_trigger();
+  pdl_wait();
+  const int m = blockIdx.x;
+  if (threadIdx.x == 0) {
+    double th = double(pos[m]);
+    for (int i = 0; i < half; ++i) {
+      theta[i] = th;
+      th = double(float(th * theta_scale));
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < half; i += blockDim.x) {
+    cos_t[size_t(m) * half + i] = cos(theta[i]);
+    sin_t[size_t(m) * half + i] = sin(theta[i]);
+  }
+}
+
+// ---- embedding --------------------------------------------------------------------
+
+// Dequantizes element e of row `row` from the tile layout (bit-exact to
+// dequantize_q6_k / dequantize_q4_k, lib.rs:1709-1744 / 1630-1664).
+__device__ __forceinline__ float tile_elem(const uint8_t* w, int type, int nb, int row, int e) {
+  const int b = e >> 8, r = e & 255, lane = row & 31;
+  if (type == TYPE_Q6_K) {
+    const uint8_t* unit = w + (size_t(row >> 5) * nb + b) * Q6K_TILE_BLOCK_BYTES;
+    const int s16 = r >> 4, within = r & 15;
+    const int j = (within & 7) >> 1, i = ((within >> 3) & 1) | ((within & 1) << 1);
+    const int s = s16 & 7, hi = s16 >> 3;
+    const uint8_t nb_byte = unit[size_t(s) * 512 + lane * 16 + j * 4 + i];
+    const int h = 2 * s + (j >> 1);
+    const uint8_t hw_byte = unit[size_t(8 + (h >> 2)) * 512 + lane * 16 + (h & 3) * 4 + i];
+    const uint32_t lo = hi ? (nb_byte >> 4) : (nb_byte & 15);
+    const uint32_t hb = (hw_byte >> (2 * (j & 1) + 4 * hi)) & 3;
+    const int q = int(lo | (hb << 4)) - 32;
+    const int sc = int(int8_t(unit[size_t(12) * 512 + lane * 16 + s16]));
+    const float d = f16_bits_to_f32(reinterpret_cast<const uint16_t*>(unit + Q6K_DPLANE_OFFSET)[lane]);
+    return __fmul_rn(__fmul_rn(d, float(sc)), float(q));
+  }
+  const uint8_t* unit = w + (size_t(row >> 5) * nb + b) * Q4K_TILE_BLOCK_BYTES;
+  const uint4 hv = *reinterpret_cast<const uint4*>(unit + lane * 16);
+  const Q4KHeader hd = q4k_header(hv);
+  const int p = r >> 6, within64 = r & 63, half = within64 >> 5, l8 = within64 & 31;
+  const int l = l8 & 7, i = l8 >> 3;
+  const uint8_t byte = unit[size_t(1 + 2 * p + (l >> 2)) * 512 + lane * 16 + (l & 3) * 4 + i];
+  const int g = 2 * p + half;
+  const uint32_t q = half ? (byte >> 4) : (byte & 15);
+  return __fsub_rn(__fmul_rn(__fmul_rn(hd.d, float(hd.sc(g))), float(q)), __fmul_rn(hd.dmin, float(hd.mn(g))));
+}
+
+// prepareInput (layers.ts:54-67): hidden = fround(embedding_row * sqrt(D)).
+__global__ void embed_kernel(const uint8_t* __restrict__ w, int type, int nb, int vocab, const int32_t* __restrict__ ids,
+                             float* __restrict__ hidden, int D, double scale, int* __restrict__ err) {
+  pdl_trigger();
+  pdl_wait();
+  const int m = blockIdx.x;
+  const int row = ids[m];
+  if (row < 0 || row >= vocab) {
+    if (threadIdx.x == 0 && err) atomicExch(err, 2);
+    return;
+  }
+  for (int e = threadIdx.x; e < D; e += blockDim.x)
+    hidden[size_t(m) * D + e] = float(double(tile_elem(w, type, nb, row, e)) * scale);
+}
+
+// ---- norms + quantize ----------------------------------------------------------------
+
+// One CTA of D/8 threads per column (thread t owns elements 8t..8t+7; warp w
+// owns 256-block w).  Mode RESID: h = x + rmsnorm(y, w_post) is written back
+// to x (the residual stream, layers.ts:359-363 / 471), then n = rmsnorm(h,
+// w_pre); otherwise n = rmsnorm(x, w_pre).  n is quantized to Q8_K for the
+// next matmul; if n_out != nullptr it is also stored as f32.
+template <bool RESID>
+__global__ void norm_quant_kernel(float* __restrict__ x, const float* __restrict__ y, const float* __restrict__ w_post,
+                                  const float* __restrict__ w_pre, double eps, int D, Q8Buf q,
+                                  float* __restrict__ n_out) {
+  __shared__ double scratch[32];
+  __shared__ __align__(16) uint8_t stage[32][256];
+  pdl_trigger();
+  pdl_wait();
+  const int m = blockIdx.x, t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const int warps = blockDim.x >> 5;
+  float h[8];
+  const float4* xp = reinterpret_cast<const float4*>(x + size_t(m) * D + 8 * t);
+  float4 a = xp[0], b = xp[1];
+  h[0] = a.x; h[1] = a.y; h[2] = a.z; h[3] = a.w; h[4] = b.x; h[5] = b.y; h[6] = b.z; h[7] = b.w;
+  if (RESID) {
+    const float4* yp = reinterpret_cast<const float4*>(y + size_t(m) * D + 8 * t);
+    const float4 c = yp[0], e = yp[1];
+    const float yv[8] = {c.x, c.y, c.z, c.w, e.x, e.y, e.z, e.w};
+    double ss = 0.0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) ss += double(yv[i]) * double(yv[i]);
+    ss = block_sum_d(ss, scratch, warps);
+    const double sc = 1.0 / sqrt(ss / double(D) + eps);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float pn = float((double(yv[i]) * sc) * double(w_post[8 * t + i]));
+      h[i] = h[i] + pn;
+    }
+    float4* xo = reinterpret_cast<float4*>(x + size_t(m) * D + 8 * t);
+    xo[0] = make_float4(h[0], h[1], h[2], h[3]);
+    xo[1] = make_float4(h[4], h[5], h[6], h[7]);
+  }
+  double ss = 0.0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) ss += double(h[i]) * double(h[i]);
+  ss = block_sum_d(ss, scratch, warps);
+  const double sc = 1.0 / sqrt(ss / double(D) + eps);
+  float n[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) n[i] = float((double(h[i]) * sc) * double(w_pre[8 * t + i]));
+  if (n_out) {
+    float4* no = reinterpret_cast<float4*>(n_out + size_t(m) * D + 8 * t);
+    no[0] = make_float4(n[0], n[1], n[2], n[3]);
+    no[1] = make_float4(n[4], n[5], n[6], n[7]);
+  }
+  q8k_block_warp(n, lane, stage[warp], q8_rec_a(q, m, warp), q8_rec_b(q, m, warp));
+}
+
+// ---- QK norm + RoPE + KV write ----------------------------------------------------
+
+// One CTA per token, one warp per head vector (HD = 256 values, 8 per lane):
+// warps [0, H) are query heads, [H, H + KVH) key heads, [H + KVH, H + 2 KVH)
+// value heads.  Query: normHeads + ropeNeox (layers.ts:201-224); key: same
+// with the key norm, then written to K[slot][kvh][:] (layers.ts:241-268);
+// value: rmsNormRowsNoWeight (layers.ts:248-253) written to V[:][kvh][slot]
+// (updateFullAttentionCache, layers.ts:887-911).
+__global__ void qkv_post_kernel(const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v,
+                                const float* __restrict__ qnw, const float* __restrict__ knw,
+                                const int32_t* __restrict__ pos, const double* __restrict__ cos_t,
+                                const double* __restrict__ sin_t, int H, int KVH, int cap, double eps, int has_kv,
+                                float* __restrict__ q_out, float* __restrict__ kc, float* __restrict__ vc) {
+  constexpr int HD = 256, HALF = 128;
+  pdl_trigger();
+  pdl_wait();
+  const int m = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int kind = warp < H ? 0 : (warp < H + KVH ? 1 : 2);
+  if (kind > 0 && !has_kv) return;
+  const int head = kind == 0 ? warp : (kind == 1 ? warp - H : warp - H - KVH);
+  const float* src = kind == 0 ? q + (size_t(m) * H + head) * HD : (kind == 1 ? k : v) + (size_t(m) * KVH + head) * HD;
+  float x[8];
+  {
+    const float4 a = reinterpret_cast<const float4*>(src + 8 * lane)[0];
+    const float4 b = reinterpret_cast<const float4*>(src + 8 * lane)[1];
+    x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w; x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+  }
+  double ss = 0.0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) ss += double(x[i]) * double(x[i]);
+  ss = warp_sum_d(ss);
+  const double sc = 1.0 / sqrt(ss / double(HD) + eps);
+  float n[8];
+  if (kind == 2) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) n[i] = float(double(x[i]) * sc);
+  } else {
+    const float* w = kind == 0 ? qnw : knw;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) n[i] = float((double(x[i]) * sc) * double(w[8 * lane + i]));
+    // RoPE NeoX: pair (i, i + 128) sits in lanes L and L + 16.
+    float partner[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) partner[i] = __shfl_xor_sync(0xffffffffu, n[i], 16);
+    const bool first = lane < 16;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int idx = (lane & 15) * 8 + i;  // pair index 0..127
+      const double c = cos_t[size_t(m) * HALF + idx], s = sin_t[size_t(m) * HALF + idx];
+      const double x0 = first ? n[i] : partner[i];
+      const double x1 = first ? partner[i] : n[i];
+      if (first) n[i] = float(x0 * c) - float(x1 * s);
+      else n[i] = float(x0 * s) + float(x1 * c);
+    }
+  }
+  if (kind == 0) {
+    float4* o = reinterpret_cast<float4*>(q_out + (size_t(m) * H + head) * HD + 8 * lane);
+    o[0] = make_float4(n[0], n[1], n[2], n[3]);
+    o[1] = make_float4(n[4], n[5], n[6], n[7]);
+  } else {
+    const int slot = pos[m] % cap;
+    if (kind == 1) {
+      float4* o = reinterpret_cast<float4*>(kc + (size_t(slot) * KVH + head) * HD + 8 * lane);
+      o[0] = make_float4(n[0], n[1], n[2], n[3]);
+      o[1] = make_float4(n[4], n[5], n[6], n[7]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) vc[(size_t(8 * lane + i) * KVH + head) * cap + slot] = n[i];
+    }
+  }
+}
+
+// ---- attention ------------------------------------------------------------------------
+
+// Split-KV decode attention (flash-decoding form of hp_gqa_attention_f32,
+// lib.rs:539-654, on the compacted full-attention range [0, pos+1)).  Grid
+// (chunks, KVH); a CTA loads one ATT_CHUNK-token slice of K and V for one KV
+// head into shared memory and serves all M tokens x (H/KVH) query heads of
+// that group: scores (f16-rounded query, scale 1, causal), a local softmax
+// (max, sum of f64 exp) and the partial output sum p*v.
+__global__ void __launch_bounds__(ATT_THREADS) attn_partial_kernel(
+    const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
+    const int32_t* __restrict__ pos, int M, int H, int KVH, int cap, float scale, float* __restrict__ part_m,
+    float* __restrict__ part_l, float* __restrict__ part_o) {
+  constexpr int HD = 256;
+  extern __shared__ __align__(16) float sm[];
+  const int chunk = blockIdx.x, kvh = blockIdx.y;
+  const int G = H / KVH, NQ = M * G;
+  float* ks = sm;                           // [ATT_CHUNK][HD]
+  float* vs = ks + ATT_CHUNK * HD;          // [HD][ATT_CHUNK + 1]
+  float* qs = vs + HD * (ATT_CHUNK + 1);    // [NQ][HD]
+  float* ps = qs + NQ * HD;                 // [NQ][ATT_CHUNK]
+  pdl_trigger();
+  pdl_wait();
+  int maxpos = 0;
+  for (int i = 0; i < M; ++i) maxpos = max(maxpos, pos[i]);
+  const int count = min(cap, maxpos + 1);
+  const int t0 = chunk * ATT_CHUNK;
+  if (t0 >= count) return;
+  const int nt = min(ATT_CHUNK, count - t0);
+  // stage K, V, queries
+  for (int i = threadIdx.x; i < nt * (HD / 4); i += blockDim.x) {
+    const int t = i / (HD / 4), d4 = i % (HD / 4);
+    reinterpret_cast<float4*>(ks + t * HD)[d4] =
+        __ldcs(reinterpret_cast<const float4*>(kc + (size_t(t0 + t) * KVH + kvh) * HD) + d4);
+  }
+  for (int i = threadIdx.x; i < HD * nt; i += blockDim.x) {
+    const int d = i / nt, t = i % nt;
+    vs[d * (ATT_CHUNK + 1) + t] = __ldcs(vc + (size_t(d) * KVH + kvh) * cap + t0 + t);
+  }
+  for (int i = threadIdx.x; i < NQ * HD; i += blockDim.x) {
+    const int qi = i / HD, d = i % HD;
+    const int m = qi / G, h = kvh * G + qi % G;
+    qs[i] = round_f16_rust(q[(size_t(m) * H + h) * HD + d]);
+  }
+  __syncthreads();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, warps = blockDim.x >> 5;
+  // scores: warp per (query, token) pair, lanes over the head dimension
+  for (int pr = warp; pr < NQ * nt; pr += warps) {
+    const int qi = pr / nt, t = pr % nt;
+    const float* qv = qs + qi * HD;
+    const float* kv = ks + t * HD;
+    float dot = 0.0f;
+#pragma unroll
+    for (int i = 0; i < HD / 32; ++i) dot += qv[lane + 32 * i] * kv[lane + 32 * i];
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, off);
+    if (lane == 0) {
+      const int m = qi / G;
+      ps[qi * ATT_CHUNK + t] = (t0 + t <= pos[m]) ? dot * scale : -INFINITY;
+    }
+  }
+  __syncthreads();
+  // local softmax per query: warp per query
+  for (int qi = warp; qi < NQ; qi += warps) {
+    float mx = -INFINITY;
+    for (int t = lane; t < nt; t += 32) mx = fmaxf(mx, ps[qi * ATT_CHUNK + t]);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    float sum = 0.0f;
+    for (int t = lane; t < nt; t += 32) {
+      const float s = ps[qi * ATT_CHUNK + t];
+      const float p = s == -INFINITY ? 0.0f : float(exp(double(s - mx)));
+      ps[qi * ATT_CHUNK + t] = p;
+      sum += p;
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+    if (lane == 0) {
+      const size_t o = (size_t(chunk) * KVH + kvh) * NQ + qi;
+      part_m[o] = mx;
+      part_l[o] = sum;
+    }
+  }
+  __syncthreads();
+  // partial outputs: thread per (query, dim)
+  for (int i = threadIdx.x; i < NQ * HD; i += blockDim.x) {
+    const int qi = i / HD, d = i % HD;
+    const float* pr = ps + qi * ATT_CHUNK;
+    const float* vr = vs + d * (ATT_CHUNK + 1);
+    float acc = 0.0f;
+    for (int t = 0; t < nt; ++t) acc += pr[t] * vr[t];
+    part_o[((size_t(chunk) * KVH + kvh) * NQ + qi) * HD + d] = acc;
+  }
+}
+
+// Combines the chunk partials of each (token, head), casts through the TS f16
+// codec (castF16Rows) and quantizes the H*HD vector of each token for the
+// output projection.  One CTA per token, warp h = head h = Q8_K block h.
+__global__ void attn_combine_kernel(const float* __restrict__ part_m, const float* __restrict__ part_l,
+                                    const float* __restrict__ part_o, const int32_t* __restrict__ pos, int M, int H,
+                                    int KVH, int cap, Q8Buf q, float* __restrict__ attn_out) {
+  constexpr int HD = 256;
+  __shared__ __align__(16) uint8_t stage[32][256];
+  pdl_trigger();
+  pdl_wait();
+  const int m = blockIdx.x, lane = threadIdx.x & 31, h = threadIdx.x >> 5;
+  const int G = H / KVH, NQ = M * G, kvh = h / G, qi = m * G + h % G;
+  int maxpos = 0;
+  for (int i = 0; i < M; ++i) maxpos = max(maxpos, pos[i]);
+  const int count = min(cap, maxpos + 1);
+  const int nch = (count + ATT_CHUNK - 1) / ATT_CHUNK;
+  float gmax = -INFINITY;
+  for (int c = 0; c < nch; ++c) gmax = fmaxf(gmax, part_m[(size_t(c) * KVH + kvh) * NQ + qi]);
+  float o[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  double l = 0.0;
+  for (int c = 0; c < nch; ++c) {
+    const size_t pi = (size_t(c) * KVH + kvh) * NQ + qi;
+    const float mc = part_m[pi];
+    if (mc == -INFINITY) continue;
+    const float w = float(exp(double(mc - gmax)));
+    l += double(w) * double(part_l[pi]);
+    const float* po = part_o + pi * HD + 8 * lane;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[i] += w * po[i];
+  }
+  float n[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) n[i] = round_f16_ts(float(double(o[i]) / l));
+  if (attn_out) {
+    float4* ao = reinterpret_cast<float4*>(attn_out + (size_t(m) * H + h) * HD + 8 * lane);
+    ao[0] = make_float4(n[0], n[1], n[2], n[3]);
+    ao[1] = make_float4(n[4], n[5], n[6], n[7]);
+  }
+  q8k_block_warp(n, lane, stage[h], q8_rec_a(q, m, h), q8_rec_b(q, m, h));
+}
+
+// ---- GEGLU ------------------------------------------------------------------------------
+
+// layers.ts:1062-1076 gelu (tanh form) with the TS f16 codec on input and
+// output; |x| >= 10 short-circuits.
+__device__ __forceinline__ double gelu_ts(float v) {
+  if (v <= -10.0f) return 0.0;
+  if (v >= 10.0f) return double(v);
+  const double x = double(round_f16_ts(v));
+  const float xx = float(x * x);
+  const float poly = float(1.0 + double(float(0.044715 * double(xx))));
+  const float lin = float(0.7978845608028654 * x);  // Math.sqrt(2 / Math.PI) as a double
+  const float inner = float(double(lin) * double(poly));
+  const float hlf = float(0.5 * x);
+  const float act = float(double(hlf) * double(float(1.0 + tanh(double(inner)))));
+  return double(round_f16_ts(act));
+}
+
+// act = fround(gelu(gate) * up) for 8 blocks per CTA (warp = block), quantized
+// for the down projection.  Grid (F/2048, M).
+__global__ void geglu_quant_kernel(const float* __restrict__ gate, const float* __restrict__ up, int F, Q8Buf q,
+                                   float* __restrict__ act_out) {
+  __shared__ __align__(16) uint8_t stage[8][256];
+  pdl_trigger();
+  pdl_wait();
+  const int m = blockIdx.y, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int b = blockIdx.x * 8 + warp;
+  const size_t base = size_t(m) * F + size_t(b) * 256 + 8 * lane;
+  const float4 g0 = reinterpret_cast<const float4*>(gate + base)[0], g1 = reinterpret_cast<const float4*>(gate + base)[1];
+  const float4 u0 = reinterpret_cast<const float4*>(up + base)[0], u1 = reinterpret_cast<const float4*>(up + base)[1];
+  const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+  const float u[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+  float a[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) a[i] = float(gelu_ts(g[i]) * double(u[i]));
+  if (act_out) {
+    float4* ao = reinterpret_cast<float4*>(act_out + base);
+    ao[0] = make_float4(a[0], a[1], a[2], a[3]);
+    ao[1] = make_float4(a[4], a[5], a[6], a[7]);
+  }
+  q8k_block_warp(a, lane, stage[warp], q8_rec_a(q, m, b), q8_rec_b(q, m, b));
+}
+
+// ---- launch helpers ---------------------------------------------------------------------
+
+template <typename... KArgs, typename... Args>
+static cudaError_t pdl_launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+cudaError_t launch_rope_table(const int32_t* pos, int M, int half, double theta_scale, double* cos_t, double* sin_t,
+                              cudaStream_t st) {
+  return pdl_launch(rope_table_kernel, dim3(M), dim3(128), 0, st, pos, half, theta_scale, cos_t, sin_t);
+}
+
+cudaError_t launch_embed(const uint8_t* w, int type, int nb, int vocab, const int32_t* ids, float* hidden, int M, int D,
+                         double scale, int* err, cudaStream_t st) {
+  return pdl_launch(embed_kernel, dim3(M), dim3(256), 0, st, w, type, nb, vocab, ids, hidden, D, scale, err);
+}
+
+cudaError_t launch_norm_quant(bool resid, float* x, const float* y, const float* w_post, const float* w_pre, double eps,
+                              int M, int D, const Q8Buf& q, float* n_out, cudaStream_t st) {
+  const dim3 grid(M), block(D / 8);
+  if (resid) return pdl_launch(norm_quant_kernel<true>, grid, block, 0, st, x, y, w_post, w_pre, eps, D, q, n_out);
+  return pdl_launch(norm_quant_kernel<false>, grid, block, 0, st, x, y, w_post, w_pre, eps, D, q, n_out);
+}
+
+cudaError_t launch_qkv_post(const float* q, const float* k, const float* v, const float* qnw, const float* knw,
+                            const int32_t* pos, const double* cos_t, const double* sin_t, int M, int H, int KVH,
+                            int cap, double eps, bool has_kv, float* q_out, float* kc, float* vc, cudaStream_t st) {
+  return pdl_launch(qkv_post_kernel, dim3(M), dim3(32 * (H + 2 * KVH)), 0, st, q, k, v, qnw, knw, pos, cos_t, sin_t, H,
+                    KVH, cap, eps, int(has_kv), q_out, kc, vc);
+}
+
+size_t attn_smem_bytes(int M, int H, int KVH) {
+  const int NQ = M * (H / KVH);
+  return sizeof(float) * (size_t(ATT_CHUNK) * 256 + size_t(256) * (ATT_CHUNK + 1) + size_t(NQ) * 256 +
+                          size_t(NQ) * ATT_CHUNK);
+}
+
+cudaError_t launch_attention(const float* q, const float* kc, const float* vc, const int32_t* pos, int M, int H,
+                             int KVH, int cap, float scale, float* part_m, float* part_l, float* part_o,
+                             cudaStream_t st) {
+  const size_t smem = attn_smem_bytes(M, H, KVH);
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(attn_partial_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  const int chunks = (cap + ATT_CHUNK - 1) / ATT_CHUNK;
+  return pdl_launch(attn_partial_kernel, dim3(chunks, KVH), dim3(ATT_THREADS), smem, st, q, kc, vc, pos, M, H, KVH, cap,
+                    scale, part_m, part_l, part_o);
+}
+
+cudaError_t launch_attn_combine(const float* part_m, const float* part_l, const float* part_o, const int32_t* pos,
+                                int M, int H, int KVH, int cap, const Q8Buf& q, float* attn_out, cudaStream_t st) {
+  return pdl_launch(attn_combine_kernel, dim3(M), dim3(32 * H), 0, st, part_m, part_l, part_o, pos, M, H, KVH, cap, q,
+                    attn_out);
+}
+
+cudaError_t launch_geglu_quant(const float* gate, const float* up, int M, int F, const Q8Buf& q, float* act_out,
+                               cudaStream_t st) {
+  return pdl_launch(geglu_quant_kernel, dim3(F / 2048, M), dim3(256), 0, st, gate, up, F, q, act_out);
+}
+
+}  // namespace hc

@@ -172,6 +172,72 @@ int hpc_lm_head_topk_q8(hpc_weight lm_head, const void *d_workspace, size_t work
 int hpc_topk_merge_keys(const uint64_t *d_keys, size_t group_count, size_t column_count, size_t k, float softcap,
                         int32_t *d_ids, float *d_vals, void *stream);
 
+/* ---- resident decoder model: decode / batched verify step ------------------
+ * A Gemma-4-style decoder (pre/post RMSNorm sandwich, per-head QK norm, NeoX
+ * RoPE, GQA over an fp32 KV cache, GEGLU FFN, tied Q6_K/Q4_K embedding / LM
+ * head) kept resident in HBM.  hpc_model_forward runs embedding -> all layers
+ * -> output norm -> LM head top-k for token_count consecutive positions in one
+ * CUDA-graph launch: the WASM provider's per-token forward
+ * (runner/wasm/layers.ts:161-473, forwardOutput :381-416) and the WebGPU
+ * batched verify forward (runner/webgpu/segment-runner.ts:1292-1606). */
+
+typedef struct hpc_model_s *hpc_model;
+
+typedef struct {
+  int hidden;        /* embeddingLength, multiple of 2048 */
+  int heads;         /* query heads */
+  int kv_heads;      /* key/value heads (GQA) */
+  int head_dim;      /* 256 */
+  int ffn;           /* feed_forward_length, multiple of 2048 */
+  int vocab;
+  int layers;
+  int kv_layers;     /* layers [0, kv_layers) own a KV cache; later layers reuse
+                        layer kv_layers-1's (kvSourceLayers, engine/src/model.ts:382-388) */
+  int context;       /* KV capacity (full attention) */
+  int max_tokens;    /* largest token_count per call, 1..8 */
+  int top_k;         /* largest top_k per call, 1..64 */
+  double rms_eps;
+  double rope_theta;
+  float final_logit_softcap; /* <= 0: none */
+} hpc_model_config;
+
+/* weight slots */
+#define HPC_W_Q 0
+#define HPC_W_K 1
+#define HPC_W_V 2
+#define HPC_W_O 3
+#define HPC_W_GATE 4
+#define HPC_W_UP 5
+#define HPC_W_DOWN 6
+#define HPC_W_COUNT 7
+/* norm slots (f32 weights) */
+#define HPC_N_ATTN 0
+#define HPC_N_Q 1
+#define HPC_N_K 2
+#define HPC_N_POST_ATTN 3
+#define HPC_N_FFN 4
+#define HPC_N_POST_FFW 5
+#define HPC_N_COUNT 6
+#define HPC_N_OUTPUT 100 /* output_norm (layer ignored) */
+
+int hpc_model_create(const hpc_model_config *config, hpc_model *out_model);
+int hpc_model_release(hpc_model model);
+/* The model does not own weight handles; they must outlive it. */
+int hpc_model_set_weight(hpc_model model, int layer, int slot, hpc_weight weight);
+int hpc_model_set_norm(hpc_model model, int layer, int slot, const float *host_values, size_t len);
+/* token_embd.weight == output weight (tied): rows are vocabulary ids. */
+int hpc_model_set_lm_head(hpc_model model, hpc_weight weight);
+/* Device pointers of one KV layer's cache: K [context][kv_heads][head_dim],
+ * V [head_dim][kv_heads][context] (layers.ts:887-911 layout). */
+int hpc_model_kv(hpc_model model, int kv_layer, float **d_key, float **d_value);
+/* One forward over token_count tokens at the given positions (all device
+ * pointers).  Writes top-k ids/values [token_count][top_k] for every position
+ * (value desc, id asc; softcap after selection), and the final residual stream
+ * [token_count][hidden] when d_hidden_out != NULL.  The first call for a
+ * token count captures a CUDA graph (run it before any outer stream capture). */
+int hpc_model_forward(hpc_model model, const int32_t *d_token_ids, const int32_t *d_positions, size_t token_count,
+                      size_t top_k, int32_t *d_ids, float *d_vals, float *d_hidden_out, void *stream);
+
 #ifdef __cplusplus
 }
 #endif
