@@ -25,6 +25,7 @@
 
 #include <cuda_fp16.h>
 
+#include "hc_bulk.cuh"
 #include "hc_common.cuh"
 #include "hc_decode.cuh"
 #include "hc_q8.cuh"
@@ -314,74 +315,105 @@ __global__ void qkv_post_kernel(const float* __restrict__ q, const float* __rest
 
 // Split-KV decode attention (flash-decoding form of hp_gqa_attention_f32,
 // lib.rs:539-654, on the compacted full-attention range [0, pos+1)).  Grid
-// (chunks, KVH); a CTA loads one ATT_CHUNK-token slice of K and V for one KV
-// head into shared memory and serves all M tokens x (H/KVH) query heads of
-// that group: scores (f16-rounded query, scale 1, causal), a local softmax
-// (max, sum of f64 exp) and the partial output sum p*v.
+// (chunks, KVH); a CTA serves all M tokens x (H/KVH) query heads of one KV
+// head over one ATT_CHUNK-token slice of the cache.  Warp 0 issues bulk
+// copies of the slice (ATT_CHUNK K rows of 1 KB, HD V rows of ATT_CHUNK*4 B)
+// into padded shared-memory rows (bank-conflict-free float4 reads),
+// completing on an mbarrier.  A slice that holds none of this step's new
+// rows (every chunk but the one or two around pos) was written by earlier
+// steps, so its copies are issued before griddepcontrol.wait and overlap the
+// kernels ahead of attention.  Then the queries are staged (rounded to f16
+// with the Rust codec, lib.rs:590-597), scores (scale 1, causal), a local
+// softmax (max, sum of f64 exp) and the partial output p*v are written for
+// the combine kernel.
+constexpr int ATT_KSTRIDE = 256 + 4;        // floats per staged K row
+constexpr int ATT_VSTRIDE = ATT_CHUNK + 4;  // floats per staged V row
+
 __global__ void __launch_bounds__(ATT_THREADS) attn_partial_kernel(
     const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
     const int32_t* __restrict__ pos, int M, int H, int KVH, int cap, float scale, float* __restrict__ part_m,
-    float* __restrict__ part_l, float* __restrict__ part_o) {
-  constexpr int HD = 256;
+    float* __restrict__ part_l, float* __restrict__ part_o, int* __restrict__ err) {
+  constexpr int HD = 256, CH = ATT_CHUNK;
+  static_assert(ATT_THREADS == HD, "thread d owns V row d");
   extern __shared__ __align__(16) float sm[];
+  __shared__ __align__(8) uint64_t bar;
   const int chunk = blockIdx.x, kvh = blockIdx.y;
   const int G = H / KVH, NQ = M * G;
-  float* ks = sm;                           // [ATT_CHUNK][HD]
-  float* vs = ks + ATT_CHUNK * HD;          // [HD][ATT_CHUNK + 1]
-  float* qs = vs + HD * (ATT_CHUNK + 1);    // [NQ][HD]
-  float* ps = qs + NQ * HD;                 // [NQ][ATT_CHUNK]
+  float* ks = sm;                     // [CH][ATT_KSTRIDE]
+  float* vs = ks + CH * ATT_KSTRIDE;  // [HD][ATT_VSTRIDE]
+  float* qs = vs + HD * ATT_VSTRIDE;  // [NQ][HD]
+  float* ps = qs + NQ * HD;           // [NQ][CH]
   pdl_trigger();
-  pdl_wait();
+  // pos is written before the step starts (not by a kernel of this step)
   int maxpos = 0;
-  for (int i = 0; i < M; ++i) maxpos = max(maxpos, pos[i]);
+  bool fresh = false;  // does the slice hold a row written in this step?
+  const int t0 = chunk * CH;
+  for (int i = 0; i < M; ++i) {
+    const int p = pos[i];
+    maxpos = max(maxpos, p);
+    fresh |= (p >= t0 && p < t0 + CH);
+  }
   const int count = min(cap, maxpos + 1);
-  const int t0 = chunk * ATT_CHUNK;
-  if (t0 >= count) return;
-  const int nt = min(ATT_CHUNK, count - t0);
-  // stage K, V, queries
-  for (int i = threadIdx.x; i < nt * (HD / 4); i += blockDim.x) {
-    const int t = i / (HD / 4), d4 = i % (HD / 4);
-    reinterpret_cast<float4*>(ks + t * HD)[d4] =
-        __ldcs(reinterpret_cast<const float4*>(kc + (size_t(t0 + t) * KVH + kvh) * HD) + d4);
+  if (t0 >= count) {
+    pdl_wait();
+    return;
   }
-  for (int i = threadIdx.x; i < HD * nt; i += blockDim.x) {
-    const int d = i / nt, t = i % nt;
-    vs[d * (ATT_CHUNK + 1) + t] = __ldcs(vc + (size_t(d) * KVH + kvh) * cap + t0 + t);
-  }
+  const int nt = min(CH, count - t0);
+  auto issue = [&]() {
+    // cap % CH == 0 keeps every copied row inside the cache even for the
+    // last, partial chunk
+    if (threadIdx.x == 0) {
+      mbar_init(&bar, 1);
+      mbar_expect_tx(&bar, uint32_t(CH * HD * 4 * 2));
+    }
+    __syncwarp();
+    for (int t = threadIdx.x; t < CH; t += 32)
+      bulk_copy_g2s(ks + t * ATT_KSTRIDE, kc + (size_t(t0 + t) * KVH + kvh) * HD, HD * 4, &bar);
+    for (int d = threadIdx.x; d < HD; d += 32)
+      bulk_copy_g2s(vs + d * ATT_VSTRIDE, vc + (size_t(d) * KVH + kvh) * cap + t0, CH * 4, &bar);
+  };
+  if (threadIdx.x < 32 && !fresh) issue();
+  pdl_wait();
+  if (threadIdx.x < 32 && fresh) issue();
   for (int i = threadIdx.x; i < NQ * HD; i += blockDim.x) {
     const int qi = i / HD, d = i % HD;
     const int m = qi / G, h = kvh * G + qi % G;
     qs[i] = round_f16_rust(q[(size_t(m) * H + h) * HD + d]);
   }
   __syncthreads();
+  if (!mbar_wait_parity(&bar, 0, err)) return;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, warps = blockDim.x >> 5;
-  // scores: warp per (query, token) pair, lanes over the head dimension
-  for (int pr = warp; pr < NQ * nt; pr += warps) {
-    const int qi = pr / nt, t = pr % nt;
-    const float* qv = qs + qi * HD;
-    const float* kv = ks + t * HD;
-    float dot = 0.0f;
-#pragma unroll
-    for (int i = 0; i < HD / 32; ++i) dot += qv[lane + 32 * i] * kv[lane + 32 * i];
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, off);
-    if (lane == 0) {
-      const int m = qi / G;
-      ps[qi * ATT_CHUNK + t] = (t0 + t <= pos[m]) ? dot * scale : -INFINITY;
+  // scores: thread per (query, token); a warp shares the query (broadcast
+  // reads) and walks 32 padded K rows
+  for (int pr = threadIdx.x; pr < NQ * CH; pr += blockDim.x) {
+    const int qi = pr / CH, t = pr % CH;
+    const float4* qv = reinterpret_cast<const float4*>(qs + qi * HD);
+    const float4* kv = reinterpret_cast<const float4*>(ks + t * ATT_KSTRIDE);
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 16
+    for (int j = 0; j < HD / 4; ++j) {
+      const float4 a = qv[j], b = kv[j];
+      acc.x = fmaf(a.x, b.x, acc.x);
+      acc.y = fmaf(a.y, b.y, acc.y);
+      acc.z = fmaf(a.z, b.z, acc.z);
+      acc.w = fmaf(a.w, b.w, acc.w);
     }
+    const float dot = (acc.x + acc.y) + (acc.z + acc.w);
+    const int m = qi / G;
+    ps[pr] = (t < nt && t0 + t <= pos[m]) ? dot * scale : -INFINITY;
   }
   __syncthreads();
-  // local softmax per query: warp per query
+  // local softmax: warp per query
   for (int qi = warp; qi < NQ; qi += warps) {
     float mx = -INFINITY;
-    for (int t = lane; t < nt; t += 32) mx = fmaxf(mx, ps[qi * ATT_CHUNK + t]);
+    for (int t = lane; t < CH; t += 32) mx = fmaxf(mx, ps[qi * CH + t]);
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
     float sum = 0.0f;
-    for (int t = lane; t < nt; t += 32) {
-      const float s = ps[qi * ATT_CHUNK + t];
-      const float p = s == -INFINITY ? 0.0f : float(exp(double(s - mx)));
-      ps[qi * ATT_CHUNK + t] = p;
+    for (int t = lane; t < CH; t += 32) {
+      const float sc = ps[qi * CH + t];
+      const float p = (sc == -INFINITY) ? 0.0f : float(exp(double(sc - mx)));
+      ps[qi * CH + t] = p;
       sum += p;
     }
 #pragma unroll
@@ -393,56 +425,105 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_partial_kernel(
     }
   }
   __syncthreads();
-  // partial outputs: thread per (query, dim)
-  for (int i = threadIdx.x; i < NQ * HD; i += blockDim.x) {
-    const int qi = i / HD, d = i % HD;
-    const float* pr = ps + qi * ATT_CHUNK;
-    const float* vr = vs + d * (ATT_CHUNK + 1);
-    float acc = 0.0f;
-    for (int t = 0; t < nt; ++t) acc += pr[t] * vr[t];
-    part_o[((size_t(chunk) * KVH + kvh) * NQ + qi) * HD + d] = acc;
+  // partial outputs: thread d holds V row d (contiguous over tokens) and
+  // serves four queries per pass; the probabilities are broadcast reads
+  const int d = threadIdx.x;
+  const float4* vr = reinterpret_cast<const float4*>(vs + d * ATT_VSTRIDE);
+  for (int qg = 0; qg < NQ; qg += 4) {
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
+    for (int j = 0; j < CH / 4; ++j) {
+      const float4 b = vr[j];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        if (qg + u < NQ) {
+          const float4 a = reinterpret_cast<const float4*>(ps + (qg + u) * CH)[j];
+          acc[u] += a.x * b.x + a.y * b.y + a.z * b.z + a.w * b.w;
+        }
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      if (qg + u < NQ) part_o[((size_t(chunk) * KVH + kvh) * NQ + qg + u) * HD + d] = acc[u];
   }
 }
 
-// Combines the chunk partials of each (token, head), casts through the TS f16
-// codec (castF16Rows) and quantizes the H*HD vector of each token for the
-// output projection.  One CTA per token, warp h = head h = Q8_K block h.
-__global__ void attn_combine_kernel(const float* __restrict__ part_m, const float* __restrict__ part_l,
-                                    const float* __restrict__ part_o, const int32_t* __restrict__ pos, int M, int H,
-                                    int KVH, int cap, Q8Buf q, float* __restrict__ attn_out) {
-  constexpr int HD = 256;
-  __shared__ __align__(16) uint8_t stage[32][256];
+// Combines the chunk partials of one (token, head): global max, rescaled
+// sums, division, the TS f16 cast (castF16Rows), then the head's 256 values
+// -- exactly Q8_K block h of the token's attention vector -- are quantized
+// for the output projection.  Grid (M, H), thread d = head dimension.
+__global__ void __launch_bounds__(256) attn_combine_kernel(const float* __restrict__ part_m,
+                                                           const float* __restrict__ part_l,
+                                                           const float* __restrict__ part_o,
+                                                           const int32_t* __restrict__ pos, int M, int H, int KVH,
+                                                           int cap, Q8Buf q, float* __restrict__ attn_out) {
+  constexpr int HD = 256, CH = ATT_CHUNK, MAXC = 4096 / ATT_CHUNK;
+  __shared__ float wch[MAXC];
+  __shared__ double red[8];
+  __shared__ float vec[HD];
+  __shared__ __align__(16) uint8_t stage[256];
   pdl_trigger();
   pdl_wait();
-  const int m = blockIdx.x, lane = threadIdx.x & 31, h = threadIdx.x >> 5;
+  const int m = blockIdx.x, h = blockIdx.y, d = threadIdx.x, lane = d & 31, warp = d >> 5;
   const int G = H / KVH, NQ = M * G, kvh = h / G, qi = m * G + h % G;
   int maxpos = 0;
   for (int i = 0; i < M; ++i) maxpos = max(maxpos, pos[i]);
   const int count = min(cap, maxpos + 1);
-  const int nch = (count + ATT_CHUNK - 1) / ATT_CHUNK;
+  const int nch = (count + CH - 1) / CH;
+  // chunk maxima -> global max
+  float mc = -INFINITY;
+  if (d < nch) mc = part_m[(size_t(d) * KVH + kvh) * NQ + qi];
+  float mx = mc;
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+  if (lane == 0) red[warp] = double(mx);
+  __syncthreads();
   float gmax = -INFINITY;
-  for (int c = 0; c < nch; ++c) gmax = fmaxf(gmax, part_m[(size_t(c) * KVH + kvh) * NQ + qi]);
-  float o[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  for (int w = 0; w < 8; ++w) gmax = fmaxf(gmax, float(red[w]));
+  __syncthreads();
+  // chunk weights and the total normalizer
+  double lw = 0.0;
+  if (d < nch) {
+    const float w = mc == -INFINITY ? 0.0f : float(exp(double(mc - gmax)));
+    wch[d] = w;
+    lw = double(w) * double(part_l[(size_t(d) * KVH + kvh) * NQ + qi]);
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) lw += __shfl_xor_sync(0xffffffffu, lw, off);
+  if (lane == 0) red[warp] = lw;
+  __syncthreads();
   double l = 0.0;
-  for (int c = 0; c < nch; ++c) {
-    const size_t pi = (size_t(c) * KVH + kvh) * NQ + qi;
-    const float mc = part_m[pi];
-    if (mc == -INFINITY) continue;
-    const float w = float(exp(double(mc - gmax)));
-    l += double(w) * double(part_l[pi]);
-    const float* po = part_o + pi * HD + 8 * lane;
+  for (int w = 0; w < 8; ++w) l += red[w];
+  // weighted sum over chunks for dimension d (independent loads, unrolled)
+  float o = 0.0f;
+  const float* po = part_o + (size_t(kvh) * NQ + qi) * HD + d;
+  const size_t cstride = size_t(KVH) * NQ * HD;
+  int c = 0;
+  for (; c + 32 <= nch; c += 32) {
+    float v[32];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) o[i] += w * po[i];
-  }
-  float n[8];
+    for (int i = 0; i < 32; ++i) v[i] = po[size_t(c + i) * cstride];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) n[i] = round_f16_ts(float(double(o[i]) / l));
-  if (attn_out) {
-    float4* ao = reinterpret_cast<float4*>(attn_out + (size_t(m) * H + h) * HD + 8 * lane);
-    ao[0] = make_float4(n[0], n[1], n[2], n[3]);
-    ao[1] = make_float4(n[4], n[5], n[6], n[7]);
+    for (int i = 0; i < 32; ++i) o += wch[c + i] * v[i];
   }
-  q8k_block_warp(n, lane, stage[h], q8_rec_a(q, m, h), q8_rec_b(q, m, h));
+  for (; c + 8 <= nch; c += 8) {
+    float v[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = po[size_t(c + i) * cstride];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o += wch[c + i] * v[i];
+  }
+  for (; c < nch; ++c) o += wch[c] * po[size_t(c) * cstride];
+  const float n = round_f16_ts(float(double(o) / l));
+  vec[d] = n;
+  if (attn_out) attn_out[(size_t(m) * H + h) * HD + d] = n;
+  __syncthreads();
+  if (warp == 0) {
+    float v8[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v8[i] = vec[8 * lane + i];
+    q8k_block_warp(v8, lane, stage, q8_rec_a(q, m, h), q8_rec_b(q, m, h));
+  }
 }
 
 // ---- GEGLU ------------------------------------------------------------------------------
@@ -531,28 +612,29 @@ cudaError_t launch_qkv_post(const float* q, const float* k, const float* v, cons
 
 size_t attn_smem_bytes(int M, int H, int KVH) {
   const int NQ = M * (H / KVH);
-  return sizeof(float) * (size_t(ATT_CHUNK) * 256 + size_t(256) * (ATT_CHUNK + 1) + size_t(NQ) * 256 +
+  return sizeof(float) * (size_t(ATT_CHUNK) * ATT_KSTRIDE + size_t(256) * ATT_VSTRIDE + size_t(NQ) * 256 +
                           size_t(NQ) * ATT_CHUNK);
 }
 
 cudaError_t launch_attention(const float* q, const float* kc, const float* vc, const int32_t* pos, int M, int H,
-                             int KVH, int cap, float scale, float* part_m, float* part_l, float* part_o,
+                             int KVH, int cap, float scale, float* part_m, float* part_l, float* part_o, int* err,
                              cudaStream_t st) {
+  if (cap % ATT_CHUNK != 0 || cap > 4096) return cudaErrorInvalidValue;
   const size_t smem = attn_smem_bytes(M, H, KVH);
   static bool attr = false;
   if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(attn_partial_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    cudaError_t e = cudaFuncSetAttribute(attn_partial_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
     if (e != cudaSuccess) return e;
     attr = true;
   }
-  const int chunks = (cap + ATT_CHUNK - 1) / ATT_CHUNK;
+  const int chunks = cap / ATT_CHUNK;
   return pdl_launch(attn_partial_kernel, dim3(chunks, KVH), dim3(ATT_THREADS), smem, st, q, kc, vc, pos, M, H, KVH, cap,
-                    scale, part_m, part_l, part_o);
+                    scale, part_m, part_l, part_o, err);
 }
 
 cudaError_t launch_attn_combine(const float* part_m, const float* part_l, const float* part_o, const int32_t* pos,
                                 int M, int H, int KVH, int cap, const Q8Buf& q, float* attn_out, cudaStream_t st) {
-  return pdl_launch(attn_combine_kernel, dim3(M), dim3(32 * H), 0, st, part_m, part_l, part_o, pos, M, H, KVH, cap, q,
+  return pdl_launch(attn_combine_kernel, dim3(M, H), dim3(256), 0, st, part_m, part_l, part_o, pos, M, H, KVH, cap, q,
                     attn_out);
 }
 

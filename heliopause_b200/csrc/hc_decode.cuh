@@ -4,7 +4,7 @@
 
 namespace hc {
 
-constexpr int ATT_CHUNK = 32;    // KV tokens per attention CTA
+constexpr int ATT_CHUNK = 64;    // KV tokens per attention CTA (context must be a multiple, <= 4096)
 constexpr int ATT_THREADS = 256;
 
 cudaError_t launch_rope_table(const int32_t* pos, int M, int half, double theta_scale, double* cos_t, double* sin_t,
@@ -18,7 +18,7 @@ cudaError_t launch_qkv_post(const float* q, const float* k, const float* v, cons
                             int cap, double eps, bool has_kv, float* q_out, float* kc, float* vc, cudaStream_t st);
 size_t attn_smem_bytes(int M, int H, int KVH);
 cudaError_t launch_attention(const float* q, const float* kc, const float* vc, const int32_t* pos, int M, int H,
-                             int KVH, int cap, float scale, float* part_m, float* part_l, float* part_o,
+                             int KVH, int cap, float scale, float* part_m, float* part_l, float* part_o, int* err,
                              cudaStream_t st);
 cudaError_t launch_attn_combine(const float* part_m, const float* part_l, const float* part_o, const int32_t* pos,
                                 int M, int H, int KVH, int cap, const Q8Buf& q, float* attn_out, cudaStream_t st);

@@ -82,7 +82,8 @@ static int check_cfg(const hpc_model_config* c) {
   if (c->ffn <= 0 || c->ffn % 2048 != 0) return hpc_fail(HPC_ERR_SHAPE, "ffn %d: must be a multiple of 2048", c->ffn);
   if (c->layers <= 0 || c->kv_layers <= 0 || c->kv_layers > c->layers)
     return hpc_fail(HPC_ERR_SHAPE, "layers %d / kv_layers %d", c->layers, c->kv_layers);
-  if (c->context <= 0 || c->vocab <= 0) return hpc_fail(HPC_ERR_SHAPE, "context / vocab");
+  if (c->context <= 0 || c->context % 64 != 0 || c->context > 4096 || c->vocab <= 0)
+    return hpc_fail(HPC_ERR_SHAPE, "context %d: a multiple of 64 up to 4096; vocab %d", c->context, c->vocab);
   if (c->max_tokens < 1 || c->max_tokens > 8) return hpc_fail(HPC_ERR_SHAPE, "max_tokens %d: 1..8", c->max_tokens);
   if (c->top_k < 1 || c->top_k > hc::TOPK_MAX) return hpc_fail(HPC_ERR_SHAPE, "top_k %d", c->top_k);
   return HPC_OK;
@@ -316,7 +317,7 @@ static int enqueue_step(hpc_model m, int M, int k, cudaStream_t st) {
                                KVH, c.context, eps, own_kv, m->qr, m->kc[kvl], m->vc[kvl], st),
            "qk norm / rope / kv");
     HPC_CK(hc::launch_attention(m->qr, m->kc[kvl], m->vc[kvl], m->pos, M, H, KVH, c.context, 1.0f, m->pm, m->pl,
-                                m->po, st),
+                                m->po, m->err, st),
            "attention");
     HPC_CK(hc::launch_attn_combine(m->pm, m->pl, m->po, m->pos, M, H, KVH, c.context, qd, nullptr, st),
            "attention combine");
