@@ -210,14 +210,14 @@ class GemvConfig1:
                                           f"rows split over {threads} threads like the WASM pool)"}
 
 
-def graph_launch_times(launches, reps: int = 3) -> float:
-    """Average device time (ms) of each callable in `launches`, measured with
-    external CUDA events captured around every launch inside one CUDA graph
-    (so the times exclude host launch overhead)."""
+def graph_launch_times(launches, reps: int = 5) -> float:
+    """Average device time (ms) of one launch: the callables in `launches` are
+    captured back to back into one CUDA graph (programmatic dependent launch
+    between them, as inside a decode step), the graph is replayed between two
+    CUDA events on the replay stream, and the elapsed time is divided by the
+    number of launches.  The mean over `reps` replays is returned."""
     import torch
     n = len(launches)
-    evs = [(torch.cuda.Event(enable_timing=True, external=True), torch.cuda.Event(enable_timing=True, external=True))
-           for _ in range(n)]
     s = torch.cuda.Stream()
     s.wait_stream(torch.cuda.current_stream())
     g = torch.cuda.CUDAGraph()
@@ -226,18 +226,22 @@ def graph_launch_times(launches, reps: int = 3) -> float:
             f()
         torch.cuda.synchronize()
         with torch.cuda.graph(g, stream=s):
-            for (a, b), f in zip(evs, launches):
-                a.record()
+            for f in launches:
                 f()
-                b.record()
     torch.cuda.current_stream().wait_stream(s)
     times = []
-    for _ in range(reps):
-        g.replay()
-        torch.cuda.synchronize()
-        times.append(statistics.mean(a.elapsed_time(b) for a, b in evs))
+    with torch.cuda.stream(s):
+        g.replay()  # warm
+        for _ in range(reps):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(s)
+            g.replay()
+            b.record(s)
+            b.synchronize()
+            times.append(a.elapsed_time(b) / n)
+    torch.cuda.synchronize()
     del g
-    return min(times)
+    return statistics.mean(times)
 
 
 class DecodeConfig3:
@@ -399,7 +403,194 @@ def cpu_baseline_from(sampler, budget_s: float) -> dict:
             "sample": f"{len(runs)} x (" + sampler.describe(tl, th) + ")"}
 
 
-WORKLOADS = {"decode-config3": DecodeConfig3, "gemv-config1": GemvConfig1}
+class _Q8Launcher:
+    """Raw C-ABI launches on a caller-owned Q8_K workspace (the graph-capturable
+    form the decode step uses): hpc_q8_quantize + hpc_matmul_q8."""
+
+    def __init__(self, k: int, m: int):
+        import ctypes as C
+
+        import torch
+
+        from heliopause_b200 import _lib
+        from heliopause_b200 import kernels as hk
+        self.C, self.L, self.hk, self.torch = C, _lib.lib(), hk, torch
+        self.k, self.m = k, m
+        nbytes = C.c_size_t()
+        hk.assert_cuda_ok(self.L.hpc_q8_workspace_bytes(k, m, C.byref(nbytes)), "workspace bytes")
+        self.ws_bytes = nbytes.value
+        self.ws = torch.zeros(self.ws_bytes, dtype=torch.uint8, device="cuda")
+
+    def stream(self):
+        return self.C.c_void_p(self.torch.cuda.current_stream().cuda_stream)
+
+    def quantize(self, x):
+        self.hk.assert_cuda_ok(self.L.hpc_q8_quantize(self.C.c_void_p(x.data_ptr()), x.numel(), self.k, self.m,
+                                                      self.C.c_void_p(self.ws.data_ptr()), self.ws_bytes,
+                                                      self.stream()), "q8")
+
+    def matmul(self, handles, outs):
+        C = self.C
+        n = len(handles)
+        hs = (C.c_void_p * n)(*[h.handle for h in handles])
+        ps = (C.c_void_p * n)(*[o.data_ptr() for o in outs])
+        ls = (C.c_size_t * n)(*[o.numel() for o in outs])
+        self.hk.assert_cuda_ok(self.L.hpc_matmul_q8(n, hs, C.c_void_p(self.ws.data_ptr()), self.ws_bytes, self.k,
+                                                    self.m, ps, ls, self.stream()), "gemv")
+
+
+class GemvConfig2:
+    """the projections of one decoder layer, launched as the
+    decode step launches them: [Q, K, V] (one launch on one Q8_K input),
+    [gate, up] (one launch), and the Q6_K down projection.  M = --m."""
+    name = "gemv-config2"
+    unit = "GB/s"
+    dtype = "u8"
+    K, F = 2048, 16384
+    copies = 4
+
+    def __init__(self, m: int = 1):
+        import torch
+
+        from heliopause_b200 import kernels as hk
+        from heliopause_b200 import synthetic as syn
+        self.torch, self.hk, self.syn, self.M = torch, hk, syn, m
+        K, F = self.K, self.F
+        shapes = [("Q4_K", K, 2048), ("Q4_K", K, 512), ("Q4_K", K, 512), ("Q4_K", K, F), ("Q4_K", K, F),
+                  ("Q6_K", F, K)]
+        self.sets = []
+        for c in range(self.copies):
+            hs = [hk.create_quantized_weight_handle(t, syn.quant_weight(syn.Q4_K if t == "Q4_K" else syn.Q6_K, n, k,
+                                                                        seed=2000 + 10 * c + i), k, n)
+                  for i, (t, k, n) in enumerate(shapes)]
+            self.sets.append(hs)
+        self.w_bytes = sum(syn.row_bytes(syn.Q4_K if t == "Q4_K" else syn.Q6_K, k) * n for t, k, n in shapes)
+        self.algo_bytes = self.w_bytes + 4 * m * (K + F) + 4 * m * (2048 + 512 + 512 + 2 * F + K)
+        self.qin = _Q8Launcher(K, m)
+        self.qdown = _Q8Launcher(F, m)
+        self.x = torch.from_numpy(syn.activations(m, K, seed=7)).cuda()
+        self.a = torch.from_numpy(syn.activations(m, F, seed=8)).cuda()
+        self.outs = [torch.empty(n * m, device="cuda") for _, _, n in shapes]
+        self.i = 0
+
+    def step(self, ev=None):
+        hs = self.sets[self.i % self.copies]
+        self.i += 1
+        self.qin.quantize(self.x)
+        self.qin.matmul(hs[0:3], self.outs[0:3])
+        self.qin.matmul(hs[3:5], self.outs[3:5])
+        self.qdown.quantize(self.a)
+        self.qdown.matmul(hs[5:6], self.outs[5:6])
+
+    def e2e_step(self, host_x):
+        hs = self.sets[self.i % self.copies]
+        self.i += 1
+        for h, n in ((hs[0], 2048), (hs[3], self.F)):
+            self.hk.mat_mul_quantized_resident(h, host_x, self.K, n, self.M)  # host in -> host out
+
+    def host_input(self):
+        return self.syn.activations(self.M, self.K, seed=7), 4 * self.K * self.M, 4 * (2048 + self.F) * self.M
+
+    def units_per_step(self) -> float:
+        return self.algo_bytes / 1e9
+
+    def kernel_launch_count(self) -> int:
+        return 5
+
+    def roofline(self, peak_gbs: float) -> dict:
+        hs = [s[3:5] for s in self.sets]
+        launches = [lambda h=h: self.qin.matmul(h, self.outs[3:5]) for h in hs]
+        ms = graph_launch_times(launches * 2)
+        algo = 2 * self.syn.row_bytes(self.syn.Q4_K, self.K) * self.F + 4 * self.K * self.M + 8 * self.F * self.M
+        achieved = algo / (ms / 1e3) / 1e9
+        return {"bound": "hbm", "achieved": achieved, "peak": peak_gbs, "unit": "GB/s", "frac": achieved / peak_gbs,
+                "traffic": None, "kernel": f"gemv_kernel<{self.M}> (gate+up, 2048 -> 2x16384 Q4_K, M={self.M})",
+                "algorithmic_bytes_per_launch": algo, "launch_ms": ms}
+
+    def config(self) -> dict:
+        return {"workload": f"config-2 projections (QKV | gate+up | Q6_K down), M={self.M} (BASELINE config 2)",
+                "K": self.K, "ffn": self.F, "M": self.M, "weight_copies_rotated": self.copies,
+                "l2": f"inputs larger than L2: {self.copies} weight sets = "
+                      f"{self.copies * self.w_bytes / 1e6:.0f} MB rotated per step"}
+
+    def cpu_baseline(self, budget_s: float, threads: int) -> dict:
+        return None
+
+
+class LmHeadConfig5:
+    """BASELINE config 5 (single GPU, M = --m): Q6_K LM head 2048 -> 262,144
+    fused with top-40 (q8 quantize, GEMV + candidate lists, merge)."""
+    name = "lmhead-config5"
+    unit = "GB/s"
+    dtype = "u8"
+    K, V, TOPK = 2048, 262144, 40
+
+    def __init__(self, m: int = 1):
+        import ctypes as C
+
+        import torch
+
+        from heliopause_b200 import kernels as hk
+        from heliopause_b200 import synthetic as syn
+        self.torch, self.hk, self.syn, self.C, self.M = torch, hk, syn, C, m
+        self.head = hk.create_quantized_weight_handle("Q6_K", syn.q6_k_weight(self.V, self.K, seed=3000),
+                                                      self.K, self.V)
+        self.w_bytes = syn.row_bytes(syn.Q6_K, self.K) * self.V
+        self.algo_bytes = self.w_bytes + 4 * self.K * m + 8 * self.TOPK * m
+        self.q = _Q8Launcher(self.K, m)
+        cb = C.c_size_t()
+        hk.assert_cuda_ok(self.q.L.hpc_lm_head_candidates_bytes(self.head.handle, m, self.TOPK, C.byref(cb)), "cand")
+        self.cand_bytes = cb.value
+        self.cand = torch.empty(self.cand_bytes, dtype=torch.uint8, device="cuda")
+        self.x = torch.from_numpy(syn.activations(m, self.K, seed=9)).cuda()
+        self.ids = torch.empty(m * self.TOPK, dtype=torch.int32, device="cuda")
+        self.vals = torch.empty(m * self.TOPK, device="cuda")
+
+    def head_launch(self):
+        C, q = self.C, self.q
+        self.hk.assert_cuda_ok(q.L.hpc_lm_head_topk_q8(
+            self.head.handle, C.c_void_p(q.ws.data_ptr()), q.ws_bytes, self.K, self.M, self.TOPK, 0,
+            C.c_void_p(self.cand.data_ptr()), self.cand_bytes, C.c_float(0.0), C.c_void_p(self.ids.data_ptr()),
+            C.c_void_p(self.vals.data_ptr()), None, q.stream()), "lm head")
+
+    def step(self, ev=None):
+        self.q.quantize(self.x)
+        self.head_launch()
+
+    def e2e_step(self, host_x):
+        ids, vals = self.hk.lm_head_topk(self.head, host_x, self.M, self.TOPK)
+        ids.cpu()
+        vals.cpu()
+
+    def host_input(self):
+        return self.syn.activations(self.M, self.K, seed=9), 4 * self.K * self.M, 8 * self.TOPK * self.M
+
+    def units_per_step(self) -> float:
+        return self.algo_bytes / 1e9
+
+    def kernel_launch_count(self) -> int:
+        return 3
+
+    def roofline(self, peak_gbs: float) -> dict:
+        self.q.quantize(self.x)
+        ms = graph_launch_times([self.head_launch] * 4)
+        achieved = self.algo_bytes / (ms / 1e3) / 1e9
+        return {"bound": "hbm", "achieved": achieved, "peak": peak_gbs, "unit": "GB/s", "frac": achieved / peak_gbs,
+                "traffic": None, "kernel": f"lmhead_topk_kernel<{self.M}> + topk_merge_kernel (Q6_K 2048 -> 262144, "
+                                           f"top-{self.TOPK}, M={self.M})",
+                "algorithmic_bytes_per_launch": self.algo_bytes, "launch_ms": ms}
+
+    def config(self) -> dict:
+        return {"workload": f"Q6_K LM head 2048 -> 262144 + top-40, M={self.M} (BASELINE config 5, one GPU)",
+                "K": self.K, "vocab": self.V, "M": self.M, "top_k": self.TOPK,
+                "l2": f"inputs larger than L2: {self.w_bytes / 1e6:.0f} MB of weights per step"}
+
+    def cpu_baseline(self, budget_s: float, threads: int) -> dict:
+        return None
+
+
+WORKLOADS = {"decode-config3": DecodeConfig3, "gemv-config1": GemvConfig1, "gemv-config2": GemvConfig2,
+             "lmhead-config5": LmHeadConfig5}
 
 
 # ------------------------------------------------------------------- main ---
@@ -465,6 +656,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="decode-config3")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--m", type=int, default=1, help="columns (tokens) for the gemv-config2 / lmhead-config5 workloads")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -484,7 +676,8 @@ def main():
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
     hk.init_device(local)
-    wl = WORKLOADS[args.workload]()
+    wl = WORKLOADS[args.workload](args.m) if args.workload in ("gemv-config2", "lmhead-config5") \
+        else WORKLOADS[args.workload]()
 
     def barrier():
         if world > 1:
@@ -523,6 +716,9 @@ def main():
     if args.workload == "decode-config3":
         host_in = torch.tensor([12345], dtype=torch.int32).pin_memory()
         h2d, d2h = 8, 8 * wl.k
+    elif hasattr(wl, "host_input"):
+        hx, h2d, d2h = wl.host_input()
+        host_in = torch.from_numpy(hx).pin_memory()
     else:
         host_in = torch.from_numpy(wl.syn.activations(wl.M, wl.K, seed=7)).pin_memory()
         h2d, d2h = 4 * wl.K * wl.M, 4 * wl.N * wl.M
@@ -546,7 +742,7 @@ def main():
     prof = ROOT / "profiles" / "traffic.json"
     if prof.exists():
         tr = json.loads(prof.read_text()).get(wl.name)
-        if tr:
+        if tr and getattr(wl, "M", 1) == 1:  # the captures are M=1 launches
             roofline["traffic"] = tr
 
     cpu = None
