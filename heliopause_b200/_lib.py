@@ -37,6 +37,7 @@ SIGNATURES = {
     "hpc_q8_quantize": (_i, [_vp, _sz, _sz, _sz, _vp, _sz, _vp]),
     "hpc_matmul_q8": (_i, [_sz, C.POINTER(_vp), _vp, _sz, _sz, _sz, C.POINTER(_vp), C.POINTER(_sz), _vp]),
     "hpc_lm_head_topk": (_i, [_vp, _vp, _sz, _sz, _sz, _sz, C.c_int32, C.c_float, _vp, _vp, _vp]),
+    "hpc_lm_head_topk_noalloc": (_i, [_vp, _vp, _sz, _sz, _sz, _sz, C.c_int32, C.c_float, _vp, _vp, _vp]),
     "hpc_lm_head_candidates_bytes": (_i, [_vp, _sz, _sz, C.POINTER(_sz)]),
     "hpc_lm_head_topk_q8": (_i, [_vp, _vp, _sz, _sz, _sz, _sz, C.c_int32, _vp, _sz, C.c_float, _vp, _vp, _vp, _vp]),
     "hpc_topk_merge_keys": (_i, [_vp, _sz, _sz, _sz, C.c_float, _vp, _vp, _vp]),

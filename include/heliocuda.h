@@ -172,6 +172,27 @@ int hpc_lm_head_topk_q8(hpc_weight lm_head, const void *d_workspace, size_t work
 int hpc_topk_merge_keys(const uint64_t *d_keys, size_t group_count, size_t column_count, size_t k, float softcap,
                         int32_t *d_ids, float *d_vals, void *stream);
 
+/* ---- LM head + top-k with no allocation inside the call --------------------
+ * No reference counterpart: an addition for callers that may not allocate
+ * device memory while they serve (all of HBM handed to weights and the KV
+ * pool up front, stream-ordered memory pools unavailable, or no allocator
+ * calls allowed on the decode path).  Same arguments, checks and results as
+ * hpc_lm_head_topk, which takes its scratch from cudaMallocAsync; this one
+ * uses a file-scope device array of HPC_NOALLOC_SCRATCH_BYTES per device:
+ *   - a call needing more scratch (Q8_K workspace + candidate lists, e.g.
+ *     1.9 MB for 262,144 rows, 8 columns, k = 64) returns HPC_ERR_SHAPE;
+ *   - the array is shared by all calls on the device: calls that overlap in
+ *     time (other streams or threads) race on it, so serialize them;
+ *   - after a call it holds that call's Q8_K activations and candidate keys;
+ *     nothing in it needs to start at zero;
+ *   - the first call on each device does one-time set-up
+ *     (cudaGetSymbolAddress, kernel attributes): make it outside any stream
+ *     capture. */
+#define HPC_NOALLOC_SCRATCH_BYTES (4u << 20)
+int hpc_lm_head_topk_noalloc(hpc_weight lm_head, const float *d_hidden, size_t hidden_len, size_t input_size,
+                             size_t column_count, size_t k, int32_t id_offset, float softcap, int32_t *d_ids,
+                             float *d_vals, void *stream);
+
 /* ---- resident decoder model: decode / batched verify step ------------------
  * A Gemma-4-style decoder (pre/post RMSNorm sandwich, per-head QK norm, NeoX
  * RoPE, GQA over an fp32 KV cache, GEGLU FFN, tied Q6_K/Q4_K embedding / LM
