@@ -533,9 +533,24 @@ class LmHeadConfig5:
         from heliopause_b200 import kernels as hk
         from heliopause_b200 import synthetic as syn
         self.torch, self.hk, self.syn, self.C, self.M = torch, hk, syn, C, m
-        self.head = hk.create_quantized_weight_handle("Q6_K", syn.q6_k_weight(self.V, self.K, seed=3000),
-                                                      self.K, self.V)
+        world, rank, _ = _dist()
+        self.world = world
+        self.scaling = "strong" if world > 1 else "weak"
+        full = syn.q6_k_weight(self.V, self.K, seed=3000)
         self.w_bytes = syn.row_bytes(syn.Q6_K, self.K) * self.V
+        if world > 1:
+            # vocabulary rows split over the ranks; keys all-gathered over NCCL
+            from heliopause_b200 import sharded_head as sh
+            first, n = sh.shard_rows(self.V, world)[rank]
+            rb = syn.row_bytes(syn.Q6_K, self.K)
+            self.backend = sh.CudaShardBackend("Q6_K", full[first * rb:(first + n) * rb], self.K, n, first, m,
+                                               self.TOPK)
+            self.sharded = sh.ShardedLmHead(self.backend, self.TOPK)
+            self.x = torch.from_numpy(syn.activations(m, self.K, seed=9)).cuda()
+            self.algo_bytes = self.w_bytes + 4 * self.K * m + 8 * self.TOPK * m
+            self.head = self.backend.handle
+            return
+        self.head = hk.create_quantized_weight_handle("Q6_K", full, self.K, self.V)
         self.algo_bytes = self.w_bytes + 4 * self.K * m + 8 * self.TOPK * m
         self.q = _Q8Launcher(self.K, m)
         cb = C.c_size_t()
@@ -554,11 +569,17 @@ class LmHeadConfig5:
             C.c_void_p(self.vals.data_ptr()), None, q.stream()), "lm head")
 
     def step(self, ev=None):
+        if self.world > 1:
+            self.sharded.topk(self.x, self.M)
+            return
         self.q.quantize(self.x)
         self.head_launch()
 
     def e2e_step(self, host_x):
-        ids, vals = self.hk.lm_head_topk(self.head, host_x, self.M, self.TOPK)
+        if self.world > 1:
+            ids, vals = self.sharded.topk(host_x.to("cuda", non_blocking=True), self.M)
+        else:
+            ids, vals = self.hk.lm_head_topk(self.head, host_x, self.M, self.TOPK)
         ids.cpu()
         vals.cpu()
 
@@ -569,9 +590,12 @@ class LmHeadConfig5:
         return self.algo_bytes / 1e9
 
     def kernel_launch_count(self) -> int:
-        return 3
+        return 4 if self.world > 1 else 3
 
     def roofline(self, peak_gbs: float) -> dict:
+        if self.world > 1:
+            return {"bound": "hbm", "achieved": None, "peak": peak_gbs, "unit": "GB/s", "frac": None,
+                    "traffic": None, "kernel": "row-sharded head: per-rank roofline is the 1-GPU line"}
         self.q.quantize(self.x)
         ms = graph_launch_times([self.head_launch] * 4)
         achieved = self.algo_bytes / (ms / 1e3) / 1e9
@@ -704,7 +728,9 @@ def main():
 
     with ClockSampler(local) as clk:
         ms = timed(wl.step, args.steps)
-    value = wl.units_per_step() * world / (ms / 1e3)
+    # weak scaling: every rank processes its own step; strong: one step's work is split over the ranks
+    ranks_of_work = world if getattr(wl, "scaling", "weak") == "weak" else 1
+    value = wl.units_per_step() * ranks_of_work / (ms / 1e3)
 
     verify = None
     if hasattr(wl, "verify_step"):
@@ -734,7 +760,7 @@ def main():
     e2e_s = torch.tensor([(time.perf_counter() - t0) / n_e2e], device="cuda", dtype=torch.float64)
     if world > 1:
         dist.all_reduce(e2e_s, op=dist.ReduceOp.MAX)
-    e2e_value = wl.units_per_step() * world / float(e2e_s[0])
+    e2e_value = wl.units_per_step() * ranks_of_work / float(e2e_s[0])
 
     peaks = _peaks()
     roofline = wl.roofline(peaks["hbm_gbs"])
@@ -742,7 +768,7 @@ def main():
     prof = ROOT / "profiles" / "traffic.json"
     if prof.exists():
         tr = json.loads(prof.read_text()).get(wl.name)
-        if tr and getattr(wl, "M", 1) == 1:  # the captures are M=1 launches
+        if tr and getattr(wl, "M", 1) == 1 and world == 1:  # the captures are 1-GPU, M=1 launches
             roofline["traffic"] = tr
 
     cpu = None
@@ -752,8 +778,8 @@ def main():
 
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": wl.unit, "n_gpus": world, "steps": args.steps,
-                "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-                "vs_baseline": None, "dtype": wl.dtype, "data": "synthetic (seeded, BASELINE distributions)",
+                "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+                "scaling": getattr(wl, "scaling", "weak"), "vs_baseline": None, "dtype": wl.dtype, "data": "synthetic (seeded, BASELINE distributions)",
                 "config": wl.config(), "roofline": roofline, "cpu_baseline": cpu,
                 "e2e": {"value": e2e_value, "unit": wl.unit, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
                 "gpu_launches": wl.kernel_launch_count() * args.steps, "clocks": clk.summary()}

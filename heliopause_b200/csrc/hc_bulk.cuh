@@ -1,6 +1,6 @@
 // hc_bulk.cuh -- one-shot bulk prefetch of weight units into shared memory.
 //
-// cp.async.bulk (no multicast) copies a CTA's weight units from HBM into
+// cp.async.bulk (plain form, one CTA as destination) copies a CTA's weight units from HBM into
 // shared memory with completion on one mbarrier.  The copies are issued
 // before griddepcontrol.wait, so under programmatic dependent launch the
 // whole weight fetch of a small GEMV overlaps the previous kernel.  The wait
