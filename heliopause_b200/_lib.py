@@ -43,6 +43,8 @@ SIGNATURES = {
     "hpc_topk_merge_keys": (_i, [_vp, _sz, _sz, _sz, C.c_float, _vp, _vp, _vp]),
     "hpc_model_create": (_i, [_vp, C.POINTER(_vp)]),
     "hpc_model_release": (_i, [_vp]),
+    "hpc_model_set_persistent": (_i, [_vp, _i]),
+    "hpc_model_step_kind": (_i, [_vp, _sz, C.POINTER(_i)]),
     "hpc_model_set_weight": (_i, [_vp, _i, _i, _vp]),
     "hpc_model_set_norm": (_i, [_vp, _i, _i, _vp, _sz]),
     "hpc_model_set_lm_head": (_i, [_vp, _vp]),

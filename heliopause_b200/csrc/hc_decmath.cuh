@@ -1,0 +1,110 @@
+// hc_decmath.cuh -- device arithmetic of the decoder layer math shared by the
+// per-kernel decode step (hc_decode.cu) and the persistent step kernel
+// (hc_persist.cu): programmatic-dependent-launch controls, the two f16
+// codecs of the reference, f64 reductions and the GEGLU activation.  Every
+// rounding point follows packages/engine/src/runner/wasm/layers.ts and
+// packages/engine/wasm-kernels/src/lib.rs as cited per function.
+#pragma once
+#include <cmath>
+
+#include <cuda_fp16.h>
+
+#include "hc_common.cuh"
+
+namespace hc {
+
+__device__ __forceinline__ void pdl_trigger() {
+#if __CUDA_ARCH__ >= 900
+  asm volatile("griddepcontrol.launch_dependents;");
+#endif
+}
+__device__ __forceinline__ void pdl_wait() {
+#if __CUDA_ARCH__ >= 900
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+#endif
+}
+
+// ---- f16 codecs ---------------------------------------------------------------
+
+// quant.ts:632-669 float32ToFloat16 (the TS codec used by layers.ts): round
+// to nearest even, |x| >= 65504 clamps to 65504, |x| < 2^-24 flushes to zero.
+__device__ __forceinline__ float round_f16_ts(float x) {
+  const float a = fabsf(x);
+  if (x != x) return x;
+  if (a >= 65504.0f) return a == INFINITY ? x : copysignf(65504.0f, x);
+  if (a < 5.9604644775390625e-8f) return copysignf(0.0f, x);
+  return __half2float(__float2half_rn(x));
+}
+
+// lib.rs:2534-2568 float32_to_float16 (the Rust codec used for the attention
+// query, lib.rs:590-597): the dropped bits round half UP, overflow clamps to
+// 0x7bff, NaN -> 0x7e00.  Returns the f16 value widened back to f32.
+__device__ __forceinline__ float round_f16_rust(float v) {
+  const uint32_t bits = __float_as_uint(v);
+  const uint32_t sign = (bits >> 16) & 0x8000u;
+  const int exp = int((bits >> 23) & 0xff);
+  const uint32_t mant = bits & 0x7fffffu;
+  uint32_t h;
+  if (exp == 0xff) {
+    h = mant == 0 ? (sign | 0x7c00u) : 0x7e00u;
+  } else {
+    const int he = exp - 127 + 15;
+    if (he >= 31) {
+      h = sign | 0x7bffu;
+    } else if (he <= 0) {
+      if (he < -10) {
+        h = sign;
+      } else {
+        const uint32_t m = mant | 0x800000u;
+        const uint32_t shift = uint32_t(14 - he);
+        h = sign | ((m + (1u << (shift - 1))) >> shift);
+      }
+    } else {
+      const uint32_t rm = mant + 0x1000u;
+      if (rm & 0x800000u) {
+        const int re = he + 1;
+        h = re >= 31 ? (sign | 0x7bffu) : (sign | uint32_t(re << 10));
+      } else {
+        h = sign | uint32_t(he << 10) | (rm >> 13);
+      }
+    }
+  }
+  return f16_bits_to_f32(h);
+}
+
+// ---- block reductions -----------------------------------------------------------
+
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+  return v;
+}
+
+// Sum over a CTA of `warps` warps (all threads call it).
+__device__ __forceinline__ double block_sum_d(double v, double* scratch, int warps) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  v = warp_sum_d(v);
+  __syncthreads();
+  if (lane == 0) scratch[warp] = v;
+  __syncthreads();
+  double t = 0.0;
+  for (int w = 0; w < warps; ++w) t += scratch[w];
+  return t;
+}
+
+// layers.ts:1062-1076 gelu (tanh form) with the TS f16 codec on input and
+// output; |x| >= 10 short-circuits.
+__device__ __forceinline__ double gelu_ts(float v) {
+  if (v <= -10.0f) return 0.0;
+  if (v >= 10.0f) return double(v);
+  const double x = double(round_f16_ts(v));
+  const float xx = float(x * x);
+  const float poly = float(1.0 + double(float(0.044715 * double(xx))));
+  const float lin = float(0.7978845608028654 * x);  // Math.sqrt(2 / Math.PI) as a double
+  const float inner = float(double(lin) * double(poly));
+  const float hlf = float(0.5 * x);
+  const float act = float(double(hlf) * double(float(1.0 + tanh(double(inner)))));
+  return double(round_f16_ts(act));
+}
+
+}  // namespace hc

@@ -27,90 +27,12 @@
 
 #include "hc_bulk.cuh"
 #include "hc_common.cuh"
+#include "hc_decmath.cuh"
 #include "hc_decode.cuh"
 #include "hc_q8.cuh"
 #include "hc_unpack.cuh"
 
 namespace hc {
-
-__device__ __forceinline__ void pdl_trigger() {
-#if __CUDA_ARCH__ >= 900
-  asm volatile("griddepcontrol.launch_dependents;");
-#endif
-}
-__device__ __forceinline__ void pdl_wait() {
-#if __CUDA_ARCH__ >= 900
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-#endif
-}
-
-// ---- f16 codecs ---------------------------------------------------------------
-
-// quant.ts:632-669 float32ToFloat16 (the TS codec used by layers.ts): round
-// to nearest even, |x| >= 65504 clamps to 65504, |x| < 2^-24 flushes to zero.
-__device__ __forceinline__ float round_f16_ts(float x) {
-  const float a = fabsf(x);
-  if (x != x) return x;
-  if (a >= 65504.0f) return a == INFINITY ? x : copysignf(65504.0f, x);
-  if (a < 5.9604644775390625e-8f) return copysignf(0.0f, x);
-  return __half2float(__float2half_rn(x));
-}
-
-// lib.rs:2534-2568 float32_to_float16 (the Rust codec used for the attention
-// query, lib.rs:590-597): the dropped bits round half UP, overflow clamps to
-// 0x7bff, NaN -> 0x7e00.  Returns the f16 value widened back to f32.
-__device__ __forceinline__ float round_f16_rust(float v) {
-  const uint32_t bits = __float_as_uint(v);
-  const uint32_t sign = (bits >> 16) & 0x8000u;
-  const int exp = int((bits >> 23) & 0xff);
-  const uint32_t mant = bits & 0x7fffffu;
-  uint32_t h;
-  if (exp == 0xff) {
-    h = mant == 0 ? (sign | 0x7c00u) : 0x7e00u;
-  } else {
-    const int he = exp - 127 + 15;
-    if (he >= 31) {
-      h = sign | 0x7bffu;
-    } else if (he <= 0) {
-      if (he < -10) {
-        h = sign;
-      } else {
-        const uint32_t m = mant | 0x800000u;
-        const uint32_t shift = uint32_t(14 - he);
-        h = sign | ((m + (1u << (shift - 1))) >> shift);
-      }
-    } else {
-      const uint32_t rm = mant + 0x1000u;
-      if (rm & 0x800000u) {
-        const int re = he + 1;
-        h = re >= 31 ? (sign | 0x7bffu) : (sign | uint32_t(re << 10));
-      } else {
-        h = sign | uint32_t(he << 10) | (rm >> 13);
-      }
-    }
-  }
-  return f16_bits_to_f32(h);
-}
-
-// ---- block reductions -----------------------------------------------------------
-
-__device__ __forceinline__ double warp_sum_d(double v) {
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
-  return v;
-}
-
-// Sum over a CTA of `warps` warps (all threads call it).
-__device__ __forceinline__ double block_sum_d(double v, double* scratch, int warps) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  v = warp_sum_d(v);
-  __syncthreads();
-  if (lane == 0) scratch[warp] = v;
-  __syncthreads();
-  double t = 0.0;
-  for (int w = 0; w < warps; ++w) t += scratch[w];
-  return t;
-}
 
 // ---- RoPE table -------------------------------------------------------------------
 
@@ -245,8 +167,10 @@ __global__ void norm_quant_kernel(float* __restrict__ x, const float* __restrict
 // warps [0, H) are query heads, [H, H + KVH) key heads, [H + KVH, H + 2 KVH)
 // value heads.  Query: normHeads + ropeNeox (layers.ts:201-224); key: same
 // with the key norm, then written to K[slot][kvh][:] (layers.ts:241-268);
-// value: rmsNormRowsNoWeight (layers.ts:248-253) written to V[:][kvh][slot]
-// (updateFullAttentionCache, layers.ts:887-911).
+// value: rmsNormRowsNoWeight (layers.ts:248-253) written to V[slot][kvh][:]
+// (updateFullAttentionCache, layers.ts:887-911, stores V dimension-major as
+// [dim][kvh][slot]; here V is token-major like K so one token's values are
+// one contiguous 1 KB row for the bulk-copy staging).
 __global__ void qkv_post_kernel(const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v,
                                 const float* __restrict__ qnw, const float* __restrict__ knw,
                                 const int32_t* __restrict__ pos, const double* __restrict__ cos_t,
@@ -305,8 +229,9 @@ __global__ void qkv_post_kernel(const float* __restrict__ q, const float* __rest
       o[0] = make_float4(n[0], n[1], n[2], n[3]);
       o[1] = make_float4(n[4], n[5], n[6], n[7]);
     } else {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) vc[(size_t(8 * lane + i) * KVH + head) * cap + slot] = n[i];
+      float4* o = reinterpret_cast<float4*>(vc + (size_t(slot) * KVH + head) * HD + 8 * lane);
+      o[0] = make_float4(n[0], n[1], n[2], n[3]);
+      o[1] = make_float4(n[4], n[5], n[6], n[7]);
     }
   }
 }
@@ -317,8 +242,8 @@ __global__ void qkv_post_kernel(const float* __restrict__ q, const float* __rest
 // lib.rs:539-654, on the compacted full-attention range [0, pos+1)).  Grid
 // (chunks, KVH); a CTA serves all M tokens x (H/KVH) query heads of one KV
 // head over one ATT_CHUNK-token slice of the cache.  Warp 0 issues bulk
-// copies of the slice (ATT_CHUNK K rows of 1 KB, HD V rows of ATT_CHUNK*4 B)
-// into padded shared-memory rows (bank-conflict-free float4 reads),
+// copies of the slice (ATT_CHUNK K rows and ATT_CHUNK V rows of 1 KB each)
+// into padded shared-memory rows (bank-conflict-free reads),
 // completing on an mbarrier.  A slice that holds none of this step's new
 // rows (every chunk but the one or two around pos) was written by earlier
 // steps, so its copies are issued before griddepcontrol.wait and overlap the
@@ -327,7 +252,6 @@ __global__ void qkv_post_kernel(const float* __restrict__ q, const float* __rest
 // softmax (max, sum of f64 exp) and the partial output p*v are written for
 // the combine kernel.
 constexpr int ATT_KSTRIDE = 256 + 4;        // floats per staged K row
-constexpr int ATT_VSTRIDE = ATT_CHUNK + 4;  // floats per staged V row
 
 __global__ void __launch_bounds__(ATT_THREADS) attn_partial_kernel(
     const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
@@ -340,8 +264,8 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_partial_kernel(
   const int chunk = blockIdx.x, kvh = blockIdx.y;
   const int G = H / KVH, NQ = M * G;
   float* ks = sm;                     // [CH][ATT_KSTRIDE]
-  float* vs = ks + CH * ATT_KSTRIDE;  // [HD][ATT_VSTRIDE]
-  float* qs = vs + HD * ATT_VSTRIDE;  // [NQ][HD]
+  float* vs = ks + CH * ATT_KSTRIDE;  // [CH][ATT_KSTRIDE]
+  float* qs = vs + CH * ATT_KSTRIDE;  // [NQ][HD]
   float* ps = qs + NQ * HD;           // [NQ][CH]
   pdl_trigger();
   // pos is written before the step starts (not by a kernel of this step)
@@ -369,8 +293,8 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_partial_kernel(
     __syncwarp();
     for (int t = threadIdx.x; t < CH; t += 32)
       bulk_copy_g2s(ks + t * ATT_KSTRIDE, kc + (size_t(t0 + t) * KVH + kvh) * HD, HD * 4, &bar);
-    for (int d = threadIdx.x; d < HD; d += 32)
-      bulk_copy_g2s(vs + d * ATT_VSTRIDE, vc + (size_t(d) * KVH + kvh) * cap + t0, CH * 4, &bar);
+    for (int t = threadIdx.x; t < CH; t += 32)
+      bulk_copy_g2s(vs + t * ATT_KSTRIDE, vc + (size_t(t0 + t) * KVH + kvh) * HD, HD * 4, &bar);
   };
   if (threadIdx.x < 32 && !fresh) issue();
   pdl_wait();
@@ -425,20 +349,21 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_partial_kernel(
     }
   }
   __syncthreads();
-  // partial outputs: thread d holds V row d (contiguous over tokens) and
-  // serves four queries per pass; the probabilities are broadcast reads
+  // partial outputs: thread d walks column d of the staged V rows (a warp
+  // reads 32 consecutive floats of a row) and serves four queries per pass;
+  // the probabilities are broadcast reads
   const int d = threadIdx.x;
-  const float4* vr = reinterpret_cast<const float4*>(vs + d * ATT_VSTRIDE);
   for (int qg = 0; qg < NQ; qg += 4) {
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll 4
     for (int j = 0; j < CH / 4; ++j) {
-      const float4 b = vr[j];
+      const float b[4] = {vs[(4 * j) * ATT_KSTRIDE + d], vs[(4 * j + 1) * ATT_KSTRIDE + d],
+                          vs[(4 * j + 2) * ATT_KSTRIDE + d], vs[(4 * j + 3) * ATT_KSTRIDE + d]};
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
         if (qg + u < NQ) {
           const float4 a = reinterpret_cast<const float4*>(ps + (qg + u) * CH)[j];
-          acc[u] += a.x * b.x + a.y * b.y + a.z * b.z + a.w * b.w;
+          acc[u] += a.x * b[0] + a.y * b[1] + a.z * b[2] + a.w * b[3];
         }
       }
     }
@@ -526,22 +451,7 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(const float* __restri
   }
 }
 
-// ---- GEGLU ------------------------------------------------------------------------------
-
-// layers.ts:1062-1076 gelu (tanh form) with the TS f16 codec on input and
-// output; |x| >= 10 short-circuits.
-__device__ __forceinline__ double gelu_ts(float v) {
-  if (v <= -10.0f) return 0.0;
-  if (v >= 10.0f) return double(v);
-  const double x = double(round_f16_ts(v));
-  const float xx = float(x * x);
-  const float poly = float(1.0 + double(float(0.044715 * double(xx))));
-  const float lin = float(0.7978845608028654 * x);  // Math.sqrt(2 / Math.PI) as a double
-  const float inner = float(double(lin) * double(poly));
-  const float hlf = float(0.5 * x);
-  const float act = float(double(hlf) * double(float(1.0 + tanh(double(inner)))));
-  return double(round_f16_ts(act));
-}
+// ---- GEGLU ----------------------------------------------------------------------------
 
 // act = fround(gelu(gate) * up) for 8 blocks per CTA (warp = block), quantized
 // for the down projection.  Grid (F/2048, M).
@@ -612,8 +522,7 @@ cudaError_t launch_qkv_post(const float* q, const float* k, const float* v, cons
 
 size_t attn_smem_bytes(int M, int H, int KVH) {
   const int NQ = M * (H / KVH);
-  return sizeof(float) * (size_t(ATT_CHUNK) * ATT_KSTRIDE + size_t(256) * ATT_VSTRIDE + size_t(NQ) * 256 +
-                          size_t(NQ) * ATT_CHUNK);
+  return sizeof(float) * (size_t(ATT_CHUNK) * ATT_KSTRIDE * 2 + size_t(NQ) * 256 + size_t(NQ) * ATT_CHUNK);
 }
 
 cudaError_t launch_attention(const float* q, const float* kc, const float* vc, const int32_t* pos, int M, int H,

@@ -231,18 +231,32 @@ class CudaDecoderModel:
             v[:, :, :filled].normal_(generator=gen)
 
     def kv(self, kv_layer: int) -> tuple[torch.Tensor, torch.Tensor]:
-        """Views of one KV layer's cache: K [context][kv_heads][head_dim],
-        V [head_dim][kv_heads][context]."""
+        """Views of one KV layer's cache in the reference's orientation: K
+        [context][kv_heads][head_dim] and V [head_dim][kv_heads][context]
+        (layers.ts:887-911).  The device stores V token-major
+        ([context][kv_heads][head_dim], like K), so the V view is a permuted,
+        non-contiguous view of that storage."""
         k = C.c_void_p()
         v = C.c_void_p()
         hk.assert_cuda_ok(_lib.lib().hpc_model_kv(self._h, kv_layer, C.byref(k), C.byref(v)), "modelKv")
         s = self.shape
         n = s.context * s.kv_heads * s.head_dim
         kt = _wrap_device(k.value, n).view(s.context, s.kv_heads, s.head_dim)
-        vt = _wrap_device(v.value, n).view(s.head_dim, s.kv_heads, s.context)
+        vt = _wrap_device(v.value, n).view(s.context, s.kv_heads, s.head_dim).permute(2, 1, 0)
         return kt, vt
 
     # ---- running -----------------------------------------------------------
+    def set_persistent(self, enable: bool) -> None:
+        """Single-token steps through the persistent step kernel (default) or
+        the per-kernel chain (hpc_model_set_persistent)."""
+        hk.assert_cuda_ok(_lib.lib().hpc_model_set_persistent(self._h, int(bool(enable))), "modelSetPersistent")
+
+    def step_kind(self, token_count: int = 1) -> int:
+        """1 if the last built step for token_count tokens is the persistent kernel."""
+        out = C.c_int()
+        hk.assert_cuda_ok(_lib.lib().hpc_model_step_kind(self._h, token_count, C.byref(out)), "modelStepKind")
+        return out.value
+
     def forward(self, token_ids, positions, top_k: int, *, return_hidden: bool = False):
         """Top-k (ids, values) of every position, [n][top_k] torch tensors."""
         ids = torch.as_tensor(token_ids, dtype=torch.int32).reshape(-1)

@@ -248,8 +248,21 @@ int hpc_model_set_weight(hpc_model model, int layer, int slot, hpc_weight weight
 int hpc_model_set_norm(hpc_model model, int layer, int slot, const float *host_values, size_t len);
 /* token_embd.weight == output weight (tied): rows are vocabulary ids. */
 int hpc_model_set_lm_head(hpc_model model, hpc_weight weight);
-/* Device pointers of one KV layer's cache: K [context][kv_heads][head_dim],
- * V [head_dim][kv_heads][context] (layers.ts:887-911 layout). */
+/* Selects how a single-token step runs: enable != 0 uses the persistent
+ * step kernel -- all layers in one cooperative launch, weights streamed
+ * through shared-memory rings -- when the model's shapes allow it (hidden
+ * 2048); 0 (the default) runs the per-kernel step.  Multi-token steps always
+ * run per kernel. */
+int hpc_model_set_persistent(hpc_model model, int enable);
+
+/* 1 if the last built step for `token_count` tokens is the persistent kernel,
+ * else 0 (valid after a forward of that token count). */
+int hpc_model_step_kind(hpc_model model, size_t token_count, int *out_kind);
+
+/* Device pointers of one KV layer's cache, f32: K [context][kv_heads][head_dim]
+ * (the layers.ts:887-911 layout) and V [context][kv_heads][head_dim] -- V is
+ * token-major like K, the transpose of the reference's [head_dim][kv_heads]
+ * [context], so that one token's values are one contiguous row. */
 int hpc_model_kv(hpc_model model, int kv_layer, float **d_key, float **d_value);
 /* One forward over token_count tokens at the given positions (all device
  * pointers).  Writes top-k ids/values [token_count][top_k] for every position
