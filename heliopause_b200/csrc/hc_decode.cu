@@ -453,29 +453,28 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(const float* __restri
 
 // ---- GEGLU ----------------------------------------------------------------------------
 
-// act = fround(gelu(gate) * up) for 8 blocks per CTA (warp = block), quantized
-// for the down projection.  Grid (F/2048, M).
-__global__ void geglu_quant_kernel(const float* __restrict__ gate, const float* __restrict__ up, int F, Q8Buf q,
-                                   float* __restrict__ act_out) {
-  __shared__ __align__(16) uint8_t stage[8][256];
+// act = fround(gelu(gate) * up), quantized for the down projection.  One CTA
+// per 256-block of one column, thread t = element t: the f64 tanh of the
+// GELU (~1k cycles) runs once per thread, all blocks in parallel; warp 0 then
+// quantizes the block.  Grid (F/256, M).
+__global__ void __launch_bounds__(256) geglu_quant_kernel(const float* __restrict__ gate, const float* __restrict__ up,
+                                                          int F, Q8Buf q, float* __restrict__ act_out) {
+  __shared__ float vals[256];
+  __shared__ __align__(16) uint8_t stage[256];
   pdl_trigger();
   pdl_wait();
-  const int m = blockIdx.y, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int b = blockIdx.x * 8 + warp;
-  const size_t base = size_t(m) * F + size_t(b) * 256 + 8 * lane;
-  const float4 g0 = reinterpret_cast<const float4*>(gate + base)[0], g1 = reinterpret_cast<const float4*>(gate + base)[1];
-  const float4 u0 = reinterpret_cast<const float4*>(up + base)[0], u1 = reinterpret_cast<const float4*>(up + base)[1];
-  const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
-  const float u[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
-  float a[8];
+  const int m = blockIdx.y, b = blockIdx.x, t = threadIdx.x, lane = t & 31;
+  const size_t e = size_t(m) * F + size_t(b) * 256 + t;
+  const float a = float(gelu_ts(gate[e]) * double(up[e]));
+  vals[t] = a;
+  if (act_out) act_out[e] = a;
+  __syncthreads();
+  if (t < 32) {
+    float v8[8];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) a[i] = float(gelu_ts(g[i]) * double(u[i]));
-  if (act_out) {
-    float4* ao = reinterpret_cast<float4*>(act_out + base);
-    ao[0] = make_float4(a[0], a[1], a[2], a[3]);
-    ao[1] = make_float4(a[4], a[5], a[6], a[7]);
+    for (int i = 0; i < 8; ++i) v8[i] = vals[8 * lane + i];
+    q8k_block_warp(v8, lane, stage, q8_rec_a(q, m, b), q8_rec_b(q, m, b));
   }
-  q8k_block_warp(a, lane, stage[warp], q8_rec_a(q, m, b), q8_rec_b(q, m, b));
 }
 
 // ---- launch helpers ---------------------------------------------------------------------
@@ -549,7 +548,7 @@ cudaError_t launch_attn_combine(const float* part_m, const float* part_l, const 
 
 cudaError_t launch_geglu_quant(const float* gate, const float* up, int M, int F, const Q8Buf& q, float* act_out,
                                cudaStream_t st) {
-  return pdl_launch(geglu_quant_kernel, dim3(F / 2048, M), dim3(256), 0, st, gate, up, F, q, act_out);
+  return pdl_launch(geglu_quant_kernel, dim3(F / 256, M), dim3(256), 0, st, gate, up, F, q, act_out);
 }
 
 }  // namespace hc

@@ -343,6 +343,9 @@ static int build_persist_plan(hpc_model m) {
     bool ok = own ? gemv(P.qkv, {L.w[HPC_W_Q], L.w[HPC_W_K], L.w[HPC_W_V]}, 0) : gemv(P.qkv, {L.w[HPC_W_Q]}, 0);
     ok = ok && gemv(P.o, {L.w[HPC_W_O]}, 1) && gemv(P.gu, {L.w[HPC_W_GATE], L.w[HPC_W_UP]}, 2) &&
          gemv(P.down, {L.w[HPC_W_DOWN]}, 3);
+    // a CTA's gate/up range may complete at most 16 activation blocks
+    const int gu_units = P.gu.tiles * P.gu.B;
+    if ((gu_units + grid - 1) / grid / (P.gu.B * 8) + 2 > 16) ok = false;
     if (!ok) return HPC_OK;
     P.n_attn = L.norm[HPC_N_ATTN];
     P.n_q = L.norm[HPC_N_Q];
@@ -358,7 +361,9 @@ static int build_persist_plan(hpc_model m) {
   size_t off[9], total = 0;
   const size_t sizes[9] = {part_floats[0] * 4, part_floats[1] * 4, part_floats[2] * 4, part_floats[3] * 4,
                            size_t(grid) * hc::P_ATT_REC * 4, hc::q8buf_bytes(D, 1), hc::q8buf_bytes(F, 1),
-                           size_t(D) * 4, (size_t(c.layers) * hc::PS_COUNT + 1) * hc::P_CTR_STRIDE * 4};
+                           size_t(D) * 4,
+                           ((size_t(c.layers) * hc::PS_COUNT + 1) * hc::P_CTR_STRIDE + size_t(c.layers) * (KVH + F / 256)) *
+                               4};
   for (int i = 0; i < 9; ++i) {
     off[i] = total;
     total += al(sizes[i]);
@@ -395,6 +400,8 @@ static int build_persist_plan(hpc_model m) {
   P.H1 = reinterpret_cast<float*>(b + off[7]);
   P.counters = reinterpret_cast<unsigned*>(b + off[8]);
   P.abort_word = reinterpret_cast<int*>(P.counters + size_t(c.layers) * hc::PS_COUNT * hc::P_CTR_STRIDE);
+  P.kvh_counters = P.counters + (size_t(c.layers) * hc::PS_COUNT + 1) * hc::P_CTR_STRIDE;
+  P.blk_counters = P.kvh_counters + size_t(c.layers) * KVH;
   P.err = m->err;
   m->persist_ctr_bytes = sizes[8];
   m->persist_grid = grid;

@@ -157,56 +157,59 @@ __device__ __forceinline__ int gemv_nseg(int B, int U, int t, int grid) {
 
 // Sums of a GEMV stage's partials for output rows of the concatenated tile
 // list, in CTA order.
-// The same for NR rows (rows[i] < 0: skipped, out 0): every load is issued
-// before the first add.
+// The same for NR rows (rows[i] < 0: skipped, out 0).  Loads are
+// unconditional (segment index clamped to the tile's last partial, the extra
+// terms added as zero), so the compiler keeps them all in flight; the sums
+// run in segment order.
 template <int NR>
 __device__ __forceinline__ void gemv_rows(const PGemv& g, const int (&rows)[NR], int grid, float (&out)[NR]) {
   const int B = pl_i(g.B), U = pl_i(g.tiles) * B, ms = pl_i(g.maxseg);
   const float* part = pl_p(g.part);
-  float v[NR][P_MAXSEG];
   int n[NR];
+  const float* src[NR];
 #pragma unroll
   for (int r = 0; r < NR; ++r) {
-    const int t = rows[r] >> 5;
+    const int row = rows[r] >= 0 ? rows[r] : 0, t = row >> 5;
     n[r] = rows[r] >= 0 ? gemv_nseg(B, U, t, grid) : 0;
-    const float* src = part + (size_t(t) * ms) * 32 + (rows[r] & 31);
-#pragma unroll
-    for (int k = 0; k < P_MAXSEG; ++k) v[r][k] = k < n[r] ? __ldcg(src + k * 32) : 0.0f;
+    src[r] = part + (size_t(t) * ms) * 32 + (row & 31);
+    out[r] = 0.0f;
   }
+  for (int k0 = 0; k0 < ms; k0 += 4) {
+    float v[NR][4];
 #pragma unroll
-  for (int r = 0; r < NR; ++r) {
-    float acc = 0.0f;
+    for (int r = 0; r < NR; ++r)
 #pragma unroll
-    for (int k = 0; k < P_MAXSEG; ++k)
-      if (k < n[r]) acc += v[r][k];
-    out[r] = acc;
+      for (int k = 0; k < 4; ++k) v[r][k] = __ldcg(src[r] + min(k0 + k, max(n[r], 1) - 1) * 32);
+#pragma unroll
+    for (int r = 0; r < NR; ++r)
+#pragma unroll
+      for (int k = 0; k < 4; ++k) out[r] += k0 + k < n[r] ? v[r][k] : 0.0f;
   }
 }
 
-// The same for 8 consecutive rows row0..row0+7 (row0 % 8 == 0, one tile):
-// the partials are loaded four segments at a time (one round for the
-// common <= 4), every load of a round issued before its adds.
+// The same for 8 consecutive rows row0..row0+7 (row0 % 8 == 0, one tile),
+// float4 loads, unconditional (clamped) as above.
 __device__ __forceinline__ void gemv_rows8(const PGemv& g, int row0, int grid, float (&out)[8]) {
-  const int B = pl_i(g.B), t = row0 >> 5, n = gemv_nseg(B, pl_i(g.tiles) * B, t, grid);
-  const float4* src =
-      reinterpret_cast<const float4*>(pl_p(g.part) + (size_t(t) * pl_i(g.maxseg)) * 32 + (row0 & 31));
+  const int B = pl_i(g.B), t = row0 >> 5, n = gemv_nseg(B, pl_i(g.tiles) * B, t, grid), ms = pl_i(g.maxseg);
+  const float4* src = reinterpret_cast<const float4*>(pl_p(g.part) + (size_t(t) * ms) * 32 + (row0 & 31));
 #pragma unroll
   for (int i = 0; i < 8; ++i) out[i] = 0.0f;
   for (int k0 = 0; k0 < n; k0 += 4) {
     float4 v[4][2];
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-      if (k0 + k < n) {
-        v[k][0] = __ldcg(src + (k0 + k) * 8);
-        v[k][1] = __ldcg(src + (k0 + k) * 8 + 1);
-      }
+      const int kk = min(k0 + k, n - 1);
+      v[k][0] = __ldcg(src + kk * 8);
+      v[k][1] = __ldcg(src + kk * 8 + 1);
     }
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
+      const float z = k0 + k < n ? 1.0f : 0.0f;
       if (k0 + k < n) {
         out[0] += v[k][0].x; out[1] += v[k][0].y; out[2] += v[k][0].z; out[3] += v[k][0].w;
         out[4] += v[k][1].x; out[5] += v[k][1].y; out[6] += v[k][1].z; out[7] += v[k][1].w;
       }
+      (void)z;
     }
   }
 }
@@ -540,12 +543,11 @@ __device__ __forceinline__ bool gemv_stage(const StreamCtx& x, Ring& r, const PG
   bool ok = true;
   float acc[1] = {0.0f};
   int cur = wt0;
+  // Two units per iteration when they belong to the same tile: two
+  // independent dot chains in flight; the sums are added in unit order, as
+  // one at a time.
 #pragma unroll 1
-  for (int u = lo; u < hi; ++u) {
-    if (!ring_wait(*x.p, r)) {
-      ok = false;
-      break;
-    }
+  for (int u = lo; u < hi;) {
     const int tile = u / B, blk = u - tile * B;
     if (tile != cur) {
       red[(cur - wt0) * 32 + lane] = acc[0];
@@ -553,9 +555,36 @@ __device__ __forceinline__ bool gemv_stage(const StreamCtx& x, Ring& r, const PG
       cur = tile;
     }
     const int type = tile < te0 ? ty0 : (tile < te1 ? ty1 : ty2);
-    const uint8_t* unit = ring_slot(r, r.seq);
-    acc[0] += type == TYPE_Q4_K ? q4k_smem_dot(unit, blk, as, lane) : q6k_smem_dot(unit, blk, as, lane);
-    ring_release(x, r);
+    const bool pair = u + 1 < hi && blk + 1 < B;
+    if (!ring_wait(*x.p, r)) {
+      ok = false;
+      break;
+    }
+    const uint8_t* unit0 = ring_slot(r, r.seq);
+    if (pair) {
+      if (!mbar_wait_parity(r.bars + ((r.seq + 1) % P_SLOTS), ((r.seq + 1) / P_SLOTS) & 1u, x.p->err)) {
+        ok = false;
+        break;
+      }
+      const uint8_t* unit1 = ring_slot(r, r.seq + 1);
+      float d0, d1;
+      if (type == TYPE_Q4_K) {
+        d0 = q4k_smem_dot(unit0, blk, as, lane);
+        d1 = q4k_smem_dot(unit1, blk + 1, as, lane);
+      } else {
+        d0 = q6k_smem_dot(unit0, blk, as, lane);
+        d1 = q6k_smem_dot(unit1, blk + 1, as, lane);
+      }
+      acc[0] += d0;
+      acc[0] += d1;
+      ring_release(x, r);
+      ring_release(x, r);
+      u += 2;
+    } else {
+      acc[0] += type == TYPE_Q4_K ? q4k_smem_dot(unit0, blk, as, lane) : q6k_smem_dot(unit0, blk, as, lane);
+      ring_release(x, r);
+      u += 1;
+    }
   }
   if (hi > lo) red[(cur - wt0) * 32 + lane] = acc[0];
   if (__syncthreads_and(ok ? 1 : 0) == 0) return false;
@@ -599,6 +628,8 @@ __device__ __forceinline__ void block_sums(double (&v)[NV], double* scratch) {
   }
   __syncthreads();
 }
+
+__device__ __forceinline__ void combine_kvh(const StreamCtx& x, int kvh, uint8_t* smem);
 
 __device__ __forceinline__ bool attention_stage(const StreamCtx& x, Ring& r, int l, uint8_t* smem) {
   const PParams& p = *x.p;
@@ -818,64 +849,108 @@ __device__ __forceinline__ bool attention_stage(const StreamCtx& x, Ring& r, int
       out[2 * P_MAX_G + g * 256 + d] = osum;
     }
   }
+  // The last attention CTA of this KV head merges the head group.
+  int* flag = reinterpret_cast<int*>(smem + SM_MISC + 320);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int last = 0;
+    if (active) {
+      __threadfence();
+      const unsigned old = atomicAdd(p.kvh_counters + size_t(l) * KVH + kvh, 1u);
+      last = int(old) + 1 == x.att_cpk;
+      __threadfence();
+    }
+    *flag = last;
+  }
+  __syncthreads();
+  if (*flag) {
+    combine_kvh(x, kvh, smem);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __threadfence();
+      atomicAdd(counter(p, l, PS_COMB), 1u);
+    }
+  }
   return true;
 }
 
-// CTA h < H: merges head h's per-CTA partials (attn_combine_kernel arithmetic),
-// casts through the TS f16 codec and quantizes Q8_K block h.
-__device__ __forceinline__ void combine_head(const StreamCtx& x, int h, uint8_t* smem) {
+// Merges the per-CTA attention partials of the G query heads of KV head kvh
+// (attn_combine_kernel arithmetic: global max, f64-exp weights, f64
+// normalizer, weighted sum in CTA order), casts through the TS f16 codec and
+// quantizes Q8_K blocks kvh*G .. kvh*G+G-1 of the O projection's input.
+// Run by the last attention CTA of the KV head.
+__device__ __forceinline__ void combine_kvh(const StreamCtx& x, int kvh, uint8_t* smem) {
   const PParams& p = *x.p;
-  const int G = p.H / p.KVH, kvh = h / G, g = h % G, d = threadIdx.x, lane = d & 31, warp = d >> 5;
-  float* wch = reinterpret_cast<float*>(smem + SM_QS);  // <= 256 CTA weights
-  double* red = reinterpret_cast<double*>(smem + SM_MISC);
-  float* vec = reinterpret_cast<float*>(smem + SM_FRESH);
-  const int nc = x.att_cpk;
+  const int G = p.H / p.KVH, nc = x.att_cpk, d = threadIdx.x, lane = x.lane, warp = x.warp;
+  float* wch = reinterpret_cast<float*>(smem + SM_QS);  // [P_MAX_G][256] weights
+  double* lsum = reinterpret_cast<double*>(smem + SM_MISC);  // [P_MAX_G]
+  float* vec = reinterpret_cast<float*>(smem + SM_ACT);  // [P_MAX_G][256]
   const float* base = p.att_part + size_t(kvh * nc) * P_ATT_REC;
-  float mc = -INFINITY;
-  if (d < nc) mc = __ldcg(base + size_t(d) * P_ATT_REC + g);
-  float mx = mc;
+  if (warp < G) {
+    const int g = warp;
+    float mx = -INFINITY;
+    for (int j = lane; j < nc; j += 32) mx = fmaxf(mx, __ldcg(base + size_t(j) * P_ATT_REC + g));
 #pragma unroll
-  for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-  if (lane == 0) red[warp] = double(mx);
-  __syncthreads();
-  float gmax = -INFINITY;
-  for (int w = 0; w < P_WARPS; ++w) gmax = fmaxf(gmax, float(red[w]));
-  __syncthreads();
-  double lw = 0.0;
-  if (d < nc) {
-    const float w = mc == -INFINITY ? 0.0f : float(exp(double(mc - gmax)));
-    wch[d] = w;
-    lw = double(w) * double(__ldcg(base + size_t(d) * P_ATT_REC + P_MAX_G + g));
+    for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    double lw = 0.0;
+    for (int j = lane; j < nc; j += 32) {
+      const float mc = __ldcg(base + size_t(j) * P_ATT_REC + g);
+      const float w = mc == -INFINITY ? 0.0f : float(exp(double(mc - mx)));
+      wch[g * 256 + j] = w;
+      lw += double(w) * double(__ldcg(base + size_t(j) * P_ATT_REC + P_MAX_G + g));
+    }
+    lw = warp_sum_d(lw);
+    if (lane == 0) lsum[g] = lw;
   }
-  const double L = block_sum_d(lw, red, P_WARPS);
-  float o = 0.0f;
-  const float* po = base + 2 * P_MAX_G + g * 256 + d;
-  for (int c = 0; c < nc; c += 32) {
-    float v[32];
-#pragma unroll
-    for (int i = 0; i < 32; ++i) v[i] = c + i < nc ? __ldcg(po + size_t(c + i) * P_ATT_REC) : 0.0f;
-#pragma unroll
-    for (int i = 0; i < 32; ++i)
-      if (c + i < nc) o += wch[c + i] * v[i];
-  }
-  vec[d] = round_f16_ts(float(double(o) / L));
   __syncthreads();
-  if (warp == 0) {
+  // thread (g, q): dimensions 4q..4q+3 of head g; 16 float4 loads in flight,
+  // unconditional (record index clamped, its weight zero beyond nc)
+  {
+    const int g = threadIdx.x >> 6, q = threadIdx.x & 63;
+    if (g < G) {
+      const float4* po = reinterpret_cast<const float4*>(base + 2 * P_MAX_G + g * 256) + q;
+      constexpr int R4 = P_ATT_REC / 4;  // float4 per record
+      float4 o4 = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int c = 0; c < nc; c += 16) {
+        float4 v[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[i] = __ldcg(po + size_t(min(c + i, nc - 1)) * R4);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float w = c + i < nc ? wch[g * 256 + c + i] : 0.0f;
+          o4.x += w * v[i].x;
+          o4.y += w * v[i].y;
+          o4.z += w * v[i].z;
+          o4.w += w * v[i].w;
+        }
+      }
+      const double L = lsum[g];
+      vec[g * 256 + 4 * q + 0] = round_f16_ts(float(double(o4.x) / L));
+      vec[g * 256 + 4 * q + 1] = round_f16_ts(float(double(o4.y) / L));
+      vec[g * 256 + 4 * q + 2] = round_f16_ts(float(double(o4.z) / L));
+      vec[g * 256 + 4 * q + 3] = round_f16_ts(float(double(o4.w) / L));
+    }
+  }
+  __syncthreads();
+  if (warp < G) {
+    const int h = kvh * G + warp, nb = p.H;
     float v8[8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) v8[i] = vec[8 * lane + i];
-    const int nb = p.H;  // 256-blocks of the attention vector
-    q8k_block_warp(v8, lane, smem + SM_STAGE, p.q8_attn + size_t(h) * Q8A_REC,
+    for (int i = 0; i < 8; ++i) v8[i] = vec[warp * 256 + 8 * lane + i];
+    q8k_block_warp(v8, lane, smem + SM_STAGE + warp * 256, p.q8_attn + size_t(h) * Q8A_REC,
                    p.q8_attn + ((size_t(nb) * Q8A_REC + 255) & ~size_t(255)) + size_t(h) * Q8B_REC);
   }
 }
 
-// CTA c < F/2048, warp w: GEGLU of 256-block 8c + w and its Q8_K records
-// (geglu_quant_kernel arithmetic).
-__device__ __forceinline__ void geglu_block(const StreamCtx& x, const PLayer& L, uint8_t* smem) {
+// One warp: GEGLU of 256-block b of the FFN activation and its Q8_K records
+// (geglu_quant_kernel arithmetic).  `scratch` is 256 floats of this warp's
+// shared memory (the loop over the f64 tanh is not unrolled, to keep code
+// small).
+__device__ __forceinline__ void geglu_block(const StreamCtx& x, const PLayer& L, int b, float* scratch,
+                                            uint8_t* stage) {
   const PParams& p = *x.p;
-  const int lane = x.lane, b = x.cta * P_WARPS + x.warp, F = p.F;
-  float a[8], gu[16];
+  const int lane = x.lane, F = p.F;
+  float gu[16];
   const int e0 = b * 256 + 8 * lane;
   int rows[16];
 #pragma unroll
@@ -884,13 +959,72 @@ __device__ __forceinline__ void geglu_block(const StreamCtx& x, const PLayer& L,
     rows[8 + i] = F + e0 + i;
   }
   gemv_rows<16>(L.gu, rows, x.grid, gu);
-  const float* gv = gu;
-  const float* uv = gu + 8;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    scratch[8 * lane + i] = gu[i];
+    scratch[8 * lane + i + 256] = gu[8 + i];
+  }
+  __syncwarp();
 #pragma unroll 1
-  for (int i = 0; i < 8; ++i) a[i] = float(gelu_ts(gv[i]) * double(uv[i]));
+  for (int i = 0; i < 8; ++i) {
+    const float g = scratch[8 * lane + i], u = scratch[256 + 8 * lane + i];
+    scratch[8 * lane + i] = float(gelu_ts(g) * double(u));
+  }
+  __syncwarp();
+  float a[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) a[i] = scratch[8 * lane + i];
   const int nb = F / 256;
-  q8k_block_warp(a, lane, smem + SM_STAGE + x.warp * 256, p.q8_act + size_t(b) * Q8A_REC,
+  q8k_block_warp(a, lane, stage, p.q8_act + size_t(b) * Q8A_REC,
                  p.q8_act + ((size_t(nb) * Q8A_REC + 255) & ~size_t(255)) + size_t(b) * Q8B_REC);
+}
+
+// After this CTA's gate/up partials are stored: it counts itself in every
+// 256-block of the activation whose gate or up tiles it produced; the CTA
+// that completes a block (the last of its producers) computes that block's
+// GEGLU + Q8_K at once, and adds the blocks it finished to the ACT counter.
+// The activation is thus built by up to F/256 CTAs as soon as each block's
+// inputs exist, without a separate stage.
+__device__ __forceinline__ void gu_epilogue(const StreamCtx& x, const PLayer& L, int l, uint8_t* smem) {
+  const PParams& p = *x.p;
+  const PGemv& g = L.gu;
+  const int B = pl_i(g.B), U = pl_i(g.tiles) * B, half = p.F / 32;  // tiles of the gate part
+  int* mine = reinterpret_cast<int*>(smem + SM_MISC + 320);          // [0] = count, [1..16] = blocks
+  unsigned* bc = p.blk_counters + size_t(l) * (p.F / 256);
+  __syncthreads();  // the CTA's partials are stored
+  if (threadIdx.x == 0) {
+    __threadfence();
+    int n = 0;
+    const int c0 = p_range_lo(U, x.cta, x.grid), c1 = p_range_lo(U, x.cta + 1, x.grid);
+    if (c1 > c0) {
+      const int t0 = c0 / B, t1 = (c1 - 1) / B;
+      for (int part = 0; part < 2; ++part) {
+        const int lo = max(t0, part * half), hi = min(t1, part * half + half - 1);
+        for (int blk = (lo - part * half) / 8; lo <= hi && blk <= (hi - part * half) / 8; ++blk) {
+          int target = 0;
+          for (int q = 0; q < 2; ++q) {
+            const int ta = q * half + 8 * blk, tb = ta + 7;
+            target += p_cta_of(tb * B + B - 1, U, x.grid) - p_cta_of(ta * B, U, x.grid) + 1;
+          }
+          const unsigned old = atomicAdd(bc + blk, 1u);
+          if (int(old) + 1 == target && n < 16) mine[1 + n++] = blk;
+        }
+      }
+    }
+    mine[0] = n;
+    __threadfence();
+  }
+  __syncthreads();
+  const int n = mine[0];
+  float* scratch = reinterpret_cast<float*>(smem + SM_ACT) + x.warp * 512;
+  for (int i = x.warp; i < n; i += P_WARPS)
+    geglu_block(x, L, mine[1 + i], scratch, smem + SM_STAGE + x.warp * 256);
+  __syncthreads();
+  if (threadIdx.x == 0 && n > 0) {
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+    __threadfence();
+    atomicAdd(counter(p, l, PS_ACT), unsigned(n));
+  }
 }
 
 // The hidden size is 2048 (one 256-block per warp); checked on the host.
@@ -948,7 +1082,7 @@ __global__ void __launch_bounds__(P_THREADS, 1) persistent_step_kernel(const PPa
   __syncthreads();
 
   const unsigned grid = gridDim.x;
-  const int act_ctas = p.F / (256 * P_WARPS);
+  const int act_blocks = p.F / 256;
   bool ok = true;
   // One pass of the stage driver per (layer, stage): every stage body has a
   // single call site, so the kernel's code stays small enough for the
@@ -965,11 +1099,11 @@ __global__ void __launch_bounds__(P_THREADS, 1) persistent_step_kernel(const PPa
       switch (st) {
         case PS_QKV: dep = l > 0 ? counter(p, l - 1, PS_DOWN) : nullptr; break;
         case PS_ATT: dep = counter(p, l, PS_QKV); break;
-        case PS_COMB: dep = counter(p, l, PS_ATT); runs = x.cta < p.H; break;
-        case PS_O: dep = counter(p, l, PS_COMB); need = unsigned(p.H); break;
+        case PS_COMB: runs = false; break;  // done by the last attention CTA of each KV head
+        case PS_O: dep = counter(p, l, PS_COMB); need = unsigned(p.KVH); break;
         case PS_GU: dep = counter(p, l, PS_O); break;
-        case PS_ACT: dep = counter(p, l, PS_GU); runs = x.cta < act_ctas; break;
-        default: dep = counter(p, l, PS_ACT); need = unsigned(act_ctas); break;
+        case PS_ACT: runs = false; break;  // done by the last producer of each activation block
+        default: dep = counter(p, l, PS_ACT); need = unsigned(act_blocks); break;
       }
       if (!runs) continue;
       if (dep && !(ok = cta_wait(p, dep, need))) break;
@@ -993,17 +1127,14 @@ __global__ void __launch_bounds__(P_THREADS, 1) persistent_step_kernel(const PPa
       // 3. the stage's work
       if (st == PS_ATT) {
         ok = attention_stage(x, r, l, smem);
-      } else if (st == PS_COMB) {
-        combine_head(x, x.cta, smem);
-      } else if (st == PS_ACT) {
-        geglu_block(x, L, smem);
       } else {
         const PGemv& g = st == PS_QKV ? L.qkv : (st == PS_O ? L.o : (st == PS_GU ? L.gu : L.down));
         ok = gemv_stage(x, r, g, smem, st == PS_DOWN);
       }
       if (!ok) break;
       // 4. publish
-      cta_signal(counter(p, l, st));
+      if (st == PS_GU) gu_epilogue(x, L, l, smem);
+      else cta_signal(counter(p, l, st));
     }
   }
   if (!ok) {

@@ -64,6 +64,8 @@ struct PParams {
   uint8_t* q8_act;    // Q8_K records of the FFN activation (q8buf_carve(base, F, 1))
   float* att_part;    // [grid][P_ATT_REC]
   unsigned* counters; // [nlayers][PS_COUNT] x P_CTR_STRIDE, zero at launch
+  unsigned* kvh_counters;  // [nlayers][KVH] attention CTAs done per KV head, zero at launch
+  unsigned* blk_counters;  // [nlayers][F/256] gate/up producers done per activation block, zero at launch
   int* abort_word;    // zero at launch; set when any wait gives up
   int* err;           // device status word (HPC_ERR_TIMEOUT on a timeout)
 };
