@@ -228,11 +228,11 @@ static int launch_gemv_ws(const hc::Q8Buf& q, int K, int cols, const hc::GemvSeg
   p.K = K;
   p.nb = K / 256;
   p.total_tiles = total_tiles;
-  hc::gemv_plan(p);
   p.q = q;
   for (int c0 = 0; c0 < cols; c0 += 8) {
     p.col0 = c0;
     p.ncols = cols - c0 < 8 ? cols - c0 : 8;
+    hc::gemv_plan(p);  // the plan depends on the column count of the launch
     HPC_CK(hc::launch_gemv(p, st), "gemv launch");
   }
   return HPC_OK;

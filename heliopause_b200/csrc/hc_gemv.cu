@@ -70,8 +70,11 @@ __device__ __forceinline__ void store_tile(const GemvParams& p, int tile, const 
   }
 }
 
-template <int NC>
-__global__ void __launch_bounds__(GEMV_THREADS, GEMV_CTAS_PER_SM) gemv_kernel(const __grid_constant__ GemvParams p) {
+// UC: register-buffer chunks per unit (Q6K_CHUNKS, or Q4K_CHUNKS for Q4_K-only
+// launches, which then fit GEMV_CTAS_PER_SM_Q4 CTAs per SM).
+template <int NC, int UC>
+__global__ void __launch_bounds__(GEMV_THREADS, UC == Q4K_CHUNKS ? GEMV_CTAS_PER_SM_Q4 : GEMV_CTAS_PER_SM)
+    gemv_kernel(const __grid_constant__ GemvParams p) {
   extern __shared__ __align__(16) uint8_t smem[];
   __shared__ float red[GEMV_WARPS_PER_CTA][NC][32];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -107,7 +110,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, GEMV_CTAS_PER_SM) gemv_kernel(co
     // memory before waiting for the previous kernel, then compute from there.
     __shared__ __align__(8) uint64_t bar;
     uint8_t* units = smem + (gemv_smem_bytes(p, nblk) + 15) / 16 * 16;  // after the activation slice
-    const int ub_max = unit_bytes(TYPE_Q6_K);
+    const int ub_max = unit_bytes(UC == Q4K_CHUNKS ? TYPE_Q4_K : TYPE_Q6_K);
     if (threadIdx.x == 0) {
       mbar_init(&bar, 1);
       uint32_t total = 0;
@@ -145,23 +148,23 @@ __global__ void __launch_bounds__(GEMV_THREADS, GEMV_CTAS_PER_SM) gemv_kernel(co
         int t;
         unit_addr(p, item0, 0, &t);
         for (int jj = 0; jj < p.bps; ++jj) {
-          UnitRegs r;
-          load_unit_smem(r, units + size_t(warp * p.bps + jj) * ub_max, t, lane);
-          unit_compute<NC>(r, t, (item0 & (p.split - 1)) * p.bps + jj - kb0, p.ncols, act, acc);
+          UnitRegsN<UC> r;
+          load_unit_smem<UC>(r, units + size_t(warp * p.bps + jj) * ub_max, t, lane);
+          unit_compute<NC, UC>(r, t, (item0 & (p.split - 1)) * p.bps + jj - kb0, p.ncols, act, acc);
         }
       }
       flush(item0, acc);
     }
   } else {
-    UnitRegs buf[2];
+    UnitRegsN<UC> buf[2];
     int first_type = TYPE_Q4_K;
-    if (item0 < nitems) load_unit(buf[0], unit_addr(p, item0, 0, &first_type), first_type, lane);
+    if (item0 < nitems) load_unit<UC>(buf[0], unit_addr(p, item0, 0, &first_type), first_type, lane);
 #if __CUDA_ARCH__ >= 900
     asm volatile("griddepcontrol.wait;" ::: "memory");
 #endif
     stage_activations(p, act_a, act_b, kb0, nblk);
     __syncthreads();
-    stream_items<NC>(p, act, item0, istride, nitems, lane, buf[0], first_type, flush);
+    stream_items<NC, UC>(p, act, item0, istride, nitems, lane, buf[0], first_type, flush);
   }
   if (p.split == 1) return;
 
@@ -224,11 +227,16 @@ int persistent_grid(int items, int cap) {
   return (warps + GEMV_WARPS_PER_CTA - 1) / GEMV_WARPS_PER_CTA;
 }
 
+static int ctas_per_sm(const GemvParams& p) { return p.q4small ? GEMV_CTAS_PER_SM_Q4 : GEMV_CTAS_PER_SM; }
+
 void gemv_plan(GemvParams& p) {
   // Split K as far as the launch still fits in one wave of resident CTAs
-  // (GEMV_CTAS_PER_SM per SM, one item per warp); parts stay >= 1 block and
-  // the cluster form is used up to 8 CTAs (split 32).
-  const int cap_warps = sm_count() * GEMV_CTAS_PER_SM * GEMV_WARPS_PER_CTA;
+  // (ctas_per_sm per SM, one item per warp); parts stay >= 1 block and the
+  // cluster form is used up to 8 CTAs (split 32).
+  p.q4small = p.ncols <= 2;
+  for (int i = 0; i < p.nseg; ++i)
+    if (p.seg[i].type != TYPE_Q4_K) p.q4small = 0;
+  const int cap_warps = sm_count() * ctas_per_sm(p) * GEMV_WARPS_PER_CTA;
   int s = 1, lg = 0;
   while (s < 32 && p.nb % (s * 2) == 0 && p.total_tiles * s * 2 <= cap_warps) {
     s *= 2;
@@ -237,9 +245,16 @@ void gemv_plan(GemvParams& p) {
   p.split = s;
   p.split_log2 = lg;
   p.bps = p.nb / s;
-  // Launches that fit in one wave stage all their units in shared memory.
-  const size_t unit_smem = size_t(GEMV_WARPS_PER_CTA) * p.bps * unit_bytes(TYPE_Q6_K);
-  p.bulk = (p.split > 1 || p.total_tiles <= cap_warps) && unit_smem <= size_t(GEMV_BULK_MAX_UNITS_SMEM);
+  // Launches that fit in one wave stage all their units in shared memory --
+  // one wave counting the CTAs that the staged units leave room for.
+  const size_t unit_smem = size_t(GEMV_WARPS_PER_CTA) * p.bps * unit_bytes(p.q4small ? TYPE_Q4_K : TYPE_Q6_K);
+  const int nblk = p.split > GEMV_WARPS_PER_CTA ? GEMV_WARPS_PER_CTA * p.bps : p.nb;
+  const size_t cta_smem = unit_smem + gemv_smem_bytes(p, nblk) + 2048;  // + static shared memory
+  const int by_smem = int(size_t(GEMV_SM_SMEM) / cta_smem);
+  const int bulk_ctas = sm_count() * (by_smem < ctas_per_sm(p) ? by_smem : ctas_per_sm(p));
+  const int grid_items = (p.total_tiles * p.split + GEMV_WARPS_PER_CTA - 1) / GEMV_WARPS_PER_CTA;
+  p.bulk = (p.split > 1 || p.total_tiles <= cap_warps) && unit_smem <= size_t(GEMV_BULK_MAX_UNITS_SMEM) &&
+           grid_items <= bulk_ctas;
   if (p.split == 1 && p.bulk) {
     // one item per warp in bulk mode: make the grid non-persistent
     p.bulk = p.total_tiles <= cap_warps;
@@ -249,19 +264,20 @@ void gemv_plan(GemvParams& p) {
 
 int gemv_grid(const GemvParams& p) {
   const int items = p.total_tiles * p.split;
-  if (p.split == 1 && !p.bulk) return persistent_grid(items, sm_count() * GEMV_CTAS_PER_SM);
+  if (p.split == 1 && !p.bulk) return persistent_grid(items, sm_count() * ctas_per_sm(p));
   return (items + GEMV_WARPS_PER_CTA - 1) / GEMV_WARPS_PER_CTA;
 }
 
-template <int NC>
+template <int NC, int UC>
 static cudaError_t launch_nc(const GemvParams& p, cudaStream_t stream) {
   const int nblk = p.split > GEMV_WARPS_PER_CTA ? GEMV_WARPS_PER_CTA * p.bps : p.nb;
   size_t smem = (gemv_smem_bytes(p, nblk) + 15) / 16 * 16;
-  if (p.bulk) smem += size_t(GEMV_WARPS_PER_CTA) * p.bps * unit_bytes(TYPE_Q6_K);
+  if (p.bulk) smem += size_t(GEMV_WARPS_PER_CTA) * p.bps * unit_bytes(UC == Q4K_CHUNKS ? TYPE_Q4_K : TYPE_Q6_K);
   if (smem > size_t(GEMV_MAX_SMEM)) return cudaErrorInvalidValue;
   static bool attr_set = false;
   if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(gemv_kernel<NC>, cudaFuncAttributeMaxDynamicSharedMemorySize, GEMV_MAX_SMEM);
+    cudaError_t e =
+        cudaFuncSetAttribute(gemv_kernel<NC, UC>, cudaFuncAttributeMaxDynamicSharedMemorySize, GEMV_MAX_SMEM);
     if (e != cudaSuccess) return e;
     attr_set = true;
   }
@@ -284,14 +300,18 @@ static cudaError_t launch_nc(const GemvParams& p, cudaStream_t stream) {
   }
   cfg.attrs = attr;
   cfg.numAttrs = na;
-  return cudaLaunchKernelEx(&cfg, gemv_kernel<NC>, p);
+  return cudaLaunchKernelEx(&cfg, gemv_kernel<NC, UC>, p);
 }
 
 cudaError_t launch_gemv(const GemvParams& p, cudaStream_t stream) {
-  if (p.ncols <= 1) return launch_nc<1>(p, stream);
-  if (p.ncols <= 2) return launch_nc<2>(p, stream);
-  if (p.ncols <= 4) return launch_nc<4>(p, stream);
-  return launch_nc<8>(p, stream);
+  if (p.q4small) {
+    if (p.ncols <= 1) return launch_nc<1, Q4K_CHUNKS>(p, stream);
+    return launch_nc<2, Q4K_CHUNKS>(p, stream);
+  }
+  if (p.ncols <= 1) return launch_nc<1, Q6K_CHUNKS>(p, stream);
+  if (p.ncols <= 2) return launch_nc<2, Q6K_CHUNKS>(p, stream);
+  if (p.ncols <= 4) return launch_nc<4, Q6K_CHUNKS>(p, stream);
+  return launch_nc<8, Q6K_CHUNKS>(p, stream);
 }
 
 }  // namespace hc

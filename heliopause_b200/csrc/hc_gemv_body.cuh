@@ -32,26 +32,33 @@ struct ActSlice {
   int kb0;           // first block of the slice
 };
 
-struct UnitRegs {
-  uint4 c[UNIT_CHUNKS];
+// One unit in registers: UC = Q6K_CHUNKS holds either type; UC = Q4K_CHUNKS
+// (launches whose weights are all Q4_K) holds Q4_K only and needs ~40 fewer
+// registers per buffer.
+template <int UC>
+struct UnitRegsN {
+  uint4 c[UC];
   uint32_t d;  // Q6_K d bits
 };
+using UnitRegs = UnitRegsN<UNIT_CHUNKS>;
 
 // Streaming loads: evict-first, no L1 allocation (weights are read once).
-__device__ __forceinline__ void load_unit(UnitRegs& r, const uint8_t* unit, int type, int lane) {
+template <int UC>
+__device__ __forceinline__ void load_unit(UnitRegsN<UC>& r, const uint8_t* unit, int type, int lane) {
   const uint4* p = reinterpret_cast<const uint4*>(unit) + lane;
-  if (type == TYPE_Q4_K) {
+  if (UC == Q4K_CHUNKS || type == TYPE_Q4_K) {
 #pragma unroll
     for (int k = 0; k < Q4K_CHUNKS; ++k) r.c[k] = __ldcs(p + k * TILE);
   } else {
 #pragma unroll
-    for (int k = 0; k < Q6K_CHUNKS; ++k) r.c[k] = __ldcs(p + k * TILE);
+    for (int k = 0; k < (UC > Q4K_CHUNKS ? Q6K_CHUNKS : 0); ++k) r.c[k] = __ldcs(p + k * TILE);
     r.d = __ldcs(reinterpret_cast<const unsigned short*>(unit + Q6K_DPLANE_OFFSET) + lane);
   }
 }
 
-template <int NC>
-__device__ __forceinline__ void q4k_regs(const UnitRegs& r, int j, int ncols, const ActSlice& act, float (&acc)[NC]) {
+template <int NC, int UC>
+__device__ __forceinline__ void q4k_regs(const UnitRegsN<UC>& r, int j, int ncols, const ActSlice& act,
+                                         float (&acc)[NC]) {
   const Q4KHeader hd = q4k_header(r.c[0]);
   int isum[NC];
 #pragma unroll
@@ -151,23 +158,28 @@ __device__ __forceinline__ void q6k_regs(const UnitRegs& r, int j, int ncols, co
 }
 
 // Loads one unit that was staged in shared memory into registers.
-__device__ __forceinline__ void load_unit_smem(UnitRegs& r, const uint8_t* unit, int type, int lane) {
+template <int UC>
+__device__ __forceinline__ void load_unit_smem(UnitRegsN<UC>& r, const uint8_t* unit, int type, int lane) {
   const uint4* p = reinterpret_cast<const uint4*>(unit) + lane;
-  if (type == TYPE_Q4_K) {
+  if (UC == Q4K_CHUNKS || type == TYPE_Q4_K) {
 #pragma unroll
     for (int k = 0; k < Q4K_CHUNKS; ++k) r.c[k] = p[k * TILE];
   } else {
 #pragma unroll
-    for (int k = 0; k < Q6K_CHUNKS; ++k) r.c[k] = p[k * TILE];
+    for (int k = 0; k < (UC > Q4K_CHUNKS ? Q6K_CHUNKS : 0); ++k) r.c[k] = p[k * TILE];
     r.d = reinterpret_cast<const uint16_t*>(unit + Q6K_DPLANE_OFFSET)[lane];
   }
 }
 
-template <int NC>
-__device__ __forceinline__ void unit_compute(const UnitRegs& r, int type, int j, int ncols, const ActSlice& act,
+template <int NC, int UC>
+__device__ __forceinline__ void unit_compute(const UnitRegsN<UC>& r, int type, int j, int ncols, const ActSlice& act,
                                              float (&acc)[NC]) {
-  if (type == TYPE_Q4_K) q4k_regs<NC>(r, j, ncols, act, acc);
-  else q6k_regs<NC>(r, j, ncols, act, acc);
+  if constexpr (UC == Q4K_CHUNKS) {
+    q4k_regs<NC, UC>(r, j, ncols, act, acc);
+  } else {
+    if (type == TYPE_Q4_K) q4k_regs<NC, UC>(r, j, ncols, act, acc);
+    else q6k_regs<NC>(r, j, ncols, act, acc);
+  }
 }
 
 // Single-column block dots reading the unit from shared memory chunk by
@@ -278,11 +290,12 @@ __device__ __forceinline__ const uint8_t* unit_addr(const GemvParams& p, int ite
 // unit is loaded one step ahead (double buffer), `flush(item, acc)` receives
 // each finished item's row sums.  buf[0] must already hold the first unit
 // (loaded by the caller before it waited for the previous kernel: PDL).
-template <int NC, class Flush>
+template <int NC, int UC = UNIT_CHUNKS, class Flush>
 __device__ __forceinline__ void stream_items(const GemvParams& p, const ActSlice& act, int item0, int istride,
-                                             int nitems, int lane, UnitRegs& buf0, int first_type, Flush& flush) {
+                                             int nitems, int lane, UnitRegsN<UC>& buf0, int first_type,
+                                             Flush& flush) {
   if (item0 >= nitems) return;
-  UnitRegs buf1;
+  UnitRegsN<UC> buf1;
   int t0 = first_type, t1 = first_type;
   int item = item0, j = 0;
   float acc[NC];
@@ -291,7 +304,7 @@ __device__ __forceinline__ void stream_items(const GemvParams& p, const ActSlice
   // One step: prefetch the unit after (item, j) into `nxt`, compute `cur`.
   // The two buffers alternate by name (no dynamic indexing, so they stay in
   // registers).
-  auto step = [&](UnitRegs& cur, int tcur, UnitRegs& nxt, int& tnxt) -> bool {
+  auto step = [&](UnitRegsN<UC>& cur, int tcur, UnitRegsN<UC>& nxt, int& tnxt) -> bool {
     int nitem = item, nj = j + 1;
     if (nj == p.bps) {
       nitem = item + istride;
@@ -299,7 +312,7 @@ __device__ __forceinline__ void stream_items(const GemvParams& p, const ActSlice
     }
     const bool has_next = nitem < nitems;
     if (has_next) load_unit(nxt, unit_addr(p, nitem, nj, &tnxt), tnxt, lane);
-    unit_compute<NC>(cur, tcur, (item & (p.split - 1)) * p.bps + j - act.kb0, p.ncols, act, acc);
+    unit_compute<NC, UC>(cur, tcur, (item & (p.split - 1)) * p.bps + j - act.kb0, p.ncols, act, acc);
     if (nj == 0) {
       flush(item, acc);
 #pragma unroll

@@ -27,6 +27,7 @@ struct GemvParams {
   int col0, ncols;  // this launch covers columns [col0, col0 + ncols), ncols <= 8
   int total_tiles;  // over all segments
   int bulk;         // 1: each CTA copies all of its units into shared memory up front
+  int q4small;      // 1: every weight is Q4_K and ncols <= 2 (Q4_K-sized register buffers, 4 CTAs per SM)
   int* err;         // device status word (bounded-wait timeouts)
   Q8Buf q;
 };
@@ -37,8 +38,10 @@ int* device_status_word();
 constexpr int GEMV_WARPS_PER_CTA = 4;
 constexpr int GEMV_THREADS = GEMV_WARPS_PER_CTA * 32;
 constexpr int GEMV_CTAS_PER_SM = 3;
+constexpr int GEMV_CTAS_PER_SM_Q4 = 4;  // Q4_K-only launches of <= 2 columns (smaller register buffers)
 constexpr int GEMV_MAX_SMEM = 200 * 1024;
 constexpr int GEMV_BULK_MAX_UNITS_SMEM = 112 * 1024;  // unit bytes a bulk-mode CTA may stage
+constexpr int GEMV_SM_SMEM = 228 * 1024;              // shared memory per SM
 
 __host__ __device__ inline int unit_bytes(int type) { return int(tile_block_bytes(type)); }
 
