@@ -161,85 +161,12 @@ __global__ void norm_quant_kernel(float* __restrict__ x, const float* __restrict
   q8k_block_warp(n, lane, stage[warp], q8_rec_a(q, m, warp), q8_rec_b(q, m, warp));
 }
 
-// ---- QK norm + RoPE + KV write ----------------------------------------------------
-
-// One CTA per token, one warp per head vector (HD = 256 values, 8 per lane):
-// warps [0, H) are query heads, [H, H + KVH) key heads, [H + KVH, H + 2 KVH)
-// value heads.  Query: normHeads + ropeNeox (layers.ts:201-224); key: same
-// with the key norm, then written to K[slot][kvh][:] (layers.ts:241-268);
-// value: rmsNormRowsNoWeight (layers.ts:248-253) written to V[slot][kvh][:]
-// (updateFullAttentionCache, layers.ts:887-911, stores V dimension-major as
-// [dim][kvh][slot]; here V is token-major like K so one token's values are
-// one contiguous 1 KB row for the bulk-copy staging).
-__global__ void qkv_post_kernel(const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v,
-                                const float* __restrict__ qnw, const float* __restrict__ knw,
-                                const int32_t* __restrict__ pos, const double* __restrict__ cos_t,
-                                const double* __restrict__ sin_t, int H, int KVH, int cap, double eps, int has_kv,
-                                float* __restrict__ q_out, float* __restrict__ kc, float* __restrict__ vc) {
-  constexpr int HD = 256, HALF = 128;
-  pdl_trigger();
-  pdl_wait();
-  const int m = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int kind = warp < H ? 0 : (warp < H + KVH ? 1 : 2);
-  if (kind > 0 && !has_kv) return;
-  const int head = kind == 0 ? warp : (kind == 1 ? warp - H : warp - H - KVH);
-  const float* src = kind == 0 ? q + (size_t(m) * H + head) * HD : (kind == 1 ? k : v) + (size_t(m) * KVH + head) * HD;
-  float x[8];
-  {
-    const float4 a = reinterpret_cast<const float4*>(src + 8 * lane)[0];
-    const float4 b = reinterpret_cast<const float4*>(src + 8 * lane)[1];
-    x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w; x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
-  }
-  double ss = 0.0;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) ss += double(x[i]) * double(x[i]);
-  ss = warp_sum_d(ss);
-  const double sc = 1.0 / sqrt(ss / double(HD) + eps);
-  float n[8];
-  if (kind == 2) {
-#pragma unroll
-    for (int i = 0; i < 8; ++i) n[i] = float(double(x[i]) * sc);
-  } else {
-    const float* w = kind == 0 ? qnw : knw;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) n[i] = float((double(x[i]) * sc) * double(w[8 * lane + i]));
-    // RoPE NeoX: pair (i, i + 128) sits in lanes L and L + 16.
-    float partner[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) partner[i] = __shfl_xor_sync(0xffffffffu, n[i], 16);
-    const bool first = lane < 16;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int idx = (lane & 15) * 8 + i;  // pair index 0..127
-      const double c = cos_t[size_t(m) * HALF + idx], s = sin_t[size_t(m) * HALF + idx];
-      const double x0 = first ? n[i] : partner[i];
-      const double x1 = first ? partner[i] : n[i];
-      if (first) n[i] = float(x0 * c) - float(x1 * s);
-      else n[i] = float(x0 * s) + float(x1 * c);
-    }
-  }
-  if (kind == 0) {
-    float4* o = reinterpret_cast<float4*>(q_out + (size_t(m) * H + head) * HD + 8 * lane);
-    o[0] = make_float4(n[0], n[1], n[2], n[3]);
-    o[1] = make_float4(n[4], n[5], n[6], n[7]);
-  } else {
-    const int slot = pos[m] % cap;
-    if (kind == 1) {
-      float4* o = reinterpret_cast<float4*>(kc + (size_t(slot) * KVH + head) * HD + 8 * lane);
-      o[0] = make_float4(n[0], n[1], n[2], n[3]);
-      o[1] = make_float4(n[4], n[5], n[6], n[7]);
-    } else {
-      float4* o = reinterpret_cast<float4*>(vc + (size_t(slot) * KVH + head) * HD + 8 * lane);
-      o[0] = make_float4(n[0], n[1], n[2], n[3]);
-      o[1] = make_float4(n[4], n[5], n[6], n[7]);
-    }
-  }
-}
-
 // ---- attention ------------------------------------------------------------------------
 
 // Split-KV decode attention (flash-decoding form of hp_gqa_attention_f32,
-// lib.rs:539-654, on the compacted full-attention range [0, pos+1)).  Grid
+// lib.rs:539-654, on the compacted full-attention range [0, pos+1)), with the
+// QK-norm / RoPE of the queries and the write of this step's K/V rows
+// (forwardAttentionLayer, layers.ts:201-268, 887-911) folded in.  Grid
 // (chunks, KVH); a CTA serves all M tokens x (H/KVH) query heads of one KV
 // head over one ATT_CHUNK-token slice of the cache.  Warp 0 issues bulk
 // copies of the slice (ATT_CHUNK K rows and ATT_CHUNK V rows of 1 KB each)
@@ -247,14 +174,51 @@ __global__ void qkv_post_kernel(const float* __restrict__ q, const float* __rest
 // completing on an mbarrier.  A slice that holds none of this step's new
 // rows (every chunk but the one or two around pos) was written by earlier
 // steps, so its copies are issued before griddepcontrol.wait and overlap the
-// kernels ahead of attention.  Then the queries are staged (rounded to f16
-// with the Rust codec, lib.rs:590-597), scores (scale 1, causal), a local
+// kernels ahead of attention.  Then the queries are normed, rotated and
+// rounded to f16 with the Rust codec (lib.rs:590-597) -- one warp per query
+// vector -- the CTA holding a new row of an own-KV layer computes it (cache
+// and staged copy), and scores (scale 1, causal), a local
 // softmax (max, sum of f64 exp) and the partial output p*v are written for
 // the combine kernel.
 constexpr int ATT_KSTRIDE = 256 + 4;        // floats per staged K row
 
+// One warp: QK-norm (f64 sum of squares, layers.ts:871-885 normHeads) of a
+// 256-vector held 8 values per lane (lane L: dimensions 8L..8L+7), optional
+// weight, optional NeoX RoPE (layers.ts:990-1033; pair (i, i+128) sits in
+// lanes L and L+16); products rounded to f32 as in the reference.
+__device__ __forceinline__ void head_norm_rope(float (&x)[8], const float* w, bool rope, const double* cos_t,
+                                               const double* sin_t, double eps, int lane) {
+  double ss = 0.0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) ss += double(x[i]) * double(x[i]);
+  ss = warp_sum_d(ss);
+  const double sc = 1.0 / sqrt(ss / 256.0 + eps);
+  if (!w) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) x[i] = float(double(x[i]) * sc);
+    return;
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) x[i] = float((double(x[i]) * sc) * double(w[8 * lane + i]));
+  if (!rope) return;
+  float partner[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) partner[i] = __shfl_xor_sync(0xffffffffu, x[i], 16);
+  const bool first = lane < 16;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int idx = (lane & 15) * 8 + i;  // pair index 0..127
+    const double c = cos_t[idx], s = sin_t[idx];
+    const double x0 = first ? x[i] : partner[i];
+    const double x1 = first ? partner[i] : x[i];
+    x[i] = first ? float(x0 * c) - float(x1 * s) : float(x0 * s) + float(x1 * c);
+  }
+}
+
 __global__ void __launch_bounds__(ATT_THREADS) attn_partial_kernel(
-    const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
+    const float* __restrict__ q, const float* __restrict__ kraw, const float* __restrict__ vraw,
+    const float* __restrict__ qnw, const float* __restrict__ knw, const double* __restrict__ cos_t,
+    const double* __restrict__ sin_t, double eps, int own_kv, float* __restrict__ kc, float* __restrict__ vc,
     const int32_t* __restrict__ pos, int M, int H, int KVH, int cap, float scale, float* __restrict__ part_m,
     float* __restrict__ part_l, float* __restrict__ part_o, int* __restrict__ err) {
   constexpr int HD = 256, CH = ATT_CHUNK;
@@ -298,15 +262,47 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_partial_kernel(
   };
   if (threadIdx.x < 32 && !fresh) issue();
   pdl_wait();
+  // a slice with new rows is copied after the wait: in a shared-KV layer the
+  // rows come from the source layer's attention launch earlier in the step
   if (threadIdx.x < 32 && fresh) issue();
-  for (int i = threadIdx.x; i < NQ * HD; i += blockDim.x) {
-    const int qi = i / HD, d = i % HD;
+  __syncthreads();  // the slice's mbarrier (initialized by thread 0) is visible before anyone waits on it
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, warps = blockDim.x >> 5;
+  // queries of this KV head's G heads for every token: QK-norm + RoPE (the
+  // token's row of the cos/sin tables), rounded with the Rust f16 codec
+  // (lib.rs:590-597); one warp per vector
+  for (int qi = warp; qi < NQ; qi += warps) {
     const int m = qi / G, h = kvh * G + qi % G;
-    qs[i] = round_f16_rust(q[(size_t(m) * H + h) * HD + d]);
+    const float* src = q + (size_t(m) * H + h) * HD + 8 * lane;
+    float x[8];
+    const float4 a = reinterpret_cast<const float4*>(src)[0], b = reinterpret_cast<const float4*>(src)[1];
+    x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w; x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+    head_norm_rope(x, qnw, true, cos_t + size_t(m) * (HD / 2), sin_t + size_t(m) * (HD / 2), eps, lane);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) qs[qi * HD + 8 * lane + i] = round_f16_rust(x[i]);
+  }
+  if (!mbar_wait_parity(&bar, 0, err)) return;
+  // own-KV layer: this step's K/V rows that fall in the slice are computed
+  // here (key: K-norm + RoPE; value: unweighted norm; layers.ts:241-268),
+  // written to the cache (layers.ts:887-911) and over the staged copies
+  if (own_kv && fresh) {
+    for (int job = warp; job < 2 * M; job += warps) {
+      const int m = job >> 1, isv = job & 1, p = pos[m];
+      if (p < t0 || p >= t0 + CH) continue;
+      const float* src = (isv ? vraw : kraw) + (size_t(m) * KVH + kvh) * HD + 8 * lane;
+      float x[8];
+      const float4 a = reinterpret_cast<const float4*>(src)[0], b = reinterpret_cast<const float4*>(src)[1];
+      x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w; x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+      head_norm_rope(x, isv ? nullptr : knw, !isv, cos_t + size_t(m) * (HD / 2), sin_t + size_t(m) * (HD / 2),
+                     eps, lane);
+      float* cache = (isv ? vc : kc) + (size_t(p % cap) * KVH + kvh) * HD + 8 * lane;
+      float* staged = (isv ? vs : ks) + (p - t0) * ATT_KSTRIDE + 8 * lane;
+      reinterpret_cast<float4*>(cache)[0] = make_float4(x[0], x[1], x[2], x[3]);
+      reinterpret_cast<float4*>(cache)[1] = make_float4(x[4], x[5], x[6], x[7]);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) staged[i] = x[i];
+    }
   }
   __syncthreads();
-  if (!mbar_wait_parity(&bar, 0, err)) return;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, warps = blockDim.x >> 5;
   // scores: thread per (query, token); a warp shares the query (broadcast
   // reads) and walks 32 padded K rows
   for (int pr = threadIdx.x; pr < NQ * CH; pr += blockDim.x) {
@@ -512,21 +508,15 @@ cudaError_t launch_norm_quant(bool resid, float* x, const float* y, const float*
   return pdl_launch(norm_quant_kernel<false>, grid, block, 0, st, x, y, w_post, w_pre, eps, D, q, n_out);
 }
 
-cudaError_t launch_qkv_post(const float* q, const float* k, const float* v, const float* qnw, const float* knw,
-                            const int32_t* pos, const double* cos_t, const double* sin_t, int M, int H, int KVH,
-                            int cap, double eps, bool has_kv, float* q_out, float* kc, float* vc, cudaStream_t st) {
-  return pdl_launch(qkv_post_kernel, dim3(M), dim3(32 * (H + 2 * KVH)), 0, st, q, k, v, qnw, knw, pos, cos_t, sin_t, H,
-                    KVH, cap, eps, int(has_kv), q_out, kc, vc);
-}
-
 size_t attn_smem_bytes(int M, int H, int KVH) {
   const int NQ = M * (H / KVH);
   return sizeof(float) * (size_t(ATT_CHUNK) * ATT_KSTRIDE * 2 + size_t(NQ) * 256 + size_t(NQ) * ATT_CHUNK);
 }
 
-cudaError_t launch_attention(const float* q, const float* kc, const float* vc, const int32_t* pos, int M, int H,
-                             int KVH, int cap, float scale, float* part_m, float* part_l, float* part_o, int* err,
-                             cudaStream_t st) {
+cudaError_t launch_attention(const float* q, const float* kraw, const float* vraw, const float* qnw, const float* knw,
+                             const double* cos_t, const double* sin_t, double eps, bool own_kv, float* kc, float* vc,
+                             const int32_t* pos, int M, int H, int KVH, int cap, float scale, float* part_m,
+                             float* part_l, float* part_o, int* err, cudaStream_t st) {
   if (cap % ATT_CHUNK != 0 || cap > 4096) return cudaErrorInvalidValue;
   const size_t smem = attn_smem_bytes(M, H, KVH);
   static bool attr = false;
@@ -536,8 +526,8 @@ cudaError_t launch_attention(const float* q, const float* kc, const float* vc, c
     attr = true;
   }
   const int chunks = cap / ATT_CHUNK;
-  return pdl_launch(attn_partial_kernel, dim3(chunks, KVH), dim3(ATT_THREADS), smem, st, q, kc, vc, pos, M, H, KVH, cap,
-                    scale, part_m, part_l, part_o, err);
+  return pdl_launch(attn_partial_kernel, dim3(chunks, KVH), dim3(ATT_THREADS), smem, st, q, kraw, vraw, qnw, knw, cos_t,
+                    sin_t, eps, int(own_kv), kc, vc, pos, M, H, KVH, cap, scale, part_m, part_l, part_o, err);
 }
 
 cudaError_t launch_attn_combine(const float* part_m, const float* part_l, const float* part_o, const int32_t* pos,

@@ -13,13 +13,15 @@ cudaError_t launch_embed(const uint8_t* w, int type, int nb, int vocab, const in
                          double scale, int* err, cudaStream_t st);
 cudaError_t launch_norm_quant(bool resid, float* x, const float* y, const float* w_post, const float* w_pre, double eps,
                               int M, int D, const Q8Buf& q, float* n_out, cudaStream_t st);
-cudaError_t launch_qkv_post(const float* q, const float* k, const float* v, const float* qnw, const float* knw,
-                            const int32_t* pos, const double* cos_t, const double* sin_t, int M, int H, int KVH,
-                            int cap, double eps, bool has_kv, float* q_out, float* kc, float* vc, cudaStream_t st);
 size_t attn_smem_bytes(int M, int H, int KVH);
-cudaError_t launch_attention(const float* q, const float* kc, const float* vc, const int32_t* pos, int M, int H,
-                             int KVH, int cap, float scale, float* part_m, float* part_l, float* part_o, int* err,
-                             cudaStream_t st);
+// Attention over the raw q (and, in an own-KV layer, raw k/v) projections of
+// M tokens: QK-norm + RoPE of the queries and of this step's K/V rows (written
+// to kc/vc), split-KV partials into part_m/part_l/part_o for
+// launch_attn_combine.
+cudaError_t launch_attention(const float* q, const float* kraw, const float* vraw, const float* qnw, const float* knw,
+                             const double* cos_t, const double* sin_t, double eps, bool own_kv, float* kc, float* vc,
+                             const int32_t* pos, int M, int H, int KVH, int cap, float scale, float* part_m,
+                             float* part_l, float* part_o, int* err, cudaStream_t st);
 cudaError_t launch_attn_combine(const float* part_m, const float* part_l, const float* part_o, const int32_t* pos,
                                 int M, int H, int KVH, int cap, const Q8Buf& q, float* attn_out, cudaStream_t st);
 cudaError_t launch_geglu_quant(const float* gate, const float* up, int M, int F, const Q8Buf& q, float* act_out,

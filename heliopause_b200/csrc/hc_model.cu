@@ -9,7 +9,7 @@
 // with per-position top-k :1441-1450).
 //
 // Kernel chain per layer (all launched with programmatic dependent launch):
-//   [norm+quant] QKV GEMV (one launch) -> QK-norm/RoPE/KV write -> split-KV
+//   [norm+quant] QKV GEMV (one launch) -> QK-norm/RoPE/KV write + split-KV
 //   attention -> combine + f16 cast + quant -> O GEMV -> post-attention
 //   residual + FFN norm + quant -> gate/up GEMV (one launch) -> GEGLU + quant
 //   -> down GEMV -> post-FFN residual + next layer's attention norm + quant.
@@ -52,7 +52,7 @@ struct hpc_model_s {
   // workspaces (sized for cfg.max_tokens columns)
   void* arena = nullptr;
   size_t arena_bytes = 0;
-  float *x = nullptr, *qb = nullptr, *kb = nullptr, *vb = nullptr, *qr = nullptr, *o = nullptr, *g = nullptr,
+  float *x = nullptr, *qb = nullptr, *kb = nullptr, *vb = nullptr, *o = nullptr, *g = nullptr,
         *u = nullptr, *f = nullptr;
   float *pm = nullptr, *pl = nullptr, *po = nullptr;
   double *cos_t = nullptr, *sin_t = nullptr;
@@ -143,7 +143,6 @@ int hpc_model_create(const hpc_model_config* cfg, hpc_model* out) {
       {(void**)&m->qb, sizeof(float) * M * H * HD},
       {(void**)&m->kb, sizeof(float) * M * KVH * HD},
       {(void**)&m->vb, sizeof(float) * M * KVH * HD},
-      {(void**)&m->qr, sizeof(float) * M * H * HD},
       {(void**)&m->o, sizeof(float) * M * D},
       {(void**)&m->g, sizeof(float) * M * F},
       {(void**)&m->u, sizeof(float) * M * F},
@@ -466,12 +465,10 @@ static int enqueue_step(hpc_model m, int M, int k, cudaStream_t st) {
     int rc = own_kv ? mm({{L.w[HPC_W_Q], m->qb}, {L.w[HPC_W_K], m->kb}, {L.w[HPC_W_V], m->vb}}, m->q8d, m->q8d_bytes, D)
                     : mm({{L.w[HPC_W_Q], m->qb}}, m->q8d, m->q8d_bytes, D);
     if (rc != HPC_OK) return rc;
-    HPC_CK(hc::launch_qkv_post(m->qb, m->kb, m->vb, L.norm[HPC_N_Q], L.norm[HPC_N_K], m->pos, m->cos_t, m->sin_t, M, H,
-                               KVH, c.context, eps, own_kv, m->qr, m->kc[kvl], m->vc[kvl], st),
-           "qk norm / rope / kv");
-    HPC_CK(hc::launch_attention(m->qr, m->kc[kvl], m->vc[kvl], m->pos, M, H, KVH, c.context, 1.0f, m->pm, m->pl,
-                                m->po, m->err, st),
-           "attention");
+    HPC_CK(hc::launch_attention(m->qb, m->kb, m->vb, L.norm[HPC_N_Q], L.norm[HPC_N_K], m->cos_t, m->sin_t, eps, own_kv,
+                                m->kc[kvl], m->vc[kvl], m->pos, M, H, KVH, c.context, 1.0f, m->pm, m->pl, m->po,
+                                m->err, st),
+           "qk norm / rope / kv + attention");
     HPC_CK(hc::launch_attn_combine(m->pm, m->pl, m->po, m->pos, M, H, KVH, c.context, qd, nullptr, st),
            "attention combine");
     rc = mm({{L.w[HPC_W_O], m->o}}, m->q8d, m->q8d_bytes, size_t(H) * HD);

@@ -649,7 +649,7 @@ __device__ __forceinline__ bool attention_stage(const StreamCtx& x, Ring& r, int
   if (active) {
     // Vectors of this KV head (thread d = dimension): the G query heads and,
     // for the CTA that holds the new token of an own-KV layer, its key and
-    // value.  QK-norm (f64 sums) and NeoX RoPE as qkv_post_kernel; queries
+    // value.  QK-norm (f64 sums) and NeoX RoPE as head_norm_rope of the per-kernel step; queries
     // are rounded with the Rust f16 codec (lib.rs:590-597).
     constexpr int NV = P_MAX_G + 2;
     const bool fresh_own = has_fresh && L.own_kv;
