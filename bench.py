@@ -288,7 +288,7 @@ class DecodeConfig3:
 
     def kernel_launch_count(self) -> int:
         s = self.shape
-        per_layer = 10  # norm, QKV, qk/rope/kv, attention, combine, O, norm, gate/up, geglu, down
+        per_layer = 9  # norm, QKV, qk-norm/rope/kv + attention, combine, O, norm, gate/up, geglu, down
         return 2 + s.layers * per_layer + 1 + 2  # rope table + embed ... final norm + LM head + merge
 
     def roofline(self, peak_gbs: float) -> dict:
