@@ -337,6 +337,40 @@ class DecodeConfig3:
                 "bytes_per_token": self.step_bytes,
                 "l2": f"inputs larger than L2: {self.step_bytes / 1e9:.2f} GB of weights+KV streamed per step"}
 
+    def mtp_run(self, n_tokens: int = 256, n_spec: int = 4, context: int = 1024) -> dict:
+        """MTP speculative decoding on this model -- a
+        one-layer draft head of the same width proposes n_spec tokens, one
+        batched verify over n_spec + 1 positions, sampling acceptance at
+        temperature 1 with seeded uniforms, n_tokens generated from position
+        `context`.  Wall clock of the whole host loop (draft, verify, accept)."""
+        import time as _t
+
+        from heliopause_b200 import generation as gen
+        from heliopause_b200.mtp import CudaMtpDraftHead, MtpDraftShape, MtpGenerator, SyntheticDraftWeights
+        torch = self.torch
+        ds = MtpDraftShape()
+        head = CudaMtpDraftHead(ds, SyntheticDraftWeights(ds, seed=7), gpu_seed=7)
+        g = MtpGenerator(self.model, head)
+        opt = gen.resolve_generation_sampling_options(do_sample=True, temperature=1.0, seed=1234)
+        rng = gen.create_deterministic_rng(opt.seed)
+        first, ctx = g.start(12345, context - 1, opt, rng)  # warms the draft/verify paths' buffers
+        g.generate(first, ctx, 8, n_spec, opt, rng)
+        rng = gen.create_deterministic_rng(opt.seed)
+        torch.cuda.synchronize()
+        t0 = _t.perf_counter()
+        first, ctx = g.start(12345, context - 1, opt, rng)
+        toks, rounds, acc = g.generate(first, ctx, n_tokens, n_spec, opt, rng)
+        torch.cuda.synchronize()
+        dt = _t.perf_counter() - t0
+        del g, head
+        torch.cuda.empty_cache()
+        return {"tokens": len(toks), "tok_per_s": len(toks) / dt, "seconds": dt, "rounds": rounds,
+                "accepted_drafts": acc, "acceptance_rate": acc / max(1, rounds * n_spec),
+                "draft_tokens_per_round": n_spec, "context_start": context,
+                "sampling": {"temperature": opt.temperature, "top_k": opt.top_k, "top_p": opt.top_p, "seed": opt.seed},
+                "note": "config 4: random draft-head weights (acceptance near chance); draft head f32 on dequantized "
+                        "weights (cuBLAS GEMV), verify = the fused decoder forward at M=n_spec+1"}
+
     @classmethod
     def cpu_sampler(cls, threads: int):
         return CpuDecodeSample(threads, cls.position, cls.k)
@@ -680,6 +714,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="decode-config3")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-mtp", action="store_true", help="skip the config-4 MTP generation field")
     ap.add_argument("--m", type=int, default=1, help="columns (tokens) for the gemv-config2 / lmhead-config5 workloads")
     args = ap.parse_args()
     if args.warmup < 3:
@@ -762,6 +797,8 @@ def main():
         dist.all_reduce(e2e_s, op=dist.ReduceOp.MAX)
     e2e_value = wl.units_per_step() * ranks_of_work / float(e2e_s[0])
 
+    mtp = wl.mtp_run() if hasattr(wl, "mtp_run") and not args.no_mtp and world == 1 else None
+
     peaks = _peaks()
     roofline = wl.roofline(peaks["hbm_gbs"])
     roofline["peak_source"] = peaks["source"]
@@ -789,6 +826,8 @@ def main():
                                 "frac_of_peak": wl.step_bytes / (ms / 1e3) / 1e9 / peaks["hbm_gbs"]}
         if verify:
             line["verify"] = verify
+        if mtp:
+            line["mtp"] = mtp
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()

@@ -183,6 +183,8 @@ class CudaDecoderModel:
 
     def set_norm(self, layer: int, slot: int, values: np.ndarray) -> None:
         v = np.ascontiguousarray(values, np.float32)
+        if slot == N_OUTPUT:
+            self.output_norm_values = v.copy()
         hk.assert_cuda_ok(_lib.lib().hpc_model_set_norm(self._h, layer, slot, v.ctypes.data_as(C.c_void_p), v.size),
                           "modelSetNorm")
 

@@ -1,0 +1,365 @@
+"""MTP speculative decoding on the GPU: the draft head ("MTP assistant") and
+the draft / batched-verify / accept loop.
+
+The draft head restates runWasmMtpAssistant
+(packages/engine/src/runner/wasm/mtp-assistant-runner.ts:43-242; the WebGPU
+runner, runner/webgpu/mtp-assistant-runner.ts, computes the same in f32):
+
+    x      = pre_projection @ [target embedding ; target current hidden]
+    per layer (attention over the TARGET's KV cache, model.ts:457-478 layer map):
+      a    = rmsNorm(x, attn_norm);  q = normHeads(Wq a, q_norm);  q = RoPE(q)
+             (full-attention NeoX, only floor(nDims * 0.25 / 2) pairs rotated)
+      o    = Wo gqa_attention(q, K, V, causal, scale 1)
+      r    = x + rmsNorm(o, post_attention_norm)
+      f    = r + rmsNorm(Wd fround(gelu(Wg n) * (Wu n)), post_ffw_norm),  n = rmsNorm(r, ffn_norm)
+      x    = fround(f * layer_output_scale)
+    h      = rmsNorm(x, output_norm)
+    backbone hidden = post_projection @ h
+    top tokens = maskedEmbeddingTopTokens(h, centroids @ h): the top
+             centroid_top_k centroids select token ids through token_ordering,
+             scored by their embedding rows . h (value desc, id asc).
+
+All matmuls are f32 products of dequantized weights with f32 inputs, as
+hp_matmul_dequantized_f32 (lib.rs:103-154) / the WebGPU F32 matmul do.  The
+weights are dequantized once by the library's bit-exact dequantization
+(hpc_weight_dequantize) and multiplied with cuBLAS f32 GEMV; the norms,
+RoPE, attention softmax (f64 exp, f16-rounded query) and GELU follow the
+reference's rounding points.  Summation orders differ from the reference's
+sequential loops, so outputs agree to f32 rounding.
+
+The loop (mtp_generate) restates generateAssistantWithMtp
+(packages/engine/src/chat.ts:692-776) with proposeMtpDraft
+(mtp-generation.ts:92-137): drafts from the pending token at the context's
+constant position, one batched verify of [pending, d1..dn] through
+CudaDecoderModel.forward, acceptance by generation.accept_mtp_draft, and the
+next context from the verify's hidden at the last committed position
+(finalizeMtpVerification; normalizedHiddenSlice,
+webgpu/mtp-target-runner.ts:225-244).
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from . import generation as gen
+from . import kernels as hk
+from . import synthetic as syn
+
+
+@dataclass(frozen=True)
+class MtpDraftShape:
+    backbone: int = 2048        # target hidden size
+    hidden: int = 2048          # draft head width
+    heads: int = 8
+    kv_heads: int = 2           # equals the target's KV heads
+    head_dim: int = 256
+    ffn: int = 8192
+    vocab: int = 262144
+    n_centroids: int = 2048
+    centroid_top_k: int = 32
+    layers: int = 1
+    rope_theta: float = 1.0e6
+    rms_eps: float = 1e-6
+
+    @property
+    def active_pairs(self) -> int:
+        """Rotated pairs of a full-attention layer (mtp-assistant-runner.ts:96)."""
+        return int(math.floor(self.head_dim * 0.25 / 2))
+
+    def matrices(self):
+        """name -> (type, K, N) of every quantized matrix (token_embd: rows = vocab)."""
+        E, D, Hq = self.hidden, self.backbone, self.heads * self.head_dim
+        m = {"mtp.pre_projection.weight": (syn.Q4_K, 2 * D, E), "mtp.post_projection.weight": (syn.Q4_K, E, D),
+             "mtp.centroids.weight": (syn.Q4_K, E, self.n_centroids), "token_embd.weight": (syn.Q6_K, E, self.vocab)}
+        for layer in range(self.layers):
+            m[f"blk.{layer}.attn_q.weight"] = (syn.Q4_K, E, Hq)
+            m[f"blk.{layer}.attn_output.weight"] = (syn.Q4_K, Hq, E)
+            m[f"blk.{layer}.ffn_gate.weight"] = (syn.Q4_K, E, self.ffn)
+            m[f"blk.{layer}.ffn_up.weight"] = (syn.Q4_K, E, self.ffn)
+            m[f"blk.{layer}.ffn_down.weight"] = (syn.Q4_K, self.ffn, E)
+        return m
+
+    def vectors(self):
+        """name -> length of every f32 norm vector."""
+        v = {"output_norm.weight": self.hidden}
+        for layer in range(self.layers):
+            for n in ("attn_norm", "post_attention_norm", "ffn_norm", "post_ffw_norm"):
+                v[f"blk.{layer}.{n}.weight"] = self.hidden
+            v[f"blk.{layer}.attn_q_norm.weight"] = self.head_dim
+        return v
+
+
+class SyntheticDraftWeights:
+    """Seeded draft head (BASELINE distributions): quantized fields uniform,
+    norms 1 + N(0, 0.1), layer output scale 1 + N(0, 0.1), token ordering a
+    seeded permutation of the vocabulary."""
+
+    def __init__(self, shape: MtpDraftShape, seed: int = 7):
+        self.s, self.seed = shape, seed
+
+    def matrix(self, name: str) -> np.ndarray:
+        t, k, n = self.s.matrices()[name]
+        return syn.quant_weight(t, n, k, seed=self.seed * 1000 + sum(map(ord, name)))
+
+    def vector(self, name: str) -> np.ndarray:
+        g = syn.rng(self.seed * 7919 + sum(map(ord, name)))
+        return (1.0 + 0.1 * g.standard_normal(self.s.vectors()[name])).astype(np.float32)
+
+    def layer_output_scale(self, layer: int) -> float:
+        g = syn.rng(self.seed * 31 + layer)
+        return float(np.float32(1.0 + 0.1 * g.standard_normal()))
+
+    def token_ordering(self) -> np.ndarray:
+        return syn.rng(self.seed * 13).permutation(self.s.vocab).astype(np.int32)
+
+
+def target_kv_layer(target_layers: int, target_kv_layers: int, draft_layers: int, draft_layer: int) -> int:
+    """mapMtpAssistantLayerToTargetKvLayer (model.ts:457-478) for a target
+    whose layers are all full-attention and whose first target_kv_layers own
+    a KV cache."""
+    bucket = min(target_layers - 1, (draft_layer + 1) * target_layers // draft_layers - 1)
+    for layer in range(bucket, -1, -1):
+        if layer < target_kv_layers:
+            return layer
+    raise ValueError(f"no target KV layer at or before depth {bucket}")
+
+
+# ---- f32 arithmetic with the reference's rounding points -------------------
+
+def _rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    """rmsNorm over the last dimension (mtp-assistant-runner.ts:275-290): f32
+    sum of squares, f64 scale, fround(fround(x * scale) * w)."""
+    ss = torch.sum(x * x, dim=-1, keepdim=True)  # f32
+    scale = 1.0 / torch.sqrt(ss.double() / x.shape[-1] + eps)
+    return ((x.double() * scale).float().double() * w.double()).float()
+
+
+def _rope_partial(q: torch.Tensor, position: int, n_dims: int, pairs: int, theta_base: float) -> torch.Tensor:
+    """ropeNeox with activePairCount (mtp-assistant-runner.ts:361-387): the
+    first `pairs` pairs (i, i + n_dims/2) of every head rotated; theta chain
+    in f32, cos/sin in f64."""
+    out = q.clone()
+    scale = theta_base ** (-2.0 / n_dims)
+    theta = float(position)
+    angles = []
+    for _ in range(pairs):
+        angles.append(theta)
+        theta = float(np.float32(theta * scale))
+    t = torch.tensor(angles, dtype=torch.float64, device=q.device)
+    c, s = torch.cos(t), torch.sin(t)
+    half = n_dims // 2
+    x0, x1 = q[:, :pairs].double(), q[:, half:half + pairs].double()
+    out[:, :pairs] = (x0 * c).float() - (x1 * s).float()
+    out[:, half:half + pairs] = (x0 * s).float() + (x1 * c).float()
+    return out
+
+
+def _gelu(v: torch.Tensor) -> torch.Tensor:
+    """gelu (mtp-assistant-runner.ts:399-411): tanh form, f32 rounding
+    points, no f16 round trip."""
+    x = v.double()
+    f = lambda t: t.float().double()
+    inner = f(f(math.sqrt(2 / math.pi) * x) * f(1 + f(0.044715 * f(x * x))))
+    out = f(f(0.5 * x) * f(1 + torch.tanh(inner)))
+    out = torch.where(x <= -10, torch.zeros_like(out), out)
+    out = torch.where(x >= 10, x, out)
+    return out.float()
+
+
+def _top_desc_id_asc(values: torch.Tensor, ids: torch.Tensor, k: int):
+    """topK ordering (runtime.ts:514-527) on the device: value descending,
+    id ascending among equal values.  `ids` must be ascending."""
+    order = torch.sort(values, descending=True, stable=True).indices[:k]
+    return ids[order], values[order]
+
+
+class CudaMtpDraftHead:
+    """The draft head resident on the current CUDA device (f32 weights)."""
+
+    def __init__(self, shape: MtpDraftShape, weights: SyntheticDraftWeights, *, gpu_seed: int | None = None):
+        """gpu_seed: generate the quantized matrices on the device (same
+        distributions, for benchmark-size heads) instead of weights.matrix."""
+        self.s = shape
+        self.w = {}
+        gen_ = None
+        if gpu_seed is not None:
+            from .model import gpu_synthetic_weight
+            gen_ = torch.Generator(device="cuda")
+            gen_.manual_seed(gpu_seed)
+        for name, (t, k, n) in shape.matrices().items():
+            data = weights.matrix(name) if gen_ is None else gpu_synthetic_weight(t, n, k, gen_)
+            h = hk.create_quantized_weight_handle("Q4_K" if t == syn.Q4_K else "Q6_K", data, k, n)
+            try:
+                self.w[name] = hk.dequantize_resident(h).reshape(n, k)
+            finally:
+                hk.release_quantized_weight_handle(h)
+        self.v = {name: torch.from_numpy(weights.vector(name)).cuda() for name in shape.vectors()}
+        self.scale = [weights.layer_output_scale(layer) for layer in range(shape.layers)]
+        order = torch.from_numpy(weights.token_ordering()).cuda().long()
+        per = shape.vocab // shape.n_centroids
+        # token_ordering slot c*per .. (c+1)*per-1 lists centroid c's tokens
+        self.centroid_tokens = order[:shape.n_centroids * per].view(shape.n_centroids, per)
+        self.centroid_ids = torch.arange(shape.n_centroids, device="cuda")
+
+    def run(self, target_embedding: torch.Tensor, target_hidden: torch.Tensor, kv, position: int, top_k: int):
+        """One draft step: (backbone hidden [backbone], ids, logits [top_k],
+        both on the device).  kv[layer] = (K [context][kv_heads][head_dim],
+        V in the reference orientation [head_dim][kv_heads][context]) of the
+        mapped target layer."""
+        s = self.s
+        x = self.w["mtp.pre_projection.weight"] @ torch.cat([target_embedding, target_hidden])
+        for layer in range(s.layers):
+            x = self._layer(layer, x, kv[layer], position)
+        h = _rms_norm(x, self.v["output_norm.weight"], s.rms_eps)
+        post = self.w["mtp.post_projection.weight"] @ h
+        ids, logits = self.masked_top_tokens(h, self.w["mtp.centroids.weight"] @ h, top_k)
+        return post, ids, logits
+
+    def masked_top_tokens(self, h: torch.Tensor, centroid_logits: torch.Tensor, top_k: int):
+        """maskedEmbeddingTopTokens (mtp-assistant-runner.ts:211-242): the
+        tokens of the top centroid_top_k centroids (deduplicated, ids outside
+        the vocabulary dropped) scored by their embedding row . h."""
+        s = self.s
+        c_ids, _ = _top_desc_id_asc(centroid_logits, self.centroid_ids, min(s.centroid_top_k, s.n_centroids))
+        toks = self.centroid_tokens[c_ids].reshape(-1)
+        toks = toks[(toks >= 0) & (toks < s.vocab)]
+        sel = torch.unique(toks)  # ascending: ties resolve to the lower id
+        vals = self.w["token_embd.weight"][sel] @ h
+        return _top_desc_id_asc(vals, sel, top_k)
+
+    def _layer(self, layer: int, x: torch.Tensor, kv, position: int) -> torch.Tensor:
+        s, w, v = self.s, self.w, self.v
+        p = f"blk.{layer}."
+        a = _rms_norm(x, v[p + "attn_norm.weight"], s.rms_eps)
+        q = _rms_norm((w[p + "attn_q.weight"] @ a).reshape(s.heads, s.head_dim), v[p + "attn_q_norm.weight"],
+                      s.rms_eps)
+        q = _rope_partial(q, position, s.head_dim, s.active_pairs, s.rope_theta)
+        o = w[p + "attn_output.weight"] @ self._attention(q, kv, position)
+        r = x + _rms_norm(o, v[p + "post_attention_norm.weight"], s.rms_eps)
+        n = _rms_norm(r, v[p + "ffn_norm.weight"], s.rms_eps)
+        act = (_gelu(w[p + "ffn_gate.weight"] @ n).double() * (w[p + "ffn_up.weight"] @ n).double()).float()
+        f = r + _rms_norm(w[p + "ffn_down.weight"] @ act, v[p + "post_ffw_norm.weight"], s.rms_eps)
+        return (f.double() * self.scale[layer]).float()
+
+    def _attention(self, q: torch.Tensor, kv, position: int) -> torch.Tensor:
+        """GQA attention of one query over the target KV (lib.rs:539-654 as
+        gqaAttentionWasm calls it for the draft head: f32 query, scale 1,
+        causal to `position`, f64 exp of the f32 score differences)."""
+        k, vv = kv  # K [ctx][kvh][hd], V [hd][kvh][ctx]
+        s = self.s
+        count = position + 1
+        g = s.heads // s.kv_heads
+        qg = q.view(s.kv_heads, g, s.head_dim)
+        scores = torch.einsum("khd,tkd->kht", qg, k[:count])           # [kvh][g][count] f32
+        p = torch.exp((scores - scores.amax(dim=-1, keepdim=True)).double()).float()
+        wts = p / p.sum(dim=-1, keepdim=True)
+        out = torch.einsum("kht,dkt->khd", wts, vv[:, :, :count])
+        return out.reshape(-1)
+
+
+# ---- the speculative decoding loop ------------------------------------------
+
+@dataclass
+class MtpContext:
+    position: int
+    current_hidden: torch.Tensor  # normalized target hidden (f32 [backbone])
+
+
+def normalized_hidden(hidden: torch.Tensor, output_norm: torch.Tensor, eps: float) -> torch.Tensor:
+    """normalizedHiddenSlice (webgpu/mtp-target-runner.ts:225-244)."""
+    return _rms_norm(hidden, output_norm, eps)
+
+
+class MtpGenerator:
+    """Target model + draft head + embedding table for the draft inputs."""
+
+    def __init__(self, target, draft: CudaMtpDraftHead):
+        """target: a loaded CudaDecoderModel (its tied embedding / LM head and
+        output norm feed the draft head's inputs)."""
+        self.t, self.d, self.ts = target, draft, target.shape
+        ds, ts = draft.s, target.shape
+        # validateMtpAssistantCompatibility (mtp-generation.ts:60-90) and the
+        # KV head size check of validateTargetKvLayer (mtp-assistant-runner.ts:258-273)
+        if ds.backbone != ts.hidden:
+            raise ValueError(f"MTP assistant backbone hidden size {ds.backbone} does not match target hidden size "
+                             f"{ts.hidden}.")
+        if ds.kv_heads != ts.kv_heads:
+            raise ValueError(f"MTP assistant KV head count {ds.kv_heads} does not match target KV head count "
+                             f"{ts.kv_heads}.")
+        if ds.vocab != ts.vocab:
+            raise ValueError(f"MTP assistant vocabulary size {ds.vocab} does not match target vocabulary size "
+                             f"{ts.vocab}.")
+        if ds.head_dim != ts.head_dim:
+            raise ValueError(f"Target KV head size mismatch for assistant layer 0: {ts.head_dim}/{ts.head_dim}")
+        self.embd = hk.dequantize_resident(target.lm_head_handle)  # [vocab][hidden] f32
+        self.out_norm = torch.from_numpy(target.output_norm_values).cuda()
+        ts = self.ts
+        self.kv_layers = [target_kv_layer(ts.layers, ts.kv_layers, draft.s.layers, i) for i in range(draft.s.layers)]
+
+    def embedding(self, token: int) -> torch.Tensor:
+        """readTargetInputEmbedding (mtp-generation.ts:190-197): row * sqrt(D), f32."""
+        return (self.embd[token].double() * math.sqrt(self.ts.hidden)).float()
+
+    def context_at(self, position: int, hidden: torch.Tensor) -> MtpContext:
+        """MtpTargetContext of a target position from its final residual."""
+        return MtpContext(position, normalized_hidden(hidden, self.out_norm, self.ts.rms_eps))
+
+    def start(self, token: int, position: int, sampling, rng):
+        """The prefill's last step (MtpTargetPrefillResult): forward `token`
+        at `position`, sample the first pending token from its top-k
+        distribution (chat.ts:700) and return it with the context there."""
+        ids, vals, hid = self.t.forward([token], [position], self.target_top_k(sampling), return_hidden=True)
+        dist = gen.MtpTokenDistribution(list(zip(ids[0].tolist(), vals[0].tolist())), self.ts.vocab)
+        return gen.sample_mtp_token_distribution(dist, sampling, rng), self.context_at(position, hid[0])
+
+    @staticmethod
+    def target_top_k(sampling) -> int:
+        """Candidates the verify forward reads back per position
+        (sampling.logitsTopK, chat.ts:730)."""
+        return sampling.logits_top_k or (1 if gen._greedy(sampling) else max(1, sampling.top_k))
+
+    def propose(self, pending: int, ctx: MtpContext, n: int, sampling, rng):
+        """proposeMtpDraft (mtp-generation.ts:92-137): constant position and
+        target KV, the backbone hidden fed back."""
+        kv = [self.t.kv(layer) for layer in self.kv_layers]
+        drafts, dists = [], []
+        token, hidden = pending, ctx.current_hidden
+        k = 1 if gen._greedy(sampling) else sampling.top_k  # mtpDraftTopK (mtp-generation.ts:230-234)
+        for _ in range(n):
+            post, ids, logits = self.d.run(self.embedding(token), hidden, kv, ctx.position, k)
+            pairs = list(zip(ids.tolist(), logits.tolist()))
+            token = gen.sample_next_token([gen.Candidate(i, v) for i, v in pairs], sampling, rng)
+            drafts.append(token)
+            dists.append(gen.MtpTokenDistribution(pairs, self.d.s.vocab, True))
+            hidden = post
+        return gen.MtpProposal(drafts, dists)
+
+    def verify(self, tokens, position: int, top_k: int):
+        """verifyMtpDraft: one batched target forward over [pending, d1..dn]
+        at positions position.. (webgpu/mtp-target-runner.ts:80-149)."""
+        ids, vals, hid = self.t.forward(tokens, [position + i for i in range(len(tokens))], top_k, return_hidden=True)
+        return gen.target_verification(ids.cpu().numpy(), vals.cpu().numpy(), self.ts.vocab, position), hid
+
+    def generate(self, first_token: int, ctx: MtpContext, n_tokens: int, n_spec: int, sampling, rng):
+        """generateAssistantWithMtp (chat.ts:692-776) without tokenizer and
+        stop tokens: `first_token` is the pending token at ctx.position + 1.
+        Returns (tokens, rounds, accepted drafts)."""
+        out, rounds, accepted = [], 0, 0
+        pending, pos = first_token, ctx.position + 1
+        top_k = self.target_top_k(sampling)
+        while len(out) < n_tokens and pos < self.ts.context:
+            budget = max(0, min(n_spec, n_tokens - len(out) - 1, self.ts.context - pos - 1))
+            prop = self.propose(pending, ctx, budget, sampling, rng) if budget else gen.MtpProposal([], [])
+            ver, hid = self.verify([pending] + prop.draft_token_ids, pos, top_k)
+            acc = gen.accept_mtp_draft(prop, ver, sampling, rng)
+            rounds += 1
+            accepted += acc.accepted_draft_length
+            committed = [pending] + prop.draft_token_ids[:acc.accepted_draft_length]
+            out.extend(committed[:n_tokens - len(out)])
+            ctx = self.context_at(pos + acc.committed_length - 1, hid[acc.committed_length - 1])
+            pos += acc.committed_length
+            pending = acc.next_token_id
+        return out, rounds, accepted

@@ -123,3 +123,62 @@ void hpo_scale_embedding(float *x, size_t n, double dim) {
     double s = sqrt(dim);
     for (size_t i = 0; i < n; i++) x[i] = (float)((double)x[i] * s);
 }
+
+/* ---- MTP draft head ("assistant") math --------------------------------- */
+
+/* packages/engine/src/runner/wasm/mtp-assistant-runner.ts:275-290 rmsNorm and
+ * runner/webgpu/mtp-target-runner.ts:225-244 normalizedHiddenSlice: unlike the
+ * decoder's rmsNormVector the sum of squares is accumulated in f32 (each square
+ * and each partial sum rounded); scale in f64; fround(fround(x * scale) * w). */
+void hpo_rms_norm_f32sum_rows(const float *x, size_t rows, size_t dim, const float *w, double eps, float *o) {
+    for (size_t r = 0; r < rows; r++) {
+        const float *xr = x + r * dim;
+        float ss = 0.0f;
+        for (size_t i = 0; i < dim; i++) ss = ss + xr[i] * xr[i];
+        double scale = 1.0 / sqrt((double)ss / (double)dim + eps);
+        for (size_t i = 0; i < dim; i++) o[r * dim + i] = (float)((double)(float)((double)xr[i] * scale) * (double)w[i]);
+    }
+}
+
+/* mtp-assistant-runner.ts:361-387 ropeNeox with activePairCount: only the first
+ * `pairs` pairs (i, i + ndims/2) of each head rotate; theta starts at the
+ * position and advances as fround(theta * base^(-2/ndims)). */
+void hpo_rope_neox_pairs(const float *x, size_t head, size_t nheads, int32_t pos, size_t ndims, size_t pairs,
+                         double freq_base, float *o) {
+    memcpy(o, x, head * nheads * sizeof(float));
+    double theta_scale = pow(freq_base, -2.0 / (double)ndims);
+    size_t half = ndims / 2;
+    for (size_t h = 0; h < nheads; h++) {
+        size_t row = h * head;
+        double theta = (double)pos;
+        for (size_t i = 0; i < pairs; i++) {
+            double x0 = x[row + i], x1 = x[row + half + i];
+            double c = cos(theta), s = sin(theta);
+            float a = (float)(x0 * c), b = (float)(x1 * s);
+            float e = (float)(x0 * s), f = (float)(x1 * c);
+            o[row + i] = a - b;
+            o[row + half + i] = e + f;
+            theta = (double)(float)(theta * theta_scale);
+        }
+    }
+}
+
+/* mtp-assistant-runner.ts:399-411 gelu (tanh form, no f16 round trips) and
+ * :150-153 the gated product fround(gelu(gate) * up). */
+static double gelu_f32points(float v) {
+    double x = v;
+    if (x <= -10.0) return 0.0;
+    if (x >= 10.0) return x;
+    float a = (float)(sqrt(2.0 / M_PI) * x);
+    float xx = (float)(x * x);
+    float b = (float)(0.044715 * (double)xx);
+    float c = (float)(1.0 + (double)b);
+    float inner = (float)((double)a * (double)c);
+    float h = (float)(0.5 * x);
+    float t = (float)(1.0 + tanh((double)inner));
+    return (double)(float)((double)h * (double)t);
+}
+
+void hpo_gelu_mul_f32(const float *gate, const float *up, size_t n, float *o) {
+    for (size_t i = 0; i < n; i++) o[i] = (float)(gelu_f32points(gate[i]) * (double)up[i]);
+}

@@ -85,6 +85,9 @@ def lib():
         L.hpo_softcap.argtypes = [_f32p, _sz, C.c_double]
         L.hpo_kv_update.argtypes = [_f32p, _f32p, _sz, _sz, _sz, _sz, _f32p, _f32p, _i32p, _sz]
         L.hpo_scale_embedding.argtypes = [_f32p, _sz, C.c_double]
+        L.hpo_rms_norm_f32sum_rows.argtypes = [_f32p, _sz, _sz, _f32p, C.c_double, _f32p]
+        L.hpo_rope_neox_pairs.argtypes = [_f32p, _sz, _sz, C.c_int32, _sz, _sz, C.c_double, _f32p]
+        L.hpo_gelu_mul_f32.argtypes = [_f32p, _f32p, _sz, _f32p]
         _lib = L
     return _lib
 
@@ -323,6 +326,34 @@ def kv_update(kc: np.ndarray, vc: np.ndarray, cap: int, nkv: int, klen: int, vle
 def scale_embedding(x, dim: int) -> np.ndarray:
     o = _f32(x).copy()
     lib().hpo_scale_embedding(_p(o, _f32p), o.size, float(dim))
+    return o
+
+
+# ------------------------------------------------------ MTP draft head math ---
+
+def rms_norm_f32sum_rows(x, w, eps: float) -> np.ndarray:
+    """mtp-assistant-runner.ts:275-290 rmsNorm (f32 sum of squares)."""
+    x = _f32(x)
+    w = _f32(w)
+    o = np.empty_like(x)
+    lib().hpo_rms_norm_f32sum_rows(_p(x, _f32p), x.size // w.size, w.size, _p(w, _f32p), eps, _p(o, _f32p))
+    return o
+
+
+def rope_neox_pairs(x, head: int, nheads: int, position: int, ndims: int, pairs: int, freq_base: float) -> np.ndarray:
+    """mtp-assistant-runner.ts:361-387 ropeNeox with activePairCount."""
+    x = _f32(x)
+    o = np.empty_like(x)
+    lib().hpo_rope_neox_pairs(_p(x, _f32p), head, nheads, position, ndims, pairs, freq_base, _p(o, _f32p))
+    return o
+
+
+def gelu_mul_f32(gate, up) -> np.ndarray:
+    """mtp-assistant-runner.ts:150-153 + 399-411: fround(gelu(gate) * up)."""
+    g = _f32(gate)
+    u = _f32(up)
+    o = np.empty_like(g)
+    lib().hpo_gelu_mul_f32(_p(g, _f32p), _p(u, _f32p), g.size, _p(o, _f32p))
     return o
 
 
