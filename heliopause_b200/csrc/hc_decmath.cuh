@@ -24,6 +24,12 @@ __device__ __forceinline__ void pdl_wait() {
 #endif
 }
 
+// Eight consecutive floats (16-byte aligned) into registers.
+__device__ __forceinline__ void load8(const float* p, float (&v)[8]) {
+  const float4 a = reinterpret_cast<const float4*>(p)[0], b = reinterpret_cast<const float4*>(p)[1];
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+
 // ---- f16 codecs ---------------------------------------------------------------
 
 // quant.ts:632-669 float32ToFloat16 (the TS codec used by layers.ts): round

@@ -120,17 +120,18 @@ __global__ void norm_quant_kernel(float* __restrict__ x, const float* __restrict
   __shared__ double scratch[32];
   __shared__ __align__(16) uint8_t stage[32][256];
   pdl_trigger();
-  pdl_wait();
   const int m = blockIdx.x, t = threadIdx.x, lane = t & 31, warp = t >> 5;
   const int warps = blockDim.x >> 5;
-  float h[8];
-  const float4* xp = reinterpret_cast<const float4*>(x + size_t(m) * D + 8 * t);
-  float4 a = xp[0], b = xp[1];
-  h[0] = a.x; h[1] = a.y; h[2] = a.z; h[3] = a.w; h[4] = b.x; h[5] = b.y; h[6] = b.z; h[7] = b.w;
+  // the norm weights are not written during the step: load them before the
+  // wait, so only the activation loads sit behind it
+  float wq[8], wp[8];
+  load8(w_pre + 8 * t, wq);
+  if (RESID) load8(w_post + 8 * t, wp);
+  pdl_wait();
+  float h[8], yv[8];
+  load8(x + size_t(m) * D + 8 * t, h);
+  if (RESID) load8(y + size_t(m) * D + 8 * t, yv);
   if (RESID) {
-    const float4* yp = reinterpret_cast<const float4*>(y + size_t(m) * D + 8 * t);
-    const float4 c = yp[0], e = yp[1];
-    const float yv[8] = {c.x, c.y, c.z, c.w, e.x, e.y, e.z, e.w};
     double ss = 0.0;
 #pragma unroll
     for (int i = 0; i < 8; ++i) ss += double(yv[i]) * double(yv[i]);
@@ -138,7 +139,7 @@ __global__ void norm_quant_kernel(float* __restrict__ x, const float* __restrict
     const double sc = 1.0 / sqrt(ss / double(D) + eps);
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      const float pn = float((double(yv[i]) * sc) * double(w_post[8 * t + i]));
+      const float pn = float((double(yv[i]) * sc) * double(wp[i]));
       h[i] = h[i] + pn;
     }
     float4* xo = reinterpret_cast<float4*>(x + size_t(m) * D + 8 * t);
@@ -152,7 +153,7 @@ __global__ void norm_quant_kernel(float* __restrict__ x, const float* __restrict
   const double sc = 1.0 / sqrt(ss / double(D) + eps);
   float n[8];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) n[i] = float((double(h[i]) * sc) * double(w_pre[8 * t + i]));
+  for (int i = 0; i < 8; ++i) n[i] = float((double(h[i]) * sc) * double(wq[i]));
   if (n_out) {
     float4* no = reinterpret_cast<float4*>(n_out + size_t(m) * D + 8 * t);
     no[0] = make_float4(n[0], n[1], n[2], n[3]);
@@ -184,22 +185,24 @@ constexpr int ATT_KSTRIDE = 256 + 4;        // floats per staged K row
 
 // One warp: QK-norm (f64 sum of squares, layers.ts:871-885 normHeads) of a
 // 256-vector held 8 values per lane (lane L: dimensions 8L..8L+7), optional
-// weight, optional NeoX RoPE (layers.ts:990-1033; pair (i, i+128) sits in
-// lanes L and L+16); products rounded to f32 as in the reference.
-__device__ __forceinline__ void head_norm_rope(float (&x)[8], const float* w, bool rope, const double* cos_t,
-                                               const double* sin_t, double eps, int lane) {
+// weight w (preloaded, same layout), optional NeoX RoPE (layers.ts:990-1033;
+// pair (i, i+128) sits in lanes L and L+16) with the lane's eight cos/sin
+// entries c8/s8 (pair indices (L mod 16)*8 .. +7); products rounded to f32
+// as in the reference.
+__device__ __forceinline__ void head_norm_rope(float (&x)[8], const float (&w)[8], bool has_w, bool rope,
+                                               const double (&c8)[8], const double (&s8)[8], double eps, int lane) {
   double ss = 0.0;
 #pragma unroll
   for (int i = 0; i < 8; ++i) ss += double(x[i]) * double(x[i]);
   ss = warp_sum_d(ss);
   const double sc = 1.0 / sqrt(ss / 256.0 + eps);
-  if (!w) {
+  if (!has_w) {
 #pragma unroll
     for (int i = 0; i < 8; ++i) x[i] = float(double(x[i]) * sc);
     return;
   }
 #pragma unroll
-  for (int i = 0; i < 8; ++i) x[i] = float((double(x[i]) * sc) * double(w[8 * lane + i]));
+  for (int i = 0; i < 8; ++i) x[i] = float((double(x[i]) * sc) * double(w[i]));
   if (!rope) return;
   float partner[8];
 #pragma unroll
@@ -207,11 +210,24 @@ __device__ __forceinline__ void head_norm_rope(float (&x)[8], const float* w, bo
   const bool first = lane < 16;
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
-    const int idx = (lane & 15) * 8 + i;  // pair index 0..127
-    const double c = cos_t[idx], s = sin_t[idx];
     const double x0 = first ? x[i] : partner[i];
     const double x1 = first ? partner[i] : x[i];
-    x[i] = first ? float(x0 * c) - float(x1 * s) : float(x0 * s) + float(x1 * c);
+    x[i] = first ? float(x0 * c8[i]) - float(x1 * s8[i]) : float(x0 * s8[i]) + float(x1 * c8[i]);
+  }
+}
+
+// The lane's eight cos and sin entries of one token's row of the RoPE tables.
+__device__ __forceinline__ void load_rope8(const double* cos_row, const double* sin_row, int lane, double (&c8)[8],
+                                           double (&s8)[8]) {
+  const double2* c = reinterpret_cast<const double2*>(cos_row + (lane & 15) * 8);
+  const double2* sn = reinterpret_cast<const double2*>(sin_row + (lane & 15) * 8);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const double2 a = c[i], b = sn[i];
+    c8[2 * i] = a.x;
+    c8[2 * i + 1] = a.y;
+    s8[2 * i] = b.x;
+    s8[2 * i + 1] = b.y;
   }
 }
 
@@ -224,7 +240,6 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_partial_kernel(
   constexpr int HD = 256, CH = ATT_CHUNK;
   static_assert(ATT_THREADS == HD, "thread d owns V row d");
   extern __shared__ __align__(16) float sm[];
-  __shared__ __align__(8) uint64_t bar;
   const int chunk = blockIdx.x, kvh = blockIdx.y;
   const int G = H / KVH, NQ = M * G;
   float* ks = sm;                     // [CH][ATT_KSTRIDE]
@@ -247,57 +262,65 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_partial_kernel(
     return;
   }
   const int nt = min(CH, count - t0);
-  auto issue = [&]() {
-    // cap % CH == 0 keeps every copied row inside the cache even for the
-    // last, partial chunk
-    if (threadIdx.x == 0) {
-      mbar_init(&bar, 1);
-      mbar_expect_tx(&bar, uint32_t(CH * HD * 4 * 2));
+  // Every row of the slice is copied before the wait (cap % CH == 0 keeps
+  // the copies of the last, partial chunk inside the cache) with 16-byte
+  // asynchronous copies spread over all threads (a warp copies 512
+  // contiguous bytes of a row).  Rows this step writes (the tokens at pos)
+  // may be stale in that copy; they are replaced below, after the copies
+  // have landed.
+  {
+    constexpr int PIECES = HD * 4 / 16;  // 16-byte pieces per row
+    for (int i = threadIdx.x; i < CH * PIECES; i += blockDim.x) {
+      const int t = i / PIECES, c = i % PIECES;
+      const size_t row = (size_t(t0 + t) * KVH + kvh) * HD + 4 * c;
+      cp_async16(ks + t * ATT_KSTRIDE + 4 * c, kc + row);
+      cp_async16(vs + t * ATT_KSTRIDE + 4 * c, vc + row);
     }
-    __syncwarp();
-    for (int t = threadIdx.x; t < CH; t += 32)
-      bulk_copy_g2s(ks + t * ATT_KSTRIDE, kc + (size_t(t0 + t) * KVH + kvh) * HD, HD * 4, &bar);
-    for (int t = threadIdx.x; t < CH; t += 32)
-      bulk_copy_g2s(vs + t * ATT_KSTRIDE, vc + (size_t(t0 + t) * KVH + kvh) * HD, HD * 4, &bar);
-  };
-  if (threadIdx.x < 32 && !fresh) issue();
-  pdl_wait();
-  // a slice with new rows is copied after the wait: in a shared-KV layer the
-  // rows come from the source layer's attention launch earlier in the step
-  if (threadIdx.x < 32 && fresh) issue();
-  __syncthreads();  // the slice's mbarrier (initialized by thread 0) is visible before anyone waits on it
+    cp_async_commit();
+  }
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, warps = blockDim.x >> 5;
+  // the QK-norm weights are not written during the step
+  float qw[8], kw[8];
+  load8(qnw + 8 * lane, qw);
+  if (own_kv && fresh) load8(knw + 8 * lane, kw);
+  pdl_wait();
   // queries of this KV head's G heads for every token: QK-norm + RoPE (the
   // token's row of the cos/sin tables), rounded with the Rust f16 codec
   // (lib.rs:590-597); one warp per vector
   for (int qi = warp; qi < NQ; qi += warps) {
     const int m = qi / G, h = kvh * G + qi % G;
-    const float* src = q + (size_t(m) * H + h) * HD + 8 * lane;
     float x[8];
-    const float4 a = reinterpret_cast<const float4*>(src)[0], b = reinterpret_cast<const float4*>(src)[1];
-    x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w; x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
-    head_norm_rope(x, qnw, true, cos_t + size_t(m) * (HD / 2), sin_t + size_t(m) * (HD / 2), eps, lane);
+    double c8[8], s8[8];
+    load8(q + (size_t(m) * H + h) * HD + 8 * lane, x);
+    load_rope8(cos_t + size_t(m) * (HD / 2), sin_t + size_t(m) * (HD / 2), lane, c8, s8);
+    head_norm_rope(x, qw, true, true, c8, s8, eps, lane);
 #pragma unroll
     for (int i = 0; i < 8; ++i) qs[qi * HD + 8 * lane + i] = round_f16_rust(x[i]);
   }
-  if (!mbar_wait_parity(&bar, 0, err)) return;
-  // own-KV layer: this step's K/V rows that fall in the slice are computed
-  // here (key: K-norm + RoPE; value: unweighted norm; layers.ts:241-268),
-  // written to the cache (layers.ts:887-911) and over the staged copies
-  if (own_kv && fresh) {
+  cp_async_wait_all();
+  __syncthreads();  // every thread's copies of the slice have landed
+  // This step's K/V rows in the slice replace the staged copies.  Own-KV
+  // layer: computed here (key: K-norm + RoPE; value: unweighted norm;
+  // layers.ts:241-268) and written to the cache (layers.ts:887-911).
+  // Shared-KV layer: read from the cache, where the source layer's attention
+  // launch earlier in the step wrote them.
+  if (fresh) {
     for (int job = warp; job < 2 * M; job += warps) {
       const int m = job >> 1, isv = job & 1, p = pos[m];
       if (p < t0 || p >= t0 + CH) continue;
-      const float* src = (isv ? vraw : kraw) + (size_t(m) * KVH + kvh) * HD + 8 * lane;
-      float x[8];
-      const float4 a = reinterpret_cast<const float4*>(src)[0], b = reinterpret_cast<const float4*>(src)[1];
-      x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w; x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
-      head_norm_rope(x, isv ? nullptr : knw, !isv, cos_t + size_t(m) * (HD / 2), sin_t + size_t(m) * (HD / 2),
-                     eps, lane);
       float* cache = (isv ? vc : kc) + (size_t(p % cap) * KVH + kvh) * HD + 8 * lane;
+      float x[8];
+      if (own_kv) {
+        double c8[8], s8[8];
+        load8((isv ? vraw : kraw) + (size_t(m) * KVH + kvh) * HD + 8 * lane, x);
+        if (!isv) load_rope8(cos_t + size_t(m) * (HD / 2), sin_t + size_t(m) * (HD / 2), lane, c8, s8);
+        head_norm_rope(x, kw, !isv, !isv, c8, s8, eps, lane);
+        reinterpret_cast<float4*>(cache)[0] = make_float4(x[0], x[1], x[2], x[3]);
+        reinterpret_cast<float4*>(cache)[1] = make_float4(x[4], x[5], x[6], x[7]);
+      } else {
+        load8(cache, x);
+      }
       float* staged = (isv ? vs : ks) + (p - t0) * ATT_KSTRIDE + 8 * lane;
-      reinterpret_cast<float4*>(cache)[0] = make_float4(x[0], x[1], x[2], x[3]);
-      reinterpret_cast<float4*>(cache)[1] = make_float4(x[4], x[5], x[6], x[7]);
 #pragma unroll
       for (int i = 0; i < 8; ++i) staged[i] = x[i];
     }
@@ -384,16 +407,28 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(const float* __restri
   __shared__ float vec[HD];
   __shared__ __align__(16) uint8_t stage[256];
   pdl_trigger();
-  pdl_wait();
   const int m = blockIdx.x, h = blockIdx.y, d = threadIdx.x, lane = d & 31, warp = d >> 5;
   const int G = H / KVH, NQ = M * G, kvh = h / G, qi = m * G + h % G;
+  // pos is written before the step starts (not by a kernel of this step)
   int maxpos = 0;
   for (int i = 0; i < M; ++i) maxpos = max(maxpos, pos[i]);
   const int count = min(cap, maxpos + 1);
   const int nch = (count + CH - 1) / CH;
+  pdl_wait();
+  // Every load is issued up front: the chunk maxima and sums (thread d <
+  // nch) and dimension d of all nch partial outputs (index clamped to the
+  // last chunk; chunks >= nch get weight 0 below).
+  float mc = -INFINITY, lc = 0.0f;
+  if (d < nch) {
+    mc = part_m[(size_t(d) * KVH + kvh) * NQ + qi];
+    lc = part_l[(size_t(d) * KVH + kvh) * NQ + qi];
+  }
+  const float* po = part_o + (size_t(kvh) * NQ + qi) * HD + d;
+  const size_t cstride = size_t(KVH) * NQ * HD;
+  float v[MAXC];
+#pragma unroll
+  for (int i = 0; i < MAXC; ++i) v[i] = po[size_t(min(i, nch - 1)) * cstride];
   // chunk maxima -> global max
-  float mc = -INFINITY;
-  if (d < nch) mc = part_m[(size_t(d) * KVH + kvh) * NQ + qi];
   float mx = mc;
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
@@ -404,10 +439,10 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(const float* __restri
   __syncthreads();
   // chunk weights and the total normalizer
   double lw = 0.0;
-  if (d < nch) {
-    const float w = mc == -INFINITY ? 0.0f : float(exp(double(mc - gmax)));
+  if (d < MAXC) {
+    const float w = (d >= nch || mc == -INFINITY) ? 0.0f : float(exp(double(mc - gmax)));
     wch[d] = w;
-    lw = double(w) * double(part_l[(size_t(d) * KVH + kvh) * NQ + qi]);
+    lw = double(w) * double(lc);
   }
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) lw += __shfl_xor_sync(0xffffffffu, lw, off);
@@ -415,26 +450,10 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(const float* __restri
   __syncthreads();
   double l = 0.0;
   for (int w = 0; w < 8; ++w) l += red[w];
-  // weighted sum over chunks for dimension d (independent loads, unrolled)
+  // weighted sum over chunks for dimension d, in chunk order
   float o = 0.0f;
-  const float* po = part_o + (size_t(kvh) * NQ + qi) * HD + d;
-  const size_t cstride = size_t(KVH) * NQ * HD;
-  int c = 0;
-  for (; c + 32 <= nch; c += 32) {
-    float v[32];
 #pragma unroll
-    for (int i = 0; i < 32; ++i) v[i] = po[size_t(c + i) * cstride];
-#pragma unroll
-    for (int i = 0; i < 32; ++i) o += wch[c + i] * v[i];
-  }
-  for (; c + 8 <= nch; c += 8) {
-    float v[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) v[i] = po[size_t(c + i) * cstride];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) o += wch[c + i] * v[i];
-  }
-  for (; c < nch; ++c) o += wch[c] * po[size_t(c) * cstride];
+  for (int i = 0; i < MAXC; ++i) o += wch[i] * v[i];
   const float n = round_f16_ts(float(double(o) / l));
   vec[d] = n;
   if (attn_out) attn_out[(size_t(m) * H + h) * HD + d] = n;

@@ -27,6 +27,7 @@
 // order than the reference's 8-lane accumulators, so outputs agree to f32
 // rounding.
 #include <cooperative_groups.h>
+#include <cstdlib>
 
 #include "hc_common.cuh"
 #include "hc_bulk.cuh"
@@ -77,6 +78,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, UC == Q4K_CHUNKS ? GEMV_CTAS_PER
     gemv_kernel(const __grid_constant__ GemvParams p) {
   extern __shared__ __align__(16) uint8_t smem[];
   __shared__ float red[GEMV_WARPS_PER_CTA][NC][32];
+  __shared__ __align__(8) uint64_t act_bar;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 #if __CUDA_ARCH__ >= 900
   asm volatile("griddepcontrol.launch_dependents;");
@@ -137,9 +139,9 @@ __global__ void __launch_bounds__(GEMV_THREADS, UC == Q4K_CHUNKS ? GEMV_CTAS_PER
 #if __CUDA_ARCH__ >= 900
     asm volatile("griddepcontrol.wait;" ::: "memory");
 #endif
-    stage_activations(p, act_a, act_b, kb0, nblk);
+    stage_activations_bulk(p, act_a, act_b, kb0, nblk, &act_bar);
     __syncthreads();
-    const bool ok = mbar_wait_parity(&bar, 0, p.err);
+    const bool ok = mbar_wait_parity(&bar, 0, p.err) & mbar_wait_parity(&act_bar, 0, p.err);
     if (item0 < nitems) {
       float acc[NC];
 #pragma unroll
@@ -158,13 +160,35 @@ __global__ void __launch_bounds__(GEMV_THREADS, UC == Q4K_CHUNKS ? GEMV_CTAS_PER
   } else {
     UnitRegsN<UC> buf[2];
     int first_type = TYPE_Q4_K;
-    if (item0 < nitems) load_unit<UC>(buf[0], unit_addr(p, item0, 0, &first_type), first_type, lane);
+    __shared__ __align__(8) uint64_t pre_bar[GEMV_WARPS_PER_CTA];
+    const int ub_max = unit_bytes(UC == Q4K_CHUNKS ? TYPE_Q4_K : TYPE_Q6_K);
+    uint8_t* staged = smem + (gemv_smem_bytes(p, nblk) + 15) / 16 * 16 + size_t(warp) * p.pre * ub_max;
+    if (item0 < nitems) {
+      load_unit<UC>(buf[0], unit_addr(p, item0, 0, &first_type), first_type, lane);
+      if (p.pre > 0 && lane == 0) {
+        // units 1..pre of this warp's item into its shared-memory slots
+        const uint32_t ub = uint32_t(unit_bytes(first_type));
+        mbar_init(&pre_bar[warp], 1);
+        mbar_expect_tx(&pre_bar[warp], ub * uint32_t(p.pre));
+        for (int jj = 1; jj <= p.pre; ++jj) {
+          int t;
+          bulk_copy_g2s(staged + size_t(jj - 1) * ub_max, unit_addr(p, item0, jj, &t), ub, &pre_bar[warp]);
+        }
+      }
+      __syncwarp();
+    }
 #if __CUDA_ARCH__ >= 900
     asm volatile("griddepcontrol.wait;" ::: "memory");
 #endif
-    stage_activations(p, act_a, act_b, kb0, nblk);
+    stage_activations_bulk(p, act_a, act_b, kb0, nblk, &act_bar);
     __syncthreads();
-    stream_items<NC, UC>(p, act, item0, istride, nitems, lane, buf[0], first_type, flush);
+    mbar_wait_parity(&act_bar, 0, p.err);
+    if (p.pre > 0) {
+      if (item0 < nitems)
+        prefetched_item<NC, UC>(p, act, item0, lane, buf[0], first_type, staged, ub_max, &pre_bar[warp], flush);
+    } else {
+      stream_items<NC, UC>(p, act, item0, istride, nitems, lane, buf[0], first_type, flush);
+    }
   }
   if (p.split == 1) return;
 
@@ -182,31 +206,33 @@ __global__ void __launch_bounds__(GEMV_THREADS, UC == Q4K_CHUNKS ? GEMV_CTAS_PER
     }
     return;
   }
-  // cluster split: CTA partial (warp order), then rank 0 sums ranks in order
+  // cluster split: every rank stores its CTA partial (warp order) into its
+  // slot of rank 0's gather array; after one cluster barrier rank 0 sums the
+  // slots in rank order (so only rank 0's own shared memory is read late)
+  __shared__ float gather[GEMV_MAX_CLUSTER][NC][32];
+  cg::cluster_group cl = cg::this_cluster();
+  const int csize = p.split / GEMV_WARPS_PER_CTA, rank = blockIdx.x % csize;
   if (warp == 0) {
+    float* dst = cl.map_shared_rank(&gather[0][0][0], 0) + rank * NC * 32;
 #pragma unroll
     for (int c = 0; c < NC; ++c) {
       float v = red[0][c][lane];
 #pragma unroll
       for (int w = 1; w < GEMV_WARPS_PER_CTA; ++w) v += red[w][c][lane];
-      red[0][c][lane] = v;
+      dst[c * 32 + lane] = v;
     }
   }
-  cg::cluster_group cl = cg::this_cluster();
   cl.sync();
-  const int csize = p.split / GEMV_WARPS_PER_CTA;
-  if (blockIdx.x % csize == 0 && warp == 0) {
+  if (rank == 0 && warp == 0) {
     float v[NC];
 #pragma unroll
     for (int c = 0; c < NC; ++c) v[c] = 0.0f;
     for (int r = 0; r < csize; ++r) {
-      const float* remote = cl.map_shared_rank(&red[0][0][0], r);
 #pragma unroll
-      for (int c = 0; c < NC; ++c) v[c] += remote[c * 32 + lane];
+      for (int c = 0; c < NC; ++c) v[c] += gather[r][c][lane];
     }
     store_tile<NC>(p, blockIdx.x / csize, v, lane);
   }
-  cl.sync();  // keep every CTA's shared memory alive until rank 0 has read it
 }
 
 int sm_count() {
@@ -229,6 +255,18 @@ int persistent_grid(int items, int cap) {
 
 static int ctas_per_sm(const GemvParams& p) { return p.q4small ? GEMV_CTAS_PER_SM_Q4 : GEMV_CTAS_PER_SM; }
 
+// Per-SM shared memory a streaming launch may fill with prefetched units:
+// GEMV_PRE_SM_SMEM, or HPC_GEMV_PREFETCH_KB (0 turns prefetching off).
+static long gemv_pre_sm_smem() {
+  static long v = -1;
+  if (v < 0) {
+    const char* e = getenv("HPC_GEMV_PREFETCH_KB");
+    v = e ? atol(e) * 1024 : long(GEMV_PRE_SM_SMEM);
+    if (v < 0) v = 0;
+  }
+  return v;
+}
+
 void gemv_plan(GemvParams& p) {
   // Split K as far as the launch still fits in one wave of resident CTAs
   // (ctas_per_sm per SM, one item per warp); parts stay >= 1 block and the
@@ -249,7 +287,7 @@ void gemv_plan(GemvParams& p) {
   // one wave counting the CTAs that the staged units leave room for.
   const size_t unit_smem = size_t(GEMV_WARPS_PER_CTA) * p.bps * unit_bytes(p.q4small ? TYPE_Q4_K : TYPE_Q6_K);
   const int nblk = p.split > GEMV_WARPS_PER_CTA ? GEMV_WARPS_PER_CTA * p.bps : p.nb;
-  const size_t cta_smem = unit_smem + gemv_smem_bytes(p, nblk) + 2048;  // + static shared memory
+  const size_t cta_smem = unit_smem + gemv_smem_bytes(p, nblk) + gemv_static_smem(p.ncols);
   const int by_smem = int(size_t(GEMV_SM_SMEM) / cta_smem);
   const int bulk_ctas = sm_count() * (by_smem < ctas_per_sm(p) ? by_smem : ctas_per_sm(p));
   const int grid_items = (p.total_tiles * p.split + GEMV_WARPS_PER_CTA - 1) / GEMV_WARPS_PER_CTA;
@@ -258,6 +296,20 @@ void gemv_plan(GemvParams& p) {
   if (p.split == 1 && p.bulk) {
     // one item per warp in bulk mode: make the grid non-persistent
     p.bulk = p.total_tiles <= cap_warps;
+  }
+  // Streaming launches of one or two columns with one item per warp
+  // prefetch units 1..pre of each item into shared memory before waiting for
+  // the previous kernel, as many as fit in GEMV_PRE_SM_SMEM shared by the
+  // CTAs that share an SM.  (Wider launches measured slower with it: the
+  // larger activation slices leave room for one unit at most.)
+  p.pre = 0;
+  if (!p.bulk && p.split > 1 && p.bps > 1 && p.ncols <= 2) {
+    const int ub = unit_bytes(p.q4small ? TYPE_Q4_K : TYPE_Q6_K);
+    const int per_sm = (grid_items + sm_count() - 1) / sm_count();
+    const long budget = long(gemv_pre_sm_smem() / per_sm) - long(gemv_smem_bytes(p, nblk)) -
+                        long(gemv_static_smem(p.ncols)) - 16;
+    const int pre = budget > 0 ? int(budget / (long(GEMV_WARPS_PER_CTA) * ub)) : 0;
+    p.pre = pre < p.bps - 1 ? pre : p.bps - 1;
   }
   p.err = device_status_word();
 }
@@ -273,6 +325,7 @@ static cudaError_t launch_nc(const GemvParams& p, cudaStream_t stream) {
   const int nblk = p.split > GEMV_WARPS_PER_CTA ? GEMV_WARPS_PER_CTA * p.bps : p.nb;
   size_t smem = (gemv_smem_bytes(p, nblk) + 15) / 16 * 16;
   if (p.bulk) smem += size_t(GEMV_WARPS_PER_CTA) * p.bps * unit_bytes(UC == Q4K_CHUNKS ? TYPE_Q4_K : TYPE_Q6_K);
+  else smem += size_t(GEMV_WARPS_PER_CTA) * p.pre * unit_bytes(UC == Q4K_CHUNKS ? TYPE_Q4_K : TYPE_Q6_K);
   if (smem > size_t(GEMV_MAX_SMEM)) return cudaErrorInvalidValue;
   static bool attr_set = false;
   if (!attr_set) {

@@ -15,6 +15,7 @@
 // so the loads of the next unit (possibly of the next item) are in flight
 // while the current one is computed.
 #pragma once
+#include "hc_bulk.cuh"
 #include "hc_common.cuh"
 #include "hc_kernels.cuh"
 #include "hc_unpack.cuh"
@@ -56,16 +57,30 @@ __device__ __forceinline__ void load_unit(UnitRegsN<UC>& r, const uint8_t* unit,
   }
 }
 
-template <int NC, int UC>
-__device__ __forceinline__ void q4k_regs(const UnitRegsN<UC>& r, int j, int ncols, const ActSlice& act,
-                                         float (&acc)[NC]) {
-  const Q4KHeader hd = q4k_header(r.c[0]);
+// Where a unit's 16-byte chunks come from: a register buffer, or shared
+// memory read chunk by chunk as the dot product consumes them.
+template <int UC>
+struct RegSrc {
+  const UnitRegsN<UC>& r;
+  __device__ __forceinline__ uint4 chunk(int k) const { return r.c[k]; }
+  __device__ __forceinline__ uint32_t dbits() const { return r.d; }
+};
+struct SmemSrc {
+  const uint4* p;       // the unit's first chunk for this lane (row)
+  const uint16_t* dp;   // this lane's Q6_K d
+  __device__ __forceinline__ uint4 chunk(int k) const { return p[k * TILE]; }
+  __device__ __forceinline__ uint32_t dbits() const { return *dp; }
+};
+
+template <int NC, class Src>
+__device__ __forceinline__ void q4k_src(const Src& r, int j, int ncols, const ActSlice& act, float (&acc)[NC]) {
+  const Q4KHeader hd = q4k_header(r.chunk(0));
   int isum[NC];
 #pragma unroll
   for (int col = 0; col < NC; ++col) isum[col] = 0;
 #pragma unroll
   for (int pp = 0; pp < 4; ++pp) {
-    const uint4 u0 = r.c[1 + 2 * pp], u1 = r.c[2 + 2 * pp];
+    const uint4 u0 = r.chunk(1 + 2 * pp), u1 = r.chunk(2 + 2 * pp);
     const uint32_t w[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
     const int s0 = hd.sc(2 * pp), s1 = hd.sc(2 * pp + 1);
 #pragma unroll
@@ -101,17 +116,19 @@ __device__ __forceinline__ void q4k_regs(const UnitRegsN<UC>& r, int j, int ncol
   }
 }
 
-template <int NC>
-__device__ __forceinline__ void q6k_regs(const UnitRegs& r, int j, int ncols, const ActSlice& act, float (&acc)[NC]) {
-  const float dw = f16_bits_to_f32(r.d);
-  const uint32_t scw[4] = {r.c[12].x, r.c[12].y, r.c[12].z, r.c[12].w};
+template <int NC, class Src>
+__device__ __forceinline__ void q6k_src(const Src& r, int j, int ncols, const ActSlice& act, float (&acc)[NC]) {
+  const float dw = f16_bits_to_f32(r.dbits());
+  const uint4 scv = r.chunk(12);
+  const uint32_t scw[4] = {scv.x, scv.y, scv.z, scv.w};
   int isum[NC];
 #pragma unroll
   for (int col = 0; col < NC; ++col) isum[col] = 0;
 #pragma unroll
   for (int s = 0; s < 8; ++s) {
-    const uint32_t nw[4] = {r.c[s].x, r.c[s].y, r.c[s].z, r.c[s].w};
-    const uint4 hv = r.c[8 + (s >> 1)];
+    const uint4 nv = r.chunk(s);
+    const uint32_t nw[4] = {nv.x, nv.y, nv.z, nv.w};
+    const uint4 hv = r.chunk(8 + (s >> 1));
     const uint32_t hw[4] = {hv.x, hv.y, hv.z, hv.w};
     uint32_t ua[4], ub[4];
 #pragma unroll
@@ -174,16 +191,32 @@ __device__ __forceinline__ void load_unit_smem(UnitRegsN<UC>& r, const uint8_t* 
 template <int NC, int UC>
 __device__ __forceinline__ void unit_compute(const UnitRegsN<UC>& r, int type, int j, int ncols, const ActSlice& act,
                                              float (&acc)[NC]) {
+  const RegSrc<UC> src{r};
   if constexpr (UC == Q4K_CHUNKS) {
-    q4k_regs<NC, UC>(r, j, ncols, act, acc);
+    q4k_src<NC>(src, j, ncols, act, acc);
   } else {
-    if (type == TYPE_Q4_K) q4k_regs<NC, UC>(r, j, ncols, act, acc);
-    else q6k_regs<NC>(r, j, ncols, act, acc);
+    if (type == TYPE_Q4_K) q4k_src<NC>(src, j, ncols, act, acc);
+    else q6k_src<NC>(src, j, ncols, act, acc);
+  }
+}
+
+// unit_compute on a unit staged in shared memory, read chunk by chunk as the
+// dot products consume it (no register buffer).
+template <int NC, int UC>
+__device__ __forceinline__ void unit_compute_smem(const uint8_t* unit, int type, int j, int ncols,
+                                                  const ActSlice& act, float (&acc)[NC], int lane) {
+  const SmemSrc src{reinterpret_cast<const uint4*>(unit) + lane,
+                    reinterpret_cast<const uint16_t*>(unit + Q6K_DPLANE_OFFSET) + lane};
+  if constexpr (UC == Q4K_CHUNKS) {
+    q4k_src<NC>(src, j, ncols, act, acc);
+  } else {
+    if (type == TYPE_Q4_K) q4k_src<NC>(src, j, ncols, act, acc);
+    else q6k_src<NC>(src, j, ncols, act, acc);
   }
 }
 
 // Single-column block dots reading the unit from shared memory chunk by
-// chunk (same arithmetic as q4k_regs / q6k_regs with NC = 1): the unit is
+// chunk (same arithmetic as q4k_src / q6k_src with NC = 1): the unit is
 // not held in registers, which keeps register pressure low inside the
 // persistent step kernel.  `unit` is the staged tile-block, lane = row.
 __device__ __forceinline__ float q4k_smem_dot(const uint8_t* unit, int j, const ActSlice& act, int lane) {
@@ -326,6 +359,40 @@ __device__ __forceinline__ void stream_items(const GemvParams& p, const ActSlice
   }
 }
 
+// One item per warp with units 1..pre already copied into shared memory
+// (`staged`, one ub_max slot per unit, completing on `bar`) and unit 0 in
+// `buf0`: computes unit 0 while loading unit pre+1, then the staged units,
+// then streams units pre+1 .. bps-1 through the two register buffers.  Units
+// are accumulated in order 0 .. bps-1, as stream_items does.
+template <int NC, int UC, class Flush>
+__device__ __forceinline__ void prefetched_item(const GemvParams& p, const ActSlice& act, int item, int lane,
+                                                UnitRegsN<UC>& buf0, int type, const uint8_t* staged, int ub_max,
+                                                uint64_t* bar, Flush& flush) {
+  float acc[NC];
+#pragma unroll
+  for (int c = 0; c < NC; ++c) acc[c] = 0.0f;
+  const int kbase = (item & (p.split - 1)) * p.bps - act.kb0;
+  UnitRegsN<UC> buf1;
+  int tt;
+  const int nxt = p.pre + 1;
+  if (nxt < p.bps) load_unit(buf1, unit_addr(p, item, nxt, &tt), type, lane);
+  unit_compute<NC, UC>(buf0, type, kbase, p.ncols, act, acc);
+  if (p.pre > 0) {
+    mbar_wait_parity(bar, 0, p.err);
+    for (int jj = 1; jj <= p.pre; ++jj)
+      unit_compute_smem<NC, UC>(staged + size_t(jj - 1) * ub_max, type, kbase + jj, p.ncols, act, acc, lane);
+  }
+  for (int j = nxt; j < p.bps; j += 2) {
+    if (j + 1 < p.bps) load_unit(buf0, unit_addr(p, item, j + 1, &tt), type, lane);
+    unit_compute<NC, UC>(buf1, type, kbase + j, p.ncols, act, acc);
+    if (j + 1 < p.bps) {
+      if (j + 2 < p.bps) load_unit(buf1, unit_addr(p, item, j + 2, &tt), type, lane);
+      unit_compute<NC, UC>(buf0, type, kbase + j + 1, p.ncols, act, acc);
+    }
+  }
+  flush(item, acc);
+}
+
 // Cooperative copy of the activation slice for blocks [kb0, kb0 + nblk) of
 // columns [col0, col0 + ncols) into shared memory (plane A then plane B).
 __device__ __forceinline__ void stage_activations(const GemvParams& p, uint8_t* dst_a, uint8_t* dst_b, int kb0,
@@ -343,6 +410,24 @@ __device__ __forceinline__ void stage_activations(const GemvParams& p, uint8_t* 
       uint4* d = reinterpret_cast<uint4*>(dst_b + size_t(c) * nblk * Q8B_REC);
       for (int i = threadIdx.x; i < nblk * Q8B_REC / 16; i += nthreads) d[i] = __ldg(s + i);
     }
+  }
+}
+
+// Thread 0 copies the CTA's activation slice (the Q8_K records of blocks
+// [kb0, kb0 + nblk) of every column, contiguous per column and plane) into
+// shared memory with bulk copies completing on `bar`, which it initializes;
+// the caller syncs the CTA before anyone waits on `bar`.  One L2 round trip
+// instead of a load/store loop.
+__device__ __forceinline__ void stage_activations_bulk(const GemvParams& p, uint8_t* dst_a, uint8_t* dst_b, int kb0,
+                                                       int nblk, uint64_t* bar) {
+  if (threadIdx.x != 0) return;
+  const uint32_t per_col = uint32_t(nblk) * uint32_t((dst_a ? Q8A_REC : 0) + (dst_b ? Q8B_REC : 0));
+  mbar_init(bar, 1);
+  mbar_expect_tx(bar, per_col * uint32_t(p.ncols));
+  for (int c = 0; c < p.ncols; ++c) {
+    const size_t rec0 = size_t(p.col0 + c) * p.nb + kb0;
+    if (dst_a) bulk_copy_g2s(dst_a + size_t(c) * nblk * Q8A_REC, p.q.a + rec0 * Q8A_REC, uint32_t(nblk * Q8A_REC), bar);
+    if (dst_b) bulk_copy_g2s(dst_b + size_t(c) * nblk * Q8B_REC, p.q.b + rec0 * Q8B_REC, uint32_t(nblk * Q8B_REC), bar);
   }
 }
 

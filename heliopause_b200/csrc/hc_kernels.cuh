@@ -28,6 +28,8 @@ struct GemvParams {
   int total_tiles;  // over all segments
   int bulk;         // 1: each CTA copies all of its units into shared memory up front
   int q4small;      // 1: every weight is Q4_K and ncols <= 2 (Q4_K-sized register buffers, 4 CTAs per SM)
+  int pre;          // streaming mode, one item per warp: units 1..pre of the item are copied into shared
+                    // memory before the wait for the previous kernel (0: only unit 0, into registers)
   int* err;         // device status word (bounded-wait timeouts)
   Q8Buf q;
 };
@@ -42,6 +44,18 @@ constexpr int GEMV_CTAS_PER_SM_Q4 = 4;  // Q4_K-only launches of <= 2 columns (s
 constexpr int GEMV_MAX_SMEM = 200 * 1024;
 constexpr int GEMV_BULK_MAX_UNITS_SMEM = 112 * 1024;  // unit bytes a bulk-mode CTA may stage
 constexpr int GEMV_SM_SMEM = 228 * 1024;              // shared memory per SM
+constexpr int GEMV_MAX_CLUSTER = 8;                   // CTAs per tile at split 32
+constexpr int GEMV_PRE_SM_SMEM = 160 * 1024;          // shared memory per SM a streaming launch may fill
+                                                      // with prefetched units (the rest serves the kernels
+                                                      // launched after it)
+
+// Static shared memory of gemv_kernel for a launch of `ncols` columns (the
+// column count rounds up to the kernel's 1/2/4/8 template): the per-warp
+// partials, rank 0's cluster gather array and the two mbarriers.
+inline size_t gemv_static_smem(int ncols) {
+  const int nc = ncols <= 1 ? 1 : ncols <= 2 ? 2 : ncols <= 4 ? 4 : 8;
+  return size_t(GEMV_WARPS_PER_CTA + GEMV_MAX_CLUSTER) * nc * 32 * 4 + 64;
+}
 
 __host__ __device__ inline int unit_bytes(int type) { return int(tile_block_bytes(type)); }
 
