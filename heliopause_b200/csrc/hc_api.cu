@@ -220,9 +220,10 @@ int hpc_quantize_q8_k(const float* d_in, size_t in_len, size_t input_size, size_
 // GEMV launches over an already-quantized workspace: one launch per group of
 // up to 8 columns, covering all segments.
 static int launch_gemv_ws(const hc::Q8Buf& q, int K, int cols, const hc::GemvSeg* segs, int nseg, int total_tiles,
-                          cudaStream_t st) {
+                          cudaStream_t st, const hc::GemvPrologue* pro = nullptr) {
   hc::GemvParams p;
   memset(&p, 0, sizeof p);
+  if (pro) p.pro = *pro;
   for (int i = 0; i < nseg; ++i) p.seg[i] = segs[i];
   p.nseg = nseg;
   p.K = K;
@@ -386,6 +387,29 @@ int hpc_matmul_q8(size_t count, const hpc_weight* handles, const void* d_workspa
   return launch_gemv_ws(q, int(input_size), int(column_count), segs, int(count), tiles,
                         static_cast<cudaStream_t>(stream));
 }
+
+}  // extern "C"
+
+// hpc_matmul_q8 whose input is computed by the fused norm prologue of every
+// CTA (hc_kernels.cuh GemvPrologue) instead of read from Q8_K records: the
+// decode step's QKV and gate/up projections for one or two columns of width
+// 2048.  `q8ws` still carries the record geometry of the launch.
+int hc_matmul_q8_prologue(size_t count, const hpc_weight* handles, const void* q8ws, size_t q8_bytes, size_t input_size,
+                          size_t column_count, float* const* d_outs, const size_t* out_lens,
+                          const hc::GemvPrologue& pro, cudaStream_t st) {
+  if (count == 0 || count > size_t(hc::GEMV_MAXSEG)) return fail(HPC_ERR_SHAPE, "matmul_q8: count %zu", count);
+  if (input_size != size_t(hc::GEMV_PRO_D) || column_count < 1 || column_count > 2)
+    return fail(HPC_ERR_SHAPE, "fused prologue: width %zu, %zu columns", input_size, column_count);
+  if (q8_bytes < hc::q8buf_bytes(int(input_size), int(column_count))) return fail(HPC_ERR_SHAPE, "workspace too small");
+  hc::GemvSeg segs[hc::GEMV_MAXSEG];
+  int tiles = 0;
+  int rc = build_segments(count, handles, d_outs, out_lens, input_size, column_count, segs, &tiles);
+  if (rc != HPC_OK) return rc;
+  hc::Q8Buf q = hc::q8buf_carve(const_cast<void*>(q8ws), int(input_size), int(column_count));
+  return launch_gemv_ws(q, int(input_size), int(column_count), segs, int(count), tiles, st, &pro);
+}
+
+extern "C" {
 
 static int lm_head_check(hpc_weight h, size_t input_size, size_t column_count, size_t k) {
   if (!valid(h)) return fail(HPC_ERR_ARG, "invalid weight handle");

@@ -109,14 +109,14 @@ __global__ void embed_kernel(const uint8_t* __restrict__ w, int type, int nb, in
 // ---- norms + quantize ----------------------------------------------------------------
 
 // One CTA of D/8 threads per column (thread t owns elements 8t..8t+7; warp w
-// owns 256-block w).  Mode RESID: h = x + rmsnorm(y, w_post) is written back
-// to x (the residual stream, layers.ts:359-363 / 471), then n = rmsnorm(h,
-// w_pre); otherwise n = rmsnorm(x, w_pre).  n is quantized to Q8_K for the
-// next matmul; if n_out != nullptr it is also stored as f32.
+// owns 256-block w).  Mode RESID: h = x + rmsnorm(y, w_post) is stored to
+// x_out (the residual stream, layers.ts:359-363 / 471; x_out may be x), then
+// n = rmsnorm(h, w_pre); otherwise n = rmsnorm(x, w_pre).  n is quantized to
+// Q8_K for the next matmul; if n_out != nullptr it is also stored as f32.
 template <bool RESID>
-__global__ void norm_quant_kernel(float* __restrict__ x, const float* __restrict__ y, const float* __restrict__ w_post,
-                                  const float* __restrict__ w_pre, double eps, int D, Q8Buf q,
-                                  float* __restrict__ n_out) {
+__global__ void norm_quant_kernel(const float* x, float* x_out, const float* __restrict__ y,
+                                  const float* __restrict__ w_post, const float* __restrict__ w_pre, double eps, int D,
+                                  Q8Buf q, float* __restrict__ n_out) {
   __shared__ double scratch[32];
   __shared__ __align__(16) uint8_t stage[32][256];
   pdl_trigger();
@@ -142,7 +142,7 @@ __global__ void norm_quant_kernel(float* __restrict__ x, const float* __restrict
       const float pn = float((double(yv[i]) * sc) * double(wp[i]));
       h[i] = h[i] + pn;
     }
-    float4* xo = reinterpret_cast<float4*>(x + size_t(m) * D + 8 * t);
+    float4* xo = reinterpret_cast<float4*>(x_out + size_t(m) * D + 8 * t);
     xo[0] = make_float4(h[0], h[1], h[2], h[3]);
     xo[1] = make_float4(h[4], h[5], h[6], h[7]);
   }
@@ -520,11 +520,13 @@ cudaError_t launch_embed(const uint8_t* w, int type, int nb, int vocab, const in
   return pdl_launch(embed_kernel, dim3(M), dim3(256), 0, st, w, type, nb, vocab, ids, hidden, D, scale, err);
 }
 
-cudaError_t launch_norm_quant(bool resid, float* x, const float* y, const float* w_post, const float* w_pre, double eps,
-                              int M, int D, const Q8Buf& q, float* n_out, cudaStream_t st) {
+cudaError_t launch_norm_quant(bool resid, const float* x, float* x_out, const float* y, const float* w_post,
+                              const float* w_pre, double eps, int M, int D, const Q8Buf& q, float* n_out,
+                              cudaStream_t st) {
   const dim3 grid(M), block(D / 8);
-  if (resid) return pdl_launch(norm_quant_kernel<true>, grid, block, 0, st, x, y, w_post, w_pre, eps, D, q, n_out);
-  return pdl_launch(norm_quant_kernel<false>, grid, block, 0, st, x, y, w_post, w_pre, eps, D, q, n_out);
+  if (resid)
+    return pdl_launch(norm_quant_kernel<true>, grid, block, 0, st, x, x_out, y, w_post, w_pre, eps, D, q, n_out);
+  return pdl_launch(norm_quant_kernel<false>, grid, block, 0, st, x, x_out, y, w_post, w_pre, eps, D, q, n_out);
 }
 
 size_t attn_smem_bytes(int M, int H, int KVH) {

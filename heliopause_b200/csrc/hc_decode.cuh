@@ -11,8 +11,9 @@ cudaError_t launch_rope_table(const int32_t* pos, int M, int half, double theta_
                               cudaStream_t st);
 cudaError_t launch_embed(const uint8_t* w, int type, int nb, int vocab, const int32_t* ids, float* hidden, int M, int D,
                          double scale, int* err, cudaStream_t st);
-cudaError_t launch_norm_quant(bool resid, float* x, const float* y, const float* w_post, const float* w_pre, double eps,
-                              int M, int D, const Q8Buf& q, float* n_out, cudaStream_t st);
+cudaError_t launch_norm_quant(bool resid, const float* x, float* x_out, const float* y, const float* w_post,
+                              const float* w_pre, double eps, int M, int D, const Q8Buf& q, float* n_out,
+                              cudaStream_t st);
 size_t attn_smem_bytes(int M, int H, int KVH);
 // Attention over the raw q (and, in an own-KV layer, raw k/v) projections of
 // M tokens: QK-norm + RoPE of the queries and of this step's K/V rows (written

@@ -31,8 +31,10 @@
 
 #include "hc_common.cuh"
 #include "hc_bulk.cuh"
+#include "hc_decmath.cuh"
 #include "hc_gemv_body.cuh"
 #include "hc_kernels.cuh"
+#include "hc_q8.cuh"
 
 namespace cg = cooperative_groups;
 
@@ -69,6 +71,85 @@ __device__ __forceinline__ void store_tile(const GemvParams& p, int tile, const 
     for (int c = 0; c < NC; ++c)
       if (c < p.ncols) sg.out[size_t(p.col0 + c) * sg.rows + row] = v[c];
   }
+}
+
+// The fused prologue (after the wait): for every column, h = x [+
+// rmsnorm(y) * w_post] (f64 sums and products rounded to f32 as
+// norm_quant_kernel / layers.ts:824-885), n = rmsnorm(h) * w_pre, and the
+// blocks of the CTA's slice [kb0, kb0 + nblk) -- each held whole by one warp
+// -- quantized to Q8_K into the shared-memory records.  CTA 0 stores h.
+__device__ __forceinline__ void gemv_prologue(const GemvParams& p, uint8_t* act_a, uint8_t* act_b, int kb0, int nblk,
+                                              int warp, int lane) {
+  __shared__ double scratch[GEMV_WARPS_PER_CTA];
+  __shared__ __align__(16) uint8_t stage[GEMV_WARPS_PER_CTA][256];
+  constexpr int D = GEMV_PRO_D;
+  const bool resid = p.pro.mode == GEMV_PRO_RESID_NORM;
+  // Thread (warp w, lane L) owns elements 8L..8L+7 of 256-blocks w and w + 4.
+  // Loads are issued as late as their use allows without a dependent round
+  // trip (w_pre goes out before the last reduction), which keeps the live
+  // registers low next to the main loop's unit buffer.
+  const int e0 = warp * 256 + 8 * lane, e1 = (warp + 4) * 256 + 8 * lane;
+  for (int c = 0; c < p.ncols; ++c) {
+    const size_t col = size_t(p.col0 + c) * D;
+    float h[16];
+    load8(p.pro.x + col + e0, *reinterpret_cast<float(*)[8]>(&h[0]));
+    load8(p.pro.x + col + e1, *reinterpret_cast<float(*)[8]>(&h[8]));
+    if (resid) {
+      float y[16], wpost[16];
+      load8(p.pro.y + col + e0, *reinterpret_cast<float(*)[8]>(&y[0]));
+      load8(p.pro.y + col + e1, *reinterpret_cast<float(*)[8]>(&y[8]));
+      load8(p.pro.w_post + e0, *reinterpret_cast<float(*)[8]>(&wpost[0]));
+      load8(p.pro.w_post + e1, *reinterpret_cast<float(*)[8]>(&wpost[8]));
+      double ss = 0.0;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) ss += double(y[i]) * double(y[i]);
+      ss = block_sum_d(ss, scratch, GEMV_WARPS_PER_CTA);
+      const double sc = 1.0 / sqrt(ss / double(D) + p.pro.eps);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) h[i] = h[i] + float((double(y[i]) * sc) * double(wpost[i]));
+      if (blockIdx.x == 0) {
+        float* xo = p.pro.x_out + col;
+        reinterpret_cast<float4*>(xo + e0)[0] = make_float4(h[0], h[1], h[2], h[3]);
+        reinterpret_cast<float4*>(xo + e0)[1] = make_float4(h[4], h[5], h[6], h[7]);
+        reinterpret_cast<float4*>(xo + e1)[0] = make_float4(h[8], h[9], h[10], h[11]);
+        reinterpret_cast<float4*>(xo + e1)[1] = make_float4(h[12], h[13], h[14], h[15]);
+      }
+    }
+    float wpre[16];
+    load8(p.pro.w_pre + e0, *reinterpret_cast<float(*)[8]>(&wpre[0]));
+    load8(p.pro.w_pre + e1, *reinterpret_cast<float(*)[8]>(&wpre[8]));
+    double ss = 0.0;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) ss += double(h[i]) * double(h[i]);
+    ss = block_sum_d(ss, scratch, GEMV_WARPS_PER_CTA);
+    const double sc = 1.0 / sqrt(ss / double(D) + p.pro.eps);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) h[i] = float((double(h[i]) * sc) * double(wpre[i]));
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int b = warp + 4 * k;
+      if (b >= kb0 && b < kb0 + nblk) {
+        const size_t r = size_t(c) * nblk + (b - kb0);
+        q8k_block_warp(*reinterpret_cast<const float(*)[8]>(&h[8 * k]), lane, stage[warp], act_a + r * Q8A_REC,
+                       act_b + r * Q8B_REC);
+      }
+    }
+  }
+}
+
+// Stages the activation slice: bulk copies of the Q8_K records written by the
+// previous kernel, or the fused prologue.  Every thread calls it after the
+// wait; on return the slice is complete for the whole CTA.
+__device__ __forceinline__ void gemv_inputs(const GemvParams& p, uint8_t* act_a, uint8_t* act_b, int kb0, int nblk,
+                                            uint64_t* act_bar, int warp, int lane) {
+  if (p.pro.mode != GEMV_PRO_NONE) {
+    gemv_prologue(p, act_a, act_b, kb0, nblk, warp, lane);
+    __syncthreads();
+    return;
+  }
+  stage_activations_bulk(p, act_a, act_b, kb0, nblk, act_bar);
+  __syncthreads();
+  mbar_wait_parity(act_bar, 0, p.err);
 }
 
 // UC: register-buffer chunks per unit (Q6K_CHUNKS, or Q4K_CHUNKS for Q4_K-only
@@ -139,9 +220,8 @@ __global__ void __launch_bounds__(GEMV_THREADS, UC == Q4K_CHUNKS ? GEMV_CTAS_PER
 #if __CUDA_ARCH__ >= 900
     asm volatile("griddepcontrol.wait;" ::: "memory");
 #endif
-    stage_activations_bulk(p, act_a, act_b, kb0, nblk, &act_bar);
-    __syncthreads();
-    const bool ok = mbar_wait_parity(&bar, 0, p.err) & mbar_wait_parity(&act_bar, 0, p.err);
+    gemv_inputs(p, act_a, act_b, kb0, nblk, &act_bar, warp, lane);
+    const bool ok = mbar_wait_parity(&bar, 0, p.err);
     if (item0 < nitems) {
       float acc[NC];
 #pragma unroll
@@ -180,9 +260,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, UC == Q4K_CHUNKS ? GEMV_CTAS_PER
 #if __CUDA_ARCH__ >= 900
     asm volatile("griddepcontrol.wait;" ::: "memory");
 #endif
-    stage_activations_bulk(p, act_a, act_b, kb0, nblk, &act_bar);
-    __syncthreads();
-    mbar_wait_parity(&act_bar, 0, p.err);
+    gemv_inputs(p, act_a, act_b, kb0, nblk, &act_bar, warp, lane);
     if (p.pre > 0) {
       if (item0 < nitems)
         prefetched_item<NC, UC>(p, act, item0, lane, buf[0], first_type, staged, ub_max, &pre_bar[warp], flush);
@@ -276,7 +354,8 @@ void gemv_plan(GemvParams& p) {
     if (p.seg[i].type != TYPE_Q4_K) p.q4small = 0;
   const int cap_warps = sm_count() * ctas_per_sm(p) * GEMV_WARPS_PER_CTA;
   int s = 1, lg = 0;
-  while (s < 32 && p.nb % (s * 2) == 0 && p.total_tiles * s * 2 <= cap_warps) {
+  const int smax = p.pro.mode != GEMV_PRO_NONE ? 8 : 32;  // a prologue slice is >= 4 aligned blocks
+  while (s < smax && p.nb % (s * 2) == 0 && p.total_tiles * s * 2 <= cap_warps) {
     s *= 2;
     ++lg;
   }

@@ -433,6 +433,10 @@ __device__ __forceinline__ void stage_activations_bulk(const GemvParams& p, uint
 
 __host__ __device__ inline void gemv_planes(const GemvParams& p, bool* need_a, bool* need_b) {
   *need_a = *need_b = false;
+  if (p.pro.mode != GEMV_PRO_NONE) {  // the prologue's quantizer writes both planes
+    *need_a = *need_b = true;
+    return;
+  }
   for (int i = 0; i < p.nseg; ++i) {
     if (p.seg[i].type == TYPE_Q4_K) *need_a = true;
     else *need_b = true;

@@ -32,3 +32,11 @@ int hpc_cuda_fail(cudaError_t e, const char* what);
     cudaError_t e_ = (call);                                \
     if (e_ != cudaSuccess) return hpc_cuda_fail(e_, what);  \
   } while (0)
+
+namespace hc {
+struct GemvPrologue;
+}
+// hpc_matmul_q8 with the fused norm prologue (hc_api.cu).
+int hc_matmul_q8_prologue(size_t count, const hpc_weight* handles, const void* q8ws, size_t q8_bytes, size_t input_size,
+                          size_t column_count, float* const* d_outs, const size_t* out_lens,
+                          const hc::GemvPrologue& pro, cudaStream_t st);

@@ -17,6 +17,23 @@ struct GemvSeg {
   int pad;
 };
 
+// Fused input of a matmul whose input is an RMSNorm of the residual stream
+// (the per-layer norm_quant_kernel folded into the GEMV): every CTA computes
+// the norm of the whole D = 2048 vector itself and quantizes the 256-blocks
+// of its K slice straight into its shared-memory activation records.
+enum { GEMV_PRO_NONE = 0, GEMV_PRO_NORM = 1, GEMV_PRO_RESID_NORM = 2 };
+struct GemvPrologue {
+  int mode;
+  int pad_;
+  const float* x;       // residual stream [col][2048]
+  const float* y;       // RESID_NORM: projection output added after its own norm [col][2048]
+  const float* w_post;  // RESID_NORM: that norm's weight
+  const float* w_pre;   // weight of the norm of this matmul's input
+  float* x_out;         // RESID_NORM: CTA 0 stores x + rmsnorm(y) * w_post here (not x: other CTAs read x)
+  double eps;
+};
+constexpr int GEMV_PRO_D = 2048;
+
 struct GemvParams {
   GemvSeg seg[GEMV_MAXSEG];
   int nseg;
@@ -32,6 +49,7 @@ struct GemvParams {
                     // memory before the wait for the previous kernel (0: only unit 0, into registers)
   int* err;         // device status word (bounded-wait timeouts)
   Q8Buf q;
+  GemvPrologue pro; // mode != NONE: activations computed by every CTA instead of read from q
 };
 
 // Device status word of the current device (hc_api.cu).
@@ -54,7 +72,7 @@ constexpr int GEMV_PRE_SM_SMEM = 160 * 1024;          // shared memory per SM a 
 // partials, rank 0's cluster gather array and the two mbarriers.
 inline size_t gemv_static_smem(int ncols) {
   const int nc = ncols <= 1 ? 1 : ncols <= 2 ? 2 : ncols <= 4 ? 4 : 8;
-  return size_t(GEMV_WARPS_PER_CTA + GEMV_MAX_CLUSTER) * nc * 32 * 4 + 64;
+  return size_t(GEMV_WARPS_PER_CTA + GEMV_MAX_CLUSTER) * nc * 32 * 4 + GEMV_WARPS_PER_CTA * 256 + 128;
 }
 
 __host__ __device__ inline int unit_bytes(int type) { return int(tile_block_bytes(type)); }

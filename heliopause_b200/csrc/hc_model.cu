@@ -52,7 +52,7 @@ struct hpc_model_s {
   // workspaces (sized for cfg.max_tokens columns)
   void* arena = nullptr;
   size_t arena_bytes = 0;
-  float *x = nullptr, *qb = nullptr, *kb = nullptr, *vb = nullptr, *o = nullptr, *g = nullptr,
+  float *x = nullptr, *h1 = nullptr, *qb = nullptr, *kb = nullptr, *vb = nullptr, *o = nullptr, *g = nullptr,
         *u = nullptr, *f = nullptr;
   float *pm = nullptr, *pl = nullptr, *po = nullptr;
   double *cos_t = nullptr, *sin_t = nullptr;
@@ -140,6 +140,7 @@ int hpc_model_create(const hpc_model_config* cfg, hpc_model* out) {
   };
   std::vector<Piece> pieces = {
       {(void**)&m->x, sizeof(float) * M * D},
+      {(void**)&m->h1, sizeof(float) * M * D},
       {(void**)&m->qb, sizeof(float) * M * H * HD},
       {(void**)&m->kb, sizeof(float) * M * KVH * HD},
       {(void**)&m->vb, sizeof(float) * M * KVH * HD},
@@ -443,27 +444,68 @@ static int enqueue_step(hpc_model m, int M, int k, cudaStream_t st) {
     if (m->persist_state == 1) {
       HPC_CK(cudaMemsetAsync(m->pparams.counters, 0, m->persist_ctr_bytes, st), "counter reset");
       HPC_CK(hc::launch_persistent_step(m->pparams, m->persist_grid, st), "persistent step launch");
-      HPC_CK(hc::launch_norm_quant(false, m->x, nullptr, nullptr, m->output_norm, eps, M, D, qd, nullptr, st),
+      HPC_CK(hc::launch_norm_quant(false, m->x, m->x, nullptr, nullptr, m->output_norm, eps, M, D, qd, nullptr, st),
              "output norm");
       return hpc_lm_head_topk_q8(emb, m->q8d, m->q8d_bytes, size_t(D), size_t(M), size_t(k), 0, m->cand,
                                  m->cand_bytes, c.final_logit_softcap, m->out_ids, m->out_vals, nullptr, st);
     }
   }
+  // One or two columns of width 2048: the RMSNorms (+ residual adds) that feed
+  // the QKV and gate/up projections are folded into those GEMVs (every CTA
+  // computes them, hc_gemv.cu gemv_prologue).  The residual stream then
+  // alternates between X (x_l, stored by the QKV prologue) and H1 (the
+  // post-attention residual, stored by the gate/up prologue), so no CTA
+  // overwrites a vector other CTAs of the same launch still read.
+  const bool fused = M <= 2 && D == hc::GEMV_PRO_D;
+  float* const X = m->x;
+  float* const H1 = fused ? m->h1 : m->x;
+  auto mm_pro = [&](std::initializer_list<std::pair<hpc_weight, float*>> ws, const hc::GemvPrologue& pro) -> int {
+    hpc_weight hs[8];
+    float* outs[8];
+    size_t lens[8];
+    int n = 0;
+    for (auto& p : ws) {
+      hs[n] = p.first;
+      outs[n] = p.second;
+      lens[n] = p.first->row_count * size_t(M);
+      ++n;
+    }
+    return hc_matmul_q8_prologue(size_t(n), hs, m->q8d, m->q8d_bytes, size_t(D), size_t(M), outs, lens, pro, st);
+  };
   for (int l = 0; l < c.layers; ++l) {
     Layer& L = m->layers[l];
     const bool own_kv = l < c.kv_layers;
     const int kvl = m->kv_source[l];
-    // attention norm (+ the previous layer's post-FFN residual)
-    if (l == 0) {
-      HPC_CK(hc::launch_norm_quant(false, m->x, nullptr, nullptr, L.norm[HPC_N_ATTN], eps, M, D, qd, nullptr, st),
-             "attn norm");
+    int rc;
+    // attention norm (+ the previous layer's post-FFN residual) and QKV
+    if (fused) {
+      hc::GemvPrologue pro{};
+      pro.eps = eps;
+      pro.w_pre = L.norm[HPC_N_ATTN];
+      if (l == 0) {
+        pro.mode = hc::GEMV_PRO_NORM;
+        pro.x = X;
+      } else {
+        pro.mode = hc::GEMV_PRO_RESID_NORM;
+        pro.x = H1;
+        pro.y = m->f;
+        pro.w_post = m->layers[l - 1].norm[HPC_N_POST_FFW];
+        pro.x_out = X;
+      }
+      rc = own_kv ? mm_pro({{L.w[HPC_W_Q], m->qb}, {L.w[HPC_W_K], m->kb}, {L.w[HPC_W_V], m->vb}}, pro)
+                  : mm_pro({{L.w[HPC_W_Q], m->qb}}, pro);
     } else {
-      HPC_CK(hc::launch_norm_quant(true, m->x, m->f, m->layers[l - 1].norm[HPC_N_POST_FFW], L.norm[HPC_N_ATTN], eps, M,
-                                   D, qd, nullptr, st),
-             "post-ffn residual + attn norm");
+      if (l == 0) {
+        HPC_CK(hc::launch_norm_quant(false, X, X, nullptr, nullptr, L.norm[HPC_N_ATTN], eps, M, D, qd, nullptr, st),
+               "attn norm");
+      } else {
+        HPC_CK(hc::launch_norm_quant(true, X, X, m->f, m->layers[l - 1].norm[HPC_N_POST_FFW], L.norm[HPC_N_ATTN], eps,
+                                     M, D, qd, nullptr, st),
+               "post-ffn residual + attn norm");
+      }
+      rc = own_kv ? mm({{L.w[HPC_W_Q], m->qb}, {L.w[HPC_W_K], m->kb}, {L.w[HPC_W_V], m->vb}}, m->q8d, m->q8d_bytes, D)
+                  : mm({{L.w[HPC_W_Q], m->qb}}, m->q8d, m->q8d_bytes, D);
     }
-    int rc = own_kv ? mm({{L.w[HPC_W_Q], m->qb}, {L.w[HPC_W_K], m->kb}, {L.w[HPC_W_V], m->vb}}, m->q8d, m->q8d_bytes, D)
-                    : mm({{L.w[HPC_W_Q], m->qb}}, m->q8d, m->q8d_bytes, D);
     if (rc != HPC_OK) return rc;
     HPC_CK(hc::launch_attention(m->qb, m->kb, m->vb, L.norm[HPC_N_Q], L.norm[HPC_N_K], m->cos_t, m->sin_t, eps, own_kv,
                                 m->kc[kvl], m->vc[kvl], m->pos, M, H, KVH, c.context, 1.0f, m->pm, m->pl, m->po,
@@ -473,18 +515,31 @@ static int enqueue_step(hpc_model m, int M, int k, cudaStream_t st) {
            "attention combine");
     rc = mm({{L.w[HPC_W_O], m->o}}, m->q8d, m->q8d_bytes, size_t(H) * HD);
     if (rc != HPC_OK) return rc;
-    HPC_CK(hc::launch_norm_quant(true, m->x, m->o, L.norm[HPC_N_POST_ATTN], L.norm[HPC_N_FFN], eps, M, D, qd, nullptr,
-                                 st),
-           "post-attn residual + ffn norm");
-    rc = mm({{L.w[HPC_W_GATE], m->g}, {L.w[HPC_W_UP], m->u}}, m->q8d, m->q8d_bytes, D);
+    // post-attention residual + FFN norm and gate/up
+    if (fused) {
+      hc::GemvPrologue pro{};
+      pro.mode = hc::GEMV_PRO_RESID_NORM;
+      pro.eps = eps;
+      pro.x = X;
+      pro.y = m->o;
+      pro.w_post = L.norm[HPC_N_POST_ATTN];
+      pro.w_pre = L.norm[HPC_N_FFN];
+      pro.x_out = H1;
+      rc = mm_pro({{L.w[HPC_W_GATE], m->g}, {L.w[HPC_W_UP], m->u}}, pro);
+    } else {
+      HPC_CK(hc::launch_norm_quant(true, X, X, m->o, L.norm[HPC_N_POST_ATTN], L.norm[HPC_N_FFN], eps, M, D, qd,
+                                   nullptr, st),
+             "post-attn residual + ffn norm");
+      rc = mm({{L.w[HPC_W_GATE], m->g}, {L.w[HPC_W_UP], m->u}}, m->q8d, m->q8d_bytes, D);
+    }
     if (rc != HPC_OK) return rc;
     HPC_CK(hc::launch_geglu_quant(m->g, m->u, M, F, qf, nullptr, st), "geglu");
     rc = mm({{L.w[HPC_W_DOWN], m->f}}, m->q8f, m->q8f_bytes, F);
     if (rc != HPC_OK) return rc;
   }
   // final post-FFN residual + output norm, then the LM head
-  HPC_CK(hc::launch_norm_quant(true, m->x, m->f, m->layers[c.layers - 1].norm[HPC_N_POST_FFW], m->output_norm, eps, M,
-                               D, qd, nullptr, st),
+  HPC_CK(hc::launch_norm_quant(true, H1, X, m->f, m->layers[c.layers - 1].norm[HPC_N_POST_FFW], m->output_norm, eps,
+                               M, D, qd, nullptr, st),
          "post-ffn residual + output norm");
   return hpc_lm_head_topk_q8(emb, m->q8d, m->q8d_bytes, size_t(D), size_t(M), size_t(k), 0, m->cand, m->cand_bytes,
                              c.final_logit_softcap, m->out_ids, m->out_vals, nullptr, st);
