@@ -288,7 +288,10 @@ class DecodeConfig3:
 
     def kernel_launch_count(self) -> int:
         s = self.shape
-        per_layer = 9  # norm, QKV, qk-norm/rope/kv + attention, combine, O, norm, gate/up, geglu, down
+        # M = 1, hidden 2048: the attention and FFN norms run inside the QKV
+        # and gate/up GEMVs (hc_model.cu enqueue_step): QKV, attention (with
+        # QK-norm/RoPE/KV write), combine, O, gate/up, GEGLU, down
+        per_layer = 7
         return 2 + s.layers * per_layer + 1 + 2  # rope table + embed ... final norm + LM head + merge
 
     def roofline(self, peak_gbs: float) -> dict:
