@@ -46,36 +46,24 @@ __device__ __forceinline__ float round_f16_ts(float x) {
 // query, lib.rs:590-597): the dropped bits round half UP, overflow clamps to
 // 0x7bff, NaN -> 0x7e00.  Returns the f16 value widened back to f32.
 __device__ __forceinline__ float round_f16_rust(float v) {
-  const uint32_t bits = __float_as_uint(v);
-  const uint32_t sign = (bits >> 16) & 0x8000u;
-  const int exp = int((bits >> 23) & 0xff);
-  const uint32_t mant = bits & 0x7fffffu;
-  uint32_t h;
-  if (exp == 0xff) {
-    h = mant == 0 ? (sign | 0x7c00u) : 0x7e00u;
-  } else {
-    const int he = exp - 127 + 15;
-    if (he >= 31) {
-      h = sign | 0x7bffu;
-    } else if (he <= 0) {
-      if (he < -10) {
-        h = sign;
-      } else {
-        const uint32_t m = mant | 0x800000u;
-        const uint32_t shift = uint32_t(14 - he);
-        h = sign | ((m + (1u << (shift - 1))) >> shift);
-      }
-    } else {
-      const uint32_t rm = mant + 0x1000u;
-      if (rm & 0x800000u) {
-        const int re = he + 1;
-        h = re >= 31 ? (sign | 0x7bffu) : (sign | uint32_t(re << 10));
-      } else {
-        h = sign | uint32_t(he << 10) | (rm >> 13);
-      }
-    }
-  }
-  return f16_bits_to_f32(h);
+  // Branch-free on the f32 bits (one result per case, then a select):
+  //   f16 normal range: add half an f16 ulp (bit 12) and clear the 13 bits
+  //     f16 drops -- a carry moves into the exponent as the codec's does --
+  //     then clamp anything that reached 2^16 to 65504 (0x7bff);
+  //   f16 subnormal range (f32 exponents 102..112): round the 24-bit
+  //     significand half up at 2^-24, scaled back exactly;
+  //   below: signed zero; Inf keeps its sign; NaN becomes 0x7e00.
+  const uint32_t bits = __float_as_uint(v), sign = bits & 0x80000000u, a = bits & 0x7fffffffu;
+  const int exp = int(a >> 23);
+  uint32_t rn = (a + 0x1000u) & 0xffffe000u;
+  rn = rn >= 0x47800000u ? 0x477fe000u : rn;
+  const int shift = min(max(126 - exp, 1), 31);
+  const uint32_t m = (a & 0x7fffffu) | 0x800000u;
+  const uint32_t hs = (m + (1u << (shift - 1))) >> shift;
+  const uint32_t fs = __float_as_uint(float(hs) * 5.9604644775390625e-8f);
+  const uint32_t r = exp >= 113 ? rn : (exp >= 102 ? fs : 0u);
+  if (exp == 255) return (a & 0x7fffffu) ? __uint_as_float(0x7fc00000u) : __uint_as_float(sign | 0x7f800000u);
+  return __uint_as_float(sign | r);
 }
 
 // ---- block reductions -----------------------------------------------------------

@@ -271,12 +271,18 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_partial_kernel(
   // have landed.
   {
     constexpr int PIECES = HD * 4 / 16;  // 16-byte pieces per row
-    for (int i = threadIdx.x; i < CH * PIECES; i += blockDim.x) {
-      const int t = i / PIECES, c = i % PIECES;
-      const size_t row = (size_t(t0 + t) * KVH + kvh) * HD + 4 * c;
-      cp_async16(ks + t * ATT_KSTRIDE + 4 * c, kc + row);
-      cp_async16(vs + t * ATT_KSTRIDE + 4 * c, vc + row);
-    }
+    // when there are fewer query vectors than warps, the warps that prepare
+    // the queries issue no copies: their q loads after the wait then do not
+    // queue behind this slice's copies
+    const int nw = int(blockDim.x >> 5), nq = M * (H / KVH), cw0 = nq < nw ? nq : 0;
+    const int ncp = (nw - cw0) * 32;
+    if (int(threadIdx.x >> 5) >= cw0)
+      for (int i = int(threadIdx.x) - cw0 * 32; i < CH * PIECES; i += ncp) {
+        const int t = i / PIECES, c = i % PIECES;
+        const size_t row = (size_t(t0 + t) * KVH + kvh) * HD + 4 * c;
+        cp_async16(ks + t * ATT_KSTRIDE + 4 * c, kc + row);
+        cp_async16(vs + t * ATT_KSTRIDE + 4 * c, vc + row);
+      }
     cp_async_commit();
   }
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, warps = blockDim.x >> 5;
