@@ -650,8 +650,130 @@ class LmHeadConfig5:
         return None
 
 
+class PrefillConfig5:
+    """BASELINE config 5 prefill: 512 tokens of N(0,1) hidden through the
+    config-3 stack (hpc_model_prefill): tensor-core (mma.sync s8) matmuls at
+    M = 512 and causal attention over the prompt."""
+    name = "prefill-config5"
+    unit = "tok/s"
+    dtype = "u8/int32 (Q4_K/Q6_K x Q8_K, s8 tensor-core mma), f32 decoder math"
+    N = 512
+
+    def __init__(self):
+        import torch
+
+        from heliopause_b200 import synthetic as syn
+        from heliopause_b200.model import CONFIG3, W_GATE, W_UP, CudaDecoderModel
+        self.torch, self.syn, self.shape = torch, syn, CONFIG3
+        self.model = CudaDecoderModel(CONFIG3, max_tokens=8, top_k=64)
+        self.model.load_gpu_synthetic(seed=1)
+        g = torch.Generator(device="cuda")
+        g.manual_seed(5)
+        self.x = torch.randn(self.N, CONFIG3.hidden, device="cuda", generator=g)
+        self.W_GATE, self.W_UP = W_GATE, W_UP
+        s = CONFIG3
+        wcount = 0
+        for layer in range(s.layers):
+            for slot in s.slots(layer):
+                k, r = s.weight_shape(slot)
+                wcount += k * r
+        # matmul MACs + causal attention (QK and PV over on average N/2 keys)
+        self.flops = 2.0 * self.N * wcount + 2.0 * 2 * s.layers * s.heads * s.head_dim * self.N * (self.N + 1) / 2
+        self.model.prefill(self.x, 0)
+        torch.cuda.synchronize()
+
+    def step(self, ev=None):
+        self.model.prefill(self.x, 0)
+
+    def e2e_step(self, host_x):
+        self.model.prefill(host_x, 0).cpu()
+
+    def host_input(self):
+        x = self.syn.rng(5).standard_normal((self.N, self.shape.hidden)).astype("float32")
+        return x, x.nbytes, x.nbytes
+
+    def units_per_step(self) -> float:
+        return float(self.N)
+
+    def kernel_launch_count(self) -> int:
+        s = self.shape
+        own, shared = s.kv_layers, s.layers - s.kv_layers
+        # norm, Q/K/V, qk-post, attention, O, norm, gate, up, geglu, down (shared-KV layers: Q only)
+        return 1 + own * 12 + shared * 10 + 1
+
+    def roofline(self, peak_gbs: float) -> dict:
+        """Dominant kernel: the gate/up matmul at M = 512 (34% of the FLOPs),
+        35 launches (one per layer's weights) back to back in a graph."""
+        import ctypes as C
+
+        from heliopause_b200 import _lib
+        from heliopause_b200 import kernels as hk
+        torch, s = self.torch, self.shape
+        L = _lib.lib()
+        nbytes = C.c_size_t()
+        L.hpc_q8_workspace_bytes(s.hidden, self.N, C.byref(nbytes))
+        ws = torch.zeros(nbytes.value, dtype=torch.uint8, device="cuda")
+        st = lambda: C.c_void_p(torch.cuda.current_stream().cuda_stream)
+        hk.assert_cuda_ok(L.hpc_q8_quantize(C.c_void_p(self.x.data_ptr()), self.x.numel(), s.hidden, self.N,
+                                            C.c_void_p(ws.data_ptr()), nbytes.value, st()), "q8")
+        g = torch.empty(self.N * s.ffn, device="cuda")
+        u = torch.empty(self.N * s.ffn, device="cuda")
+        launches = []
+        for layer in range(s.layers):
+            hg = self.model.weight_handles[(layer, self.W_GATE)]
+            hu = self.model.weight_handles[(layer, self.W_UP)]
+
+            def f(hg=hg, hu=hu):
+                hs = (C.c_void_p * 2)(hg.handle, hu.handle)
+                outs = (C.c_void_p * 2)(g.data_ptr(), u.data_ptr())
+                lens = (C.c_size_t * 2)(self.N * s.ffn, self.N * s.ffn)
+                hk.assert_cuda_ok(L.hpc_matmul_q8(2, hs, C.c_void_p(ws.data_ptr()), nbytes.value, s.hidden, self.N,
+                                                  outs, lens, st()), "gemm")
+            launches.append(f)
+        ms = graph_launch_times(launches)
+        flops = 2.0 * self.N * s.hidden * 2 * s.ffn
+        achieved = flops / (ms / 1e3) / 1e12
+        peaks = _peaks()
+        peak = peaks.get("bf16_tflops") or 1590.0
+        return {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                "traffic": None, "kernel": "gemm_tc_kernel<Q4_K> x2 (ffn gate+up, 2048 -> 2x16384, M=512)",
+                "peak_note": "measured dense bf16 cuBLAS peak; the kernel computes s8 x s8 -> s32 on mma.sync",
+                "flops_per_launch": flops, "launch_ms": ms}
+
+    def config(self) -> dict:
+        s = self.shape
+        return {"workload": "prefill 512 tokens through the config-3 stack (BASELINE config 5)", "tokens": self.N,
+                "layers": s.layers, "hidden": s.hidden, "ffn": s.ffn, "positions": "0..511",
+                "flops_per_step": self.flops, "l2": "2.3 GB of weights per step, larger than L2"}
+
+    def cpu_baseline(self, budget_s: float, threads: int) -> dict:
+        """The oracle's layer (C restatement) for 8 tokens of one config-3
+        layer, scaled to 35 layers."""
+        import numpy as np
+
+        from heliopause_b200.model import SyntheticWeights
+        from oracle.decoder_oracle import OracleDecoder
+        s = self.shape
+        ref = OracleDecoder(s, SyntheticWeights(s, 1), threads=threads)
+        ref.set_kv(0, np.zeros((s.context, s.kv_heads, s.head_dim), np.float32),
+                   np.zeros((s.head_dim, s.kv_heads, s.context), np.float32))
+        x = self.syn.rng(5).standard_normal((8, s.hidden)).astype(np.float32).reshape(-1)
+        ref.layer(0, x, list(range(8)))  # warm the prepared-scale cache
+        t0 = time.perf_counter()
+        runs = 0
+        while True:
+            ref.layer(0, x, list(range(8)))
+            runs += 1
+            if time.perf_counter() - t0 >= budget_s:
+                break
+        per_layer = (time.perf_counter() - t0) / runs
+        return {"value": 8.0 / (per_layer * s.layers), "unit": "tok/s", "cores": threads, "kind": "port",
+                "sample": f"{runs} x one config-3 layer over 8 prompt tokens ({per_layer:.2f} s each) on {threads} "
+                          f"threads, scaled to {s.layers} layers"}
+
+
 WORKLOADS = {"decode-config3": DecodeConfig3, "gemv-config1": GemvConfig1, "gemv-config2": GemvConfig2,
-             "lmhead-config5": LmHeadConfig5}
+             "lmhead-config5": LmHeadConfig5, "prefill-config5": PrefillConfig5}
 
 
 # ------------------------------------------------------------------- main ---

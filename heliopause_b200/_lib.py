@@ -50,6 +50,7 @@ SIGNATURES = {
     "hpc_model_set_lm_head": (_i, [_vp, _vp]),
     "hpc_model_kv": (_i, [_vp, _i, C.POINTER(_vp), C.POINTER(_vp)]),
     "hpc_model_forward": (_i, [_vp, _vp, _vp, _sz, _sz, _vp, _vp, _vp, _vp]),
+    "hpc_model_prefill": (_i, [_vp, _vp, _vp, _sz, _vp, _vp]),
 }
 
 

@@ -230,6 +230,10 @@ static int launch_gemv_ws(const hc::Q8Buf& q, int K, int cols, const hc::GemvSeg
   p.nb = K / 256;
   p.total_tiles = total_tiles;
   p.q = q;
+  if (cols >= hc::TC_MIN_COLS && !pro) {
+    for (int i = 0; i < nseg; ++i) HPC_CK(hc::launch_gemm_tc(segs[i], K / 256, q, 0, cols, st), "tensor-core matmul");
+    return HPC_OK;
+  }
   for (int c0 = 0; c0 < cols; c0 += 8) {
     p.col0 = c0;
     p.ncols = cols - c0 < 8 ? cols - c0 : 8;
@@ -423,7 +427,15 @@ static int lm_head_check(hpc_weight h, size_t input_size, size_t column_count, s
   return HPC_OK;
 }
 
+// Inputs of >= TC_MIN_COLS columns take the tensor-core path: the logits
+// [col][rows] (256-byte aligned) followed by one candidate list per
+// LOGITS_CHUNK_ROWS-row chunk per column.  Narrower inputs: one list per CTA
+// of the fused GEMV + top-k kernel.
+static size_t tc_chunks(hpc_weight h) { return (h->row_count + hc::LOGITS_CHUNK_ROWS - 1) / hc::LOGITS_CHUNK_ROWS; }
+static size_t tc_logits_bytes(hpc_weight h, size_t cols) { return (cols * h->row_count * sizeof(float) + 255) / 256 * 256; }
+
 static size_t cand_bytes_for(hpc_weight h, size_t cols, size_t k) {
+  if (cols >= size_t(hc::TC_MIN_COLS)) return tc_logits_bytes(h, cols) + tc_chunks(h) * k * cols * sizeof(uint64_t);
   const int tiles = int(h->rows_pad / hc::TILE);
   return size_t(hc::lmhead_grid(tiles)) * hc::LMHEAD_LISTS * k * cols * sizeof(uint64_t);
 }
@@ -449,6 +461,27 @@ int hpc_lm_head_topk_q8(hpc_weight h, const void* d_workspace, size_t workspace_
     return fail(HPC_ERR_SHAPE, "candidate buffer too small: %zu bytes", candidates_bytes);
   if (id_offset < 0 || size_t(id_offset) + h->row_count > size_t(INT32_MAX)) return fail(HPC_ERR_SHAPE, "id offset");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (column_count >= size_t(hc::TC_MIN_COLS)) {
+    // tensor-core logits, chunked candidate lists, then the same merge
+    float* logits = static_cast<float*>(d_candidates);
+    uint64_t* cand = reinterpret_cast<uint64_t*>(static_cast<char*>(d_candidates) + tc_logits_bytes(h, column_count));
+    hc::GemvSeg seg;
+    memset(&seg, 0, sizeof seg);
+    seg.w = h->d_data;
+    seg.out = logits;
+    seg.type = h->type;
+    seg.rows = int(h->row_count);
+    const hc::Q8Buf q = hc::q8buf_carve(const_cast<void*>(d_workspace), int(input_size), int(column_count));
+    HPC_CK(hc::launch_gemm_tc(seg, int(input_size / 256), q, 0, int(column_count), st), "tensor-core LM head");
+    const size_t col_stride = tc_chunks(h) * k;
+    HPC_CK(hc::launch_logits_topk(logits, int(h->row_count), int(column_count), int(k), id_offset, cand, col_stride,
+                                  st),
+           "logits top-k");
+    HPC_CK(hc::launch_topk_merge(cand, int(col_stride), col_stride, int(k), k, int(column_count), int(k), softcap,
+                                 d_ids, d_vals, d_keys, st),
+           "top-k merge launch");
+    return HPC_OK;
+  }
   const int tiles = int(h->rows_pad / hc::TILE);
   const int grid = hc::lmhead_grid(tiles);
   hc::LmHeadParams P;

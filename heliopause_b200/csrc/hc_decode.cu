@@ -499,6 +499,167 @@ __global__ void __launch_bounds__(256) geglu_quant_kernel(const float* __restric
   }
 }
 
+// ---- prefill: many tokens per call -----------------------------------------------------
+
+// QK-norm + RoPE of every token's queries (rounded with the Rust f16 codec,
+// lib.rs:590-597) into qh[m][h][256], and, in an own-KV layer, the tokens'
+// K (norm + RoPE) and V (unweighted norm) rows into the cache (layers.ts:
+// 201-268, 887-911).  One CTA per token, one warp per head vector.
+__global__ void prefill_qkv_post_kernel(const float* __restrict__ q, const float* __restrict__ kraw,
+                                        const float* __restrict__ vraw, const float* __restrict__ qnw,
+                                        const float* __restrict__ knw, const double* __restrict__ cos_t,
+                                        const double* __restrict__ sin_t, double eps, int own_kv, float* __restrict__ kc,
+                                        float* __restrict__ vc, const int32_t* __restrict__ pos, int H, int KVH, int cap,
+                                        float* __restrict__ qh) {
+  constexpr int HD = 256;
+  const int m = blockIdx.x, lane = threadIdx.x & 31, job = threadIdx.x >> 5;
+  const int jobs = own_kv ? H + 2 * KVH : H;
+  if (job >= jobs) return;
+  float x[8], w[8];
+  double c8[8], s8[8];
+  load_rope8(cos_t + size_t(m) * (HD / 2), sin_t + size_t(m) * (HD / 2), lane, c8, s8);
+  if (job < H) {
+    load8(q + (size_t(m) * H + job) * HD + 8 * lane, x);
+    load8(qnw + 8 * lane, w);
+    head_norm_rope(x, w, true, true, c8, s8, eps, lane);
+    float* dst = qh + (size_t(m) * H + job) * HD + 8 * lane;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) dst[i] = round_f16_rust(x[i]);
+    return;
+  }
+  const int isv = (job - H) / KVH, kvh = (job - H) % KVH;
+  load8((isv ? vraw : kraw) + (size_t(m) * KVH + kvh) * HD + 8 * lane, x);
+  if (!isv) load8(knw + 8 * lane, w);
+  head_norm_rope(x, w, !isv, !isv, c8, s8, eps, lane);
+  float* cache = (isv ? vc : kc) + (size_t(pos[m] % cap) * KVH + kvh) * HD + 8 * lane;
+  reinterpret_cast<float4*>(cache)[0] = make_float4(x[0], x[1], x[2], x[3]);
+  reinterpret_cast<float4*>(cache)[1] = make_float4(x[4], x[5], x[6], x[7]);
+}
+
+// Causal GQA attention of PF_QT consecutive tokens x the G query heads of one
+// KV head (hp_gqa_attention_f32, lib.rs:539-654, scale 1): KV chunks of
+// PF_CK keys are staged with cp.async; each query vector keeps an online
+// softmax (running max, f64 exp of the differences, f32 sum) and thread d
+// accumulates dimension d of every query's output.  The result is cast with
+// the TS f16 codec (castF16Rows, layers.ts:982-988) and its 256-block (one
+// head) quantized to Q8_K for the output projection.  Grid
+// (ceil(M / PF_QT), KVH); tokens are consecutive positions pos[0] + m.
+constexpr int PF_QT = 8, PF_CK = 32;
+__global__ void __launch_bounds__(256) prefill_attn_kernel(const float* __restrict__ qh, const float* __restrict__ kc,
+                                                          const float* __restrict__ vc, const int32_t* __restrict__ pos,
+                                                          int M, int H, int KVH, int cap, Q8Buf qo,
+                                                          float* __restrict__ attn_out) {
+  constexpr int HD = 256, NQ_MAX = PF_QT * 8;  // G <= 8
+  extern __shared__ __align__(16) float psm[];
+  const int G = H / KVH, NQ = PF_QT * G, kvh = blockIdx.y, m0 = blockIdx.x * PF_QT;
+  float* qs = psm;                          // [NQ][HD]
+  float* ks = qs + NQ * HD;                 // [PF_CK][ATT_KSTRIDE]
+  float* vs = ks + PF_CK * ATT_KSTRIDE;     // [PF_CK][HD]
+  float* ps = vs + PF_CK * HD;              // [NQ][PF_CK]
+  __shared__ float alpha[NQ_MAX], run_m[NQ_MAX], run_l[NQ_MAX];
+  __shared__ __align__(16) uint8_t stage[8][256];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int mt = min(PF_QT, M - m0);
+  // queries: vector qi = token (qi / G) of the tile, head kvh * G + qi % G
+  for (int i = tid; i < NQ * HD / 4; i += blockDim.x) {
+    const int qi = (4 * i) / HD, d = (4 * i) % HD, mm = min(qi / G, mt - 1);
+    reinterpret_cast<float4*>(qs)[i] =
+        *reinterpret_cast<const float4*>(qh + (size_t(m0 + mm) * H + kvh * G + qi % G) * HD + d);
+  }
+  if (tid < NQ) {
+    run_m[tid] = -INFINITY;
+    run_l[tid] = 0.0f;
+  }
+  float o[NQ_MAX];
+#pragma unroll
+  for (int i = 0; i < NQ_MAX; ++i) o[i] = 0.0f;
+  const int last = pos[m0 + mt - 1];  // causal: keys 0 .. last
+  const int start = max(0, last + 1 - cap);
+  for (int k0 = start; k0 <= last; k0 += PF_CK) {
+    const int nk = min(PF_CK, last + 1 - k0);
+    for (int i = tid; i < PF_CK * (HD / 4); i += blockDim.x) {
+      const int j = i / (HD / 4), c = i % (HD / 4), key = k0 + min(j, nk - 1);
+      const size_t row = (size_t(key % cap) * KVH + kvh) * HD + 4 * c;
+      cp_async16(ks + j * ATT_KSTRIDE + 4 * c, kc + row);
+      cp_async16(vs + j * HD + 4 * c, vc + row);
+    }
+    cp_async_commit();
+    cp_async_wait_all();
+    __syncthreads();
+    // scores, causal per query token
+    for (int e = tid; e < NQ * PF_CK; e += blockDim.x) {
+      const int qi = e / PF_CK, j = e % PF_CK;
+      const float4* qv = reinterpret_cast<const float4*>(qs + qi * HD);
+      const float4* kv = reinterpret_cast<const float4*>(ks + j * ATT_KSTRIDE);
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 16
+      for (int c = 0; c < HD / 4; ++c) {
+        const float4 a = qv[c], b = kv[c];
+        acc.x = fmaf(a.x, b.x, acc.x);
+        acc.y = fmaf(a.y, b.y, acc.y);
+        acc.z = fmaf(a.z, b.z, acc.z);
+        acc.w = fmaf(a.w, b.w, acc.w);
+      }
+      const int mq = qi / G;
+      const bool ok = j < nk && mq < mt && k0 + j <= pos[m0 + mq];
+      ps[e] = ok ? (acc.x + acc.y) + (acc.z + acc.w) : -INFINITY;
+    }
+    __syncthreads();
+    // online softmax: warp per query vector, lane = key
+    for (int qi = warp; qi < NQ; qi += 8) {
+      const float sc = ps[qi * PF_CK + lane];
+      float mx = sc;
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+      const float mo = run_m[qi], mn = fmaxf(mo, mx);
+      const float p = (sc == -INFINITY) ? 0.0f : float(exp(double(sc - mn)));
+      float sum = p;
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+      ps[qi * PF_CK + lane] = p;
+      __syncwarp();
+      if (lane == 0) {
+        const float a = (mo == -INFINITY) ? 0.0f : float(exp(double(mo - mn)));
+        alpha[qi] = a;
+        run_l[qi] = run_l[qi] * a + sum;
+        run_m[qi] = mn;
+      }
+    }
+    __syncthreads();
+    // outputs: thread d owns dimension d of every query vector
+    const int d = tid;
+#pragma unroll
+    for (int qi = 0; qi < NQ_MAX; ++qi) {
+      if (qi < NQ) {
+        float acc = o[qi] * alpha[qi];
+        const float* pr = ps + qi * PF_CK;
+        for (int j = 0; j < nk; ++j) acc += pr[j] * vs[j * HD + d];
+        o[qi] = acc;
+      }
+    }
+    __syncthreads();
+  }
+  // normalize, f16 cast, quantize each (token, head) block
+  float* outv = ks;  // reuse: [NQ][HD]
+#pragma unroll
+  for (int qi = 0; qi < NQ_MAX; ++qi)
+    if (qi < NQ) outv[qi * HD + tid] = round_f16_ts(float(double(o[qi]) / double(run_l[qi])));
+  __syncthreads();
+  for (int qi = warp; qi < NQ; qi += 8) {
+    const int mq = qi / G, h = kvh * G + qi % G;
+    if (mq >= mt) continue;
+    float v8[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v8[i] = outv[qi * HD + 8 * lane + i];
+    if (attn_out) {
+      float* dst = attn_out + (size_t(m0 + mq) * H + h) * HD + 8 * lane;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) dst[i] = v8[i];
+    }
+    q8k_block_warp(v8, lane, stage[warp], q8_rec_a(qo, m0 + mq, h), q8_rec_b(qo, m0 + mq, h));
+  }
+}
+
 // ---- launch helpers ---------------------------------------------------------------------
 
 template <typename... KArgs, typename... Args>
@@ -571,6 +732,37 @@ cudaError_t launch_attn_combine(const float* part_m, const float* part_l, const 
 cudaError_t launch_geglu_quant(const float* gate, const float* up, int M, int F, const Q8Buf& q, float* act_out,
                                cudaStream_t st) {
   return pdl_launch(geglu_quant_kernel, dim3(F / 256, M), dim3(256), 0, st, gate, up, F, q, act_out);
+}
+
+cudaError_t launch_prefill_qkv_post(const float* q, const float* kraw, const float* vraw, const float* qnw,
+                                   const float* knw, const double* cos_t, const double* sin_t, double eps, bool own_kv,
+                                   float* kc, float* vc, const int32_t* pos, int M, int H, int KVH, int cap, float* qh,
+                                   cudaStream_t st) {
+  const int jobs = own_kv ? H + 2 * KVH : H;
+  if (jobs > 32) return cudaErrorInvalidValue;
+  prefill_qkv_post_kernel<<<M, 32 * jobs, 0, st>>>(q, kraw, vraw, qnw, knw, cos_t, sin_t, eps, int(own_kv), kc, vc, pos,
+                                                   H, KVH, cap, qh);
+  return cudaGetLastError();
+}
+
+size_t prefill_attn_smem_bytes(int H, int KVH) {
+  const int NQ = PF_QT * (H / KVH);
+  return sizeof(float) * (size_t(NQ) * 256 + size_t(PF_CK) * ATT_KSTRIDE + size_t(PF_CK) * 256 + size_t(NQ) * PF_CK);
+}
+
+cudaError_t launch_prefill_attention(const float* qh, const float* kc, const float* vc, const int32_t* pos, int M,
+                                     int H, int KVH, int cap, const Q8Buf& qo, float* attn_out, cudaStream_t st) {
+  if (H / KVH > 8) return cudaErrorInvalidValue;
+  const size_t smem = prefill_attn_smem_bytes(H, KVH);
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(prefill_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  prefill_attn_kernel<<<dim3(unsigned((M + PF_QT - 1) / PF_QT), unsigned(KVH)), 256, smem, st>>>(
+      qh, kc, vc, pos, M, H, KVH, cap, qo, attn_out);
+  return cudaGetLastError();
 }
 
 }  // namespace hc

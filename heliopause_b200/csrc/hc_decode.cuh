@@ -28,4 +28,14 @@ cudaError_t launch_attn_combine(const float* part_m, const float* part_l, const 
 cudaError_t launch_geglu_quant(const float* gate, const float* up, int M, int F, const Q8Buf& q, float* act_out,
                                cudaStream_t st);
 
+// Prefill (many tokens at consecutive positions): QK-norm/RoPE of every
+// token's queries into qh [M][H][256] and its K/V rows into the cache, then
+// causal attention writing the Q8_K records of the output projection's input.
+cudaError_t launch_prefill_qkv_post(const float* q, const float* kraw, const float* vraw, const float* qnw,
+                                   const float* knw, const double* cos_t, const double* sin_t, double eps, bool own_kv,
+                                   float* kc, float* vc, const int32_t* pos, int M, int H, int KVH, int cap, float* qh,
+                                   cudaStream_t st);
+cudaError_t launch_prefill_attention(const float* qh, const float* kc, const float* vc, const int32_t* pos, int M,
+                                     int H, int KVH, int cap, const Q8Buf& qo, float* attn_out, cudaStream_t st);
+
 }  // namespace hc

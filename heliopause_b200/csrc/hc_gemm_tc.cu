@@ -1,0 +1,303 @@
+// hc_gemm_tc.cu -- Q4_K / Q6_K x Q8_K matmul on the tensor cores for wide
+// inputs (M >= TC_MIN_COLS columns): prefill and the M = 64 LM head, where the
+// product is a dense contraction rather than a weight stream.
+//
+// Same arithmetic as the GEMV (hc_gemv_body.cuh, i.e. vec_dot_q4_k_q8_k /
+// vec_dot_q6_k_q8_k, lib.rs:2117-2172 / 1924-1968): the integer sum of every
+// (row, column, sub-block) is exact, then scaled by the sub-block's integer
+// scale, summed over the block in int32, and combined with d, dmin and the
+// activation's d in f32 once per 256-block.
+//
+// Why mma.sync (s8, int32 accumulators in registers) and not tcgen05: the
+// K-quant scales are per row and per 32- (Q4_K) or 16-element (Q6_K)
+// sub-block, small integers that must multiply the exact sub-block sums
+// before they are added.  With register accumulators that is one integer
+// multiply-add per accumulator after each MMA; tcgen05's TMEM accumulators
+// would need a round trip per K = 32 step, and its block-scaled kinds take
+// only power-of-two style scale formats.
+//
+// Decomposition: a CTA of 8 warps covers 4 weight tiles (128 rows) x 64
+// columns; warp w takes tile w % 4 and columns 32 (w / 4) .. + 31 as 2 x 4
+// m16n8 accumulator tiles.  Per 256-block the CTA stages its 4 weight units
+// (the row-tile layout of hc_common.cuh, unchanged) and its 64 columns' Q8_K
+// records with cp.async into one of two shared-memory stages, so block b + 1
+// streams in while block b is computed.  The tile layout already stores the
+// 4-bit / 6-bit values in the order the dp4a path pairs them with the record
+// bytes; read with lane = (row, 4-word group), the same words are exactly the
+// A fragments of m16n8k32 (Q4_K) / m16n8k16 (Q6_K), and the record words are
+// the B fragments, so no repack is needed.
+#include "hc_bulk.cuh"
+#include "hc_common.cuh"
+#include "hc_kernels.cuh"
+#include "hc_unpack.cuh"
+
+namespace hc {
+
+constexpr int TC_WARPS = 8;
+constexpr int TC_THREADS = 32 * TC_WARPS;
+constexpr int TC_TILES = 4;   // weight tiles (32 rows) per CTA
+constexpr int TC_COLS = 64;   // columns per CTA
+
+struct TcParams {
+  const uint8_t* w;    // tile layout
+  const uint8_t* act;  // the Q8_K record plane this type reads (A for Q4_K, B for Q6_K), [col][nb]
+  float* out;          // out[col * rows + row]
+  int rows, tiles, nb, ncols, col0;
+};
+
+template <int TYPE>
+struct TcType {
+  static constexpr int UB = TYPE == TYPE_Q4_K ? 4608 : 6720;
+  static constexpr int REC = TYPE == TYPE_Q4_K ? Q8A_REC : Q8B_REC;
+  static constexpr int STAGE = TC_TILES * UB + TC_COLS * REC;
+};
+
+__device__ __forceinline__ void mma_k32(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                        uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
+      : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+}
+
+__device__ __forceinline__ void mma_k16(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
+  asm volatile("mma.sync.aligned.m16n8k16.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%7,%7,%7,%7};"
+               : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3])
+               : "r"(a0), "r"(a1), "r"(b0), "r"(0));
+}
+
+__device__ __forceinline__ uint32_t lds32(const uint8_t* p) { return *reinterpret_cast<const uint32_t*>(p); }
+
+// One 256-block of a warp's 32 rows x 32 columns.  Lane (g = lane / 4,
+// t = lane % 4): rows 16 mg + g and 16 mg + g + 8, columns 8 ng + 2t, + 1.
+template <int TYPE>
+__device__ __forceinline__ void tc_block(const uint8_t* unit, const uint8_t* act, float (&acc)[2][4][4], int g,
+                                         int t) {
+  constexpr int REC = TcType<TYPE>::REC;
+  int isum[2][4][4];
+#pragma unroll
+  for (int mg = 0; mg < 2; ++mg)
+#pragma unroll
+    for (int ng = 0; ng < 4; ++ng)
+#pragma unroll
+      for (int r = 0; r < 4; ++r) isum[mg][ng][r] = 0;
+  if constexpr (TYPE == TYPE_Q4_K) {
+    Q4KHeader hd[2][2];
+#pragma unroll
+    for (int mg = 0; mg < 2; ++mg)
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+        hd[mg][h] = q4k_header(*reinterpret_cast<const uint4*>(unit + (16 * mg + 8 * h + g) * 16));
+#pragma unroll
+    for (int pp = 0; pp < 4; ++pp) {
+      uint32_t w[2][4];  // [mg][row g low word, row g+8 low word, row g high word, row g+8 high word]
+#pragma unroll
+      for (int mg = 0; mg < 2; ++mg) {
+        w[mg][0] = lds32(unit + (1 + 2 * pp) * 512 + (16 * mg + g) * 16 + 4 * t);
+        w[mg][1] = lds32(unit + (1 + 2 * pp) * 512 + (16 * mg + g + 8) * 16 + 4 * t);
+        w[mg][2] = lds32(unit + (2 + 2 * pp) * 512 + (16 * mg + g) * 16 + 4 * t);
+        w[mg][3] = lds32(unit + (2 + 2 * pp) * 512 + (16 * mg + g + 8) * 16 + 4 * t);
+      }
+#pragma unroll
+      for (int ng = 0; ng < 4; ++ng) {
+        const uint8_t* rec = act + (8 * ng + g) * REC + 64 * pp + 4 * t;
+        const uint32_t bl0 = lds32(rec), bl1 = lds32(rec + 16), bh0 = lds32(rec + 32), bh1 = lds32(rec + 48);
+#pragma unroll
+        for (int mg = 0; mg < 2; ++mg) {
+          int clo[4], chi[4];
+          mma_k32(clo, w[mg][0] & 0x0f0f0f0fu, w[mg][1] & 0x0f0f0f0fu, w[mg][2] & 0x0f0f0f0fu,
+                  w[mg][3] & 0x0f0f0f0fu, bl0, bl1);
+          mma_k32(chi, (w[mg][0] >> 4) & 0x0f0f0f0fu, (w[mg][1] >> 4) & 0x0f0f0f0fu, (w[mg][2] >> 4) & 0x0f0f0f0fu,
+                  (w[mg][3] >> 4) & 0x0f0f0f0fu, bh0, bh1);
+#pragma unroll
+          for (int r = 0; r < 4; ++r) {
+            const Q4KHeader& h = hd[mg][r >> 1];
+            isum[mg][ng][r] += h.sc(2 * pp) * clo[r] + h.sc(2 * pp + 1) * chi[r];
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int ng = 0; ng < 4; ++ng) {
+#pragma unroll
+      for (int cc = 0; cc < 2; ++cc) {
+        const uint8_t* rec = act + (8 * ng + 2 * t + cc) * REC;
+        const uint4 bs = *reinterpret_cast<const uint4*>(rec + Q8A_BS);
+        const float d8 = *reinterpret_cast<const float*>(rec + Q8A_D);
+#pragma unroll
+        for (int mg = 0; mg < 2; ++mg)
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const Q4KHeader& hh = hd[mg][h];
+            int ms = __dp2a_lo(int(bs.x), int(hh.mn_lo), 0);
+            ms = __dp2a_hi(int(bs.y), int(hh.mn_lo), ms);
+            ms = __dp2a_lo(int(bs.z), int(hh.mn_hi), ms);
+            ms = __dp2a_hi(int(bs.w), int(hh.mn_hi), ms);
+            const int r = 2 * h + cc;
+            acc[mg][ng][r] += __fmul_rn(hh.d, d8) * float(isum[mg][ng][r]) - __fmul_rn(hh.dmin, d8) * float(ms);
+          }
+      }
+    }
+  } else {
+    uint32_t scw[2][2][4];
+    float dw[2][2];
+#pragma unroll
+    for (int mg = 0; mg < 2; ++mg)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int row = 16 * mg + 8 * h + g;
+        const uint4 s4 = *reinterpret_cast<const uint4*>(unit + 12 * 512 + row * 16);
+        scw[mg][h][0] = s4.x;
+        scw[mg][h][1] = s4.y;
+        scw[mg][h][2] = s4.z;
+        scw[mg][h][3] = s4.w;
+        dw[mg][h] = f16_bits_to_f32(reinterpret_cast<const uint16_t*>(unit + Q6K_DPLANE_OFFSET)[row]);
+      }
+#pragma unroll
+    for (int s = 0; s < 8; ++s) {
+      uint32_t ua[2][2], ub[2][2];  // [mg][row g, row g+8]
+#pragma unroll
+      for (int mg = 0; mg < 2; ++mg)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int row = 16 * mg + 8 * h + g;
+          const uint32_t nw = lds32(unit + s * 512 + row * 16 + 4 * t);
+          const uint32_t hw = lds32(unit + (8 + (s >> 1)) * 512 + row * 16 + 4 * (2 * (s & 1) + (t >> 1)));
+          q6k_unpack(nw, hw, t & 1, ua[mg][h], ub[mg][h]);
+        }
+#pragma unroll
+      for (int ng = 0; ng < 4; ++ng) {
+        const uint8_t* rec = act + (8 * ng + g) * REC + 4 * t;
+        const uint32_t ba = lds32(rec + 16 * s), bb = lds32(rec + 16 * (s + 8));
+#pragma unroll
+        for (int mg = 0; mg < 2; ++mg) {
+          int ca[4], cb[4];
+          mma_k16(ca, ua[mg][0], ua[mg][1], ba);
+          mma_k16(cb, ub[mg][0], ub[mg][1], bb);
+#pragma unroll
+          for (int r = 0; r < 4; ++r) {
+            const uint32_t* sw = scw[mg][r >> 1];
+            const int sa = int(int8_t((sw[s >> 2] >> (8 * (s & 3))) & 0xff));
+            const int sb = int(int8_t((sw[(s + 8) >> 2] >> (8 * ((s + 8) & 3))) & 0xff));
+            isum[mg][ng][r] += sa * ca[r] + sb * cb[r];
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int ng = 0; ng < 4; ++ng) {
+#pragma unroll
+      for (int cc = 0; cc < 2; ++cc) {
+        const uint8_t* rec = act + (8 * ng + 2 * t + cc) * REC;
+        const uint4 b0 = *reinterpret_cast<const uint4*>(rec + Q8B_BS);
+        const uint4 b1 = *reinterpret_cast<const uint4*>(rec + Q8B_BS + 16);
+        const float d8 = *reinterpret_cast<const float*>(rec + Q8B_D);
+#pragma unroll
+        for (int mg = 0; mg < 2; ++mg)
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const uint32_t* sw = scw[mg][h];
+            int corr = __dp2a_lo(int(b0.x), int(sw[0]), 0);
+            corr = __dp2a_hi(int(b0.y), int(sw[0]), corr);
+            corr = __dp2a_lo(int(b0.z), int(sw[1]), corr);
+            corr = __dp2a_hi(int(b0.w), int(sw[1]), corr);
+            corr = __dp2a_lo(int(b1.x), int(sw[2]), corr);
+            corr = __dp2a_hi(int(b1.y), int(sw[2]), corr);
+            corr = __dp2a_lo(int(b1.z), int(sw[3]), corr);
+            corr = __dp2a_hi(int(b1.w), int(sw[3]), corr);
+            const int r = 2 * h + cc;
+            acc[mg][ng][r] += __fmul_rn(dw[mg][h], d8) * float(isum[mg][ng][r] - 32 * corr);
+          }
+      }
+    }
+  }
+}
+
+template <int TYPE>
+__global__ void __launch_bounds__(TC_THREADS, 2) gemm_tc_kernel(const __grid_constant__ TcParams p) {
+  using T = TcType<TYPE>;
+  extern __shared__ __align__(16) uint8_t smem[];
+  const int tile0 = int(blockIdx.x) * TC_TILES, col0 = p.col0 + int(blockIdx.y) * TC_COLS;
+  const int warp = int(threadIdx.x >> 5), lane = int(threadIdx.x & 31), g = lane >> 2, t = lane & 3;
+  const int wt = warp & 3, wh = warp >> 2;
+  // Tiles past the end and columns past ncols are read clamped (never out of
+  // the buffers) and not stored.
+  auto issue = [&](int b, uint8_t* st) {
+    for (int i = int(threadIdx.x); i < TC_TILES * T::UB / 16; i += TC_THREADS) {
+      const int u = i / (T::UB / 16), o = i % (T::UB / 16);
+      const int tile = min(tile0 + u, p.tiles - 1);
+      cp_async16(st + u * T::UB + o * 16, p.w + (size_t(tile) * p.nb + b) * T::UB + o * 16);
+    }
+    for (int i = int(threadIdx.x); i < TC_COLS * T::REC / 16; i += TC_THREADS) {
+      const int c = i / (T::REC / 16), o = i % (T::REC / 16);
+      const int col = min(col0 + c, p.col0 + p.ncols - 1);
+      cp_async16(st + TC_TILES * T::UB + c * T::REC + o * 16, p.act + (size_t(col) * p.nb + b) * T::REC + o * 16);
+    }
+    cp_async_commit();
+  };
+  float acc[2][4][4];
+#pragma unroll
+  for (int mg = 0; mg < 2; ++mg)
+#pragma unroll
+    for (int ng = 0; ng < 4; ++ng)
+#pragma unroll
+      for (int r = 0; r < 4; ++r) acc[mg][ng][r] = 0.0f;
+  issue(0, smem);
+  for (int b = 0; b < p.nb; ++b) {
+    if (b + 1 < p.nb) {
+      issue(b + 1, smem + ((b + 1) & 1) * T::STAGE);
+      asm volatile("cp.async.wait_group 1;" ::: "memory");
+    } else {
+      asm volatile("cp.async.wait_group 0;" ::: "memory");
+    }
+    __syncthreads();
+    const uint8_t* st = smem + (b & 1) * T::STAGE;
+    tc_block<TYPE>(st + wt * T::UB, st + TC_TILES * T::UB + (32 * wh) * T::REC, acc, g, t);
+    __syncthreads();  // every warp is done with this stage before it is refilled
+  }
+  const int tile = tile0 + wt;
+  if (tile >= p.tiles) return;
+#pragma unroll
+  for (int mg = 0; mg < 2; ++mg)
+#pragma unroll
+    for (int ng = 0; ng < 4; ++ng)
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const int row = tile * TILE + 16 * mg + g + 8 * (r >> 1);
+        const int col = col0 + 32 * wh + 8 * ng + 2 * t + (r & 1);
+        if (row < p.rows && col < p.col0 + p.ncols) p.out[size_t(col) * p.rows + row] = acc[mg][ng][r];
+      }
+}
+
+template <int TYPE>
+static cudaError_t launch_tc(const TcParams& p, cudaStream_t st) {
+  const size_t smem = 2 * size_t(TcType<TYPE>::STAGE);
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<TYPE>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  const dim3 grid(unsigned((p.tiles + TC_TILES - 1) / TC_TILES), unsigned((p.ncols + TC_COLS - 1) / TC_COLS));
+  gemm_tc_kernel<TYPE><<<grid, TC_THREADS, smem, st>>>(p);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_gemm_tc(const GemvSeg& seg, int nb, const Q8Buf& q, int col0, int ncols, cudaStream_t st) {
+  TcParams p;
+  p.w = seg.w;
+  p.out = seg.out;
+  p.rows = seg.rows;
+  p.tiles = (seg.rows + TILE - 1) / TILE;
+  p.nb = nb;
+  p.ncols = ncols;
+  p.col0 = col0;
+  if (seg.type == TYPE_Q4_K) {
+    p.act = q.a;
+    return launch_tc<TYPE_Q4_K>(p, st);
+  }
+  p.act = q.b;
+  return launch_tc<TYPE_Q6_K>(p, st);
+}
+
+}  // namespace hc

@@ -110,4 +110,9 @@ int sm_count();
 int persistent_grid(int items, int cap);
 cudaError_t launch_gemv(const GemvParams& p, cudaStream_t stream);
 
+// Inputs of at least TC_MIN_COLS columns go to the tensor-core matmul
+// (hc_gemm_tc.cu), one launch per weight covering every column.
+constexpr int TC_MIN_COLS = 16;
+cudaError_t launch_gemm_tc(const GemvSeg& seg, int nb, const Q8Buf& q, int col0, int ncols, cudaStream_t st);
+
 }  // namespace hc

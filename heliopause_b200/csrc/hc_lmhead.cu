@@ -149,6 +149,57 @@ __global__ void __launch_bounds__(GEMV_THREADS, GEMV_CTAS_PER_SM) lmhead_topk_ke
   }
 }
 
+// Top-k candidates of materialized logits (the tensor-core LM head for wide
+// inputs): CTA (chunk, column) walks rows [chunk * chunk_rows, +chunk_rows)
+// of one column, each of its 4 warps keeping a running list over 32-row
+// steps (topk_insert_warp), then the 4 lists are merged by rank into the
+// CTA's k candidates at cand[col * col_stride + chunk * k].
+__global__ void __launch_bounds__(GEMV_THREADS) logits_topk_kernel(const float* __restrict__ logits, int rows,
+                                                                   int chunk_rows, int k, int32_t id_offset,
+                                                                   uint64_t* __restrict__ cand, size_t col_stride) {
+  __shared__ uint64_t best[GEMV_WARPS_PER_CTA][TOPK_MAX];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int col = blockIdx.y, chunk = blockIdx.x;
+  for (int i = threadIdx.x; i < GEMV_WARPS_PER_CTA * TOPK_MAX; i += blockDim.x) (&best[0][0])[i] = 0ull;
+  __syncthreads();
+  const int lo = chunk * chunk_rows, hi = min(rows, lo + chunk_rows);
+  const float* src = logits + size_t(col) * rows;
+  for (int base = lo + 32 * warp; base < hi; base += 32 * GEMV_WARPS_PER_CTA) {
+    const int row = base + lane;
+    const uint64_t key = row < hi ? topk_key(src[row], uint32_t(id_offset + row)) : 0ull;
+    topk_insert_warp(best[warp], k, key, lane);
+  }
+  __syncthreads();
+  uint64_t* out = cand + size_t(col) * col_stride + size_t(chunk) * k;
+  for (int i = threadIdx.x; i < k; i += blockDim.x) out[i] = 0ull;
+  __syncthreads();
+  for (int t = threadIdx.x; t < GEMV_WARPS_PER_CTA * k; t += blockDim.x) {
+    const int w = t / k, i = t % k;
+    const uint64_t e = best[w][i];
+    if (e == 0ull) continue;
+    int rank = i;
+    for (int o = 0; o < GEMV_WARPS_PER_CTA; ++o) {
+      if (o == w) continue;
+      int a = 0, b = k;  // first index whose key is <= e
+      while (a < b) {
+        const int mid = (a + b) >> 1;
+        if (best[o][mid] > e) a = mid + 1;
+        else b = mid;
+      }
+      rank += a;
+    }
+    if (rank < k) out[rank] = e;
+  }
+}
+
+cudaError_t launch_logits_topk(const float* logits, int rows, int cols, int k, int32_t id_offset, uint64_t* cand,
+                               size_t col_stride, cudaStream_t stream) {
+  const dim3 grid(unsigned((rows + LOGITS_CHUNK_ROWS - 1) / LOGITS_CHUNK_ROWS), unsigned(cols));
+  logits_topk_kernel<<<grid, GEMV_THREADS, 0, stream>>>(logits, rows, LOGITS_CHUNK_ROWS, k, id_offset, cand,
+                                                        col_stride);
+  return cudaGetLastError();
+}
+
 // Candidate i of column c lives at c*col_stride + (i / group)*group_stride +
 // i % group, so both [col][n] and all-gathered [rank][col][k] layouts merge
 // without a transpose.

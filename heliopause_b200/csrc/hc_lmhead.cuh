@@ -18,6 +18,12 @@ int lmhead_grid(int ntiles);
 // Candidates per CTA per column: the CTA's merged list of k.
 constexpr int LMHEAD_LISTS = 1;
 cudaError_t launch_lmhead_topk(const LmHeadParams& P, int grid, cudaStream_t stream);
+// Tensor-core LM head (inputs of >= TC_MIN_COLS columns): the logits are
+// written to scratch by launch_gemm_tc, then reduced to candidates in chunks
+// of LOGITS_CHUNK_ROWS rows per column.
+constexpr int LOGITS_CHUNK_ROWS = 2048;
+cudaError_t launch_logits_topk(const float* logits, int rows, int cols, int k, int32_t id_offset, uint64_t* cand,
+                               size_t col_stride, cudaStream_t stream);
 cudaError_t launch_topk_merge(const uint64_t* cand, int n, size_t col_stride, int group, size_t group_stride, int cols,
                               int k, float softcap, int32_t* ids, float* vals, uint64_t* keys_out,
                               cudaStream_t stream);

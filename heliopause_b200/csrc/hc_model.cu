@@ -77,6 +77,15 @@ struct hpc_model_s {
   void* persist_buf = nullptr;
   hc::PParams pparams{};
   size_t persist_ctr_bytes = 0;
+  // prefill workspace (hpc_model_prefill), grown to the largest token count seen
+  void* pf_arena = nullptr;
+  int pf_cap = 0;
+  float *pf_x = nullptr, *pf_q = nullptr, *pf_k = nullptr, *pf_v = nullptr, *pf_qh = nullptr, *pf_o = nullptr,
+        *pf_g = nullptr, *pf_u = nullptr, *pf_f = nullptr;
+  double *pf_cos = nullptr, *pf_sin = nullptr;
+  int32_t* pf_pos = nullptr;
+  void *pf_q8d = nullptr, *pf_q8f = nullptr;
+  size_t pf_q8d_bytes = 0, pf_q8f_bytes = 0;
 };
 
 static bool model_valid(const hpc_model_s* m) { return m && m->magic == kModelMagic; }
@@ -196,6 +205,7 @@ int hpc_model_release(hpc_model m) {
   cudaFree(m->cand);
   cudaFree(m->d_players);
   cudaFree(m->persist_buf);
+  cudaFree(m->pf_arena);
   if (m->capture_stream) cudaStreamDestroy(m->capture_stream);
   m->magic = 0;
   delete m;
@@ -618,6 +628,126 @@ int hpc_model_forward(hpc_model m, const int32_t* d_token_ids, const int32_t* d_
   if (d_hidden_out)
     HPC_CK(cudaMemcpyAsync(d_hidden_out, m->x, sizeof(float) * M * c.hidden, cudaMemcpyDeviceToDevice, st),
            "hidden out");
+  return HPC_OK;
+}
+
+
+}  // extern "C"
+
+// Grows the prefill workspace to `M` tokens (one arena; the old one is freed).
+static int prefill_reserve(hpc_model m, int M) {
+  if (M <= m->pf_cap) return HPC_OK;
+  const hpc_model_config& c = m->cfg;
+  const int D = c.hidden, F = c.ffn, H = c.heads, KVH = c.kv_heads, HD = c.head_dim;
+  cudaFree(m->pf_arena);
+  m->pf_arena = nullptr;
+  m->pf_cap = 0;
+  m->pf_q8d_bytes = hc::q8buf_bytes(D, M);
+  m->pf_q8f_bytes = hc::q8buf_bytes(F, M);
+  struct Piece {
+    void** p;
+    size_t bytes;
+  };
+  std::vector<Piece> pieces = {
+      {(void**)&m->pf_x, sizeof(float) * M * D},          {(void**)&m->pf_q, sizeof(float) * M * H * HD},
+      {(void**)&m->pf_k, sizeof(float) * M * KVH * HD},   {(void**)&m->pf_v, sizeof(float) * M * KVH * HD},
+      {(void**)&m->pf_qh, sizeof(float) * M * H * HD},    {(void**)&m->pf_o, sizeof(float) * M * D},
+      {(void**)&m->pf_g, sizeof(float) * M * F},          {(void**)&m->pf_u, sizeof(float) * M * F},
+      {(void**)&m->pf_f, sizeof(float) * M * D},          {(void**)&m->pf_cos, sizeof(double) * M * HD / 2},
+      {(void**)&m->pf_sin, sizeof(double) * M * HD / 2},  {(void**)&m->pf_pos, sizeof(int32_t) * M},
+      {&m->pf_q8d, m->pf_q8d_bytes},                      {&m->pf_q8f, m->pf_q8f_bytes},
+  };
+  size_t total = 0;
+  for (auto& p : pieces) total += (p.bytes + 255) / 256 * 256;
+  HPC_CK(cudaMalloc(&m->pf_arena, total), "prefill workspace");
+  char* cur = static_cast<char*>(m->pf_arena);
+  for (auto& p : pieces) {
+    *p.p = cur;
+    cur += (p.bytes + 255) / 256 * 256;
+  }
+  m->pf_cap = M;
+  return HPC_OK;
+}
+
+extern "C" {
+
+int hpc_model_prefill(hpc_model m, const float* d_hidden_in, const int32_t* d_positions, size_t token_count,
+                      float* d_hidden_out, void* stream) {
+  if (!model_valid(m)) return hpc_fail(HPC_ERR_ARG, "invalid model");
+  const hpc_model_config& c = m->cfg;
+  if (token_count < 1 || token_count > size_t(c.context))
+    return hpc_fail(HPC_ERR_SHAPE, "prefill token count %zu outside 1..%d", token_count, c.context);
+  if (!d_hidden_in || !d_positions || !d_hidden_out) return hpc_fail(HPC_ERR_ARG, "null pointer");
+  int rc = model_ready(m);
+  if (rc != HPC_OK) return rc;
+  std::lock_guard<std::mutex> lock(m->mu);
+  const int M = int(token_count);
+  rc = prefill_reserve(m, M);
+  if (rc != HPC_OK) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int D = c.hidden, F = c.ffn, H = c.heads, KVH = c.kv_heads, HD = c.head_dim;
+  const double eps = c.rms_eps;
+  const hc::Q8Buf qd = hc::q8buf_carve(m->pf_q8d, D, M);
+  const hc::Q8Buf qf = hc::q8buf_carve(m->pf_q8f, F, M);
+  float* X = m->pf_x;
+  HPC_CK(cudaMemcpyAsync(X, d_hidden_in, sizeof(float) * M * D, cudaMemcpyDeviceToDevice, st), "hidden in");
+  HPC_CK(cudaMemcpyAsync(m->pf_pos, d_positions, sizeof(int32_t) * M, cudaMemcpyDeviceToDevice, st), "positions");
+  HPC_CK(hc::launch_rope_table(m->pf_pos, M, HD / 2, std::pow(c.rope_theta, -2.0 / double(HD)), m->pf_cos, m->pf_sin,
+                               st),
+         "rope table");
+  auto mm = [&](std::initializer_list<std::pair<hpc_weight, float*>> ws, const void* q8, size_t q8_bytes,
+                size_t K) -> int {
+    hpc_weight hs[8];
+    float* outs[8];
+    size_t lens[8];
+    int n = 0;
+    for (auto& p : ws) {
+      hs[n] = p.first;
+      outs[n] = p.second;
+      lens[n] = p.first->row_count * size_t(M);
+      ++n;
+    }
+    return hpc_matmul_q8(size_t(n), hs, q8, q8_bytes, K, size_t(M), outs, lens, st);
+  };
+  for (int l = 0; l < c.layers; ++l) {
+    Layer& L = m->layers[l];
+    const bool own_kv = l < c.kv_layers;
+    const int kvl = m->kv_source[l];
+    if (l == 0)
+      HPC_CK(hc::launch_norm_quant(false, X, X, nullptr, nullptr, L.norm[HPC_N_ATTN], eps, M, D, qd, nullptr, st),
+             "attn norm");
+    else
+      HPC_CK(hc::launch_norm_quant(true, X, X, m->pf_f, m->layers[l - 1].norm[HPC_N_POST_FFW], L.norm[HPC_N_ATTN], eps,
+                                   M, D, qd, nullptr, st),
+             "post-ffn residual + attn norm");
+    rc = own_kv ? mm({{L.w[HPC_W_Q], m->pf_q}, {L.w[HPC_W_K], m->pf_k}, {L.w[HPC_W_V], m->pf_v}}, m->pf_q8d,
+                     m->pf_q8d_bytes, D)
+                : mm({{L.w[HPC_W_Q], m->pf_q}}, m->pf_q8d, m->pf_q8d_bytes, D);
+    if (rc != HPC_OK) return rc;
+    HPC_CK(hc::launch_prefill_qkv_post(m->pf_q, m->pf_k, m->pf_v, L.norm[HPC_N_Q], L.norm[HPC_N_K], m->pf_cos,
+                                       m->pf_sin, eps, own_kv, m->kc[kvl], m->vc[kvl], m->pf_pos, M, H, KVH, c.context,
+                                       m->pf_qh, st),
+           "prefill qk norm / rope / kv");
+    HPC_CK(hc::launch_prefill_attention(m->pf_qh, m->kc[kvl], m->vc[kvl], m->pf_pos, M, H, KVH, c.context, qd, nullptr,
+                                        st),
+           "prefill attention");
+    rc = mm({{L.w[HPC_W_O], m->pf_o}}, m->pf_q8d, m->pf_q8d_bytes, size_t(H) * HD);
+    if (rc != HPC_OK) return rc;
+    HPC_CK(hc::launch_norm_quant(true, X, X, m->pf_o, L.norm[HPC_N_POST_ATTN], L.norm[HPC_N_FFN], eps, M, D, qd,
+                                 nullptr, st),
+           "post-attn residual + ffn norm");
+    rc = mm({{L.w[HPC_W_GATE], m->pf_g}, {L.w[HPC_W_UP], m->pf_u}}, m->pf_q8d, m->pf_q8d_bytes, D);
+    if (rc != HPC_OK) return rc;
+    HPC_CK(hc::launch_geglu_quant(m->pf_g, m->pf_u, M, F, qf, nullptr, st), "geglu");
+    rc = mm({{L.w[HPC_W_DOWN], m->pf_f}}, m->pf_q8f, m->pf_q8f_bytes, F);
+    if (rc != HPC_OK) return rc;
+  }
+  // the last post-FFN residual (the output norm's quantization is computed
+  // and discarded: prefill returns the residual stream)
+  HPC_CK(hc::launch_norm_quant(true, X, X, m->pf_f, m->layers[c.layers - 1].norm[HPC_N_POST_FFW], m->output_norm, eps,
+                               M, D, qd, nullptr, st),
+         "post-ffn residual");
+  HPC_CK(cudaMemcpyAsync(d_hidden_out, X, sizeof(float) * M * D, cudaMemcpyDeviceToDevice, st), "hidden out");
   return HPC_OK;
 }
 

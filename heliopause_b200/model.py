@@ -282,6 +282,20 @@ class CudaDecoderModel:
             return ids_out, vals_out, self.hidden[:n].clone()
         return ids_out, vals_out
 
+    def prefill(self, hidden: torch.Tensor, start: int) -> torch.Tensor:
+        """SegmentRunner.runTokensHidden for a prompt: `hidden` [n][hidden]
+        (f32, the embedded tokens) at positions start .. start+n-1 through all
+        layers (hpc_model_prefill).  Writes the tokens' K/V and returns the
+        final residual stream [n][hidden]."""
+        x = hidden.to(device="cuda", dtype=torch.float32).contiguous().reshape(-1, self.shape.hidden)
+        n = x.shape[0]
+        pos = torch.arange(start, start + n, dtype=torch.int32, device="cuda")
+        out = torch.empty_like(x)
+        st = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+        hk.assert_cuda_ok(_lib.lib().hpc_model_prefill(self._h, C.c_void_p(x.data_ptr()), C.c_void_p(pos.data_ptr()),
+                                                       n, C.c_void_p(out.data_ptr()), st), "modelPrefill")
+        return out
+
     def decode_token(self, token_id: int, position: int, top_k: int):
         """ModelRunner.decodeToken: one token -> its top-k candidates."""
         ids, vals = self.forward([token_id], [position], top_k)

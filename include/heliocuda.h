@@ -272,6 +272,19 @@ int hpc_model_kv(hpc_model model, int kv_layer, float **d_key, float **d_value);
 int hpc_model_forward(hpc_model model, const int32_t *d_token_ids, const int32_t *d_positions, size_t token_count,
                       size_t top_k, int32_t *d_ids, float *d_vals, float *d_hidden_out, void *stream);
 
+/* Prefill: token_count (1..context) hidden vectors [token_count][hidden]
+ * (the embedding output, f32) at consecutive positions d_positions[0] + i
+ * through every layer.  It writes every token's K/V into the cache and the
+ * final residual stream to d_hidden_out [token_count][hidden].  This is the
+ * reference's SegmentRunner.runTokensHidden / prefill path
+ * (runner/segment-runner.ts:18-34, forward.ts:128-161;
+ * runner/webgpu/segment-runner.ts:1292-1795 runBatchedPrefillFromBoundary).
+ * Inputs of >= 16 columns run the matmuls on the tensor cores.  The
+ * attention is causal over [0, position].  The launches are eager (no graph),
+ * and the workspace grows to the largest token count seen. */
+int hpc_model_prefill(hpc_model model, const float *d_hidden_in, const int32_t *d_positions, size_t token_count,
+                      float *d_hidden_out, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

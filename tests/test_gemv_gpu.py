@@ -105,6 +105,13 @@ def _oracle_matmul(oracle, type_id, w, x, k, rows, cols):
     (syn.Q6_K, 16384, 2048, 8),
     (syn.Q6_K, 2048, 520, 2),
     (syn.Q6_K, 512, 33, 9),
+    # tensor-core path (>= 16 columns)
+    (syn.Q4_K, 2048, 2048, 64),
+    (syn.Q4_K, 768, 100, 70),      # ragged rows and columns
+    (syn.Q4_K, 2048, 1024, 512),   # prefill width
+    (syn.Q6_K, 2048, 520, 64),
+    (syn.Q6_K, 16384, 2048, 16),
+    (syn.Q6_K, 256, 33, 17),
 ])
 def test_matmul_matches_oracle(oracle, type_id, k, rows, cols):
     w = syn.quant_weight(type_id, rows, k, seed=rows * 3 + cols)

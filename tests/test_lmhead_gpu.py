@@ -49,6 +49,10 @@ def _check_topk(ids, vals, logits, k):
     (syn.Q6_K, 50000, 64, 3),    # ragged last tile, TOPK_MAX
     (syn.Q4_K, 4096, 1, 9),      # greedy (top-1), > 8 columns
     (syn.Q6_K, 40, 40, 1),       # k == rows
+    # tensor-core path (>= 16 columns): materialized logits, chunked lists
+    (syn.Q6_K, 20000, 40, 64),   # config-5 width, ragged last chunk
+    (syn.Q6_K, 50000, 64, 17),
+    (syn.Q4_K, 4096, 1, 20),
 ])
 def test_lm_head_topk_matches_oracle(oracle, type_id, rows, k, cols):
     kdim = 2048
@@ -84,6 +88,17 @@ def test_ties_prefer_lower_id_and_softcap(oracle):
     assert np.all(v == v[0])
     capped = np.float32(np.tanh(np.float64(v[0]) / 30.0) * 30.0)
     assert np.all(vals2.cpu().numpy()[0] == capped)
+    # the same on the tensor-core path: 16 columns, rows spread over chunks
+    rows = 5000
+    w = np.tile(one, rows)
+    x = np.tile(syn.activations(1, kdim, seed=4), 16)
+    h = hk.create_quantized_weight_handle("Q6_K", w, kdim, rows)
+    try:
+        ids, vals = hk.lm_head_topk(h, torch.from_numpy(x).cuda(), 16, 10, id_offset=7)
+    finally:
+        hk.release_quantized_weight_handle(h)
+    assert all(r == list(range(7, 17)) for r in ids.cpu().numpy().tolist())
+    assert np.all(vals.cpu().numpy() == v[0])
 
 
 def test_topk_errors():
