@@ -8,6 +8,7 @@
 // row_count)".
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -217,6 +218,19 @@ int hpc_quantize_q8_k(const float* d_in, size_t in_len, size_t input_size, size_
   return HPC_OK;
 }
 
+// Narrowest launch (columns) that runs on the tensor-core GEMV:
+// GEMV_MMA_MIN_COLS, or HPC_GEMV_MMA_MIN_COLS (9 keeps every launch of up to
+// 8 columns on the dp4a GEMV).
+static int gemv_mma_min_cols() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("HPC_GEMV_MMA_MIN_COLS");
+    v = e ? atoi(e) : hc::GEMV_MMA_MIN_COLS;
+    if (v < 1) v = 1;
+  }
+  return v;
+}
+
 // GEMV launches over an already-quantized workspace: one launch per group of
 // up to 8 columns, covering all segments.
 static int launch_gemv_ws(const hc::Q8Buf& q, int K, int cols, const hc::GemvSeg* segs, int nseg, int total_tiles,
@@ -237,6 +251,10 @@ static int launch_gemv_ws(const hc::Q8Buf& q, int K, int cols, const hc::GemvSeg
   for (int c0 = 0; c0 < cols; c0 += 8) {
     p.col0 = c0;
     p.ncols = cols - c0 < 8 ? cols - c0 : 8;
+    if (p.ncols >= gemv_mma_min_cols() && !pro) {
+      HPC_CK(hc::launch_gemv_mma(p, st), "tensor-core gemv launch");
+      continue;
+    }
     hc::gemv_plan(p);  // the plan depends on the column count of the launch
     HPC_CK(hc::launch_gemv(p, st), "gemv launch");
   }

@@ -54,6 +54,22 @@ __device__ __forceinline__ bool mbar_wait_parity(uint64_t* bar, uint32_t parity,
   }
 }
 
+// mbar_wait_parity for waits that are expected to last (a weight unit still
+// in flight): each try_wait may suspend the warp for up to SLEEP_HINT_NS
+// until the phase completes, so a waiting warp does not take issue slots
+// from the warps that are computing.  Same bound and status as above.
+constexpr unsigned SLEEP_HINT_NS = 20000;
+__device__ __forceinline__ bool mbar_wait_parity_sleep(uint64_t* bar, uint32_t parity, int* err) {
+  uint32_t ok;
+  asm volatile(
+      "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3; selp.u32 %0, 1, 0, p; }"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(SLEEP_HINT_NS)
+      : "memory");
+  if (ok) return true;
+  return mbar_wait_parity(bar, parity, err);
+}
+
 // dst, src, bytes: multiples of 16.
 __device__ __forceinline__ void bulk_copy_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile(

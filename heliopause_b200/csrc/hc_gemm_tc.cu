@@ -29,7 +29,7 @@
 #include "hc_bulk.cuh"
 #include "hc_common.cuh"
 #include "hc_kernels.cuh"
-#include "hc_unpack.cuh"
+#include "hc_mma.cuh"
 
 namespace hc {
 
@@ -51,167 +51,6 @@ struct TcType {
   static constexpr int REC = TYPE == TYPE_Q4_K ? Q8A_REC : Q8B_REC;
   static constexpr int STAGE = TC_TILES * UB + TC_COLS * REC;
 };
-
-__device__ __forceinline__ void mma_k32(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
-                                        uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
-      : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
-}
-
-__device__ __forceinline__ void mma_k16(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
-  asm volatile("mma.sync.aligned.m16n8k16.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%7,%7,%7,%7};"
-               : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3])
-               : "r"(a0), "r"(a1), "r"(b0), "r"(0));
-}
-
-__device__ __forceinline__ uint32_t lds32(const uint8_t* p) { return *reinterpret_cast<const uint32_t*>(p); }
-
-// One 256-block of a warp's 32 rows x 32 columns.  Lane (g = lane / 4,
-// t = lane % 4): rows 16 mg + g and 16 mg + g + 8, columns 8 ng + 2t, + 1.
-template <int TYPE>
-__device__ __forceinline__ void tc_block(const uint8_t* unit, const uint8_t* act, float (&acc)[2][4][4], int g,
-                                         int t) {
-  constexpr int REC = TcType<TYPE>::REC;
-  int isum[2][4][4];
-#pragma unroll
-  for (int mg = 0; mg < 2; ++mg)
-#pragma unroll
-    for (int ng = 0; ng < 4; ++ng)
-#pragma unroll
-      for (int r = 0; r < 4; ++r) isum[mg][ng][r] = 0;
-  if constexpr (TYPE == TYPE_Q4_K) {
-    Q4KHeader hd[2][2];
-#pragma unroll
-    for (int mg = 0; mg < 2; ++mg)
-#pragma unroll
-      for (int h = 0; h < 2; ++h)
-        hd[mg][h] = q4k_header(*reinterpret_cast<const uint4*>(unit + (16 * mg + 8 * h + g) * 16));
-#pragma unroll
-    for (int pp = 0; pp < 4; ++pp) {
-      uint32_t w[2][4];  // [mg][row g low word, row g+8 low word, row g high word, row g+8 high word]
-#pragma unroll
-      for (int mg = 0; mg < 2; ++mg) {
-        w[mg][0] = lds32(unit + (1 + 2 * pp) * 512 + (16 * mg + g) * 16 + 4 * t);
-        w[mg][1] = lds32(unit + (1 + 2 * pp) * 512 + (16 * mg + g + 8) * 16 + 4 * t);
-        w[mg][2] = lds32(unit + (2 + 2 * pp) * 512 + (16 * mg + g) * 16 + 4 * t);
-        w[mg][3] = lds32(unit + (2 + 2 * pp) * 512 + (16 * mg + g + 8) * 16 + 4 * t);
-      }
-#pragma unroll
-      for (int ng = 0; ng < 4; ++ng) {
-        const uint8_t* rec = act + (8 * ng + g) * REC + 64 * pp + 4 * t;
-        const uint32_t bl0 = lds32(rec), bl1 = lds32(rec + 16), bh0 = lds32(rec + 32), bh1 = lds32(rec + 48);
-#pragma unroll
-        for (int mg = 0; mg < 2; ++mg) {
-          int clo[4], chi[4];
-          mma_k32(clo, w[mg][0] & 0x0f0f0f0fu, w[mg][1] & 0x0f0f0f0fu, w[mg][2] & 0x0f0f0f0fu,
-                  w[mg][3] & 0x0f0f0f0fu, bl0, bl1);
-          mma_k32(chi, (w[mg][0] >> 4) & 0x0f0f0f0fu, (w[mg][1] >> 4) & 0x0f0f0f0fu, (w[mg][2] >> 4) & 0x0f0f0f0fu,
-                  (w[mg][3] >> 4) & 0x0f0f0f0fu, bh0, bh1);
-#pragma unroll
-          for (int r = 0; r < 4; ++r) {
-            const Q4KHeader& h = hd[mg][r >> 1];
-            isum[mg][ng][r] += h.sc(2 * pp) * clo[r] + h.sc(2 * pp + 1) * chi[r];
-          }
-        }
-      }
-    }
-#pragma unroll
-    for (int ng = 0; ng < 4; ++ng) {
-#pragma unroll
-      for (int cc = 0; cc < 2; ++cc) {
-        const uint8_t* rec = act + (8 * ng + 2 * t + cc) * REC;
-        const uint4 bs = *reinterpret_cast<const uint4*>(rec + Q8A_BS);
-        const float d8 = *reinterpret_cast<const float*>(rec + Q8A_D);
-#pragma unroll
-        for (int mg = 0; mg < 2; ++mg)
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const Q4KHeader& hh = hd[mg][h];
-            int ms = __dp2a_lo(int(bs.x), int(hh.mn_lo), 0);
-            ms = __dp2a_hi(int(bs.y), int(hh.mn_lo), ms);
-            ms = __dp2a_lo(int(bs.z), int(hh.mn_hi), ms);
-            ms = __dp2a_hi(int(bs.w), int(hh.mn_hi), ms);
-            const int r = 2 * h + cc;
-            acc[mg][ng][r] += __fmul_rn(hh.d, d8) * float(isum[mg][ng][r]) - __fmul_rn(hh.dmin, d8) * float(ms);
-          }
-      }
-    }
-  } else {
-    uint32_t scw[2][2][4];
-    float dw[2][2];
-#pragma unroll
-    for (int mg = 0; mg < 2; ++mg)
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int row = 16 * mg + 8 * h + g;
-        const uint4 s4 = *reinterpret_cast<const uint4*>(unit + 12 * 512 + row * 16);
-        scw[mg][h][0] = s4.x;
-        scw[mg][h][1] = s4.y;
-        scw[mg][h][2] = s4.z;
-        scw[mg][h][3] = s4.w;
-        dw[mg][h] = f16_bits_to_f32(reinterpret_cast<const uint16_t*>(unit + Q6K_DPLANE_OFFSET)[row]);
-      }
-#pragma unroll
-    for (int s = 0; s < 8; ++s) {
-      uint32_t ua[2][2], ub[2][2];  // [mg][row g, row g+8]
-#pragma unroll
-      for (int mg = 0; mg < 2; ++mg)
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int row = 16 * mg + 8 * h + g;
-          const uint32_t nw = lds32(unit + s * 512 + row * 16 + 4 * t);
-          const uint32_t hw = lds32(unit + (8 + (s >> 1)) * 512 + row * 16 + 4 * (2 * (s & 1) + (t >> 1)));
-          q6k_unpack(nw, hw, t & 1, ua[mg][h], ub[mg][h]);
-        }
-#pragma unroll
-      for (int ng = 0; ng < 4; ++ng) {
-        const uint8_t* rec = act + (8 * ng + g) * REC + 4 * t;
-        const uint32_t ba = lds32(rec + 16 * s), bb = lds32(rec + 16 * (s + 8));
-#pragma unroll
-        for (int mg = 0; mg < 2; ++mg) {
-          int ca[4], cb[4];
-          mma_k16(ca, ua[mg][0], ua[mg][1], ba);
-          mma_k16(cb, ub[mg][0], ub[mg][1], bb);
-#pragma unroll
-          for (int r = 0; r < 4; ++r) {
-            const uint32_t* sw = scw[mg][r >> 1];
-            const int sa = int(int8_t((sw[s >> 2] >> (8 * (s & 3))) & 0xff));
-            const int sb = int(int8_t((sw[(s + 8) >> 2] >> (8 * ((s + 8) & 3))) & 0xff));
-            isum[mg][ng][r] += sa * ca[r] + sb * cb[r];
-          }
-        }
-      }
-    }
-#pragma unroll
-    for (int ng = 0; ng < 4; ++ng) {
-#pragma unroll
-      for (int cc = 0; cc < 2; ++cc) {
-        const uint8_t* rec = act + (8 * ng + 2 * t + cc) * REC;
-        const uint4 b0 = *reinterpret_cast<const uint4*>(rec + Q8B_BS);
-        const uint4 b1 = *reinterpret_cast<const uint4*>(rec + Q8B_BS + 16);
-        const float d8 = *reinterpret_cast<const float*>(rec + Q8B_D);
-#pragma unroll
-        for (int mg = 0; mg < 2; ++mg)
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const uint32_t* sw = scw[mg][h];
-            int corr = __dp2a_lo(int(b0.x), int(sw[0]), 0);
-            corr = __dp2a_hi(int(b0.y), int(sw[0]), corr);
-            corr = __dp2a_lo(int(b0.z), int(sw[1]), corr);
-            corr = __dp2a_hi(int(b0.w), int(sw[1]), corr);
-            corr = __dp2a_lo(int(b1.x), int(sw[2]), corr);
-            corr = __dp2a_hi(int(b1.y), int(sw[2]), corr);
-            corr = __dp2a_lo(int(b1.z), int(sw[3]), corr);
-            corr = __dp2a_hi(int(b1.w), int(sw[3]), corr);
-            const int r = 2 * h + cc;
-            acc[mg][ng][r] += __fmul_rn(dw[mg][h], d8) * float(isum[mg][ng][r] - 32 * corr);
-          }
-      }
-    }
-  }
-}
 
 template <int TYPE>
 __global__ void __launch_bounds__(TC_THREADS, 2) gemm_tc_kernel(const __grid_constant__ TcParams p) {
@@ -252,7 +91,7 @@ __global__ void __launch_bounds__(TC_THREADS, 2) gemm_tc_kernel(const __grid_con
     }
     __syncthreads();
     const uint8_t* st = smem + (b & 1) * T::STAGE;
-    tc_block<TYPE>(st + wt * T::UB, st + TC_TILES * T::UB + (32 * wh) * T::REC, acc, g, t);
+    tc_block<TYPE, 4>(st + wt * T::UB, st + TC_TILES * T::UB + (32 * wh) * T::REC, T::REC, acc, g, t);
     __syncthreads();  // every warp is done with this stage before it is refilled
   }
   const int tile = tile0 + wt;

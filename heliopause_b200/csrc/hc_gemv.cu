@@ -324,12 +324,14 @@ int sm_count() {
   return sms;
 }
 
-int persistent_grid(int items, int cap) {
-  const int warps_cap = cap * GEMV_WARPS_PER_CTA;
+int persistent_grid_w(int items, int cap, int warps_per_cta) {
+  const int warps_cap = cap * warps_per_cta;
   const int per = (items + warps_cap - 1) / warps_cap;                   // items per warp
   const int warps = (items + per - 1) / per;                             // warps needed
-  return (warps + GEMV_WARPS_PER_CTA - 1) / GEMV_WARPS_PER_CTA;
+  return (warps + warps_per_cta - 1) / warps_per_cta;
 }
+
+int persistent_grid(int items, int cap) { return persistent_grid_w(items, cap, GEMV_WARPS_PER_CTA); }
 
 static int ctas_per_sm(const GemvParams& p) { return p.q4small ? GEMV_CTAS_PER_SM_Q4 : GEMV_CTAS_PER_SM; }
 

@@ -50,6 +50,7 @@ struct GemvParams {
   int q4small;      // 1: every weight is Q4_K and ncols <= 2 (Q4_K-sized register buffers, 4 CTAs per SM)
   int pre;          // streaming mode, one item per warp: units 1..pre of the item are copied into shared
                     // memory before the wait for the previous kernel (0: only unit 0, into registers)
+  int ring;         // tensor-core GEMV (hc_gemv_mma.cu): weight-unit slots per warp
   int* err;         // device status word (bounded-wait timeouts)
   Q8Buf q;
   GemvPrologue pro; // mode != NONE: activations computed by every CTA instead of read from q
@@ -108,11 +109,16 @@ int sm_count();
 // Persistent grid over `items` items, one warp per item at a time: the fewest
 // CTAs (<= cap) that give every warp the same number of items.
 int persistent_grid(int items, int cap);
+int persistent_grid_w(int items, int cap, int warps_per_cta);
 cudaError_t launch_gemv(const GemvParams& p, cudaStream_t stream);
 
 // Inputs of at least TC_MIN_COLS columns go to the tensor-core matmul
 // (hc_gemm_tc.cu), one launch per weight covering every column.
 constexpr int TC_MIN_COLS = 16;
+// Inputs of GEMV_MMA_MIN_COLS .. 8 columns go to the tensor-core GEMV
+// (hc_gemv_mma.cu); fewer to the dp4a GEMV.
+constexpr int GEMV_MMA_MIN_COLS = 3;
+cudaError_t launch_gemv_mma(GemvParams& p, cudaStream_t stream);
 cudaError_t launch_gemm_tc(const GemvSeg& seg, int nb, const Q8Buf& q, int col0, int ncols, cudaStream_t st);
 
 }  // namespace hc

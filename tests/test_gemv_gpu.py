@@ -105,6 +105,11 @@ def _oracle_matmul(oracle, type_id, w, x, k, rows, cols):
     (syn.Q6_K, 16384, 2048, 8),
     (syn.Q6_K, 2048, 520, 2),
     (syn.Q6_K, 512, 33, 9),
+    # tensor-core GEMV (3..8 columns): persistent, in-CTA and cluster splits
+    (syn.Q6_K, 16384, 2048, 5),    # verify-width down projection
+    (syn.Q4_K, 256, 7, 3),         # one block, one ragged tile
+    (syn.Q6_K, 768, 100, 6),
+    (syn.Q4_K, 4096, 65, 7),
     # tensor-core path (>= 16 columns)
     (syn.Q4_K, 2048, 2048, 64),
     (syn.Q4_K, 768, 100, 70),      # ragged rows and columns
@@ -126,7 +131,7 @@ def test_matmul_matches_oracle(oracle, type_id, k, rows, cols):
     print(f"outputs needing the re-association term: {n_reassoc} of {got.size}")
 
 
-@pytest.mark.parametrize("cols", [1, 2, 4, 8])
+@pytest.mark.parametrize("cols", [1, 2, 4, 5, 8])
 def test_multi_projection_config2(oracle, cols):
     k = 2048
     specs = [("Q", syn.Q4_K, 2048), ("K", syn.Q4_K, 512), ("V", syn.Q6_K, 512), ("gate", syn.Q4_K, 16384),
