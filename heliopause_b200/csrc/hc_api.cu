@@ -452,9 +452,14 @@ static int lm_head_check(hpc_weight h, size_t input_size, size_t column_count, s
 static size_t tc_chunks(hpc_weight h) { return (h->row_count + hc::LOGITS_CHUNK_ROWS - 1) / hc::LOGITS_CHUNK_ROWS; }
 static size_t tc_logits_bytes(hpc_weight h, size_t cols) { return (cols * h->row_count * sizeof(float) + 255) / 256 * 256; }
 
+// Inputs of GEMV_MMA_MIN_COLS .. 8 columns: the tensor-core LM head + top-k,
+// one list per CTA of its persistent grid.
+static bool lm_head_mma(size_t cols) { return cols >= size_t(gemv_mma_min_cols()) && cols <= 8; }
+
 static size_t cand_bytes_for(hpc_weight h, size_t cols, size_t k) {
   if (cols >= size_t(hc::TC_MIN_COLS)) return tc_logits_bytes(h, cols) + tc_chunks(h) * k * cols * sizeof(uint64_t);
   const int tiles = int(h->rows_pad / hc::TILE);
+  if (lm_head_mma(cols)) return size_t(hc::lmhead_mma_grid(tiles)) * k * cols * sizeof(uint64_t);
   return size_t(hc::lmhead_grid(tiles)) * hc::LMHEAD_LISTS * k * cols * sizeof(uint64_t);
 }
 
@@ -521,8 +526,19 @@ int hpc_lm_head_topk_q8(hpc_weight h, const void* d_workspace, size_t workspace_
   P.k = int(k);
   P.id_offset = id_offset;
   P.cand = static_cast<uint64_t*>(d_candidates);
-  P.cand_col_stride = size_t(grid) * hc::LMHEAD_LISTS * k;
   const int cols = int(column_count);
+  if (lm_head_mma(column_count)) {
+    const int mgrid = hc::lmhead_mma_grid(tiles);
+    P.cand_col_stride = size_t(mgrid) * k;
+    P.g.col0 = 0;
+    P.g.ncols = cols;
+    HPC_CK(hc::launch_lmhead_mma(P, mgrid, st), "tensor-core lm head launch");
+    HPC_CK(hc::launch_topk_merge(P.cand, mgrid * int(k), P.cand_col_stride, int(k), k, cols, int(k), softcap, d_ids,
+                                 d_vals, d_keys, st),
+           "top-k merge launch");
+    return HPC_OK;
+  }
+  P.cand_col_stride = size_t(grid) * hc::LMHEAD_LISTS * k;
   for (int c0 = 0; c0 < cols; c0 += 8) {
     P.g.col0 = c0;
     P.g.ncols = cols - c0 < 8 ? cols - c0 : 8;

@@ -183,6 +183,7 @@ __global__ void norm_quant_kernel(const float* x, float* x_out, const float* __r
 // softmax (max, sum of f64 exp) and the partial output p*v are written for
 // the combine kernel.
 constexpr int ATT_KSTRIDE = 256 + 4;        // floats per staged K row
+constexpr int ATT_QB = 8;                   // queries per thread per pass (scores and outputs)
 
 // One warp: QK-norm (f64 sum of squares, layers.ts:871-885 normHeads) of a
 // 256-vector held 8 values per lane (lane L: dimensions 8L..8L+7), optional
@@ -232,6 +233,7 @@ __device__ __forceinline__ void load_rope8(const double* cos_row, const double* 
   }
 }
 
+template <bool WIDE>
 __global__ void __launch_bounds__(ATT_THREADS) attn_partial_kernel(
     const float* __restrict__ q, const float* __restrict__ kraw, const float* __restrict__ vraw,
     const float* __restrict__ qnw, const float* __restrict__ knw, const double* __restrict__ cos_t,
@@ -333,24 +335,63 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_partial_kernel(
     }
   }
   __syncthreads();
-  // scores: thread per (query, token); a warp shares the query (broadcast
-  // reads) and walks 32 padded K rows
-  for (int pr = threadIdx.x; pr < NQ * CH; pr += blockDim.x) {
-    const int qi = pr / CH, t = pr % CH;
-    const float4* qv = reinterpret_cast<const float4*>(qs + qi * HD);
-    const float4* kv = reinterpret_cast<const float4*>(ks + t * ATT_KSTRIDE);
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  // scores.  One KV head's query vectors for one token (NQ <= 4): thread per
+  // (query, token); a warp shares the query (broadcast reads) and walks 32
+  // padded K rows.  Wider steps: thread (token t = tid % CH, query lane qg =
+  // tid / CH) computes the dots of queries qg, qg + QL, ... (up to ATT_QB
+  // per pass) with token t, so each 16-byte piece of its K row is read once
+  // for all of them.  Both forms keep the same order inside a dot (four lanes
+  // of partial sums, then (x + y) + (z + w)), so a dot does not depend on how
+  // many tokens the step carries.
+  if (!WIDE) {
+    for (int pr = threadIdx.x; pr < NQ * CH; pr += blockDim.x) {
+      const int qi = pr / CH, t = pr % CH;
+      const float4* qv = reinterpret_cast<const float4*>(qs + qi * HD);
+      const float4* kv = reinterpret_cast<const float4*>(ks + t * ATT_KSTRIDE);
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll 16
-    for (int j = 0; j < HD / 4; ++j) {
-      const float4 a = qv[j], b = kv[j];
-      acc.x = fmaf(a.x, b.x, acc.x);
-      acc.y = fmaf(a.y, b.y, acc.y);
-      acc.z = fmaf(a.z, b.z, acc.z);
-      acc.w = fmaf(a.w, b.w, acc.w);
+      for (int j = 0; j < HD / 4; ++j) {
+        const float4 a = qv[j], b = kv[j];
+        acc.x = fmaf(a.x, b.x, acc.x);
+        acc.y = fmaf(a.y, b.y, acc.y);
+        acc.z = fmaf(a.z, b.z, acc.z);
+        acc.w = fmaf(a.w, b.w, acc.w);
+      }
+      const float dot = (acc.x + acc.y) + (acc.z + acc.w);
+      const int m = qi / G;
+      ps[pr] = (t < nt && t0 + t <= pos[m]) ? dot * scale : -INFINITY;
     }
-    const float dot = (acc.x + acc.y) + (acc.z + acc.w);
-    const int m = qi / G;
-    ps[pr] = (t < nt && t0 + t <= pos[m]) ? dot * scale : -INFINITY;
+  } else {
+    constexpr int QL = ATT_THREADS / CH;  // query lanes
+    const int t = int(threadIdx.x) % CH, qg = int(threadIdx.x) / CH;
+    const float4* kv = reinterpret_cast<const float4*>(ks + t * ATT_KSTRIDE);
+    for (int q0 = qg; q0 < NQ; q0 += QL * ATT_QB) {
+      float4 acc[ATT_QB];
+#pragma unroll
+      for (int u = 0; u < ATT_QB; ++u) acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+      for (int j = 0; j < HD / 4; ++j) {
+        const float4 b = kv[j];
+#pragma unroll
+        for (int u = 0; u < ATT_QB; ++u) {
+          if (q0 + QL * u < NQ) {
+            const float4 a = reinterpret_cast<const float4*>(qs + (q0 + QL * u) * HD)[j];
+            acc[u].x = fmaf(a.x, b.x, acc[u].x);
+            acc[u].y = fmaf(a.y, b.y, acc[u].y);
+            acc[u].z = fmaf(a.z, b.z, acc[u].z);
+            acc[u].w = fmaf(a.w, b.w, acc[u].w);
+          }
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < ATT_QB; ++u) {
+        const int qi = q0 + QL * u;
+        if (qi < NQ) {
+          const float dot = (acc[u].x + acc[u].y) + (acc[u].z + acc[u].w);
+          ps[qi * CH + t] = (t < nt && t0 + t <= pos[qi / G]) ? dot * scale : -INFINITY;
+        }
+      }
+    }
   }
   __syncthreads();
   // local softmax: warp per query
@@ -376,10 +417,10 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_partial_kernel(
   }
   __syncthreads();
   // partial outputs: thread d walks column d of the staged V rows (a warp
-  // reads 32 consecutive floats of a row) and serves four queries per pass;
-  // the probabilities are broadcast reads
+  // reads 32 consecutive floats of a row) and serves four queries per pass
+  // (NQ <= 4) or ATT_QB (wider steps); the probabilities are broadcast reads
   const int d = threadIdx.x;
-  for (int qg = 0; qg < NQ; qg += 4) {
+  if (!WIDE) {
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll 4
     for (int j = 0; j < CH / 4; ++j) {
@@ -387,6 +428,27 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_partial_kernel(
                           vs[(4 * j + 2) * ATT_KSTRIDE + d], vs[(4 * j + 3) * ATT_KSTRIDE + d]};
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
+        if (u < NQ) {
+          const float4 a = reinterpret_cast<const float4*>(ps + u * CH)[j];
+          acc[u] += a.x * b[0] + a.y * b[1] + a.z * b[2] + a.w * b[3];
+        }
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      if (u < NQ) part_o[((size_t(chunk) * KVH + kvh) * NQ + u) * HD + d] = acc[u];
+    return;
+  }
+  for (int qg = 0; qg < NQ; qg += ATT_QB) {
+    float acc[ATT_QB];
+#pragma unroll
+    for (int u = 0; u < ATT_QB; ++u) acc[u] = 0.f;
+#pragma unroll 2
+    for (int j = 0; j < CH / 4; ++j) {
+      const float b[4] = {vs[(4 * j) * ATT_KSTRIDE + d], vs[(4 * j + 1) * ATT_KSTRIDE + d],
+                          vs[(4 * j + 2) * ATT_KSTRIDE + d], vs[(4 * j + 3) * ATT_KSTRIDE + d]};
+#pragma unroll
+      for (int u = 0; u < ATT_QB; ++u) {
         if (qg + u < NQ) {
           const float4 a = reinterpret_cast<const float4*>(ps + (qg + u) * CH)[j];
           acc[u] += a.x * b[0] + a.y * b[1] + a.z * b[2] + a.w * b[3];
@@ -394,7 +456,7 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_partial_kernel(
       }
     }
 #pragma unroll
-    for (int u = 0; u < 4; ++u)
+    for (int u = 0; u < ATT_QB; ++u)
       if (qg + u < NQ) part_o[((size_t(chunk) * KVH + kvh) * NQ + qg + u) * HD + d] = acc[u];
   }
 }
@@ -710,17 +772,26 @@ cudaError_t launch_attention(const float* q, const float* kraw, const float* vra
   const size_t smem = attn_smem_bytes(M, H, KVH);
   static bool attr = false;
   if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(attn_partial_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
-    if (e != cudaSuccess) return e;
-    // maximal shared-memory carveout: the SMs still running the QKV GEMV's
-    // CTAs can take an attention CTA (~140 KB) without draining first
-    // (measured: decode +1.6%; the GEMVs keep the default split)
-    use_max_carveout(reinterpret_cast<const void*>(attn_partial_kernel));
+    for (const void* fn : {reinterpret_cast<const void*>(attn_partial_kernel<false>),
+                           reinterpret_cast<const void*>(attn_partial_kernel<true>)}) {
+      cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
+      if (e != cudaSuccess) return e;
+      // maximal shared-memory carveout: the SMs still running the QKV GEMV's
+      // CTAs can take an attention CTA (~140 KB) without draining first
+      // (measured: decode +1.6%; the GEMVs keep the default split)
+      use_max_carveout(fn);
+    }
     attr = true;
   }
   const int chunks = cap / ATT_CHUNK;
-  return pdl_launch(attn_partial_kernel, dim3(chunks, KVH), dim3(ATT_THREADS), smem, st, q, kraw, vraw, qnw, knw, cos_t,
-                    sin_t, eps, int(own_kv), kc, vc, pos, M, H, KVH, cap, scale, part_m, part_l, part_o, err);
+  // more than four query vectors per KV head: the register-blocked form
+  if (M * (H / KVH) > ATT_THREADS / ATT_CHUNK)
+    return pdl_launch(attn_partial_kernel<true>, dim3(chunks, KVH), dim3(ATT_THREADS), smem, st, q, kraw, vraw, qnw,
+                      knw, cos_t, sin_t, eps, int(own_kv), kc, vc, pos, M, H, KVH, cap, scale, part_m, part_l, part_o,
+                      err);
+  return pdl_launch(attn_partial_kernel<false>, dim3(chunks, KVH), dim3(ATT_THREADS), smem, st, q, kraw, vraw, qnw,
+                    knw, cos_t, sin_t, eps, int(own_kv), kc, vc, pos, M, H, KVH, cap, scale, part_m, part_l, part_o,
+                    err);
 }
 
 cudaError_t launch_attn_combine(const float* part_m, const float* part_l, const float* part_o, const int32_t* pos,

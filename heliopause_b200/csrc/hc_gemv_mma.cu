@@ -37,12 +37,12 @@
 #include "hc_gemv_body.cuh"
 #include "hc_kernels.cuh"
 #include "hc_mma.cuh"
+#include "hc_mma_stream.cuh"
 
 namespace cg = cooperative_groups;
 
 namespace hc {
 
-constexpr int GM_COLS = 8;
 constexpr int GM_MAX_RING = 4;
 constexpr int GM_MIN_RING = 2;
 constexpr int GM_MAX_CLUSTER = 8;
@@ -54,23 +54,6 @@ struct GmShape {
   static constexpr int CTAS = W == 8 ? 2 : 3;
   static constexpr size_t STATIC_SMEM = size_t(W + GM_MAX_CLUSTER) * GM_COLS * 32 * 4 + (W * GM_MAX_RING + 1) * 8 + 64;
 };
-
-// Column stride of the activation slice: nblk records plus 16 bytes, so the
-// eight columns' B-fragment words fall in distinct banks.
-__host__ __device__ inline int gm_col_stride(int nblk, int rec) { return nblk * rec + 16; }
-
-__host__ __device__ inline size_t gm_act_bytes(const GemvParams& p, int nblk) {
-  bool a, b;
-  gemv_planes(p, &a, &b);
-  const size_t s = size_t(GM_COLS) * ((a ? gm_col_stride(nblk, Q8A_REC) : 0) + (b ? gm_col_stride(nblk, Q8B_REC) : 0));
-  return (s + 15) / 16 * 16;
-}
-
-__host__ __device__ inline int gm_slot_bytes(const GemvParams& p) {
-  bool a, b;
-  gemv_planes(p, &a, &b);
-  return unit_bytes(b ? TYPE_Q6_K : TYPE_Q4_K);
-}
 
 template <int GM_WARPS>
 __global__ void __launch_bounds__(GmShape<GM_WARPS>::THREADS, GmShape<GM_WARPS>::CTAS)
@@ -104,107 +87,34 @@ __global__ void __launch_bounds__(GmShape<GM_WARPS>::THREADS, GmShape<GM_WARPS>:
   const int cs_a = gm_col_stride(nblk, Q8A_REC), cs_b = gm_col_stride(nblk, Q8B_REC);
   uint8_t* act_a = need_a ? smem : nullptr;
   uint8_t* act_b = need_b ? smem + (need_a ? size_t(GM_COLS) * cs_a : 0) : nullptr;
-  const int slot = gm_slot_bytes(p), R = p.ring;
-  uint8_t* ring = smem + gm_act_bytes(p, nblk) + size_t(warp) * R * slot;
-  uint64_t* wb = bars[warp];
-
-  // This warp's unit stream: unit u is block u % bps of item item0 + (u / bps) * istride.
-  // The units of one item are contiguous (a tile's blocks follow each other),
-  // so an item is its first unit's address and its type.
-  const int n = item0 < nitems ? ((nitems - 1 - item0) / istride + 1) * p.bps : 0;
-  struct ItemRef {
-    const uint8_t* base;
-    int type;
-  };
-  auto item_ref = [&](int item) {
-    ItemRef r;
-    r.base = unit_addr(p, item, 0, &r.type);
-    return r;
-  };
-  ItemRef iss = item_ref(item0 < nitems ? item0 : 0);  // lane 0's issue cursor
-  int iss_item = 0;
-  auto issue = [&](int u) {  // lane 0, in increasing u
-    const int k = u / p.bps;
-    if (k != iss_item) {
-      iss_item = k;
-      iss = item_ref(item0 + k * istride);
-    }
-    const uint32_t ub = uint32_t(unit_bytes(iss.type));
-    uint64_t* b = wb + (u % R);
-    mbar_expect_tx(b, ub);
-    bulk_copy_g2s(ring + size_t(u % R) * slot, iss.base + size_t(u % p.bps) * ub, ub, b);
-  };
-  int issued = n < R ? n : R;
-  if (lane == 0) {
-    for (int s = 0; s < R; ++s) mbar_init(wb + s, 1);
-    for (int u = 0; u < issued; ++u) issue(u);
-  }
-  __syncwarp();
+  const int slot = gm_slot_bytes(p);
+  MmaStream ms(p, item0, istride, nitems, smem + gm_act_bytes(p, nblk) + size_t(warp) * p.ring * slot, slot,
+               bars[warp], lane);
+  ms.prime();
 #if __CUDA_ARCH__ >= 900
   asm volatile("griddepcontrol.wait;" ::: "memory");
 #endif
-  // Activation slice: columns col0 .. col0 + 7 (clamped to the last real
-  // column), blocks [kb0, kb0 + nblk), one bulk copy per column and plane.
-  if (threadIdx.x == 0) {
-    const uint32_t per_col = uint32_t(nblk) * uint32_t((need_a ? Q8A_REC : 0) + (need_b ? Q8B_REC : 0));
-    mbar_init(&act_bar, 1);
-    mbar_expect_tx(&act_bar, per_col * GM_COLS);
-    for (int c = 0; c < GM_COLS; ++c) {
-      const size_t rec0 = size_t(p.col0 + (c < p.ncols ? c : p.ncols - 1)) * p.nb + kb0;
-      if (need_a) bulk_copy_g2s(act_a + size_t(c) * cs_a, p.q.a + rec0 * Q8A_REC, uint32_t(nblk * Q8A_REC), &act_bar);
-      if (need_b) bulk_copy_g2s(act_b + size_t(c) * cs_b, p.q.b + rec0 * Q8B_REC, uint32_t(nblk * Q8B_REC), &act_bar);
-    }
-  }
+  stage_act_slice8(p, act_a, act_b, cs_a, cs_b, kb0, nblk, &act_bar);
   __syncthreads();
   bool ok = mbar_wait_parity(&act_bar, 0, p.err);
-
-  float acc[2][1][4];
+  auto flush = [&](int item, const float (&acc)[2][1][4]) {
+    const int tile = item >> p.split_log2;
 #pragma unroll
-  for (int mg = 0; mg < 2; ++mg)
+    for (int mg = 0; mg < 2; ++mg)
 #pragma unroll
-    for (int r = 0; r < 4; ++r) acc[mg][0][r] = 0.0f;
-  int u = 0, item = item0, j = 0;
-  int ty = n ? item_ref(item0).type : TYPE_Q4_K;
-  for (; ok && u < n; ++u) {
-    if (!mbar_wait_parity_sleep(wb + (u % R), uint32_t(u / R) & 1u, p.err)) {
-      ok = false;
-      break;
-    }
-    const uint8_t* unit = ring + size_t(u % R) * slot;
-    const int jj = (item & (p.split - 1)) * p.bps + j - kb0;  // block inside the CTA's slice
-    if (ty == TYPE_Q4_K) tc_block<TYPE_Q4_K, 1>(unit, act_a + jj * Q8A_REC, cs_a, acc, g, t);
-    else tc_block<TYPE_Q6_K, 1>(unit, act_b + jj * Q8B_REC, cs_b, acc, g, t);
-    __syncwarp();  // every lane has consumed the slot: refill it
-    if (u + R < n) {
-      if (lane == 0) issue(u + R);
-      ++issued;
-    }
-    if (j == p.bps - 1) {
-      const int tile = item >> p.split_log2;
-#pragma unroll
-      for (int mg = 0; mg < 2; ++mg)
-#pragma unroll
-        for (int r = 0; r < 4; ++r) {
-          const int row = 16 * mg + g + 8 * (r >> 1), col = 2 * t + (r & 1);
-          if (p.split == 1) {
-            const GemvSeg& sg = p.seg[seg_of(p, tile)];
-            const int grow = (tile - sg.tile_begin) * TILE + row;
-            if (grow < sg.rows && col < p.ncols) sg.out[size_t(p.col0 + col) * sg.rows + grow] = acc[mg][0][r];
-          } else {
-            red[warp][col][row] = acc[mg][0][r];
-          }
-          acc[mg][0][r] = 0.0f;
+      for (int r = 0; r < 4; ++r) {
+        const int row = 16 * mg + g + 8 * (r >> 1), col = 2 * t + (r & 1);
+        if (p.split == 1) {
+          const GemvSeg& sg = p.seg[seg_of(p, tile)];
+          const int grow = (tile - sg.tile_begin) * TILE + row;
+          if (grow < sg.rows && col < p.ncols) sg.out[size_t(p.col0 + col) * sg.rows + grow] = acc[mg][0][r];
+        } else {
+          red[warp][col][row] = acc[mg][0][r];
         }
-      item += istride;
-      j = 0;
-      if (u + 1 < n) ty = item_ref(item).type;
-    } else {
-      ++j;
-    }
-  }
+      }
+  };
+  ok = ms.run(act_a, act_b, cs_a, cs_b, kb0, ok, g, t, flush);
   if (!ok) {
-    // bounded wait for this warp's copies still in flight before the CTA may exit
-    for (; u < issued; ++u) mbar_wait_parity(wb + (u % R), uint32_t(u / R) & 1u, nullptr);
     if (p.split > 1) {
 #pragma unroll
       for (int c = 0; c < GM_COLS; ++c) red[warp][c][lane] = 0.0f;

@@ -23,6 +23,7 @@
 #include "hc_gemv_body.cuh"
 #include "hc_kernels.cuh"
 #include "hc_lmhead.cuh"
+#include "hc_mma_stream.cuh"
 
 namespace hc {
 
@@ -147,6 +148,135 @@ __global__ void __launch_bounds__(GEMV_THREADS, GEMV_CTAS_PER_SM) lmhead_topk_ke
       if (rank < P.k) out[rank] = e;
     }
   }
+}
+
+// Tensor-core LM head for 3..8 columns: the weight stream and block products
+// of the tensor-core GEMV (hc_mma_stream.cuh) over a persistent grid of
+// LMM_WARPS-warp CTAs walking the head's tiles, fused with the same per-warp
+// top-k lists as lmhead_topk_kernel.  A finished tile's 32 x 8 sums go from
+// the accumulator layout to lane = row through a padded shared-memory
+// transpose, then each column's keys are inserted into the warp's list.  The
+// CTA merges its warps' lists by rank into k candidates per column at
+// cand[col * cand_col_stride + blockIdx.x * k].
+constexpr int LMM_WARPS = 8;
+constexpr int LMM_TSTRIDE = 36;  // transpose row stride: conflict-free writes (accumulator layout) and reads
+
+__host__ __device__ inline size_t lmm_list_bytes(const LmHeadParams& P) {
+  return size_t(LMM_WARPS) * P.g.ncols * P.k * sizeof(uint64_t);
+}
+
+__global__ void __launch_bounds__(LMM_WARPS * 32, 1) lmhead_mma_kernel(const __grid_constant__ LmHeadParams P) {
+  const GemvParams& p = P.g;
+  extern __shared__ __align__(16) uint8_t smem[];
+  __shared__ float tr[LMM_WARPS][GM_COLS * LMM_TSTRIDE];
+  __shared__ __align__(8) uint64_t bars[LMM_WARPS][4];
+  __shared__ __align__(8) uint64_t act_bar;
+  const int lane = int(threadIdx.x & 31), warp = int(threadIdx.x >> 5), g = lane >> 2, t = lane & 3;
+#if __CUDA_ARCH__ >= 900
+  asm volatile("griddepcontrol.launch_dependents;");
+#endif
+  const int nitems = p.total_tiles;
+  const int item0 = int(blockIdx.x) * LMM_WARPS + warp, istride = int(gridDim.x) * LMM_WARPS;
+  bool need_a, need_b;
+  gemv_planes(p, &need_a, &need_b);
+  const int cs_a = gm_col_stride(p.nb, Q8A_REC), cs_b = gm_col_stride(p.nb, Q8B_REC);
+  uint8_t* act_a = need_a ? smem : nullptr;
+  uint8_t* act_b = need_b ? smem + (need_a ? size_t(GM_COLS) * cs_a : 0) : nullptr;
+  uint64_t* lists = reinterpret_cast<uint64_t*>(smem + gm_act_bytes(p, p.nb));  // [warp][col][k]
+  const int slot = gm_slot_bytes(p);
+  uint8_t* ring = smem + gm_act_bytes(p, p.nb) + (lmm_list_bytes(P) + 15) / 16 * 16;
+  MmaStream ms(p, item0, istride, nitems, ring + size_t(warp) * p.ring * slot, slot, bars[warp], lane);
+  ms.prime();
+  const int nl = LMM_WARPS * p.ncols * P.k;
+  for (int i = int(threadIdx.x); i < nl; i += int(blockDim.x)) lists[i] = 0ull;
+#if __CUDA_ARCH__ >= 900
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+#endif
+  stage_act_slice8(p, act_a, act_b, cs_a, cs_b, 0, p.nb, &act_bar);
+  __syncthreads();
+  bool ok = mbar_wait_parity(&act_bar, 0, p.err);
+  float* trw = tr[warp];
+  uint64_t* wl = lists + size_t(warp) * p.ncols * P.k;
+  const int rows = p.seg[0].rows;
+  auto flush = [&](int tile, const float (&acc)[2][1][4]) {
+#pragma unroll
+    for (int mg = 0; mg < 2; ++mg)
+#pragma unroll
+      for (int r = 0; r < 4; ++r) trw[(2 * t + (r & 1)) * LMM_TSTRIDE + 16 * mg + g + 8 * (r >> 1)] = acc[mg][0][r];
+    __syncwarp();
+    const int row = tile * TILE + lane;
+    for (int c = 0; c < p.ncols; ++c) {
+      const uint64_t key = row < rows ? topk_key(trw[c * LMM_TSTRIDE + lane], uint32_t(P.id_offset + row)) : 0ull;
+      topk_insert_warp(wl + c * P.k, P.k, key, lane);
+    }
+    __syncwarp();
+  };
+  ms.run(act_a, act_b, cs_a, cs_b, 0, ok, g, t, flush);
+  __syncthreads();
+  // merge the warps' lists by rank (real keys are distinct; empty slots are 0)
+  for (int c = 0; c < p.ncols; ++c) {
+    uint64_t* out = P.cand + size_t(p.col0 + c) * P.cand_col_stride + size_t(blockIdx.x) * P.k;
+    for (int i = int(threadIdx.x); i < P.k; i += int(blockDim.x)) out[i] = 0ull;
+  }
+  __syncthreads();
+  for (int c = 0; c < p.ncols; ++c) {
+    uint64_t* out = P.cand + size_t(p.col0 + c) * P.cand_col_stride + size_t(blockIdx.x) * P.k;
+    for (int x = int(threadIdx.x); x < LMM_WARPS * P.k; x += int(blockDim.x)) {
+      const int w = x / P.k, i = x % P.k;
+      const uint64_t e = lists[(size_t(w) * p.ncols + c) * P.k + i];
+      if (e == 0ull) continue;
+      int rank = i;
+      for (int o = 0; o < LMM_WARPS; ++o) {
+        if (o == w) continue;
+        const uint64_t* lo_list = lists + (size_t(o) * p.ncols + c) * P.k;
+        int lo = 0, hi = P.k;  // first index whose key is <= e
+        while (lo < hi) {
+          const int mid = (lo + hi) >> 1;
+          if (lo_list[mid] > e) lo = mid + 1;
+          else hi = mid;
+        }
+        rank += lo;
+      }
+      if (rank < P.k) out[rank] = e;
+    }
+  }
+}
+
+int lmhead_mma_grid(int ntiles) {
+  const int by_tiles = (ntiles + LMM_WARPS - 1) / LMM_WARPS;
+  return by_tiles < sm_count() ? by_tiles : sm_count();
+}
+
+// Ring depth: as deep as 200 KB of dynamic shared memory allows (2..4).
+static size_t lmm_smem(const LmHeadParams& P, int ring) {
+  return gm_act_bytes(P.g, P.g.nb) + (lmm_list_bytes(P) + 15) / 16 * 16 +
+         size_t(LMM_WARPS) * ring * gm_slot_bytes(P.g);
+}
+
+cudaError_t launch_lmhead_mma(LmHeadParams& P, int grid, cudaStream_t stream) {
+  if (P.g.ncols < 1 || P.g.ncols > GM_COLS || P.g.split != 1 || P.g.bps != P.g.nb) return cudaErrorInvalidValue;
+  int ring = 4;
+  while (ring > 2 && lmm_smem(P, ring) > size_t(GEMV_MAX_SMEM)) --ring;
+  const size_t smem = lmm_smem(P, ring);
+  if (smem > size_t(GEMV_MAX_SMEM)) return cudaErrorInvalidValue;
+  P.g.ring = ring;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(lmhead_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, GEMV_MAX_SMEM);
+    if (e != cudaSuccess) return e;
+    attr_set = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(grid));
+  cfg.blockDim = dim3(LMM_WARPS * 32);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, lmhead_mma_kernel, P);
 }
 
 // Top-k candidates of materialized logits (the tensor-core LM head for wide

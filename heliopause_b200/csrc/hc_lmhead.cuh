@@ -18,6 +18,10 @@ int lmhead_grid(int ntiles);
 // Candidates per CTA per column: the CTA's merged list of k.
 constexpr int LMHEAD_LISTS = 1;
 cudaError_t launch_lmhead_topk(const LmHeadParams& P, int grid, cudaStream_t stream);
+// Tensor-core LM head + top-k for 3..8 columns (one launch, persistent
+// grid of lmhead_mma_grid CTAs, one candidate list per CTA per column).
+int lmhead_mma_grid(int ntiles);
+cudaError_t launch_lmhead_mma(LmHeadParams& P, int grid, cudaStream_t stream);
 // Tensor-core LM head (inputs of >= TC_MIN_COLS columns): the logits are
 // written to scratch by launch_gemm_tc, then reduced to candidates in chunks
 // of LOGITS_CHUNK_ROWS rows per column.

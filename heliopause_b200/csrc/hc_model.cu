@@ -270,9 +270,15 @@ int hpc_model_set_lm_head(hpc_model m, hpc_weight w) {
   if (w->input_size != size_t(m->cfg.hidden) || w->row_count != size_t(m->cfg.vocab))
     return hpc_fail(HPC_ERR_SHAPE, "LM head %zux%zu", w->input_size, w->row_count);
   m->lm_head = w;
+  // the candidate layout depends on the kernel a column count selects, so the
+  // buffer serves the largest need over every token count of a step
   size_t cb = 0;
-  int rc = hpc_lm_head_candidates_bytes(w, size_t(m->cfg.max_tokens), size_t(m->cfg.top_k), &cb);
-  if (rc != HPC_OK) return rc;
+  for (int cols = 1; cols <= m->cfg.max_tokens; ++cols) {
+    size_t need = 0;
+    int rc = hpc_lm_head_candidates_bytes(w, size_t(cols), size_t(m->cfg.top_k), &need);
+    if (rc != HPC_OK) return rc;
+    if (need > cb) cb = need;
+  }
   if (cb > m->cand_bytes) {
     cudaFree(m->cand);
     m->cand = nullptr;

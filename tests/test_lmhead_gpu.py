@@ -49,6 +49,9 @@ def _check_topk(ids, vals, logits, k):
     (syn.Q6_K, 50000, 64, 3),    # ragged last tile, TOPK_MAX
     (syn.Q4_K, 4096, 1, 9),      # greedy (top-1), > 8 columns
     (syn.Q6_K, 40, 40, 1),       # k == rows
+    # tensor-core LM head + top-k (3..8 columns)
+    (syn.Q4_K, 4096, 64, 8),
+    (syn.Q6_K, 100, 10, 4),      # fewer tiles than one CTA's warps
     # tensor-core path (>= 16 columns): materialized logits, chunked lists
     (syn.Q6_K, 20000, 40, 64),   # config-5 width, ragged last chunk
     (syn.Q6_K, 50000, 64, 17),
@@ -98,6 +101,15 @@ def test_ties_prefer_lower_id_and_softcap(oracle):
     finally:
         hk.release_quantized_weight_handle(h)
     assert all(r == list(range(7, 17)) for r in ids.cpu().numpy().tolist())
+    assert np.all(vals.cpu().numpy() == v[0])
+    # and on the tensor-core LM head of 3..8 columns
+    x = np.tile(syn.activations(1, kdim, seed=4), 5)
+    h = hk.create_quantized_weight_handle("Q6_K", w, kdim, rows)
+    try:
+        ids, vals = hk.lm_head_topk(h, torch.from_numpy(x).cuda(), 5, 10, id_offset=3)
+    finally:
+        hk.release_quantized_weight_handle(h)
+    assert all(r == list(range(3, 13)) for r in ids.cpu().numpy().tolist())
     assert np.all(vals.cpu().numpy() == v[0])
 
 
