@@ -365,14 +365,27 @@ class DecodeConfig3:
         toks, rounds, acc = g.generate(first, ctx, n_tokens, n_spec, opt, rng)
         torch.cuda.synchronize()
         dt = _t.perf_counter() - t0
+        # one draft step on its own (device time of the step's graph and copies)
+        kv = [self.model.kv(layer) for layer in g.kv_layers]
+        emb, hid = g.embedding(12345), ctx.current_hidden
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        head.run(emb, hid, kv, ctx.position, 64)
+        a.record()
+        for _ in range(20):
+            head.run(emb, hid, kv, ctx.position, 64)
+        b.record()
+        torch.cuda.synchronize()
+        draft_ms = a.elapsed_time(b) / 20
+        head.close()
         del g, head
         torch.cuda.empty_cache()
         return {"tokens": len(toks), "tok_per_s": len(toks) / dt, "seconds": dt, "rounds": rounds,
                 "accepted_drafts": acc, "acceptance_rate": acc / max(1, rounds * n_spec),
-                "draft_tokens_per_round": n_spec, "context_start": context,
+                "draft_tokens_per_round": n_spec, "context_start": context, "draft_step_ms": draft_ms,
                 "sampling": {"temperature": opt.temperature, "top_k": opt.top_k, "top_p": opt.top_p, "seed": opt.seed},
-                "note": "config 4: random draft-head weights (acceptance near chance); draft head f32 on dequantized "
-                        "weights (cuBLAS GEMV), verify = the fused decoder forward at M=n_spec+1"}
+                "note": "config 4: random draft-head weights (acceptance near chance); draft head = hpc_draft_step "
+                        "(f32 dequantized weights, one CUDA graph per step), verify = the fused decoder forward at "
+                        "M=n_spec+1; tok_per_s is the wall clock of the host loop (host-side sampling per draft)"}
 
     @classmethod
     def cpu_sampler(cls, threads: int):

@@ -51,6 +51,14 @@ SIGNATURES = {
     "hpc_model_kv": (_i, [_vp, _i, C.POINTER(_vp), C.POINTER(_vp)]),
     "hpc_model_forward": (_i, [_vp, _vp, _vp, _sz, _sz, _vp, _vp, _vp, _vp]),
     "hpc_model_prefill": (_i, [_vp, _vp, _vp, _sz, _vp, _vp]),
+    "hpc_draft_create": (_i, [_vp, C.POINTER(_vp)]),
+    "hpc_draft_release": (_i, [_vp]),
+    "hpc_draft_set_matrix": (_i, [_vp, _i, _i, _vp]),
+    "hpc_draft_set_vector": (_i, [_vp, _i, _i, _vp, _sz]),
+    "hpc_draft_set_layer_scale": (_i, [_vp, _i, C.c_float]),
+    "hpc_draft_set_token_ordering": (_i, [_vp, _vp, _sz]),
+    "hpc_draft_set_target_kv": (_i, [_vp, _i, _vp, _vp]),
+    "hpc_draft_step": (_i, [_vp, _vp, _vp, _i, _sz, _vp, _vp, _vp, _vp]),
 }
 
 
@@ -60,6 +68,15 @@ class ModelConfig(C.Structure):
                 ("ffn", C.c_int), ("vocab", C.c_int), ("layers", C.c_int), ("kv_layers", C.c_int),
                 ("context", C.c_int), ("max_tokens", C.c_int), ("top_k", C.c_int), ("rms_eps", C.c_double),
                 ("rope_theta", C.c_double), ("final_logit_softcap", C.c_float)]
+
+
+class DraftConfig(C.Structure):
+    """hpc_draft_config (include/heliocuda.h)."""
+    _fields_ = [("backbone", C.c_int), ("hidden", C.c_int), ("heads", C.c_int), ("kv_heads", C.c_int),
+                ("head_dim", C.c_int), ("ffn", C.c_int), ("vocab", C.c_int), ("n_centroids", C.c_int),
+                ("centroid_top_k", C.c_int), ("layers", C.c_int), ("context", C.c_int), ("max_top_k", C.c_int),
+                ("rms_eps", C.c_double), ("rope_theta", C.c_double)]
+
 
 _lib = None
 

@@ -19,13 +19,14 @@ runner, runner/webgpu/mtp-assistant-runner.ts, computes the same in f32):
              centroid_top_k centroids select token ids through token_ordering,
              scored by their embedding rows . h (value desc, id asc).
 
-All matmuls are f32 products of dequantized weights with f32 inputs, as
-hp_matmul_dequantized_f32 (lib.rs:103-154) / the WebGPU F32 matmul do.  The
-weights are dequantized once by the library's bit-exact dequantization
-(hpc_weight_dequantize) and multiplied with cuBLAS f32 GEMV; the norms,
-RoPE, attention softmax (f64 exp, f16-rounded query) and GELU follow the
-reference's rounding points.  Summation orders differ from the reference's
-sequential loops, so outputs agree to f32 rounding.
+The step runs in the library (hpc_draft_step, csrc/hc_draft.cu: one CUDA
+graph of its own kernels).  All matmuls are f32 products of dequantized
+weights with f32 inputs, as hp_matmul_dequantized_f32 (lib.rs:103-154) / the
+WebGPU F32 matmul do: each matrix is dequantized once by the library's
+bit-exact dequantization into f32 rows.  The norms, RoPE, attention softmax
+(f64 exp, f32 query) and GELU follow the reference's rounding points.
+Summation orders differ from the reference's sequential loops, so outputs
+agree to f32 rounding.
 
 The loop (mtp_generate) restates generateAssistantWithMtp
 (packages/engine/src/chat.ts:692-776) with proposeMtpDraft
@@ -137,127 +138,114 @@ def _rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
     return ((x.double() * scale).float().double() * w.double()).float()
 
 
-def _rope_partial(q: torch.Tensor, position: int, n_dims: int, pairs: int, theta_base: float) -> torch.Tensor:
-    """ropeNeox with activePairCount (mtp-assistant-runner.ts:361-387): the
-    first `pairs` pairs (i, i + n_dims/2) of every head rotated; theta chain
-    in f32, cos/sin in f64."""
-    out = q.clone()
-    scale = theta_base ** (-2.0 / n_dims)
-    theta = float(position)
-    angles = []
-    for _ in range(pairs):
-        angles.append(theta)
-        theta = float(np.float32(theta * scale))
-    t = torch.tensor(angles, dtype=torch.float64, device=q.device)
-    c, s = torch.cos(t), torch.sin(t)
-    half = n_dims // 2
-    x0, x1 = q[:, :pairs].double(), q[:, half:half + pairs].double()
-    out[:, :pairs] = (x0 * c).float() - (x1 * s).float()
-    out[:, half:half + pairs] = (x0 * s).float() + (x1 * c).float()
-    return out
+# draft matrix / vector names -> library ids (include/heliocuda.h HPC_DW_* / HPC_DN_*)
+_DW = {"mtp.pre_projection.weight": 100, "mtp.post_projection.weight": 101, "mtp.centroids.weight": 102,
+       "token_embd.weight": 103, "attn_q.weight": 0, "attn_output.weight": 1, "ffn_gate.weight": 2,
+       "ffn_up.weight": 3, "ffn_down.weight": 4}
+_DN = {"output_norm.weight": 100, "attn_norm.weight": 0, "attn_q_norm.weight": 1, "post_attention_norm.weight": 2,
+       "ffn_norm.weight": 3, "post_ffw_norm.weight": 4}
+DRAFT_CONTEXT = 4096  # positions the draft head accepts (the target's context may be smaller)
 
 
-def _gelu(v: torch.Tensor) -> torch.Tensor:
-    """gelu (mtp-assistant-runner.ts:399-411): tanh form, f32 rounding
-    points, no f16 round trip."""
-    x = v.double()
-    f = lambda t: t.float().double()
-    inner = f(f(math.sqrt(2 / math.pi) * x) * f(1 + f(0.044715 * f(x * x))))
-    out = f(f(0.5 * x) * f(1 + torch.tanh(inner)))
-    out = torch.where(x <= -10, torch.zeros_like(out), out)
-    out = torch.where(x >= 10, x, out)
-    return out.float()
-
-
-def _top_desc_id_asc(values: torch.Tensor, ids: torch.Tensor, k: int):
-    """topK ordering (runtime.ts:514-527) on the device: value descending,
-    id ascending among equal values.  `ids` must be ascending."""
-    order = torch.sort(values, descending=True, stable=True).indices[:k]
-    return ids[order], values[order]
+def _split_name(name: str) -> tuple[int, str]:
+    """'blk.{layer}.{rest}' -> (layer, rest); head-wide names -> (0, name)."""
+    if name.startswith("blk."):
+        _, layer, rest = name.split(".", 2)
+        return int(layer), rest
+    return 0, name
 
 
 class CudaMtpDraftHead:
-    """The draft head resident on the current CUDA device (f32 weights)."""
+    """The draft head resident on the current CUDA device (hpc_draft_*): each
+    matrix dequantized once into f32 rows, one step per CUDA graph."""
 
-    def __init__(self, shape: MtpDraftShape, weights: SyntheticDraftWeights, *, gpu_seed: int | None = None):
+    def __init__(self, shape: MtpDraftShape, weights: SyntheticDraftWeights, *, gpu_seed: int | None = None,
+                 max_top_k: int = 64):
         """gpu_seed: generate the quantized matrices on the device (same
         distributions, for benchmark-size heads) instead of weights.matrix."""
+        import ctypes as C
+
+        from . import _lib
         self.s = shape
-        self.w = {}
-        gen_ = None
-        if gpu_seed is not None:
-            from .model import gpu_synthetic_weight
-            gen_ = torch.Generator(device="cuda")
-            gen_.manual_seed(gpu_seed)
-        for name, (t, k, n) in shape.matrices().items():
-            data = weights.matrix(name) if gen_ is None else gpu_synthetic_weight(t, n, k, gen_)
-            h = hk.create_quantized_weight_handle("Q4_K" if t == syn.Q4_K else "Q6_K", data, k, n)
-            try:
-                self.w[name] = hk.dequantize_resident(h).reshape(n, k)
-            finally:
-                hk.release_quantized_weight_handle(h)
-        self.v = {name: torch.from_numpy(weights.vector(name)).cuda() for name in shape.vectors()}
-        self.scale = [weights.layer_output_scale(layer) for layer in range(shape.layers)]
-        order = torch.from_numpy(weights.token_ordering()).cuda().long()
-        per = shape.vocab // shape.n_centroids
-        # token_ordering slot c*per .. (c+1)*per-1 lists centroid c's tokens
-        self.centroid_tokens = order[:shape.n_centroids * per].view(shape.n_centroids, per)
-        self.centroid_ids = torch.arange(shape.n_centroids, device="cuda")
+        self._C, self._L = C, _lib.lib()
+        self.max_top_k = max_top_k
+        cfg = _lib.DraftConfig(shape.backbone, shape.hidden, shape.heads, shape.kv_heads, shape.head_dim, shape.ffn,
+                               shape.vocab, shape.n_centroids, shape.centroid_top_k, shape.layers, DRAFT_CONTEXT,
+                               max_top_k, shape.rms_eps, shape.rope_theta)
+        h = C.c_void_p()
+        hk.assert_cuda_ok(self._L.hpc_draft_create(C.byref(cfg), C.byref(h)), "draftCreate")
+        self._h = h
+        try:
+            gen_ = None
+            if gpu_seed is not None:
+                from .model import gpu_synthetic_weight
+                gen_ = torch.Generator(device="cuda")
+                gen_.manual_seed(gpu_seed)
+            for name, (t, k, n) in shape.matrices().items():
+                data = weights.matrix(name) if gen_ is None else gpu_synthetic_weight(t, n, k, gen_)
+                wh = hk.create_quantized_weight_handle("Q4_K" if t == syn.Q4_K else "Q6_K", data, k, n)
+                try:
+                    layer, rest = _split_name(name)
+                    hk.assert_cuda_ok(self._L.hpc_draft_set_matrix(self._h, _DW[rest], layer, wh.handle),
+                                      f"draftSetMatrix {name}")
+                finally:
+                    hk.release_quantized_weight_handle(wh)
+            for name in shape.vectors():
+                v = np.ascontiguousarray(weights.vector(name), np.float32)
+                layer, rest = _split_name(name)
+                hk.assert_cuda_ok(self._L.hpc_draft_set_vector(self._h, _DN[rest], layer, v.ctypes.data, v.size),
+                                  f"draftSetVector {name}")
+            for layer in range(shape.layers):
+                hk.assert_cuda_ok(self._L.hpc_draft_set_layer_scale(self._h, layer,
+                                                                    C.c_float(weights.layer_output_scale(layer))),
+                                  "draftSetLayerScale")
+            order = np.ascontiguousarray(weights.token_ordering(), np.int32)
+            hk.assert_cuda_ok(self._L.hpc_draft_set_token_ordering(self._h, order.ctypes.data, order.size),
+                              "draftSetTokenOrdering")
+        except Exception:
+            self.close()
+            raise
+        self._kv_keep = []
+        self.post = torch.empty(shape.backbone, device="cuda")
+        self.ids = torch.empty(max_top_k, dtype=torch.int32, device="cuda")
+        self.vals = torch.empty(max_top_k, device="cuda")
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            self._L.hpc_draft_release(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
     def run(self, target_embedding: torch.Tensor, target_hidden: torch.Tensor, kv, position: int, top_k: int):
-        """One draft step: (backbone hidden [backbone], ids, logits [top_k],
-        both on the device).  kv[layer] = (K [context][kv_heads][head_dim],
-        V in the reference orientation [head_dim][kv_heads][context]) of the
-        mapped target layer."""
-        s = self.s
-        x = self.w["mtp.pre_projection.weight"] @ torch.cat([target_embedding, target_hidden])
-        for layer in range(s.layers):
-            x = self._layer(layer, x, kv[layer], position)
-        h = _rms_norm(x, self.v["output_norm.weight"], s.rms_eps)
-        post = self.w["mtp.post_projection.weight"] @ h
-        ids, logits = self.masked_top_tokens(h, self.w["mtp.centroids.weight"] @ h, top_k)
-        return post, ids, logits
-
-    def masked_top_tokens(self, h: torch.Tensor, centroid_logits: torch.Tensor, top_k: int):
-        """maskedEmbeddingTopTokens (mtp-assistant-runner.ts:211-242): the
-        tokens of the top centroid_top_k centroids (deduplicated, ids outside
-        the vocabulary dropped) scored by their embedding row . h."""
-        s = self.s
-        c_ids, _ = _top_desc_id_asc(centroid_logits, self.centroid_ids, min(s.centroid_top_k, s.n_centroids))
-        toks = self.centroid_tokens[c_ids].reshape(-1)
-        toks = toks[(toks >= 0) & (toks < s.vocab)]
-        sel = torch.unique(toks)  # ascending: ties resolve to the lower id
-        vals = self.w["token_embd.weight"][sel] @ h
-        return _top_desc_id_asc(vals, sel, top_k)
-
-    def _layer(self, layer: int, x: torch.Tensor, kv, position: int) -> torch.Tensor:
-        s, w, v = self.s, self.w, self.v
-        p = f"blk.{layer}."
-        a = _rms_norm(x, v[p + "attn_norm.weight"], s.rms_eps)
-        q = _rms_norm((w[p + "attn_q.weight"] @ a).reshape(s.heads, s.head_dim), v[p + "attn_q_norm.weight"],
-                      s.rms_eps)
-        q = _rope_partial(q, position, s.head_dim, s.active_pairs, s.rope_theta)
-        o = w[p + "attn_output.weight"] @ self._attention(q, kv, position)
-        r = x + _rms_norm(o, v[p + "post_attention_norm.weight"], s.rms_eps)
-        n = _rms_norm(r, v[p + "ffn_norm.weight"], s.rms_eps)
-        act = (_gelu(w[p + "ffn_gate.weight"] @ n).double() * (w[p + "ffn_up.weight"] @ n).double()).float()
-        f = r + _rms_norm(w[p + "ffn_down.weight"] @ act, v[p + "post_ffw_norm.weight"], s.rms_eps)
-        return (f.double() * self.scale[layer]).float()
-
-    def _attention(self, q: torch.Tensor, kv, position: int) -> torch.Tensor:
-        """GQA attention of one query over the target KV (lib.rs:539-654 as
-        gqaAttentionWasm calls it for the draft head: f32 query, scale 1,
-        causal to `position`, f64 exp of the f32 score differences)."""
-        k, vv = kv  # K [ctx][kvh][hd], V [hd][kvh][ctx]
-        s = self.s
-        count = position + 1
-        g = s.heads // s.kv_heads
-        qg = q.view(s.kv_heads, g, s.head_dim)
-        scores = torch.einsum("khd,tkd->kht", qg, k[:count])           # [kvh][g][count] f32
-        p = torch.exp((scores - scores.amax(dim=-1, keepdim=True)).double()).float()
-        wts = p / p.sum(dim=-1, keepdim=True)
-        out = torch.einsum("kht,dkt->khd", wts, vv[:, :, :count])
-        return out.reshape(-1)
+        """One draft step: (backbone hidden [backbone], ids, logits [top_k]),
+        on the device.  kv[layer] = (K [context][kv_heads][head_dim], V in the
+        reference orientation [head_dim][kv_heads][context]) of the mapped
+        target layer; V is used token-major (a view of the model's own
+        storage when it is one, else a contiguous copy)."""
+        C = self._C
+        keep = []
+        for layer, (k, v) in enumerate(kv):
+            k = k.contiguous()
+            vt = v.permute(2, 1, 0)
+            if not vt.is_contiguous():
+                vt = vt.contiguous()
+            keep += [k, vt]
+            hk.assert_cuda_ok(self._L.hpc_draft_set_target_kv(self._h, layer, C.c_void_p(k.data_ptr()),
+                                                              C.c_void_p(vt.data_ptr())), "draftSetTargetKv")
+        self._kv_keep = keep
+        emb = target_embedding.to(device="cuda", dtype=torch.float32).contiguous()
+        hid = target_hidden.to(device="cuda", dtype=torch.float32).contiguous()
+        st = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+        hk.assert_cuda_ok(self._L.hpc_draft_step(self._h, C.c_void_p(emb.data_ptr()), C.c_void_p(hid.data_ptr()),
+                                                 int(position), int(top_k), C.c_void_p(self.post.data_ptr()),
+                                                 C.c_void_p(self.ids.data_ptr()), C.c_void_p(self.vals.data_ptr()),
+                                                 st), "draftStep")
+        return self.post.clone(), self.ids[:top_k].long(), self.vals[:top_k].clone()
 
 
 # ---- the speculative decoding loop ------------------------------------------

@@ -285,6 +285,73 @@ int hpc_model_forward(hpc_model model, const int32_t *d_token_ids, const int32_t
 int hpc_model_prefill(hpc_model model, const float *d_hidden_in, const int32_t *d_positions, size_t token_count,
                       float *d_hidden_out, void *stream);
 
+/* ---- MTP draft head ("MTP assistant") -----------------------------------
+ * runWasmMtpAssistant (runner/wasm/mtp-assistant-runner.ts:43-242) on the
+ * GPU: pre projection over [target embedding ; target hidden], the draft
+ * layers attending over the TARGET's KV cache, output norm, post projection
+ * and maskedEmbeddingTopTokens (top centroids -> token ordering -> embedding
+ * rows . h).  The matmuls are f32 products of the bit-exactly dequantized
+ * weights (hp_matmul_dequantized_f32, lib.rs:103-154); each matrix is
+ * dequantized once into the draft head's own f32 copy when it is set, so the
+ * handles may be released afterwards.  One step is one CUDA graph. */
+
+typedef struct hpc_draft_s *hpc_draft;
+
+typedef struct {
+  int backbone;       /* target hidden size */
+  int hidden;         /* draft width (multiple of 256, <= 8192) */
+  int heads;
+  int kv_heads;       /* the target's KV heads */
+  int head_dim;       /* 256 */
+  int ffn;
+  int vocab;
+  int n_centroids;    /* <= 4096 */
+  int centroid_top_k;
+  int layers;
+  int context;        /* largest position + 1 (multiple of 64, <= 4096) */
+  int max_top_k;      /* 1..64 */
+  double rms_eps;
+  double rope_theta;
+} hpc_draft_config;
+
+/* matrices: per layer (layer index applies) */
+#define HPC_DW_Q 0
+#define HPC_DW_O 1
+#define HPC_DW_GATE 2
+#define HPC_DW_UP 3
+#define HPC_DW_DOWN 4
+#define HPC_DW_LAYER_COUNT 5
+/* matrices: head-wide (layer ignored) */
+#define HPC_DW_PRE 100       /* mtp.pre_projection.weight  [hidden][2 * backbone] */
+#define HPC_DW_POST 101      /* mtp.post_projection.weight [backbone][hidden] */
+#define HPC_DW_CENTROIDS 102 /* mtp.centroids.weight       [n_centroids][hidden] */
+#define HPC_DW_EMBD 103      /* token_embd.weight          [vocab][hidden] */
+/* f32 vectors */
+#define HPC_DN_ATTN 0
+#define HPC_DN_Q 1           /* attn_q_norm, head_dim values */
+#define HPC_DN_POST_ATTN 2
+#define HPC_DN_FFN 3
+#define HPC_DN_POST_FFW 4
+#define HPC_DN_LAYER_COUNT 5
+#define HPC_DN_OUTPUT 100    /* output_norm (layer ignored) */
+
+int hpc_draft_create(const hpc_draft_config *config, hpc_draft *out_draft);
+int hpc_draft_release(hpc_draft draft);
+int hpc_draft_set_matrix(hpc_draft draft, int which, int layer, hpc_weight weight);
+int hpc_draft_set_vector(hpc_draft draft, int which, int layer, const float *host_values, size_t len);
+int hpc_draft_set_layer_scale(hpc_draft draft, int layer, float scale);
+/* token_ordering: n_centroids * per entries; centroid c lists its tokens at
+ * [c * per, (c + 1) * per); centroid_top_k * per <= 4096 */
+int hpc_draft_set_token_ordering(hpc_draft draft, const int32_t *host_ordering, size_t len);
+/* The mapped target KV layer of draft layer `layer` (model.ts:457-478), both
+ * [context][kv_heads][head_dim] f32 -- the layout hpc_model_kv returns. */
+int hpc_draft_set_target_kv(hpc_draft draft, int layer, const float *d_key, const float *d_value);
+/* One draft step at the target context's position (proposeMtpDraft keeps it
+ * constant, mtp-generation.ts:92-137): backbone hidden [backbone] and the
+ * top_k (token id, logit) pairs, value desc / id asc, into device buffers. */
+int hpc_draft_step(hpc_draft draft, const float *d_embedding, const float *d_hidden, int position, size_t top_k,
+                   float *d_post_out, int32_t *d_ids, float *d_vals, void *stream);
+
 #ifdef __cplusplus
 }
 #endif
