@@ -49,7 +49,11 @@ template <int TYPE>
 struct TcType {
   static constexpr int UB = TYPE == TYPE_Q4_K ? 4608 : 6720;
   static constexpr int REC = TYPE == TYPE_Q4_K ? Q8A_REC : Q8B_REC;
-  static constexpr int STAGE = TC_TILES * UB + TC_COLS * REC;
+  // staged record stride: 304 bytes (76 words) for both planes puts the
+  // eight columns' B-fragment words in distinct banks (288 would map
+  // columns g and g + 4 onto the same ones)
+  static constexpr int SREC = 304;
+  static constexpr int STAGE = TC_TILES * UB + TC_COLS * SREC;
 };
 
 template <int TYPE>
@@ -70,7 +74,7 @@ __global__ void __launch_bounds__(TC_THREADS, 2) gemm_tc_kernel(const __grid_con
     for (int i = int(threadIdx.x); i < TC_COLS * T::REC / 16; i += TC_THREADS) {
       const int c = i / (T::REC / 16), o = i % (T::REC / 16);
       const int col = min(col0 + c, p.col0 + p.ncols - 1);
-      cp_async16(st + TC_TILES * T::UB + c * T::REC + o * 16, p.act + (size_t(col) * p.nb + b) * T::REC + o * 16);
+      cp_async16(st + TC_TILES * T::UB + c * T::SREC + o * 16, p.act + (size_t(col) * p.nb + b) * T::REC + o * 16);
     }
     cp_async_commit();
   };
@@ -91,7 +95,7 @@ __global__ void __launch_bounds__(TC_THREADS, 2) gemm_tc_kernel(const __grid_con
     }
     __syncthreads();
     const uint8_t* st = smem + (b & 1) * T::STAGE;
-    tc_block<TYPE, 4>(st + wt * T::UB, st + TC_TILES * T::UB + (32 * wh) * T::REC, T::REC, acc, g, t);
+    tc_block<TYPE, 4>(st + wt * T::UB, st + TC_TILES * T::UB + (32 * wh) * T::SREC, T::SREC, acc, g, t);
     __syncthreads();  // every warp is done with this stage before it is refilled
   }
   const int tile = tile0 + wt;
