@@ -722,6 +722,197 @@ __global__ void __launch_bounds__(256) prefill_attn_kernel(const float* __restri
   }
 }
 
+// Split form of the prefill attention: the keys of a query tile are cut into
+// PF_SK-key splits, one CTA per (tile, split, KV head), so the causal work of
+// the long tiles spreads over many CTAs; prefill_attn_merge_kernel merges
+// the splits.  Per CTA: the PF_QT tokens x G heads of the tile (qs, rows
+// padded for conflict-free reads), keys in PF_CK chunks (online softmax:
+// running max, f64 exp of the differences, f32 sums), scores as 2 x 2
+// register blocks (a warp covers 8 query vectors x 16 keys), outputs with
+// thread d = dimension over 4 keys per step.  Writes the split's max, sum and
+// unnormalized output per (token, head) to part_m / part_l / part_o at
+// ((token * H + head) * nsplit + split).
+constexpr int PF_SK = 128;       // keys per split
+constexpr int PF_QSTRIDE = 260;  // floats per staged query row
+__global__ void __launch_bounds__(256) prefill_attn_split_kernel(const float* __restrict__ qh,
+                                                                const float* __restrict__ kc,
+                                                                const float* __restrict__ vc,
+                                                                const int32_t* __restrict__ pos, int M, int H, int KVH,
+                                                                int cap, int nsplit, float* __restrict__ part_m,
+                                                                float* __restrict__ part_l, float* __restrict__ part_o) {
+  constexpr int HD = 256, NQ_MAX = PF_QT * 4;  // G <= 4
+  extern __shared__ __align__(16) float psm[];
+  const int G = H / KVH, NQ = PF_QT * G, kvh = int(blockIdx.y);
+  const int tile = int(blockIdx.x) / nsplit, split = int(blockIdx.x) % nsplit, m0 = tile * PF_QT;
+  const int mt = min(PF_QT, M - m0);
+  const int last = pos[m0 + mt - 1];
+  const int start = max(0, last + 1 - cap);
+  const int k_lo = start + split * PF_SK, k_hi = min(start + (split + 1) * PF_SK, last + 1);
+  if (k_lo >= k_hi) return;  // this tile's window ends before the split
+  float* qs = psm;                           // [NQ][PF_QSTRIDE]
+  float* ks = qs + NQ * PF_QSTRIDE;          // [PF_CK][ATT_KSTRIDE]
+  float* vs = ks + PF_CK * ATT_KSTRIDE;      // [PF_CK][HD]
+  float* ps = vs + PF_CK * HD;               // [NQ][PF_CK]
+  __shared__ float alpha[NQ_MAX], run_m[NQ_MAX], run_l[NQ_MAX];
+  const int tid = int(threadIdx.x), lane = tid & 31, warp = tid >> 5;
+  for (int i = tid; i < NQ * HD / 4; i += int(blockDim.x)) {
+    const int qi = (4 * i) / HD, d = (4 * i) % HD, mm = min(qi / G, mt - 1);
+    *reinterpret_cast<float4*>(qs + qi * PF_QSTRIDE + d) =
+        *reinterpret_cast<const float4*>(qh + (size_t(m0 + mm) * H + kvh * G + qi % G) * HD + d);
+  }
+  if (tid < NQ) {
+    run_m[tid] = -INFINITY;
+    run_l[tid] = 0.0f;
+  }
+  float o[NQ_MAX];
+#pragma unroll
+  for (int i = 0; i < NQ_MAX; ++i) o[i] = 0.0f;
+  for (int k0 = k_lo; k0 < k_hi; k0 += PF_CK) {
+    const int nk = min(PF_CK, k_hi - k0);
+    for (int i = tid; i < PF_CK * (HD / 4); i += int(blockDim.x)) {
+      const int j = i / (HD / 4), c = i % (HD / 4), key = k0 + min(j, nk - 1);
+      const size_t row = (size_t(key % cap) * KVH + kvh) * HD + 4 * c;
+      cp_async16(ks + j * ATT_KSTRIDE + 4 * c, kc + row);
+      cp_async16(vs + j * HD + 4 * c, vc + row);
+    }
+    cp_async_commit();
+    cp_async_wait_all();
+    __syncthreads();
+    // scores: warp w covers query pairs 4 (w % 4) .. + 3 and key pairs
+    // 8 (w / 4) .. + 7 (lane: query pair lane / 8, key pair lane % 8); more
+    // query vectors than 32 take further passes
+    for (int qb = 0; qb < NQ; qb += 32) {
+      const int qa = qb + 2 * (4 * (warp & 3) + (lane >> 3)), kb = 2 * (8 * (warp >> 2) + (lane & 7));
+      if (qa < NQ) {
+        const float4* q0 = reinterpret_cast<const float4*>(qs + qa * PF_QSTRIDE);
+        const float4* q1 = reinterpret_cast<const float4*>(qs + (qa + 1) * PF_QSTRIDE);
+        const float4* kv0 = reinterpret_cast<const float4*>(ks + kb * ATT_KSTRIDE);
+        const float4* kv1 = reinterpret_cast<const float4*>(ks + (kb + 1) * ATT_KSTRIDE);
+        float4 a00 = make_float4(0.f, 0.f, 0.f, 0.f), a01 = a00, a10 = a00, a11 = a00;
+#pragma unroll 8
+        for (int c = 0; c < HD / 4; ++c) {
+          const float4 x0 = q0[c], x1 = q1[c], y0 = kv0[c], y1 = kv1[c];
+          a00.x = fmaf(x0.x, y0.x, a00.x); a00.y = fmaf(x0.y, y0.y, a00.y);
+          a00.z = fmaf(x0.z, y0.z, a00.z); a00.w = fmaf(x0.w, y0.w, a00.w);
+          a01.x = fmaf(x0.x, y1.x, a01.x); a01.y = fmaf(x0.y, y1.y, a01.y);
+          a01.z = fmaf(x0.z, y1.z, a01.z); a01.w = fmaf(x0.w, y1.w, a01.w);
+          a10.x = fmaf(x1.x, y0.x, a10.x); a10.y = fmaf(x1.y, y0.y, a10.y);
+          a10.z = fmaf(x1.z, y0.z, a10.z); a10.w = fmaf(x1.w, y0.w, a10.w);
+          a11.x = fmaf(x1.x, y1.x, a11.x); a11.y = fmaf(x1.y, y1.y, a11.y);
+          a11.z = fmaf(x1.z, y1.z, a11.z); a11.w = fmaf(x1.w, y1.w, a11.w);
+        }
+        const float4 acc[2][2] = {{a00, a01}, {a10, a11}};
+#pragma unroll
+        for (int i = 0; i < 2; ++i)
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            const int qi = qa + i, key = kb + j;
+            const int mq = qi / G;
+            const bool ok = key < nk && mq < mt && k0 + key <= pos[m0 + min(mq, mt - 1)];
+            const float4 v = acc[i][j];
+            ps[qi * PF_CK + key] = ok ? (v.x + v.y) + (v.z + v.w) : -INFINITY;
+          }
+      }
+    }
+    __syncthreads();
+    // online softmax: warp per query vector, lane = key
+    for (int qi = warp; qi < NQ; qi += 8) {
+      const float sc = ps[qi * PF_CK + lane];
+      float mx = sc;
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+      const float mo = run_m[qi], mn = fmaxf(mo, mx);
+      const float p = (sc == -INFINITY) ? 0.0f : float(exp(double(sc - mn)));
+      float sum = p;
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+      ps[qi * PF_CK + lane] = p;
+      __syncwarp();
+      if (lane == 0) {
+        const float a = (mo == -INFINITY) ? 0.0f : float(exp(double(mo - mn)));
+        alpha[qi] = a;
+        run_l[qi] = run_l[qi] * a + sum;
+        run_m[qi] = mn;
+      }
+    }
+    __syncthreads();
+    // outputs: thread d owns dimension d of every query vector, 4 keys per step
+    const int d = tid;
+#pragma unroll
+    for (int qi = 0; qi < NQ_MAX; ++qi)
+      if (qi < NQ) o[qi] *= alpha[qi];
+    for (int j = 0; j < nk; j += 4) {
+      const float b0 = vs[j * HD + d], b1 = vs[(j + 1) * HD + d], b2 = vs[(j + 2) * HD + d],
+                  b3 = vs[(j + 3) * HD + d];
+#pragma unroll
+      for (int qi = 0; qi < NQ_MAX; ++qi) {
+        if (qi < NQ) {
+          const float4 pr = *reinterpret_cast<const float4*>(ps + qi * PF_CK + j);
+          o[qi] += pr.x * b0 + pr.y * b1 + pr.z * b2 + pr.w * b3;
+        }
+      }
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int qi = 0; qi < NQ_MAX; ++qi) {
+    if (qi < NQ && qi / G < mt) {
+      const size_t ix = (size_t(m0 + qi / G) * H + kvh * G + qi % G) * nsplit + split;
+      if (tid == 0) {
+        part_m[ix] = run_m[qi];
+        part_l[ix] = run_l[qi];
+      }
+      part_o[ix * HD + tid] = o[qi];
+    }
+  }
+}
+
+// Merges the splits of one (token, head): the splits of its tile's window
+// that reach the token (global max, f64-exp weights, f64 sum, weighted
+// outputs), the TS f16 cast (castF16Rows) and the head's Q8_K block for the
+// output projection.  Grid (M, H), thread d = dimension.
+__global__ void __launch_bounds__(256) prefill_attn_merge_kernel(const float* __restrict__ part_m,
+                                                                const float* __restrict__ part_l,
+                                                                const float* __restrict__ part_o,
+                                                                const int32_t* __restrict__ pos, int M, int H, int cap,
+                                                                int nsplit, Q8Buf qo, float* __restrict__ attn_out) {
+  constexpr int HD = 256;
+  __shared__ float w[64];
+  __shared__ double lsum;
+  __shared__ float vec[HD];
+  const int m = int(blockIdx.x), h = int(blockIdx.y), d = int(threadIdx.x);
+  const int tile = m / PF_QT, mt = min(PF_QT, M - tile * PF_QT);
+  const int last = pos[tile * PF_QT + mt - 1];
+  const int start = max(0, last + 1 - cap);
+  const int ns = min(nsplit, (pos[m] - start) / PF_SK + 1);  // splits holding keys <= pos[m]
+  const size_t base = (size_t(m) * H + h) * nsplit;
+  if (d == 0) {
+    float mx = -INFINITY;
+    for (int s = 0; s < ns; ++s) mx = fmaxf(mx, part_m[base + s]);
+    double l = 0.0;
+    for (int s = 0; s < ns; ++s) {
+      const float ms = part_m[base + s];
+      const float ws = ms == -INFINITY ? 0.0f : float(exp(double(ms - mx)));
+      w[s] = ws;
+      l += double(ws) * double(part_l[base + s]);
+    }
+    lsum = l;
+  }
+  __syncthreads();
+  float o = 0.0f;
+  for (int s = 0; s < ns; ++s) o += w[s] * part_o[(base + s) * HD + d];
+  const float n = round_f16_ts(float(double(o) / lsum));
+  vec[d] = n;
+  if (attn_out) attn_out[(size_t(m) * H + h) * HD + d] = n;
+  __syncthreads();
+  if (d < 32) {
+    float v8[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v8[i] = vec[8 * d + i];
+    q8k_block_warp(v8, d, nullptr, q8_rec_a(qo, m, h), q8_rec_b(qo, m, h));
+  }
+}
+
 // ---- launch helpers ---------------------------------------------------------------------
 
 template <typename... KArgs, typename... Args>
@@ -819,6 +1010,39 @@ cudaError_t launch_prefill_qkv_post(const float* q, const float* kraw, const flo
 size_t prefill_attn_smem_bytes(int H, int KVH) {
   const int NQ = PF_QT * (H / KVH);
   return sizeof(float) * (size_t(NQ) * 256 + size_t(PF_CK) * ATT_KSTRIDE + size_t(PF_CK) * 256 + size_t(NQ) * PF_CK);
+}
+
+size_t prefill_split_smem_bytes(int H, int KVH) {
+  const int NQ = PF_QT * (H / KVH);
+  return sizeof(float) * (size_t(NQ) * PF_QSTRIDE + size_t(PF_CK) * ATT_KSTRIDE + size_t(PF_CK) * 256 +
+                          size_t(NQ) * PF_CK);
+}
+
+int prefill_attn_splits(int cap, int max_pos) {
+  const int window = min(cap, max_pos + 1);
+  return (window + PF_SK - 1) / PF_SK;
+}
+
+cudaError_t launch_prefill_attention_split(const float* qh, const float* kc, const float* vc, const int32_t* pos,
+                                           int M, int H, int KVH, int cap, int nsplit, float* part_m, float* part_l,
+                                           float* part_o, const Q8Buf& qo, float* attn_out, cudaStream_t st) {
+  if (H / KVH > 4 || nsplit < 1 || nsplit > 64) return cudaErrorInvalidValue;
+  const size_t smem = prefill_split_smem_bytes(H, KVH);
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e =
+        cudaFuncSetAttribute(prefill_attn_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  const int tiles = (M + PF_QT - 1) / PF_QT;
+  prefill_attn_split_kernel<<<dim3(unsigned(tiles * nsplit), unsigned(KVH)), 256, smem, st>>>(
+      qh, kc, vc, pos, M, H, KVH, cap, nsplit, part_m, part_l, part_o);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  prefill_attn_merge_kernel<<<dim3(unsigned(M), unsigned(H)), 256, 0, st>>>(part_m, part_l, part_o, pos, M, H, cap,
+                                                                           nsplit, qo, attn_out);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_prefill_attention(const float* qh, const float* kc, const float* vc, const int32_t* pos, int M,

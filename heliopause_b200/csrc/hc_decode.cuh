@@ -37,5 +37,12 @@ cudaError_t launch_prefill_qkv_post(const float* q, const float* kraw, const flo
                                    cudaStream_t st);
 cudaError_t launch_prefill_attention(const float* qh, const float* kc, const float* vc, const int32_t* pos, int M,
                                      int H, int KVH, int cap, const Q8Buf& qo, float* attn_out, cudaStream_t st);
+// The split form: nsplit = prefill_attn_splits(cap, largest position) splits
+// of the key window per query tile, partials [M][H][nsplit] (+ [256] for
+// part_o), then the merge (f16 cast + Q8_K, as launch_prefill_attention).
+int prefill_attn_splits(int cap, int max_pos);
+cudaError_t launch_prefill_attention_split(const float* qh, const float* kc, const float* vc, const int32_t* pos,
+                                           int M, int H, int KVH, int cap, int nsplit, float* part_m, float* part_l,
+                                           float* part_o, const Q8Buf& qo, float* attn_out, cudaStream_t st);
 
 }  // namespace hc

@@ -43,6 +43,7 @@ struct TcParams {
   const uint8_t* act;  // the Q8_K record plane this type reads (A for Q4_K, B for Q6_K), [col][nb]
   float* out;          // out[col * rows + row]
   int rows, tiles, nb, ncols, col0;
+  int ksplit;          // 1, or 2: grid.z halves of K, atomically added into a zeroed out
 };
 
 template <int TYPE>
@@ -85,16 +86,18 @@ __global__ void __launch_bounds__(TC_THREADS, 2) gemm_tc_kernel(const __grid_con
     for (int ng = 0; ng < 4; ++ng)
 #pragma unroll
       for (int r = 0; r < 4; ++r) acc[mg][ng][r] = 0.0f;
-  issue(0, smem);
-  for (int b = 0; b < p.nb; ++b) {
-    if (b + 1 < p.nb) {
-      issue(b + 1, smem + ((b + 1) & 1) * T::STAGE);
+  // K range of this CTA: all blocks, or one half (ksplit 2)
+  const int kb0 = int(blockIdx.z) * (p.nb / p.ksplit), kb1 = kb0 + p.nb / p.ksplit;
+  issue(kb0, smem);
+  for (int b = kb0; b < kb1; ++b) {
+    if (b + 1 < kb1) {
+      issue(b + 1, smem + ((b + 1 - kb0) & 1) * T::STAGE);
       asm volatile("cp.async.wait_group 1;" ::: "memory");
     } else {
       asm volatile("cp.async.wait_group 0;" ::: "memory");
     }
     __syncthreads();
-    const uint8_t* st = smem + (b & 1) * T::STAGE;
+    const uint8_t* st = smem + ((b - kb0) & 1) * T::STAGE;
     tc_block<TYPE, 4>(st + wt * T::UB, st + TC_TILES * T::UB + (32 * wh) * T::SREC, T::SREC, acc, g, t);
     __syncthreads();  // every warp is done with this stage before it is refilled
   }
@@ -108,7 +111,12 @@ __global__ void __launch_bounds__(TC_THREADS, 2) gemm_tc_kernel(const __grid_con
       for (int r = 0; r < 4; ++r) {
         const int row = tile * TILE + 16 * mg + g + 8 * (r >> 1);
         const int col = col0 + 32 * wh + 8 * ng + 2 * t + (r & 1);
-        if (row < p.rows && col < p.col0 + p.ncols) p.out[size_t(col) * p.rows + row] = acc[mg][ng][r];
+        if (row < p.rows && col < p.col0 + p.ncols) {
+          // two halves: a + b is the same sum in either order, so the
+          // result stays deterministic
+          if (p.ksplit == 1) p.out[size_t(col) * p.rows + row] = acc[mg][ng][r];
+          else atomicAdd(p.out + size_t(col) * p.rows + row, acc[mg][ng][r]);
+        }
       }
 }
 
@@ -121,7 +129,12 @@ static cudaError_t launch_tc(const TcParams& p, cudaStream_t st) {
     if (e != cudaSuccess) return e;
     attr = true;
   }
-  const dim3 grid(unsigned((p.tiles + TC_TILES - 1) / TC_TILES), unsigned((p.ncols + TC_COLS - 1) / TC_COLS));
+  const dim3 grid(unsigned((p.tiles + TC_TILES - 1) / TC_TILES), unsigned((p.ncols + TC_COLS - 1) / TC_COLS),
+                  unsigned(p.ksplit));
+  if (p.ksplit > 1) {
+    cudaError_t e = cudaMemsetAsync(p.out + size_t(p.col0) * p.rows, 0, sizeof(float) * size_t(p.ncols) * p.rows, st);
+    if (e != cudaSuccess) return e;
+  }
   gemm_tc_kernel<TYPE><<<grid, TC_THREADS, smem, st>>>(p);
   return cudaGetLastError();
 }
@@ -135,6 +148,10 @@ cudaError_t launch_gemm_tc(const GemvSeg& seg, int nb, const Q8Buf& q, int col0,
   p.nb = nb;
   p.ncols = ncols;
   p.col0 = col0;
+  // fewer CTAs than two per SM (narrow outputs: the 2048-row projections)
+  // and an even block count: split K in two
+  const int ctas = ((p.tiles + TC_TILES - 1) / TC_TILES) * ((ncols + TC_COLS - 1) / TC_COLS);
+  p.ksplit = (ctas < 2 * sm_count() && nb % 2 == 0) ? 2 : 1;
   if (seg.type == TYPE_Q4_K) {
     p.act = q.a;
     return launch_tc<TYPE_Q4_K>(p, st);

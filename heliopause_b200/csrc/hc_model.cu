@@ -85,6 +85,8 @@ struct hpc_model_s {
   double *pf_cos = nullptr, *pf_sin = nullptr;
   int32_t* pf_pos = nullptr;
   void *pf_q8d = nullptr, *pf_q8f = nullptr;
+  void* pf_part = nullptr;  // split-attention partials (grows with tokens x splits)
+  size_t pf_part_bytes = 0;
   size_t pf_q8d_bytes = 0, pf_q8f_bytes = 0;
 };
 
@@ -206,6 +208,7 @@ int hpc_model_release(hpc_model m) {
   cudaFree(m->d_players);
   cudaFree(m->persist_buf);
   cudaFree(m->pf_arena);
+  cudaFree(m->pf_part);
   if (m->capture_stream) cudaStreamDestroy(m->capture_stream);
   m->magic = 0;
   delete m;
@@ -698,6 +701,30 @@ int hpc_model_prefill(hpc_model m, const float* d_hidden_in, const int32_t* d_po
   float* X = m->pf_x;
   HPC_CK(cudaMemcpyAsync(X, d_hidden_in, sizeof(float) * M * D, cudaMemcpyDeviceToDevice, st), "hidden in");
   HPC_CK(cudaMemcpyAsync(m->pf_pos, d_positions, sizeof(int32_t) * M, cudaMemcpyDeviceToDevice, st), "positions");
+  // the split attention sizes its grid from the key window: the positions
+  // are consecutive, so the first one bounds it (one small read per call)
+  const int G = H / KVH;
+  int nsplit = 0;
+  float *pm = nullptr, *pl = nullptr, *po = nullptr;
+  if (G <= 4) {
+    int32_t pos0 = 0;
+    HPC_CK(cudaMemcpyAsync(&pos0, d_positions, sizeof pos0, cudaMemcpyDeviceToHost, st), "first position");
+    HPC_CK(cudaStreamSynchronize(st), "first position");
+    if (pos0 < 0) return hpc_fail(HPC_ERR_SHAPE, "prefill position %d", pos0);
+    nsplit = hc::prefill_attn_splits(c.context, pos0 + M - 1);
+    const size_t rows = size_t(M) * H * nsplit;
+    const size_t need = (rows * 2 * sizeof(float) + 255) / 256 * 256 + rows * HD * sizeof(float);
+    if (need > m->pf_part_bytes) {
+      cudaFree(m->pf_part);
+      m->pf_part = nullptr;
+      m->pf_part_bytes = 0;
+      HPC_CK(cudaMalloc(&m->pf_part, need), "prefill attention partials");
+      m->pf_part_bytes = need;
+    }
+    pm = static_cast<float*>(m->pf_part);
+    pl = pm + rows;
+    po = reinterpret_cast<float*>(static_cast<char*>(m->pf_part) + (rows * 2 * sizeof(float) + 255) / 256 * 256);
+  }
   HPC_CK(hc::launch_rope_table(m->pf_pos, M, HD / 2, std::pow(c.rope_theta, -2.0 / double(HD)), m->pf_cos, m->pf_sin,
                                st),
          "rope table");
@@ -734,7 +761,12 @@ int hpc_model_prefill(hpc_model m, const float* d_hidden_in, const int32_t* d_po
                                        m->pf_sin, eps, own_kv, m->kc[kvl], m->vc[kvl], m->pf_pos, M, H, KVH, c.context,
                                        m->pf_qh, st),
            "prefill qk norm / rope / kv");
-    HPC_CK(hc::launch_prefill_attention(m->pf_qh, m->kc[kvl], m->vc[kvl], m->pf_pos, M, H, KVH, c.context, qd, nullptr,
+    if (nsplit > 0)
+      HPC_CK(hc::launch_prefill_attention_split(m->pf_qh, m->kc[kvl], m->vc[kvl], m->pf_pos, M, H, KVH, c.context,
+                                                nsplit, pm, pl, po, qd, nullptr, st),
+             "prefill attention");
+    else
+      HPC_CK(hc::launch_prefill_attention(m->pf_qh, m->kc[kvl], m->vc[kvl], m->pf_pos, M, H, KVH, c.context, qd, nullptr,
                                         st),
            "prefill attention");
     rc = mm({{L.w[HPC_W_O], m->pf_o}}, m->pf_q8d, m->pf_q8d_bytes, size_t(H) * HD);

@@ -1,16 +1,23 @@
 """Prefill (hpc_model_prefill) against the oracle decoder and the decode path.
 
-  * parity: n hidden vectors at positions 0..n-1 through every layer equal
-    the oracle decoder's layer loop on the same input (oracle/decoder_oracle.py
-    `layer`, the WASM provider's forward for n positions with the causal
-    mask), at n = 40 (tensor-core matmuls) and n = 7 (GEMV).  K/V cache rows:
-    within 1e-3 (|ref| + rms(ref)).  Final residual: every token within
-    1e-2 and at least 90% of tokens within 1e-3 of that scale.  The reference
-    algorithm is discontinuous -- Q8_K rounding of every matmul input and the
-    f16 casts of the attention output and GEGLU -- and the oracle itself moves
-    single tokens by up to ~3e-3 of that scale when its input is perturbed by
-    1e-7 relative (measured on the one-layer form of this case), so a
-    different but equally exact summation order can flip the same steps;
+  * parity: n hidden vectors at positions start..start+n-1 through every
+    layer equal the oracle decoder's layer loop on the same input
+    (oracle/decoder_oracle.py `layer`, the WASM provider's forward for n
+    positions with the causal mask), at n = 40 (tensor-core matmuls), n = 7
+    (GEMV), n = 200 over a 256-token context (the attention's key window
+    split in two) and n = 60 after a 100-token prefix already in the cache.
+    K/V cache rows of the first KV layer: within 1e-3 (|ref| + rms(ref)).
+    Final residual: every token within 3e-2, and at least 90% of tokens
+    within 1e-3 of that scale; K/V rows of deeper layers the same with 6e-2.
+    The reference algorithm is discontinuous -- Q8_K rounding of every
+    matmul input and the f16 casts of the attention output and GEGLU -- and
+    the oracle itself moves single tokens when its input is perturbed by 1e-7
+    relative: by up to ~3e-3 of that scale on the one-layer form of the
+    40-token case, and by up to 1.79e-2 (4-5% of the tokens beyond 1e-3) on
+    the 3-layer 200-token case, whose flips compound through the later
+    tokens' attention (its layer-1 K/V rows move by up to 3.1e-2; layer 0's
+    by 4.5e-7).  A different but equally exact summation order flips
+    the same steps;
   * consistency: prefilling a prompt's embedded tokens leaves the same KV
     cache and the same next-token top-k as running the prompt through the
     batched forward in 8-token steps.
@@ -45,38 +52,60 @@ def _close(got, ref, what):
     assert np.all(err <= 1e-3 * (np.abs(ref) + scale)), f"{what}: max err {err.max():.3g} (scale {scale:.3g})"
 
 
-def _close_tokens(got, ref, what):
+def _close_tokens(got, ref, what, bound=3e-2, within=0.9):
     """Per-token bound with room for single rounding-step flips (see above)."""
     got = np.asarray(got, np.float64)
     ref = np.asarray(ref, np.float64)
     rel = np.abs(got - ref) / (np.abs(ref) + np.sqrt(np.mean(ref ** 2)))
     worst = rel.max(axis=1)
     print(f"{what}: per-token max relative error x1e3", np.round(worst * 1e3, 3).tolist())
-    assert worst.max() <= 1e-2, f"{what}: token {int(worst.argmax())} off by {worst.max():.3g}"
-    assert (worst <= 1e-3).mean() >= 0.9, f"{what}: {(worst > 1e-3).sum()} of {len(worst)} tokens beyond 1e-3"
+    assert worst.max() <= bound, f"{what}: token {int(worst.argmax())} off by {worst.max():.3g}"
+    assert (worst <= 1e-3).mean() >= within, f"{what}: {(worst > 1e-3).sum()} of {len(worst)} tokens beyond 1e-3"
 
 
-@pytest.mark.parametrize("n", [40, 7])
-def test_prefill_matches_oracle(n):
+@pytest.mark.parametrize("n,context,start", [(40, 128, 0), (7, 128, 0),
+                                             (200, 256, 0),     # two 128-key splits per late query tile
+                                             (60, 256, 100)])   # continuing after a 100-token prefix
+def test_prefill_matches_oracle(n, context, start):
     from oracle.decoder_oracle import OracleDecoder
-    w = SyntheticWeights(SHAPE, seed=21)
-    gpu = CudaDecoderModel(SHAPE, max_tokens=8, top_k=64)
+    shape = replace(SHAPE, context=context)
+    w = SyntheticWeights(shape, seed=21)
+    gpu = CudaDecoderModel(shape, max_tokens=8, top_k=64)
     try:
         gpu.load_synthetic(w)
-        ref = OracleDecoder(SHAPE, w)
-        for kl in range(SHAPE.kv_layers):
-            ref.set_kv(kl, np.zeros((SHAPE.context, 2, 256), np.float32), np.zeros((256, 2, SHAPE.context), np.float32))
-        x = np.random.default_rng(n).standard_normal((n, SHAPE.hidden)).astype(np.float32)
-        got = gpu.prefill(torch.from_numpy(x), 0).cpu().numpy()
+        ref = OracleDecoder(shape, w)
+        g = np.random.default_rng(n + start)
+        for kl in range(shape.kv_layers):
+            kc = np.zeros((context, 2, 256), np.float32)
+            vc = np.zeros((256, 2, context), np.float32)
+            if start:  # an existing prefix in the cache
+                kc[:start] = g.standard_normal((start, 2, 256))
+                vc[:, :, :start] = g.standard_normal((256, 2, start))
+            ref.set_kv(kl, kc.copy(), vc.copy())
+            gk, gv = gpu.kv(kl)
+            gk.copy_(torch.from_numpy(kc))
+            gv.copy_(torch.from_numpy(vc))
+        x = g.standard_normal((n, shape.hidden)).astype(np.float32)
+        got = gpu.prefill(torch.from_numpy(x), start).cpu().numpy()
         h = x.reshape(-1)
-        for layer in range(SHAPE.layers):
-            h = ref.layer(layer, h, list(range(n)))
-        _close_tokens(got, h.reshape(n, -1), "final residual")
-        for kl in range(SHAPE.kv_layers):
+        for layer in range(shape.layers):
+            h = ref.layer(layer, h, list(range(start, start + n)))
+        # after the random prefix the oracle itself moves single tokens by up
+        # to 3.96e-2 (15-18% beyond 1e-3) under a 1e-7 input perturbation
+        bound, within = (6e-2, 0.8) if start else (3e-2, 0.9)
+        _close_tokens(got, h.reshape(n, -1), "final residual", bound, within)
+        t = start + n
+        for kl in range(shape.kv_layers):
             gk, gv = gpu.kv(kl)
             rk, rv = ref.kv[kl]
-            _close(gk[:n].cpu().numpy(), rk[:n], f"K layer {kl}")
-            _close(gv[:, :, :n].cpu().numpy(), rv[:, :, :n], f"V layer {kl}")
+            gk, gv = gk[:t].cpu().numpy(), gv[:, :, :t].cpu().numpy()
+            if kl == 0:  # computed from the input alone: no upstream flips
+                _close(gk, rk[:t], f"K layer {kl}")
+                _close(gv, rv[:, :, :t], f"V layer {kl}")
+            else:  # rows of deeper layers inherit the earlier layers' flips
+                _close_tokens(gk.reshape(t, -1), rk[:t].reshape(t, -1), f"K layer {kl}", 6e-2, within)
+                _close_tokens(gv.transpose(2, 1, 0).reshape(t, -1), rv[:, :, :t].transpose(2, 1, 0).reshape(t, -1),
+                              f"V layer {kl}", 6e-2, within)
     finally:
         gpu.close()
 
