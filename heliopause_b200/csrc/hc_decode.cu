@@ -561,6 +561,29 @@ __global__ void __launch_bounds__(256) geglu_quant_kernel(const float* __restric
   }
 }
 
+// The wide (prefill) form: a warp per 256-block (lane: elements 8L..8L+7),
+// eight blocks per CTA and no CTA barrier; same arithmetic, same records as
+// geglu_quant_kernel.  Grid (ceil(F / 2048), M).
+__global__ void __launch_bounds__(256) geglu_quant_wide_kernel(const float* __restrict__ gate,
+                                                               const float* __restrict__ up, int F, Q8Buf q,
+                                                               float* __restrict__ act_out) {
+  pdl_trigger();
+  pdl_wait();
+  const int m = int(blockIdx.y), lane = int(threadIdx.x & 31), b = int(blockIdx.x) * 8 + int(threadIdx.x >> 5);
+  if (b * 256 >= F) return;
+  const size_t e = size_t(m) * F + size_t(b) * 256 + 8 * lane;
+  float g[8], u[8], v8[8];
+  load8(gate + e, g);
+  load8(up + e, u);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v8[i] = float(gelu_ts(g[i]) * double(u[i]));
+  if (act_out) {
+    reinterpret_cast<float4*>(act_out + e)[0] = make_float4(v8[0], v8[1], v8[2], v8[3]);
+    reinterpret_cast<float4*>(act_out + e)[1] = make_float4(v8[4], v8[5], v8[6], v8[7]);
+  }
+  q8k_block_warp(v8, lane, nullptr, q8_rec_a(q, m, b), q8_rec_b(q, m, b));
+}
+
 // ---- prefill: many tokens per call -----------------------------------------------------
 
 // QK-norm + RoPE of every token's queries (rounded with the Rust f16 codec,
@@ -993,6 +1016,9 @@ cudaError_t launch_attn_combine(const float* part_m, const float* part_l, const 
 
 cudaError_t launch_geglu_quant(const float* gate, const float* up, int M, int F, const Q8Buf& q, float* act_out,
                                cudaStream_t st) {
+  if (M >= GEGLU_WIDE_MIN_COLS)
+    return pdl_launch(geglu_quant_wide_kernel, dim3((F / 256 + 7) / 8, M), dim3(256), 0, st, gate, up, F, q,
+                      act_out);
   return pdl_launch(geglu_quant_kernel, dim3(F / 256, M), dim3(256), 0, st, gate, up, F, q, act_out);
 }
 

@@ -25,6 +25,10 @@ cudaError_t launch_attention(const float* q, const float* kraw, const float* vra
                              float* part_l, float* part_o, int* err, cudaStream_t st);
 cudaError_t launch_attn_combine(const float* part_m, const float* part_l, const float* part_o, const int32_t* pos,
                                 int M, int H, int KVH, int cap, const Q8Buf& q, float* attn_out, cudaStream_t st);
+// Launches of at least GEGLU_WIDE_MIN_COLS columns (prefill) take a warp per
+// 256-block; narrower ones a thread per element, which spreads the f64
+// GELU of a decode step over more threads.
+constexpr int GEGLU_WIDE_MIN_COLS = 16;
 cudaError_t launch_geglu_quant(const float* gate, const float* up, int M, int F, const Q8Buf& q, float* act_out,
                                cudaStream_t st);
 
