@@ -280,8 +280,10 @@ int hpc_model_forward(hpc_model model, const int32_t *d_token_ids, const int32_t
  * (runner/segment-runner.ts:18-34, forward.ts:128-161;
  * runner/webgpu/segment-runner.ts:1292-1795 runBatchedPrefillFromBoundary).
  * Inputs of >= 16 columns run the matmuls on the tensor cores.  The
- * attention is causal over [0, position].  The launches are eager (no graph),
- * and the workspace grows to the largest token count seen. */
+ * attention is causal over [0, position].  The launches are eager (no graph):
+ * the call reads d_positions[0] back to size the attention's key windows (one
+ * synchronization of `stream` per call), and the workspace grows to the
+ * largest token count seen. */
 int hpc_model_prefill(hpc_model model, const float *d_hidden_in, const int32_t *d_positions, size_t token_count,
                       float *d_hidden_out, void *stream);
 
