@@ -320,3 +320,47 @@ def test_mtp_sampled_generation_is_deterministic(gpu_device):
     assert runs[0] == runs[1]
     toks, rounds, acc = runs[0]
     assert len(toks) == 20 and 1 <= rounds <= 20 and 0 <= acc <= 20 - rounds
+
+
+@pytest.mark.gpu
+def test_draft_head_rejects_bad_use(gpu_device):
+    """hpc_draft_* validation through the C-ABI: a shape it cannot run, a step
+    before the weights and target KV are set, a matrix of the wrong shape,
+    and top-k / position outside the configured range each return their
+    status code (nothing is launched)."""
+    import ctypes as C
+
+    from heliopause_b200 import _lib
+    from heliopause_b200 import kernels as hk
+    L = _lib.lib()
+    s = TINY_D
+    cfg = _lib.DraftConfig(s.backbone, s.hidden, s.heads, s.kv_heads, s.head_dim, s.ffn, s.vocab, s.n_centroids,
+                           s.centroid_top_k, s.layers, 64, 16, s.rms_eps, s.rope_theta)
+    bad = _lib.DraftConfig.from_buffer_copy(cfg)
+    bad.head_dim = 128
+    h = C.c_void_p()
+    assert L.hpc_draft_create(C.byref(bad), C.byref(h)) == hk.ERR_SHAPE
+    assert L.hpc_draft_create(C.byref(cfg), C.byref(h)) == hk.OK
+    try:
+        x = torch.zeros(s.backbone, device="cuda")
+        post = torch.empty(s.backbone, device="cuda")
+        ids = torch.empty(16, dtype=torch.int32, device="cuda")
+        vals = torch.empty(16, device="cuda")
+
+        def step(position, k):
+            return L.hpc_draft_step(h, C.c_void_p(x.data_ptr()), C.c_void_p(x.data_ptr()), position, k,
+                                    C.c_void_p(post.data_ptr()), C.c_void_p(ids.data_ptr()),
+                                    C.c_void_p(vals.data_ptr()), None)
+        assert step(3, 4) == hk.ERR_ARG  # weights not loaded
+        w = SyntheticDraftWeights(s, seed=3)
+        t, k, n = s.matrices()["mtp.post_projection.weight"]
+        wrong = hk.create_quantized_weight_handle("Q4_K", w.matrix("mtp.post_projection.weight"), k, n)
+        try:  # the post projection given as the pre projection (K = 2 * backbone expected)
+            assert L.hpc_draft_set_matrix(h, 100, 0, wrong.handle) == hk.ERR_SHAPE
+        finally:
+            hk.release_quantized_weight_handle(wrong)
+        assert step(64, 4) == hk.ERR_SHAPE   # position past the context
+        assert step(3, 0) == hk.ERR_SHAPE    # top-k 0
+        assert step(3, 17) == hk.ERR_SHAPE   # top-k above max_top_k
+    finally:
+        assert L.hpc_draft_release(h) == hk.OK
