@@ -21,10 +21,13 @@
 // m16n8 accumulator tiles.  Per 256-block the CTA stages its 4 weight units
 // (the row-tile layout of hc_common.cuh, unchanged) and its 64 columns' Q8_K
 // records with cp.async into one of two shared-memory stages, so block b + 1
-// streams in while block b is computed.  The tile layout already stores the
-// 4-bit / 6-bit values in the order the dp4a path pairs them with the record
-// bytes; read with lane = (row, 4-word group), the same words are exactly the
-// A fragments of m16n8k32 (Q4_K) / m16n8k16 (Q6_K), and the record words are
+// streams in while block b is computed.  The records are staged at a
+// 304-byte stride, which keeps the B-fragment loads of the eight columns in
+// distinct banks.  Launches of fewer CTAs than two per SM (the 2048-row
+// projections) split K in two halves over grid.z, whose partials are added
+// atomically into a zeroed output: with exactly two addends the sum does not
+// depend on their order.  The block products themselves are hc_mma.cuh's:
+// the row-tile layout's words are directly the A fragments, the record words
 // the B fragments, so no repack is needed.
 #include "hc_bulk.cuh"
 #include "hc_common.cuh"
