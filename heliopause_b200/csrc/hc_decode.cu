@@ -183,7 +183,12 @@ __global__ void norm_quant_kernel(const float* x, float* x_out, const float* __r
 // softmax (max, sum of f64 exp) and the partial output p*v are written for
 // the combine kernel.
 constexpr int ATT_KSTRIDE = 256 + 4;        // floats per staged K row
-constexpr int ATT_QB = 8;                   // queries per thread per pass (scores and outputs)
+constexpr int ATT_QB = 8;                   // queries per thread per output pass (wide form)
+constexpr int ATT_QBS = 4;                  // queries per thread per score pass (wide form)
+// The wide form (more than four query vectors per KV head) runs twice the
+// threads: its ~155 KB of staged rows and queries hold one CTA per SM, and
+// eight warps there left the scheduler idle (44% issue, latency-bound).
+constexpr int ATT_WIDE_THREADS = 2 * ATT_THREADS;
 
 // One warp: QK-norm (f64 sum of squares, layers.ts:871-885 normHeads) of a
 // 256-vector held 8 values per lane (lane L: dimensions 8L..8L+7), optional
@@ -234,7 +239,7 @@ __device__ __forceinline__ void load_rope8(const double* cos_row, const double* 
 }
 
 template <bool WIDE>
-__global__ void __launch_bounds__(ATT_THREADS) attn_partial_kernel(
+__global__ void __launch_bounds__(WIDE ? ATT_WIDE_THREADS : ATT_THREADS) attn_partial_kernel(
     const float* __restrict__ q, const float* __restrict__ kraw, const float* __restrict__ vraw,
     const float* __restrict__ qnw, const float* __restrict__ knw, const double* __restrict__ cos_t,
     const double* __restrict__ sin_t, double eps, int own_kv, float* __restrict__ kc, float* __restrict__ vc,
@@ -362,18 +367,18 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_partial_kernel(
       ps[pr] = (t < nt && t0 + t <= pos[m]) ? dot * scale : -INFINITY;
     }
   } else {
-    constexpr int QL = ATT_THREADS / CH;  // query lanes
+    constexpr int QL = ATT_WIDE_THREADS / CH;  // query lanes
     const int t = int(threadIdx.x) % CH, qg = int(threadIdx.x) / CH;
     const float4* kv = reinterpret_cast<const float4*>(ks + t * ATT_KSTRIDE);
-    for (int q0 = qg; q0 < NQ; q0 += QL * ATT_QB) {
-      float4 acc[ATT_QB];
+    for (int q0 = qg; q0 < NQ; q0 += QL * ATT_QBS) {
+      float4 acc[ATT_QBS];
 #pragma unroll
-      for (int u = 0; u < ATT_QB; ++u) acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int u = 0; u < ATT_QBS; ++u) acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll 4
       for (int j = 0; j < HD / 4; ++j) {
         const float4 b = kv[j];
 #pragma unroll
-        for (int u = 0; u < ATT_QB; ++u) {
+        for (int u = 0; u < ATT_QBS; ++u) {
           if (q0 + QL * u < NQ) {
             const float4 a = reinterpret_cast<const float4*>(qs + (q0 + QL * u) * HD)[j];
             acc[u].x = fmaf(a.x, b.x, acc[u].x);
@@ -384,7 +389,7 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_partial_kernel(
         }
       }
 #pragma unroll
-      for (int u = 0; u < ATT_QB; ++u) {
+      for (int u = 0; u < ATT_QBS; ++u) {
         const int qi = q0 + QL * u;
         if (qi < NQ) {
           const float dot = (acc[u].x + acc[u].y) + (acc[u].z + acc[u].w);
@@ -418,8 +423,9 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_partial_kernel(
   __syncthreads();
   // partial outputs: thread d walks column d of the staged V rows (a warp
   // reads 32 consecutive floats of a row) and serves four queries per pass
-  // (NQ <= 4) or ATT_QB (wider steps); the probabilities are broadcast reads
-  const int d = threadIdx.x;
+  // (NQ <= 4) or ATT_QB (wider steps, where the two halves of the CTA take
+  // alternate passes); the probabilities are broadcast reads
+  const int d = threadIdx.x & (HD - 1);
   if (!WIDE) {
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll 4
@@ -439,7 +445,7 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_partial_kernel(
       if (u < NQ) part_o[((size_t(chunk) * KVH + kvh) * NQ + u) * HD + d] = acc[u];
     return;
   }
-  for (int qg = 0; qg < NQ; qg += ATT_QB) {
+  for (int qg = int(threadIdx.x / HD) * ATT_QB; qg < NQ; qg += (ATT_WIDE_THREADS / HD) * ATT_QB) {
     float acc[ATT_QB];
 #pragma unroll
     for (int u = 0; u < ATT_QB; ++u) acc[u] = 0.f;
@@ -1000,7 +1006,7 @@ cudaError_t launch_attention(const float* q, const float* kraw, const float* vra
   const int chunks = cap / ATT_CHUNK;
   // more than four query vectors per KV head: the register-blocked form
   if (M * (H / KVH) > ATT_THREADS / ATT_CHUNK)
-    return pdl_launch(attn_partial_kernel<true>, dim3(chunks, KVH), dim3(ATT_THREADS), smem, st, q, kraw, vraw, qnw,
+    return pdl_launch(attn_partial_kernel<true>, dim3(chunks, KVH), dim3(ATT_WIDE_THREADS), smem, st, q, kraw, vraw, qnw,
                       knw, cos_t, sin_t, eps, int(own_kv), kc, vc, pos, M, H, KVH, cap, scale, part_m, part_l, part_o,
                       err);
   return pdl_launch(attn_partial_kernel<false>, dim3(chunks, KVH), dim3(ATT_THREADS), smem, st, q, kraw, vraw, qnw,
