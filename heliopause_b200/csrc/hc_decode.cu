@@ -183,8 +183,8 @@ __global__ void norm_quant_kernel(const float* x, float* x_out, const float* __r
 // softmax (max, sum of f64 exp) and the partial output p*v are written for
 // the combine kernel.
 constexpr int ATT_KSTRIDE = 256 + 4;        // floats per staged K row
-constexpr int ATT_QB = 8;                   // queries per thread per output pass (wide form)
-constexpr int ATT_QBS = 4;                  // queries per thread per score pass (wide form)
+constexpr int ATT_QB = 8;                   // general wide form: queries per thread per output pass
+constexpr int ATT_QBS = 4;                  // general wide form: queries per thread per score pass
 // The wide form (more than four query vectors per KV head) runs twice the
 // threads: its ~155 KB of staged rows and queries hold one CTA per SM, and
 // eight warps there left the scheduler idle (44% issue, latency-bound).
@@ -238,7 +238,10 @@ __device__ __forceinline__ void load_rope8(const double* cos_row, const double* 
   }
 }
 
-template <bool WIDE>
+// Wide form: QS query slots per thread in the score pass (ATT_WIDE_THREADS /
+// ATT_CHUNK query lanes) and PB per half of the CTA in the output pass.  The
+// loops cover any NQ; sized to NQ no slot idles (a slot past NQ still issues).
+template <bool WIDE, int QS = ATT_QBS, int PB = ATT_QB>
 __global__ void __launch_bounds__(WIDE ? ATT_WIDE_THREADS : ATT_THREADS) attn_partial_kernel(
     const float* __restrict__ q, const float* __restrict__ kraw, const float* __restrict__ vraw,
     const float* __restrict__ qnw, const float* __restrict__ knw, const double* __restrict__ cos_t,
@@ -343,8 +346,8 @@ __global__ void __launch_bounds__(WIDE ? ATT_WIDE_THREADS : ATT_THREADS) attn_pa
   // scores.  One KV head's query vectors for one token (NQ <= 4): thread per
   // (query, token); a warp shares the query (broadcast reads) and walks 32
   // padded K rows.  Wider steps: thread (token t = tid % CH, query lane qg =
-  // tid / CH) computes the dots of queries qg, qg + QL, ... (up to ATT_QB
-  // per pass) with token t, so each 16-byte piece of its K row is read once
+  // tid / CH) computes the dots of queries qg, qg + QL, ... (QS per pass)
+  // with token t, so each 16-byte piece of its K row is read once
   // for all of them.  Both forms keep the same order inside a dot (four lanes
   // of partial sums, then (x + y) + (z + w)), so a dot does not depend on how
   // many tokens the step carries.
@@ -370,15 +373,15 @@ __global__ void __launch_bounds__(WIDE ? ATT_WIDE_THREADS : ATT_THREADS) attn_pa
     constexpr int QL = ATT_WIDE_THREADS / CH;  // query lanes
     const int t = int(threadIdx.x) % CH, qg = int(threadIdx.x) / CH;
     const float4* kv = reinterpret_cast<const float4*>(ks + t * ATT_KSTRIDE);
-    for (int q0 = qg; q0 < NQ; q0 += QL * ATT_QBS) {
-      float4 acc[ATT_QBS];
+    for (int q0 = qg; q0 < NQ; q0 += QL * QS) {
+      float4 acc[QS];
 #pragma unroll
-      for (int u = 0; u < ATT_QBS; ++u) acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int u = 0; u < QS; ++u) acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll 4
       for (int j = 0; j < HD / 4; ++j) {
         const float4 b = kv[j];
 #pragma unroll
-        for (int u = 0; u < ATT_QBS; ++u) {
+        for (int u = 0; u < QS; ++u) {
           if (q0 + QL * u < NQ) {
             const float4 a = reinterpret_cast<const float4*>(qs + (q0 + QL * u) * HD)[j];
             acc[u].x = fmaf(a.x, b.x, acc[u].x);
@@ -389,7 +392,7 @@ __global__ void __launch_bounds__(WIDE ? ATT_WIDE_THREADS : ATT_THREADS) attn_pa
         }
       }
 #pragma unroll
-      for (int u = 0; u < ATT_QBS; ++u) {
+      for (int u = 0; u < QS; ++u) {
         const int qi = q0 + QL * u;
         if (qi < NQ) {
           const float dot = (acc[u].x + acc[u].y) + (acc[u].z + acc[u].w);
@@ -423,7 +426,7 @@ __global__ void __launch_bounds__(WIDE ? ATT_WIDE_THREADS : ATT_THREADS) attn_pa
   __syncthreads();
   // partial outputs: thread d walks column d of the staged V rows (a warp
   // reads 32 consecutive floats of a row) and serves four queries per pass
-  // (NQ <= 4) or ATT_QB (wider steps, where the two halves of the CTA take
+  // (NQ <= 4) or PB (wider steps, where the two halves of the CTA take
   // alternate passes); the probabilities are broadcast reads
   const int d = threadIdx.x & (HD - 1);
   if (!WIDE) {
@@ -445,16 +448,16 @@ __global__ void __launch_bounds__(WIDE ? ATT_WIDE_THREADS : ATT_THREADS) attn_pa
       if (u < NQ) part_o[((size_t(chunk) * KVH + kvh) * NQ + u) * HD + d] = acc[u];
     return;
   }
-  for (int qg = int(threadIdx.x / HD) * ATT_QB; qg < NQ; qg += (ATT_WIDE_THREADS / HD) * ATT_QB) {
-    float acc[ATT_QB];
+  for (int qg = int(threadIdx.x / HD) * PB; qg < NQ; qg += (ATT_WIDE_THREADS / HD) * PB) {
+    float acc[PB];
 #pragma unroll
-    for (int u = 0; u < ATT_QB; ++u) acc[u] = 0.f;
+    for (int u = 0; u < PB; ++u) acc[u] = 0.f;
 #pragma unroll 2
     for (int j = 0; j < CH / 4; ++j) {
       const float b[4] = {vs[(4 * j) * ATT_KSTRIDE + d], vs[(4 * j + 1) * ATT_KSTRIDE + d],
                           vs[(4 * j + 2) * ATT_KSTRIDE + d], vs[(4 * j + 3) * ATT_KSTRIDE + d]};
 #pragma unroll
-      for (int u = 0; u < ATT_QB; ++u) {
+      for (int u = 0; u < PB; ++u) {
         if (qg + u < NQ) {
           const float4 a = reinterpret_cast<const float4*>(ps + (qg + u) * CH)[j];
           acc[u] += a.x * b[0] + a.y * b[1] + a.z * b[2] + a.w * b[3];
@@ -462,7 +465,7 @@ __global__ void __launch_bounds__(WIDE ? ATT_WIDE_THREADS : ATT_THREADS) attn_pa
       }
     }
 #pragma unroll
-    for (int u = 0; u < ATT_QB; ++u)
+    for (int u = 0; u < PB; ++u)
       if (qg + u < NQ) part_o[((size_t(chunk) * KVH + kvh) * NQ + qg + u) * HD + d] = acc[u];
   }
 }
@@ -984,6 +987,23 @@ size_t attn_smem_bytes(int M, int H, int KVH) {
   return sizeof(float) * (size_t(ATT_CHUNK) * ATT_KSTRIDE * 2 + size_t(NQ) * 256 + size_t(NQ) * ATT_CHUNK);
 }
 
+namespace {
+using AttnKernel = decltype(&attn_partial_kernel<false>);
+// Wide forms sized to NQ = 8, 12, ..., 32 query vectors per KV head (four
+// heads per KV head at 2..8 tokens): ceil(NQ / 8) score slots and
+// ceil(NQ / 2) output slots per half, so every slot holds a query and the
+// two halves each take one output pass.  Index (NQ - 8) / 4.
+constexpr AttnKernel kAttnSized[] = {
+    attn_partial_kernel<true, 1, 4>,  attn_partial_kernel<true, 2, 6>,  attn_partial_kernel<true, 2, 8>,
+    attn_partial_kernel<true, 3, 10>, attn_partial_kernel<true, 3, 12>, attn_partial_kernel<true, 4, 14>,
+    attn_partial_kernel<true, 4, 16>};
+
+AttnKernel attn_wide_kernel(int nq) {
+  if (nq >= 8 && nq <= 32 && nq % 4 == 0) return kAttnSized[(nq - 8) / 4];
+  return attn_partial_kernel<true>;
+}
+}  // namespace
+
 cudaError_t launch_attention(const float* q, const float* kraw, const float* vraw, const float* qnw, const float* knw,
                              const double* cos_t, const double* sin_t, double eps, bool own_kv, float* kc, float* vc,
                              const int32_t* pos, int M, int H, int KVH, int cap, float scale, float* part_m,
@@ -992,8 +1012,11 @@ cudaError_t launch_attention(const float* q, const float* kraw, const float* vra
   const size_t smem = attn_smem_bytes(M, H, KVH);
   static bool attr = false;
   if (!attr) {
-    for (const void* fn : {reinterpret_cast<const void*>(attn_partial_kernel<false>),
-                           reinterpret_cast<const void*>(attn_partial_kernel<true>)}) {
+    AttnKernel all[] = {attn_partial_kernel<false>, attn_partial_kernel<true>, kAttnSized[0], kAttnSized[1],
+                        kAttnSized[2],              kAttnSized[3],             kAttnSized[4], kAttnSized[5],
+                        kAttnSized[6]};
+    for (AttnKernel k : all) {
+      const void* fn = reinterpret_cast<const void*>(k);
       cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
       if (e != cudaSuccess) return e;
       // maximal shared-memory carveout: the SMs still running the QKV GEMV's
@@ -1006,7 +1029,7 @@ cudaError_t launch_attention(const float* q, const float* kraw, const float* vra
   const int chunks = cap / ATT_CHUNK;
   // more than four query vectors per KV head: the register-blocked form
   if (M * (H / KVH) > ATT_THREADS / ATT_CHUNK)
-    return pdl_launch(attn_partial_kernel<true>, dim3(chunks, KVH), dim3(ATT_WIDE_THREADS), smem, st, q, kraw, vraw, qnw,
+    return pdl_launch(attn_wide_kernel(M * (H / KVH)), dim3(chunks, KVH), dim3(ATT_WIDE_THREADS), smem, st, q, kraw, vraw, qnw,
                       knw, cos_t, sin_t, eps, int(own_kv), kc, vc, pos, M, H, KVH, cap, scale, part_m, part_l, part_o,
                       err);
   return pdl_launch(attn_partial_kernel<false>, dim3(chunks, KVH), dim3(ATT_THREADS), smem, st, q, kraw, vraw, qnw,
