@@ -240,7 +240,8 @@ __device__ __forceinline__ void load_rope8(const double* cos_row, const double* 
 
 // Wide form: QS query slots per thread in the score pass (ATT_WIDE_THREADS /
 // ATT_CHUNK query lanes) and PB per half of the CTA in the output pass.  The
-// loops cover any NQ; sized to NQ no slot idles (a slot past NQ still issues).
+// loops cover any NQ; sized to NQ, a thread idles at most one score slot and
+// no output slot (a slot past NQ still issues its instructions).
 template <bool WIDE, int QS = ATT_QBS, int PB = ATT_QB>
 __global__ void __launch_bounds__(WIDE ? ATT_WIDE_THREADS : ATT_THREADS) attn_partial_kernel(
     const float* __restrict__ q, const float* __restrict__ kraw, const float* __restrict__ vraw,
@@ -991,8 +992,10 @@ namespace {
 using AttnKernel = decltype(&attn_partial_kernel<false>);
 // Wide forms sized to NQ = 8, 12, ..., 32 query vectors per KV head (four
 // heads per KV head at 2..8 tokens): ceil(NQ / 8) score slots and
-// ceil(NQ / 2) output slots per half, so every slot holds a query and the
-// two halves each take one output pass.  Index (NQ - 8) / 4.
+// ceil(NQ / 2) output slots per half: every output slot holds a query, the
+// two halves each take one output pass, and a score lane idles at most one
+// slot (at NQ = 20, lanes 4..7 have two queries for three slots).  Index
+// (NQ - 8) / 4.
 constexpr AttnKernel kAttnSized[] = {
     attn_partial_kernel<true, 1, 4>,  attn_partial_kernel<true, 2, 6>,  attn_partial_kernel<true, 2, 8>,
     attn_partial_kernel<true, 3, 10>, attn_partial_kernel<true, 3, 12>, attn_partial_kernel<true, 4, 14>,
