@@ -87,6 +87,25 @@ def test_small_decode_and_verify_match_oracle():
         gpu.close()
 
 
+@pytest.mark.parametrize("m", [2, 3, 4, 6, 7, 8])
+def test_verify_widths_match_oracle(m):
+    # Every step width the model accepts (max_tokens 8) against the oracle.
+    # Widths 2..8 carry 4*m query vectors per KV head, and each width takes
+    # its own attention instantiation, with query slots sized to that count.
+    # Width 2 runs the dp4a GEMVs; widths 3..8 run the tensor-core GEMV and
+    # LM head.
+    k = 40
+    gpu, ref = _build(SMALL, filled=40, seed=7 + m)
+    try:
+        toks = [(17 + 613 * i) % SMALL.vocab for i in range(m)]
+        pos = list(range(40, 40 + m))
+        ids_g, vals_g, hid_g = gpu.forward(toks, pos, k, return_hidden=True)
+        ids_r, vals_r, hid_r, logits_r = ref.forward(toks, pos, k)
+        _check_step(ids_g.cpu().numpy(), vals_g.cpu().numpy(), hid_g.cpu().numpy(), ids_r, vals_r, hid_r, logits_r, k)
+    finally:
+        gpu.close()
+
+
 def test_verify_equals_sequential_decodes():
     # A batched verify over positions p..p+4 must equal five single-token
     # decodes (the causal mask makes them the same computation).
