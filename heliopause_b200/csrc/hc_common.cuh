@@ -42,7 +42,19 @@
 #include <cstdint>
 #include <cuda_runtime.h>
 
+#include "hc_once.h"
+
 namespace hc {
+
+// once_per_device (hc_once.h) on the calling thread's current device: a
+// launcher's one-time kernel-attribute set-up, done again on each device.
+template <class F>
+inline cudaError_t once_per_current_device(std::atomic<uint64_t>& done, F&& set) {
+  int dev = 0;
+  const cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  return once_per_device<cudaError_t>(done, dev, static_cast<F&&>(set));
+}
 
 constexpr int QK = 256;
 constexpr int TILE = 32;

@@ -1013,22 +1013,23 @@ cudaError_t launch_attention(const float* q, const float* kraw, const float* vra
                              float* part_l, float* part_o, int* err, cudaStream_t st) {
   if (cap % ATT_CHUNK != 0 || cap > 4096) return cudaErrorInvalidValue;
   const size_t smem = attn_smem_bytes(M, H, KVH);
-  static bool attr = false;
-  if (!attr) {
-    AttnKernel all[] = {attn_partial_kernel<false>, attn_partial_kernel<true>, kAttnSized[0], kAttnSized[1],
-                        kAttnSized[2],              kAttnSized[3],             kAttnSized[4], kAttnSized[5],
-                        kAttnSized[6]};
+  static std::atomic<uint64_t> attr{0};
+  const cudaError_t ea = once_per_current_device(attr, [] {
+    const AttnKernel all[] = {attn_partial_kernel<false>, attn_partial_kernel<true>, kAttnSized[0], kAttnSized[1],
+                              kAttnSized[2],              kAttnSized[3],             kAttnSized[4], kAttnSized[5],
+                              kAttnSized[6]};
     for (AttnKernel k : all) {
       const void* fn = reinterpret_cast<const void*>(k);
-      cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
+      const cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
       if (e != cudaSuccess) return e;
       // maximal shared-memory carveout: the SMs still running the QKV GEMV's
       // CTAs can take an attention CTA (~140 KB) without draining first
       // (measured: decode +1.6%; the GEMVs keep the default split)
       use_max_carveout(fn);
     }
-    attr = true;
-  }
+    return cudaSuccess;
+  });
+  if (ea != cudaSuccess) return ea;
   const int chunks = cap / ATT_CHUNK;
   // more than four query vectors per KV head: the register-blocked form
   if (M * (H / KVH) > ATT_THREADS / ATT_CHUNK)
@@ -1086,13 +1087,11 @@ cudaError_t launch_prefill_attention_split(const float* qh, const float* kc, con
                                            float* part_o, const Q8Buf& qo, float* attn_out, cudaStream_t st) {
   if (H / KVH > 4 || nsplit < 1 || nsplit > 64) return cudaErrorInvalidValue;
   const size_t smem = prefill_split_smem_bytes(H, KVH);
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e =
-        cudaFuncSetAttribute(prefill_attn_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    if (e != cudaSuccess) return e;
-    attr = true;
-  }
+  static std::atomic<uint64_t> attr{0};
+  const cudaError_t ea = once_per_current_device(attr, [] {
+    return cudaFuncSetAttribute(prefill_attn_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+  });
+  if (ea != cudaSuccess) return ea;
   const int tiles = (M + PF_QT - 1) / PF_QT;
   prefill_attn_split_kernel<<<dim3(unsigned(tiles * nsplit), unsigned(KVH)), 256, smem, st>>>(
       qh, kc, vc, pos, M, H, KVH, cap, nsplit, part_m, part_l, part_o);
@@ -1107,12 +1106,11 @@ cudaError_t launch_prefill_attention(const float* qh, const float* kc, const flo
                                      int H, int KVH, int cap, const Q8Buf& qo, float* attn_out, cudaStream_t st) {
   if (H / KVH > 8) return cudaErrorInvalidValue;
   const size_t smem = prefill_attn_smem_bytes(H, KVH);
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(prefill_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-    if (e != cudaSuccess) return e;
-    attr = true;
-  }
+  static std::atomic<uint64_t> attr{0};
+  const cudaError_t ea = once_per_current_device(attr, [smem] {
+    return cudaFuncSetAttribute(prefill_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  });
+  if (ea != cudaSuccess) return ea;
   prefill_attn_kernel<<<dim3(unsigned((M + PF_QT - 1) / PF_QT), unsigned(KVH)), 256, smem, st>>>(
       qh, kc, vc, pos, M, H, KVH, cap, qo, attn_out);
   return cudaGetLastError();

@@ -126,12 +126,11 @@ __global__ void __launch_bounds__(TC_THREADS, 2) gemm_tc_kernel(const __grid_con
 template <int TYPE>
 static cudaError_t launch_tc(const TcParams& p, cudaStream_t st) {
   const size_t smem = 2 * size_t(TcType<TYPE>::STAGE);
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<TYPE>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-    if (e != cudaSuccess) return e;
-    attr = true;
-  }
+  static std::atomic<uint64_t> attr{0};
+  const cudaError_t ea = once_per_current_device(attr, [smem] {
+    return cudaFuncSetAttribute(gemm_tc_kernel<TYPE>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  });
+  if (ea != cudaSuccess) return ea;
   const dim3 grid(unsigned((p.tiles + TC_TILES - 1) / TC_TILES), unsigned((p.ncols + TC_COLS - 1) / TC_COLS),
                   unsigned(p.ksplit));
   if (p.ksplit > 1) {

@@ -408,13 +408,11 @@ static cudaError_t launch_nc(const GemvParams& p, cudaStream_t stream) {
   if (p.bulk) smem += size_t(GEMV_WARPS_PER_CTA) * p.bps * unit_bytes(UC == Q4K_CHUNKS ? TYPE_Q4_K : TYPE_Q6_K);
   else smem += size_t(GEMV_WARPS_PER_CTA) * p.pre * unit_bytes(UC == Q4K_CHUNKS ? TYPE_Q4_K : TYPE_Q6_K);
   if (smem > size_t(GEMV_MAX_SMEM)) return cudaErrorInvalidValue;
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaError_t e =
-        cudaFuncSetAttribute(gemv_kernel<NC, UC>, cudaFuncAttributeMaxDynamicSharedMemorySize, GEMV_MAX_SMEM);
-    if (e != cudaSuccess) return e;
-    attr_set = true;
-  }
+  static std::atomic<uint64_t> attr_set{0};
+  const cudaError_t ea = once_per_current_device(attr_set, [] {
+    return cudaFuncSetAttribute(gemv_kernel<NC, UC>, cudaFuncAttributeMaxDynamicSharedMemorySize, GEMV_MAX_SMEM);
+  });
+  if (ea != cudaSuccess) return ea;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(unsigned(gemv_grid(p)));
   cfg.blockDim = dim3(GEMV_THREADS);

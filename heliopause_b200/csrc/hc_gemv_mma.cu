@@ -240,12 +240,11 @@ static cudaError_t launch_gemv_mma_w(GemvParams& p, cudaStream_t stream) {
   size_t smem;
   gemv_mma_plan<W>(p, &grid, &smem);
   if (p.split == 0 || smem > size_t(GEMV_MAX_SMEM)) return cudaErrorInvalidValue;
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(gemv_mma_kernel<W>, cudaFuncAttributeMaxDynamicSharedMemorySize, GEMV_MAX_SMEM);
-    if (e != cudaSuccess) return e;
-    attr_set = true;
-  }
+  static std::atomic<uint64_t> attr_set{0};
+  const cudaError_t ea = once_per_current_device(attr_set, [] {
+    return cudaFuncSetAttribute(gemv_mma_kernel<W>, cudaFuncAttributeMaxDynamicSharedMemorySize, GEMV_MAX_SMEM);
+  });
+  if (ea != cudaSuccess) return ea;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(unsigned(grid));
   cfg.blockDim = dim3(GmShape<W>::THREADS);

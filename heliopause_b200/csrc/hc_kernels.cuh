@@ -1,6 +1,7 @@
 // hc_kernels.cuh -- launchers shared between the kernel files and the C ABI.
 #pragma once
 #include <mutex>
+#include <utility>
 #include <vector>
 
 #include "hc_common.cuh"
@@ -81,18 +82,20 @@ inline size_t gemv_static_smem(int ncols) {
 
 __host__ __device__ inline int unit_bytes(int type) { return int(tile_block_bytes(type)); }
 
-// Asks for the maximal shared-memory carveout for kernel `fn` (once), so its
-// CTAs, launched early under programmatic dependent launch, can join SMs
-// that still run the previous kernel without those SMs first draining to
-// change their L1 / shared-memory split.
+// Asks for the maximal shared-memory carveout for kernel `fn` (once per
+// device), so its CTAs, launched early under programmatic dependent launch,
+// can join SMs that still run the previous kernel without those SMs first
+// draining to change their L1 / shared-memory split.
 inline void use_max_carveout(const void* fn) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return;
   static std::mutex mu;
-  static std::vector<const void*> done;
+  static std::vector<std::pair<const void*, int>> done;
   std::lock_guard<std::mutex> lock(mu);
-  for (const void* d : done)
-    if (d == fn) return;
+  for (const auto& d : done)
+    if (d.first == fn && d.second == dev) return;
   cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout, int(cudaSharedmemCarveoutMaxShared));
-  done.push_back(fn);
+  done.emplace_back(fn, dev);
 }
 
 cudaError_t launch_q8k_quantize(const float* x, int K, int cols, const Q8Buf& q, int8_t* nat_qs, int16_t* nat_bs32,

@@ -260,12 +260,11 @@ cudaError_t launch_lmhead_mma(LmHeadParams& P, int grid, cudaStream_t stream) {
   const size_t smem = lmm_smem(P, ring);
   if (smem > size_t(GEMV_MAX_SMEM)) return cudaErrorInvalidValue;
   P.g.ring = ring;
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(lmhead_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, GEMV_MAX_SMEM);
-    if (e != cudaSuccess) return e;
-    attr_set = true;
-  }
+  static std::atomic<uint64_t> attr_set{0};
+  const cudaError_t ea = once_per_current_device(attr_set, [] {
+    return cudaFuncSetAttribute(lmhead_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, GEMV_MAX_SMEM);
+  });
+  if (ea != cudaSuccess) return ea;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(unsigned(grid));
   cfg.blockDim = dim3(LMM_WARPS * 32);
@@ -568,13 +567,11 @@ int lmhead_grid(int ntiles) { return persistent_grid(ntiles, sm_count() * GEMV_C
 
 template <int NC>
 static cudaError_t launch_lm_nc(const LmHeadParams& P, int grid, cudaStream_t stream) {
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(lmhead_topk_kernel<NC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         GEMV_MAX_SMEM);
-    if (e != cudaSuccess) return e;
-    attr_set = true;
-  }
+  static std::atomic<uint64_t> attr_set{0};
+  const cudaError_t ea = once_per_current_device(attr_set, [] {
+    return cudaFuncSetAttribute(lmhead_topk_kernel<NC>, cudaFuncAttributeMaxDynamicSharedMemorySize, GEMV_MAX_SMEM);
+  });
+  if (ea != cudaSuccess) return ea;
   const size_t smem = gemv_smem_bytes(P.g, P.g.nb);
   if (smem > size_t(GEMV_MAX_SMEM)) return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg = {};

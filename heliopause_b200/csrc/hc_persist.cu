@@ -1175,10 +1175,13 @@ int persist_maxseg(int tiles, int B, int grid, bool* warp_tiles_ok) {
 }
 
 int persist_grid() {
-  static int cached = -1;
-  if (cached >= 0) return cached;
+  // per device: the grid + 1 once computed, 0 before (a failed query is not
+  // kept, so the next call asks again)
+  static std::atomic<int> cached[64];
   int dev = 0, sms = 0, per_sm = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+  const int c = cached[dev].load(std::memory_order_acquire);
+  if (c > 0) return c - 1;
   if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
   if (cudaFuncSetAttribute(persistent_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(SM_TOTAL)) !=
       cudaSuccess)
@@ -1186,8 +1189,9 @@ int persist_grid() {
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, persistent_step_kernel, P_THREADS, SM_TOTAL) !=
       cudaSuccess)
     return 0;
-  cached = per_sm >= 1 ? sms : 0;
-  return cached;
+  const int grid = per_sm >= 1 ? sms : 0;
+  cached[dev].store(grid + 1, std::memory_order_release);
+  return grid;
 }
 
 cudaError_t launch_persistent_step(const PParams& p, int grid, cudaStream_t st) {

@@ -64,7 +64,10 @@ int hpc_device_error(void);
 
 /* Select the device for subsequent calls on this thread and check it is an
  * sm_100 part.  Replaces prefillWasmExports() instantiation
- * (runner/wasm/wasm-kernels.ts:416-426). */
+ * (runner/wasm/wasm-kernels.ts:416-426).  One process may drive several
+ * devices, one per host thread.  Each launcher sets its kernel attributes
+ * on a device at its first call there; make that first call outside any
+ * stream capture. */
 int hpc_device_init(int device);
 
 /* Upload a GGUF-layout weight (host bytes) and repack it in HBM.  Only Q4_K
