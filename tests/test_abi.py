@@ -55,3 +55,62 @@ def test_assert_cuda_ok_messages():
         kernels.assert_cuda_ok(kernels.ERR_CUDA, "x")
     kernels.assert_cuda_ok(kernels.OK, "x")
     assert kernels.quantized_type_id("Q4_K") == 1 and kernels.quantized_type_id("Q6_K") == 3
+
+
+# ---- prototypes in include/*.h against the ctypes table -----------------------
+
+_C_SCALARS = {"size_t": ("u", 8), "int": ("i", 4), "int32_t": ("i", 4), "uint32_t": ("u", 4),
+              "int64_t": ("i", 8), "uint64_t": ("u", 8), "float": ("f", 4), "double": ("f", 8)}
+_C_HANDLES = {"hpc_weight", "hpc_model", "hpc_draft"}  # typedefs of struct pointers
+
+
+def _header_prototypes():
+    """name -> (return type, [parameter declarations]) for every hpc_* prototype."""
+    import re
+    protos = {}
+    for h in _lib.HEADERS:
+        src = h.read_text()
+        src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+        src = re.sub(r"//[^\n]*", "", src)
+        src = re.sub(r"^[ \t]*#[^\n]*", "", src, flags=re.M)
+        for ret, name, params in re.findall(r"([A-Za-z_][\w\s*]*?)\b(hpc_\w+)\s*\(([^)]*)\)\s*;", src):
+            ps = [" ".join(p.split()) for p in params.split(",")]
+            protos[name] = (" ".join(ret.split()), [] if ps in (["void"], [""]) else ps)
+    return protos
+
+
+def _c_kind(decl):
+    """'p' for pointers and handles, else (signedness/float, bytes)."""
+    if "*" in decl:
+        return "p"
+    words = [w for w in decl.split() if w not in ("const", "volatile")]
+    base = words[0] if len(words) == 1 else " ".join(words[:-1])  # drop the parameter name
+    if base in _C_HANDLES:
+        return "p"
+    assert base in _C_SCALARS, f"unclassified C type {base!r} in {decl!r}"
+    return _C_SCALARS[base]
+
+
+def _ctypes_kind(t):
+    if t in (C.c_void_p, C.c_char_p) or (isinstance(t, type) and issubclass(t, C._Pointer)):
+        return "p"
+    if t in (C.c_float, C.c_double):
+        return ("f", C.sizeof(t))
+    return ("i" if t(-1).value < 0 else "u", C.sizeof(t))
+
+
+def test_ctypes_signatures_match_header_prototypes():
+    protos = _header_prototypes()
+    assert sorted(protos) == _lib.header_symbols()
+    bad = []
+    for name, (res, args) in _lib.SIGNATURES.items():
+        ret, params = protos[name]
+        if len(params) != len(args):
+            bad.append(f"{name}: {len(params)} parameters in the header, {len(args)} in ctypes")
+            continue
+        if _c_kind(ret + " r") != _ctypes_kind(res):
+            bad.append(f"{name}: return {ret!r} vs {res}")
+        for i, (decl, t) in enumerate(zip(params, args)):
+            if _c_kind(decl) != _ctypes_kind(t):
+                bad.append(f"{name} arg {i} {decl!r}: {_c_kind(decl)} vs ctypes {t} {_ctypes_kind(t)}")
+    assert not bad, "\n".join(bad)
