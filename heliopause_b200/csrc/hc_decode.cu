@@ -1013,6 +1013,7 @@ cudaError_t launch_attention(const float* q, const float* kraw, const float* vra
                              float* part_l, float* part_o, int* err, cudaStream_t st) {
   if (cap % ATT_CHUNK != 0 || cap > 4096) return cudaErrorInvalidValue;
   const size_t smem = attn_smem_bytes(M, H, KVH);
+  if (smem > ATT_MAX_SMEM) return cudaErrorInvalidValue;
   static std::atomic<uint64_t> attr{0};
   const cudaError_t ea = once_per_current_device(attr, [] {
     const AttnKernel all[] = {attn_partial_kernel<false>, attn_partial_kernel<true>, kAttnSized[0], kAttnSized[1],
@@ -1020,7 +1021,7 @@ cudaError_t launch_attention(const float* q, const float* kraw, const float* vra
                               kAttnSized[6]};
     for (AttnKernel k : all) {
       const void* fn = reinterpret_cast<const void*>(k);
-      const cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
+      const cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(ATT_MAX_SMEM));
       if (e != cudaSuccess) return e;
       // maximal shared-memory carveout: the SMs still running the QKV GEMV's
       // CTAs can take an attention CTA (~140 KB) without draining first

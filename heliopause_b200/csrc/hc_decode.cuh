@@ -14,7 +14,10 @@ cudaError_t launch_embed(const uint8_t* w, int type, int nb, int vocab, const in
 cudaError_t launch_norm_quant(bool resid, const float* x, float* x_out, const float* y, const float* w_post,
                               const float* w_pre, double eps, int M, int D, const Q8Buf& q, float* n_out,
                               cudaStream_t st);
+// Dynamic shared memory of one attention CTA for M tokens (staged K/V rows,
+// queries, scores), and the most the attention kernels are allowed.
 size_t attn_smem_bytes(int M, int H, int KVH);
+constexpr size_t ATT_MAX_SMEM = 220 * 1024;
 // Attention over the raw q (and, in an own-KV layer, raw k/v) projections of
 // M tokens: QK-norm + RoPE of the queries and of this step's K/V rows (written
 // to kc/vc), split-KV partials into part_m/part_l/part_o for

@@ -106,6 +106,13 @@ static int check_cfg(const hpc_model_config* c) {
   if (c->context <= 0 || c->context % 64 != 0 || c->context > 4096 || c->vocab <= 0)
     return hpc_fail(HPC_ERR_SHAPE, "context %d: a multiple of 64 up to 4096; vocab %d", c->context, c->vocab);
   if (c->max_tokens < 1 || c->max_tokens > 8) return hpc_fail(HPC_ERR_SHAPE, "max_tokens %d: 1..8", c->max_tokens);
+  // an attention CTA stages the queries of every token for its KV head: the
+  // widest step must fit the attention kernels' shared memory
+  const size_t att_smem = hc::attn_smem_bytes(c->max_tokens, c->heads, c->kv_heads);
+  if (att_smem > hc::ATT_MAX_SMEM)
+    return hpc_fail(HPC_ERR_SHAPE,
+                    "max_tokens %d x %d query heads per KV head needs %zu bytes of attention shared memory (max %zu)",
+                    c->max_tokens, c->heads / c->kv_heads, att_smem, hc::ATT_MAX_SMEM);
   if (c->top_k < 1 || c->top_k > hc::TOPK_MAX) return hpc_fail(HPC_ERR_SHAPE, "top_k %d", c->top_k);
   return HPC_OK;
 }

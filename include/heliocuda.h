@@ -218,7 +218,9 @@ typedef struct {
   int kv_layers;     /* layers [0, kv_layers) own a KV cache; later layers reuse
                         layer kv_layers-1's (kvSourceLayers, engine/src/model.ts:382-388) */
   int context;       /* KV capacity (full attention) */
-  int max_tokens;    /* largest token_count per call, 1..8 */
+  int max_tokens;    /* largest token_count per call, 1..8; max_tokens *
+                        heads / kv_heads <= 72 (the query vectors one
+                        attention CTA stages), else HPC_ERR_SHAPE */
   int top_k;         /* largest top_k per call, 1..64 */
   double rms_eps;
   double rope_theta;

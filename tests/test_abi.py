@@ -114,3 +114,17 @@ def test_ctypes_signatures_match_header_prototypes():
             if _c_kind(decl) != _ctypes_kind(t):
                 bad.append(f"{name} arg {i} {decl!r}: {_c_kind(decl)} vs ctypes {t} {_ctypes_kind(t)}")
     assert not bad, "\n".join(bad)
+
+
+def test_model_create_rejects_attention_wider_than_shared_memory():
+    # An attention CTA stages the queries of every token of a step for its KV
+    # head (1,280 bytes each beside 130 KB of K/V rows), so 16 query heads per
+    # KV head at 8 tokens per step cannot fit the kernels' 220 KB: rejected at
+    # create time, before any device work, instead of failing in a forward.
+    cfg = _lib.ModelConfig(hidden=4096, heads=16, kv_heads=1, head_dim=256, ffn=2048, vocab=4096, layers=1,
+                           kv_layers=1, context=64, max_tokens=8, top_k=8, rms_eps=1e-6, rope_theta=1e4,
+                           final_logit_softcap=0.0)
+    out = C.c_void_p()
+    assert _lib.lib().hpc_model_create(C.byref(cfg), C.byref(out)) == kernels.ERR_SHAPE
+    assert "attention shared memory" in _lib.last_error()
+    assert not out.value
