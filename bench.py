@@ -60,6 +60,7 @@ class ClockSampler:
         self.index = index
         self.proc = None
         self.lines: list[str] = []
+        self.skip = 0
         self.t = None
 
     def __enter__(self):
@@ -69,6 +70,12 @@ class ClockSampler:
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
+            # nvidia-smi takes a moment to start: wait (up to 5 s) for its
+            # first sample so that the timed region is covered
+            t0 = time.perf_counter()
+            while not self.lines and time.perf_counter() - t0 < 5.0 and self.proc.poll() is None:
+                time.sleep(0.01)
+            self.skip = len(self.lines)
         except (OSError, FileNotFoundError):
             self.proc = None
         return self
@@ -90,7 +97,7 @@ class ClockSampler:
     def summary(self) -> dict:
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        for ln in self.lines[self.skip:] or self.lines[-1:]:
             f = [x.strip() for x in ln.split(",")]
             if len(f) < 9:
                 continue
@@ -180,7 +187,7 @@ class GemvConfig1:
         ms = graph_launch_times(launches * 2)
         achieved = self.algo_bytes / (ms / 1e3) / 1e9
         return {"bound": "hbm", "achieved": achieved, "peak": peak_gbs, "unit": "GB/s", "frac": achieved / peak_gbs,
-                "traffic": None, "kernel": "gemv_kernel<1> (Q4_K 2048 -> 16384, M=1)",
+                "traffic": None, "kernel": "hc_gemv_kernel<1> (Q4_K 2048 -> 16384, M=1)",
                 "algorithmic_bytes_per_launch": self.algo_bytes, "launch_ms": ms}
 
     unit = "GB/s"
@@ -328,7 +335,7 @@ class DecodeConfig3:
         algo = 2 * self.syn.row_bytes(self.syn.Q4_K, s.hidden) * s.ffn + 4 * s.hidden + 8 * s.ffn
         achieved = algo / (ms / 1e3) / 1e9
         return {"bound": "hbm", "achieved": achieved, "peak": peak_gbs, "unit": "GB/s", "frac": achieved / peak_gbs,
-                "traffic": None, "kernel": "gemv_kernel<1> (ffn gate+up, 2048 -> 2x16384 Q4_K, M=1)",
+                "traffic": None, "kernel": "hc_gemv_kernel<1> (ffn gate+up, 2048 -> 2x16384 Q4_K, M=1)",
                 "algorithmic_bytes_per_launch": algo, "launch_ms": ms}
 
     def config(self) -> dict:
@@ -492,7 +499,7 @@ class _Q8Launcher:
 class GemvConfig2:
     """the projections of one decoder layer, launched as the
     decode step launches them: [Q, K, V] (one launch on one Q8_K input),
-    [gate, up] (one launch), and the Q6_K down projection.  M = --m."""
+    [gate, up] (one launch), and the Q6_K down projection.  M = --cols."""
     name = "gemv-config2"
     unit = "GB/s"
     dtype = "u8"
@@ -554,7 +561,7 @@ class GemvConfig2:
         algo = 2 * self.syn.row_bytes(self.syn.Q4_K, self.K) * self.F + 4 * self.K * self.M + 8 * self.F * self.M
         achieved = algo / (ms / 1e3) / 1e9
         return {"bound": "hbm", "achieved": achieved, "peak": peak_gbs, "unit": "GB/s", "frac": achieved / peak_gbs,
-                "traffic": None, "kernel": f"gemv_kernel<{self.M}> (gate+up, 2048 -> 2x16384 Q4_K, M={self.M})",
+                "traffic": None, "kernel": f"hc_gemv_kernel<{self.M}> (gate+up, 2048 -> 2x16384 Q4_K, M={self.M})",
                 "algorithmic_bytes_per_launch": algo, "launch_ms": ms}
 
     def config(self) -> dict:
@@ -568,7 +575,7 @@ class GemvConfig2:
 
 
 class LmHeadConfig5:
-    """BASELINE config 5 (single GPU, M = --m): Q6_K LM head 2048 -> 262,144
+    """BASELINE config 5 (single GPU, M = --cols): Q6_K LM head 2048 -> 262,144
     fused with top-40 (q8 quantize, GEMV + candidate lists, merge)."""
     name = "lmhead-config5"
     unit = "GB/s"
@@ -650,7 +657,7 @@ class LmHeadConfig5:
         ms = graph_launch_times([self.head_launch] * 4)
         achieved = self.algo_bytes / (ms / 1e3) / 1e9
         return {"bound": "hbm", "achieved": achieved, "peak": peak_gbs, "unit": "GB/s", "frac": achieved / peak_gbs,
-                "traffic": None, "kernel": f"lmhead_topk_kernel<{self.M}> + topk_merge_kernel (Q6_K 2048 -> 262144, "
+                "traffic": None, "kernel": f"hc_lmhead_topk_kernel<{self.M}> + hc_topk_merge_kernel (Q6_K 2048 -> 262144, "
                                            f"top-{self.TOPK}, M={self.M})",
                 "algorithmic_bytes_per_launch": self.algo_bytes, "launch_ms": ms}
 
@@ -749,7 +756,7 @@ class PrefillConfig5:
         peaks = _peaks()
         peak = peaks.get("bf16_tflops") or 1590.0
         return {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
-                "traffic": None, "kernel": "gemm_tc_kernel<Q4_K> x2 (ffn gate+up, 2048 -> 2x16384, M=512)",
+                "traffic": None, "kernel": "hc_gemm_tc_kernel<Q4_K> x2 (ffn gate+up, 2048 -> 2x16384, M=512)",
                 "peak_note": "measured dense bf16 cuBLAS peak; the kernel computes s8 x s8 -> s32 on mma.sync",
                 "flops_per_launch": flops, "launch_ms": ms}
 
@@ -783,6 +790,76 @@ class PrefillConfig5:
         return {"value": 8.0 / (per_layer * s.layers), "unit": "tok/s", "cores": threads, "kind": "port",
                 "sample": f"{runs} x one config-3 layer over 8 prompt tokens ({per_layer:.2f} s each) on {threads} "
                           f"threads, scaled to {s.layers} layers"}
+
+
+def sharded_lm_head_run(world: int, rank: int, steps: int, warmup: int) -> dict:
+    """The row-sharded Q6_K LM head 2048 -> 262,144 + top-40 over every rank
+    (BASELINE config 5 / the multi-GPU row of the scope table): each rank holds
+    its contiguous vocabulary slice, runs the fused GEMV + top-k with its
+    first row as the id offset, the 64-bit keys are all-gathered over NCCL and
+    every rank merges them (heliopause_b200/sharded_head.py).  For M = 1, 5
+    and 64 columns: device time per call (CUDA events, max over ranks), the
+    time of the local slice alone, and hence the all-gather + merge share.
+    Rank 0 checks the merged ids and values against the unsharded
+    hpc_lm_head_topk on the whole head."""
+    import torch
+    import torch.distributed as dist
+
+    from heliopause_b200 import kernels as hk
+    from heliopause_b200 import sharded_head as sh
+    from heliopause_b200 import synthetic as syn
+    K, V, k = 2048, 262144, 40
+    full = syn.q6_k_weight(V, K, seed=3000)
+    first, n = sh.shard_rows(V, world)[rank]
+    rb = syn.row_bytes(syn.Q6_K, K)
+    backend = sh.CudaShardBackend("Q6_K", full[first * rb:(first + n) * rb], K, n, first, 64, k)
+    head = sh.ShardedLmHead(backend, k)
+    whole = hk.create_quantized_weight_handle("Q6_K", full, K, V) if rank == 0 else None
+    del full
+
+    def device_ms(fn, count):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        dist.barrier()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(count):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        dist.barrier()
+        t = torch.tensor([a.elapsed_time(b) / count], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t[0])
+
+    out = {"vocab": V, "hidden": K, "top_k": k, "ranks": world, "rows_per_rank": n, "scaling": "strong",
+           "collective": "all_gather_into_tensor of k*M int64 keys per rank (NCCL), then hpc_topk_merge_keys",
+           "per_m": []}
+    count = max(10, min(steps, 50))
+    for m in (1, 5, 64):
+        x = torch.from_numpy(syn.activations(m, K, seed=9 + m)).cuda()
+        total = device_ms(lambda: head.topk(x, m), count)
+        local = device_ms(lambda: backend.local_keys(x, m), count)
+        ids, vals = head.topk(x, m)
+        entry = {"m": m, "ms_per_call": total, "local_slice_ms": local,
+                 "gather_merge_ms": max(0.0, total - local), "gather_merge_share": max(0.0, total - local) / total,
+                 "columns_per_s": m / (total / 1e3),
+                 "weight_gbs_per_rank": syn.row_bytes(syn.Q6_K, K) * n / (local / 1e3) / 1e9}
+        if rank == 0:
+            rid, rval = hk.lm_head_topk(whole, x, m, k)
+            gi, gv = ids.reshape(m, k).cpu(), vals.reshape(m, k).cpu()
+            ri, rv = rid.reshape(m, k).cpu(), rval.reshape(m, k).cpu()
+            entry["ids_equal_unsharded"] = bool(torch.equal(gi, ri))
+            entry["values_equal_unsharded"] = bool(torch.equal(gv, rv))
+        out["per_m"].append(entry)
+    if whole is not None:
+        hk.release_quantized_weight_handle(whole)
+    backend.release()
+    torch.cuda.synchronize()
+    dist.barrier()
+    return out
 
 
 WORKLOADS = {"decode-config3": DecodeConfig3, "gemv-config1": GemvConfig1, "gemv-config2": GemvConfig2,
@@ -853,7 +930,8 @@ def main():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="decode-config3")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-mtp", action="store_true", help="skip the config-4 MTP generation field")
-    ap.add_argument("--m", type=int, default=1, help="columns (tokens) for the gemv-config2 / lmhead-config5 workloads")
+    ap.add_argument("--cols", type=int, default=1,
+                    help="columns (tokens) for the gemv-config2 / lmhead-config5 workloads")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -873,7 +951,7 @@ def main():
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
     hk.init_device(local)
-    wl = WORKLOADS[args.workload](args.m) if args.workload in ("gemv-config2", "lmhead-config5") \
+    wl = WORKLOADS[args.workload](args.cols) if args.workload in ("gemv-config2", "lmhead-config5") \
         else WORKLOADS[args.workload]()
 
     def barrier():
@@ -936,6 +1014,8 @@ def main():
     e2e_value = wl.units_per_step() * ranks_of_work / float(e2e_s[0])
 
     mtp = wl.mtp_run() if hasattr(wl, "mtp_run") and not args.no_mtp and world == 1 else None
+    sharded = sharded_lm_head_run(world, rank, args.steps, args.warmup) \
+        if world > 1 and args.workload == "decode-config3" else None
 
     peaks = _peaks()
     roofline = wl.roofline(peaks["hbm_gbs"])
@@ -950,6 +1030,14 @@ def main():
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         threads = len(os.sched_getaffinity(0))
         cpu = wl.cpu_baseline(10.0, threads)
+        # the reference's own default pool size: "auto" = min(8, max(1, floor(cores / 2)))
+        # (runner/wasm/acceleration.ts:277-283)
+        auto = min(8, max(1, threads // 2))
+        if cpu is not None and auto != threads:
+            d = wl.cpu_baseline(10.0, auto)
+            cpu["reference_default_threads"] = {"cores": auto, "value": d["value"], "unit": d["unit"],
+                                                "rule": "min(8, max(1, floor(cores/2))), acceleration.ts:277-283",
+                                                "sample": d["sample"]}
 
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": wl.unit, "n_gpus": world, "steps": args.steps,
@@ -966,6 +1054,8 @@ def main():
             line["verify"] = verify
         if mtp:
             line["mtp"] = mtp
+        if sharded:
+            line["sharded_lm_head"] = sharded
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()

@@ -33,6 +33,8 @@ SIGNATURES = {
     "hpc_matmul_quantized_prepared_multi_f32": (_i, [_sz, _vp, _sz, _sz, _sz, C.POINTER(_vp), C.POINTER(_vp),
                                                      C.POINTER(_sz), _vp]),
     "hpc_matmul_quantized_f32": (_i, [_i, _vp, _sz, _vp, _sz, _sz, _sz, _sz, _vp, _sz]),
+    "hpc_matmul_dequantized_f32": (_i, [_i, _vp, _sz, _vp, _sz, _sz, _sz, _sz, _vp, _sz]),
+    "hpc_matmul_dequantized_prepared_f32": (_i, [_vp, _vp, _sz, _sz, _sz, _sz, _vp, _sz, _vp]),
     "hpc_q8_workspace_bytes": (_i, [_sz, _sz, C.POINTER(_sz)]),
     "hpc_q8_quantize": (_i, [_vp, _sz, _sz, _sz, _vp, _sz, _vp]),
     "hpc_matmul_q8": (_i, [_sz, C.POINTER(_vp), _vp, _sz, _sz, _sz, C.POINTER(_vp), C.POINTER(_sz), _vp]),
@@ -43,8 +45,6 @@ SIGNATURES = {
     "hpc_topk_merge_keys": (_i, [_vp, _sz, _sz, _sz, C.c_float, _vp, _vp, _vp]),
     "hpc_model_create": (_i, [_vp, C.POINTER(_vp)]),
     "hpc_model_release": (_i, [_vp]),
-    "hpc_model_set_persistent": (_i, [_vp, _i]),
-    "hpc_model_step_kind": (_i, [_vp, _sz, C.POINTER(_i)]),
     "hpc_model_set_weight": (_i, [_vp, _i, _i, _vp]),
     "hpc_model_set_norm": (_i, [_vp, _i, _i, _vp, _sz]),
     "hpc_model_set_lm_head": (_i, [_vp, _vp]),

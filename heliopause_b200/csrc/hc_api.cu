@@ -369,6 +369,59 @@ int hpc_matmul_quantized_f32(int type_id, const uint8_t* host_weight, size_t wei
   return HPC_OK;
 }
 
+int hpc_matmul_dequantized_prepared_f32(hpc_weight h, const float* d_in, size_t in_len, size_t input_size,
+                                        size_t row_count, size_t column_count, float* d_out, size_t out_len,
+                                        void* stream) {
+  if (in_len != input_size * column_count || out_len != row_count * column_count)
+    return fail(HPC_ERR_SHAPE, "dequantized matmul shape mismatch: input %zu output %zu", in_len, out_len);
+  if (!valid(h)) return fail(HPC_ERR_ARG, "invalid weight handle");
+  size_t rb;
+  if (!row_bytes(h->type, input_size, &rb)) return fail(HPC_ERR_TYPE, "unsupported type %d for input size %zu", h->type, input_size);
+  if (h->input_size != input_size || h->row_count != row_count)
+    return fail(HPC_ERR_SHAPE, "handle shape mismatch: %zux%zu vs %zux%zu", h->input_size, h->row_count, input_size, row_count);
+  if (column_count == 0 || row_count == 0) return HPC_OK;
+  if (!d_in || !d_out) return fail(HPC_ERR_ARG, "null pointer");
+  if (column_count > size_t(65535) * 8) return fail(HPC_ERR_SHAPE, "too many columns");
+  int dev = 0;
+  HPC_CK(cudaGetDevice(&dev), "cudaGetDevice");
+  if (dev != h->device) return fail(HPC_ERR_ARG, "weight on device %d, current %d", h->device, dev);
+  HPC_CK(hc::launch_dequant_matmul(h->type, h->d_data, h->nb, int(row_count), int(h->rows_pad), d_in, int(input_size),
+                                   int(column_count), d_out, static_cast<cudaStream_t>(stream)),
+         "dequantized matmul launch");
+  return HPC_OK;
+}
+
+int hpc_matmul_dequantized_f32(int type_id, const uint8_t* host_weight, size_t weight_len, const float* host_in,
+                               size_t in_len, size_t input_size, size_t row_count, size_t column_count, float* host_out,
+                               size_t out_len) {
+  if (in_len != input_size * column_count || out_len != row_count * column_count)
+    return fail(HPC_ERR_SHAPE, "dequantized matmul shape mismatch");
+  size_t rb;
+  if (!row_bytes(type_id, input_size, &rb)) return fail(HPC_ERR_TYPE, "unsupported type %d", type_id);
+  if (weight_len != rb * row_count) return fail(HPC_ERR_SHAPE, "weight length %zu", weight_len);
+  if (column_count == 0 || row_count == 0) return HPC_OK;
+  if (!host_in || !host_out) return fail(HPC_ERR_ARG, "null pointer");
+  hpc_weight h = nullptr;
+  int rc = hpc_weight_upload(type_id, host_weight, weight_len, input_size, row_count, &h);
+  if (rc != HPC_OK) return rc;
+  float* d_in = nullptr;
+  float* d_out = nullptr;
+  cudaError_t e = cudaMalloc(&d_in, in_len * sizeof(float));
+  if (e == cudaSuccess) e = cudaMalloc(&d_out, out_len * sizeof(float));
+  if (e == cudaSuccess) e = cudaMemcpy(d_in, host_in, in_len * sizeof(float), cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) {
+    rc = hpc_matmul_dequantized_prepared_f32(h, d_in, in_len, input_size, row_count, column_count, d_out, out_len,
+                                             nullptr);
+    if (rc == HPC_OK) e = cudaMemcpy(host_out, d_out, out_len * sizeof(float), cudaMemcpyDeviceToHost);
+  }
+  cudaFree(d_in);
+  cudaFree(d_out);
+  hpc_weight_release(h);
+  if (rc != HPC_OK) return rc;
+  if (e != cudaSuccess) return cuda_fail(e, "one-shot dequantized matmul");
+  return HPC_OK;
+}
+
 int hpc_q8_workspace_bytes(size_t input_size, size_t column_count, size_t* out_bytes) {
   if (!out_bytes) return fail(HPC_ERR_ARG, "null out_bytes");
   if (input_size == 0 || input_size % 256 || column_count > (size_t(1) << 20))

@@ -40,7 +40,7 @@ namespace hc {
 // cos/sin of the NeoX RoPE angles for each token (layers.ts:1012-1030):
 // theta_0 = position, theta_{i+1} = fround(theta_i * base^(-2/ndims)); the
 // chain is serial (one thread), the cos/sin are parallel.  One CTA per token.
-__global__ void rope_table_kernel(const int32_t* __restrict__ pos, int half, double theta_scale,
+__global__ void hc_rope_table_kernel(const int32_t* __restrict__ pos, int half, double theta_scale,
                                   double* __restrict__ cos_t, double* __restrict__ sin_t) {
   __shared__ double theta[512];
   pdl_trigger();
@@ -93,7 +93,7 @@ __device__ __forceinline__ float tile_elem(const uint8_t* w, int type, int nb, i
 }
 
 // prepareInput (layers.ts:54-67): hidden = fround(embedding_row * sqrt(D)).
-__global__ void embed_kernel(const uint8_t* __restrict__ w, int type, int nb, int vocab, const int32_t* __restrict__ ids,
+__global__ void hc_embed_kernel(const uint8_t* __restrict__ w, int type, int nb, int vocab, const int32_t* __restrict__ ids,
                              float* __restrict__ hidden, int D, double scale, int* __restrict__ err) {
   pdl_trigger();
   pdl_wait();
@@ -115,7 +115,7 @@ __global__ void embed_kernel(const uint8_t* __restrict__ w, int type, int nb, in
 // n = rmsnorm(h, w_pre); otherwise n = rmsnorm(x, w_pre).  n is quantized to
 // Q8_K for the next matmul; if n_out != nullptr it is also stored as f32.
 template <bool RESID>
-__global__ void norm_quant_kernel(const float* x, float* x_out, const float* __restrict__ y,
+__global__ void hc_norm_quant_kernel(const float* x, float* x_out, const float* __restrict__ y,
                                   const float* __restrict__ w_post, const float* __restrict__ w_pre, double eps, int D,
                                   Q8Buf q, float* __restrict__ n_out) {
   __shared__ double scratch[32];
@@ -243,7 +243,7 @@ __device__ __forceinline__ void load_rope8(const double* cos_row, const double* 
 // loops cover any NQ; sized to NQ, a thread idles at most one score slot and
 // no output slot (a slot past NQ still issues its instructions).
 template <bool WIDE, int QS = ATT_QBS, int PB = ATT_QB>
-__global__ void __launch_bounds__(WIDE ? ATT_WIDE_THREADS : ATT_THREADS) attn_partial_kernel(
+__global__ void __launch_bounds__(WIDE ? ATT_WIDE_THREADS : ATT_THREADS) hc_attn_partial_kernel(
     const float* __restrict__ q, const float* __restrict__ kraw, const float* __restrict__ vraw,
     const float* __restrict__ qnw, const float* __restrict__ knw, const double* __restrict__ cos_t,
     const double* __restrict__ sin_t, double eps, int own_kv, float* __restrict__ kc, float* __restrict__ vc,
@@ -475,7 +475,7 @@ __global__ void __launch_bounds__(WIDE ? ATT_WIDE_THREADS : ATT_THREADS) attn_pa
 // sums, division, the TS f16 cast (castF16Rows), then the head's 256 values
 // -- exactly Q8_K block h of the token's attention vector -- are quantized
 // for the output projection.  Grid (M, H), thread d = head dimension.
-__global__ void __launch_bounds__(256) attn_combine_kernel(const float* __restrict__ part_m,
+__global__ void __launch_bounds__(256) hc_attn_combine_kernel(const float* __restrict__ part_m,
                                                            const float* __restrict__ part_l,
                                                            const float* __restrict__ part_o,
                                                            const int32_t* __restrict__ pos, int M, int H, int KVH,
@@ -551,7 +551,7 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(const float* __restri
 // per 256-block of one column, thread t = element t: the f64 tanh of the
 // GELU (~1k cycles) runs once per thread, all blocks in parallel; warp 0 then
 // quantizes the block.  Grid (F/256, M).
-__global__ void __launch_bounds__(256) geglu_quant_kernel(const float* __restrict__ gate, const float* __restrict__ up,
+__global__ void __launch_bounds__(256) hc_geglu_quant_kernel(const float* __restrict__ gate, const float* __restrict__ up,
                                                           int F, Q8Buf q, float* __restrict__ act_out) {
   __shared__ float vals[256];
   __shared__ __align__(16) uint8_t stage[256];
@@ -573,8 +573,8 @@ __global__ void __launch_bounds__(256) geglu_quant_kernel(const float* __restric
 
 // The wide (prefill) form: a warp per 256-block (lane: elements 8L..8L+7),
 // eight blocks per CTA and no CTA barrier; same arithmetic, same records as
-// geglu_quant_kernel.  Grid (ceil(F / 2048), M).
-__global__ void __launch_bounds__(256) geglu_quant_wide_kernel(const float* __restrict__ gate,
+// hc_geglu_quant_kernel.  Grid (ceil(F / 2048), M).
+__global__ void __launch_bounds__(256) hc_geglu_quant_wide_kernel(const float* __restrict__ gate,
                                                                const float* __restrict__ up, int F, Q8Buf q,
                                                                float* __restrict__ act_out) {
   pdl_trigger();
@@ -600,7 +600,7 @@ __global__ void __launch_bounds__(256) geglu_quant_wide_kernel(const float* __re
 // lib.rs:590-597) into qh[m][h][256], and, in an own-KV layer, the tokens'
 // K (norm + RoPE) and V (unweighted norm) rows into the cache (layers.ts:
 // 201-268, 887-911).  One CTA per token, one warp per head vector.
-__global__ void prefill_qkv_post_kernel(const float* __restrict__ q, const float* __restrict__ kraw,
+__global__ void hc_prefill_qkv_post_kernel(const float* __restrict__ q, const float* __restrict__ kraw,
                                         const float* __restrict__ vraw, const float* __restrict__ qnw,
                                         const float* __restrict__ knw, const double* __restrict__ cos_t,
                                         const double* __restrict__ sin_t, double eps, int own_kv, float* __restrict__ kc,
@@ -640,7 +640,7 @@ __global__ void prefill_qkv_post_kernel(const float* __restrict__ q, const float
 // head) quantized to Q8_K for the output projection.  Grid
 // (ceil(M / PF_QT), KVH); tokens are consecutive positions pos[0] + m.
 constexpr int PF_QT = 8, PF_CK = 32;
-__global__ void __launch_bounds__(256) prefill_attn_kernel(const float* __restrict__ qh, const float* __restrict__ kc,
+__global__ void __launch_bounds__(256) hc_prefill_attn_kernel(const float* __restrict__ qh, const float* __restrict__ kc,
                                                           const float* __restrict__ vc, const int32_t* __restrict__ pos,
                                                           int M, int H, int KVH, int cap, Q8Buf qo,
                                                           float* __restrict__ attn_out) {
@@ -757,7 +757,7 @@ __global__ void __launch_bounds__(256) prefill_attn_kernel(const float* __restri
 
 // Split form of the prefill attention: the keys of a query tile are cut into
 // PF_SK-key splits, one CTA per (tile, split, KV head), so the causal work of
-// the long tiles spreads over many CTAs; prefill_attn_merge_kernel merges
+// the long tiles spreads over many CTAs; hc_prefill_attn_merge_kernel merges
 // the splits.  Per CTA: the PF_QT tokens x G heads of the tile (qs, rows
 // padded for conflict-free reads), keys in PF_CK chunks (online softmax:
 // running max, f64 exp of the differences, f32 sums), scores as 2 x 2
@@ -767,7 +767,7 @@ __global__ void __launch_bounds__(256) prefill_attn_kernel(const float* __restri
 // ((token * H + head) * nsplit + split).
 constexpr int PF_SK = 128;       // keys per split
 constexpr int PF_QSTRIDE = 260;  // floats per staged query row
-__global__ void __launch_bounds__(256) prefill_attn_split_kernel(const float* __restrict__ qh,
+__global__ void __launch_bounds__(256) hc_prefill_attn_split_kernel(const float* __restrict__ qh,
                                                                 const float* __restrict__ kc,
                                                                 const float* __restrict__ vc,
                                                                 const int32_t* __restrict__ pos, int M, int H, int KVH,
@@ -904,7 +904,7 @@ __global__ void __launch_bounds__(256) prefill_attn_split_kernel(const float* __
 // that reach the token (global max, f64-exp weights, f64 sum, weighted
 // outputs), the TS f16 cast (castF16Rows) and the head's Q8_K block for the
 // output projection.  Grid (M, H), thread d = dimension.
-__global__ void __launch_bounds__(256) prefill_attn_merge_kernel(const float* __restrict__ part_m,
+__global__ void __launch_bounds__(256) hc_prefill_attn_merge_kernel(const float* __restrict__ part_m,
                                                                 const float* __restrict__ part_l,
                                                                 const float* __restrict__ part_o,
                                                                 const int32_t* __restrict__ pos, int M, int H, int cap,
@@ -966,12 +966,12 @@ static cudaError_t pdl_launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
 
 cudaError_t launch_rope_table(const int32_t* pos, int M, int half, double theta_scale, double* cos_t, double* sin_t,
                               cudaStream_t st) {
-  return pdl_launch(rope_table_kernel, dim3(M), dim3(128), 0, st, pos, half, theta_scale, cos_t, sin_t);
+  return pdl_launch(hc_rope_table_kernel, dim3(M), dim3(128), 0, st, pos, half, theta_scale, cos_t, sin_t);
 }
 
 cudaError_t launch_embed(const uint8_t* w, int type, int nb, int vocab, const int32_t* ids, float* hidden, int M, int D,
                          double scale, int* err, cudaStream_t st) {
-  return pdl_launch(embed_kernel, dim3(M), dim3(256), 0, st, w, type, nb, vocab, ids, hidden, D, scale, err);
+  return pdl_launch(hc_embed_kernel, dim3(M), dim3(256), 0, st, w, type, nb, vocab, ids, hidden, D, scale, err);
 }
 
 cudaError_t launch_norm_quant(bool resid, const float* x, float* x_out, const float* y, const float* w_post,
@@ -979,8 +979,8 @@ cudaError_t launch_norm_quant(bool resid, const float* x, float* x_out, const fl
                               cudaStream_t st) {
   const dim3 grid(M), block(D / 8);
   if (resid)
-    return pdl_launch(norm_quant_kernel<true>, grid, block, 0, st, x, x_out, y, w_post, w_pre, eps, D, q, n_out);
-  return pdl_launch(norm_quant_kernel<false>, grid, block, 0, st, x, x_out, y, w_post, w_pre, eps, D, q, n_out);
+    return pdl_launch(hc_norm_quant_kernel<true>, grid, block, 0, st, x, x_out, y, w_post, w_pre, eps, D, q, n_out);
+  return pdl_launch(hc_norm_quant_kernel<false>, grid, block, 0, st, x, x_out, y, w_post, w_pre, eps, D, q, n_out);
 }
 
 size_t attn_smem_bytes(int M, int H, int KVH) {
@@ -989,7 +989,7 @@ size_t attn_smem_bytes(int M, int H, int KVH) {
 }
 
 namespace {
-using AttnKernel = decltype(&attn_partial_kernel<false>);
+using AttnKernel = decltype(&hc_attn_partial_kernel<false>);
 // Wide forms sized to NQ = 8, 12, ..., 32 query vectors per KV head (four
 // heads per KV head at 2..8 tokens): ceil(NQ / 8) score slots and
 // ceil(NQ / 2) output slots per half: every output slot holds a query, the
@@ -997,13 +997,13 @@ using AttnKernel = decltype(&attn_partial_kernel<false>);
 // slot (at NQ = 20, lanes 4..7 have two queries for three slots).  Index
 // (NQ - 8) / 4.
 constexpr AttnKernel kAttnSized[] = {
-    attn_partial_kernel<true, 1, 4>,  attn_partial_kernel<true, 2, 6>,  attn_partial_kernel<true, 2, 8>,
-    attn_partial_kernel<true, 3, 10>, attn_partial_kernel<true, 3, 12>, attn_partial_kernel<true, 4, 14>,
-    attn_partial_kernel<true, 4, 16>};
+    hc_attn_partial_kernel<true, 1, 4>,  hc_attn_partial_kernel<true, 2, 6>,  hc_attn_partial_kernel<true, 2, 8>,
+    hc_attn_partial_kernel<true, 3, 10>, hc_attn_partial_kernel<true, 3, 12>, hc_attn_partial_kernel<true, 4, 14>,
+    hc_attn_partial_kernel<true, 4, 16>};
 
 AttnKernel attn_wide_kernel(int nq) {
   if (nq >= 8 && nq <= 32 && nq % 4 == 0) return kAttnSized[(nq - 8) / 4];
-  return attn_partial_kernel<true>;
+  return hc_attn_partial_kernel<true>;
 }
 }  // namespace
 
@@ -1016,7 +1016,7 @@ cudaError_t launch_attention(const float* q, const float* kraw, const float* vra
   if (smem > ATT_MAX_SMEM) return cudaErrorInvalidValue;
   static std::atomic<uint64_t> attr{0};
   const cudaError_t ea = once_per_current_device(attr, [] {
-    const AttnKernel all[] = {attn_partial_kernel<false>, attn_partial_kernel<true>, kAttnSized[0], kAttnSized[1],
+    const AttnKernel all[] = {hc_attn_partial_kernel<false>, hc_attn_partial_kernel<true>, kAttnSized[0], kAttnSized[1],
                               kAttnSized[2],              kAttnSized[3],             kAttnSized[4], kAttnSized[5],
                               kAttnSized[6]};
     for (AttnKernel k : all) {
@@ -1037,23 +1037,23 @@ cudaError_t launch_attention(const float* q, const float* kraw, const float* vra
     return pdl_launch(attn_wide_kernel(M * (H / KVH)), dim3(chunks, KVH), dim3(ATT_WIDE_THREADS), smem, st, q, kraw, vraw, qnw,
                       knw, cos_t, sin_t, eps, int(own_kv), kc, vc, pos, M, H, KVH, cap, scale, part_m, part_l, part_o,
                       err);
-  return pdl_launch(attn_partial_kernel<false>, dim3(chunks, KVH), dim3(ATT_THREADS), smem, st, q, kraw, vraw, qnw,
+  return pdl_launch(hc_attn_partial_kernel<false>, dim3(chunks, KVH), dim3(ATT_THREADS), smem, st, q, kraw, vraw, qnw,
                     knw, cos_t, sin_t, eps, int(own_kv), kc, vc, pos, M, H, KVH, cap, scale, part_m, part_l, part_o,
                     err);
 }
 
 cudaError_t launch_attn_combine(const float* part_m, const float* part_l, const float* part_o, const int32_t* pos,
                                 int M, int H, int KVH, int cap, const Q8Buf& q, float* attn_out, cudaStream_t st) {
-  return pdl_launch(attn_combine_kernel, dim3(M, H), dim3(256), 0, st, part_m, part_l, part_o, pos, M, H, KVH, cap, q,
+  return pdl_launch(hc_attn_combine_kernel, dim3(M, H), dim3(256), 0, st, part_m, part_l, part_o, pos, M, H, KVH, cap, q,
                     attn_out);
 }
 
 cudaError_t launch_geglu_quant(const float* gate, const float* up, int M, int F, const Q8Buf& q, float* act_out,
                                cudaStream_t st) {
   if (M >= GEGLU_WIDE_MIN_COLS)
-    return pdl_launch(geglu_quant_wide_kernel, dim3((F / 256 + 7) / 8, M), dim3(256), 0, st, gate, up, F, q,
+    return pdl_launch(hc_geglu_quant_wide_kernel, dim3((F / 256 + 7) / 8, M), dim3(256), 0, st, gate, up, F, q,
                       act_out);
-  return pdl_launch(geglu_quant_kernel, dim3(F / 256, M), dim3(256), 0, st, gate, up, F, q, act_out);
+  return pdl_launch(hc_geglu_quant_kernel, dim3(F / 256, M), dim3(256), 0, st, gate, up, F, q, act_out);
 }
 
 cudaError_t launch_prefill_qkv_post(const float* q, const float* kraw, const float* vraw, const float* qnw,
@@ -1062,7 +1062,7 @@ cudaError_t launch_prefill_qkv_post(const float* q, const float* kraw, const flo
                                    cudaStream_t st) {
   const int jobs = own_kv ? H + 2 * KVH : H;
   if (jobs > 32) return cudaErrorInvalidValue;
-  prefill_qkv_post_kernel<<<M, 32 * jobs, 0, st>>>(q, kraw, vraw, qnw, knw, cos_t, sin_t, eps, int(own_kv), kc, vc, pos,
+  hc_prefill_qkv_post_kernel<<<M, 32 * jobs, 0, st>>>(q, kraw, vraw, qnw, knw, cos_t, sin_t, eps, int(own_kv), kc, vc, pos,
                                                    H, KVH, cap, qh);
   return cudaGetLastError();
 }
@@ -1090,15 +1090,15 @@ cudaError_t launch_prefill_attention_split(const float* qh, const float* kc, con
   const size_t smem = prefill_split_smem_bytes(H, KVH);
   static std::atomic<uint64_t> attr{0};
   const cudaError_t ea = once_per_current_device(attr, [] {
-    return cudaFuncSetAttribute(prefill_attn_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    return cudaFuncSetAttribute(hc_prefill_attn_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
   });
   if (ea != cudaSuccess) return ea;
   const int tiles = (M + PF_QT - 1) / PF_QT;
-  prefill_attn_split_kernel<<<dim3(unsigned(tiles * nsplit), unsigned(KVH)), 256, smem, st>>>(
+  hc_prefill_attn_split_kernel<<<dim3(unsigned(tiles * nsplit), unsigned(KVH)), 256, smem, st>>>(
       qh, kc, vc, pos, M, H, KVH, cap, nsplit, part_m, part_l, part_o);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  prefill_attn_merge_kernel<<<dim3(unsigned(M), unsigned(H)), 256, 0, st>>>(part_m, part_l, part_o, pos, M, H, cap,
+  hc_prefill_attn_merge_kernel<<<dim3(unsigned(M), unsigned(H)), 256, 0, st>>>(part_m, part_l, part_o, pos, M, H, cap,
                                                                            nsplit, qo, attn_out);
   return cudaGetLastError();
 }
@@ -1107,12 +1107,15 @@ cudaError_t launch_prefill_attention(const float* qh, const float* kc, const flo
                                      int H, int KVH, int cap, const Q8Buf& qo, float* attn_out, cudaStream_t st) {
   if (H / KVH > 8) return cudaErrorInvalidValue;
   const size_t smem = prefill_attn_smem_bytes(H, KVH);
+  // the limit is set once per device, so it is the bound of the widest group
+  // this kernel accepts (8 query heads per KV head), not this call's need
   static std::atomic<uint64_t> attr{0};
-  const cudaError_t ea = once_per_current_device(attr, [smem] {
-    return cudaFuncSetAttribute(prefill_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  const cudaError_t ea = once_per_current_device(attr, [] {
+    return cudaFuncSetAttribute(hc_prefill_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                int(prefill_attn_smem_bytes(8, 1)));
   });
   if (ea != cudaSuccess) return ea;
-  prefill_attn_kernel<<<dim3(unsigned((M + PF_QT - 1) / PF_QT), unsigned(KVH)), 256, smem, st>>>(
+  hc_prefill_attn_kernel<<<dim3(unsigned((M + PF_QT - 1) / PF_QT), unsigned(KVH)), 256, smem, st>>>(
       qh, kc, vc, pos, M, H, KVH, cap, qo, attn_out);
   return cudaGetLastError();
 }

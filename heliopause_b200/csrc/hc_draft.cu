@@ -43,7 +43,7 @@ constexpr int DT_THREADS = 1024; // top-k selection: one CTA
 constexpr int DT_MAXN = 4096;    // keys one selection sorts
 
 // y[row] = sum_k W[row][k] * x[k] over f32 rows, x = [x0[0..k0) ; x1[..]].
-__global__ void __launch_bounds__(32 * DG_ROWS) dgemv_kernel(const float* __restrict__ W, int N, int K,
+__global__ void __launch_bounds__(32 * DG_ROWS) hc_dgemv_kernel(const float* __restrict__ W, int N, int K,
                                                              const float* __restrict__ x0, int k0,
                                                              const float* __restrict__ x1, float* __restrict__ y) {
   extern __shared__ __align__(16) float xs[];
@@ -93,7 +93,7 @@ __device__ __forceinline__ float norm_elem(float x, double scale, float w) {
 // mode 0: out1 = rmsNorm(x, w1)
 // mode 1: out1 = r = x + rmsNorm(y, w1); out2 = rmsNorm(r, w2)
 // mode 2: out1 = fround((x + rmsNorm(y, w1)) * scale)
-__global__ void __launch_bounds__(DN_THREADS) dnorm_kernel(int mode, int n, const float* __restrict__ x,
+__global__ void __launch_bounds__(DN_THREADS) hc_dnorm_kernel(int mode, int n, const float* __restrict__ x,
                                                            const float* __restrict__ y, const float* __restrict__ w1,
                                                            const float* __restrict__ w2, double eps, float scale,
                                                            float* __restrict__ out1, float* __restrict__ out2) {
@@ -125,7 +125,7 @@ __global__ void __launch_bounds__(DN_THREADS) dnorm_kernel(int mode, int n, cons
 // rotate; theta starts at the position and advances as
 // fround(theta * base^(-2/hd)); cos/sin in f64.  One CTA per head, thread =
 // dimension.
-__global__ void __launch_bounds__(256) dqrope_kernel(float* __restrict__ q, const float* __restrict__ qnw, int hd,
+__global__ void __launch_bounds__(256) hc_dqrope_kernel(float* __restrict__ q, const float* __restrict__ qnw, int hd,
                                                      const int* __restrict__ pos, int pairs, double theta_scale,
                                                      double eps) {
   __shared__ float red[32];
@@ -151,9 +151,9 @@ __global__ void __launch_bounds__(256) dqrope_kernel(float* __restrict__ q, cons
 // GQA attention of one token's query heads over the target KV (K and V both
 // [cap][kvh][hd], causal to *pos, scale 1, f32 query; lib.rs:539-654 as the
 // draft head calls it): split over DA_CHUNK-token slices, local max / sum of
-// f64 exp / sum of p * v per slice, merged by dattn_combine_kernel.
+// f64 exp / sum of p * v per slice, merged by hc_dattn_combine_kernel.
 // Grid (cap / DA_CHUNK, kvh); thread d = dimension.
-__global__ void __launch_bounds__(256) dattn_partial_kernel(const float* __restrict__ q, const float* __restrict__ kc,
+__global__ void __launch_bounds__(256) hc_dattn_partial_kernel(const float* __restrict__ q, const float* __restrict__ kc,
                                                             const float* __restrict__ vc, const int* __restrict__ pos,
                                                             int H, int KVH, float* __restrict__ part_m,
                                                             float* __restrict__ part_l, float* __restrict__ part_o) {
@@ -218,7 +218,7 @@ __global__ void __launch_bounds__(256) dattn_partial_kernel(const float* __restr
 
 // Merges the slices of one head: global max, f64-exp slice weights, f64 sum,
 // weighted outputs, division.  Grid H; thread d = dimension.
-__global__ void __launch_bounds__(256) dattn_combine_kernel(const float* __restrict__ part_m,
+__global__ void __launch_bounds__(256) hc_dattn_combine_kernel(const float* __restrict__ part_m,
                                                             const float* __restrict__ part_l,
                                                             const float* __restrict__ part_o,
                                                             const int* __restrict__ pos, int H, int KVH,
@@ -262,7 +262,7 @@ __device__ __forceinline__ double gelu_f32points(float v) {
   return double(float(double(hx) * double(t)));
 }
 
-__global__ void dgeglu_kernel(const float* __restrict__ g, const float* __restrict__ u, int n, float* __restrict__ o) {
+__global__ void hc_dgeglu_kernel(const float* __restrict__ g, const float* __restrict__ u, int n, float* __restrict__ o) {
   const int i = int(blockIdx.x * blockDim.x + threadIdx.x);
   if (i < n) o[i] = float(gelu_f32points(g[i]) * double(u[i]));
 }
@@ -278,7 +278,7 @@ __device__ __forceinline__ uint64_t dkey(float v, uint32_t id) {
 
 // Top-k of n <= DT_MAXN entries (values with id = index, or ready keys):
 // bitonic sort of the keys, descending, in one CTA.  *d_k (device) or k.
-__global__ void __launch_bounds__(DT_THREADS) dtopk_kernel(const float* __restrict__ vals,
+__global__ void __launch_bounds__(DT_THREADS) hc_dtopk_kernel(const float* __restrict__ vals,
                                                            const uint64_t* __restrict__ keys, int n, int k,
                                                            const int* __restrict__ d_k, int32_t* __restrict__ out_ids,
                                                            float* __restrict__ out_vals) {
@@ -318,7 +318,7 @@ __global__ void __launch_bounds__(DT_THREADS) dtopk_kernel(const float* __restri
 // top centroids' token lists (token_ordering[c * per + j]) scored by its
 // embedding row . h; ids outside the vocabulary get the empty key.  A warp
 // per slot.
-__global__ void __launch_bounds__(256) dscores_kernel(const float* __restrict__ E, int hid, int vocab,
+__global__ void __launch_bounds__(256) hc_dscores_kernel(const float* __restrict__ E, int hid, int vocab,
                                                       const int32_t* __restrict__ ordering, int per,
                                                       const int32_t* __restrict__ c_ids, int slots,
                                                       const float* __restrict__ h, uint64_t* __restrict__ keys) {
@@ -348,7 +348,7 @@ __global__ void __launch_bounds__(256) dscores_kernel(const float* __restrict__ 
 }
 
 // The step's inputs: [embedding ; hidden] into xin, the position and top-k.
-__global__ void dinputs_kernel(const float* __restrict__ emb, const float* __restrict__ hid, int n, float* xin,
+__global__ void hc_dinputs_kernel(const float* __restrict__ emb, const float* __restrict__ hid, int n, float* xin,
                                int* d_pos, int position, int* d_k, int k) {
   const int i = int(blockIdx.x * blockDim.x + threadIdx.x);
   if (i < n) {
@@ -590,13 +590,13 @@ static int draft_enqueue(hpc_draft d, cudaStream_t st) {
   const hpc_draft_config& c = d->cfg;
   const int E = c.hidden, D = c.backbone, Hq = c.heads * c.head_dim, F = c.ffn;
   auto gemv = [&](const float* W, int N, int K, const float* x0, int k0, const float* x1, float* y) -> int {
-    dgemv_kernel<<<(N + DG_ROWS - 1) / DG_ROWS, 32 * DG_ROWS, size_t(K) * 4, st>>>(W, N, K, x0, k0, x1, y);
+    hc_dgemv_kernel<<<(N + DG_ROWS - 1) / DG_ROWS, 32 * DG_ROWS, size_t(K) * 4, st>>>(W, N, K, x0, k0, x1, y);
     HPC_CK(cudaGetLastError(), "draft gemv");
     return HPC_OK;
   };
   auto norm = [&](int mode, int n, const float* x, const float* y, const float* w1, const float* w2, float scale,
                   float* o1, float* o2) -> int {
-    dnorm_kernel<<<1, DN_THREADS, size_t(n) * 4, st>>>(mode, n, x, y, w1, w2, c.rms_eps, scale, o1, o2);
+    hc_dnorm_kernel<<<1, DN_THREADS, size_t(n) * 4, st>>>(mode, n, x, y, w1, w2, c.rms_eps, scale, o1, o2);
     HPC_CK(cudaGetLastError(), "draft norm");
     return HPC_OK;
   };
@@ -609,18 +609,18 @@ static int draft_enqueue(hpc_draft d, cudaStream_t st) {
     DraftLayer& L = d->layers[size_t(l)];
     if ((rc = norm(0, E, d->x, nullptr, L.n[HPC_DN_ATTN], nullptr, 1.0f, d->a, nullptr)) != HPC_OK) return rc;
     if ((rc = gemv(L.w[HPC_DW_Q], Hq, E, d->a, E, d->a, d->q)) != HPC_OK) return rc;
-    dqrope_kernel<<<c.heads, 256, 0, st>>>(d->q, L.n[HPC_DN_Q], c.head_dim, d->d_pos, pairs, theta_scale, c.rms_eps);
+    hc_dqrope_kernel<<<c.heads, 256, 0, st>>>(d->q, L.n[HPC_DN_Q], c.head_dim, d->d_pos, pairs, theta_scale, c.rms_eps);
     HPC_CK(cudaGetLastError(), "draft q norm / rope");
-    dattn_partial_kernel<<<dim3(chunks, c.kv_heads), 256, size_t(G) * (256 + DA_CHUNK) * 4, st>>>(
+    hc_dattn_partial_kernel<<<dim3(chunks, c.kv_heads), 256, size_t(G) * (256 + DA_CHUNK) * 4, st>>>(
         d->q, L.kc, L.vc, d->d_pos, c.heads, c.kv_heads, d->pm, d->pl, d->po);
     HPC_CK(cudaGetLastError(), "draft attention");
-    dattn_combine_kernel<<<c.heads, 256, 0, st>>>(d->pm, d->pl, d->po, d->d_pos, c.heads, c.kv_heads, d->att);
+    hc_dattn_combine_kernel<<<c.heads, 256, 0, st>>>(d->pm, d->pl, d->po, d->d_pos, c.heads, c.kv_heads, d->att);
     HPC_CK(cudaGetLastError(), "draft attention combine");
     if ((rc = gemv(L.w[HPC_DW_O], E, Hq, d->att, Hq, d->att, d->o)) != HPC_OK) return rc;
     if ((rc = norm(1, E, d->x, d->o, L.n[HPC_DN_POST_ATTN], L.n[HPC_DN_FFN], 1.0f, d->r, d->nn)) != HPC_OK) return rc;
     if ((rc = gemv(L.w[HPC_DW_GATE], F, E, d->nn, E, d->nn, d->g)) != HPC_OK) return rc;
     if ((rc = gemv(L.w[HPC_DW_UP], F, E, d->nn, E, d->nn, d->u)) != HPC_OK) return rc;
-    dgeglu_kernel<<<(F + 255) / 256, 256, 0, st>>>(d->g, d->u, F, d->act);
+    hc_dgeglu_kernel<<<(F + 255) / 256, 256, 0, st>>>(d->g, d->u, F, d->act);
     HPC_CK(cudaGetLastError(), "draft geglu");
     if ((rc = gemv(L.w[HPC_DW_DOWN], E, F, d->act, F, d->act, d->dn)) != HPC_OK) return rc;
     if ((rc = norm(2, E, d->r, d->dn, L.n[HPC_DN_POST_FFW], nullptr, L.scale, d->x, nullptr)) != HPC_OK) return rc;
@@ -628,14 +628,14 @@ static int draft_enqueue(hpc_draft d, cudaStream_t st) {
   if ((rc = norm(0, E, d->x, nullptr, d->out_norm, nullptr, 1.0f, d->h, nullptr)) != HPC_OK) return rc;
   if ((rc = gemv(d->post, D, E, d->h, E, d->h, d->post_out)) != HPC_OK) return rc;
   if ((rc = gemv(d->cent, c.n_centroids, E, d->h, E, d->h, d->cent_out)) != HPC_OK) return rc;
-  dtopk_kernel<<<1, DT_THREADS, 0, st>>>(d->cent_out, nullptr, c.n_centroids, c.centroid_top_k, nullptr, d->c_ids,
+  hc_dtopk_kernel<<<1, DT_THREADS, 0, st>>>(d->cent_out, nullptr, c.n_centroids, c.centroid_top_k, nullptr, d->c_ids,
                                          d->c_vals);
   HPC_CK(cudaGetLastError(), "draft centroid top-k");
   const int slots = c.centroid_top_k * d->per;
-  dscores_kernel<<<(slots + 7) / 8, 256, 0, st>>>(d->embd, E, c.vocab, d->ordering, d->per, d->c_ids, slots, d->h,
+  hc_dscores_kernel<<<(slots + 7) / 8, 256, 0, st>>>(d->embd, E, c.vocab, d->ordering, d->per, d->c_ids, slots, d->h,
                                                   d->keys);
   HPC_CK(cudaGetLastError(), "draft token scores");
-  dtopk_kernel<<<1, DT_THREADS, 0, st>>>(nullptr, d->keys, slots, 0, d->d_k, d->out_ids, d->out_vals);
+  hc_dtopk_kernel<<<1, DT_THREADS, 0, st>>>(nullptr, d->keys, slots, 0, d->d_k, d->out_ids, d->out_vals);
   HPC_CK(cudaGetLastError(), "draft token top-k");
   return HPC_OK;
 }
@@ -662,7 +662,7 @@ int hpc_draft_step(hpc_draft d, const float* d_embedding, const float* d_hidden,
                     c.centroid_top_k * d->per);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int D = c.backbone;
-  hc::dinputs_kernel<<<(D + 255) / 256, 256, 0, st>>>(d_embedding, d_hidden, D, d->xin, d->d_pos, position, d->d_k,
+  hc::hc_dinputs_kernel<<<(D + 255) / 256, 256, 0, st>>>(d_embedding, d_hidden, D, d->xin, d->d_pos, position, d->d_k,
                                                       int(top_k));
   HPC_CK(cudaGetLastError(), "draft inputs");
   if (!d->graph || d->graph_kv != kv) {

@@ -61,7 +61,7 @@ struct TcType {
 };
 
 template <int TYPE>
-__global__ void __launch_bounds__(TC_THREADS, 2) gemm_tc_kernel(const __grid_constant__ TcParams p) {
+__global__ void __launch_bounds__(TC_THREADS, 2) hc_gemm_tc_kernel(const __grid_constant__ TcParams p) {
   using T = TcType<TYPE>;
   extern __shared__ __align__(16) uint8_t smem[];
   const int tile0 = int(blockIdx.x) * TC_TILES, col0 = p.col0 + int(blockIdx.y) * TC_COLS;
@@ -128,7 +128,7 @@ static cudaError_t launch_tc(const TcParams& p, cudaStream_t st) {
   const size_t smem = 2 * size_t(TcType<TYPE>::STAGE);
   static std::atomic<uint64_t> attr{0};
   const cudaError_t ea = once_per_current_device(attr, [smem] {
-    return cudaFuncSetAttribute(gemm_tc_kernel<TYPE>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    return cudaFuncSetAttribute(hc_gemm_tc_kernel<TYPE>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   });
   if (ea != cudaSuccess) return ea;
   const dim3 grid(unsigned((p.tiles + TC_TILES - 1) / TC_TILES), unsigned((p.ncols + TC_COLS - 1) / TC_COLS),
@@ -137,7 +137,7 @@ static cudaError_t launch_tc(const TcParams& p, cudaStream_t st) {
     cudaError_t e = cudaMemsetAsync(p.out + size_t(p.col0) * p.rows, 0, sizeof(float) * size_t(p.ncols) * p.rows, st);
     if (e != cudaSuccess) return e;
   }
-  gemm_tc_kernel<TYPE><<<grid, TC_THREADS, smem, st>>>(p);
+  hc_gemm_tc_kernel<TYPE><<<grid, TC_THREADS, smem, st>>>(p);
   return cudaGetLastError();
 }
 

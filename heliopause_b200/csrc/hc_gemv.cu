@@ -75,7 +75,7 @@ __device__ __forceinline__ void store_tile(const GemvParams& p, int tile, const 
 
 // The fused prologue (after the wait): for every column, h = x [+
 // rmsnorm(y) * w_post] (f64 sums and products rounded to f32 as
-// norm_quant_kernel / layers.ts:824-885), n = rmsnorm(h) * w_pre, and the
+// hc_norm_quant_kernel / layers.ts:824-885), n = rmsnorm(h) * w_pre, and the
 // blocks of the CTA's slice [kb0, kb0 + nblk) -- each held whole by one warp
 // -- quantized to Q8_K into the shared-memory records.  CTA 0 stores h.
 __device__ __forceinline__ void gemv_prologue(const GemvParams& p, uint8_t* act_a, uint8_t* act_b, int kb0, int nblk,
@@ -156,7 +156,7 @@ __device__ __forceinline__ void gemv_inputs(const GemvParams& p, uint8_t* act_a,
 // launches, which then fit GEMV_CTAS_PER_SM_Q4 CTAs per SM).
 template <int NC, int UC>
 __global__ void __launch_bounds__(GEMV_THREADS, UC == Q4K_CHUNKS ? GEMV_CTAS_PER_SM_Q4 : GEMV_CTAS_PER_SM)
-    gemv_kernel(const __grid_constant__ GemvParams p) {
+    hc_gemv_kernel(const __grid_constant__ GemvParams p) {
   extern __shared__ __align__(16) uint8_t smem[];
   __shared__ float red[GEMV_WARPS_PER_CTA][NC][32];
   __shared__ __align__(8) uint64_t act_bar;
@@ -410,7 +410,7 @@ static cudaError_t launch_nc(const GemvParams& p, cudaStream_t stream) {
   if (smem > size_t(GEMV_MAX_SMEM)) return cudaErrorInvalidValue;
   static std::atomic<uint64_t> attr_set{0};
   const cudaError_t ea = once_per_current_device(attr_set, [] {
-    return cudaFuncSetAttribute(gemv_kernel<NC, UC>, cudaFuncAttributeMaxDynamicSharedMemorySize, GEMV_MAX_SMEM);
+    return cudaFuncSetAttribute(hc_gemv_kernel<NC, UC>, cudaFuncAttributeMaxDynamicSharedMemorySize, GEMV_MAX_SMEM);
   });
   if (ea != cudaSuccess) return ea;
   cudaLaunchConfig_t cfg = {};
@@ -432,7 +432,7 @@ static cudaError_t launch_nc(const GemvParams& p, cudaStream_t stream) {
   }
   cfg.attrs = attr;
   cfg.numAttrs = na;
-  return cudaLaunchKernelEx(&cfg, gemv_kernel<NC, UC>, p);
+  return cudaLaunchKernelEx(&cfg, hc_gemv_kernel<NC, UC>, p);
 }
 
 cudaError_t launch_gemv(const GemvParams& p, cudaStream_t stream) {

@@ -215,86 +215,6 @@ __device__ __forceinline__ void unit_compute_smem(const uint8_t* unit, int type,
   }
 }
 
-// Single-column block dots reading the unit from shared memory chunk by
-// chunk (same arithmetic as q4k_src / q6k_src with NC = 1): the unit is
-// not held in registers, which keeps register pressure low inside the
-// persistent step kernel.  `unit` is the staged tile-block, lane = row.
-__device__ __forceinline__ float q4k_smem_dot(const uint8_t* unit, int j, const ActSlice& act, int lane) {
-  const uint4* u = reinterpret_cast<const uint4*>(unit) + lane;
-  const Q4KHeader hd = q4k_header(u[0]);
-  const uint8_t* rec = act.a + j * Q8A_REC;
-  int isum = 0;
-#pragma unroll
-  for (int pp = 0; pp < 4; ++pp) {
-    const uint4 u0 = u[(1 + 2 * pp) * TILE], u1 = u[(2 + 2 * pp) * TILE];
-    const uint32_t w[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
-    const uint4 a0 = *reinterpret_cast<const uint4*>(rec + 64 * pp);
-    const uint4 a1 = *reinterpret_cast<const uint4*>(rec + 64 * pp + 16);
-    const uint4 a2 = *reinterpret_cast<const uint4*>(rec + 64 * pp + 32);
-    const uint4 a3 = *reinterpret_cast<const uint4*>(rec + 64 * pp + 48);
-    const uint32_t al[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-    const uint32_t ah[8] = {a2.x, a2.y, a2.z, a2.w, a3.x, a3.y, a3.z, a3.w};
-    int tl = 0, th = 0;
-#pragma unroll
-    for (int l = 0; l < 8; ++l) {
-      tl = dp4a(w[l] & 0x0f0f0f0fu, al[l], tl);
-      th = dp4a((w[l] >> 4) & 0x0f0f0f0fu, ah[l], th);
-    }
-    isum += hd.sc(2 * pp) * tl + hd.sc(2 * pp + 1) * th;
-  }
-  const uint4 bs = *reinterpret_cast<const uint4*>(rec + Q8A_BS);
-  int ms = __dp2a_lo(int(bs.x), int(hd.mn_lo), 0);
-  ms = __dp2a_hi(int(bs.y), int(hd.mn_lo), ms);
-  ms = __dp2a_lo(int(bs.z), int(hd.mn_hi), ms);
-  ms = __dp2a_hi(int(bs.w), int(hd.mn_hi), ms);
-  const float d8 = *reinterpret_cast<const float*>(rec + Q8A_D);
-  return __fmul_rn(hd.d, d8) * float(isum) - __fmul_rn(hd.dmin, d8) * float(ms);
-}
-
-__device__ __forceinline__ float q6k_smem_dot(const uint8_t* unit, int j, const ActSlice& act, int lane) {
-  const uint4* u = reinterpret_cast<const uint4*>(unit) + lane;
-  const float dw = f16_bits_to_f32(reinterpret_cast<const uint16_t*>(unit + Q6K_DPLANE_OFFSET)[lane]);
-  const uint4 scv = u[12 * TILE];
-  const uint32_t scw[4] = {scv.x, scv.y, scv.z, scv.w};
-  const uint8_t* rec = act.b + j * Q8B_REC;
-  int isum = 0;
-#pragma unroll
-  for (int s = 0; s < 8; ++s) {
-    const uint4 nv = u[s * TILE];
-    const uint32_t nw[4] = {nv.x, nv.y, nv.z, nv.w};
-    const uint4 hv = u[(8 + (s >> 1)) * TILE];
-    const uint32_t hw[4] = {hv.x, hv.y, hv.z, hv.w};
-    uint32_t ua[4], ub[4];
-#pragma unroll
-    for (int jj = 0; jj < 4; ++jj) q6k_unpack(nw[jj], hw[2 * (s & 1) + (jj >> 1)], jj & 1, ua[jj], ub[jj]);
-    const int sa = int(int8_t((scw[s >> 2] >> (8 * (s & 3))) & 0xff));
-    const int sb = int(int8_t((scw[(s + 8) >> 2] >> (8 * ((s + 8) & 3))) & 0xff));
-    const uint4 A = *reinterpret_cast<const uint4*>(rec + 16 * s);
-    const uint4 B = *reinterpret_cast<const uint4*>(rec + 16 * (s + 8));
-    int ta = dp4a(ua[0], A.x, 0);
-    ta = dp4a(ua[1], A.y, ta);
-    ta = dp4a(ua[2], A.z, ta);
-    ta = dp4a(ua[3], A.w, ta);
-    int tb = dp4a(ub[0], B.x, 0);
-    tb = dp4a(ub[1], B.y, tb);
-    tb = dp4a(ub[2], B.z, tb);
-    tb = dp4a(ub[3], B.w, tb);
-    isum += sa * ta + sb * tb;
-  }
-  const uint4 b0 = *reinterpret_cast<const uint4*>(rec + Q8B_BS);
-  const uint4 b1 = *reinterpret_cast<const uint4*>(rec + Q8B_BS + 16);
-  int corr = __dp2a_lo(int(b0.x), int(scw[0]), 0);
-  corr = __dp2a_hi(int(b0.y), int(scw[0]), corr);
-  corr = __dp2a_lo(int(b0.z), int(scw[1]), corr);
-  corr = __dp2a_hi(int(b0.w), int(scw[1]), corr);
-  corr = __dp2a_lo(int(b1.x), int(scw[2]), corr);
-  corr = __dp2a_hi(int(b1.y), int(scw[2]), corr);
-  corr = __dp2a_lo(int(b1.z), int(scw[3]), corr);
-  corr = __dp2a_hi(int(b1.w), int(scw[3]), corr);
-  const float d8 = *reinterpret_cast<const float*>(rec + Q8B_D);
-  return __fmul_rn(dw, d8) * float(isum - 32 * corr);
-}
-
 __device__ __forceinline__ int seg_of(const GemvParams& p, int tile_g) {
   int si = 0;
 #pragma unroll

@@ -57,7 +57,7 @@ struct GmShape {
 
 template <int GM_WARPS>
 __global__ void __launch_bounds__(GmShape<GM_WARPS>::THREADS, GmShape<GM_WARPS>::CTAS)
-    gemv_mma_kernel(const __grid_constant__ GemvParams p) {
+    hc_gemv_mma_kernel(const __grid_constant__ GemvParams p) {
   extern __shared__ __align__(16) uint8_t smem[];
   __shared__ float red[GM_WARPS][GM_COLS][32];
   __shared__ __align__(8) uint64_t bars[GM_WARPS][GM_MAX_RING];
@@ -242,7 +242,7 @@ static cudaError_t launch_gemv_mma_w(GemvParams& p, cudaStream_t stream) {
   if (p.split == 0 || smem > size_t(GEMV_MAX_SMEM)) return cudaErrorInvalidValue;
   static std::atomic<uint64_t> attr_set{0};
   const cudaError_t ea = once_per_current_device(attr_set, [] {
-    return cudaFuncSetAttribute(gemv_mma_kernel<W>, cudaFuncAttributeMaxDynamicSharedMemorySize, GEMV_MAX_SMEM);
+    return cudaFuncSetAttribute(hc_gemv_mma_kernel<W>, cudaFuncAttributeMaxDynamicSharedMemorySize, GEMV_MAX_SMEM);
   });
   if (ea != cudaSuccess) return ea;
   cudaLaunchConfig_t cfg = {};
@@ -264,7 +264,7 @@ static cudaError_t launch_gemv_mma_w(GemvParams& p, cudaStream_t stream) {
   }
   cfg.attrs = attr;
   cfg.numAttrs = na;
-  return cudaLaunchKernelEx(&cfg, gemv_mma_kernel<W>, p);
+  return cudaLaunchKernelEx(&cfg, hc_gemv_mma_kernel<W>, p);
 }
 
 static int gemv_mma_warps() {

@@ -22,7 +22,7 @@ struct GemvSeg {
 };
 
 // Fused input of a matmul whose input is an RMSNorm of the residual stream
-// (the per-layer norm_quant_kernel folded into the GEMV): every CTA computes
+// (the per-layer hc_norm_quant_kernel folded into the GEMV): every CTA computes
 // the norm of the whole D = 2048 vector itself and quantizes the 256-blocks
 // of its K slice straight into its shared-memory activation records.
 enum { GEMV_PRO_NONE = 0, GEMV_PRO_NORM = 1, GEMV_PRO_RESID_NORM = 2 };
@@ -72,7 +72,7 @@ constexpr int GEMV_PRE_SM_SMEM = 160 * 1024;          // shared memory per SM a 
                                                       // with prefetched units (the rest serves the kernels
                                                       // launched after it)
 
-// Static shared memory of gemv_kernel for a launch of `ncols` columns (the
+// Static shared memory of hc_gemv_kernel for a launch of `ncols` columns (the
 // column count rounds up to the kernel's 1/2/4/8 template): the per-warp
 // partials, rank 0's cluster gather array and the two mbarriers.
 inline size_t gemv_static_smem(int ncols) {
@@ -103,6 +103,10 @@ cudaError_t launch_q8k_quantize(const float* x, int K, int cols, const Q8Buf& q,
 cudaError_t launch_repack(int type, const uint8_t* src, uint8_t* dst, int rows, int rows_pad, int nb,
                           cudaStream_t stream);
 cudaError_t launch_dequant(int type, const uint8_t* w, float* out, int rows, int nb, cudaStream_t stream);
+// hp_matmul_dequantized_f32 arithmetic on a resident (tile-layout) weight:
+// out[col * rows + row], one sequential f32 chain per (row, column).
+cudaError_t launch_dequant_matmul(int type, const uint8_t* w, int nb, int rows, int rows_pad, const float* x, int K,
+                                  int cols, float* out, cudaStream_t stream);
 
 // Picks the K split for a launch; fills p.split and p.bps.
 void gemv_plan(GemvParams& p);

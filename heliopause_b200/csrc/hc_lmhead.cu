@@ -92,7 +92,7 @@ struct TopkFlush {
 // Persistent grid over the head's tiles; every warp owns whole tiles and its
 // own running top-k per column, so no barrier is needed until the end.
 template <int NC>
-__global__ void __launch_bounds__(GEMV_THREADS, GEMV_CTAS_PER_SM) lmhead_topk_kernel(
+__global__ void __launch_bounds__(GEMV_THREADS, GEMV_CTAS_PER_SM) hc_lmhead_topk_kernel(
     const __grid_constant__ LmHeadParams P) {
   const GemvParams& p = P.g;
   extern __shared__ __align__(16) uint8_t smem[];
@@ -153,7 +153,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, GEMV_CTAS_PER_SM) lmhead_topk_ke
 // Tensor-core LM head for 3..8 columns: the weight stream and block products
 // of the tensor-core GEMV (hc_mma_stream.cuh) over a persistent grid of
 // LMM_WARPS-warp CTAs walking the head's tiles, fused with the same per-warp
-// top-k lists as lmhead_topk_kernel.  A finished tile's 32 x 8 sums go from
+// top-k lists as hc_lmhead_topk_kernel.  A finished tile's 32 x 8 sums go from
 // the accumulator layout to lane = row through a padded shared-memory
 // transpose, then each column's keys are inserted into the warp's list.  The
 // CTA merges its warps' lists by rank into k candidates per column at
@@ -165,7 +165,7 @@ __host__ __device__ inline size_t lmm_list_bytes(const LmHeadParams& P) {
   return size_t(LMM_WARPS) * P.g.ncols * P.k * sizeof(uint64_t);
 }
 
-__global__ void __launch_bounds__(LMM_WARPS * 32, 1) lmhead_mma_kernel(const __grid_constant__ LmHeadParams P) {
+__global__ void __launch_bounds__(LMM_WARPS * 32, 1) hc_lmhead_mma_kernel(const __grid_constant__ LmHeadParams P) {
   const GemvParams& p = P.g;
   extern __shared__ __align__(16) uint8_t smem[];
   __shared__ float tr[LMM_WARPS][GM_COLS * LMM_TSTRIDE];
@@ -262,7 +262,7 @@ cudaError_t launch_lmhead_mma(LmHeadParams& P, int grid, cudaStream_t stream) {
   P.g.ring = ring;
   static std::atomic<uint64_t> attr_set{0};
   const cudaError_t ea = once_per_current_device(attr_set, [] {
-    return cudaFuncSetAttribute(lmhead_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, GEMV_MAX_SMEM);
+    return cudaFuncSetAttribute(hc_lmhead_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, GEMV_MAX_SMEM);
   });
   if (ea != cudaSuccess) return ea;
   cudaLaunchConfig_t cfg = {};
@@ -275,7 +275,7 @@ cudaError_t launch_lmhead_mma(LmHeadParams& P, int grid, cudaStream_t stream) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, lmhead_mma_kernel, P);
+  return cudaLaunchKernelEx(&cfg, hc_lmhead_mma_kernel, P);
 }
 
 // Top-k candidates of materialized logits (the tensor-core LM head for wide
@@ -283,7 +283,7 @@ cudaError_t launch_lmhead_mma(LmHeadParams& P, int grid, cudaStream_t stream) {
 // of one column, each of its 4 warps keeping a running list over 32-row
 // steps (topk_insert_warp), then the 4 lists are merged by rank into the
 // CTA's k candidates at cand[col * col_stride + chunk * k].
-__global__ void __launch_bounds__(GEMV_THREADS) logits_topk_kernel(const float* __restrict__ logits, int rows,
+__global__ void __launch_bounds__(GEMV_THREADS) hc_logits_topk_kernel(const float* __restrict__ logits, int rows,
                                                                    int chunk_rows, int k, int32_t id_offset,
                                                                    uint64_t* __restrict__ cand, size_t col_stride) {
   __shared__ uint64_t best[GEMV_WARPS_PER_CTA][TOPK_MAX];
@@ -324,7 +324,7 @@ __global__ void __launch_bounds__(GEMV_THREADS) logits_topk_kernel(const float* 
 cudaError_t launch_logits_topk(const float* logits, int rows, int cols, int k, int32_t id_offset, uint64_t* cand,
                                size_t col_stride, cudaStream_t stream) {
   const dim3 grid(unsigned((rows + LOGITS_CHUNK_ROWS - 1) / LOGITS_CHUNK_ROWS), unsigned(cols));
-  logits_topk_kernel<<<grid, GEMV_THREADS, 0, stream>>>(logits, rows, LOGITS_CHUNK_ROWS, k, id_offset, cand,
+  hc_logits_topk_kernel<<<grid, GEMV_THREADS, 0, stream>>>(logits, rows, LOGITS_CHUNK_ROWS, k, id_offset, cand,
                                                         col_stride);
   return cudaGetLastError();
 }
@@ -452,7 +452,7 @@ __device__ void radix_select_topk(const uint64_t* c, int n, int group, size_t gr
 // mergeTopCandidates does; the selected keys too when keys_out != nullptr.
 constexpr int MERGE_SURV = 1024;
 
-__global__ void __launch_bounds__(MERGE_THREADS) topk_merge_kernel(const uint64_t* __restrict__ cand, int n,
+__global__ void __launch_bounds__(MERGE_THREADS) hc_topk_merge_kernel(const uint64_t* __restrict__ cand, int n,
                                                                    size_t col_stride, int group, size_t group_stride,
                                                                    int k, float softcap, int32_t* __restrict__ ids,
                                                                    float* __restrict__ vals,
@@ -569,7 +569,7 @@ template <int NC>
 static cudaError_t launch_lm_nc(const LmHeadParams& P, int grid, cudaStream_t stream) {
   static std::atomic<uint64_t> attr_set{0};
   const cudaError_t ea = once_per_current_device(attr_set, [] {
-    return cudaFuncSetAttribute(lmhead_topk_kernel<NC>, cudaFuncAttributeMaxDynamicSharedMemorySize, GEMV_MAX_SMEM);
+    return cudaFuncSetAttribute(hc_lmhead_topk_kernel<NC>, cudaFuncAttributeMaxDynamicSharedMemorySize, GEMV_MAX_SMEM);
   });
   if (ea != cudaSuccess) return ea;
   const size_t smem = gemv_smem_bytes(P.g, P.g.nb);
@@ -584,7 +584,7 @@ static cudaError_t launch_lm_nc(const LmHeadParams& P, int grid, cudaStream_t st
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, lmhead_topk_kernel<NC>, P);
+  return cudaLaunchKernelEx(&cfg, hc_lmhead_topk_kernel<NC>, P);
 }
 
 cudaError_t launch_lmhead_topk(const LmHeadParams& P, int grid, cudaStream_t stream) {
@@ -606,7 +606,7 @@ cudaError_t launch_topk_merge(const uint64_t* cand, int n, size_t col_stride, in
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, topk_merge_kernel, cand, n, col_stride, group, group_stride, k, softcap, ids, vals,
+  return cudaLaunchKernelEx(&cfg, hc_topk_merge_kernel, cand, n, col_stride, group, group_stride, k, softcap, ids, vals,
                             keys_out);
 }
 

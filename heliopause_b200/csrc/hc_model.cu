@@ -27,7 +27,6 @@
 #include "hc_internal.h"
 #include "hc_kernels.cuh"
 #include "hc_lmhead.cuh"
-#include "hc_persist.cuh"
 
 namespace {
 
@@ -69,14 +68,6 @@ struct hpc_model_s {
   std::vector<cudaGraphExec_t> graphs;
   std::vector<int> graph_k;
   cudaStream_t capture_stream = nullptr;
-  // persistent single-token step (hc_persist.cu)
-  bool persist_enabled = false;
-  int persist_state = 0;  // 0 = plan not built, 1 = usable, -1 = not supported for this model
-  int persist_grid = 0;
-  hc::PLayer* d_players = nullptr;
-  void* persist_buf = nullptr;
-  hc::PParams pparams{};
-  size_t persist_ctr_bytes = 0;
   // prefill workspace (hpc_model_prefill), grown to the largest token count seen
   void* pf_arena = nullptr;
   int pf_cap = 0;
@@ -212,8 +203,6 @@ int hpc_model_release(hpc_model m) {
   cudaFree(m->output_norm);
   cudaFree(m->arena);
   cudaFree(m->cand);
-  cudaFree(m->d_players);
-  cudaFree(m->persist_buf);
   cudaFree(m->pf_arena);
   cudaFree(m->pf_part);
   if (m->capture_stream) cudaStreamDestroy(m->capture_stream);
@@ -227,7 +216,6 @@ static void invalidate_graphs(hpc_model m) {
     if (g) cudaGraphExecDestroy(g);
     g = nullptr;
   }
-  m->persist_state = 0;  // the plan holds weight pointers: rebuild on the next step
 }
 
 int hpc_model_set_weight(hpc_model m, int layer, int slot, hpc_weight w) {
@@ -299,19 +287,6 @@ int hpc_model_set_lm_head(hpc_model m, hpc_weight w) {
   return HPC_OK;
 }
 
-int hpc_model_set_persistent(hpc_model m, int enable) {
-  if (!model_valid(m)) return hpc_fail(HPC_ERR_ARG, "invalid model");
-  m->persist_enabled = enable != 0;
-  invalidate_graphs(m);
-  return HPC_OK;
-}
-
-int hpc_model_step_kind(hpc_model m, size_t token_count, int* out_kind) {
-  if (!model_valid(m) || !out_kind) return hpc_fail(HPC_ERR_ARG, "invalid model / null out");
-  *out_kind = (token_count == 1 && m->persist_enabled && m->persist_state == 1) ? 1 : 0;
-  return HPC_OK;
-}
-
 int hpc_model_kv(hpc_model m, int kv_layer, float** d_key, float** d_value) {
   if (!model_valid(m)) return hpc_fail(HPC_ERR_ARG, "invalid model");
   if (kv_layer < 0 || kv_layer >= m->cfg.kv_layers) return hpc_fail(HPC_ERR_ARG, "kv layer %d", kv_layer);
@@ -321,119 +296,6 @@ int hpc_model_kv(hpc_model m, int kv_layer, float** d_key, float** d_value) {
 }
 
 }  // extern "C"
-
-// Builds the persistent-step plan (per-layer weight tables, partial and
-// record buffers, counters).  Sets persist_state to -1 when the model's
-// shapes fall outside what the persistent kernel supports; the per-kernel
-// step then serves M = 1 too.
-static int build_persist_plan(hpc_model m) {
-  const hpc_model_config& c = m->cfg;
-  m->persist_state = -1;
-  cudaFree(m->d_players);
-  cudaFree(m->persist_buf);
-  m->d_players = nullptr;
-  m->persist_buf = nullptr;
-  const int D = c.hidden, F = c.ffn, H = c.heads, KVH = c.kv_heads;
-  const int grid = hc::persist_grid();
-  if (grid == 0 || D != 2048 || H * 256 != D || H % KVH != 0 || H / KVH > hc::P_MAX_G ||
-      F % 2048 != 0 || (F / 256) * hc::Q8B_REC > hc::P_ACT_BYTES || c.context % hc::P_ATT_TOK != 0 ||
-      grid % KVH != 0 || grid < H || grid < F / 2048 || grid / KVH > 256)
-    return HPC_OK;
-  std::vector<hc::PLayer> pl(c.layers);
-  size_t part_floats[4] = {0, 0, 0, 0};
-  auto gemv = [&](hc::PGemv& g, std::initializer_list<hpc_weight> ws, int kind) -> bool {
-    memset(&g, 0, sizeof g);
-    int tiles = 0, n = 0;
-    for (hpc_weight w : ws) {
-      g.w[n] = w->d_data;
-      g.type[n] = w->type;
-      tiles += int(w->rows_pad / hc::TILE);
-      g.tile_end[n] = tiles;
-      if (n == 0) g.B = w->nb;
-      else if (w->nb != g.B) return false;
-      ++n;
-    }
-    for (int i = n; i < 3; ++i) g.tile_end[i] = tiles;
-    g.nseg = n;
-    g.tiles = tiles;
-    bool warp_ok = false;
-    if (size_t(tiles) * g.B * grid >= (size_t(1) << 31)) return false;
-    g.maxseg = hc::persist_maxseg(tiles, g.B, grid, &warp_ok);
-    part_floats[kind] = std::max(part_floats[kind], size_t(tiles) * g.maxseg * 32);
-    return warp_ok && g.maxseg <= hc::P_MAXSEG;
-  };
-  for (int l = 0; l < c.layers; ++l) {
-    const Layer& L = m->layers[l];
-    hc::PLayer& P = pl[l];
-    const bool own = l < c.kv_layers;
-    bool ok = own ? gemv(P.qkv, {L.w[HPC_W_Q], L.w[HPC_W_K], L.w[HPC_W_V]}, 0) : gemv(P.qkv, {L.w[HPC_W_Q]}, 0);
-    ok = ok && gemv(P.o, {L.w[HPC_W_O]}, 1) && gemv(P.gu, {L.w[HPC_W_GATE], L.w[HPC_W_UP]}, 2) &&
-         gemv(P.down, {L.w[HPC_W_DOWN]}, 3);
-    // a CTA's gate/up range may complete at most 16 activation blocks
-    const int gu_units = P.gu.tiles * P.gu.B;
-    if ((gu_units + grid - 1) / grid / (P.gu.B * 8) + 2 > 16) ok = false;
-    if (!ok) return HPC_OK;
-    P.n_attn = L.norm[HPC_N_ATTN];
-    P.n_q = L.norm[HPC_N_Q];
-    P.n_k = L.norm[HPC_N_K];
-    P.n_post_attn = L.norm[HPC_N_POST_ATTN];
-    P.n_ffn = L.norm[HPC_N_FFN];
-    P.n_post_ffw = L.norm[HPC_N_POST_FFW];
-    P.kc = m->kc[m->kv_source[l]];
-    P.vc = m->vc[m->kv_source[l]];
-    P.own_kv = own ? 1 : 0;
-  }
-  auto al = [](size_t x) { return (x + 255) & ~size_t(255); };
-  size_t off[9], total = 0;
-  const size_t sizes[9] = {part_floats[0] * 4, part_floats[1] * 4, part_floats[2] * 4, part_floats[3] * 4,
-                           size_t(grid) * hc::P_ATT_REC * 4, hc::q8buf_bytes(D, 1), hc::q8buf_bytes(F, 1),
-                           size_t(D) * 4,
-                           ((size_t(c.layers) * hc::PS_COUNT + 1) * hc::P_CTR_STRIDE + size_t(c.layers) * (KVH + F / 256)) *
-                               4};
-  for (int i = 0; i < 9; ++i) {
-    off[i] = total;
-    total += al(sizes[i]);
-  }
-  HPC_CK(cudaMalloc(&m->persist_buf, total), "cudaMalloc(persistent step buffers)");
-  HPC_CK(cudaMemset(m->persist_buf, 0, total), "cudaMemset(persistent step buffers)");
-  char* b = static_cast<char*>(m->persist_buf);
-  for (auto& P : pl) {
-    P.qkv.part = reinterpret_cast<float*>(b + off[0]);
-    P.o.part = reinterpret_cast<float*>(b + off[1]);
-    P.gu.part = reinterpret_cast<float*>(b + off[2]);
-    P.down.part = reinterpret_cast<float*>(b + off[3]);
-  }
-  HPC_CK(cudaMalloc(&m->d_players, sizeof(hc::PLayer) * pl.size()), "cudaMalloc(persistent plan)");
-  HPC_CK(cudaMemcpy(m->d_players, pl.data(), sizeof(hc::PLayer) * pl.size(), cudaMemcpyHostToDevice),
-         "persistent plan upload");
-  hc::PParams& P = m->pparams;
-  memset(&P, 0, sizeof P);
-  P.layers = m->d_players;
-  P.nlayers = c.layers;
-  P.D = D;
-  P.F = F;
-  P.H = H;
-  P.KVH = KVH;
-  P.cap = c.context;
-  P.eps = c.rms_eps;
-  P.pos = m->pos;
-  P.cos_t = m->cos_t;
-  P.sin_t = m->sin_t;
-  P.X = m->x;
-  P.att_part = reinterpret_cast<float*>(b + off[4]);
-  P.q8_attn = reinterpret_cast<uint8_t*>(b + off[5]);
-  P.q8_act = reinterpret_cast<uint8_t*>(b + off[6]);
-  P.H1 = reinterpret_cast<float*>(b + off[7]);
-  P.counters = reinterpret_cast<unsigned*>(b + off[8]);
-  P.abort_word = reinterpret_cast<int*>(P.counters + size_t(c.layers) * hc::PS_COUNT * hc::P_CTR_STRIDE);
-  P.kvh_counters = P.counters + (size_t(c.layers) * hc::PS_COUNT + 1) * hc::P_CTR_STRIDE;
-  P.blk_counters = P.kvh_counters + size_t(c.layers) * KVH;
-  P.err = m->err;
-  m->persist_ctr_bytes = sizes[8];
-  m->persist_grid = grid;
-  m->persist_state = 1;
-  return HPC_OK;
-}
 
 // Enqueues the whole step for M tokens on `st` (inputs already in m->ids/pos).
 static int enqueue_step(hpc_model m, int M, int k, cudaStream_t st) {
@@ -462,20 +324,6 @@ static int enqueue_step(hpc_model m, int M, int k, cudaStream_t st) {
   HPC_CK(hc::launch_embed(emb->d_data, emb->type, emb->nb, c.vocab, m->ids, m->x, M, D, std::sqrt(double(D)), m->err,
                           st),
          "embedding");
-  if (M == 1 && m->persist_enabled) {
-    if (m->persist_state == 0) {
-      int rc = build_persist_plan(m);
-      if (rc != HPC_OK) return rc;
-    }
-    if (m->persist_state == 1) {
-      HPC_CK(cudaMemsetAsync(m->pparams.counters, 0, m->persist_ctr_bytes, st), "counter reset");
-      HPC_CK(hc::launch_persistent_step(m->pparams, m->persist_grid, st), "persistent step launch");
-      HPC_CK(hc::launch_norm_quant(false, m->x, m->x, nullptr, nullptr, m->output_norm, eps, M, D, qd, nullptr, st),
-             "output norm");
-      return hpc_lm_head_topk_q8(emb, m->q8d, m->q8d_bytes, size_t(D), size_t(M), size_t(k), 0, m->cand,
-                                 m->cand_bytes, c.final_logit_softcap, m->out_ids, m->out_vals, nullptr, st);
-    }
-  }
   // One or two columns of width 2048: the RMSNorms (+ residual adds) that feed
   // the QKV and gate/up projections are folded into those GEMVs (every CTA
   // computes them, hc_gemv.cu gemv_prologue).  The residual stream then

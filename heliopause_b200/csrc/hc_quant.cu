@@ -15,7 +15,7 @@
 namespace hc {
 
 template <bool NATURAL>
-__global__ void __launch_bounds__(256) q8k_quantize_kernel(const float* __restrict__ x, int K, int cols, Q8Buf q,
+__global__ void __launch_bounds__(256) hc_q8k_quantize_kernel(const float* __restrict__ x, int K, int cols, Q8Buf q,
                                                            int8_t* __restrict__ nat_qs,
                                                            int16_t* __restrict__ nat_bs32,
                                                            float* __restrict__ nat_d) {
@@ -58,8 +58,8 @@ cudaError_t launch_q8k_quantize(const float* x, int K, int cols, const Q8Buf& q,
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (nat_qs) return cudaLaunchKernelEx(&cfg, q8k_quantize_kernel<true>, x, K, cols, q, nat_qs, nat_bs32, nat_d);
-  return cudaLaunchKernelEx(&cfg, q8k_quantize_kernel<false>, x, K, cols, q, (int8_t*)nullptr, (int16_t*)nullptr,
+  if (nat_qs) return cudaLaunchKernelEx(&cfg, hc_q8k_quantize_kernel<true>, x, K, cols, q, nat_qs, nat_bs32, nat_d);
+  return cudaLaunchKernelEx(&cfg, hc_q8k_quantize_kernel<false>, x, K, cols, q, (int8_t*)nullptr, (int16_t*)nullptr,
                             (float*)nullptr);
 }
 

@@ -15,7 +15,7 @@ namespace hc {
 
 // ---- repack: one thread per (row, block) -----------------------------------
 
-__global__ void repack_q4k_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, int rows,
+__global__ void hc_repack_q4k_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, int rows,
                                   int rows_pad, int nb) {
   const size_t t = blockIdx.x * size_t(blockDim.x) + threadIdx.x;
   if (t >= size_t(rows_pad) * nb) return;
@@ -57,7 +57,7 @@ __device__ __forceinline__ int q6_elem(int s, int j, int i) {
   return 16 * s + 2 * j + off[i];
 }
 
-__global__ void repack_q6k_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, int rows,
+__global__ void hc_repack_q6k_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, int rows,
                                   int rows_pad, int nb) {
   const size_t t = blockIdx.x * size_t(blockDim.x) + threadIdx.x;
   if (t >= size_t(rows_pad) * nb) return;
@@ -112,64 +112,129 @@ __global__ void repack_q6k_kernel(const uint8_t* __restrict__ src, uint8_t* __re
   *reinterpret_cast<uint16_t*>(base + Q6K_DPLANE_OFFSET + size_t(lane) * 2) = uint16_t(blk[208] | (blk[209] << 8));
 }
 
-// ---- dequantize from the tile layout: one thread per (row, block) -----------
+// ---- dequantize from the tile layout ------------------------------------------
+//
+// The per-row pieces below are shared by the dequantize kernels and by the
+// dequantized matmul, so the bit-exact dequant test covers both.
 
-__global__ void dequant_q4k_kernel(const uint8_t* __restrict__ w, float* __restrict__ out, int rows, int nb) {
-  const size_t t = blockIdx.x * size_t(blockDim.x) + threadIdx.x;
-  if (t >= size_t(rows) * nb) return;
-  const int row = int(t / nb), b = int(t % nb);
-  const uint4* c = reinterpret_cast<const uint4*>(w + (size_t(row / TILE) * nb + b) * Q4K_TILE_BLOCK_BYTES) + (row % TILE);
-  Q4KHeader hd = q4k_header(c[0]);
-  float* o = out + size_t(row) * nb * QK + size_t(b) * QK;
-  for (int ch = 0; ch < 8; ++ch) {
-    const uint4 v = c[size_t(1 + ch) * TILE];
-    const uint32_t words[4] = {v.x, v.y, v.z, v.w};
-    const int p = ch >> 1;
-    const float d1 = __fmul_rn(hd.d, float(hd.sc(2 * p))), d2 = __fmul_rn(hd.d, float(hd.sc(2 * p + 1)));
-    const float m1 = __fmul_rn(hd.dmin, float(hd.mn(2 * p))), m2 = __fmul_rn(hd.dmin, float(hd.mn(2 * p + 1)));
-    for (int k = 0; k < 4; ++k) {
-      const int l = 4 * (ch & 1) + k;
-      for (int i = 0; i < 4; ++i) {
-        const uint32_t byte = (words[k] >> (8 * i)) & 0xff;
-        const int j = l + 8 * i;  // position inside the 32-byte pair
-        o[64 * p + j] = __fsub_rn(__fmul_rn(d1, float(byte & 15)), m1);
-        o[64 * p + 32 + j] = __fsub_rn(__fmul_rn(d2, float(byte >> 4)), m2);
-      }
+// Row `r` of a Q4_K tile-block: the 32 values of quant chunk ch (0..7) into
+// o[0..256): elements 64p + j (low nibbles) and 64p + 32 + j (high), p = ch/2.
+__device__ __forceinline__ void q4k_dequant_chunk(const uint8_t* tb, int r, int ch, float* o) {
+  const uint4* c = reinterpret_cast<const uint4*>(tb) + r;
+  const Q4KHeader hd = q4k_header(c[0]);
+  const uint4 v = c[size_t(1 + ch) * TILE];
+  const uint32_t words[4] = {v.x, v.y, v.z, v.w};
+  const int p = ch >> 1;
+  const float d1 = __fmul_rn(hd.d, float(hd.sc(2 * p))), d2 = __fmul_rn(hd.d, float(hd.sc(2 * p + 1)));
+  const float m1 = __fmul_rn(hd.dmin, float(hd.mn(2 * p))), m2 = __fmul_rn(hd.dmin, float(hd.mn(2 * p + 1)));
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int l = 4 * (ch & 1) + k;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t byte = (words[k] >> (8 * i)) & 0xff;
+      const int j = l + 8 * i;  // position inside the 32-byte pair
+      o[64 * p + j] = __fsub_rn(__fmul_rn(d1, float(byte & 15)), m1);
+      o[64 * p + 32 + j] = __fsub_rn(__fmul_rn(d2, float(byte >> 4)), m2);
     }
   }
 }
 
-__global__ void dequant_q6k_kernel(const uint8_t* __restrict__ w, float* __restrict__ out, int rows, int nb) {
+// Row `r` of a Q6_K tile-block: the 32 values of 16-groups s and s + 8
+// (s = 0..7) into o[0..256).
+__device__ __forceinline__ void q6k_dequant_group(const uint8_t* tb, int r, int s, float* o) {
+  const uint4* c = reinterpret_cast<const uint4*>(tb) + r;
+  const float d = f16_bits_to_f32(reinterpret_cast<const uint16_t*>(tb + Q6K_DPLANE_OFFSET)[r]);
+  const uint4 scv = c[12 * TILE];
+  const uint32_t scw[4] = {scv.x, scv.y, scv.z, scv.w};
+  const uint4 nv = c[size_t(s) * TILE];
+  const uint32_t nw[4] = {nv.x, nv.y, nv.z, nv.w};
+  const uint4 hv = c[size_t(8 + (s >> 1)) * TILE];
+  const uint32_t hw4[4] = {hv.x, hv.y, hv.z, hv.w};
+  const int sa = int(int8_t((scw[s >> 2] >> (8 * (s & 3))) & 0xff));
+  const int sb = int(int8_t((scw[(s + 8) >> 2] >> (8 * ((s + 8) & 3))) & 0xff));
+  const float da = __fmul_rn(d, float(sa)), db = __fmul_rn(d, float(sb));
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint32_t hw = hw4[2 * (s & 1) + (j >> 1)];
+    uint32_t ua, ub;
+    q6k_unpack(nw[j], hw, j & 1, ua, ub);
+    const int off[4] = {0, 8, 1, 9};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int qa = int((ua >> (8 * i)) & 0xff) - 32;
+      const int qb = int((ub >> (8 * i)) & 0xff) - 32;
+      o[16 * s + 2 * j + off[i]] = __fmul_rn(da, float(qa));
+      o[16 * (s + 8) + 2 * j + off[i]] = __fmul_rn(db, float(qb));
+    }
+  }
+}
+
+// One thread per (row, block).
+__global__ void hc_dequant_q4k_kernel(const uint8_t* __restrict__ w, float* __restrict__ out, int rows, int nb) {
   const size_t t = blockIdx.x * size_t(blockDim.x) + threadIdx.x;
   if (t >= size_t(rows) * nb) return;
   const int row = int(t / nb), b = int(t % nb);
-  const uint8_t* base = w + (size_t(row / TILE) * nb + b) * Q6K_TILE_BLOCK_BYTES;
-  const uint4* c = reinterpret_cast<const uint4*>(base) + (row % TILE);
-  const float d = f16_bits_to_f32(reinterpret_cast<const uint16_t*>(base + Q6K_DPLANE_OFFSET)[row % TILE]);
-  const uint4 scv = c[12 * TILE];
-  const uint32_t scw[4] = {scv.x, scv.y, scv.z, scv.w};
+  const uint8_t* tb = w + (size_t(row / TILE) * nb + b) * Q4K_TILE_BLOCK_BYTES;
   float* o = out + size_t(row) * nb * QK + size_t(b) * QK;
-  for (int s = 0; s < 8; ++s) {
-    const uint4 nv = c[size_t(s) * TILE];
-    const uint32_t nw[4] = {nv.x, nv.y, nv.z, nv.w};
-    const uint4 hv = c[size_t(8 + (s >> 1)) * TILE];
-    const uint32_t hw4[4] = {hv.x, hv.y, hv.z, hv.w};
-    const int sa = int(int8_t((scw[s >> 2] >> (8 * (s & 3))) & 0xff));
-    const int sb = int(int8_t((scw[(s + 8) >> 2] >> (8 * ((s + 8) & 3))) & 0xff));
-    const float da = __fmul_rn(d, float(sa)), db = __fmul_rn(d, float(sb));
-    for (int j = 0; j < 4; ++j) {
-      const uint32_t hw = hw4[2 * (s & 1) + (j >> 1)];
-      uint32_t ua, ub;
-      q6k_unpack(nw[j], hw, j & 1, ua, ub);
-      const int off[4] = {0, 8, 1, 9};
-      for (int i = 0; i < 4; ++i) {
-        const int qa = int((ua >> (8 * i)) & 0xff) - 32;
-        const int qb = int((ub >> (8 * i)) & 0xff) - 32;
-        o[16 * s + 2 * j + off[i]] = __fmul_rn(da, float(qa));
-        o[16 * (s + 8) + 2 * j + off[i]] = __fmul_rn(db, float(qb));
-      }
+  for (int ch = 0; ch < 8; ++ch) q4k_dequant_chunk(tb, row % TILE, ch, o);
+}
+
+__global__ void hc_dequant_q6k_kernel(const uint8_t* __restrict__ w, float* __restrict__ out, int rows, int nb) {
+  const size_t t = blockIdx.x * size_t(blockDim.x) + threadIdx.x;
+  if (t >= size_t(rows) * nb) return;
+  const int row = int(t / nb), b = int(t % nb);
+  const uint8_t* tb = w + (size_t(row / TILE) * nb + b) * Q6K_TILE_BLOCK_BYTES;
+  float* o = out + size_t(row) * nb * QK + size_t(b) * QK;
+  for (int s = 0; s < 8; ++s) q6k_dequant_group(tb, row % TILE, s, o);
+}
+
+// ---- dequantized matmul (hp_matmul_dequantized_f32, lib.rs:103-154) ---------
+//
+// out[col * rows + row] = the sequential f32 sum over k of
+// fround(w[row][k] * x[col][k]), w the bit-exact dequantized row: one
+// thread per (row, column) runs the reference's own chain
+// sum = fround(sum + fround(w * x)) in index order (no fused multiply-add,
+// no reassociation), so the result is the reference's bit for bit.
+// CTA = one 32-row tile x DM_COLS columns; per 256-block the tile's rows are
+// dequantized into shared memory (8 threads per row) and the columns' input
+// slice staged beside them.
+constexpr int DM_COLS = 8;
+
+__global__ void __launch_bounds__(256) hc_dequant_matmul_kernel(const uint8_t* __restrict__ w, int type, int nb,
+                                                                int rows, const float* __restrict__ x, int K, int cols,
+                                                                float* __restrict__ out) {
+  __shared__ float ws[TILE][QK + 1];
+  __shared__ float xs[DM_COLS][QK];
+  const int tile = int(blockIdx.x), col0 = int(blockIdx.y) * DM_COLS;
+  const int t = int(threadIdx.x), warp = t >> 5, lane = t & 31;
+  const int ncols = min(DM_COLS, cols - col0);
+  const size_t ub = type == TYPE_Q4_K ? Q4K_TILE_BLOCK_BYTES : Q6K_TILE_BLOCK_BYTES;
+  float sum = 0.0f;
+  for (int b = 0; b < nb; ++b) {
+    const uint8_t* tb = w + (size_t(tile) * nb + b) * ub;
+    if (type == TYPE_Q4_K) q4k_dequant_chunk(tb, t >> 3, t & 7, ws[t >> 3]);
+    else q6k_dequant_group(tb, t >> 3, t & 7, ws[t >> 3]);
+    for (int i = t; i < ncols * QK; i += 256) xs[i / QK][i % QK] = x[size_t(col0 + i / QK) * K + size_t(b) * QK + i % QK];
+    __syncthreads();
+    if (warp < ncols) {
+      const float* wr = ws[lane];
+      const float* xc = xs[warp];
+#pragma unroll 8
+      for (int i = 0; i < QK; ++i) sum = __fadd_rn(sum, __fmul_rn(wr[i], xc[i]));
     }
+    __syncthreads();
   }
+  const int row = tile * TILE + lane;
+  if (warp < ncols && row < rows) out[size_t(col0 + warp) * rows + row] = sum;
+}
+
+cudaError_t launch_dequant_matmul(int type, const uint8_t* w, int nb, int rows, int rows_pad, const float* x, int K,
+                                  int cols, float* out, cudaStream_t stream) {
+  if (cols <= 0 || rows <= 0) return cudaSuccess;
+  const dim3 grid(unsigned(rows_pad / TILE), unsigned((cols + DM_COLS - 1) / DM_COLS));
+  hc_dequant_matmul_kernel<<<grid, 256, 0, stream>>>(w, type, nb, rows, x, K, cols, out);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_repack(int type, const uint8_t* src, uint8_t* dst, int rows, int rows_pad, int nb,
@@ -177,8 +242,8 @@ cudaError_t launch_repack(int type, const uint8_t* src, uint8_t* dst, int rows, 
   const size_t n = size_t(rows_pad) * nb;
   const int threads = 128;
   const unsigned blocks = unsigned((n + threads - 1) / threads);
-  if (type == TYPE_Q4_K) repack_q4k_kernel<<<blocks, threads, 0, stream>>>(src, dst, rows, rows_pad, nb);
-  else repack_q6k_kernel<<<blocks, threads, 0, stream>>>(src, dst, rows, rows_pad, nb);
+  if (type == TYPE_Q4_K) hc_repack_q4k_kernel<<<blocks, threads, 0, stream>>>(src, dst, rows, rows_pad, nb);
+  else hc_repack_q6k_kernel<<<blocks, threads, 0, stream>>>(src, dst, rows, rows_pad, nb);
   return cudaGetLastError();
 }
 
@@ -186,8 +251,8 @@ cudaError_t launch_dequant(int type, const uint8_t* w, float* out, int rows, int
   const size_t n = size_t(rows) * nb;
   const int threads = 128;
   const unsigned blocks = unsigned((n + threads - 1) / threads);
-  if (type == TYPE_Q4_K) dequant_q4k_kernel<<<blocks, threads, 0, stream>>>(w, out, rows, nb);
-  else dequant_q6k_kernel<<<blocks, threads, 0, stream>>>(w, out, rows, nb);
+  if (type == TYPE_Q4_K) hc_dequant_q4k_kernel<<<blocks, threads, 0, stream>>>(w, out, rows, nb);
+  else hc_dequant_q6k_kernel<<<blocks, threads, 0, stream>>>(w, out, rows, nb);
   return cudaGetLastError();
 }
 

@@ -13,6 +13,7 @@ runs on the GPU through libheliocuda.so:
     releaseWasmQuantizedWeightHandle :576   release_quantized_weight_handle
     matMulQuantizedWasmResident   :593      mat_mul_quantized_resident
     matMulQuantizedWasmResidentMulti :648   mat_mul_quantized_resident_multi
+    matMulDequantizedWasm         :468      mat_mul_dequantized
     quantizedTypeId               :1908     quantized_type_id
 
 Activations and outputs are torch CUDA tensors (float32); numpy arrays are
@@ -219,6 +220,37 @@ def mat_mul_quantized(type_name: str, weight_bytes, input_columns, input_size: i
                                                column_count, out.ctypes.data_as(C.c_void_p), out.size)
     assert_cuda_ok(code, "matMulQuantized")
     return out
+
+
+def mat_mul_dequantized(type_name: str, weight_bytes, input_columns, input_size: int, row_count: int,
+                        column_count: int) -> np.ndarray:
+    """wasm-kernels.ts:468-520 matMulDequantizedWasm -> hp_matmul_dequantized_f32
+    (lib.rs:103-154): bit-exact dequantized rows times the input columns with
+    the reference's sequential f32 sum; host buffers in and out."""
+    tid = quantized_type_id(type_name)
+    w = np.ascontiguousarray(np.frombuffer(weight_bytes, dtype=np.uint8)
+                             if isinstance(weight_bytes, (bytes, bytearray, memoryview)) else weight_bytes,
+                             dtype=np.uint8)
+    x = np.ascontiguousarray(input_columns, dtype=np.float32)
+    if x.size != input_size * column_count:
+        raise CudaKernelError(ERR_SHAPE, f"Dequantized matmul input shape mismatch: {x.size}")
+    out = np.empty(row_count * column_count, np.float32)
+    code = _lib.lib().hpc_matmul_dequantized_f32(tid, w.ctypes.data_as(C.c_void_p), w.size,
+                                                 x.ctypes.data_as(C.c_void_p), x.size, input_size, row_count,
+                                                 column_count, out.ctypes.data_as(C.c_void_p), out.size)
+    assert_cuda_ok(code, "matMulDequantized")
+    return out
+
+
+def mat_mul_dequantized_resident(handle: CudaQuantizedWeightHandle, input_columns, input_size: int, row_count: int,
+                                 column_count: int):
+    """The same arithmetic on a resident weight (hpc_matmul_dequantized_prepared_f32)."""
+    x, from_host = _as_device_f32(input_columns)
+    out = torch.empty(row_count * column_count, dtype=torch.float32, device="cuda")
+    code = _lib.lib().hpc_matmul_dequantized_prepared_f32(handle.handle, _ptr(x), x.numel(), input_size, row_count,
+                                                          column_count, _ptr(out), out.numel(), _stream())
+    assert_cuda_ok(code, "matMulDequantizedResident")
+    return out.cpu().numpy() if from_host else out
 
 
 def lm_head_topk(handle: CudaQuantizedWeightHandle, hidden, column_count: int, k: int, *, softcap: float = 0.0,

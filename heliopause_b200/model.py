@@ -248,17 +248,6 @@ class CudaDecoderModel:
         return kt, vt
 
     # ---- running -----------------------------------------------------------
-    def set_persistent(self, enable: bool) -> None:
-        """Single-token steps through the persistent step kernel (default) or
-        the per-kernel chain (hpc_model_set_persistent)."""
-        hk.assert_cuda_ok(_lib.lib().hpc_model_set_persistent(self._h, int(bool(enable))), "modelSetPersistent")
-
-    def step_kind(self, token_count: int = 1) -> int:
-        """1 if the last built step for token_count tokens is the persistent kernel."""
-        out = C.c_int()
-        hk.assert_cuda_ok(_lib.lib().hpc_model_step_kind(self._h, token_count, C.byref(out)), "modelStepKind")
-        return out.value
-
     def forward(self, token_ids, positions, top_k: int, *, return_hidden: bool = False):
         """Top-k (ids, values) of every position, [n][top_k] torch tensors."""
         ids = torch.as_tensor(token_ids, dtype=torch.int32).reshape(-1)

@@ -123,6 +123,23 @@ int hpc_matmul_quantized_f32(int type_id, const uint8_t *host_weight, size_t wei
                              size_t in_len, size_t input_size, size_t row_count, size_t column_count,
                              float *host_out, size_t out_len);
 
+/* Dequantized matmul: every weight row is dequantized bit-exactly and
+ * multiplied by each input column with the reference's sequential f32 sum
+ * (sum = fround(sum + fround(w * x)) in index order), so outputs equal
+ * hp_matmul_dequantized_f32 (lib.rs:103-154) bit for bit.  The reference
+ * calls it through matMulDequantizedWasm (wasm-kernels.ts:468-520) for the
+ * MTP draft head (runner/wasm/mtp-assistant-runner.ts:156-180).  Same
+ * validation order and codes as the WASM export.  One-shot on HOST buffers
+ * (upload, multiply, download, release; synchronous): */
+int hpc_matmul_dequantized_f32(int type_id, const uint8_t *host_weight, size_t weight_len, const float *host_in,
+                               size_t in_len, size_t input_size, size_t row_count, size_t column_count,
+                               float *host_out, size_t out_len);
+
+/* Same arithmetic on a resident weight and device buffers, stream-ordered. */
+int hpc_matmul_dequantized_prepared_f32(hpc_weight handle, const float *d_in, size_t in_len, size_t input_size,
+                                        size_t row_count, size_t column_count, float *d_out, size_t out_len,
+                                        void *stream);
+
 /* ---- caller-provided scratch ("workspace") variants ----------------------
  * The activation is quantized once into a workspace the caller allocates
  * (no allocation inside the call, so these can be captured in a CUDA graph),
@@ -253,17 +270,6 @@ int hpc_model_set_weight(hpc_model model, int layer, int slot, hpc_weight weight
 int hpc_model_set_norm(hpc_model model, int layer, int slot, const float *host_values, size_t len);
 /* token_embd.weight == output weight (tied): rows are vocabulary ids. */
 int hpc_model_set_lm_head(hpc_model model, hpc_weight weight);
-/* Selects how a single-token step runs: enable != 0 uses the persistent
- * step kernel -- all layers in one cooperative launch, weights streamed
- * through shared-memory rings -- when the model's shapes allow it (hidden
- * 2048); 0 (the default) runs the per-kernel step.  Multi-token steps always
- * run per kernel. */
-int hpc_model_set_persistent(hpc_model model, int enable);
-
-/* 1 if the last built step for `token_count` tokens is the persistent kernel,
- * else 0 (valid after a forward of that token count). */
-int hpc_model_step_kind(hpc_model model, size_t token_count, int *out_kind);
-
 /* Device pointers of one KV layer's cache, f32: K [context][kv_heads][head_dim]
  * (the layers.ts:887-911 layout) and V [context][kv_heads][head_dim] -- V is
  * token-major like K, the transpose of the reference's [head_dim][kv_heads]

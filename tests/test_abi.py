@@ -39,6 +39,12 @@ def test_shape_errors_precede_device_work():
     assert L.hpc_matmul_quantized_f32(1, vp(w), 143, vp(x), 256, 256, 1, 1, vp(o), 1) == kernels.ERR_SHAPE
     # input size not a multiple of 256 for a K-quant -> ERR_TYPE (row_bytes is None)
     assert L.hpc_matmul_quantized_f32(1, vp(w), 144, vp(x), 200, 200, 1, 1, vp(o), 1) == kernels.ERR_TYPE
+    # the dequantized matmul answers in the order of hp_matmul_dequantized_f32 (lib.rs:115-125)
+    assert L.hpc_matmul_dequantized_f32(1, vp(w), 144, vp(x), 255, 256, 1, 1, vp(o), 1) == kernels.ERR_SHAPE
+    assert L.hpc_matmul_dequantized_f32(42, vp(w), 144, vp(x), 256, 256, 1, 1, vp(o), 1) == kernels.ERR_TYPE
+    assert L.hpc_matmul_dequantized_f32(3, vp(w), 144, vp(x), 256, 256, 1, 1, vp(o), 1) == kernels.ERR_SHAPE
+    assert L.hpc_matmul_dequantized_prepared_f32(None, None, 5, 256, 4, 1, None, 4, None) == kernels.ERR_SHAPE
+    assert L.hpc_matmul_dequantized_prepared_f32(None, None, 256, 256, 4, 1, None, 4, None) == kernels.ERR_ARG
     h = C.c_void_p()
     assert L.hpc_weight_upload(5, vp(w), 34, 32, 1, C.byref(h)) == kernels.ERR_TYPE  # Q8_0 is not resident
     assert L.hpc_weight_upload(1, vp(w), 100, 256, 1, C.byref(h)) == kernels.ERR_SHAPE

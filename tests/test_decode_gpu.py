@@ -106,6 +106,25 @@ def test_verify_widths_match_oracle(m):
         gpu.close()
 
 
+@pytest.mark.parametrize("kv_heads,m", [(1, 1), (1, 5), (1, 8), (8, 5), (8, 7)])
+def test_group_sizes_match_oracle(kv_heads, m):
+    # Query vectors per KV head (m * heads / kv_heads) outside the sized wide
+    # forms {8, 12, ..., 32} run the general wide attention form: 40 and 64
+    # (8 query heads per KV head at widths 5 and 8) and 5 and 7 (one query
+    # head per KV head); 8 at width 1 runs a sized form.
+    k = 40
+    shape = replace(SMALL, kv_heads=kv_heads)
+    gpu, ref = _build(shape, filled=40, seed=13 + m + kv_heads)
+    try:
+        toks = [(29 + 411 * i) % shape.vocab for i in range(m)]
+        pos = list(range(40, 40 + m))
+        ids_g, vals_g, hid_g = gpu.forward(toks, pos, k, return_hidden=True)
+        ids_r, vals_r, hid_r, logits_r = ref.forward(toks, pos, k)
+        _check_step(ids_g.cpu().numpy(), vals_g.cpu().numpy(), hid_g.cpu().numpy(), ids_r, vals_r, hid_r, logits_r, k)
+    finally:
+        gpu.close()
+
+
 def test_verify_equals_sequential_decodes():
     # A batched verify over positions p..p+4 must equal five single-token
     # decodes (the causal mask makes them the same computation).
@@ -146,57 +165,3 @@ def test_small_greedy_64_steps():
     finally:
         gpu.close()
     print("greedy flips (step, gpu, ref, margin):", flips)
-
-
-def test_persistent_step_matches_per_kernel_step_and_oracle():
-    # The single-token step can run as one persistent kernel; the per-kernel
-    # chain is the other implementation of the same forward.
-    k = 40
-    gpu, ref = _build(SMALL, filled=40)
-    try:
-        gpu.set_persistent(True)
-        ids_p, vals_p, hid_p = gpu.forward([17], [40], k, return_hidden=True)
-        assert gpu.step_kind(1) == 1, "the persistent step did not run"
-        gpu.set_persistent(False)
-        ids_k, vals_k, hid_k = gpu.forward([17], [40], k, return_hidden=True)
-        assert gpu.step_kind(1) == 0
-        ids_r, vals_r, hid_r, logits_r = ref.forward([17], [40], k)
-        for ids_g, vals_g, hid_g in ((ids_p, vals_p, hid_p), (ids_k, vals_k, hid_k)):
-            _check_step(ids_g.cpu().numpy(), vals_g.cpu().numpy(), hid_g.cpu().numpy(), ids_r, vals_r, hid_r,
-                        logits_r, k)
-    finally:
-        gpu.close()
-
-
-def _paths_agree(ids_a, vals_a, hid_a, ids_b, vals_b, hid_b):
-    hid_a, hid_b = hid_a.astype(np.float64), hid_b.astype(np.float64)
-    scale = np.sqrt(np.mean(hid_b ** 2, axis=1, keepdims=True))
-    err = np.abs(hid_a - hid_b)
-    assert np.all(err <= 1e-3 * (np.abs(hid_b) + scale)), f"hidden max err {err.max():.3g}"
-    assert np.all(np.abs(vals_a - vals_b) <= _logit_tol(vals_b))
-    for i in range(ids_a.shape[0]):
-        if ids_a[i, 0] != ids_b[i, 0]:
-            assert abs(vals_b[i, 0] - vals_b[i, 1]) <= _logit_tol(vals_b[i, 0]), f"top-1 {ids_a[i, 0]} vs {ids_b[i, 0]}"
-
-
-def test_persistent_step_config3_matches_per_kernel_step():
-    # Full BASELINE config-3 shape (35 layers, Q6_K attn_v / ffn_down on
-    # alternate layers, 15 shared-KV layers, context 4096): the persistent
-    # step and the per-kernel step agree, at the last position and at a short
-    # context.
-    m = CudaDecoderModel(CONFIG3, max_tokens=8, top_k=64)
-    try:
-        m.load_gpu_synthetic(seed=1)
-        for position in (4095, 100):
-            m.set_persistent(True)
-            m.fill_kv_random(position, seed=3)
-            ids_p, vals_p, hid_p = m.forward([12345], [position], 40, return_hidden=True)
-            assert m.step_kind(1) == 1
-            m.set_persistent(False)
-            m.fill_kv_random(position, seed=3)
-            ids_k, vals_k, hid_k = m.forward([12345], [position], 40, return_hidden=True)
-            _paths_agree(ids_p.cpu().numpy(), vals_p.cpu().numpy(), hid_p.cpu().numpy(), ids_k.cpu().numpy(),
-                         vals_k.cpu().numpy(), hid_k.cpu().numpy())
-        hk.device_error()
-    finally:
-        m.close()

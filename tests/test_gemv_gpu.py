@@ -183,3 +183,22 @@ def test_repeated_calls_are_deterministic():
         assert torch.equal(a, b)
     finally:
         hk.release_quantized_weight_handle(h)
+
+
+@pytest.mark.parametrize("type_id,k,rows,cols", [(syn.Q4_K, 2048, 512, 3), (syn.Q6_K, 2048, 300, 1),
+                                                 (syn.Q6_K, 16384, 64, 2), (syn.Q4_K, 256, 33, 9)])
+def test_matmul_dequantized_bit_exact(oracle, type_id, k, rows, cols):
+    # hp_matmul_dequantized_f32 (lib.rs:103-154): bit-exact dequantized rows,
+    # one sequential f32 chain per (row, column) -- equal to the oracle bit for
+    # bit, through the one-shot host entry point and the resident one.
+    w = syn.quant_weight(type_id, rows, k, seed=31 + rows)
+    x = syn.activations(cols, k, seed=32 + cols)
+    ref = oracle.matmul_dequantized(type_id, w, x, k, rows, cols)
+    got = hk.mat_mul_dequantized(TNAME[type_id], w, x, k, rows, cols)
+    assert np.array_equal(got.view(np.uint32), ref.astype(np.float32).view(np.uint32))
+    h = hk.create_quantized_weight_handle(TNAME[type_id], w, k, rows)
+    try:
+        res = hk.mat_mul_dequantized_resident(h, torch.from_numpy(x).cuda(), k, rows, cols).cpu().numpy()
+    finally:
+        hk.release_quantized_weight_handle(h)
+    assert np.array_equal(res.view(np.uint32), ref.astype(np.float32).view(np.uint32))

@@ -5,7 +5,8 @@
     (oracle/decoder_oracle.py `layer`, the WASM provider's forward for n
     positions with the causal mask), at n = 40 (tensor-core matmuls), n = 7
     (GEMV), n = 200 over a 256-token context (the attention's key window
-    split in two) and n = 60 after a 100-token prefix already in the cache.
+    split in two), n = 60 after a 100-token prefix already in the cache, and
+    n = 40 with 8 query heads per KV head (the unsplit attention form).
     K/V cache rows of the first KV layer: within 1e-3 (|ref| + rms(ref)).
     Final residual: every token within 3e-2, and at least 90% of tokens
     within 1e-3 of that scale; K/V rows of deeper layers the same with 6e-2.
@@ -63,12 +64,14 @@ def _close_tokens(got, ref, what, bound=3e-2, within=0.9):
     assert (worst <= 1e-3).mean() >= within, f"{what}: {(worst > 1e-3).sum()} of {len(worst)} tokens beyond 1e-3"
 
 
-@pytest.mark.parametrize("n,context,start", [(40, 128, 0), (7, 128, 0),
-                                             (200, 256, 0),     # two 128-key splits per late query tile
-                                             (60, 256, 100)])   # continuing after a 100-token prefix
-def test_prefill_matches_oracle(n, context, start):
+@pytest.mark.parametrize("n,context,start,kv_heads", [(40, 128, 0, 2), (7, 128, 0, 2),
+                                                      (200, 256, 0, 2),    # two 128-key splits per late query tile
+                                                      (60, 256, 100, 2),   # continuing after a 100-token prefix
+                                                      (40, 128, 0, 1)])    # 8 query heads per KV head: unsplit form
+def test_prefill_matches_oracle(n, context, start, kv_heads):
     from oracle.decoder_oracle import OracleDecoder
-    shape = replace(SHAPE, context=context)
+    shape = replace(SHAPE, context=context, kv_heads=kv_heads)
+    nkv = shape.kv_heads
     w = SyntheticWeights(shape, seed=21)
     gpu = CudaDecoderModel(shape, max_tokens=8, top_k=64)
     try:
@@ -76,11 +79,11 @@ def test_prefill_matches_oracle(n, context, start):
         ref = OracleDecoder(shape, w)
         g = np.random.default_rng(n + start)
         for kl in range(shape.kv_layers):
-            kc = np.zeros((context, 2, 256), np.float32)
-            vc = np.zeros((256, 2, context), np.float32)
+            kc = np.zeros((context, nkv, 256), np.float32)
+            vc = np.zeros((256, nkv, context), np.float32)
             if start:  # an existing prefix in the cache
-                kc[:start] = g.standard_normal((start, 2, 256))
-                vc[:, :, :start] = g.standard_normal((256, 2, start))
+                kc[:start] = g.standard_normal((start, nkv, 256))
+                vc[:, :, :start] = g.standard_normal((256, nkv, start))
             ref.set_kv(kl, kc.copy(), vc.copy())
             gk, gv = gpu.kv(kl)
             gk.copy_(torch.from_numpy(kc))

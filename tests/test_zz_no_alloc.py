@@ -4,7 +4,8 @@ C-ABI.  Two calls in a row on different inputs each match the allocating
 entry point (ids exactly, values within rtol 1e-3 / atol 1e-4), so what a
 call leaves in the shared scratch does not leak into the next one.  A call
 whose scratch exceeds HPC_NOALLOC_SCRATCH_BYTES is refused with
-HPC_ERR_SHAPE before any launch.  Collected last (file name) and
+HPC_ERR_SHAPE before any launch, and the widest call that still fits
+matches the allocating entry point.  Collected last (file name) and
 independent of the other test files' state.
 """
 import ctypes as C
@@ -57,32 +58,40 @@ def test_noalloc_matches_allocating_entry_point_twice_in_a_row(env):
         hk.release_quantized_weight_handle(head)
 
 
-def test_noalloc_refuses_scratch_beyond_its_size(env):
+def test_noalloc_at_its_size_limit(env):
+    # The widest call that still fits the static scratch (Q8_K records plus
+    # candidate lists within a column of HPC_NOALLOC_SCRATCH_BYTES) matches
+    # the allocating entry point, so the carve near the array's upper end is
+    # right; one column more is refused with HPC_ERR_SHAPE before any launch.
     torch, hk, L = env
     kdim, rows, k = 256, 65536, 64
     head = hk.create_quantized_weight_handle("Q6_K", syn.q6_k_weight(rows, kdim, seed=7), kdim, rows)
     try:
         need = C.c_size_t()
 
-        def cand(cols):
+        def scratch(cols):
             assert L.hpc_lm_head_candidates_bytes(head.handle, cols, k, C.byref(need)) == 0
-            return need.value
+            cand = need.value
+            assert L.hpc_q8_workspace_bytes(kdim, cols, C.byref(need)) == 0
+            return need.value + cand
 
-        big = 1
-        while cand(big) <= SCRATCH_BYTES:  # the first column count whose candidates alone exceed the scratch
-            big += 1
-        for cols, fits in ((big // 2, True), (big, False)):
-            x = torch.from_numpy(syn.activations(cols, kdim, seed=cols)).cuda()
-            ids = torch.empty(cols * k, dtype=torch.int32, device="cuda")
-            vals = torch.empty(cols * k, device="cuda")
-            rc = L.hpc_lm_head_topk_noalloc(head.handle, C.c_void_p(x.data_ptr()), x.numel(), kdim, cols, k, 0,
-                                            C.c_float(0.0), C.c_void_p(ids.data_ptr()), C.c_void_p(vals.data_ptr()),
-                                            None)
-            if fits:
-                assert rc == 0, L.hpc_last_error()
-            else:
-                assert rc == hk.ERR_SHAPE
-                assert b"static" in L.hpc_last_error()
+        fit = 1
+        while scratch(fit + 1) <= SCRATCH_BYTES:
+            fit += 1
+        assert scratch(fit) > SCRATCH_BYTES - scratch(fit) / fit * 2, "the fitting call is not near the limit"
+        x = torch.from_numpy(syn.activations(fit, kdim, seed=fit)).cuda()
+        ids, vals = _call(L, "hpc_lm_head_topk_noalloc", torch, head, x, fit, k, 0.0)
+        rids, rvals = _call(L, "hpc_lm_head_topk", torch, head, x, fit, k, 0.0)
+        assert np.array_equal(ids, rids)
+        assert np.all(np.abs(vals.astype(np.float64) - rvals) <= 1e-4 + 1e-3 * np.abs(rvals))
+        cols = fit + 1
+        x = torch.from_numpy(syn.activations(cols, kdim, seed=cols)).cuda()
+        ids = torch.empty(cols * k, dtype=torch.int32, device="cuda")
+        vals = torch.empty(cols * k, device="cuda")
+        rc = L.hpc_lm_head_topk_noalloc(head.handle, C.c_void_p(x.data_ptr()), x.numel(), kdim, cols, k, 0,
+                                        C.c_float(0.0), C.c_void_p(ids.data_ptr()), C.c_void_p(vals.data_ptr()), None)
+        assert rc == hk.ERR_SHAPE
+        assert b"static" in L.hpc_last_error()
         torch.cuda.synchronize()
     finally:
         hk.release_quantized_weight_handle(head)
