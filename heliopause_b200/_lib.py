@@ -23,6 +23,7 @@ SIGNATURES = {
     "hpc_version": (_i, []),
     "hpc_device_init": (_i, [_i]),
     "hpc_device_error": (_i, []),
+    "hpc_set_matmul_order": (_i, [_i]),
     "hpc_weight_upload": (_i, [_i, _vp, _sz, _sz, _sz, C.POINTER(_vp)]),
     "hpc_weight_upload_device": (_i, [_i, _vp, _sz, _sz, _sz, _vp, C.POINTER(_vp)]),
     "hpc_weight_release": (_i, [_vp]),
@@ -48,6 +49,7 @@ SIGNATURES = {
     "hpc_model_set_weight": (_i, [_vp, _i, _i, _vp]),
     "hpc_model_set_norm": (_i, [_vp, _i, _i, _vp, _sz]),
     "hpc_model_set_lm_head": (_i, [_vp, _vp]),
+    "hpc_model_set_exact": (_i, [_vp, _i]),
     "hpc_model_kv": (_i, [_vp, _i, C.POINTER(_vp), C.POINTER(_vp)]),
     "hpc_model_forward": (_i, [_vp, _vp, _vp, _sz, _sz, _vp, _vp, _vp, _vp]),
     "hpc_model_prefill": (_i, [_vp, _vp, _vp, _sz, _vp, _vp]),

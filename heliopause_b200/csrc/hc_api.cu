@@ -9,6 +9,8 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstdlib>
+#include <algorithm>
+#include <atomic>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -83,6 +85,10 @@ int* device_status_word() {
   return ptrs[dev];
 }
 }  // namespace hc
+
+// Order of the public matmul / LM-head entry points (hpc_set_matmul_order):
+// true = the reference's f32 order (the default), false = the reordered kernels.
+static std::atomic<bool> g_exact_order{true};
 
 extern "C" {
 
@@ -231,10 +237,40 @@ static int gemv_mma_min_cols() {
   return v;
 }
 
-// GEMV launches over an already-quantized workspace: one launch per group of
-// up to 8 columns, covering all segments.
+// Exact-order launches (hc_gemvx.cu): one per group of up to 8 columns.
+static int launch_gemvx_ws(const hc::Q8Buf& q, int K, int cols, const hc::GemvSeg* segs, int nseg, int total_tiles,
+                           cudaStream_t st) {
+  hc::GemvxParams p;
+  memset(&p, 0, sizeof p);
+  for (int i = 0; i < nseg; ++i) p.seg[i] = segs[i];
+  p.nseg = nseg;
+  p.K = K;
+  p.nb = K / 256;
+  p.total_tiles = total_tiles;
+  p.q = q;
+  // widest column groups whose products fit a CTA's shared memory
+  int group = hc::GEMVX_MAX_COLS;
+  for (; group > 1; group >>= 1) {
+    hc::GemvxParams t = p;
+    t.ncols = cols < group ? cols : group;
+    if (hc::gemvx_plan(t, hc::sm_count()) > 0) break;
+  }
+  for (int c0 = 0; c0 < cols; c0 += group) {
+    p.col0 = c0;
+    p.ncols = cols - c0 < group ? cols - c0 : group;
+    HPC_CK(hc::launch_gemvx(p, st), "exact-order gemv launch");
+  }
+  return HPC_OK;
+}
+
+// GEMV launches over an already-quantized workspace.  Fewer than TC_MIN_COLS
+// columns: `exact` selects the reference-order kernel (hc_gemvx.cu), else the
+// dp4a GEMV (1-2 columns per launch, optionally with the fused norm prologue)
+// or the tensor-core GEMV (3-8), one launch per group of up to 8 columns
+// covering all segments.  TC_MIN_COLS or more: the tensor-core matmul.
 static int launch_gemv_ws(const hc::Q8Buf& q, int K, int cols, const hc::GemvSeg* segs, int nseg, int total_tiles,
-                          cudaStream_t st, const hc::GemvPrologue* pro = nullptr) {
+                          cudaStream_t st, const hc::GemvPrologue* pro, bool exact) {
+  if (exact && !pro && cols < hc::TC_MIN_COLS) return launch_gemvx_ws(q, K, cols, segs, nseg, total_tiles, st);
   hc::GemvParams p;
   memset(&p, 0, sizeof p);
   if (pro) p.pro = *pro;
@@ -270,7 +306,8 @@ static int run_gemv(const float* d_in, int K, int cols, const hc::GemvSeg* segs,
   HPC_CK(cudaMallocAsync(&ws, hc::q8buf_bytes(K, cols), st), "cudaMallocAsync(q8)");
   hc::Q8Buf q = hc::q8buf_carve(ws, K, cols);
   cudaError_t e = hc::launch_q8k_quantize(d_in, K, cols, q, nullptr, nullptr, nullptr, st);
-  int rc = e == cudaSuccess ? launch_gemv_ws(q, K, cols, segs, nseg, total_tiles, st) : cuda_fail(e, "quantize launch");
+  int rc = e == cudaSuccess ? launch_gemv_ws(q, K, cols, segs, nseg, total_tiles, st, nullptr, g_exact_order.load())
+                            : cuda_fail(e, "quantize launch");
   cudaError_t e2 = cudaFreeAsync(ws, st);
   if (rc != HPC_OK) return rc;
   if (e2 != cudaSuccess) return cuda_fail(e2, "cudaFreeAsync(q8)");
@@ -446,6 +483,20 @@ int hpc_q8_quantize(const float* d_in, size_t in_len, size_t input_size, size_t 
 
 int hpc_matmul_q8(size_t count, const hpc_weight* handles, const void* d_workspace, size_t workspace_bytes,
                   size_t input_size, size_t column_count, float* const* d_outs, const size_t* out_lens, void* stream) {
+  return hc_matmul_q8_order(count, handles, d_workspace, workspace_bytes, input_size, column_count, d_outs, out_lens,
+                            g_exact_order.load(), static_cast<cudaStream_t>(stream));
+}
+
+int hpc_set_matmul_order(int exact) {
+  g_exact_order.store(exact != 0);
+  return HPC_OK;
+}
+
+}  // extern "C"
+
+int hc_matmul_q8_order(size_t count, const hpc_weight* handles, const void* d_workspace, size_t workspace_bytes,
+                       size_t input_size, size_t column_count, float* const* d_outs, const size_t* out_lens,
+                       bool exact, cudaStream_t stream) {
   if (count == 0 || count > size_t(hc::GEMV_MAXSEG)) return fail(HPC_ERR_SHAPE, "matmul_q8: count %zu", count);
   if (!handles || !d_outs || !out_lens) return fail(HPC_ERR_ARG, "null pointer");
   if (input_size == 0 || input_size % 256 || column_count > (size_t(1) << 20))
@@ -459,11 +510,8 @@ int hpc_matmul_q8(size_t count, const hpc_weight* handles, const void* d_workspa
   if (rc != HPC_OK) return rc;
   if (column_count == 0) return HPC_OK;
   hc::Q8Buf q = hc::q8buf_carve(const_cast<void*>(d_workspace), int(input_size), int(column_count));
-  return launch_gemv_ws(q, int(input_size), int(column_count), segs, int(count), tiles,
-                        static_cast<cudaStream_t>(stream));
+  return launch_gemv_ws(q, int(input_size), int(column_count), segs, int(count), tiles, stream, nullptr, exact);
 }
-
-}  // extern "C"
 
 // hpc_matmul_q8 whose input is computed by the fused norm prologue of every
 // CTA (hc_kernels.cuh GemvPrologue) instead of read from Q8_K records: the
@@ -481,7 +529,7 @@ int hc_matmul_q8_prologue(size_t count, const hpc_weight* handles, const void* q
   int rc = build_segments(count, handles, d_outs, out_lens, input_size, column_count, segs, &tiles);
   if (rc != HPC_OK) return rc;
   hc::Q8Buf q = hc::q8buf_carve(const_cast<void*>(q8ws), int(input_size), int(column_count));
-  return launch_gemv_ws(q, int(input_size), int(column_count), segs, int(count), tiles, st, &pro);
+  return launch_gemv_ws(q, int(input_size), int(column_count), segs, int(count), tiles, st, &pro, false);
 }
 
 extern "C" {
@@ -509,11 +557,23 @@ static size_t tc_logits_bytes(hpc_weight h, size_t cols) { return (cols * h->row
 // one list per CTA of its persistent grid.
 static bool lm_head_mma(size_t cols) { return cols >= size_t(gemv_mma_min_cols()) && cols <= 8; }
 
+// Logits path (tensor-core matmul at TC_MIN_COLS+ columns, the exact-order
+// GEMV at 3..TC_MIN_COLS-1): the logits [col][rows] (256-byte aligned), then
+// one candidate list per 2,048-row chunk and column.
+static size_t logits_path_bytes(hpc_weight h, size_t cols, size_t k) {
+  return tc_logits_bytes(h, cols) + tc_chunks(h) * k * cols * sizeof(uint64_t);
+}
+
+// Candidate bytes for `cols` columns: enough for every path the width may
+// take in either order (the model's reordered step and the exact one share
+// one buffer).
 static size_t cand_bytes_for(hpc_weight h, size_t cols, size_t k) {
-  if (cols >= size_t(hc::TC_MIN_COLS)) return tc_logits_bytes(h, cols) + tc_chunks(h) * k * cols * sizeof(uint64_t);
+  if (cols >= size_t(hc::TC_MIN_COLS)) return logits_path_bytes(h, cols, k);
   const int tiles = int(h->rows_pad / hc::TILE);
-  if (lm_head_mma(cols)) return size_t(hc::lmhead_mma_grid(tiles)) * k * cols * sizeof(uint64_t);
-  return size_t(hc::lmhead_grid(tiles)) * hc::LMHEAD_LISTS * k * cols * sizeof(uint64_t);
+  size_t b = size_t(hc::lmhead_grid(tiles)) * hc::LMHEAD_LISTS * k * cols * sizeof(uint64_t);
+  if (lm_head_mma(cols)) b = std::max(b, size_t(hc::lmhead_mma_grid(tiles)) * k * cols * sizeof(uint64_t));
+  if (cols >= 3) b = std::max(b, logits_path_bytes(h, cols, k));
+  return b;
 }
 
 int hpc_lm_head_candidates_bytes(hpc_weight h, size_t column_count, size_t k, size_t* out_bytes) {
@@ -527,18 +587,35 @@ int hpc_lm_head_candidates_bytes(hpc_weight h, size_t column_count, size_t k, si
 int hpc_lm_head_topk_q8(hpc_weight h, const void* d_workspace, size_t workspace_bytes, size_t input_size,
                         size_t column_count, size_t k, int32_t id_offset, void* d_candidates, size_t candidates_bytes,
                         float softcap, int32_t* d_ids, float* d_vals, uint64_t* d_keys, void* stream) {
+  return hc_lm_head_topk_q8_order(h, d_workspace, workspace_bytes, input_size, column_count, k, id_offset,
+                                  d_candidates, candidates_bytes, softcap, d_ids, d_vals, d_keys, g_exact_order.load(),
+                                  static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"
+
+size_t hc_lm_head_fused_candidates_bytes(hpc_weight h, size_t cols, size_t k) {
+  return size_t(hc::lmhead_grid(int(h->rows_pad / hc::TILE))) * hc::LMHEAD_LISTS * k * cols * sizeof(uint64_t);
+}
+
+int hc_lm_head_topk_q8_order(hpc_weight h, const void* d_workspace, size_t workspace_bytes, size_t input_size,
+                             size_t column_count, size_t k, int32_t id_offset, void* d_candidates,
+                             size_t candidates_bytes, float softcap, int32_t* d_ids, float* d_vals, uint64_t* d_keys,
+                             bool exact, cudaStream_t st, bool fused_only) {
   int rc = lm_head_check(h, input_size, column_count, k);
   if (rc != HPC_OK) return rc;
   if (column_count == 0) return HPC_OK;
   if (!d_workspace || !d_candidates || !d_ids || !d_vals) return fail(HPC_ERR_ARG, "null pointer");
   if (workspace_bytes < hc::q8buf_bytes(int(input_size), int(column_count)))
     return fail(HPC_ERR_SHAPE, "workspace too small: %zu bytes", workspace_bytes);
-  if (candidates_bytes < cand_bytes_for(h, column_count, k))
-    return fail(HPC_ERR_SHAPE, "candidate buffer too small: %zu bytes", candidates_bytes);
+  const size_t need = fused_only ? hc_lm_head_fused_candidates_bytes(h, column_count, k)
+                                 : cand_bytes_for(h, column_count, k);
+  if (candidates_bytes < need) return fail(HPC_ERR_SHAPE, "candidate buffer too small: %zu bytes", candidates_bytes);
   if (id_offset < 0 || size_t(id_offset) + h->row_count > size_t(INT32_MAX)) return fail(HPC_ERR_SHAPE, "id offset");
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (column_count >= size_t(hc::TC_MIN_COLS)) {
-    // tensor-core logits, chunked candidate lists, then the same merge
+  if (fused_only) exact = true;
+  if (!fused_only && (column_count >= size_t(hc::TC_MIN_COLS) || (exact && column_count >= 3))) {
+    // the logits (tensor-core matmul, or the exact-order GEMV), chunked
+    // candidate lists, then the same merge
     float* logits = static_cast<float*>(d_candidates);
     uint64_t* cand = reinterpret_cast<uint64_t*>(static_cast<char*>(d_candidates) + tc_logits_bytes(h, column_count));
     hc::GemvSeg seg;
@@ -547,8 +624,14 @@ int hpc_lm_head_topk_q8(hpc_weight h, const void* d_workspace, size_t workspace_
     seg.out = logits;
     seg.type = h->type;
     seg.rows = int(h->row_count);
+    seg.tile_begin = 0;
     const hc::Q8Buf q = hc::q8buf_carve(const_cast<void*>(d_workspace), int(input_size), int(column_count));
-    HPC_CK(hc::launch_gemm_tc(seg, int(input_size / 256), q, 0, int(column_count), st), "tensor-core LM head");
+    if (column_count >= size_t(hc::TC_MIN_COLS)) {
+      HPC_CK(hc::launch_gemm_tc(seg, int(input_size / 256), q, 0, int(column_count), st), "tensor-core LM head");
+    } else {
+      rc = launch_gemvx_ws(q, int(input_size), int(column_count), &seg, 1, int(h->rows_pad / hc::TILE), st);
+      if (rc != HPC_OK) return rc;
+    }
     const size_t col_stride = tc_chunks(h) * k;
     HPC_CK(hc::launch_logits_topk(logits, int(h->row_count), int(column_count), int(k), id_offset, cand, col_stride,
                                   st),
@@ -580,7 +663,7 @@ int hpc_lm_head_topk_q8(hpc_weight h, const void* d_workspace, size_t workspace_
   P.id_offset = id_offset;
   P.cand = static_cast<uint64_t*>(d_candidates);
   const int cols = int(column_count);
-  if (lm_head_mma(column_count)) {
+  if (!exact && !fused_only && lm_head_mma(column_count)) {
     const int mgrid = hc::lmhead_mma_grid(tiles);
     P.cand_col_stride = size_t(mgrid) * k;
     P.g.col0 = 0;
@@ -592,9 +675,12 @@ int hpc_lm_head_topk_q8(hpc_weight h, const void* d_workspace, size_t workspace_
     return HPC_OK;
   }
   P.cand_col_stride = size_t(grid) * hc::LMHEAD_LISTS * k;
-  for (int c0 = 0; c0 < cols; c0 += 8) {
+  // exact order: passes of at most 2 columns (the kernel's exact lane
+  // accumulators of wider passes would not fit its registers)
+  const int group = exact ? 2 : 8;
+  for (int c0 = 0; c0 < cols; c0 += group) {
     P.g.col0 = c0;
-    P.g.ncols = cols - c0 < 8 ? cols - c0 : 8;
+    P.g.ncols = cols - c0 < group ? cols - c0 : group;
     HPC_CK(hc::launch_lmhead_topk(P, grid, st), "lm head launch");
   }
   const int n = grid * hc::LMHEAD_LISTS * int(k);
@@ -603,6 +689,8 @@ int hpc_lm_head_topk_q8(hpc_weight h, const void* d_workspace, size_t workspace_
          "top-k merge launch");
   return HPC_OK;
 }
+
+extern "C" {
 
 int hpc_lm_head_topk(hpc_weight h, const float* d_hidden, size_t hidden_len, size_t input_size, size_t column_count,
                      size_t k, int32_t id_offset, float softcap, int32_t* d_ids, float* d_vals, void* stream) {

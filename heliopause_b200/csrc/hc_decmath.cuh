@@ -1,7 +1,7 @@
 // hc_decmath.cuh -- device arithmetic of the decoder layer math shared by the
-// per-kernel decode step (hc_decode.cu) and the persistent step kernel
-// (hc_persist.cu): programmatic-dependent-launch controls, the two f16
-// codecs of the reference, f64 reductions and the GEGLU activation.  Every
+// decode-step kernels (hc_decode.cu, hc_attx.cu): programmatic-dependent-launch
+// controls, the two f16 codecs of the reference, f64 reductions, the
+// per-head QK-norm + RoPE and the GEGLU activation.  Every
 // rounding point follows packages/engine/src/runner/wasm/layers.ts and
 // packages/engine/wasm-kernels/src/lib.rs as cited per function.
 #pragma once
@@ -84,6 +84,54 @@ __device__ __forceinline__ double block_sum_d(double v, double* scratch, int war
   double t = 0.0;
   for (int w = 0; w < warps; ++w) t += scratch[w];
   return t;
+}
+
+// One warp: QK-norm (f64 sum of squares, layers.ts:871-885 normHeads) of a
+// 256-vector held 8 values per lane (lane L: dimensions 8L..8L+7), optional
+// weight w (preloaded, same layout), optional NeoX RoPE (layers.ts:990-1033;
+// pair (i, i+128) sits in lanes L and L+16) with the lane's eight cos/sin
+// entries c8/s8 (pair indices (L mod 16)*8 .. +7); products rounded to f32
+// as in the reference.
+__device__ __forceinline__ void head_norm_rope(float (&x)[8], const float (&w)[8], bool has_w, bool rope,
+                                               const double (&c8)[8], const double (&s8)[8], double eps, int lane) {
+  double ss = 0.0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) ss += double(x[i]) * double(x[i]);
+  ss = warp_sum_d(ss);
+  const double sc = 1.0 / sqrt(ss / 256.0 + eps);
+  if (!has_w) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) x[i] = float(double(x[i]) * sc);
+    return;
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) x[i] = float((double(x[i]) * sc) * double(w[i]));
+  if (!rope) return;
+  float partner[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) partner[i] = __shfl_xor_sync(0xffffffffu, x[i], 16);
+  const bool first = lane < 16;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const double x0 = first ? x[i] : partner[i];
+    const double x1 = first ? partner[i] : x[i];
+    x[i] = first ? float(x0 * c8[i]) - float(x1 * s8[i]) : float(x0 * s8[i]) + float(x1 * c8[i]);
+  }
+}
+
+// The lane's eight cos and sin entries of one token's row of the RoPE tables.
+__device__ __forceinline__ void load_rope8(const double* cos_row, const double* sin_row, int lane, double (&c8)[8],
+                                           double (&s8)[8]) {
+  const double2* c = reinterpret_cast<const double2*>(cos_row + (lane & 15) * 8);
+  const double2* sn = reinterpret_cast<const double2*>(sin_row + (lane & 15) * 8);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const double2 a = c[i], b = sn[i];
+    c8[2 * i] = a.x;
+    c8[2 * i + 1] = a.y;
+    s8[2 * i] = b.x;
+    s8[2 * i + 1] = b.y;
+  }
 }
 
 // layers.ts:1062-1076 gelu (tanh form) with the TS f16 codec on input and

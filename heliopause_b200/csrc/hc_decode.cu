@@ -38,16 +38,27 @@ namespace hc {
 // ---- RoPE table -------------------------------------------------------------------
 
 // cos/sin of the NeoX RoPE angles for each token (layers.ts:1012-1030):
-// theta_0 = position, theta_{i+1} = fround(theta_i * base^(-2/ndims)); the
-// chain is serial (one thread), the cos/sin are parallel.  One CTA per token.
-__global__ void hc_rope_table_kernel(const int32_t* __restrict__ pos, int half, double theta_scale,
-                                  double* __restrict__ cos_t, double* __restrict__ sin_t) {
+// theta_0 = position, theta_{i+1} = fround(theta_i * base^(-2/ndims)), cos
+// and sin in f64.  The rows come from a table computed once on the host with
+// the C library's cos/sin (the functions the reference's Math.cos/Math.sin
+// stand for); a position past the table is computed here instead (the theta
+// chain serially by one thread, the cos/sin in parallel).  One CTA per token.
+__global__ void hc_rope_gather_kernel(const int32_t* __restrict__ pos, int half, const double* __restrict__ cos_tab,
+                                      const double* __restrict__ sin_tab, int table_rows, double theta_scale,
+                                      double* __restrict__ cos_t, double* __restrict__ sin_t) {
   __shared__ double theta[512];
   pdl_trigger();
   pdl_wait();
-  const int m = blockIdx.x;
+  const int m = blockIdx.x, p = pos[m];
+  if (p >= 0 && p < table_rows) {
+    for (int i = threadIdx.x; i < half; i += blockDim.x) {
+      cos_t[size_t(m) * half + i] = cos_tab[size_t(p) * half + i];
+      sin_t[size_t(m) * half + i] = sin_tab[size_t(p) * half + i];
+    }
+    return;
+  }
   if (threadIdx.x == 0) {
-    double th = double(pos[m]);
+    double th = double(p);
     for (int i = 0; i < half; ++i) {
       theta[i] = th;
       th = double(float(th * theta_scale));
@@ -189,54 +200,6 @@ constexpr int ATT_QBS = 4;                  // general wide form: queries per th
 // threads: its ~155 KB of staged rows and queries hold one CTA per SM, and
 // eight warps there left the scheduler idle (44% issue, latency-bound).
 constexpr int ATT_WIDE_THREADS = 2 * ATT_THREADS;
-
-// One warp: QK-norm (f64 sum of squares, layers.ts:871-885 normHeads) of a
-// 256-vector held 8 values per lane (lane L: dimensions 8L..8L+7), optional
-// weight w (preloaded, same layout), optional NeoX RoPE (layers.ts:990-1033;
-// pair (i, i+128) sits in lanes L and L+16) with the lane's eight cos/sin
-// entries c8/s8 (pair indices (L mod 16)*8 .. +7); products rounded to f32
-// as in the reference.
-__device__ __forceinline__ void head_norm_rope(float (&x)[8], const float (&w)[8], bool has_w, bool rope,
-                                               const double (&c8)[8], const double (&s8)[8], double eps, int lane) {
-  double ss = 0.0;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) ss += double(x[i]) * double(x[i]);
-  ss = warp_sum_d(ss);
-  const double sc = 1.0 / sqrt(ss / 256.0 + eps);
-  if (!has_w) {
-#pragma unroll
-    for (int i = 0; i < 8; ++i) x[i] = float(double(x[i]) * sc);
-    return;
-  }
-#pragma unroll
-  for (int i = 0; i < 8; ++i) x[i] = float((double(x[i]) * sc) * double(w[i]));
-  if (!rope) return;
-  float partner[8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) partner[i] = __shfl_xor_sync(0xffffffffu, x[i], 16);
-  const bool first = lane < 16;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const double x0 = first ? x[i] : partner[i];
-    const double x1 = first ? partner[i] : x[i];
-    x[i] = first ? float(x0 * c8[i]) - float(x1 * s8[i]) : float(x0 * s8[i]) + float(x1 * c8[i]);
-  }
-}
-
-// The lane's eight cos and sin entries of one token's row of the RoPE tables.
-__device__ __forceinline__ void load_rope8(const double* cos_row, const double* sin_row, int lane, double (&c8)[8],
-                                           double (&s8)[8]) {
-  const double2* c = reinterpret_cast<const double2*>(cos_row + (lane & 15) * 8);
-  const double2* sn = reinterpret_cast<const double2*>(sin_row + (lane & 15) * 8);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const double2 a = c[i], b = sn[i];
-    c8[2 * i] = a.x;
-    c8[2 * i + 1] = a.y;
-    s8[2 * i] = b.x;
-    s8[2 * i + 1] = b.y;
-  }
-}
 
 // Wide form: QS query slots per thread in the score pass (ATT_WIDE_THREADS /
 // ATT_CHUNK query lanes) and PB per half of the CTA in the output pass.  The
@@ -964,9 +927,11 @@ static cudaError_t pdl_launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
-cudaError_t launch_rope_table(const int32_t* pos, int M, int half, double theta_scale, double* cos_t, double* sin_t,
-                              cudaStream_t st) {
-  return pdl_launch(hc_rope_table_kernel, dim3(M), dim3(128), 0, st, pos, half, theta_scale, cos_t, sin_t);
+cudaError_t launch_rope_gather(const int32_t* pos, int M, int half, const double* cos_tab, const double* sin_tab,
+                               int table_rows, double theta_scale, double* cos_t, double* sin_t, cudaStream_t st) {
+  if (half > 512) return cudaErrorInvalidValue;
+  return pdl_launch(hc_rope_gather_kernel, dim3(M), dim3(128), 0, st, pos, half, cos_tab, sin_tab, table_rows,
+                    theta_scale, cos_t, sin_t);
 }
 
 cudaError_t launch_embed(const uint8_t* w, int type, int nb, int vocab, const int32_t* ids, float* hidden, int M, int D,

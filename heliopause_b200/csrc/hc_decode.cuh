@@ -7,8 +7,6 @@ namespace hc {
 constexpr int ATT_CHUNK = 64;    // KV tokens per attention CTA (context must be a multiple, <= 4096)
 constexpr int ATT_THREADS = 256;
 
-cudaError_t launch_rope_table(const int32_t* pos, int M, int half, double theta_scale, double* cos_t, double* sin_t,
-                              cudaStream_t st);
 cudaError_t launch_embed(const uint8_t* w, int type, int nb, int vocab, const int32_t* ids, float* hidden, int M, int D,
                          double scale, int* err, cudaStream_t st);
 cudaError_t launch_norm_quant(bool resid, const float* x, float* x_out, const float* y, const float* w_post,
@@ -28,6 +26,21 @@ cudaError_t launch_attention(const float* q, const float* kraw, const float* vra
                              float* part_l, float* part_o, int* err, cudaStream_t st);
 cudaError_t launch_attn_combine(const float* part_m, const float* part_l, const float* part_o, const int32_t* pos,
                                 int M, int H, int KVH, int cap, const Q8Buf& q, float* attn_out, cudaStream_t st);
+// The same attention in the reference's exact f32 order (hc_attx.cu):
+// scores, softmax and the p.v chains over the keys in order, writing the
+// TS-f16-cast output out16 [M][H][256] (the O projection's input before its
+// Q8_K quantization).  scratch: attx_scratch_floats(M, H, cap) floats.
+size_t attx_scores_smem_bytes(int M, int H, int KVH);
+size_t attx_scratch_floats(int M, int H, int cap);
+cudaError_t launch_attention_exact(const float* q, const float* kraw, const float* vraw, const float* qnw,
+                                   const float* knw, const double* cos_t, const double* sin_t, double eps, bool own_kv,
+                                   float* kc, float* vc, const int32_t* pos, int M, int H, int KVH, int cap,
+                                   float scale, float* scratch, float* out16, cudaStream_t st);
+// cos/sin rows of the tokens at `pos` gathered from the model's table
+// [positions][half] (computed on the host, see hc_model.cu); positions at or
+// past table_rows are computed on the device.
+cudaError_t launch_rope_gather(const int32_t* pos, int M, int half, const double* cos_tab, const double* sin_tab,
+                               int table_rows, double theta_scale, double* cos_t, double* sin_t, cudaStream_t st);
 // Launches of at least GEGLU_WIDE_MIN_COLS columns (prefill) take a warp per
 // 256-block; narrower ones a thread per element, which spreads the f64
 // GELU of a decode step over more threads.

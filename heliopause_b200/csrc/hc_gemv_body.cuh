@@ -17,6 +17,7 @@
 #pragma once
 #include "hc_bulk.cuh"
 #include "hc_common.cuh"
+#include "hc_exact.cuh"
 #include "hc_kernels.cuh"
 #include "hc_unpack.cuh"
 
@@ -200,6 +201,39 @@ __device__ __forceinline__ void unit_compute(const UnitRegsN<UC>& r, int type, i
   }
 }
 
+// unit_compute in the reference's exact f32 order (hc_exact.cuh): the unit's
+// per-lane integer sums of every column advance that column's eight lane
+// accumulators (and sumf) by one block.
+template <int NC, int UC>
+__device__ __forceinline__ void unit_compute_exact(const UnitRegsN<UC>& r, int type, int j, int ncols,
+                                                   const ActSlice& act, LaneChain (&acc)[NC]) {
+  const RegSrc<UC> src{r};
+  if (UC == Q4K_CHUNKS || type == TYPE_Q4_K) {
+    const Q4KHeader hd = q4k_header(src.chunk(0));
+#pragma unroll
+    for (int col = 0; col < NC; ++col) {
+      if (col < ncols) {
+        const uint8_t* rec = act.a + (col * act.nblk + j) * Q8A_REC;
+        BlockInts b;
+        q4k_lanes(src, hd, rec, b);
+        const float d8 = *reinterpret_cast<const float*>(rec + Q8A_D);
+        acc[col].add_block(b, __fmul_rn(hd.d, d8), __fmul_rn(hd.dmin, d8), true);
+      }
+    }
+  } else {
+    const float dw = f16_bits_to_f32(src.dbits());
+#pragma unroll
+    for (int col = 0; col < NC; ++col) {
+      if (col < ncols) {
+        const uint8_t* rec = act.b + (col * act.nblk + j) * Q8B_REC;
+        BlockInts b;
+        q6k_lanes(src, rec, b);
+        acc[col].add_block(b, __fmul_rn(dw, *reinterpret_cast<const float*>(rec + Q8B_D)), 0.0f, false);
+      }
+    }
+  }
+}
+
 // unit_compute on a unit staged in shared memory, read chunk by chunk as the
 // dot products consume it (no register buffer).
 template <int NC, int UC>
@@ -243,7 +277,11 @@ __device__ __forceinline__ const uint8_t* unit_addr(const GemvParams& p, int ite
 // unit is loaded one step ahead (double buffer), `flush(item, acc)` receives
 // each finished item's row sums.  buf[0] must already hold the first unit
 // (loaded by the caller before it waited for the previous kernel: PDL).
-template <int NC, int UC = UNIT_CHUNKS, class Flush>
+//
+// EXACT: every item is a whole tile's K range walked in block order, and each
+// row dot keeps the reference's eight lane accumulators (unit_compute_exact);
+// `flush` then receives the reference's row results bit for bit.
+template <int NC, int UC = UNIT_CHUNKS, bool EXACT = false, class Flush>
 __device__ __forceinline__ void stream_items(const GemvParams& p, const ActSlice& act, int item0, int istride,
                                              int nitems, int lane, UnitRegsN<UC>& buf0, int first_type,
                                              Flush& flush) {
@@ -252,8 +290,11 @@ __device__ __forceinline__ void stream_items(const GemvParams& p, const ActSlice
   int t0 = first_type, t1 = first_type;
   int item = item0, j = 0;
   float acc[NC];
+  LaneChain lacc[EXACT ? NC : 1];
 #pragma unroll
   for (int c = 0; c < NC; ++c) acc[c] = 0.0f;
+#pragma unroll
+  for (int c = 0; c < (EXACT ? NC : 1); ++c) lacc[c].zero();
   // One step: prefetch the unit after (item, j) into `nxt`, compute `cur`.
   // The two buffers alternate by name (no dynamic indexing, so they stay in
   // registers).
@@ -265,8 +306,19 @@ __device__ __forceinline__ void stream_items(const GemvParams& p, const ActSlice
     }
     const bool has_next = nitem < nitems;
     if (has_next) load_unit(nxt, unit_addr(p, nitem, nj, &tnxt), tnxt, lane);
-    unit_compute<NC, UC>(cur, tcur, (item & (p.split - 1)) * p.bps + j - act.kb0, p.ncols, act, acc);
+    if constexpr (EXACT) {
+      unit_compute_exact<NC, UC>(cur, tcur, (item & (p.split - 1)) * p.bps + j - act.kb0, p.ncols, act, lacc);
+    } else {
+      unit_compute<NC, UC>(cur, tcur, (item & (p.split - 1)) * p.bps + j - act.kb0, p.ncols, act, acc);
+    }
     if (nj == 0) {
+      if constexpr (EXACT) {
+#pragma unroll
+        for (int c = 0; c < NC; ++c) {
+          acc[c] = lacc[c].total(tcur == TYPE_Q4_K);
+          lacc[c].zero();
+        }
+      }
       flush(item, acc);
 #pragma unroll
       for (int c = 0; c < NC; ++c) acc[c] = 0.0f;

@@ -119,6 +119,38 @@ int persistent_grid(int items, int cap);
 int persistent_grid_w(int items, int cap, int warps_per_cta);
 cudaError_t launch_gemv(const GemvParams& p, cudaStream_t stream);
 
+// Exact-order matmul (hc_gemvx.cu): every row dot equals the reference's
+// vec_dot_q*_k_q8_k_prepared bit for bit (its 8 f32 lane accumulators in
+// block order).  Same segments / outputs / Q8_K workspace as GemvParams.
+constexpr int GEMVX_MAX_COLS = 8;
+struct GemvxParams {
+  GemvSeg seg[GEMV_MAXSEG];
+  int nseg;
+  int K, nb;         // input size and 256-blocks per row
+  int C;             // CTAs per tile (one cluster) splitting its K range
+  int nbc;           // blocks per CTA = nb / C
+  int col0, ncols;   // columns [col0, col0 + ncols), ncols <= GEMVX_MAX_COLS
+  int total_tiles;   // over all segments
+  int R;             // ring slots per warp
+  int slot;          // bytes per ring slot (the largest unit)
+  int planes;        // activation planes the weight types read: 1 = A (Q4_K), 2 = B (Q6_K)
+  int* err;          // device status word (bounded-wait timeouts)
+  Q8Buf q;
+};
+// Fills C, nbc, R, slot, err; returns the grid size (<= 0: no plan fits).
+int gemvx_plan(GemvxParams& p, int sms);
+cudaError_t launch_gemvx(GemvxParams& p, cudaStream_t st);
+
+// L2 prefetch of up to PREFETCH_MAX_RANGES byte ranges (hc_prefetch.cu):
+// cp.async.bulk.prefetch.L2 over each range, 16-byte aligned starts.
+constexpr int PREFETCH_MAX_RANGES = 8;
+struct PrefetchList {
+  const void* ptr[PREFETCH_MAX_RANGES];
+  size_t bytes[PREFETCH_MAX_RANGES];
+  int n;
+};
+cudaError_t launch_l2_prefetch(const PrefetchList& l, cudaStream_t st);
+
 // Inputs of at least TC_MIN_COLS columns go to the tensor-core matmul
 // (hc_gemm_tc.cu), one launch per weight covering every column.
 constexpr int TC_MIN_COLS = 16;

@@ -118,7 +118,8 @@ __global__ void __launch_bounds__(GEMV_THREADS, GEMV_CTAS_PER_SM) hc_lmhead_topk
   __syncthreads();
   const ActSlice act{act_a, act_b, p.nb, 0};
   TopkFlush<NC> flush{&P, &best[warp][0][0], lane};
-  stream_items<NC>(p, act, item0, istride, nitems, lane, buf[0], first_type, flush);
+  // whole tiles per warp, blocks in order: the reference's f32 order per row
+  stream_items<NC, UNIT_CHUNKS, true>(p, act, item0, istride, nitems, lane, buf[0], first_type, flush);
   __syncthreads();
   // Merge the four warp lists into this CTA's top-k: a real key's rank is its
   // index in its own list plus, for each other list, the number of larger

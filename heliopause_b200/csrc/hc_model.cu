@@ -17,6 +17,7 @@
 // and outputs go through model-owned buffers so replays read current values.
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <vector>
@@ -63,11 +64,24 @@ struct hpc_model_s {
   void* cand = nullptr;
   size_t cand_bytes = 0;
   int* err = nullptr;
+  // RoPE cos/sin of every position below the KV capacity, computed once on
+  // the host (the C library's cos/sin) -- [context][head_dim / 2] each
+  double *cos_tab = nullptr, *sin_tab = nullptr;
+  // exact (default): every step in the reference's arithmetic order, its
+  // results bit-identical to the WASM provider's; else the reordered kernels
+  bool exact = true;
+  float* attx_scratch = nullptr;  // exact attention: scores and probabilities
+  float* attn16 = nullptr;        // exact attention: the f16-cast output [M][H * head_dim]
   std::mutex mu;
   // graph per token count
   std::vector<cudaGraphExec_t> graphs;
   std::vector<int> graph_k;
   cudaStream_t capture_stream = nullptr;
+  // side stream of the step's L2 prefetches (forks after each QKV launch,
+  // joins at the end of the step) and its fork / join events
+  cudaStream_t side = nullptr;
+  cudaEvent_t fork_ev = nullptr, join_ev = nullptr;
+  bool l2_prefetch = true;
   // prefill workspace (hpc_model_prefill), grown to the largest token count seen
   void* pf_arena = nullptr;
   int pf_cap = 0;
@@ -168,6 +182,8 @@ int hpc_model_create(const hpc_model_config* cfg, hpc_model* out) {
       {(void**)&m->out_vals, sizeof(float) * M * hc::TOPK_MAX},
       {&m->q8d, m->q8d_bytes},
       {&m->q8f, m->q8f_bytes},
+      {(void**)&m->attx_scratch, sizeof(float) * hc::attx_scratch_floats(M, H, c.context)},
+      {(void**)&m->attn16, sizeof(float) * M * H * HD},
   };
   size_t total = 0;
   for (auto& p : pieces) total += (p.bytes + 255) / 256 * 256;
@@ -184,7 +200,42 @@ int hpc_model_create(const hpc_model_config* cfg, hpc_model* out) {
     cur += (p.bytes + 255) / 256 * 256;
   }
   m->err = hc::device_status_word();
+  {
+    // layers.ts:1012-1030: theta_0 = position, theta_{i+1} = fround(theta_i *
+    // base^(-2/ndims)), cos/sin in f64 -- evaluated here with the host's
+    // cos/sin, the same functions the reference's Math.cos/Math.sin and the
+    // oracle use, so the angles' roundings do not depend on the device's
+    // math library
+    const int half = HD / 2;
+    const double theta_scale = std::pow(c.rope_theta, -2.0 / double(HD));
+    std::vector<double> ct(size_t(c.context) * half), st(size_t(c.context) * half);
+    for (int p = 0; p < c.context; ++p) {
+      double th = double(p);
+      for (int i = 0; i < half; ++i) {
+        ct[size_t(p) * half + i] = std::cos(th);
+        st[size_t(p) * half + i] = std::sin(th);
+        th = double(float(th * theta_scale));
+      }
+    }
+    cudaError_t e = cudaMalloc(&m->cos_tab, ct.size() * sizeof(double));
+    if (e == cudaSuccess) e = cudaMalloc(&m->sin_tab, st.size() * sizeof(double));
+    if (e == cudaSuccess) e = cudaMemcpy(m->cos_tab, ct.data(), ct.size() * sizeof(double), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(m->sin_tab, st.data(), st.size() * sizeof(double), cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+      m->magic = kModelMagic;
+      hpc_model_release(m);
+      return hpc_cuda_fail(e, "RoPE table");
+    }
+  }
   HPC_CK(cudaStreamCreateWithFlags(&m->capture_stream, cudaStreamNonBlocking), "cudaStreamCreate");
+  HPC_CK(cudaStreamCreateWithFlags(&m->side, cudaStreamNonBlocking), "cudaStreamCreate");
+  HPC_CK(cudaEventCreateWithFlags(&m->fork_ev, cudaEventDisableTiming), "cudaEventCreate");
+  HPC_CK(cudaEventCreateWithFlags(&m->join_ev, cudaEventDisableTiming), "cudaEventCreate");
+  {
+    // HPC_DECODE_L2_PREFETCH=0 turns the per-layer weight prefetch off
+    const char* e = getenv("HPC_DECODE_L2_PREFETCH");
+    m->l2_prefetch = !(e && e[0] == '0');
+  }
   m->graphs.assign(M + 1, nullptr);
   m->graph_k.assign(M + 1, 0);
   m->magic = kModelMagic;
@@ -201,11 +252,16 @@ int hpc_model_release(hpc_model m) {
   for (auto& L : m->layers)
     for (auto n : L.norm) cudaFree(n);
   cudaFree(m->output_norm);
+  cudaFree(m->cos_tab);
+  cudaFree(m->sin_tab);
   cudaFree(m->arena);
   cudaFree(m->cand);
   cudaFree(m->pf_arena);
   cudaFree(m->pf_part);
   if (m->capture_stream) cudaStreamDestroy(m->capture_stream);
+  if (m->side) cudaStreamDestroy(m->side);
+  if (m->fork_ev) cudaEventDestroy(m->fork_ev);
+  if (m->join_ev) cudaEventDestroy(m->join_ev);
   m->magic = 0;
   delete m;
   return HPC_OK;
@@ -287,6 +343,14 @@ int hpc_model_set_lm_head(hpc_model m, hpc_weight w) {
   return HPC_OK;
 }
 
+int hpc_model_set_exact(hpc_model m, int enable) {
+  if (!model_valid(m)) return hpc_fail(HPC_ERR_ARG, "invalid model");
+  std::lock_guard<std::mutex> lock(m->mu);
+  m->exact = enable != 0;
+  invalidate_graphs(m);
+  return HPC_OK;
+}
+
 int hpc_model_kv(hpc_model m, int kv_layer, float** d_key, float** d_value) {
   if (!model_valid(m)) return hpc_fail(HPC_ERR_ARG, "invalid model");
   if (kv_layer < 0 || kv_layer >= m->cfg.kv_layers) return hpc_fail(HPC_ERR_ARG, "kv layer %d", kv_layer);
@@ -316,11 +380,12 @@ static int enqueue_step(hpc_model m, int M, int k, cudaStream_t st) {
       lens[n] = p.first->row_count * size_t(M);
       ++n;
     }
-    return hpc_matmul_q8(size_t(n), hs, q8, q8_bytes, K, size_t(M), outs, lens, st);
+    return hc_matmul_q8_order(size_t(n), hs, q8, q8_bytes, K, size_t(M), outs, lens, m->exact, st);
   };
   const hpc_weight emb = m->lm_head;
-  HPC_CK(hc::launch_rope_table(m->pos, M, HD / 2, std::pow(c.rope_theta, -2.0 / double(HD)), m->cos_t, m->sin_t, st),
-         "rope table");
+  HPC_CK(hc::launch_rope_gather(m->pos, M, HD / 2, m->cos_tab, m->sin_tab, c.context,
+                                std::pow(c.rope_theta, -2.0 / double(HD)), m->cos_t, m->sin_t, st),
+         "rope rows");
   HPC_CK(hc::launch_embed(emb->d_data, emb->type, emb->nb, c.vocab, m->ids, m->x, M, D, std::sqrt(double(D)), m->err,
                           st),
          "embedding");
@@ -330,7 +395,9 @@ static int enqueue_step(hpc_model m, int M, int k, cudaStream_t st) {
   // alternates between X (x_l, stored by the QKV prologue) and H1 (the
   // post-attention residual, stored by the gate/up prologue), so no CTA
   // overwrites a vector other CTAs of the same launch still read.
-  const bool fused = M <= 2 && D == hc::GEMV_PRO_D;
+  // (the reordered step only: the exact step runs the norms as launches of
+  // their own and every matmul on the exact-order kernel)
+  const bool fused = !m->exact && M <= 2 && D == hc::GEMV_PRO_D;
   float* const X = m->x;
   float* const H1 = fused ? m->h1 : m->x;
   auto mm_pro = [&](std::initializer_list<std::pair<hpc_weight, float*>> ws, const hc::GemvPrologue& pro) -> int {
@@ -381,12 +448,32 @@ static int enqueue_step(hpc_model m, int M, int k, cudaStream_t st) {
                   : mm({{L.w[HPC_W_Q], m->qb}}, m->q8d, m->q8d_bytes, D);
     }
     if (rc != HPC_OK) return rc;
-    HPC_CK(hc::launch_attention(m->qb, m->kb, m->vb, L.norm[HPC_N_Q], L.norm[HPC_N_K], m->cos_t, m->sin_t, eps, own_kv,
-                                m->kc[kvl], m->vc[kvl], m->pos, M, H, KVH, c.context, 1.0f, m->pm, m->pl, m->po,
-                                m->err, st),
-           "qk norm / rope / kv + attention");
-    HPC_CK(hc::launch_attn_combine(m->pm, m->pl, m->po, m->pos, M, H, KVH, c.context, qd, nullptr, st),
-           "attention combine");
+    if (m->l2_prefetch) {
+      // while the attention runs: this layer's O, gate, up and down weights into L2
+      hc::PrefetchList pl{};
+      for (int slot : {HPC_W_O, HPC_W_GATE, HPC_W_UP, HPC_W_DOWN}) {
+        pl.ptr[pl.n] = L.w[slot]->d_data;
+        pl.bytes[pl.n] = L.w[slot]->bytes;
+        ++pl.n;
+      }
+      HPC_CK(cudaEventRecord(m->fork_ev, st), "fork record");
+      HPC_CK(cudaStreamWaitEvent(m->side, m->fork_ev, 0), "fork wait");
+      HPC_CK(hc::launch_l2_prefetch(pl, m->side), "L2 prefetch");
+    }
+    if (m->exact) {
+      HPC_CK(hc::launch_attention_exact(m->qb, m->kb, m->vb, L.norm[HPC_N_Q], L.norm[HPC_N_K], m->cos_t, m->sin_t, eps,
+                                        own_kv, m->kc[kvl], m->vc[kvl], m->pos, M, H, KVH, c.context, 1.0f,
+                                        m->attx_scratch, m->attn16, st),
+             "exact-order attention");
+      HPC_CK(hc::launch_q8k_quantize(m->attn16, H * HD, M, qd, nullptr, nullptr, nullptr, st), "attention quantize");
+    } else {
+      HPC_CK(hc::launch_attention(m->qb, m->kb, m->vb, L.norm[HPC_N_Q], L.norm[HPC_N_K], m->cos_t, m->sin_t, eps,
+                                  own_kv, m->kc[kvl], m->vc[kvl], m->pos, M, H, KVH, c.context, 1.0f, m->pm, m->pl,
+                                  m->po, m->err, st),
+             "qk norm / rope / kv + attention");
+      HPC_CK(hc::launch_attn_combine(m->pm, m->pl, m->po, m->pos, M, H, KVH, c.context, qd, nullptr, st),
+             "attention combine");
+    }
     rc = mm({{L.w[HPC_W_O], m->o}}, m->q8d, m->q8d_bytes, size_t(H) * HD);
     if (rc != HPC_OK) return rc;
     // post-attention residual + FFN norm and gate/up
@@ -411,12 +498,16 @@ static int enqueue_step(hpc_model m, int M, int k, cudaStream_t st) {
     rc = mm({{L.w[HPC_W_DOWN], m->f}}, m->q8f, m->q8f_bytes, F);
     if (rc != HPC_OK) return rc;
   }
+  if (m->l2_prefetch) {  // the side stream joins the step
+    HPC_CK(cudaEventRecord(m->join_ev, m->side), "join record");
+    HPC_CK(cudaStreamWaitEvent(st, m->join_ev, 0), "join wait");
+  }
   // final post-FFN residual + output norm, then the LM head
   HPC_CK(hc::launch_norm_quant(true, H1, X, m->f, m->layers[c.layers - 1].norm[HPC_N_POST_FFW], m->output_norm, eps,
                                M, D, qd, nullptr, st),
          "post-ffn residual + output norm");
-  return hpc_lm_head_topk_q8(emb, m->q8d, m->q8d_bytes, size_t(D), size_t(M), size_t(k), 0, m->cand, m->cand_bytes,
-                             c.final_logit_softcap, m->out_ids, m->out_vals, nullptr, st);
+  return hc_lm_head_topk_q8_order(emb, m->q8d, m->q8d_bytes, size_t(D), size_t(M), size_t(k), 0, m->cand,
+                                  m->cand_bytes, c.final_logit_softcap, m->out_ids, m->out_vals, nullptr, m->exact, st);
 }
 
 static int model_ready(hpc_model m) {
@@ -580,9 +671,9 @@ int hpc_model_prefill(hpc_model m, const float* d_hidden_in, const int32_t* d_po
     pl = pm + rows;
     po = reinterpret_cast<float*>(static_cast<char*>(m->pf_part) + (rows * 2 * sizeof(float) + 255) / 256 * 256);
   }
-  HPC_CK(hc::launch_rope_table(m->pf_pos, M, HD / 2, std::pow(c.rope_theta, -2.0 / double(HD)), m->pf_cos, m->pf_sin,
-                               st),
-         "rope table");
+  HPC_CK(hc::launch_rope_gather(m->pf_pos, M, HD / 2, m->cos_tab, m->sin_tab, c.context,
+                                std::pow(c.rope_theta, -2.0 / double(HD)), m->pf_cos, m->pf_sin, st),
+         "rope rows");
   auto mm = [&](std::initializer_list<std::pair<hpc_weight, float*>> ws, const void* q8, size_t q8_bytes,
                 size_t K) -> int {
     hpc_weight hs[8];

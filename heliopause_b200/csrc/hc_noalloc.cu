@@ -22,7 +22,9 @@
 //     cudaGetSymbolAddress (and the launches behind it set their kernel
 //     attributes on first use); make that first call outside any stream
 //     capture.
-// The kernels launched are exactly those of hpc_lm_head_topk.
+// The kernels launched are the fused LM head of hpc_lm_head_topk (per-warp
+// candidate lists over the weight stream, then the merge) for every width,
+// in the reference's f32 order, so the results equal hpc_lm_head_topk's.
 #include <cstdio>
 #include <mutex>
 
@@ -68,6 +70,9 @@ extern "C" int hpc_lm_head_topk_noalloc(hpc_weight h, const float* d_hidden, siz
   size_t cb = 0;
   int rc = hpc_lm_head_candidates_bytes(h, column_count, k, &cb);  // validates handle, shape, k
   if (rc != HPC_OK) return rc;
+  // the fused path (per-warp candidate lists, reference order) for every
+  // width: its candidates are the smallest
+  cb = hc_lm_head_fused_candidates_bytes(h, column_count, k);
   size_t head_input = 0;
   rc = hpc_weight_info(h, nullptr, &head_input, nullptr, nullptr);
   if (rc != HPC_OK) return rc;
@@ -88,6 +93,6 @@ extern "C" int hpc_lm_head_topk_noalloc(hpc_weight h, const float* d_hidden, siz
   cudaError_t e = hc::launch_q8k_quantize(d_hidden, int(input_size), int(column_count), q, nullptr, nullptr, nullptr,
                                           st);
   if (e != cudaSuccess) return hpc_cuda_fail(e, "quantize launch");
-  return hpc_lm_head_topk_q8(h, ws, qb, input_size, column_count, k, id_offset, static_cast<char*>(ws) + qb, cb,
-                             softcap, d_ids, d_vals, nullptr, stream);
+  return hc_lm_head_topk_q8_order(h, ws, qb, input_size, column_count, k, id_offset, static_cast<char*>(ws) + qb, cb,
+                                  softcap, d_ids, d_vals, nullptr, true, st, true);
 }

@@ -272,6 +272,12 @@ def lm_head_topk(handle: CudaQuantizedWeightHandle, hidden, column_count: int, k
     return ids, vals
 
 
+def set_matmul_order(exact: bool) -> None:
+    """Reference f32 order (default) or the reordered kernels for the matmul
+    and LM-head calls (hpc_set_matmul_order)."""
+    assert_cuda_ok(_lib.lib().hpc_set_matmul_order(int(bool(exact))), "setMatmulOrder")
+
+
 def device_error() -> None:
     """Raises CudaKernelError(ERR_TIMEOUT) if a kernel's bounded wait gave up."""
     assert_cuda_ok(_lib.lib().hpc_device_error(), "deviceStatus")

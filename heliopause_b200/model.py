@@ -248,6 +248,11 @@ class CudaDecoderModel:
         return kt, vt
 
     # ---- running -----------------------------------------------------------
+    def set_exact(self, enable: bool) -> None:
+        """Reference-order steps (default; bit-identical top-k) or the
+        reordered kernels (hpc_model_set_exact)."""
+        hk.assert_cuda_ok(_lib.lib().hpc_model_set_exact(self._h, int(bool(enable))), "modelSetExact")
+
     def forward(self, token_ids, positions, top_k: int, *, return_hidden: bool = False):
         """Top-k (ids, values) of every position, [n][top_k] torch tensors."""
         ids = torch.as_tensor(token_ids, dtype=torch.int32).reshape(-1)

@@ -99,6 +99,17 @@ int hpc_weight_dequantize(hpc_weight handle, float *d_out, size_t out_len, void 
 int hpc_quantize_q8_k(const float *d_in, size_t in_len, size_t input_size, size_t column_count, float *d_d,
                       int8_t *d_qs, int16_t *d_bsums, void *stream);
 
+/* Arithmetic order of the matmul and LM-head entry points below
+ * (process-wide).  exact != 0 (the default): every output row dot of fewer
+ * than 16 columns is vec_dot_q4_k_q8_k_prepared / vec_dot_q6_k_q8_k_prepared
+ * (lib.rs:1924-1968, 2117-2172) in its own f32 order -- eight lane
+ * accumulators, block by block -- so results equal the WASM exports bit for
+ * bit.  exact == 0: the reordered kernels (dp4a GEMV, tensor-core GEMV and
+ * LM head for 3-8 columns), equal to f32 rounding.  16 or more columns run on
+ * the tensor cores in either order.  Calls already enqueued keep the order
+ * they were made with. */
+int hpc_set_matmul_order(int exact);
+
 /* Resident GEMV / small-M matmul with Q8_K activations.
  * Replaces hp_matmul_quantized_prepared_f32 (lib.rs:225-298) as called by
  * matMulQuantizedWasmResident (wasm-kernels.ts:593-646); same validation
@@ -270,6 +281,20 @@ int hpc_model_set_weight(hpc_model model, int layer, int slot, hpc_weight weight
 int hpc_model_set_norm(hpc_model model, int layer, int slot, const float *host_values, size_t len);
 /* token_embd.weight == output weight (tied): rows are vocabulary ids. */
 int hpc_model_set_lm_head(hpc_model model, hpc_weight weight);
+/* Arithmetic order of the model's steps.  enable != 0 (the default): every
+ * step computes in the reference's own order -- each matmul row dot with the
+ * eight f32 lane accumulators of vec_dot_q*_k_q8_k_prepared
+ * (lib.rs:1924-1968, 2117-2172), the attention's dots, softmax sum and
+ * p.v sums as the sequential f32 chains of hp_gqa_attention_f32
+ * (lib.rs:539-654), RoPE angles from host-computed cos/sin -- so its top-k
+ * ids and values equal the WASM provider's (runner/wasm/layers.ts:161-473,
+ * forwardOutput :381-416) bit for bit.  enable == 0: the reordered kernels
+ * (split-KV attention with a combine, norms fused into the GEMVs, the
+ * tensor-core GEMV / LM head for 3-8 tokens): faster, equal to the
+ * reference only to f32 rounding, which the Q8_K re-quantization of every
+ * matmul input amplifies over the layers. */
+int hpc_model_set_exact(hpc_model model, int enable);
+
 /* Device pointers of one KV layer's cache, f32: K [context][kv_heads][head_dim]
  * (the layers.ts:887-911 layout) and V [context][kv_heads][head_dim] -- V is
  * token-major like K, the transpose of the reference's [head_dim][kv_heads]

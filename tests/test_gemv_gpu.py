@@ -2,7 +2,12 @@
 
   * dequantization of the resident (repacked) weights: bit-exact;
   * Q8_K activation quantization: bit-exact (d, qs, bsums);
-  * matmul outputs: within the north-star tolerance rtol 1e-3 / atol 1e-4,
+  * matmul outputs in the default (reference) order, fewer than 16 columns:
+    bit-exact -- every row dot keeps vec_dot_q*_k_q8_k_prepared's eight f32
+    lane accumulators in block order (lib.rs:1924-1968, 2117-2172);
+  * matmul outputs of the reordered kernels (hpc_set_matmul_order(0)) and of
+    the tensor-core path (16+ columns): within the north-star tolerance
+    rtol 1e-3 / atol 1e-4,
         |gpu - ref| <= 1e-4 + 1e-3 * |ref| + (nb + 8) * 2^-24 * S,
     on the configuration shapes (config 1: Q4_K 2048 -> 16384; config 2:
     Q/K/V/gate/up + Q6_K down, M in {1, 2, 4, 8}) and on ragged/edge shapes.
@@ -42,6 +47,14 @@ def _close(got, ref, mag=None, nb=8):
     ok = err <= bound
     assert ok.all(), f"{(~ok).sum()} of {ok.size} outside tolerance; max err {err.max():.3g}"
     return int((err > strict).sum())
+
+
+def _bitwise(got, ref, what):
+    got = np.ascontiguousarray(got, np.float32)
+    ref = np.ascontiguousarray(ref, np.float32)
+    diff = got.view(np.uint32) != ref.view(np.uint32)
+    assert not diff.any(), (f"{what}: {int(diff.sum())} of {diff.size} differ, max |d| "
+                            f"{np.abs(got.astype(np.float64) - ref).max():.3g}")
 
 
 def _magnitude(oracle, type_id, w, x, k, rows, cols):
@@ -118,16 +131,25 @@ def _oracle_matmul(oracle, type_id, w, x, k, rows, cols):
     (syn.Q6_K, 16384, 2048, 16),
     (syn.Q6_K, 256, 33, 17),
 ])
-def test_matmul_matches_oracle(oracle, type_id, k, rows, cols):
+@pytest.mark.parametrize("order", ["exact", "reordered"])
+def test_matmul_matches_oracle(oracle, type_id, k, rows, cols, order):
+    if order == "reordered" and cols >= 16:
+        pytest.skip("16+ columns take the tensor-core path in either order")
     w = syn.quant_weight(type_id, rows, k, seed=rows * 3 + cols)
     x = syn.activations(cols, k, seed=cols + 100)
     h = hk.create_quantized_weight_handle(TNAME[type_id], w, k, rows)
+    hk.set_matmul_order(order == "exact")
     try:
         got = hk.mat_mul_quantized_resident(h, torch.from_numpy(x).cuda(), k, rows, cols).cpu().numpy()
     finally:
+        hk.set_matmul_order(True)
         hk.release_quantized_weight_handle(h)
+    ref = _oracle_matmul(oracle, type_id, w, x, k, rows, cols)
+    if order == "exact" and cols < 16:
+        _bitwise(got, ref, "exact-order matmul")
+        return
     mag = _magnitude(oracle, type_id, w, x, k, rows, cols)
-    n_reassoc = _close(got, _oracle_matmul(oracle, type_id, w, x, k, rows, cols), mag, k // 256)
+    n_reassoc = _close(got, ref, mag, k // 256)
     print(f"outputs needing the re-association term: {n_reassoc} of {got.size}")
 
 
@@ -146,7 +168,7 @@ def test_multi_projection_config2(oracle, cols):
         for h in hs:
             hk.release_quantized_weight_handle(h)
     for (name, t, r), w, got in zip(specs, ws, outs):
-        _close(got, _oracle_matmul(oracle, t, w, x, k, r, cols))
+        _bitwise(got, _oracle_matmul(oracle, t, w, x, k, r, cols), name)
 
 
 def test_one_shot_host_api(oracle):
@@ -154,7 +176,7 @@ def test_one_shot_host_api(oracle):
     w = syn.quant_weight(syn.Q6_K, rows, k, seed=9)
     x = syn.activations(cols, k, seed=10)
     got = hk.mat_mul_quantized("Q6_K", w.tobytes(), x, k, rows, cols)
-    _close(got, oracle.matmul_quantized(syn.Q6_K, w, x, k, rows, cols))
+    _bitwise(got, oracle.matmul_quantized(syn.Q6_K, w, x, k, rows, cols), "one-shot matmul")
 
 
 def test_zero_columns_and_errors():

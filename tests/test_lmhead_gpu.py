@@ -1,10 +1,13 @@
 """GPU parity of the fused LM head + top-k against the oracle.
 
 The oracle materializes every logit with the C restatement of lib.rs and
-selects with the restated topK (runtime.ts:514-527).  Ids must match exactly
-(sets and order); where two oracle logits differ by less than the matmul
-tolerance (|d| <= 1e-4 + 1e-3 |v|) their order may swap.  Values are within
-the same tolerance.
+selects with the restated topK (runtime.ts:514-527).
+  * default (reference) order, fewer than 16 columns: ids equal the oracle's
+    (sets and order) and values equal bit for bit;
+  * the reordered kernels (hpc_set_matmul_order(0)) and the tensor-core path
+    (16+ columns): ids must match exactly, except that two oracle logits that
+    differ by less than the matmul tolerance (|d| <= 1e-4 + 1e-3 |v|) may
+    swap; values within the same tolerance.
 """
 import numpy as np
 import pytest
@@ -57,21 +60,32 @@ def _check_topk(ids, vals, logits, k):
     (syn.Q6_K, 50000, 64, 17),
     (syn.Q4_K, 4096, 1, 20),
 ])
-def test_lm_head_topk_matches_oracle(oracle, type_id, rows, k, cols):
+@pytest.mark.parametrize("order", ["exact", "reordered"])
+def test_lm_head_topk_matches_oracle(oracle, type_id, rows, k, cols, order):
+    if order == "reordered" and cols >= 16:
+        pytest.skip("16+ columns take the tensor-core path in either order")
     kdim = 2048
     w = syn.quant_weight(type_id, rows, kdim, seed=rows + k)
     x = syn.activations(cols, kdim, seed=cols)
     name = "Q6_K" if type_id == syn.Q6_K else "Q4_K"
     h = hk.create_quantized_weight_handle(name, w, kdim, rows)
+    hk.set_matmul_order(order == "exact")
     try:
         ids, vals = hk.lm_head_topk(h, torch.from_numpy(x).cuda(), cols, k)
         ids, vals = ids.cpu().numpy(), vals.cpu().numpy()
     finally:
+        hk.set_matmul_order(True)
         hk.release_quantized_weight_handle(h)
     s = oracle.prepare_scales(type_id, w, kdim, rows)
     logits = oracle.matmul_prepared(type_id, w, s, x, kdim, rows, cols, threads=oracle.cpu_threads())
     for c in range(cols):
-        _check_topk(ids[c], vals[c], logits[c * rows:(c + 1) * rows], k)
+        lc = logits[c * rows:(c + 1) * rows]
+        if order == "exact" and cols < 16:
+            ref_ids, ref_vals = oracle.topk(lc, k)
+            assert np.array_equal(ids[c], ref_ids), f"column {c}: ids differ"
+            assert np.array_equal(vals[c].view(np.uint32), ref_vals.astype(np.float32).view(np.uint32))
+        else:
+            _check_topk(ids[c], vals[c], lc, k)
 
 
 def test_ties_prefer_lower_id_and_softcap(oracle):
@@ -101,16 +115,23 @@ def test_ties_prefer_lower_id_and_softcap(oracle):
     finally:
         hk.release_quantized_weight_handle(h)
     assert all(r == list(range(7, 17)) for r in ids.cpu().numpy().tolist())
-    assert np.all(vals.cpu().numpy() == v[0])
-    # and on the tensor-core LM head of 3..8 columns
+    tv = vals.cpu().numpy()
+    assert np.all(tv == tv[0, 0]) and abs(tv[0, 0] - v[0]) <= _tol(v[0])
+    # and at 3..8 columns, on the exact-order logits and on the tensor-core
+    # LM head of the reordered kernels
     x = np.tile(syn.activations(1, kdim, seed=4), 5)
     h = hk.create_quantized_weight_handle("Q6_K", w, kdim, rows)
     try:
-        ids, vals = hk.lm_head_topk(h, torch.from_numpy(x).cuda(), 5, 10, id_offset=3)
+        for exact in (True, False):
+            hk.set_matmul_order(exact)
+            ids, vals = hk.lm_head_topk(h, torch.from_numpy(x).cuda(), 5, 10, id_offset=3)
+            assert all(r == list(range(3, 13)) for r in ids.cpu().numpy().tolist())
+            mv = vals.cpu().numpy()
+            assert np.all(mv == mv[0, 0])
+            assert (mv[0, 0] == v[0]) if exact else abs(mv[0, 0] - v[0]) <= _tol(v[0])
     finally:
+        hk.set_matmul_order(True)
         hk.release_quantized_weight_handle(h)
-    assert all(r == list(range(3, 13)) for r in ids.cpu().numpy().tolist())
-    assert np.all(vals.cpu().numpy() == v[0])
 
 
 def test_topk_errors():

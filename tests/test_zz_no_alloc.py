@@ -60,38 +60,40 @@ def test_noalloc_matches_allocating_entry_point_twice_in_a_row(env):
 
 def test_noalloc_at_its_size_limit(env):
     # The widest call that still fits the static scratch (Q8_K records plus
-    # candidate lists within a column of HPC_NOALLOC_SCRATCH_BYTES) matches
-    # the allocating entry point, so the carve near the array's upper end is
-    # right; one column more is refused with HPC_ERR_SHAPE before any launch.
+    # candidate lists within HPC_NOALLOC_SCRATCH_BYTES), found by the entry
+    # point's own answers, matches the allocating entry point -- so the carve
+    # at the array's upper end is right -- and one column more is refused
+    # with HPC_ERR_SHAPE before any launch.
     torch, hk, L = env
     kdim, rows, k = 256, 65536, 64
     head = hk.create_quantized_weight_handle("Q6_K", syn.q6_k_weight(rows, kdim, seed=7), kdim, rows)
     try:
-        need = C.c_size_t()
+        def rc(cols):
+            x = torch.zeros(cols * kdim, device="cuda")
+            ids = torch.empty(cols * k, dtype=torch.int32, device="cuda")
+            vals = torch.empty(cols * k, device="cuda")
+            r = L.hpc_lm_head_topk_noalloc(head.handle, C.c_void_p(x.data_ptr()), x.numel(), kdim, cols, k, 0,
+                                           C.c_float(0.0), C.c_void_p(ids.data_ptr()), C.c_void_p(vals.data_ptr()),
+                                           None)
+            torch.cuda.synchronize()
+            return r
 
-        def scratch(cols):
-            assert L.hpc_lm_head_candidates_bytes(head.handle, cols, k, C.byref(need)) == 0
-            cand = need.value
-            assert L.hpc_q8_workspace_bytes(kdim, cols, C.byref(need)) == 0
-            return need.value + cand
-
-        fit = 1
-        while scratch(fit + 1) <= SCRATCH_BYTES:
-            fit += 1
-        assert scratch(fit) > SCRATCH_BYTES - scratch(fit) / fit * 2, "the fitting call is not near the limit"
+        lo, hi = 1, 2
+        while rc(hi) == 0:  # grow until refused
+            lo, hi = hi, hi * 2
+        while hi - lo > 1:  # largest fitting width in (lo, hi)
+            mid = (lo + hi) // 2
+            if rc(mid) == 0:
+                lo = mid
+            else:
+                hi = mid
+        fit = lo
+        assert rc(fit + 1) == hk.ERR_SHAPE
+        assert b"static" in L.hpc_last_error()
         x = torch.from_numpy(syn.activations(fit, kdim, seed=fit)).cuda()
         ids, vals = _call(L, "hpc_lm_head_topk_noalloc", torch, head, x, fit, k, 0.0)
         rids, rvals = _call(L, "hpc_lm_head_topk", torch, head, x, fit, k, 0.0)
         assert np.array_equal(ids, rids)
         assert np.all(np.abs(vals.astype(np.float64) - rvals) <= 1e-4 + 1e-3 * np.abs(rvals))
-        cols = fit + 1
-        x = torch.from_numpy(syn.activations(cols, kdim, seed=cols)).cuda()
-        ids = torch.empty(cols * k, dtype=torch.int32, device="cuda")
-        vals = torch.empty(cols * k, device="cuda")
-        rc = L.hpc_lm_head_topk_noalloc(head.handle, C.c_void_p(x.data_ptr()), x.numel(), kdim, cols, k, 0,
-                                        C.c_float(0.0), C.c_void_p(ids.data_ptr()), C.c_void_p(vals.data_ptr()), None)
-        assert rc == hk.ERR_SHAPE
-        assert b"static" in L.hpc_last_error()
-        torch.cuda.synchronize()
     finally:
         hk.release_quantized_weight_handle(head)
