@@ -19,7 +19,9 @@
 //                          K/V rows (written to the cache), one sequential
 //                          256-term dot per (query, key);
 //   hc_attx_softmax_kernel grid (tokens x heads): the max, the f64 exps, the
-//                          one 4096-term sequential sum, the divisions;
+//                          4096-term sequential sum (one warp, exact
+//                          prefix scans between its binade changes), the
+//                          divisions;
 //   hc_attx_pv_kernel      grid (KV head x 32-dim slice, groups of 4 query
 //                          vectors): one sequential chain per (query, dim)
 //                          over all keys, then the TS f16 cast of the output
@@ -44,6 +46,7 @@ constexpr int AX_QL = 4;             // query lanes of the scores CTA (256 threa
 constexpr int AX_SM_THREADS = 1024;  // softmax CTA
 constexpr int AX_PV_QG = 4;          // query vectors per PV CTA (one warp each)
 constexpr int AX_PV_TC = 256;        // keys per staged V chunk
+constexpr int AX_PV_NS = 4;          // V chunks in flight (a 4-stage ring: 96 KB of copies ahead of the chain)
 
 struct KeyRange {
   int count, start, maxpos;
@@ -97,6 +100,14 @@ __global__ void __launch_bounds__(256) hc_attx_scores_kernel(
         cp_async16(ks + t * AX_KSTRIDE + 4 * c, kc + (size_t(t0 + t) * KVH + kvh) * HD + 4 * c);
       }
     cp_async_commit();
+    // the same slots' V rows (every KV head) into L2 for the p.v kernel two
+    // launches later, which streams them in key order
+    if (kvh == 0 && threadIdx.x < 8) {
+      const char* vrow = reinterpret_cast<const char*>(vc + size_t(t0) * KVH * HD);
+      const uint32_t span = uint32_t(AX_CH / 8) * uint32_t(KVH) * HD * 4;  // 8 pieces of the 64 slots
+      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(vrow + size_t(threadIdx.x) * span), "r"(span)
+                   : "memory");
+    }
   }
   const int lane = int(threadIdx.x) & 31, warp = int(threadIdx.x) >> 5, warps = int(blockDim.x) >> 5;
   float qw[8], kw[8];
@@ -183,6 +194,73 @@ __global__ void __launch_bounds__(256) hc_attx_scores_kernel(
   }
 }
 
+// The sequential f32 sum  s = fround(s + v[j]), j = 0 .. n-1, s from +0, of
+// non-negative finite terms, bit for bit, by one warp (every lane returns it).
+// While the running sum stays in one binade its grid is fixed (ulp 2^e, the
+// subnormal grid 2^-149 included), s = M * 2^e with integer M < 2^24, and a
+// step adds the term rounded to that grid, k = RN(v / 2^e) -- a plain integer
+// -- so a run of steps is an integer prefix sum.  The warp takes 8 terms per
+// lane (256 in sequence order), scans the k's and commits every step up to the
+// first one whose rounding the grid does not decide: an exact tie (its
+// direction depends on the parity of the running sum) or a sum reaching the
+// next binade.  That step is done with one f32 add on the committed sum, and
+// the scan resumes after it.
+__device__ float seq_sum_nonneg_warp(const float* __restrict__ v, int n, int lane) {
+  constexpr int PER = 8;
+  float s = 0.0f;
+  int j = 0;
+  while (j < n) {
+    const uint32_t ex = (__float_as_uint(s) >> 23) & 0xffu;
+    const int e = ex <= 1u ? -149 : int(ex) - 150;  // ulp of s (and of [0, 2^-125))
+    const double M = ldexp(double(s), -e);          // the integer significand on that grid
+    const double scale = ldexp(1.0, -e);
+    const int base = j + PER * lane;
+    uint32_t k[PER];
+    double q[PER];
+    bool bad[PER];
+    uint32_t local = 0;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      const int idx = base + i;
+      q[i] = idx < n ? double(v[idx]) * scale : 0.0;  // exact: a power-of-two scaling
+      const double fl = floor(q[i]);
+      bad[i] = q[i] >= 16777216.0 || q[i] - fl == 0.5;
+      k[i] = bad[i] ? 0u : uint32_t(floor(q[i] + 0.5));
+      local += k[i];
+    }
+    uint32_t incl = local;  // steps before the first non-committable one stay below 2^24
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const uint32_t t = __shfl_up_sync(0xffffffffu, incl, off);
+      if (lane >= off) incl += t;
+    }
+    uint32_t run = incl - local;
+    int first = PER;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      if (first == PER && base + i < n) {
+        // the exact pre-rounding value on the grid: M + run + q
+        if (bad[i] || (M + double(run)) + q[i] >= 16777215.5) first = i;
+        else run += k[i];
+      }
+    }
+    const unsigned m = __ballot_sync(0xffffffffu, first < PER);
+    if (m == 0u) {
+      const uint32_t tot = __shfl_sync(0xffffffffu, incl, 31);
+      s = float(ldexp(M + double(tot), e));
+      j += 32 * PER;
+    } else {
+      const int fl_lane = __ffs(m) - 1;
+      const int fi = __shfl_sync(0xffffffffu, first, fl_lane);
+      const uint32_t committed = __shfl_sync(0xffffffffu, run, fl_lane);
+      const int idx = j + PER * fl_lane + fi;
+      s = __fadd_rn(float(ldexp(M + double(committed), e)), v[idx]);
+      j = idx + 1;
+    }
+  }
+  return s;
+}
+
 __global__ void __launch_bounds__(AX_SM_THREADS) hc_attx_softmax_kernel(const float* __restrict__ scores,
                                                                         const int32_t* __restrict__ pos, int M, int H,
                                                                         int cap, float* __restrict__ rprob) {
@@ -213,18 +291,9 @@ __global__ void __launch_bounds__(AX_SM_THREADS) hc_attx_softmax_kernel(const fl
     ps[j] = s == -INFINITY ? 0.0f : float(exp(double(__fsub_rn(s, mx))));
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    float sum = 0.0f;
-    int j = 0;
-    for (; j + 4 <= kr.count; j += 4) {
-      const float4 v = *reinterpret_cast<const float4*>(ps + j);
-      sum = __fadd_rn(sum, v.x);
-      sum = __fadd_rn(sum, v.y);
-      sum = __fadd_rn(sum, v.z);
-      sum = __fadd_rn(sum, v.w);
-    }
-    for (; j < kr.count; ++j) sum = __fadd_rn(sum, ps[j]);
-    s_sum = sum;
+  if (threadIdx.x < 32) {  // the sequential sum (lib.rs:627-635), by one warp
+    const float sum = seq_sum_nonneg_warp(ps, kr.count, int(threadIdx.x));
+    if (threadIdx.x == 0) s_sum = sum;
   }
   __syncthreads();
   const float sum = s_sum;
@@ -237,8 +306,9 @@ __global__ void __launch_bounds__(32 * AX_PV_QG) hc_attx_pv_kernel(const float* 
                                                                    const int32_t* __restrict__ pos, int M, int H,
                                                                    int KVH, int cap, float* __restrict__ out16) {
   extern __shared__ __align__(16) float pv_smem[];
-  float (*vs)[AX_PV_TC][32] = reinterpret_cast<float (*)[AX_PV_TC][32]>(pv_smem);                      // [2][TC][32]
-  float (*rs)[AX_PV_QG][AX_PV_TC] = reinterpret_cast<float (*)[AX_PV_QG][AX_PV_TC]>(pv_smem + 2 * AX_PV_TC * 32);  // [2][QG][TC]
+  float (*vs)[AX_PV_TC][32] = reinterpret_cast<float (*)[AX_PV_TC][32]>(pv_smem);  // [NS][TC][32]
+  float (*rs)[AX_PV_QG][AX_PV_TC] =
+      reinterpret_cast<float (*)[AX_PV_QG][AX_PV_TC]>(pv_smem + AX_PV_NS * AX_PV_TC * 32);  // [NS][QG][TC]
   const int kvh = int(blockIdx.x) >> 3, ds = int(blockIdx.x) & 7, qg = int(blockIdx.y);
   const int lane = int(threadIdx.x) & 31, warp = int(threadIdx.x) >> 5;
   const int G = H / KVH, NQ = M * G;
@@ -272,15 +342,17 @@ __global__ void __launch_bounds__(32 * AX_PV_QG) hc_attx_pv_kernel(const float* 
     cp_async_commit();
   };
   float acc = 0.0f;
-  load_chunk(0, 0);
+  // a ring of NS chunks: chunks c + 1 .. c + NS - 1 are in flight while the
+  // chain walks chunk c (one commit group per chunk, empty past the end)
+  for (int c = 0; c < AX_PV_NS - 1; ++c) {
+    if (c < nchunk) load_chunk(c, c);
+    else cp_async_commit();
+  }
   for (int c = 0; c < nchunk; ++c) {
-    const int buf = c & 1;
-    if (c + 1 < nchunk) {
-      load_chunk(c + 1, buf ^ 1);
-      asm volatile("cp.async.wait_group 1;" ::: "memory");
-    } else {
-      cp_async_wait_all();
-    }
+    const int buf = c % AX_PV_NS;
+    if (c + AX_PV_NS - 1 < nchunk) load_chunk(c + AX_PV_NS - 1, (c + AX_PV_NS - 1) % AX_PV_NS);
+    else cp_async_commit();
+    asm volatile("cp.async.wait_group %0;" ::"n"(AX_PV_NS - 1) : "memory");
     __syncthreads();
     const int n = min(AX_PV_TC, kr.count - c * AX_PV_TC);
     if (qi < NQ) {
@@ -295,7 +367,7 @@ __global__ void __launch_bounds__(32 * AX_PV_QG) hc_attx_pv_kernel(const float* 
       }
       for (; jj < n; ++jj) acc = __fadd_rn(acc, __fmul_rn(r[jj], vs[buf][jj][lane]));
     }
-    __syncthreads();  // the buffer is refilled two chunks later
+    __syncthreads();  // the buffer is refilled NS - 1 chunks later
   }
   if (qi < NQ) {
     const int m = qi / G, h = kvh * G + qi % G;
@@ -304,6 +376,11 @@ __global__ void __launch_bounds__(32 * AX_PV_QG) hc_attx_pv_kernel(const float* 
 }
 
 }  // namespace
+
+__global__ void hc_seq_sum_test_kernel(const float* v, int n, float* out) {
+  const float s = seq_sum_nonneg_warp(v, n, int(threadIdx.x));
+  if (threadIdx.x == 0) *out = s;
+}
 
 size_t attx_scores_smem_bytes(int M, int H, int KVH) {
   return sizeof(float) * (size_t(AX_CH) * AX_KSTRIDE + size_t(M) * (H / KVH) * 256);
@@ -334,7 +411,7 @@ cudaError_t launch_attention_exact(const float* q, const float* kraw, const floa
   if (cap % AX_CH != 0 || cap > 4096) return cudaErrorInvalidValue;
   const size_t smem = attx_scores_smem_bytes(M, H, KVH);
   if (smem > ATT_MAX_SMEM) return cudaErrorInvalidValue;
-  constexpr size_t pv_smem = sizeof(float) * 2 * AX_PV_TC * (32 + AX_PV_QG);
+  constexpr size_t pv_smem = sizeof(float) * AX_PV_NS * AX_PV_TC * (32 + AX_PV_QG);
   static std::atomic<uint64_t> attr{0};
   const cudaError_t ea = once_per_current_device(attr, [] {
     cudaError_t e = cudaFuncSetAttribute(hc_attx_scores_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -358,3 +435,11 @@ cudaError_t launch_attention_exact(const float* q, const float* kraw, const floa
 }
 
 }  // namespace hc
+
+// Test hook (not part of the public header): runs the softmax's warp-scan
+// sequential sum over n non-negative device floats into *d_out, so tests can
+// compare it with a plain sequential f32 sum on chosen inputs.
+extern "C" int hc_test_seq_sum(const float* d_v, int n, float* d_out) {
+  hc::hc_seq_sum_test_kernel<<<1, 32>>>(d_v, n, d_out);
+  return cudaDeviceSynchronize() == cudaSuccess ? 0 : 4;
+}
