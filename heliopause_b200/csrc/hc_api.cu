@@ -239,19 +239,25 @@ static int gemv_mma_min_cols() {
 
 // Exact-order launches (hc_gemvx.cu): one per group of up to 8 columns.
 static int launch_gemvx_ws(const hc::Q8Buf& q, int K, int cols, const hc::GemvSeg* segs, int nseg, int total_tiles,
-                           cudaStream_t st) {
+                           cudaStream_t st, const hc::GemvPrologue* pro = nullptr) {
   hc::GemvxParams p;
   memset(&p, 0, sizeof p);
+  if (pro) p.pro = *pro;
   for (int i = 0; i < nseg; ++i) p.seg[i] = segs[i];
   p.nseg = nseg;
   p.K = K;
   p.nb = K / 256;
   p.total_tiles = total_tiles;
   p.q = q;
-  // widest column groups whose products fit a CTA's shared memory
+  // widest column groups the warp-per-tile form takes, or whose products fit
+  // a CTA's shared memory in the split form
   int group = hc::GEMVX_MAX_COLS;
   for (; group > 1; group >>= 1) {
     hc::GemvxParams t = p;
+    t.ncols = cols < group ? cols : group;
+    int wgrid = 0;
+    if (hc::gemvw_plan(t, hc::sm_count(), &wgrid) > 0 && wgrid > 0) break;
+    t = p;
     t.ncols = cols < group ? cols : group;
     if (hc::gemvx_plan(t, hc::sm_count()) > 0) break;
   }
@@ -511,6 +517,25 @@ int hc_matmul_q8_order(size_t count, const hpc_weight* handles, const void* d_wo
   if (column_count == 0) return HPC_OK;
   hc::Q8Buf q = hc::q8buf_carve(const_cast<void*>(d_workspace), int(input_size), int(column_count));
   return launch_gemv_ws(q, int(input_size), int(column_count), segs, int(count), tiles, stream, nullptr, exact);
+}
+
+// The exact-order matmul whose input every CTA computes itself
+// (GemvPrologue: the norms of the residual stream, or the Q8_K of a
+// vector as it is): the exact decode step's QKV, O and gate/up projections
+// of width 2048, any column count up to the model's step width.
+int hc_matmul_q8_exact_prologue(size_t count, const hpc_weight* handles, const void* q8ws, size_t q8_bytes,
+                                size_t input_size, size_t column_count, float* const* d_outs, const size_t* out_lens,
+                                const hc::GemvPrologue& pro, cudaStream_t st) {
+  if (count == 0 || count > size_t(hc::GEMV_MAXSEG)) return fail(HPC_ERR_SHAPE, "matmul_q8: count %zu", count);
+  if (input_size != size_t(hc::GEMV_PRO_D) || column_count < 1 || column_count > size_t(hc::GEMVX_MAX_COLS))
+    return fail(HPC_ERR_SHAPE, "exact prologue: width %zu, %zu columns", input_size, column_count);
+  if (q8_bytes < hc::q8buf_bytes(int(input_size), int(column_count))) return fail(HPC_ERR_SHAPE, "workspace too small");
+  hc::GemvSeg segs[hc::GEMV_MAXSEG];
+  int tiles = 0;
+  int rc = build_segments(count, handles, d_outs, out_lens, input_size, column_count, segs, &tiles);
+  if (rc != HPC_OK) return rc;
+  hc::Q8Buf q = hc::q8buf_carve(const_cast<void*>(q8ws), int(input_size), int(column_count));
+  return launch_gemvx_ws(q, int(input_size), int(column_count), segs, int(count), tiles, st, &pro);
 }
 
 // hpc_matmul_q8 whose input is computed by the fused norm prologue of every

@@ -19,16 +19,26 @@
 //                          K/V rows (written to the cache), one sequential
 //                          256-term dot per (query, key);
 //   hc_attx_softmax_kernel grid (tokens x heads): the max, the f64 exps, the
-//                          4096-term sequential sum (one warp, exact
-//                          prefix scans between its binade changes), the
-//                          divisions;
+//                          one 4096-term sequential sum, the divisions;
 //   hc_attx_pv_kernel      grid (KV head x 32-dim slice, groups of 4 query
 //                          vectors): one sequential chain per (query, dim)
-//                          over all keys, then the TS f16 cast of the output
-//                          (castF16Rows, layers.ts:982-988).
+//                          over all keys, lane = dim, then the TS f16 cast of
+//                          the output (castF16Rows, layers.ts:982-988).  A
+//                          producer warp feeds a ring of 256-key stages: the
+//                          stage's V slice [256 slots][32 dims] as one 2-D
+//                          TMA tensor copy
+//                          (per-key bulk copies where the stage wraps the
+//                          slot ring) and the group's probabilities as one
+//                          bulk copy per query, completion on the stage's
+//                          mbarrier; the four chain warps do nothing but the
+//                          chain, whose dependent adds bound the kernel.
 // The Q8_K quantization of the cast output for the O projection follows as
 // its own launch.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include <cmath>
+#include <mutex>
 
 #include "hc_bulk.cuh"
 #include "hc_common.cuh"
@@ -44,9 +54,13 @@ constexpr int AX_CH = 64;            // key slots per scores CTA
 constexpr int AX_KSTRIDE = 256 + 4;  // floats per staged K row (conflict-free 16-byte reads)
 constexpr int AX_QL = 4;             // query lanes of the scores CTA (256 threads / 64 keys)
 constexpr int AX_SM_THREADS = 1024;  // softmax CTA
-constexpr int AX_PV_QG = 4;          // query vectors per PV CTA (one warp each)
-constexpr int AX_PV_TC = 256;        // keys per staged V chunk
-constexpr int AX_PV_NS = 4;          // V chunks in flight (a 4-stage ring: 96 KB of copies ahead of the chain)
+constexpr int AX_PV_QG = 4;          // query vectors per PV CTA (one chain warp each)
+constexpr int AX_PV_TC = 256;        // keys per ring stage
+constexpr int AX_PV_NS = 4;          // ring stages (three stages of copies ahead of the chain)
+constexpr int AX_PV_DS = 32;         // dims per CTA: one per lane
+constexpr int AX_PV_THREADS = 32 * (AX_PV_QG + 1);  // chain warps + the producer warp
+// floats per stage: V [TC][64], probabilities [QG][TC]
+constexpr int AX_PV_STAGE = AX_PV_TC * AX_PV_DS + AX_PV_QG * AX_PV_TC;
 
 struct KeyRange {
   int count, start, maxpos;
@@ -60,6 +74,37 @@ __device__ __forceinline__ KeyRange key_range(const int32_t* pos, int M, int cap
   r.count = min(cap, mx + 1);
   r.start = mx + 1 - r.count;
   return r;
+}
+
+// U query chains of one key (queries q0, q0 + 4, ...): each dot is the
+// reference's sequential chain over the 256 dims; the key row's 16-byte
+// pieces are read once for all U.
+template <int U>
+__device__ __forceinline__ void score_chains(const float4* __restrict__ kv, const float* __restrict__ qs, int q0,
+                                             bool key, int kpos, int j, int G, int H, int kvh, int cap, float scale,
+                                             const int32_t* __restrict__ pos, float* __restrict__ scores) {
+  float dot[U];
+#pragma unroll
+  for (int u = 0; u < U; ++u) dot[u] = 0.0f;
+#pragma unroll 4
+  for (int i4 = 0; i4 < 64; ++i4) {
+    const float4 b = kv[i4];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const float4 a = reinterpret_cast<const float4*>(qs + (q0 + AX_QL * u) * 256)[i4];
+      dot[u] = __fadd_rn(dot[u], __fmul_rn(a.x, b.x));
+      dot[u] = __fadd_rn(dot[u], __fmul_rn(a.y, b.y));
+      dot[u] = __fadd_rn(dot[u], __fmul_rn(a.z, b.z));
+      dot[u] = __fadd_rn(dot[u], __fmul_rn(a.w, b.w));
+    }
+  }
+  if (!key) return;
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+    const int qi = q0 + AX_QL * u, m = qi / G, h = kvh * G + qi % G;
+    // mask 0 where the key is visible: fround(fround(dot * scale) + 0)
+    scores[(size_t(m) * H + h) * cap + j] = kpos <= pos[m] ? __fadd_rn(__fmul_rn(dot[u], scale), 0.0f) : -INFINITY;
+  }
 }
 
 __global__ void __launch_bounds__(256) hc_attx_scores_kernel(
@@ -77,11 +122,10 @@ __global__ void __launch_bounds__(256) hc_attx_scores_kernel(
   const KeyRange kr = key_range(pos, M, cap);  // pos is set before the step starts
   const int t0 = chunk * AX_CH;
   // a slot s holds key j = (s - start) mod cap when j < count
-  bool any = false, fresh = false;
-  for (int t = 0; t < AX_CH; ++t) {
-    const int j = (t0 + t - kr.start + cap) % cap;
-    any |= j < kr.count;
-  }
+  // every slot holds a key once the ring is full; before that start = 0 and
+  // the keys are the slots below count
+  const bool any = kr.count == cap || t0 < kr.count;
+  bool fresh = false;
   for (int i = 0; i < M; ++i) {
     const int s = pos[i] % cap;
     fresh |= (s >= t0 && s < t0 + AX_CH);
@@ -161,110 +205,30 @@ __global__ void __launch_bounds__(256) hc_attx_scores_kernel(
   const bool key = j < kr.count;
   const int kpos = kr.start + j;  // absolute position of the key
   const float4* kv = reinterpret_cast<const float4*>(ks + t * AX_KSTRIDE);
-  constexpr int U = 4;  // chains per pass
-  for (int q0 = ql; q0 < NQ; q0 += AX_QL * U) {
-    float dot[U];
-#pragma unroll
-    for (int u = 0; u < U; ++u) dot[u] = 0.0f;
-#pragma unroll 2
-    for (int i4 = 0; i4 < HD / 4; ++i4) {
-      const float4 b = kv[i4];
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int qi = q0 + AX_QL * u;
-        if (qi < NQ) {
-          const float4 a = reinterpret_cast<const float4*>(qs + qi * HD)[i4];
-          dot[u] = __fadd_rn(dot[u], __fmul_rn(a.x, b.x));
-          dot[u] = __fadd_rn(dot[u], __fmul_rn(a.y, b.y));
-          dot[u] = __fadd_rn(dot[u], __fmul_rn(a.z, b.z));
-          dot[u] = __fadd_rn(dot[u], __fmul_rn(a.w, b.w));
-        }
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int qi = q0 + AX_QL * u;
-      if (qi < NQ && key) {
-        const int m = qi / G, h = kvh * G + qi % G;
-        // mask 0 where the key is visible: fround(fround(dot * scale) + 0)
-        scores[(size_t(m) * H + h) * cap + j] =
-            kpos <= pos[m] ? __fadd_rn(__fmul_rn(dot[u], scale), 0.0f) : -INFINITY;
-      }
+  // this thread's queries ql, ql + 4, ...: passes of at most 4 chains, each
+  // pass sized to the chains it really has
+  const int mine = NQ > ql ? (NQ - ql + AX_QL - 1) / AX_QL : 0;
+  for (int u0 = 0; u0 < mine; u0 += 4) {
+    const int cnt = min(4, mine - u0), q0 = ql + AX_QL * u0;
+    switch (cnt) {
+      case 1: score_chains<1>(kv, qs, q0, key, kpos, j, G, H, kvh, cap, scale, pos, scores); break;
+      case 2: score_chains<2>(kv, qs, q0, key, kpos, j, G, H, kvh, cap, scale, pos, scores); break;
+      case 3: score_chains<3>(kv, qs, q0, key, kpos, j, G, H, kvh, cap, scale, pos, scores); break;
+      default: score_chains<4>(kv, qs, q0, key, kpos, j, G, H, kvh, cap, scale, pos, scores); break;
     }
   }
 }
 
-// The sequential f32 sum  s = fround(s + v[j]), j = 0 .. n-1, s from +0, of
-// non-negative finite terms, bit for bit, by one warp (every lane returns it).
-// While the running sum stays in one binade its grid is fixed (ulp 2^e, the
-// subnormal grid 2^-149 included), s = M * 2^e with integer M < 2^24, and a
-// step adds the term rounded to that grid, k = RN(v / 2^e) -- a plain integer
-// -- so a run of steps is an integer prefix sum.  The warp takes 8 terms per
-// lane (256 in sequence order), scans the k's and commits every step up to the
-// first one whose rounding the grid does not decide: an exact tie (its
-// direction depends on the parity of the running sum) or a sum reaching the
-// next binade.  That step is done with one f32 add on the committed sum, and
-// the scan resumes after it.
-__device__ float seq_sum_nonneg_warp(const float* __restrict__ v, int n, int lane) {
-  constexpr int PER = 8;
-  float s = 0.0f;
-  int j = 0;
-  while (j < n) {
-    const uint32_t ex = (__float_as_uint(s) >> 23) & 0xffu;
-    const int e = ex <= 1u ? -149 : int(ex) - 150;  // ulp of s (and of [0, 2^-125))
-    const double M = ldexp(double(s), -e);          // the integer significand on that grid
-    const double scale = ldexp(1.0, -e);
-    const int base = j + PER * lane;
-    uint32_t k[PER];
-    double q[PER];
-    bool bad[PER];
-    uint32_t local = 0;
-#pragma unroll
-    for (int i = 0; i < PER; ++i) {
-      const int idx = base + i;
-      q[i] = idx < n ? double(v[idx]) * scale : 0.0;  // exact: a power-of-two scaling
-      const double fl = floor(q[i]);
-      bad[i] = q[i] >= 16777216.0 || q[i] - fl == 0.5;
-      k[i] = bad[i] ? 0u : uint32_t(floor(q[i] + 0.5));
-      local += k[i];
-    }
-    uint32_t incl = local;  // steps before the first non-committable one stay below 2^24
-#pragma unroll
-    for (int off = 1; off < 32; off <<= 1) {
-      const uint32_t t = __shfl_up_sync(0xffffffffu, incl, off);
-      if (lane >= off) incl += t;
-    }
-    uint32_t run = incl - local;
-    int first = PER;
-#pragma unroll
-    for (int i = 0; i < PER; ++i) {
-      if (first == PER && base + i < n) {
-        // the exact pre-rounding value on the grid: M + run + q
-        if (bad[i] || (M + double(run)) + q[i] >= 16777215.5) first = i;
-        else run += k[i];
-      }
-    }
-    const unsigned m = __ballot_sync(0xffffffffu, first < PER);
-    if (m == 0u) {
-      const uint32_t tot = __shfl_sync(0xffffffffu, incl, 31);
-      s = float(ldexp(M + double(tot), e));
-      j += 32 * PER;
-    } else {
-      const int fl_lane = __ffs(m) - 1;
-      const int fi = __shfl_sync(0xffffffffu, first, fl_lane);
-      const uint32_t committed = __shfl_sync(0xffffffffu, run, fl_lane);
-      const int idx = j + PER * fl_lane + fi;
-      s = __fadd_rn(float(ldexp(M + double(committed), e)), v[idx]);
-      j = idx + 1;
-    }
-  }
-  return s;
-}
+// The exps run in rounds of AX_SM_ROUND keys on warps 1 .. 31; a round's
+// named barrier (warps 1 .. 31 arrive, warp 0 waits) hands it to thread 0,
+// whose sequential sum then overlaps the later rounds' exps.
+constexpr int AX_SM_ROUND = AX_SM_THREADS - 32;  // 992 keys: at most 5 rounds (named barriers 1 .. 5)
+static_assert(AX_SM_ROUND % 32 == 0, "rounds of whole 32-key blocks");
 
 __global__ void __launch_bounds__(AX_SM_THREADS) hc_attx_softmax_kernel(const float* __restrict__ scores,
                                                                         const int32_t* __restrict__ pos, int M, int H,
                                                                         int cap, float* __restrict__ rprob) {
-  __shared__ float ps[4096];
+  __shared__ __align__(16) float ps[4096 + 32];  // 32 spare words: the sum's last prefetch reads past the keys
   __shared__ float red[AX_SM_THREADS / 32];
   __shared__ float s_sum;
   const int m = int(blockIdx.x) / H, h = int(blockIdx.x) % H;
@@ -286,13 +250,55 @@ __global__ void __launch_bounds__(AX_SM_THREADS) hc_attx_softmax_kernel(const fl
   __syncthreads();
   mx = -INFINITY;
   for (int w = 0; w < int(blockDim.x >> 5); ++w) mx = fmaxf(mx, red[w]);
-  for (int j = int(threadIdx.x); j < kr.count; j += int(blockDim.x)) {
-    const float s = ps[j];
-    ps[j] = s == -INFINITY ? 0.0f : float(exp(double(__fsub_rn(s, mx))));
-  }
-  __syncthreads();
-  if (threadIdx.x < 32) {  // the sequential sum (lib.rs:627-635), by one warp
-    const float sum = seq_sum_nonneg_warp(ps, kr.count, int(threadIdx.x));
+  const int rounds = (kr.count + AX_SM_ROUND - 1) / AX_SM_ROUND;
+  if (threadIdx.x >= 32) {
+    for (int r = 0; r < rounds; ++r) {
+      const int j = r * AX_SM_ROUND + int(threadIdx.x) - 32;
+      if (j < kr.count) {
+        const float s = ps[j];
+        ps[j] = s == -INFINITY ? 0.0f : float(exp(double(__fsub_rn(s, mx))));
+      }
+      asm volatile("bar.arrive %0, %1;" ::"r"(1 + r), "r"(AX_SM_THREADS) : "memory");
+    }
+  } else {
+    // warp 0: thread 0 adds round by round, one dependent add per key
+    // (lib.rs:627-635).  A round is 31 blocks of 32 keys; a block's 32 keys
+    // are loaded (as two 16-key halves, eight broadcast 16-byte reads) while
+    // the previous half is added, with no branch inside the loop.
+    float sum = 0.0f;
+    const float4* p4 = reinterpret_cast<const float4*>(ps);
+    for (int r = 0; r < rounds; ++r) {
+      asm volatile("bar.sync %0, %1;" ::"r"(1 + r), "r"(AX_SM_THREADS) : "memory");
+      if (threadIdx.x == 0) {
+        const int j0 = r * AX_SM_ROUND, j1 = min(kr.count, j0 + AX_SM_ROUND);
+        const int n32 = (j1 - j0) / 32;
+        float4 a[4], b[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) a[i] = p4[j0 / 4 + i];
+        for (int blk = 0; blk < n32; ++blk) {
+          const int q = (j0 + 32 * blk) / 4;  // float4 index of the block
+#pragma unroll
+          for (int i = 0; i < 4; ++i) b[i] = p4[q + 4 + i];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            sum = __fadd_rn(sum, a[i].x);
+            sum = __fadd_rn(sum, a[i].y);
+            sum = __fadd_rn(sum, a[i].z);
+            sum = __fadd_rn(sum, a[i].w);
+          }
+#pragma unroll
+          for (int i = 0; i < 4; ++i) a[i] = p4[q + 8 + i];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            sum = __fadd_rn(sum, b[i].x);
+            sum = __fadd_rn(sum, b[i].y);
+            sum = __fadd_rn(sum, b[i].z);
+            sum = __fadd_rn(sum, b[i].w);
+          }
+        }
+        for (int j = j0 + 32 * n32; j < j1; ++j) sum = __fadd_rn(sum, ps[j]);
+      }
+    }
     if (threadIdx.x == 0) s_sum = sum;
   }
   __syncthreads();
@@ -301,91 +307,148 @@ __global__ void __launch_bounds__(AX_SM_THREADS) hc_attx_softmax_kernel(const fl
   for (int j = int(threadIdx.x); j < kr.count; j += int(blockDim.x)) r[j] = __fdiv_rn(ps[j], sum);
 }
 
-__global__ void __launch_bounds__(32 * AX_PV_QG) hc_attx_pv_kernel(const float* __restrict__ rprob,
+// One chain warp's pass over a full stage: out += fround(r_j * v_j) key by
+// key.  Keys go in blocks of 16: the block's probabilities as four
+// broadcast 16-byte reads and its values one conflict-free word per lane,
+// all loaded before the block's adds.
+__device__ __forceinline__ float pv_stage_full(const float4* __restrict__ r4, const float* __restrict__ v, float acc) {
+#pragma unroll 4
+  for (int blk = 0; blk < AX_PV_TC / 16; ++blk) {
+    float4 pr[4];
+    float vv[16];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) pr[i] = r4[blk * 4 + i];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) vv[i] = v[(blk * 16 + i) * AX_PV_DS];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      acc = __fadd_rn(acc, __fmul_rn(pr[i].x, vv[4 * i]));
+      acc = __fadd_rn(acc, __fmul_rn(pr[i].y, vv[4 * i + 1]));
+      acc = __fadd_rn(acc, __fmul_rn(pr[i].z, vv[4 * i + 2]));
+      acc = __fadd_rn(acc, __fmul_rn(pr[i].w, vv[4 * i + 3]));
+    }
+  }
+  return acc;
+}
+
+// One 2-D TMA tile load (no multicast): box at element (x, y) of `map` into
+// this CTA's shared memory, completion on `bar`.
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// vmap: the V cache as a 2-D f32 tensor [cap slots][KVH * 256], box [256][32].
+__global__ void __launch_bounds__(AX_PV_THREADS) hc_attx_pv_kernel(const __grid_constant__ CUtensorMap vmap,
+                                                                   const float* __restrict__ rprob,
                                                                    const float* __restrict__ vc,
                                                                    const int32_t* __restrict__ pos, int M, int H,
-                                                                   int KVH, int cap, float* __restrict__ out16) {
-  extern __shared__ __align__(16) float pv_smem[];
-  float (*vs)[AX_PV_TC][32] = reinterpret_cast<float (*)[AX_PV_TC][32]>(pv_smem);  // [NS][TC][32]
-  float (*rs)[AX_PV_QG][AX_PV_TC] =
-      reinterpret_cast<float (*)[AX_PV_QG][AX_PV_TC]>(pv_smem + AX_PV_NS * AX_PV_TC * 32);  // [NS][QG][TC]
-  const int kvh = int(blockIdx.x) >> 3, ds = int(blockIdx.x) & 7, qg = int(blockIdx.y);
+                                                                   int KVH, int cap, float* __restrict__ out16,
+                                                                   int* err) {
+  extern __shared__ __align__(128) float pv_smem[];  // [NS][AX_PV_STAGE]
+  __shared__ __align__(8) uint64_t full[AX_PV_NS], empty[AX_PV_NS];
+  constexpr int SLICES = 256 / AX_PV_DS;  // dim slices per KV head
+  const int kvh = int(blockIdx.x) / SLICES, ds = int(blockIdx.x) % SLICES, qg = int(blockIdx.y);
   const int lane = int(threadIdx.x) & 31, warp = int(threadIdx.x) >> 5;
   const int G = H / KVH, NQ = M * G;
-  const int qi = qg * AX_PV_QG + warp;
+  const int nq = min(AX_PV_QG, NQ - qg * AX_PV_QG);  // query vectors of this group
   pdl_trigger();
   const KeyRange kr = key_range(pos, M, cap);
   const int nchunk = (kr.count + AX_PV_TC - 1) / AX_PV_TC;
-  pdl_wait();  // the probabilities (previous launch) and this step's V rows (two launches back)
-  auto load_chunk = [&](int c, int buf) {
-    const int j0 = c * AX_PV_TC, n = min(AX_PV_TC, kr.count - j0);
-    // V: 8 sixteen-byte pieces per key (this slice's 32 dims)
-    for (int i = int(threadIdx.x); i < n * 8; i += int(blockDim.x)) {
-      const int jj = i >> 3, pc = i & 7;
-      const int slot = (kr.start + j0 + jj) % cap;
-      cp_async16(&vs[buf][jj][4 * pc], vc + (size_t(slot) * KVH + kvh) * 256 + ds * 32 + 4 * pc);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < AX_PV_NS; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], AX_PV_QG);
     }
-    // probabilities of the group's query vectors
-    for (int i = int(threadIdx.x); i < AX_PV_QG * (AX_PV_TC / 4); i += int(blockDim.x)) {
-      const int w = i / (AX_PV_TC / 4), pc = i % (AX_PV_TC / 4);
-      const int qw = qg * AX_PV_QG + w;
-      if (qw < NQ && 4 * pc < n) {
-        const int mm = qw / G, hh = kvh * G + qw % G;
-        const float* src = rprob + (size_t(mm) * H + hh) * cap + j0 + 4 * pc;
-        if (4 * pc + 4 <= n) {
-          cp_async16(&rs[buf][w][4 * pc], src);
-        } else {
-          for (int e = 0; 4 * pc + e < n; ++e) rs[buf][w][4 * pc + e] = src[e];
+  }
+  __syncthreads();
+  pdl_wait();  // the probabilities (previous launch) and this step's V rows (two launches back)
+  if (warp == AX_PV_QG) {
+    // producer: stage c % NS holds keys [256c, 256c + n); it is refilled once
+    // the four chain warps have released it
+    int y0 = kr.start;  // slot of the stage's first key
+    int issued = 0;
+    bool ok = true;
+    for (int c = 0, s = 0, ph = 0; c < nchunk; ++c) {
+      if (c >= AX_PV_NS && !mbar_wait_parity_sleep(&empty[s], uint32_t(ph ^ 1), err)) {
+        ok = false;
+        break;
+      }
+      const int j0 = c * AX_PV_TC, n = min(AX_PV_TC, kr.count - j0);
+      const int n4 = (n + 3) & ~3;  // probability rows are padded to 16 bytes (cap is a multiple of 64)
+      float* vs = pv_smem + size_t(s) * AX_PV_STAGE;
+      float* ps = vs + AX_PV_TC * AX_PV_DS;
+      const bool wraps = y0 + n > cap;
+      // the tile load always moves the whole box (rows past cap read as zeros)
+      constexpr uint32_t ROWB = AX_PV_DS * 4;
+      const uint32_t vbytes = wraps ? uint32_t(n) * ROWB : uint32_t(AX_PV_TC) * ROWB;
+      if (lane == 0) {
+        mbar_expect_tx(&full[s], vbytes + uint32_t(nq * n4) * 4u);
+        if (!wraps) tma_load_2d(vs, &vmap, kvh * 256 + ds * AX_PV_DS, y0, &full[s]);
+      }
+      __syncwarp();
+      if (wraps) {
+        for (int jj = lane; jj < n; jj += 32) {
+          const int sl = y0 + jj < cap ? y0 + jj : y0 + jj - cap;
+          bulk_copy_g2s(vs + jj * AX_PV_DS, vc + (size_t(sl) * KVH + kvh) * 256 + ds * AX_PV_DS, ROWB, &full[s]);
         }
       }
-    }
-    cp_async_commit();
-  };
-  float acc = 0.0f;
-  // a ring of NS chunks: chunks c + 1 .. c + NS - 1 are in flight while the
-  // chain walks chunk c (one commit group per chunk, empty past the end)
-  for (int c = 0; c < AX_PV_NS - 1; ++c) {
-    if (c < nchunk) load_chunk(c, c);
-    else cp_async_commit();
-  }
-  for (int c = 0; c < nchunk; ++c) {
-    const int buf = c % AX_PV_NS;
-    if (c + AX_PV_NS - 1 < nchunk) load_chunk(c + AX_PV_NS - 1, (c + AX_PV_NS - 1) % AX_PV_NS);
-    else cp_async_commit();
-    asm volatile("cp.async.wait_group %0;" ::"n"(AX_PV_NS - 1) : "memory");
-    __syncthreads();
-    const int n = min(AX_PV_TC, kr.count - c * AX_PV_TC);
-    if (qi < NQ) {
-      const float* r = rs[buf][warp];
-      int jj = 0;
-      for (; jj + 4 <= n; jj += 4) {
-        const float4 p4 = *reinterpret_cast<const float4*>(r + jj);
-        acc = __fadd_rn(acc, __fmul_rn(p4.x, vs[buf][jj][lane]));
-        acc = __fadd_rn(acc, __fmul_rn(p4.y, vs[buf][jj + 1][lane]));
-        acc = __fadd_rn(acc, __fmul_rn(p4.z, vs[buf][jj + 2][lane]));
-        acc = __fadd_rn(acc, __fmul_rn(p4.w, vs[buf][jj + 3][lane]));
+      y0 += AX_PV_TC;
+      if (y0 >= cap) y0 -= cap;
+      if (lane < nq) {
+        const int qw = qg * AX_PV_QG + lane, mm = qw / G, hh = kvh * G + qw % G;
+        bulk_copy_g2s(ps + lane * AX_PV_TC, rprob + (size_t(mm) * H + hh) * cap + j0, uint32_t(n4) * 4u, &full[s]);
       }
-      for (; jj < n; ++jj) acc = __fadd_rn(acc, __fmul_rn(r[jj], vs[buf][jj][lane]));
+      ++issued;
+      if (++s == AX_PV_NS) {
+        s = 0;
+        ph ^= 1;
+      }
     }
-    __syncthreads();  // the buffer is refilled NS - 1 chunks later
+    if (!ok)  // let the copies in flight land before the CTA exits
+      for (int c = max(0, issued - AX_PV_NS); c < issued; ++c)
+        mbar_wait_parity(&full[c % AX_PV_NS], uint32_t(c / AX_PV_NS) & 1u, nullptr);
+    return;
   }
-  if (qi < NQ) {
-    const int m = qi / G, h = kvh * G + qi % G;
-    out16[(size_t(m) * H + h) * 256 + ds * 32 + lane] = round_f16_ts(acc);
+  // chain warps: query vector qg * 4 + warp, lane = dim ds * 32 + lane
+  const bool active = warp < nq;
+  float acc = 0.0f;
+  bool ok = true;
+  for (int c = 0, s = 0, ph = 0; c < nchunk; ++c) {
+    if (ok && !mbar_wait_parity_sleep(&full[s], uint32_t(ph), err)) ok = false;
+    if (ok && active) {
+      const float* vs = pv_smem + size_t(s) * AX_PV_STAGE;
+      const float* r = vs + AX_PV_TC * AX_PV_DS + warp * AX_PV_TC;
+      const int n = min(AX_PV_TC, kr.count - c * AX_PV_TC);
+      if (n == AX_PV_TC) {
+        acc = pv_stage_full(reinterpret_cast<const float4*>(r), vs + lane, acc);
+      } else {
+        for (int jj = 0; jj < n; ++jj) acc = __fadd_rn(acc, __fmul_rn(r[jj], vs[jj * AX_PV_DS + lane]));
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+    if (++s == AX_PV_NS) {
+      s = 0;
+      ph ^= 1;
+    }
+  }
+  if (active) {
+    const int qi = qg * AX_PV_QG + warp, m = qi / G, h = kvh * G + qi % G;
+    out16[(size_t(m) * H + h) * 256 + ds * AX_PV_DS + lane] = round_f16_ts(acc);
   }
 }
 
 }  // namespace
 
-__global__ void hc_seq_sum_test_kernel(const float* v, int n, float* out) {
-  const float s = seq_sum_nonneg_warp(v, n, int(threadIdx.x));
-  if (threadIdx.x == 0) *out = s;
-}
-
 size_t attx_scores_smem_bytes(int M, int H, int KVH) {
   return sizeof(float) * (size_t(AX_CH) * AX_KSTRIDE + size_t(M) * (H / KVH) * 256);
 }
 
+// scores [M][H][cap], then the probabilities [M][H][cap]
 size_t attx_scratch_floats(int M, int H, int cap) { return 2 * size_t(M) * H * cap; }
 
 template <typename... KArgs, typename... Args>
@@ -404,6 +467,28 @@ static cudaError_t pdl_launch_x(void (*kernel)(KArgs...), dim3 grid, dim3 block,
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
+// cuTensorMapEncodeTiled through the runtime's driver entry point (the
+// library does not link the driver library itself).
+static cudaError_t encode_v_map(CUtensorMap* map, const float* vc, int KVH, int cap) {
+  static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+  static cudaError_t got = cudaSuccess;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q{};
+    got = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", reinterpret_cast<void**>(&encode), cudaEnableDefault, &q);
+    if (got == cudaSuccess && (q != cudaDriverEntryPointSuccess || !encode)) got = cudaErrorSymbolNotFound;
+  });
+  if (got != cudaSuccess) return got;
+  const cuuint64_t dims[2] = {cuuint64_t(KVH) * 256, cuuint64_t(cap)};
+  const cuuint64_t strides[1] = {cuuint64_t(KVH) * 256 * sizeof(float)};
+  const cuuint32_t box[2] = {AX_PV_DS, AX_PV_TC};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(vc), dims, strides, box, estr,
+                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
 cudaError_t launch_attention_exact(const float* q, const float* kraw, const float* vraw, const float* qnw,
                                    const float* knw, const double* cos_t, const double* sin_t, double eps, bool own_kv,
                                    float* kc, float* vc, const int32_t* pos, int M, int H, int KVH, int cap,
@@ -411,7 +496,7 @@ cudaError_t launch_attention_exact(const float* q, const float* kraw, const floa
   if (cap % AX_CH != 0 || cap > 4096) return cudaErrorInvalidValue;
   const size_t smem = attx_scores_smem_bytes(M, H, KVH);
   if (smem > ATT_MAX_SMEM) return cudaErrorInvalidValue;
-  constexpr size_t pv_smem = sizeof(float) * AX_PV_NS * AX_PV_TC * (32 + AX_PV_QG);
+  constexpr size_t pv_smem = sizeof(float) * AX_PV_NS * AX_PV_STAGE;
   static std::atomic<uint64_t> attr{0};
   const cudaError_t ea = once_per_current_device(attr, [] {
     cudaError_t e = cudaFuncSetAttribute(hc_attx_scores_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -430,16 +515,13 @@ cudaError_t launch_attention_exact(const float* q, const float* kraw, const floa
   e = pdl_launch_x(hc_attx_softmax_kernel, dim3(M * H), dim3(AX_SM_THREADS), 0, st, scores, pos, M, H, cap, rprob);
   if (e != cudaSuccess) return e;
   const int NQ = M * (H / KVH);
-  return pdl_launch_x(hc_attx_pv_kernel, dim3(KVH * 8, (NQ + AX_PV_QG - 1) / AX_PV_QG), dim3(32 * AX_PV_QG), pv_smem,
-                      st, rprob, vc, pos, M, H, KVH, cap, out16);
+  CUtensorMap vmap;
+  e = encode_v_map(&vmap, vc, KVH, cap);
+  if (e != cudaSuccess) return e;
+  return pdl_launch_x(hc_attx_pv_kernel, dim3(KVH * (256 / AX_PV_DS), (NQ + AX_PV_QG - 1) / AX_PV_QG),
+                      dim3(AX_PV_THREADS), pv_smem,
+                      st, vmap, rprob, vc, pos, M, H, KVH, cap, out16, device_status_word());
 }
 
 }  // namespace hc
 
-// Test hook (not part of the public header): runs the softmax's warp-scan
-// sequential sum over n non-negative device floats into *d_out, so tests can
-// compare it with a plain sequential f32 sum on chosen inputs.
-extern "C" int hc_test_seq_sum(const float* d_v, int n, float* d_out) {
-  hc::hc_seq_sum_test_kernel<<<1, 32>>>(d_v, n, d_out);
-  return cudaDeviceSynchronize() == cudaSuccess ? 0 : 4;
-}

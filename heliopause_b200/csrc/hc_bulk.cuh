@@ -55,19 +55,35 @@ __device__ __forceinline__ bool mbar_wait_parity(uint64_t* bar, uint32_t parity,
 }
 
 // mbar_wait_parity for waits that are expected to last (a weight unit still
-// in flight): each try_wait may suspend the warp for up to SLEEP_HINT_NS
+// in flight): every try_wait may suspend the warp for up to SLEEP_HINT_NS
 // until the phase completes, so a waiting warp does not take issue slots
-// from the warps that are computing.  Same bound and status as above.
-constexpr unsigned SLEEP_HINT_NS = 20000;
+// from the warps that are computing (a plain try_wait loop spins).  Same
+// bound and status as above.
+constexpr unsigned SLEEP_HINT_NS = 1000;
 __device__ __forceinline__ bool mbar_wait_parity_sleep(uint64_t* bar, uint32_t parity, int* err) {
-  uint32_t ok;
-  asm volatile(
-      "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3; selp.u32 %0, 1, 0, p; }"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity), "r"(SLEEP_HINT_NS)
-      : "memory");
-  if (ok) return true;
-  return mbar_wait_parity(bar, parity, err);
+  unsigned long long t0 = 0;
+  for (int it = 0;; ++it) {
+    uint32_t ok;
+    asm volatile(
+        "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3; selp.u32 %0, 1, 0, p; }"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(SLEEP_HINT_NS)
+        : "memory");
+    if (ok) return true;
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    if (it == 0) {
+      t0 = t;
+    } else if (t - t0 > WAIT_LIMIT_NS) {
+      if (err) atomicExch(err, DEVICE_ERR_TIMEOUT);
+      return false;
+    }
+  }
+}
+
+// A plain arrival (count 1) on an mbarrier of this CTA.
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("{ .reg .b64 st; mbarrier.arrive.shared::cta.b64 st, [%0]; }" ::"r"(smem_u32(bar)) : "memory");
 }
 
 // dst, src, bytes: multiples of 16.

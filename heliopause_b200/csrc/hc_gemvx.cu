@@ -27,12 +27,15 @@
 // memory (every lane reads the same record words; they stay in L1/L2).
 #include <cooperative_groups.h>
 
+#include <cstdlib>
+
 #include "hc_bulk.cuh"
 #include "hc_common.cuh"
 #include "hc_decmath.cuh"
 #include "hc_exact.cuh"
 #include "hc_gemv_body.cuh"
 #include "hc_kernels.cuh"
+#include "hc_q8.cuh"
 
 namespace cg = cooperative_groups;
 
@@ -69,6 +72,58 @@ __host__ __device__ inline size_t gx_smem_bytes(const GemvxParams& p) {
          gx_act_bytes(p);
 }
 
+// The prologue (after the wait): warp w holds 256-block w of the width-2048
+// input (lane L: elements 256w + 8L .. +7), as hc_norm_quant_kernel does, and
+// every step rounds as there: for each column, RESID_NORM h = x +
+// f32((y * s_y) * w_post) (CTA 0 stores h to x_out), NORM / RESID_NORM
+// n = f32((h * s_h) * w_pre) with s = 1 / sqrt(sum of squares / D + eps) in
+// f64, QUANT n = x; then the blocks of this CTA's part are quantized to Q8_K
+// straight into its shared-memory records.
+__device__ __forceinline__ void gx_prologue(const GemvxParams& p, uint8_t* act_a, uint8_t* act_b, int rank, int warp,
+                                            int lane) {
+  __shared__ double scratch[GX_WARPS];
+  constexpr int D = GEMV_PRO_D;
+  const GemvPrologue& pro = p.pro;
+  const int e0 = warp * 256 + 8 * lane;
+  float wq[8], wp[8];
+  if (pro.mode != GEMV_PRO_QUANT) load8(pro.w_pre + e0, wq);
+  if (pro.mode == GEMV_PRO_RESID_NORM) load8(pro.w_post + e0, wp);
+  for (int c = 0; c < p.ncols; ++c) {
+    const size_t col = size_t(p.col0 + c) * D;
+    float h[8];
+    load8(pro.x + col + e0, h);
+    if (pro.mode == GEMV_PRO_RESID_NORM) {
+      float y[8];
+      load8(pro.y + col + e0, y);
+      double ss = 0.0;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ss += double(y[i]) * double(y[i]);
+      ss = block_sum_d(ss, scratch, GX_WARPS);
+      const double sc = 1.0 / sqrt(ss / double(D) + pro.eps);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) h[i] = h[i] + float((double(y[i]) * sc) * double(wp[i]));
+      if (blockIdx.x == 0) {
+        float4* xo = reinterpret_cast<float4*>(pro.x_out + col + e0);
+        xo[0] = make_float4(h[0], h[1], h[2], h[3]);
+        xo[1] = make_float4(h[4], h[5], h[6], h[7]);
+      }
+    }
+    if (pro.mode != GEMV_PRO_QUANT) {
+      double ss = 0.0;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ss += double(h[i]) * double(h[i]);
+      ss = block_sum_d(ss, scratch, GX_WARPS);
+      const double sc = 1.0 / sqrt(ss / double(D) + pro.eps);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) h[i] = float((double(h[i]) * sc) * double(wq[i]));
+    }
+    const int jb = warp - rank * p.nbc;
+    if (jb >= 0 && jb < p.nbc)
+      q8k_block_warp(h, lane, nullptr, act_a + (size_t(c) * p.nbc + jb) * Q8A_REC,
+                     act_b + (size_t(c) * p.nbc + jb) * Q8B_REC);
+  }
+}
+
 template <int NC>
 __global__ void __launch_bounds__(GX_THREADS, 1) hc_gemvx_kernel(const __grid_constant__ GemvxParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
@@ -90,26 +145,41 @@ __global__ void __launch_bounds__(GX_THREADS, 1) hc_gemvx_kernel(const __grid_co
   __shared__ __align__(8) uint64_t act_bar;
   uint64_t* wb = bars + warp * R;
 
-  // unit u of this warp: tile (u / bpw) of the cluster's list, local block warp + 8 * (u % bpw)
-  auto issue = [&](int u) {
-    const int tile = cid + (u / bpw) * ncl;
-    const int b = rank * p.nbc + warp + GX_WARPS * (u % bpw);
+  // unit u of this warp: tile (u / bpw) of the cluster's list, local block
+  // warp + 8 * (u % bpw), ring slot u % R; the issue side walks them with
+  // counters (lane 0 only)
+  int is_i = 0, is_k = 0, is_s = 0;
+  auto issue_next = [&]() {
+    const int tile = cid + is_i * ncl;
+    const int b = rank * p.nbc + warp + GX_WARPS * is_k;
     const GemvSeg& sg = p.seg[gx_seg_of(p, tile)];
     const uint32_t ub = uint32_t(unit_bytes(sg.type));
-    uint64_t* bar = wb + (u % R);
+    uint64_t* bar = wb + is_s;
     mbar_expect_tx(bar, ub);
-    bulk_copy_g2s(ring + size_t(u % R) * p.slot, sg.w + (size_t(tile - sg.tile_begin) * p.nb + b) * ub, ub, bar);
+    bulk_copy_g2s(ring + size_t(is_s) * p.slot, sg.w + (size_t(tile - sg.tile_begin) * p.nb + b) * ub, ub, bar);
+    if (++is_k == bpw) {
+      is_k = 0;
+      ++is_i;
+    }
+    if (++is_s == R) is_s = 0;
   };
   const int primed = n < R ? n : R;
   if (lane == 0) {
     for (int s = 0; s < R; ++s) mbar_init(wb + s, 1);
-    for (int u = 0; u < primed; ++u) issue(u);
+    for (int u = 0; u < primed; ++u) issue_next();
   }
   __syncwarp();
   pdl_wait();  // the activation records are written by the previous kernel
   // this CTA's activation records (blocks [rank * nbc, (rank + 1) * nbc) of
-  // every column), one bulk copy per column and plane
-  if (threadIdx.x == 0) {
+  // every column): computed by the prologue, or one bulk copy per column and
+  // plane of the records the previous kernel wrote
+  if (p.pro.mode != GEMV_PRO_NONE) {
+    gx_prologue(p, act_a, act_b, rank, warp, lane);
+    if (threadIdx.x == 0) {  // the wait below then passes at once
+      mbar_init(&act_bar, 1);
+      asm volatile("{ .reg .b64 st; mbarrier.arrive.shared::cta.b64 st, [%0]; }" ::"r"(smem_u32(&act_bar)) : "memory");
+    }
+  } else if (threadIdx.x == 0) {
     mbar_init(&act_bar, 1);
     mbar_expect_tx(&act_bar, uint32_t(gx_act_bytes(p)));
     for (int c = 0; c < p.ncols; ++c) {
@@ -123,6 +193,8 @@ __global__ void __launch_bounds__(GX_THREADS, 1) hc_gemvx_kernel(const __grid_co
   __syncthreads();
   bool ok = mbar_wait_parity(&act_bar, 0, p.err);
   int issued = primed;
+  int rs = 0;         // ring slot of the next unit consumed
+  uint32_t rph = 0;   // its phase parity
   for (int i = 0; i < ntl; ++i) {
     const int tile = cid + i * ncl;
     const GemvSeg& sg = p.seg[gx_seg_of(p, tile)];
@@ -130,10 +202,10 @@ __global__ void __launch_bounds__(GX_THREADS, 1) hc_gemvx_kernel(const __grid_co
     float* pbuf = prod + size_t(i & 1) * pstride;
     for (int k = 0; k < bpw; ++k) {
       const int u = i * bpw + k;
-      if (ok && !mbar_wait_parity_sleep(wb + (u % R), uint32_t(u / R) & 1u, p.err)) ok = false;
+      if (ok && !mbar_wait_parity_sleep(wb + rs, rph, p.err)) ok = false;
       const int jb = warp + GX_WARPS * k;  // block inside this CTA's part
       if (ok) {
-        const uint8_t* unit = ring + size_t(u % R) * p.slot;
+        const uint8_t* unit = ring + size_t(rs) * p.slot;
         const SmemSrc src{reinterpret_cast<const uint4*>(unit) + lane,
                           reinterpret_cast<const uint16_t*>(unit + Q6K_DPLANE_OFFSET) + lane};
         float* pb = pbuf + size_t(jb) * p.ncols * GX_PROD + lane;
@@ -172,8 +244,12 @@ __global__ void __launch_bounds__(GX_THREADS, 1) hc_gemvx_kernel(const __grid_co
       }
       __syncwarp();  // every lane has read the slot: refill it
       if (u + R < n) {
-        if (ok && lane == 0) issue(u + R);
+        if (ok && lane == 0) issue_next();
         if (ok) ++issued;
+      }
+      if (++rs == R) {
+        rs = 0;
+        rph ^= 1u;
       }
     }
     // every part's products of this tile are in place
@@ -186,16 +262,20 @@ __global__ void __launch_bounds__(GX_THREADS, 1) hc_gemvx_kernel(const __grid_co
       float* f = fin + size_t(i & 1) * fstride;
       const float* pb = prod + size_t(i & 1) * pstride;
       if (ok) {
+        const int bstride = p.ncols * GX_PROD;  // floats between consecutive blocks' products
         for (int c = 0; c < p.ncols; ++c) {
           for (int kk = warp; kk < 9; kk += GX_WARPS) {
             float acc = 0.0f;
             const float* base = pb + (size_t(c) * 9 + kk) * 32 + lane;
+            for (int r = 0; r < C; ++r) {  // blocks in row order: rank by rank
+              const float* src = r == 0 ? base : cg::this_cluster().map_shared_rank(base, r);
+              if (kk < 8) {
 #pragma unroll 8
-            for (int b = 0; b < p.nb; ++b) {
-              const int r = b / p.nbc, jb = b - r * p.nbc;
-              const float* src = base + size_t(jb) * p.ncols * GX_PROD;
-              if (C > 1 && r != 0) src = cg::this_cluster().map_shared_rank(src, r);
-              acc = kk < 8 ? __fadd_rn(acc, *src) : __fsub_rn(acc, *src);
+                for (int jb = 0; jb < p.nbc; ++jb) acc = __fadd_rn(acc, src[jb * bstride]);
+              } else {
+#pragma unroll 8
+                for (int jb = 0; jb < p.nbc; ++jb) acc = __fsub_rn(acc, src[jb * bstride]);
+              }
             }
             f[(c * 9 + kk) * 32 + lane] = acc;
           }
@@ -219,7 +299,296 @@ __global__ void __launch_bounds__(GX_THREADS, 1) hc_gemvx_kernel(const __grid_co
     for (int u = n < issued ? n : issued, v = 0; v < u; ++v) mbar_wait_parity(wb + (v % R), uint32_t(v / R) & 1u, nullptr);
 }
 
+// ---- warp-per-tile form (rows of at most GW_MAX_NB blocks) -----------------
+//
+// A warp owns one (tile, column group) work item and walks the tile's nb
+// blocks in order itself, the reference's nine accumulators of each of its
+// columns in registers (LaneChain): no product buffer, no barrier, no chain
+// phase.  Units stream through the warp's own ring of R slots (one bulk copy
+// each, issued before griddepcontrol.wait for the first R units); the CTA's
+// activation records (every column, every block) are staged once.  Work
+// items go to warps round-robin over the CTAs first (item i -> CTA i mod
+// grid), so a launch with few tiles still spreads over the SMs.
+constexpr int GW_MAX_NB = 16;
+
+__host__ __device__ inline size_t gw_smem_bytes(const GemvxParams& p) {
+  return size_t(GX_WARPS) * p.R * p.slot + gx_act_bytes(p);
+}
+
+template <int NC>
+__global__ void __launch_bounds__(GX_THREADS, 1) hc_gemvw_kernel(const __grid_constant__ GemvxParams p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ __align__(8) uint64_t bars[GX_WARPS * GX_MAX_R];
+  __shared__ __align__(8) uint64_t act_bar;
+  const int lane = int(threadIdx.x) & 31, warp = int(threadIdx.x) >> 5;
+  pdl_trigger();
+  const int R = p.R, nb = p.nb;
+  const int ngroups = (p.ncols + NC - 1) / NC;  // column groups of NC columns
+  const int nitems = p.total_tiles * ngroups;   // item = tile * ngroups + group
+  const int gw = warp * int(gridDim.x) + int(blockIdx.x), nw = GX_WARPS * int(gridDim.x);
+  const int nmine = gw < nitems ? (nitems - 1 - gw) / nw + 1 : 0;
+  const int n = nmine * nb;  // this warp's units
+  uint8_t* ring = smem + size_t(warp) * R * p.slot;
+  uint8_t* act_a = smem + size_t(GX_WARPS) * R * p.slot;                          // [ncols][nb][288]
+  uint8_t* act_b = act_a + ((p.planes & 1) ? size_t(p.ncols) * nb * Q8A_REC : 0);  // [ncols][nb][304]
+  uint64_t* wb = bars + warp * R;
+
+  // issue side (lane 0): unit (item, block b) into slot s
+  int is_item = gw, is_tile = gw / ngroups, is_b = 0, is_s = 0;
+  auto issue_next = [&]() {
+    const GemvSeg& sg = p.seg[gx_seg_of(p, is_tile)];
+    const uint32_t ub = uint32_t(unit_bytes(sg.type));
+    uint64_t* bar = wb + is_s;
+    mbar_expect_tx(bar, ub);
+    bulk_copy_g2s(ring + size_t(is_s) * p.slot, sg.w + (size_t(is_tile - sg.tile_begin) * nb + is_b) * ub, ub, bar);
+    if (++is_b == nb) {
+      is_b = 0;
+      is_item += nw;
+      is_tile = is_item / ngroups;
+    }
+    if (++is_s == R) is_s = 0;
+  };
+  const int primed = n < R ? n : R;
+  if (lane == 0) {
+    for (int s = 0; s < R; ++s) mbar_init(wb + s, 1);
+    for (int u = 0; u < primed; ++u) issue_next();
+  }
+  __syncwarp();
+  pdl_wait();  // the activation records are written by the previous kernel
+  if (p.pro.mode != GEMV_PRO_NONE) {
+    gx_prologue(p, act_a, act_b, 0, warp, lane);
+    if (threadIdx.x == 0) {
+      mbar_init(&act_bar, 1);
+      mbar_arrive(&act_bar);
+    }
+  } else if (threadIdx.x == 0) {
+    mbar_init(&act_bar, 1);
+    mbar_expect_tx(&act_bar, uint32_t(gx_act_bytes(p)));
+    for (int c = 0; c < p.ncols; ++c) {
+      const size_t rec0 = size_t(p.col0 + c) * nb;
+      if (p.planes & 1)
+        bulk_copy_g2s(act_a + size_t(c) * nb * Q8A_REC, p.q.a + rec0 * Q8A_REC, uint32_t(nb * Q8A_REC), &act_bar);
+      if (p.planes & 2)
+        bulk_copy_g2s(act_b + size_t(c) * nb * Q8B_REC, p.q.b + rec0 * Q8B_REC, uint32_t(nb * Q8B_REC), &act_bar);
+    }
+  }
+  __syncthreads();
+  bool ok = mbar_wait_parity(&act_bar, 0, p.err);
+  int issued = primed, u = 0, rs = 0;
+  uint32_t rph = 0;
+  for (int it = 0; it < nmine; ++it) {
+    const int item = gw + it * nw;
+    const int tile = item / ngroups, c0 = (item - tile * ngroups) * NC;
+    const GemvSeg& sg = p.seg[gx_seg_of(p, tile)];
+    const bool q4 = sg.type == TYPE_Q4_K;
+    LaneChain ch[NC];
+#pragma unroll
+    for (int c = 0; c < NC; ++c) ch[c].zero();
+    for (int b = 0; b < nb; ++b, ++u) {
+      if (ok && !mbar_wait_parity_sleep(wb + rs, rph, p.err)) ok = false;
+      if (ok) {
+        const uint8_t* unit = ring + size_t(rs) * p.slot;
+        const SmemSrc src{reinterpret_cast<const uint4*>(unit) + lane,
+                          reinterpret_cast<const uint16_t*>(unit + Q6K_DPLANE_OFFSET) + lane};
+        if (q4) {
+          const Q4KHeader hd = q4k_header(src.chunk(0));
+#pragma unroll
+          for (int c = 0; c < NC; ++c) {
+            if (c0 + c < p.ncols) {
+              const uint8_t* rec = act_a + (size_t(c0 + c) * nb + b) * Q8A_REC;
+              BlockInts bi;
+              q4k_lanes(src, hd, rec, bi);
+              const float d8 = *reinterpret_cast<const float*>(rec + Q8A_D);
+              ch[c].add_block(bi, __fmul_rn(hd.d, d8), __fmul_rn(hd.dmin, d8), true);
+            }
+          }
+        } else {
+          const float dw = f16_bits_to_f32(src.dbits());
+#pragma unroll
+          for (int c = 0; c < NC; ++c) {
+            if (c0 + c < p.ncols) {
+              const uint8_t* rec = act_b + (size_t(c0 + c) * nb + b) * Q8B_REC;
+              BlockInts bi;
+              q6k_lanes(src, rec, bi);
+              ch[c].add_block(bi, __fmul_rn(dw, *reinterpret_cast<const float*>(rec + Q8B_D)), 0.0f, false);
+            }
+          }
+        }
+      }
+      __syncwarp();  // every lane has read the slot: refill it
+      if (u + R < n && ok) {
+        if (lane == 0) issue_next();
+        ++issued;
+      }
+      if (++rs == R) {
+        rs = 0;
+        rph ^= 1u;
+      }
+    }
+    if (ok) {
+      const int row = (tile - sg.tile_begin) * TILE + lane;
+      if (row < sg.rows) {
+#pragma unroll
+        for (int c = 0; c < NC; ++c)
+          if (c0 + c < p.ncols) sg.out[size_t(p.col0 + c0 + c) * sg.rows + row] = ch[c].total(q4);
+      }
+    }
+  }
+  if (!ok)
+    for (int v = 0; v < issued; ++v) mbar_wait_parity(wb + (v % R), uint32_t(v / R) & 1u, nullptr);
+}
+
+// ---- relay form (long rows: nb = 8 * NBP blocks) ------------------------------
+//
+// One CTA per (tile, column): warp w owns blocks [w * NBP, (w + 1) * NBP) of
+// the row, streams its NBP units through its ring and parks the reference's
+// nine f32 products of each block (d * aux32[l], dmin * sumi) in its own
+// shared-memory slab prod[w][NBP][9][32] (the block loop stays rolled: one
+// copy of the block decode keeps the kernel inside the instruction cache).
+// The nine accumulators then pass from warp to warp in block order through
+// shared memory (relay[w][9][32], one mbarrier per hop): warp w adds its
+// products to what warp w - 1 handed over, exactly the reference's
+// sequential block loop, and warp 7 writes the row total.  Only the hops are
+// serial; the integer work of all 8 * NBP blocks runs in parallel.
+constexpr int GR_PARTS = GX_WARPS;
+
+__host__ __device__ inline size_t gr_act_bytes(const GemvxParams& p) {
+  return size_t(p.nb) * (((p.planes & 1) ? Q8A_REC : 0) + ((p.planes & 2) ? Q8B_REC : 0));
+}
+__host__ __device__ inline size_t gr_smem_bytes(const GemvxParams& p) {
+  return size_t(GR_PARTS) * p.R * p.slot + gr_act_bytes(p) + size_t(GR_PARTS) * GX_PROD * sizeof(float) +
+         size_t(GR_PARTS) * (p.nb / GR_PARTS) * GX_PROD * sizeof(float);
+}
+constexpr int GR_MAX_SMEM = 220 * 1024;
+
+template <int NBP>
+__global__ void __launch_bounds__(GX_THREADS, 1) hc_gemvr_kernel(const __grid_constant__ GemvxParams p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ __align__(8) uint64_t bars[GX_WARPS * GX_MAX_R];
+  __shared__ __align__(8) uint64_t act_bar;
+  __shared__ __align__(8) uint64_t hop[GR_PARTS];
+  const int lane = int(threadIdx.x) & 31, warp = int(threadIdx.x) >> 5;
+  pdl_trigger();
+  const int R = p.R, nb = p.nb;
+  const int tile = int(blockIdx.x) / p.ncols, c = int(blockIdx.x) - tile * p.ncols;
+  const GemvSeg& sg = p.seg[gx_seg_of(p, tile)];
+  const bool q4 = sg.type == TYPE_Q4_K;
+  const uint32_t ub = uint32_t(unit_bytes(sg.type));
+  const uint8_t* wtile = sg.w + size_t(tile - sg.tile_begin) * nb * ub;
+  uint8_t* ring = smem + size_t(warp) * R * p.slot;
+  uint8_t* act_a = smem + size_t(GR_PARTS) * R * p.slot;              // [nb][288]
+  uint8_t* act_b = act_a + ((p.planes & 1) ? size_t(nb) * Q8A_REC : 0);  // [nb][304]
+  float* relay = reinterpret_cast<float*>(act_a + gr_act_bytes(p));      // [8][9][32]
+  float* prod = relay + GR_PARTS * GX_PROD + size_t(warp) * NBP * GX_PROD + lane;  // this warp's [NBP][9][32]
+  uint64_t* wb = bars + warp * R;
+  const int b0 = warp * NBP;
+  if (lane == 0) {
+    for (int s = 0; s < R; ++s) mbar_init(wb + s, 1);
+    for (int k = 0; k < R && k < NBP; ++k) {
+      mbar_expect_tx(wb + k, ub);
+      bulk_copy_g2s(ring + size_t(k) * p.slot, wtile + size_t(b0 + k) * ub, ub, wb + k);
+    }
+  }
+  if (threadIdx.x == 0)
+    for (int w = 0; w < GR_PARTS; ++w) mbar_init(&hop[w], 32);
+  __syncwarp();
+  pdl_wait();  // the activation records are written by the previous kernel
+  if (threadIdx.x == 0) {
+    mbar_init(&act_bar, 1);
+    mbar_expect_tx(&act_bar, uint32_t(gr_act_bytes(p)));
+    const size_t rec0 = size_t(p.col0 + c) * nb;
+    if (p.planes & 1) bulk_copy_g2s(act_a, p.q.a + rec0 * Q8A_REC, uint32_t(nb * Q8A_REC), &act_bar);
+    if (p.planes & 2) bulk_copy_g2s(act_b, p.q.b + rec0 * Q8B_REC, uint32_t(nb * Q8B_REC), &act_bar);
+  }
+  __syncthreads();
+  bool ok = mbar_wait_parity(&act_bar, 0, p.err);
+  int issued = R < NBP ? R : NBP;
+  int rs = 0;
+  uint32_t rph = 0;
+#pragma unroll 1
+  for (int k = 0; k < NBP; ++k) {
+    if (ok && !mbar_wait_parity_sleep(wb + rs, rph, p.err)) ok = false;
+    const int b = b0 + k;
+    if (ok) {
+      const uint8_t* unit = ring + size_t(rs) * p.slot;
+      const SmemSrc src{reinterpret_cast<const uint4*>(unit) + lane,
+                        reinterpret_cast<const uint16_t*>(unit + Q6K_DPLANE_OFFSET) + lane};
+      BlockInts bi;
+      float d, dm = 0.0f;
+      if (q4) {
+        const Q4KHeader hd = q4k_header(src.chunk(0));
+        const uint8_t* rec = act_a + size_t(b) * Q8A_REC;
+        q4k_lanes(src, hd, rec, bi);
+        const float d8 = *reinterpret_cast<const float*>(rec + Q8A_D);
+        d = __fmul_rn(hd.d, d8);
+        dm = __fmul_rn(hd.dmin, d8);
+      } else {
+        const uint8_t* rec = act_b + size_t(b) * Q8B_REC;
+        q6k_lanes(src, rec, bi);
+        d = __fmul_rn(f16_bits_to_f32(src.dbits()), *reinterpret_cast<const float*>(rec + Q8B_D));
+      }
+      float* pk = prod + k * GX_PROD;
+#pragma unroll
+      for (int l = 0; l < 8; ++l) pk[l * 32] = __fmul_rn(d, float(bi.aux[l]));
+      pk[8 * 32] = __fmul_rn(dm, float(bi.msum));
+    }
+    __syncwarp();  // every lane has read the slot: refill it
+    if (k + R < NBP && ok) {
+      if (lane == 0) {
+        mbar_expect_tx(wb + rs, ub);
+        bulk_copy_g2s(ring + size_t(rs) * p.slot, wtile + size_t(b + R) * ub, ub, wb + rs);
+      }
+      ++issued;
+    }
+    if (++rs == R) {
+      rs = 0;
+      rph ^= 1u;
+    }
+  }
+  // the relay: the accumulators after blocks 0 .. b0 - 1 come from warp - 1
+  float acc[9];
+#pragma unroll
+  for (int l = 0; l < 9; ++l) acc[l] = 0.0f;
+  if (warp > 0) {
+    if (ok && !mbar_wait_parity_sleep(&hop[warp], 0, p.err)) ok = false;
+#pragma unroll
+    for (int l = 0; l < 9; ++l) acc[l] = relay[(warp * 9 + l) * 32 + lane];
+  }
+#pragma unroll
+  for (int k = 0; k < NBP; ++k) {  // each lane reads back only its own words
+    const float* pk = prod + k * GX_PROD;
+#pragma unroll
+    for (int l = 0; l < 8; ++l) acc[l] = __fadd_rn(acc[l], pk[l * 32]);
+    if (q4) acc[8] = __fsub_rn(acc[8], pk[8 * 32]);
+  }
+  if (warp + 1 < GR_PARTS) {
+#pragma unroll
+    for (int l = 0; l < 9; ++l) relay[((warp + 1) * 9 + l) * 32 + lane] = acc[l];
+    mbar_arrive(&hop[warp + 1]);  // each lane releases its own words
+  } else if (ok) {
+    float t = 0.0f;
+#pragma unroll
+    for (int l = 0; l < 8; ++l) t = __fadd_rn(t, acc[l]);
+    const float v = q4 ? __fadd_rn(acc[8], t) : t;
+    const int row = (tile - sg.tile_begin) * TILE + lane;
+    if (row < sg.rows) sg.out[size_t(p.col0 + c) * sg.rows + row] = v;
+  }
+  if (!ok)
+    for (int v = 0; v < issued; ++v) mbar_wait_parity(wb + (v % R), uint32_t(v / R) & 1u, nullptr);
+}
+
 }  // namespace
+
+// HPC_GEMVX_SPLIT=1 keeps every launch on the split (cluster) form, for
+// comparing the two forms.
+static bool gemvx_force_split() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("HPC_GEMVX_SPLIT");
+    v = e && atoi(e) != 0 ? 1 : 0;
+  }
+  return v == 1;
+}
 
 int gemvx_plan(GemvxParams& p, int sms) {
   // ring slot: the largest unit among the launch's weights
@@ -228,6 +597,12 @@ int gemvx_plan(GemvxParams& p, int sms) {
   for (int i = 0; i < p.nseg; ++i) {
     p.slot = max(p.slot, unit_bytes(p.seg[i].type));
     p.planes |= p.seg[i].type == TYPE_Q4_K ? 1 : 2;
+  }
+  if (p.pro.mode != GEMV_PRO_NONE) {
+    // the prologue writes both planes, and needs the whole width-2048 row
+    // (one 256-block per warp) in one CTA
+    if (p.K != GEMV_PRO_D) return -1;
+    p.planes = 3;
   }
   // split long rows over a cluster until the launch covers every SM once
   // (a CTA keeps at least 8 blocks, one per warp), and further while a CTA's
@@ -254,6 +629,8 @@ int gemvx_plan(GemvxParams& p, int sms) {
       const int cl = min(p.total_tiles, max(1, sms * ctas / p.C));
       const int rounds = (p.total_tiles + cl - 1) / cl * ctas;
       const long inflight = long(ctas) * GX_WARPS * r * p.slot;
+      // (ties: more bytes in flight; two CTAs per SM win equal bytes -- twice
+      // the warps to hide the shared-memory and barrier latencies)
       if (rounds < best_rounds || (rounds == best_rounds && inflight > best_inflight)) {
         best_rounds = rounds;
         best_inflight = inflight;
@@ -267,6 +644,104 @@ int gemvx_plan(GemvxParams& p, int sms) {
   const int clusters = min(p.total_tiles, max(1, sms * best_ctas / p.C));
   p.err = device_status_word();
   return clusters * p.C;
+}
+
+// Warp-per-tile plan: columns per warp (returned) -- the fewest for which
+// the work items fit two rounds of the launch's warps -- and the deepest
+// ring that fits; returns the grid size via *grid (0: not this form, also
+// for launches of fewer than two work items per SM).
+int gemvw_plan(GemvxParams& p, int sms, int* grid) {
+  *grid = 0;
+  if (p.nb > GW_MAX_NB || p.ncols < 1 || p.ncols > GEMVX_MAX_COLS) return 0;
+  p.slot = 0;
+  p.planes = 0;
+  for (int i = 0; i < p.nseg; ++i) {
+    p.slot = max(p.slot, unit_bytes(p.seg[i].type));
+    p.planes |= p.seg[i].type == TYPE_Q4_K ? 1 : 2;
+  }
+  if (p.pro.mode != GEMV_PRO_NONE) {
+    if (p.K != GEMV_PRO_D) return 0;
+    p.planes = 3;
+  }
+  p.C = 1;
+  p.nbc = p.nb;
+  int nc = 1;
+  while (nc < p.ncols && p.total_tiles * ((p.ncols + nc - 1) / nc) > 2 * GX_WARPS * sms) nc *= 2;
+  if (nc > p.ncols) nc = p.ncols <= 1 ? 1 : p.ncols <= 2 ? 2 : p.ncols <= 4 ? 4 : 8;
+  for (p.R = GX_MAX_R; p.R >= 1; --p.R)
+    if (gw_smem_bytes(p) <= size_t(GEMV_MAX_SMEM)) break;
+  if (p.R < 1) return 0;
+  const int nitems = p.total_tiles * ((p.ncols + nc - 1) / nc);
+  // a launch of few items (fewer than two warps per SM) runs each item on a
+  // single warp's serial block loop: the split form spreads it wider
+  if (nitems < 2 * sms) return 0;
+  *grid = min(sms, nitems);
+  p.err = device_status_word();
+  return nc <= 1 ? 1 : nc <= 2 ? 2 : nc <= 4 ? 4 : 8;
+}
+
+// Relay plan: rows of 16, 32 or 64 blocks, no prologue, every segment one
+// type; the deepest ring (at most the blocks per part) that fits.  Returns
+// the blocks per part (0: not this form).
+static int gemvr_plan(GemvxParams& p) {
+  if (p.pro.mode != GEMV_PRO_NONE || p.nb % GR_PARTS != 0) return 0;
+  const int nbp = p.nb / GR_PARTS;
+  if (nbp != 2 && nbp != 4 && nbp != 8) return 0;
+  p.slot = 0;
+  p.planes = 0;
+  for (int i = 0; i < p.nseg; ++i) {
+    p.slot = max(p.slot, unit_bytes(p.seg[i].type));
+    p.planes |= p.seg[i].type == TYPE_Q4_K ? 1 : 2;
+  }
+  p.C = 1;
+  p.nbc = p.nb;
+  for (p.R = min(GX_MAX_R, nbp); p.R >= 1; --p.R)
+    if (gr_smem_bytes(p) <= size_t(GR_MAX_SMEM)) break;
+  if (p.R < 1) return 0;
+  p.err = device_status_word();
+  return nbp;
+}
+
+template <int NBP>
+static cudaError_t launch_r(const GemvxParams& p, cudaStream_t st) {
+  const size_t smem = gr_smem_bytes(p);
+  static std::atomic<uint64_t> attr_set{0};
+  const cudaError_t ea = once_per_current_device(attr_set, [] {
+    return cudaFuncSetAttribute(hc_gemvr_kernel<NBP>, cudaFuncAttributeMaxDynamicSharedMemorySize, GR_MAX_SMEM);
+  });
+  if (ea != cudaSuccess) return ea;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(p.total_tiles * p.ncols));
+  cfg.blockDim = dim3(GX_THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, hc_gemvr_kernel<NBP>, p);
+}
+
+template <int NC>
+static cudaError_t launch_w(const GemvxParams& p, int grid, cudaStream_t st) {
+  const size_t smem = gw_smem_bytes(p);
+  static std::atomic<uint64_t> attr_set{0};
+  const cudaError_t ea = once_per_current_device(attr_set, [] {
+    return cudaFuncSetAttribute(hc_gemvw_kernel<NC>, cudaFuncAttributeMaxDynamicSharedMemorySize, GEMV_MAX_SMEM);
+  });
+  if (ea != cudaSuccess) return ea;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(grid));
+  cfg.blockDim = dim3(GX_THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, hc_gemvw_kernel<NC>, p);
 }
 
 template <int NC>
@@ -301,6 +776,21 @@ static cudaError_t launch_x(const GemvxParams& p, int grid, cudaStream_t st) {
 
 cudaError_t launch_gemvx(GemvxParams& p, cudaStream_t st) {
   if (p.ncols < 1 || p.ncols > GEMVX_MAX_COLS) return cudaErrorInvalidValue;
+  if (!gemvx_force_split()) {
+    int wgrid = 0;
+    const int nc = gemvw_plan(p, sm_count(), &wgrid);
+    if (nc > 0 && wgrid > 0) {
+      if (nc == 1) return launch_w<1>(p, wgrid, st);
+      if (nc == 2) return launch_w<2>(p, wgrid, st);
+      if (nc == 4) return launch_w<4>(p, wgrid, st);
+      return launch_w<8>(p, wgrid, st);
+    }
+    GemvxParams r = p;
+    const int nbp = gemvr_plan(r);
+    if (nbp == 2) return launch_r<2>(r, st);
+    if (nbp == 4) return launch_r<4>(r, st);
+    if (nbp == 8) return launch_r<8>(r, st);
+  }
   const int grid = gemvx_plan(p, sm_count());
   if (grid <= 0) return cudaErrorInvalidValue;
   if (p.ncols <= 1) return launch_x<1>(p, grid, st);

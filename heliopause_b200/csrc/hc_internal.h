@@ -40,6 +40,11 @@ struct GemvPrologue;
 int hc_matmul_q8_prologue(size_t count, const hpc_weight* handles, const void* q8ws, size_t q8_bytes, size_t input_size,
                           size_t column_count, float* const* d_outs, const size_t* out_lens,
                           const hc::GemvPrologue& pro, cudaStream_t st);
+// The exact-order matmul with every CTA computing its input (hc_gemvx.cu
+// prologue): width 2048, up to 8 columns.
+int hc_matmul_q8_exact_prologue(size_t count, const hpc_weight* handles, const void* q8ws, size_t q8_bytes,
+                                size_t input_size, size_t column_count, float* const* d_outs, const size_t* out_lens,
+                                const hc::GemvPrologue& pro, cudaStream_t st);
 // hpc_matmul_q8 with the order chosen: exact = the reference's f32 order
 // (every path hpc_matmul_* exposes), or the reordered fast kernels (dp4a /
 // tensor-core GEMV) the model's reordered step uses.

@@ -25,7 +25,7 @@ struct GemvSeg {
 // (the per-layer hc_norm_quant_kernel folded into the GEMV): every CTA computes
 // the norm of the whole D = 2048 vector itself and quantizes the 256-blocks
 // of its K slice straight into its shared-memory activation records.
-enum { GEMV_PRO_NONE = 0, GEMV_PRO_NORM = 1, GEMV_PRO_RESID_NORM = 2 };
+enum { GEMV_PRO_NONE = 0, GEMV_PRO_NORM = 1, GEMV_PRO_RESID_NORM = 2, GEMV_PRO_QUANT = 3 };
 struct GemvPrologue {
   int mode;
   int pad_;
@@ -136,9 +136,16 @@ struct GemvxParams {
   int planes;        // activation planes the weight types read: 1 = A (Q4_K), 2 = B (Q6_K)
   int* err;          // device status word (bounded-wait timeouts)
   Q8Buf q;
+  // mode != NONE: every CTA computes its activation records itself from
+  // pro.x (width GEMV_PRO_D): NORM / RESID_NORM as the GEMV prologue of the
+  // reordered step, QUANT = Q8_K of pro.x as it is (x_out, y, w_* unused)
+  GemvPrologue pro;
 };
 // Fills C, nbc, R, slot, err; returns the grid size (<= 0: no plan fits).
 int gemvx_plan(GemvxParams& p, int sms);
+// The warp-per-tile form (rows of at most 16 blocks): returns the columns per
+// warp (0: the form does not apply) and the grid size in *grid.
+int gemvw_plan(GemvxParams& p, int sms, int* grid);
 cudaError_t launch_gemvx(GemvxParams& p, cudaStream_t st);
 
 // L2 prefetch of up to PREFETCH_MAX_RANGES byte ranges (hc_prefetch.cu):

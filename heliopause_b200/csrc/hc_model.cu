@@ -64,9 +64,13 @@ struct hpc_model_s {
   void* cand = nullptr;
   size_t cand_bytes = 0;
   int* err = nullptr;
-  // RoPE cos/sin of every position below the KV capacity, computed once on
-  // the host (the C library's cos/sin) -- [context][head_dim / 2] each
+  // RoPE cos/sin of positions 0 .. rope_rows - 1 (twice the KV capacity, at
+  // least 1024: decoding continues past the context on the slot ring),
+  // computed once on the host (the C library's cos/sin) --
+  // [rope_rows][head_dim / 2] each; later positions use the device's f64
+  // cos/sin
   double *cos_tab = nullptr, *sin_tab = nullptr;
+  int rope_rows = 0;
   // exact (default): every step in the reference's arithmetic order, its
   // results bit-identical to the WASM provider's; else the reordered kernels
   bool exact = true;
@@ -208,8 +212,9 @@ int hpc_model_create(const hpc_model_config* cfg, hpc_model* out) {
     // math library
     const int half = HD / 2;
     const double theta_scale = std::pow(c.rope_theta, -2.0 / double(HD));
-    std::vector<double> ct(size_t(c.context) * half), st(size_t(c.context) * half);
-    for (int p = 0; p < c.context; ++p) {
+    m->rope_rows = std::max(2 * c.context, 1024);
+    std::vector<double> ct(size_t(m->rope_rows) * half), st(size_t(m->rope_rows) * half);
+    for (int p = 0; p < m->rope_rows; ++p) {
       double th = double(p);
       for (int i = 0; i < half; ++i) {
         ct[size_t(p) * half + i] = std::cos(th);
@@ -384,7 +389,7 @@ static int enqueue_step(hpc_model m, int M, int k, cudaStream_t st) {
     return hc_matmul_q8_order(size_t(n), hs, q8, q8_bytes, K, size_t(M), outs, lens, m->exact, st);
   };
   const hpc_weight emb = m->lm_head;
-  HPC_CK(hc::launch_rope_gather(m->pos, M, HD / 2, m->cos_tab, m->sin_tab, c.context,
+  HPC_CK(hc::launch_rope_gather(m->pos, M, HD / 2, m->cos_tab, m->sin_tab, m->rope_rows,
                                 std::pow(c.rope_theta, -2.0 / double(HD)), m->cos_t, m->sin_t, st),
          "rope rows");
   HPC_CK(hc::launch_embed(emb->d_data, emb->type, emb->nb, c.vocab, m->ids, m->x, M, D, std::sqrt(double(D)), m->err,
@@ -396,9 +401,10 @@ static int enqueue_step(hpc_model m, int M, int k, cudaStream_t st) {
   // alternates between X (x_l, stored by the QKV prologue) and H1 (the
   // post-attention residual, stored by the gate/up prologue), so no CTA
   // overwrites a vector other CTAs of the same launch still read.
-  // (the reordered step only: the exact step runs the norms as launches of
-  // their own and every matmul on the exact-order kernel)
-  const bool fused = !m->exact && M <= 2 && D == hc::GEMV_PRO_D;
+  // The exact step folds them the same way into its exact-order GEMVs, at
+  // every width up to 8, and also the Q8_K of the attention output into the
+  // O projection.
+  const bool fused = (m->exact || M <= 2) && D == hc::GEMV_PRO_D;
   float* const X = m->x;
   float* const H1 = fused ? m->h1 : m->x;
   auto mm_pro = [&](std::initializer_list<std::pair<hpc_weight, float*>> ws, const hc::GemvPrologue& pro) -> int {
@@ -412,6 +418,9 @@ static int enqueue_step(hpc_model m, int M, int k, cudaStream_t st) {
       lens[n] = p.first->row_count * size_t(M);
       ++n;
     }
+    if (m->exact)
+      return hc_matmul_q8_exact_prologue(size_t(n), hs, m->q8d, m->q8d_bytes, size_t(D), size_t(M), outs, lens, pro,
+                                         st);
     return hc_matmul_q8_prologue(size_t(n), hs, m->q8d, m->q8d_bytes, size_t(D), size_t(M), outs, lens, pro, st);
   };
   for (int l = 0; l < c.layers; ++l) {
@@ -466,7 +475,6 @@ static int enqueue_step(hpc_model m, int M, int k, cudaStream_t st) {
                                         own_kv, m->kc[kvl], m->vc[kvl], m->pos, M, H, KVH, c.context, 1.0f,
                                         m->attx_scratch, m->attn16, st),
              "exact-order attention");
-      HPC_CK(hc::launch_q8k_quantize(m->attn16, H * HD, M, qd, nullptr, nullptr, nullptr, st), "attention quantize");
     } else {
       HPC_CK(hc::launch_attention(m->qb, m->kb, m->vb, L.norm[HPC_N_Q], L.norm[HPC_N_K], m->cos_t, m->sin_t, eps,
                                   own_kv, m->kc[kvl], m->vc[kvl], m->pos, M, H, KVH, c.context, 1.0f, m->pm, m->pl,
@@ -475,7 +483,16 @@ static int enqueue_step(hpc_model m, int M, int k, cudaStream_t st) {
       HPC_CK(hc::launch_attn_combine(m->pm, m->pl, m->po, m->pos, M, H, KVH, c.context, qd, nullptr, st),
              "attention combine");
     }
-    rc = mm({{L.w[HPC_W_O], m->o}}, m->q8d, m->q8d_bytes, size_t(H) * HD);
+    if (m->exact && H * HD == hc::GEMV_PRO_D) {
+      hc::GemvPrologue pro{};  // the O projection quantizes the f16-cast attention output itself
+      pro.mode = hc::GEMV_PRO_QUANT;
+      pro.x = m->attn16;
+      rc = mm_pro({{L.w[HPC_W_O], m->o}}, pro);
+    } else {
+      if (m->exact)
+        HPC_CK(hc::launch_q8k_quantize(m->attn16, H * HD, M, qd, nullptr, nullptr, nullptr, st), "attention quantize");
+      rc = mm({{L.w[HPC_W_O], m->o}}, m->q8d, m->q8d_bytes, size_t(H) * HD);
+    }
     if (rc != HPC_OK) return rc;
     // post-attention residual + FFN norm and gate/up
     if (fused) {
@@ -672,7 +689,7 @@ int hpc_model_prefill(hpc_model m, const float* d_hidden_in, const int32_t* d_po
     pl = pm + rows;
     po = reinterpret_cast<float*>(static_cast<char*>(m->pf_part) + (rows * 2 * sizeof(float) + 255) / 256 * 256);
   }
-  HPC_CK(hc::launch_rope_gather(m->pf_pos, M, HD / 2, m->cos_tab, m->sin_tab, c.context,
+  HPC_CK(hc::launch_rope_gather(m->pf_pos, M, HD / 2, m->cos_tab, m->sin_tab, m->rope_rows,
                                 std::pow(c.rope_theta, -2.0 / double(HD)), m->pf_cos, m->pf_sin, st),
          "rope rows");
   auto mm = [&](std::initializer_list<std::pair<hpc_weight, float*>> ws, const void* q8, size_t q8_bytes,

@@ -114,6 +114,21 @@ def test_exact_group_sizes(kv_heads, m):
         gpu.close()
 
 
+def test_exact_kv_ring_wrap():
+    # Positions past the context: the keys are the last `context` positions,
+    # key j in slot (start + j) % context (hp_gqa_attention_f32's ring).  At
+    # context 512 a 256-key p.v stage starts mid-ring and the next one wraps
+    # past the last slot, which the kernel fills with per-key copies.
+    shape = replace(SMALL, context=512)
+    gpu, ref = _build(shape, filled=512, seed=19)
+    try:
+        ids = _exact_step(gpu, ref, [91], [700], 40, "decode at 700 (ring of 512)")
+        _exact_step(gpu, ref, [int(ids[0, 0]), 8, 4000, 77, 1234], [701, 702, 703, 704, 705], 40,
+                    "verify at 701..705 (ring of 512)")
+    finally:
+        gpu.close()
+
+
 def test_exact_verify_equals_sequential_decodes():
     # A batched verify over positions p..p+4 equals five single-token decodes
     # bit for bit (the causal mask makes them the same computation, and the
