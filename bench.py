@@ -187,7 +187,7 @@ class GemvConfig1:
         ms = graph_launch_times(launches * 2)
         achieved = self.algo_bytes / (ms / 1e3) / 1e9
         return {"bound": "hbm", "achieved": achieved, "peak": peak_gbs, "unit": "GB/s", "frac": achieved / peak_gbs,
-                "traffic": None, "kernel": "hc_gemvx_kernel<1> (Q4_K 2048 -> 16384, M=1, reference f32 order)",
+                "traffic": None, "kernel": "hc_gemvw_kernel<1> (Q4_K 2048 -> 16384, M=1, reference f32 order)",
                 "algorithmic_bytes_per_launch": self.algo_bytes, "launch_ms": ms}
 
     unit = "GB/s"
@@ -352,15 +352,44 @@ class DecodeConfig3:
         ms = graph_launch_times(launches)
         algo = 2 * self.syn.row_bytes(self.syn.Q4_K, s.hidden) * s.ffn + 4 * s.hidden + 8 * s.ffn
         achieved = algo / (ms / 1e3) / 1e9
+        # the same launch as the step runs it: the post-attention residual and
+        # the FFN RMSNorm computed by every CTA before it streams the weights
+        # (hpc_matmul_rmsnorm_f32), 35 launches back to back with PDL
+        xr = torch.randn(s.hidden, device="cuda")
+        yr = torch.randn(s.hidden, device="cuda")
+        wpost = torch.ones(s.hidden, device="cuda")
+        wpre = torch.ones(s.hidden, device="cuda")
+        xo = torch.empty(s.hidden, device="cuda")
+        step_launches = []
+        for layer in range(s.layers):
+            hg = self.model.weight_handles[(layer, self.W_GATE)]
+            hu = self.model.weight_handles[(layer, self.W_UP)]
+
+            def f2(hg=hg, hu=hu):
+                hs = (C.c_void_p * 2)(hg.handle, hu.handle)
+                outs = (C.c_void_p * 2)(g.data_ptr(), u.data_ptr())
+                lens = (C.c_size_t * 2)(s.ffn, s.ffn)
+                hk.assert_cuda_ok(L.hpc_matmul_rmsnorm_f32(2, hs, C.c_void_p(ws.data_ptr()), nbytes.value, s.hidden, 1,
+                                                           C.c_void_p(xr.data_ptr()), C.c_void_p(yr.data_ptr()),
+                                                           C.c_void_p(wpost.data_ptr()), C.c_void_p(wpre.data_ptr()),
+                                                           1e-6, C.c_void_p(xo.data_ptr()), outs, lens,
+                                                           C.c_void_p(torch.cuda.current_stream().cuda_stream)),
+                                  "gemv + norm prologue")
+            step_launches.append(f2)
+        ms_step = graph_launch_times(step_launches)
+        achieved_step = algo / (ms_step / 1e3) / 1e9
         return {"bound": "hbm", "achieved": achieved, "peak": peak_gbs, "unit": "GB/s", "frac": achieved / peak_gbs,
-                "traffic": None, "kernel": "hc_gemvx_kernel<1> (ffn gate+up, 2048 -> 2x16384 Q4_K, M=1, reference "
-                                           "f32 order: the kernel the default step runs)",
-                "algorithmic_bytes_per_launch": algo, "launch_ms": ms}
+                "traffic": None, "kernel": "hc_gemvw_kernel<1> (ffn gate+up, 2048 -> 2x16384 Q4_K, M=1, reference "
+                                           "f32 order, input pre-quantized: hpc_matmul_q8)",
+                "algorithmic_bytes_per_launch": algo, "launch_ms": ms,
+                "in_step": {"kernel": "the same launch with the step's fused prologue (residual add, two RMSNorms, "
+                                      "Q8_K in every CTA: hpc_matmul_rmsnorm_f32), as the default step runs it",
+                            "launch_ms": ms_step, "achieved": achieved_step, "frac": achieved_step / peak_gbs}}
 
     def config(self) -> dict:
         s = self.shape
         return {"workload": "decode one token, E4B-shaped Q4_K_M decoder (BASELINE config 3)",
-                "order": "reference f32 order (bit-exact to the oracle), L2 prefetch of each layer's O/FFN weights",
+                "order": "reference f32 order (bit-exact to the oracle)",
                 "layers": s.layers, "hidden": s.hidden, "heads": s.heads, "kv_heads": s.kv_heads,
                 "head_dim": s.head_dim, "ffn": s.ffn, "vocab": s.vocab, "kv_layers": s.kv_layers,
                 "context": s.context, "position": self.position, "top_k": self.k, "kv_dtype": "f32",
@@ -581,7 +610,7 @@ class GemvConfig2:
         algo = 2 * self.syn.row_bytes(self.syn.Q4_K, self.K) * self.F + 4 * self.K * self.M + 8 * self.F * self.M
         achieved = algo / (ms / 1e3) / 1e9
         return {"bound": "hbm", "achieved": achieved, "peak": peak_gbs, "unit": "GB/s", "frac": achieved / peak_gbs,
-                "traffic": None, "kernel": f"hc_gemvx_kernel (gate+up, 2048 -> 2x16384 Q4_K, M={self.M}, reference f32 order)",
+                "traffic": None, "kernel": f"hc_gemvw_kernel (gate+up, 2048 -> 2x16384 Q4_K, M={self.M}, reference f32 order)",
                 "algorithmic_bytes_per_launch": algo, "launch_ms": ms}
 
     def config(self) -> dict:

@@ -39,6 +39,8 @@ SIGNATURES = {
     "hpc_q8_workspace_bytes": (_i, [_sz, _sz, C.POINTER(_sz)]),
     "hpc_q8_quantize": (_i, [_vp, _sz, _sz, _sz, _vp, _sz, _vp]),
     "hpc_matmul_q8": (_i, [_sz, C.POINTER(_vp), _vp, _sz, _sz, _sz, C.POINTER(_vp), C.POINTER(_sz), _vp]),
+    "hpc_matmul_rmsnorm_f32": (_i, [_sz, C.POINTER(_vp), _vp, _sz, _sz, _sz, _vp, _vp, _vp, _vp, C.c_double, _vp,
+                                    C.POINTER(_vp), C.POINTER(_sz), _vp]),
     "hpc_lm_head_topk": (_i, [_vp, _vp, _sz, _sz, _sz, _sz, C.c_int32, C.c_float, _vp, _vp, _vp]),
     "hpc_lm_head_topk_noalloc": (_i, [_vp, _vp, _sz, _sz, _sz, _sz, C.c_int32, C.c_float, _vp, _vp, _vp]),
     "hpc_lm_head_candidates_bytes": (_i, [_vp, _sz, _sz, C.POINTER(_sz)]),

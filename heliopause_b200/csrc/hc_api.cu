@@ -559,6 +559,33 @@ int hc_matmul_q8_prologue(size_t count, const hpc_weight* handles, const void* q
 
 extern "C" {
 
+int hpc_matmul_rmsnorm_f32(size_t count, const hpc_weight* handles, void* d_workspace, size_t workspace_bytes,
+                           size_t input_size, size_t column_count, const float* d_x, const float* d_y,
+                           const float* d_w_post, const float* d_w_pre, double eps, float* d_x_out,
+                           float* const* d_outs, const size_t* out_lens, void* stream) {
+  if (!handles || !d_workspace || !d_x || !d_w_pre || !d_outs || !out_lens) return fail(HPC_ERR_ARG, "null pointer");
+  if (d_y && (!d_w_post || !d_x_out)) return fail(HPC_ERR_ARG, "residual form needs w_post and x_out");
+  if (d_y && d_x_out == d_x) return fail(HPC_ERR_ARG, "x_out aliases x");
+  hc::GemvPrologue pro{};
+  pro.mode = d_y ? hc::GEMV_PRO_RESID_NORM : hc::GEMV_PRO_NORM;
+  pro.x = d_x;
+  pro.y = d_y;
+  pro.w_post = d_w_post;
+  pro.w_pre = d_w_pre;
+  pro.x_out = d_x_out;
+  pro.eps = eps;
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (g_exact_order.load())
+    return hc_matmul_q8_exact_prologue(count, handles, d_workspace, workspace_bytes, input_size, column_count, d_outs,
+                                       out_lens, pro, st);
+  return hc_matmul_q8_prologue(count, handles, d_workspace, workspace_bytes, input_size, column_count, d_outs,
+                               out_lens, pro, st);
+}
+
+}  // extern "C"
+
+extern "C" {
+
 static int lm_head_check(hpc_weight h, size_t input_size, size_t column_count, size_t k) {
   if (!valid(h)) return fail(HPC_ERR_ARG, "invalid weight handle");
   if (h->input_size != input_size) return fail(HPC_ERR_SHAPE, "LM head input size %zu vs %zu", h->input_size, input_size);

@@ -331,7 +331,7 @@ __device__ __forceinline__ float pv_stage_full(const float4* __restrict__ r4, co
   return acc;
 }
 
-// One 2-D TMA tile load (no multicast): box at element (x, y) of `map` into
+// One 2-D TMA tile load (this CTA only): box at element (x, y) of `map` into
 // this CTA's shared memory, completion on `bar`.
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
   asm volatile(

@@ -11,14 +11,17 @@
 //     x = fround(f * layer_output_scale)
 //   h   = rmsNorm(x, output_norm); post = post_projection @ h
 //   top tokens = maskedEmbeddingTopTokens(h, centroids @ h)             :211-242
-// The matmuls are f32 products of the bit-exactly dequantized weights with
-// f32 inputs (matMulAssistantWeight :160-183 -> hp_matmul_dequantized_f32,
-// lib.rs:103-154): the weights are dequantized once at load into f32 rows
-// and every step streams them with a warp-per-row GEMV.  Rounding points
-// follow the reference (f32 sums of squares and f64 norm scales, the f32 theta
-// chain of the partial RoPE with f64 cos/sin, f64 exp of f32 score
-// differences, fround of the gated GELU); summation orders differ from its
-// sequential loops, so results agree to f32 rounding.
+// The matmuls are matMulAssistantWeight (:160-183 -> hp_matmul_dequantized_f32,
+// lib.rs:103-154): each weight element dequantized bit-exactly from the
+// resident row tiles (the head keeps its own copy of the quantized bytes,
+// 7x fewer than f32 rows) and one sequential f32 chain per output row in
+// index order -- the reference's own sum, bit for bit
+// (hc_dequant_matmul_kernel).  The masked token scores (:211-242) are the
+// same chain over the gathered embedding rows.  Elsewhere rounding points
+// follow the reference (f32 sums of squares and f64 norm scales, the f32
+// theta chain of the partial RoPE with f64 cos/sin, f64 exp of f32 score
+// differences, fround of the gated GELU) while the norm and attention sums
+// run in parallel orders, so those agree to f32 rounding.
 //
 // One step is one CUDA graph (captured on first use, re-captured when the
 // target KV pointers change): the position and top-k travel in device
@@ -32,42 +35,15 @@
 #include "hc_decmath.cuh"
 #include "hc_internal.h"
 #include "hc_kernels.cuh"
+#include "hc_unpack.cuh"
 
 namespace hc {
 namespace {
 
-constexpr int DG_ROWS = 8;       // GEMV rows per CTA (a warp per row)
 constexpr int DN_THREADS = 1024; // norm kernels: one CTA
 constexpr int DA_CHUNK = 64;     // attention tokens per CTA
 constexpr int DT_THREADS = 1024; // top-k selection: one CTA
 constexpr int DT_MAXN = 4096;    // keys one selection sorts
-
-// y[row] = sum_k W[row][k] * x[k] over f32 rows, x = [x0[0..k0) ; x1[..]].
-__global__ void __launch_bounds__(32 * DG_ROWS) hc_dgemv_kernel(const float* __restrict__ W, int N, int K,
-                                                             const float* __restrict__ x0, int k0,
-                                                             const float* __restrict__ x1, float* __restrict__ y) {
-  extern __shared__ __align__(16) float xs[];
-  for (int i = int(threadIdx.x); i < K; i += int(blockDim.x)) xs[i] = i < k0 ? x0[i] : x1[i - k0];
-  __syncthreads();
-  const int warp = int(threadIdx.x >> 5), lane = int(threadIdx.x & 31);
-  const int row = int(blockIdx.x) * DG_ROWS + warp;
-  if (row >= N) return;
-  const float4* w = reinterpret_cast<const float4*>(W + size_t(row) * K);
-  const float4* xv = reinterpret_cast<const float4*>(xs);
-  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 4
-  for (int j = lane; j < K / 4; j += 32) {
-    const float4 a = __ldcs(w + j), b = xv[j];
-    acc.x = fmaf(a.x, b.x, acc.x);
-    acc.y = fmaf(a.y, b.y, acc.y);
-    acc.z = fmaf(a.z, b.z, acc.z);
-    acc.w = fmaf(a.w, b.w, acc.w);
-  }
-  float s = (acc.x + acc.y) + (acc.z + acc.w);
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
-  if (lane == 0) y[row] = s;
-}
 
 // f32 sum of squares of v[0..n) over the CTA (every thread gets the total).
 __device__ float block_sumsq_f32(const float* v, int n, float* red) {
@@ -316,14 +292,23 @@ __global__ void __launch_bounds__(DT_THREADS) hc_dtopk_kernel(const float* __res
 
 // maskedEmbeddingTopTokens (mtp-assistant-runner.ts:211-242): slot s of the
 // top centroids' token lists (token_ordering[c * per + j]) scored by its
-// embedding row . h; ids outside the vocabulary get the empty key.  A warp
-// per slot.
-__global__ void __launch_bounds__(256) hc_dscores_kernel(const float* __restrict__ E, int hid, int vocab,
-                                                      const int32_t* __restrict__ ordering, int per,
-                                                      const int32_t* __restrict__ c_ids, int slots,
-                                                      const float* __restrict__ h, uint64_t* __restrict__ keys) {
+// embedding row . h -- the row dequantized bit-exactly from its row tile and
+// one sequential f32 chain over the hidden index, as
+// hp_matmul_dequantized_f32 on the gathered rows; ids outside the vocabulary
+// get the empty key.  A warp per slot: per 256-block, eight lanes dequantize
+// the row's block into the warp's shared row buffer, lane 0 walks it.
+constexpr int DS_WARPS = 8;
+__global__ void __launch_bounds__(32 * DS_WARPS) hc_dscores_kernel(const uint8_t* __restrict__ E, int type, int nb,
+                                                                int vocab, const int32_t* __restrict__ ordering,
+                                                                int per, const int32_t* __restrict__ c_ids, int slots,
+                                                                const float* __restrict__ h,
+                                                                uint64_t* __restrict__ keys) {
+  extern __shared__ __align__(16) float ds_smem[];  // h [nb * 256], then [DS_WARPS][256] row blocks
   const int warp = int(threadIdx.x >> 5), lane = int(threadIdx.x & 31);
-  const int slot = int(blockIdx.x) * 8 + warp;
+  const int K = nb * QK;
+  for (int i = int(threadIdx.x); i < K; i += int(blockDim.x)) ds_smem[i] = h[i];
+  __syncthreads();
+  const int slot = int(blockIdx.x) * DS_WARPS + warp;
   if (slot >= slots) return;
   const int c = c_ids[slot / per];
   const int tok = c >= 0 ? ordering[size_t(c) * per + slot % per] : -1;
@@ -331,20 +316,24 @@ __global__ void __launch_bounds__(256) hc_dscores_kernel(const float* __restrict
     if (lane == 0) keys[slot] = 0ull;
     return;
   }
-  const float4* e = reinterpret_cast<const float4*>(E + size_t(tok) * hid);
-  const float4* hv = reinterpret_cast<const float4*>(h);
-  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int j = lane; j < hid / 4; j += 32) {
-    const float4 a = __ldg(e + j), b = __ldg(hv + j);
-    acc.x = fmaf(a.x, b.x, acc.x);
-    acc.y = fmaf(a.y, b.y, acc.y);
-    acc.z = fmaf(a.z, b.z, acc.z);
-    acc.w = fmaf(a.w, b.w, acc.w);
+  float* row = ds_smem + K + warp * QK;
+  const size_t ub = type == TYPE_Q4_K ? Q4K_TILE_BLOCK_BYTES : Q6K_TILE_BLOCK_BYTES;
+  float sum = 0.0f;
+  for (int b = 0; b < nb; ++b) {
+    const uint8_t* tb = E + (size_t(tok / TILE) * nb + b) * ub;
+    if (lane < 8) {
+      if (type == TYPE_Q4_K) q4k_dequant_chunk(tb, tok % TILE, lane, row);
+      else q6k_dequant_group(tb, tok % TILE, lane, row);
+    }
+    __syncwarp();
+    if (lane == 0) {
+      const float* hb = ds_smem + b * QK;
+#pragma unroll 16
+      for (int i = 0; i < QK; ++i) sum = __fadd_rn(sum, __fmul_rn(row[i], hb[i]));
+    }
+    __syncwarp();
   }
-  float s = (acc.x + acc.y) + (acc.z + acc.w);
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
-  if (lane == 0) keys[slot] = dkey(s, uint32_t(tok));
+  if (lane == 0) keys[slot] = dkey(sum, uint32_t(tok));
 }
 
 // The step's inputs: [embedding ; hidden] into xin, the position and top-k.
@@ -368,8 +357,15 @@ namespace {
 
 constexpr uint32_t kDraftMagic = 0x48504444u;  // "HPDD"
 
+// One matrix of the head: its own copy of the resident row-tile bytes.
+struct DraftMat {
+  uint8_t* w = nullptr;
+  size_t bytes = 0;
+  int type = 0, nb = 0, rows = 0, rows_pad = 0;
+};
+
 struct DraftLayer {
-  float* w[HPC_DW_LAYER_COUNT] = {};
+  DraftMat w[HPC_DW_LAYER_COUNT];
   float* n[HPC_DN_LAYER_COUNT] = {};
   float scale = 1.0f;
   const float* kc = nullptr;
@@ -383,10 +379,7 @@ struct hpc_draft_s {
   int device = 0;
   hpc_draft_config cfg{};
   int per = 0;  // token_ordering entries per centroid
-  float* pre = nullptr;
-  float* post = nullptr;
-  float* cent = nullptr;
-  float* embd = nullptr;
+  DraftMat pre, post, cent, embd;
   float* out_norm = nullptr;
   int32_t* ordering = nullptr;
   std::vector<DraftLayer> layers;
@@ -404,7 +397,11 @@ struct hpc_draft_s {
 static bool draft_valid(hpc_draft d) { return d && d->magic == kDraftMagic; }
 
 static void draft_free(hpc_draft d) {
-  float** fs[] = {&d->pre, &d->post, &d->cent, &d->embd, &d->out_norm, &d->xin, &d->x, &d->a, &d->q, &d->att,
+  for (DraftMat* m : {&d->pre, &d->post, &d->cent, &d->embd}) {
+    cudaFree(m->w);
+    *m = DraftMat{};
+  }
+  float** fs[] = {&d->out_norm, &d->xin, &d->x, &d->a, &d->q, &d->att,
                   &d->o, &d->r, &d->nn, &d->g, &d->u, &d->act, &d->dn, &d->h, &d->post_out, &d->cent_out,
                   &d->pm, &d->pl, &d->po, &d->out_vals, &d->c_vals};
   for (float** p : fs) {
@@ -412,7 +409,10 @@ static void draft_free(hpc_draft d) {
     *p = nullptr;
   }
   for (auto& L : d->layers) {
-    for (float*& p : L.w) cudaFree(p);
+    for (DraftMat& m : L.w) {
+      cudaFree(m.w);
+      m = DraftMat{};
+    }
     for (float*& p : L.n) cudaFree(p);
   }
   cudaFree(d->ordering);
@@ -430,8 +430,8 @@ static void draft_invalidate(hpc_draft d) {
   d->graph = nullptr;
 }
 
-// Matrix `which` of the draft head: its (input, rows) and its f32 slot.
-static int draft_matrix(hpc_draft d, int which, int layer, size_t* k, size_t* n, float*** slot) {
+// Matrix `which` of the draft head: its (input, rows) and its slot.
+static int draft_matrix(hpc_draft d, int which, int layer, size_t* k, size_t* n, DraftMat** slot) {
   const hpc_draft_config& c = d->cfg;
   const size_t E = size_t(c.hidden), D = size_t(c.backbone), Hq = size_t(c.heads) * c.head_dim;
   if (which >= HPC_DW_PRE) {
@@ -520,16 +520,24 @@ int hpc_draft_set_matrix(hpc_draft d, int which, int layer, hpc_weight w) {
   if (!draft_valid(d)) return hpc_fail(HPC_ERR_ARG, "invalid draft head");
   if (!hpc_weight_valid(w)) return hpc_fail(HPC_ERR_ARG, "invalid weight handle");
   size_t k = 0, n = 0;
-  float** slot = nullptr;
+  DraftMat* slot = nullptr;
   int rc = draft_matrix(d, which, layer, &k, &n, &slot);
   if (rc != HPC_OK) return rc;
   if (w->input_size != k || w->row_count != n)
     return hpc_fail(HPC_ERR_SHAPE, "draft matrix %d: %zux%zu, expected %zux%zu", which, w->input_size, w->row_count,
                     k, n);
-  if (!*slot) HPC_CK(cudaMalloc(slot, 4 * k * n), "cudaMalloc(draft matrix)");
-  // the bit-exact dequantization of the resident weight, once (f32 rows)
-  HPC_CK(hc::launch_dequant(w->type, w->d_data, *slot, int(n), w->nb, nullptr), "draft dequantize");
-  HPC_CK(cudaDeviceSynchronize(), "draft dequantize");
+  if (slot->w && slot->bytes != w->bytes) {
+    cudaFree(slot->w);
+    slot->w = nullptr;
+  }
+  if (!slot->w) HPC_CK(cudaMalloc(&slot->w, w->bytes), "cudaMalloc(draft matrix)");
+  // the resident row tiles, copied (the caller may release its handle)
+  HPC_CK(cudaMemcpy(slot->w, w->d_data, w->bytes, cudaMemcpyDeviceToDevice), "draft matrix copy");
+  slot->bytes = w->bytes;
+  slot->type = w->type;
+  slot->nb = w->nb;
+  slot->rows = int(w->row_count);
+  slot->rows_pad = int(w->rows_pad);
   draft_invalidate(d);
   return HPC_OK;
 }
@@ -589,9 +597,10 @@ static int draft_enqueue(hpc_draft d, cudaStream_t st) {
   using namespace hc;
   const hpc_draft_config& c = d->cfg;
   const int E = c.hidden, D = c.backbone, Hq = c.heads * c.head_dim, F = c.ffn;
-  auto gemv = [&](const float* W, int N, int K, const float* x0, int k0, const float* x1, float* y) -> int {
-    hc_dgemv_kernel<<<(N + DG_ROWS - 1) / DG_ROWS, 32 * DG_ROWS, size_t(K) * 4, st>>>(W, N, K, x0, k0, x1, y);
-    HPC_CK(cudaGetLastError(), "draft gemv");
+  // y = W x with hp_matmul_dequantized_f32's arithmetic (one sequential
+  // chain per row over the bit-exactly dequantized weights)
+  auto gemv = [&](const DraftMat& W, const float* x, float* y) -> int {
+    HPC_CK(launch_dequant_matmul(W.type, W.w, W.nb, W.rows, W.rows_pad, x, W.nb * QK, 1, y, st), "draft gemv");
     return HPC_OK;
   };
   auto norm = [&](int mode, int n, const float* x, const float* y, const float* w1, const float* w2, float scale,
@@ -600,7 +609,7 @@ static int draft_enqueue(hpc_draft d, cudaStream_t st) {
     HPC_CK(cudaGetLastError(), "draft norm");
     return HPC_OK;
   };
-  int rc = gemv(d->pre, E, 2 * D, d->xin, 2 * D, d->xin, d->x);
+  int rc = gemv(d->pre, d->xin, d->x);
   if (rc != HPC_OK) return rc;
   const int pairs = int(std::floor(double(c.head_dim) * 0.25 / 2.0));
   const double theta_scale = std::pow(c.rope_theta, -2.0 / double(c.head_dim));
@@ -608,7 +617,7 @@ static int draft_enqueue(hpc_draft d, cudaStream_t st) {
   for (int l = 0; l < c.layers; ++l) {
     DraftLayer& L = d->layers[size_t(l)];
     if ((rc = norm(0, E, d->x, nullptr, L.n[HPC_DN_ATTN], nullptr, 1.0f, d->a, nullptr)) != HPC_OK) return rc;
-    if ((rc = gemv(L.w[HPC_DW_Q], Hq, E, d->a, E, d->a, d->q)) != HPC_OK) return rc;
+    if ((rc = gemv(L.w[HPC_DW_Q], d->a, d->q)) != HPC_OK) return rc;
     hc_dqrope_kernel<<<c.heads, 256, 0, st>>>(d->q, L.n[HPC_DN_Q], c.head_dim, d->d_pos, pairs, theta_scale, c.rms_eps);
     HPC_CK(cudaGetLastError(), "draft q norm / rope");
     hc_dattn_partial_kernel<<<dim3(chunks, c.kv_heads), 256, size_t(G) * (256 + DA_CHUNK) * 4, st>>>(
@@ -616,24 +625,24 @@ static int draft_enqueue(hpc_draft d, cudaStream_t st) {
     HPC_CK(cudaGetLastError(), "draft attention");
     hc_dattn_combine_kernel<<<c.heads, 256, 0, st>>>(d->pm, d->pl, d->po, d->d_pos, c.heads, c.kv_heads, d->att);
     HPC_CK(cudaGetLastError(), "draft attention combine");
-    if ((rc = gemv(L.w[HPC_DW_O], E, Hq, d->att, Hq, d->att, d->o)) != HPC_OK) return rc;
+    if ((rc = gemv(L.w[HPC_DW_O], d->att, d->o)) != HPC_OK) return rc;
     if ((rc = norm(1, E, d->x, d->o, L.n[HPC_DN_POST_ATTN], L.n[HPC_DN_FFN], 1.0f, d->r, d->nn)) != HPC_OK) return rc;
-    if ((rc = gemv(L.w[HPC_DW_GATE], F, E, d->nn, E, d->nn, d->g)) != HPC_OK) return rc;
-    if ((rc = gemv(L.w[HPC_DW_UP], F, E, d->nn, E, d->nn, d->u)) != HPC_OK) return rc;
+    if ((rc = gemv(L.w[HPC_DW_GATE], d->nn, d->g)) != HPC_OK) return rc;
+    if ((rc = gemv(L.w[HPC_DW_UP], d->nn, d->u)) != HPC_OK) return rc;
     hc_dgeglu_kernel<<<(F + 255) / 256, 256, 0, st>>>(d->g, d->u, F, d->act);
     HPC_CK(cudaGetLastError(), "draft geglu");
-    if ((rc = gemv(L.w[HPC_DW_DOWN], E, F, d->act, F, d->act, d->dn)) != HPC_OK) return rc;
+    if ((rc = gemv(L.w[HPC_DW_DOWN], d->act, d->dn)) != HPC_OK) return rc;
     if ((rc = norm(2, E, d->r, d->dn, L.n[HPC_DN_POST_FFW], nullptr, L.scale, d->x, nullptr)) != HPC_OK) return rc;
   }
   if ((rc = norm(0, E, d->x, nullptr, d->out_norm, nullptr, 1.0f, d->h, nullptr)) != HPC_OK) return rc;
-  if ((rc = gemv(d->post, D, E, d->h, E, d->h, d->post_out)) != HPC_OK) return rc;
-  if ((rc = gemv(d->cent, c.n_centroids, E, d->h, E, d->h, d->cent_out)) != HPC_OK) return rc;
+  if ((rc = gemv(d->post, d->h, d->post_out)) != HPC_OK) return rc;
+  if ((rc = gemv(d->cent, d->h, d->cent_out)) != HPC_OK) return rc;
   hc_dtopk_kernel<<<1, DT_THREADS, 0, st>>>(d->cent_out, nullptr, c.n_centroids, c.centroid_top_k, nullptr, d->c_ids,
                                          d->c_vals);
   HPC_CK(cudaGetLastError(), "draft centroid top-k");
   const int slots = c.centroid_top_k * d->per;
-  hc_dscores_kernel<<<(slots + 7) / 8, 256, 0, st>>>(d->embd, E, c.vocab, d->ordering, d->per, d->c_ids, slots, d->h,
-                                                  d->keys);
+  hc_dscores_kernel<<<(slots + DS_WARPS - 1) / DS_WARPS, 32 * DS_WARPS, size_t(E + DS_WARPS * QK) * 4, st>>>(
+      d->embd.w, d->embd.type, d->embd.nb, c.vocab, d->ordering, d->per, d->c_ids, slots, d->h, d->keys);
   HPC_CK(cudaGetLastError(), "draft token scores");
   hc_dtopk_kernel<<<1, DT_THREADS, 0, st>>>(nullptr, d->keys, slots, 0, d->d_k, d->out_ids, d->out_vals);
   HPC_CK(cudaGetLastError(), "draft token top-k");
@@ -647,12 +656,12 @@ int hpc_draft_step(hpc_draft d, const float* d_embedding, const float* d_hidden,
   if (!d_embedding || !d_hidden || !d_post_out || !d_ids || !d_vals) return hpc_fail(HPC_ERR_ARG, "null pointer");
   if (position < 0 || position >= c.context) return hpc_fail(HPC_ERR_SHAPE, "draft position %d", position);
   if (top_k < 1 || top_k > size_t(c.max_top_k)) return hpc_fail(HPC_ERR_SHAPE, "draft top-k %zu", top_k);
-  if (!d->pre || !d->post || !d->cent || !d->embd || !d->ordering)
+  if (!d->pre.w || !d->post.w || !d->cent.w || !d->embd.w || !d->ordering)
     return hpc_fail(HPC_ERR_ARG, "draft head weights not loaded");
   std::vector<const void*> kv;
   for (auto& L : d->layers) {
-    for (float* w : L.w)
-      if (!w) return hpc_fail(HPC_ERR_ARG, "draft layer weights not loaded");
+    for (const DraftMat& w : L.w)
+      if (!w.w) return hpc_fail(HPC_ERR_ARG, "draft layer weights not loaded");
     if (!L.kc || !L.vc) return hpc_fail(HPC_ERR_ARG, "draft target KV not set");
     kv.push_back(L.kc);
     kv.push_back(L.vc);

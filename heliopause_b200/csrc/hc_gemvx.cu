@@ -452,8 +452,11 @@ __global__ void __launch_bounds__(GX_THREADS, 1) hc_gemvw_kernel(const __grid_co
 // serial; the integer work of all 8 * NBP blocks runs in parallel.
 constexpr int GR_PARTS = GX_WARPS;
 
+// activation records: the CTA's column only, or every column when the
+// prologue computes them (it norms the whole launch's input)
+__host__ __device__ inline int gr_act_cols(const GemvxParams& p) { return p.pro.mode != GEMV_PRO_NONE ? p.ncols : 1; }
 __host__ __device__ inline size_t gr_act_bytes(const GemvxParams& p) {
-  return size_t(p.nb) * (((p.planes & 1) ? Q8A_REC : 0) + ((p.planes & 2) ? Q8B_REC : 0));
+  return size_t(gr_act_cols(p)) * p.nb * (((p.planes & 1) ? Q8A_REC : 0) + ((p.planes & 2) ? Q8B_REC : 0));
 }
 __host__ __device__ inline size_t gr_smem_bytes(const GemvxParams& p) {
   return size_t(GR_PARTS) * p.R * p.slot + gr_act_bytes(p) + size_t(GR_PARTS) * GX_PROD * sizeof(float) +
@@ -476,9 +479,10 @@ __global__ void __launch_bounds__(GX_THREADS, 1) hc_gemvr_kernel(const __grid_co
   const uint32_t ub = uint32_t(unit_bytes(sg.type));
   const uint8_t* wtile = sg.w + size_t(tile - sg.tile_begin) * nb * ub;
   uint8_t* ring = smem + size_t(warp) * R * p.slot;
-  uint8_t* act_a = smem + size_t(GR_PARTS) * R * p.slot;              // [nb][288]
-  uint8_t* act_b = act_a + ((p.planes & 1) ? size_t(nb) * Q8A_REC : 0);  // [nb][304]
-  float* relay = reinterpret_cast<float*>(act_a + gr_act_bytes(p));      // [8][9][32]
+  const int acols = gr_act_cols(p);
+  uint8_t* act_a = smem + size_t(GR_PARTS) * R * p.slot;                      // [acols][nb][288]
+  uint8_t* act_b = act_a + ((p.planes & 1) ? size_t(acols) * nb * Q8A_REC : 0);  // [acols][nb][304]
+  float* relay = reinterpret_cast<float*>(act_a + gr_act_bytes(p));  // [8][9][32]
   float* prod = relay + GR_PARTS * GX_PROD + size_t(warp) * NBP * GX_PROD + lane;  // this warp's [NBP][9][32]
   uint64_t* wb = bars + warp * R;
   const int b0 = warp * NBP;
@@ -493,7 +497,13 @@ __global__ void __launch_bounds__(GX_THREADS, 1) hc_gemvr_kernel(const __grid_co
     for (int w = 0; w < GR_PARTS; ++w) mbar_init(&hop[w], 32);
   __syncwarp();
   pdl_wait();  // the activation records are written by the previous kernel
-  if (threadIdx.x == 0) {
+  if (p.pro.mode != GEMV_PRO_NONE) {
+    gx_prologue(p, act_a, act_b, 0, warp, lane);  // every column (row width 2048: one block per warp)
+    if (threadIdx.x == 0) {
+      mbar_init(&act_bar, 1);
+      mbar_arrive(&act_bar);
+    }
+  } else if (threadIdx.x == 0) {
     mbar_init(&act_bar, 1);
     mbar_expect_tx(&act_bar, uint32_t(gr_act_bytes(p)));
     const size_t rec0 = size_t(p.col0 + c) * nb;
@@ -502,6 +512,9 @@ __global__ void __launch_bounds__(GX_THREADS, 1) hc_gemvr_kernel(const __grid_co
   }
   __syncthreads();
   bool ok = mbar_wait_parity(&act_bar, 0, p.err);
+  const int ac = acols > 1 ? c : 0;  // this CTA's column among the staged records
+  act_a += size_t(ac) * nb * Q8A_REC;
+  act_b += size_t(ac) * nb * Q8B_REC;
   int issued = R < NBP ? R : NBP;
   int rs = 0;
   uint32_t rph = 0;
@@ -579,15 +592,16 @@ __global__ void __launch_bounds__(GX_THREADS, 1) hc_gemvr_kernel(const __grid_co
 
 }  // namespace
 
-// HPC_GEMVX_SPLIT=1 keeps every launch on the split (cluster) form, for
-// comparing the two forms.
-static bool gemvx_force_split() {
+// HPC_GEMVX_FORM = w | r | x pins every launch that form takes to the
+// warp-per-tile, relay or split (cluster) form, for comparing them; unset,
+// the planners choose.
+static char gemvx_form() {
   static int v = -1;
   if (v < 0) {
-    const char* e = getenv("HPC_GEMVX_SPLIT");
-    v = e && atoi(e) != 0 ? 1 : 0;
+    const char* e = getenv("HPC_GEMVX_FORM");
+    v = e && (e[0] == 'w' || e[0] == 'r' || e[0] == 'x') ? e[0] : 0;
   }
-  return v == 1;
+  return char(v);
 }
 
 int gemvx_plan(GemvxParams& p, int sms) {
@@ -649,8 +663,8 @@ int gemvx_plan(GemvxParams& p, int sms) {
 // Warp-per-tile plan: columns per warp (returned) -- the fewest for which
 // the work items fit two rounds of the launch's warps -- and the deepest
 // ring that fits; returns the grid size via *grid (0: not this form, also
-// for launches of fewer than two work items per SM).
-int gemvw_plan(GemvxParams& p, int sms, int* grid) {
+// for launches of few work items per SM).
+int gemvw_plan(GemvxParams& p, int sms, int* grid, bool any_size) {
   *grid = 0;
   if (p.nb > GW_MAX_NB || p.ncols < 1 || p.ncols > GEMVX_MAX_COLS) return 0;
   p.slot = 0;
@@ -672,9 +686,11 @@ int gemvw_plan(GemvxParams& p, int sms, int* grid) {
     if (gw_smem_bytes(p) <= size_t(GEMV_MAX_SMEM)) break;
   if (p.R < 1) return 0;
   const int nitems = p.total_tiles * ((p.ncols + nc - 1) / nc);
-  // a launch of few items (fewer than two warps per SM) runs each item on a
-  // single warp's serial block loop: the split form spreads it wider
-  if (nitems < 2 * sms) return 0;
+  // a launch of few items runs each item on a single warp's serial block
+  // loop, and the split form spreads it wider: measured, the split form is
+  // faster below 4 one-column items per SM (config 1: 512 items, 6.5 vs
+  // 7.6 us) and below 2 items per SM with more columns
+  if (nitems < (p.ncols == 1 ? 4 : 2) * sms && !any_size) return 0;
   *grid = min(sms, nitems);
   p.err = device_status_word();
   return nc <= 1 ? 1 : nc <= 2 ? 2 : nc <= 4 ? 4 : 8;
@@ -684,15 +700,17 @@ int gemvw_plan(GemvxParams& p, int sms, int* grid) {
 // type; the deepest ring (at most the blocks per part) that fits.  Returns
 // the blocks per part (0: not this form).
 static int gemvr_plan(GemvxParams& p) {
-  if (p.pro.mode != GEMV_PRO_NONE || p.nb % GR_PARTS != 0) return 0;
+  if (p.nb % GR_PARTS != 0) return 0;
+  if (p.pro.mode != GEMV_PRO_NONE && p.K != GEMV_PRO_D) return 0;
   const int nbp = p.nb / GR_PARTS;
-  if (nbp != 2 && nbp != 4 && nbp != 8) return 0;
+  if (nbp != 1 && nbp != 2 && nbp != 4 && nbp != 8) return 0;
   p.slot = 0;
   p.planes = 0;
   for (int i = 0; i < p.nseg; ++i) {
     p.slot = max(p.slot, unit_bytes(p.seg[i].type));
     p.planes |= p.seg[i].type == TYPE_Q4_K ? 1 : 2;
   }
+  if (p.pro.mode != GEMV_PRO_NONE) p.planes = 3;  // the prologue writes both planes
   p.C = 1;
   p.nbc = p.nb;
   for (p.R = min(GX_MAX_R, nbp); p.R >= 1; --p.R)
@@ -776,17 +794,22 @@ static cudaError_t launch_x(const GemvxParams& p, int grid, cudaStream_t st) {
 
 cudaError_t launch_gemvx(GemvxParams& p, cudaStream_t st) {
   if (p.ncols < 1 || p.ncols > GEMVX_MAX_COLS) return cudaErrorInvalidValue;
-  if (!gemvx_force_split()) {
+  const char form = gemvx_form();
+  if (form == 0 || form == 'w') {
     int wgrid = 0;
-    const int nc = gemvw_plan(p, sm_count(), &wgrid);
+    const int nc = gemvw_plan(p, sm_count(), &wgrid, form == 'w');
     if (nc > 0 && wgrid > 0) {
       if (nc == 1) return launch_w<1>(p, wgrid, st);
       if (nc == 2) return launch_w<2>(p, wgrid, st);
       if (nc == 4) return launch_w<4>(p, wgrid, st);
       return launch_w<8>(p, wgrid, st);
     }
+  }
+  // the relay form serves rows of 16+ blocks (and, pinned, rows of 8)
+  if (form == 0 || form == 'r') {
     GemvxParams r = p;
-    const int nbp = gemvr_plan(r);
+    const int nbp = form == 'r' || p.nb > GW_MAX_NB ? gemvr_plan(r) : 0;
+    if (nbp == 1) return launch_r<1>(r, st);
     if (nbp == 2) return launch_r<2>(r, st);
     if (nbp == 4) return launch_r<4>(r, st);
     if (nbp == 8) return launch_r<8>(r, st);

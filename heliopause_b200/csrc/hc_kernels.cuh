@@ -145,7 +145,7 @@ struct GemvxParams {
 int gemvx_plan(GemvxParams& p, int sms);
 // The warp-per-tile form (rows of at most 16 blocks): returns the columns per
 // warp (0: the form does not apply) and the grid size in *grid.
-int gemvw_plan(GemvxParams& p, int sms, int* grid);
+int gemvw_plan(GemvxParams& p, int sms, int* grid, bool any_size = false);
 cudaError_t launch_gemvx(GemvxParams& p, cudaStream_t st);
 
 // L2 prefetch of up to PREFETCH_MAX_RANGES byte ranges (hc_prefetch.cu):

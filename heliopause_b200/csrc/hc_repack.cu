@@ -117,60 +117,8 @@ __global__ void hc_repack_q6k_kernel(const uint8_t* __restrict__ src, uint8_t* _
 // The per-row pieces below are shared by the dequantize kernels and by the
 // dequantized matmul, so the bit-exact dequant test covers both.
 
-// Row `r` of a Q4_K tile-block: the 32 values of quant chunk ch (0..7) into
-// o[0..256): elements 64p + j (low nibbles) and 64p + 32 + j (high), p = ch/2.
-__device__ __forceinline__ void q4k_dequant_chunk(const uint8_t* tb, int r, int ch, float* o) {
-  const uint4* c = reinterpret_cast<const uint4*>(tb) + r;
-  const Q4KHeader hd = q4k_header(c[0]);
-  const uint4 v = c[size_t(1 + ch) * TILE];
-  const uint32_t words[4] = {v.x, v.y, v.z, v.w};
-  const int p = ch >> 1;
-  const float d1 = __fmul_rn(hd.d, float(hd.sc(2 * p))), d2 = __fmul_rn(hd.d, float(hd.sc(2 * p + 1)));
-  const float m1 = __fmul_rn(hd.dmin, float(hd.mn(2 * p))), m2 = __fmul_rn(hd.dmin, float(hd.mn(2 * p + 1)));
-#pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    const int l = 4 * (ch & 1) + k;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const uint32_t byte = (words[k] >> (8 * i)) & 0xff;
-      const int j = l + 8 * i;  // position inside the 32-byte pair
-      o[64 * p + j] = __fsub_rn(__fmul_rn(d1, float(byte & 15)), m1);
-      o[64 * p + 32 + j] = __fsub_rn(__fmul_rn(d2, float(byte >> 4)), m2);
-    }
-  }
-}
+// (q4k_dequant_chunk / q6k_dequant_group: hc_unpack.cuh)
 
-// Row `r` of a Q6_K tile-block: the 32 values of 16-groups s and s + 8
-// (s = 0..7) into o[0..256).
-__device__ __forceinline__ void q6k_dequant_group(const uint8_t* tb, int r, int s, float* o) {
-  const uint4* c = reinterpret_cast<const uint4*>(tb) + r;
-  const float d = f16_bits_to_f32(reinterpret_cast<const uint16_t*>(tb + Q6K_DPLANE_OFFSET)[r]);
-  const uint4 scv = c[12 * TILE];
-  const uint32_t scw[4] = {scv.x, scv.y, scv.z, scv.w};
-  const uint4 nv = c[size_t(s) * TILE];
-  const uint32_t nw[4] = {nv.x, nv.y, nv.z, nv.w};
-  const uint4 hv = c[size_t(8 + (s >> 1)) * TILE];
-  const uint32_t hw4[4] = {hv.x, hv.y, hv.z, hv.w};
-  const int sa = int(int8_t((scw[s >> 2] >> (8 * (s & 3))) & 0xff));
-  const int sb = int(int8_t((scw[(s + 8) >> 2] >> (8 * ((s + 8) & 3))) & 0xff));
-  const float da = __fmul_rn(d, float(sa)), db = __fmul_rn(d, float(sb));
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const uint32_t hw = hw4[2 * (s & 1) + (j >> 1)];
-    uint32_t ua, ub;
-    q6k_unpack(nw[j], hw, j & 1, ua, ub);
-    const int off[4] = {0, 8, 1, 9};
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int qa = int((ua >> (8 * i)) & 0xff) - 32;
-      const int qb = int((ub >> (8 * i)) & 0xff) - 32;
-      o[16 * s + 2 * j + off[i]] = __fmul_rn(da, float(qa));
-      o[16 * (s + 8) + 2 * j + off[i]] = __fmul_rn(db, float(qb));
-    }
-  }
-}
-
-// One thread per (row, block).
 __global__ void hc_dequant_q4k_kernel(const uint8_t* __restrict__ w, float* __restrict__ out, int rows, int nb) {
   const size_t t = blockIdx.x * size_t(blockDim.x) + threadIdx.x;
   if (t >= size_t(rows) * nb) return;
@@ -196,45 +144,88 @@ __global__ void hc_dequant_q6k_kernel(const uint8_t* __restrict__ w, float* __re
 // thread per (row, column) runs the reference's own chain
 // sum = fround(sum + fround(w * x)) in index order (no fused multiply-add,
 // no reassociation), so the result is the reference's bit for bit.
-// CTA = one 32-row tile x DM_COLS columns; per 256-block the tile's rows are
-// dequantized into shared memory (8 threads per row) and the columns' input
-// slice staged beside them.
-constexpr int DM_COLS = 8;
+// CTA = one 32-row tile x NC columns: NC chain warps (lane = row) and four
+// dequant warps.  Per 256-block the dequant warps write the tile's rows
+// (row stride 260 floats: 16-byte reads by lane = row hit distinct banks)
+// and the columns' input slice into one half of a double buffer while the
+// chain warps walk the other half, four elements per pair of 16-byte reads;
+// one CTA barrier per block.  The chain's dependent adds are the bound.
+constexpr int DM_DQ_WARPS = 4;
+constexpr int DM_ROW = QK + 4;  // floats per staged row
 
-__global__ void __launch_bounds__(256) hc_dequant_matmul_kernel(const uint8_t* __restrict__ w, int type, int nb,
-                                                                int rows, const float* __restrict__ x, int K, int cols,
-                                                                float* __restrict__ out) {
-  __shared__ float ws[TILE][QK + 1];
-  __shared__ float xs[DM_COLS][QK];
-  const int tile = int(blockIdx.x), col0 = int(blockIdx.y) * DM_COLS;
-  const int t = int(threadIdx.x), warp = t >> 5, lane = t & 31;
-  const int ncols = min(DM_COLS, cols - col0);
+template <int NC>
+__global__ void __launch_bounds__(32 * (NC + DM_DQ_WARPS)) hc_dequant_matmul_kernel(
+    const uint8_t* __restrict__ w, int type, int nb, int rows, const float* __restrict__ x, int K, int cols,
+    float* __restrict__ out) {
+  extern __shared__ __align__(16) float dm_smem[];  // ws [2][32][DM_ROW], then xs [2][NC][256]
+  float* ws = dm_smem;
+  float* xs = dm_smem + 2 * TILE * DM_ROW;
+  const int tile = int(blockIdx.x), col0 = int(blockIdx.y) * NC;
+  const int warp = int(threadIdx.x) >> 5, lane = int(threadIdx.x) & 31;
+  const int ncols = min(NC, cols - col0);
   const size_t ub = type == TYPE_Q4_K ? Q4K_TILE_BLOCK_BYTES : Q6K_TILE_BLOCK_BYTES;
+  const int dt = int(threadIdx.x) - 32 * NC;  // dequant thread index (< 0: a chain warp)
+  auto fill = [&](int b, int buf) {
+    const uint8_t* tb = w + (size_t(tile) * nb + b) * ub;
+    float* wb = ws + buf * TILE * DM_ROW;
+    for (int task = dt; task < TILE * 8; task += 32 * DM_DQ_WARPS) {  // (row, 32-element part)
+      const int r = task >> 3, part = task & 7;
+      if (type == TYPE_Q4_K) q4k_dequant_chunk(tb, r, part, wb + r * DM_ROW);
+      else q6k_dequant_group(tb, r, part, wb + r * DM_ROW);
+    }
+    float* xb = xs + buf * NC * QK;
+    for (int i = dt; i < ncols * QK; i += 32 * DM_DQ_WARPS)
+      xb[i] = x[size_t(col0 + i / QK) * K + size_t(b) * QK + i % QK];
+  };
+  if (dt >= 0) fill(0, 0);
+  __syncthreads();
   float sum = 0.0f;
   for (int b = 0; b < nb; ++b) {
-    const uint8_t* tb = w + (size_t(tile) * nb + b) * ub;
-    if (type == TYPE_Q4_K) q4k_dequant_chunk(tb, t >> 3, t & 7, ws[t >> 3]);
-    else q6k_dequant_group(tb, t >> 3, t & 7, ws[t >> 3]);
-    for (int i = t; i < ncols * QK; i += 256) xs[i / QK][i % QK] = x[size_t(col0 + i / QK) * K + size_t(b) * QK + i % QK];
-    __syncthreads();
-    if (warp < ncols) {
-      const float* wr = ws[lane];
-      const float* xc = xs[warp];
+    const int buf = b & 1;
+    if (warp < NC) {
+      if (warp < ncols) {
+        const float4* wr = reinterpret_cast<const float4*>(ws + buf * TILE * DM_ROW + lane * DM_ROW);
+        const float4* xc = reinterpret_cast<const float4*>(xs + (buf * NC + warp) * QK);
 #pragma unroll 8
-      for (int i = 0; i < QK; ++i) sum = __fadd_rn(sum, __fmul_rn(wr[i], xc[i]));
+        for (int i = 0; i < QK / 4; ++i) {
+          const float4 a = wr[i], v = xc[i];
+          sum = __fadd_rn(sum, __fmul_rn(a.x, v.x));
+          sum = __fadd_rn(sum, __fmul_rn(a.y, v.y));
+          sum = __fadd_rn(sum, __fmul_rn(a.z, v.z));
+          sum = __fadd_rn(sum, __fmul_rn(a.w, v.w));
+        }
+      }
+    } else if (b + 1 < nb) {
+      fill(b + 1, buf ^ 1);
     }
-    __syncthreads();
+    __syncthreads();  // block b consumed, block b + 1 staged
   }
   const int row = tile * TILE + lane;
   if (warp < ncols && row < rows) out[size_t(col0 + warp) * rows + row] = sum;
 }
 
+template <int NC>
+static cudaError_t launch_dm(int type, const uint8_t* w, int nb, int rows, int rows_pad, const float* x, int K,
+                             int cols, float* out, cudaStream_t stream) {
+  constexpr size_t smem = sizeof(float) * (2 * TILE * DM_ROW + 2 * NC * QK);
+  static std::atomic<uint64_t> attr{0};
+  const cudaError_t ea = once_per_current_device(attr, [] {
+    return cudaFuncSetAttribute(hc_dequant_matmul_kernel<NC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                int(smem));
+  });
+  if (ea != cudaSuccess) return ea;
+  const dim3 grid(unsigned(rows_pad / TILE), unsigned((cols + NC - 1) / NC));
+  hc_dequant_matmul_kernel<NC><<<grid, 32 * (NC + DM_DQ_WARPS), smem, stream>>>(w, type, nb, rows, x, K, cols, out);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_dequant_matmul(int type, const uint8_t* w, int nb, int rows, int rows_pad, const float* x, int K,
                                   int cols, float* out, cudaStream_t stream) {
   if (cols <= 0 || rows <= 0) return cudaSuccess;
-  const dim3 grid(unsigned(rows_pad / TILE), unsigned((cols + DM_COLS - 1) / DM_COLS));
-  hc_dequant_matmul_kernel<<<grid, 256, 0, stream>>>(w, type, nb, rows, x, K, cols, out);
-  return cudaGetLastError();
+  if (cols == 1) return launch_dm<1>(type, w, nb, rows, rows_pad, x, K, cols, out, stream);
+  if (cols == 2) return launch_dm<2>(type, w, nb, rows, rows_pad, x, K, cols, out, stream);
+  if (cols <= 4) return launch_dm<4>(type, w, nb, rows, rows_pad, x, K, cols, out, stream);
+  return launch_dm<8>(type, w, nb, rows, rows_pad, x, K, cols, out, stream);
 }
 
 cudaError_t launch_repack(int type, const uint8_t* src, uint8_t* dst, int rows, int rows_pad, int nb,

@@ -203,6 +203,37 @@ def mat_mul_quantized_resident_multi(handles, input_columns, input_size: int, co
     return [o.cpu().numpy() for o in outs] if from_host else outs
 
 
+def mat_mul_rmsnorm(handles, x, w_pre, column_count: int, *, y=None, w_post=None, eps: float = 1e-6):
+    """The decode step's norm-fused projection (hpc_matmul_rmsnorm_f32):
+    h = x + rmsNorm(y) * w_post (or x when y is None), then every weight
+    times Q8_K(rmsNorm(h) * w_pre) -- wasm/layers.ts:161-247's rmsNorm,
+    quantize_q8_k and hp_matmul_quantized_prepared_multi_f32 in one launch.
+    Device tensors in; returns (outputs, h or None)."""
+    handles = list(handles)
+    n = len(handles)
+    if not 1 <= n <= 8:
+        raise CudaKernelError(ERR_SHAPE, f"matMulRmsNorm: {n} weights")
+    d = int(handles[0].input_size)
+    for t in (x, w_pre) + ((y, w_post) if y is not None else ()):
+        if not (t.is_cuda and t.dtype == torch.float32 and t.is_contiguous()):
+            raise CudaKernelError(ERR_ARG, "matMulRmsNorm: contiguous f32 device tensors")
+    nbytes = C.c_size_t()
+    assert_cuda_ok(_lib.lib().hpc_q8_workspace_bytes(d, column_count, C.byref(nbytes)), "q8 workspace")
+    ws = torch.empty(nbytes.value, dtype=torch.uint8, device="cuda")
+    outs = [torch.empty(h.row_count * column_count, dtype=torch.float32, device="cuda") for h in handles]
+    x_out = torch.empty_like(x) if y is not None else None
+    hs = (C.c_void_p * n)(*[h.handle for h in handles])
+    os_ = (C.c_void_p * n)(*[o.data_ptr() for o in outs])
+    ls = (C.c_size_t * n)(*[o.numel() for o in outs])
+    code = _lib.lib().hpc_matmul_rmsnorm_f32(n, hs, _ptr(ws), nbytes.value, d, column_count, _ptr(x),
+                                             _ptr(y) if y is not None else None,
+                                             _ptr(w_post) if w_post is not None else None, _ptr(w_pre),
+                                             float(eps), _ptr(x_out) if x_out is not None else None, os_, ls,
+                                             _stream())
+    assert_cuda_ok(code, "matMulRmsNorm")
+    return outs, x_out
+
+
 def mat_mul_quantized(type_name: str, weight_bytes, input_columns, input_size: int, row_count: int,
                       column_count: int) -> np.ndarray:
     """wasm-kernels.ts:416-466 -> hp_matmul_quantized_f32 (lib.rs:41): host

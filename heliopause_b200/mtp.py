@@ -157,7 +157,9 @@ def _split_name(name: str) -> tuple[int, str]:
 
 class CudaMtpDraftHead:
     """The draft head resident on the current CUDA device (hpc_draft_*): each
-    matrix dequantized once into f32 rows, one step per CUDA graph."""
+    matrix kept as quantized row tiles and multiplied with
+    hp_matmul_dequantized_f32's arithmetic (bit-exact dequantization, one
+    sequential f32 chain per row), one step per CUDA graph."""
 
     def __init__(self, shape: MtpDraftShape, weights: SyntheticDraftWeights, *, gpu_seed: int | None = None,
                  max_top_k: int = 64):

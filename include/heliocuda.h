@@ -170,6 +170,22 @@ int hpc_q8_quantize(const float *d_in, size_t in_len, size_t input_size, size_t 
 int hpc_matmul_q8(size_t count, const hpc_weight *handles, const void *d_workspace, size_t workspace_bytes,
                   size_t input_size, size_t column_count, float *const *d_outs, const size_t *out_lens, void *stream);
 
+/* The norm-fused projection of the decode step: the rmsNorm of the residual
+ * stream (wasm/layers.ts:161-247 -- optionally after adding the previous
+ * projection through its post-norm), quantize_q8_k (lib.rs:1774-1811) and
+ * the prepared multi matmul (lib.rs:302-426), with the norms and the
+ * quantization computed inside the matmul launch by every CTA:
+ *   h = d_y ? x + f32(rmsNorm(y) * w_post) : x     (h stored to d_x_out when d_y)
+ *   out_i = W_i . Q8_K(f32(rmsNorm(h) * w_pre))
+ * rmsNorm in f64 as the WASM provider computes it.  input_size must be 2048
+ * and column_count 1..8 (1..2 under the reordered matmul order);
+ * d_x_out must not alias d_x.  The workspace carries the Q8_K geometry as
+ * for hpc_matmul_q8. */
+int hpc_matmul_rmsnorm_f32(size_t count, const hpc_weight *handles, void *d_workspace, size_t workspace_bytes,
+                           size_t input_size, size_t column_count, const float *d_x, const float *d_y,
+                           const float *d_w_post, const float *d_w_pre, double eps, float *d_x_out,
+                           float *const *d_outs, const size_t *out_lens, void *stream);
+
 /* ---- LM head with on-GPU top-k --------------------------------------------
  * Ordering everywhere: value descending, then vocabulary id ascending
  * (topK, runtime.ts:514-527; betterValue in TOPK_CHUNK_CANDIDATES_WGSL,

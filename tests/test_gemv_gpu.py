@@ -171,6 +171,36 @@ def test_multi_projection_config2(oracle, cols):
         _bitwise(got, _oracle_matmul(oracle, t, w, x, k, r, cols), name)
 
 
+@pytest.mark.parametrize("cols,residual", [(1, False), (1, True), (5, True), (8, True)])
+def test_matmul_rmsnorm_matches_oracle(oracle, cols, residual):
+    # hpc_matmul_rmsnorm_f32 (the step's norm-fused QKV / gate-up form) against
+    # the oracle's rmsNorm rows -> quantize_q8_k -> prepared matmul, bit for bit
+    from oracle import oracle as o
+    k, eps = 2048, 1e-6
+    specs = [(syn.Q4_K, 16384), (syn.Q6_K, 512)]
+    g = np.random.default_rng(cols + 10 * residual)
+    x = g.normal(0, 1, (cols, k)).astype(np.float32)
+    y = g.normal(0, 3, (cols, k)).astype(np.float32)
+    w_post = (1 + g.normal(0, 0.1, k)).astype(np.float32)
+    w_pre = (1 + g.normal(0, 0.1, k)).astype(np.float32)
+    ws = [syn.quant_weight(t, r, k, seed=70 + i) for i, (t, r) in enumerate(specs)]
+    hs = [hk.create_quantized_weight_handle(TNAME[t], w, k, r) for (t, r), w in zip(specs, ws)]
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    try:
+        outs, h_out = hk.mat_mul_rmsnorm(hs, dev(x), dev(w_pre), cols, y=dev(y) if residual else None,
+                                         w_post=dev(w_post) if residual else None, eps=eps)
+        outs = [t.cpu().numpy() for t in outs]
+    finally:
+        for h in hs:
+            hk.release_quantized_weight_handle(h)
+    h = (x + o.rms_norm_rows(y, w_post, eps)).astype(np.float32) if residual else x
+    if residual:
+        _bitwise(h_out.cpu().numpy().reshape(cols, k), h, "residual stream")
+    n = o.rms_norm_rows(h, w_pre, eps)
+    for (t, r), w, got in zip(specs, ws, outs):
+        _bitwise(got, _oracle_matmul(oracle, t, w, n, k, r, cols), f"type {t} x {r}")
+
+
 def test_one_shot_host_api(oracle):
     k, rows, cols = 1024, 300, 3
     w = syn.quant_weight(syn.Q6_K, rows, k, seed=9)
