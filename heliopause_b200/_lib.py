@@ -24,6 +24,7 @@ SIGNATURES = {
     "hpc_device_init": (_i, [_i]),
     "hpc_device_error": (_i, []),
     "hpc_set_matmul_order": (_i, [_i]),
+    "hpc_set_wide_matmul_kind": (_i, [_i]),
     "hpc_weight_upload": (_i, [_i, _vp, _sz, _sz, _sz, C.POINTER(_vp)]),
     "hpc_weight_upload_device": (_i, [_i, _vp, _sz, _sz, _sz, _vp, C.POINTER(_vp)]),
     "hpc_weight_release": (_i, [_vp]),

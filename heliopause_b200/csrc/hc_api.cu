@@ -559,6 +559,12 @@ int hc_matmul_q8_prologue(size_t count, const hpc_weight* handles, const void* q
 
 extern "C" {
 
+int hpc_set_wide_matmul_kind(int kind) {
+  if (kind != 0 && kind != 1) return fail(HPC_ERR_ARG, "wide matmul kind %d", kind);
+  hc::set_gemm_t5(kind == 1);
+  return HPC_OK;
+}
+
 int hpc_matmul_rmsnorm_f32(size_t count, const hpc_weight* handles, void* d_workspace, size_t workspace_bytes,
                            size_t input_size, size_t column_count, const float* d_x, const float* d_y,
                            const float* d_w_post, const float* d_w_pre, double eps, float* d_x_out,

@@ -142,6 +142,7 @@ static cudaError_t launch_tc(const TcParams& p, cudaStream_t st) {
 }
 
 cudaError_t launch_gemm_tc(const GemvSeg& seg, int nb, const Q8Buf& q, int col0, int ncols, cudaStream_t st) {
+  if (seg.type == TYPE_Q4_K && gemm_t5_enabled()) return launch_gemm_t5(seg, nb, q, col0, ncols, st);
   TcParams p;
   p.w = seg.w;
   p.out = seg.out;

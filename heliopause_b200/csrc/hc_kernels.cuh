@@ -166,5 +166,10 @@ constexpr int TC_MIN_COLS = 16;
 constexpr int GEMV_MMA_MIN_COLS = 3;
 cudaError_t launch_gemv_mma(GemvParams& p, cudaStream_t stream);
 cudaError_t launch_gemm_tc(const GemvSeg& seg, int nb, const Q8Buf& q, int col0, int ncols, cudaStream_t st);
+// The same product for Q4_K on tcgen05 (hc_gemm_t5.cu); HPC_GEMM_T5=1 routes
+// launch_gemm_tc's Q4_K launches here.
+bool gemm_t5_enabled();
+void set_gemm_t5(bool on);
+cudaError_t launch_gemm_t5(const GemvSeg& seg, int nb, const Q8Buf& q, int col0, int ncols, cudaStream_t st);
 
 }  // namespace hc

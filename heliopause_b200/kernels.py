@@ -203,6 +203,12 @@ def mat_mul_quantized_resident_multi(handles, input_columns, input_size: int, co
     return [o.cpu().numpy() for o in outs] if from_host else outs
 
 
+def set_wide_matmul_kind(kind: int) -> None:
+    """Tensor-core kind of the >= 16-column Q4_K matmul: 0 = mma.sync
+    (default), 1 = tcgen05 (hpc_set_wide_matmul_kind)."""
+    assert_cuda_ok(_lib.lib().hpc_set_wide_matmul_kind(int(kind)), "setWideMatmulKind")
+
+
 def mat_mul_rmsnorm(handles, x, w_pre, column_count: int, *, y=None, w_post=None, eps: float = 1e-6):
     """The decode step's norm-fused projection (hpc_matmul_rmsnorm_f32):
     h = x + rmsNorm(y) * w_post (or x when y is None), then every weight

@@ -170,6 +170,14 @@ int hpc_q8_quantize(const float *d_in, size_t in_len, size_t input_size, size_t 
 int hpc_matmul_q8(size_t count, const hpc_weight *handles, const void *d_workspace, size_t workspace_bytes,
                   size_t input_size, size_t column_count, float *const *d_outs, const size_t *out_lens, void *stream);
 
+/* The tensor-core kind of the >= 16-column Q4_K matmul (prefill, the wide LM
+ * head): 0 = mma.sync s8 (default), 1 = tcgen05.mma kind::i8 with the
+ * accumulators in tensor memory.  Both compute the same integer block sums
+ * and the same f32 combine; results are bit-identical where the mma.sync
+ * launch does not split K (it splits launches of fewer than two CTAs per
+ * SM in two halves, added atomically).  Process-wide. */
+int hpc_set_wide_matmul_kind(int kind);
+
 /* The norm-fused projection of the decode step: the rmsNorm of the residual
  * stream (wasm/layers.ts:161-247 -- optionally after adding the previous
  * projection through its post-norm), quantize_q8_k (lib.rs:1774-1811) and

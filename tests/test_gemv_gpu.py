@@ -201,6 +201,26 @@ def test_matmul_rmsnorm_matches_oracle(oracle, cols, residual):
         _bitwise(got, _oracle_matmul(oracle, t, w, n, k, r, cols), f"type {t} x {r}")
 
 
+@pytest.mark.parametrize("rows,k,cols", [(256, 512, 64), (1000, 768, 70), (16384, 2048, 512), (32, 256, 16)])
+def test_tcgen05_matmul_equals_mma_sync(rows, k, cols):
+    # the tcgen05 kind::i8 matmul (split 3-bit scale halves, accumulators in
+    # tensor memory) against the mma.sync one: the same integer block sums and
+    # f32 combine, so the outputs are bit-identical (shapes whose mma.sync
+    # launch does not split K)
+    w = syn.quant_weight(syn.Q4_K, rows, k, seed=rows + cols)
+    x = torch.from_numpy(syn.activations(cols, k, seed=cols + 3)).cuda()
+    h = hk.create_quantized_weight_handle("Q4_K", w, k, rows)
+    try:
+        hk.set_wide_matmul_kind(0)
+        ref = hk.mat_mul_quantized_resident(h, x, k, rows, cols).cpu().numpy()
+        hk.set_wide_matmul_kind(1)
+        got = hk.mat_mul_quantized_resident(h, x, k, rows, cols).cpu().numpy()
+    finally:
+        hk.set_wide_matmul_kind(0)
+        hk.release_quantized_weight_handle(h)
+    _bitwise(got, ref, "tcgen05 vs mma.sync")
+
+
 def test_one_shot_host_api(oracle):
     k, rows, cols = 1024, 300, 3
     w = syn.quant_weight(syn.Q6_K, rows, k, seed=9)
