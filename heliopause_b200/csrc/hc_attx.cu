@@ -19,7 +19,9 @@
 //                          K/V rows (written to the cache), one sequential
 //                          256-term dot per (query, key);
 //   hc_attx_softmax_kernel grid (tokens x heads): the max, the f64 exps, the
-//                          one 4096-term sequential sum, the divisions;
+//                          4096-term sequential sum (evaluated as integer
+//                          runs inside binades, the same f32 value), the
+//                          divisions;
 //   hc_attx_pv_kernel      grid (KV head x 32-dim slice, groups of 4 query
 //                          vectors): one sequential chain per (query, dim)
 //                          over all keys, lane = dim, then the TS f16 cast of
@@ -219,92 +221,234 @@ __global__ void __launch_bounds__(256) hc_attx_scores_kernel(
   }
 }
 
-// The exps run in rounds of AX_SM_ROUND keys on warps 1 .. 31; a round's
-// named barrier (warps 1 .. 31 arrive, warp 0 waits) hands it to thread 0,
-// whose sequential sum then overlaps the later rounds' exps.
-constexpr int AX_SM_ROUND = AX_SM_THREADS - 32;  // 992 keys: at most 5 rounds (named barriers 1 .. 5)
-static_assert(AX_SM_ROUND % 32 == 0, "rounds of whole 32-key blocks");
+// The sequential f32 sum of the probabilities (lib.rs:627-635), computed in
+// parallel with the same result.  While the running sum stays inside one
+// binade [2^e, 2^(e+1)) every partial sum is a multiple of u = 2^(e-23), so
+// fl(s + x) = s + u*k with k = x/u rounded to the nearest integer (x >= 0,
+// no tie): the adds of a run inside one binade are integer adds and may be
+// regrouped.  (Below 2^-125 the grid is 2^-149 and every add is exact: binade
+// index -126.)  An f64 prefix sum P locates the partial sums: the sum only
+// grows, so after j + 1 terms |s_j - P_j| <= (j + 1) 2^-24 s_j, and s_j is at
+// least the largest term so far.  A key whose bracket
+// [max(P_{j-1}(1 - m), max_{i<j} x_i), P_j (1 + m)], m = (j + 2) 2^-23, lies in
+// one binade and whose x/u is not a tie is "safe": its add is u*k.  The
+// others (key 0, binade crossings, ties, brackets that touch a boundary) are
+// added in key order by one thread, each followed by the integer total of
+// the safe run after it, which is the partial sum the dependent chain
+// reaches at the run's end.
+constexpr int AX_SM_KPT = 4;      // keys per thread: 4 x 1024 covers the 4096-slot cap
+constexpr int AX_SM_LIST = 1024;  // unsafe keys held; more take the plain chain
+static_assert(AX_SM_KPT * AX_SM_THREADS == 4096, "one pass over the largest key count");
+
+__device__ __forceinline__ int binade_index(double v) {  // v >= 0
+  const int e = int((__double_as_longlong(v) >> 52) & 0x7ff) - 1023;
+  return v > 0.0 ? max(e, -126) : -126;
+}
 
 __global__ void __launch_bounds__(AX_SM_THREADS) hc_attx_softmax_kernel(const float* __restrict__ scores,
                                                                         const int32_t* __restrict__ pos, int M, int H,
                                                                         int cap, float* __restrict__ rprob) {
-  __shared__ __align__(16) float ps[4096 + 32];  // 32 spare words: the sum's last prefetch reads past the keys
-  __shared__ float red[AX_SM_THREADS / 32];
+  __shared__ __align__(16) float ps[4096];
+  __shared__ signed char eb[4096];           // binade index of each key's bracket
+  __shared__ int uq[AX_SM_LIST];             // unsafe keys, in order
+  __shared__ unsigned uk[AX_SM_LIST + 1];    // sum of the safe k before each unsafe key (+ the total)
+  __shared__ __align__(8) float2 xr[AX_SM_LIST];  // per unsafe key: its term, the run after it
+  __shared__ double dsum[32];
+  __shared__ float fmx[32], fpm[32];
+  __shared__ int nsum[32];
+  __shared__ unsigned ksum[32];
+  __shared__ int s_nuns;
   __shared__ float s_sum;
   const int m = int(blockIdx.x) / H, h = int(blockIdx.x) % H;
+  const int t = int(threadIdx.x), lane = t & 31, w = t >> 5;
   pdl_trigger();
   const KeyRange kr = key_range(pos, M, cap);
   pdl_wait();
-  // the max over every key (exact and order-free; -inf never wins over a
-  // visible key, and every token sees its own key)
   const float* sc = scores + (size_t(m) * H + h) * cap;
+  const int j0 = AX_SM_KPT * t;
+  float x[AX_SM_KPT];
   float mx = -INFINITY;
-  for (int j = int(threadIdx.x); j < kr.count; j += int(blockDim.x)) {
-    const float s = sc[j];
-    ps[j] = s;
-    mx = fmaxf(mx, s);
+#pragma unroll
+  for (int i = 0; i < AX_SM_KPT; ++i) {
+    x[i] = j0 + i < kr.count ? sc[j0 + i] : -INFINITY;
+    mx = fmaxf(mx, x[i]);
   }
+  // the max over every key (exact and order-free; every token sees its own key)
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+  if (lane == 0) fmx[w] = mx;
   __syncthreads();
-  mx = -INFINITY;
-  for (int w = 0; w < int(blockDim.x >> 5); ++w) mx = fmaxf(mx, red[w]);
-  const int rounds = (kr.count + AX_SM_ROUND - 1) / AX_SM_ROUND;
-  if (threadIdx.x >= 32) {
-    for (int r = 0; r < rounds; ++r) {
-      const int j = r * AX_SM_ROUND + int(threadIdx.x) - 32;
-      if (j < kr.count) {
-        const float s = ps[j];
-        ps[j] = s == -INFINITY ? 0.0f : float(exp(double(__fsub_rn(s, mx))));
-      }
-      asm volatile("bar.arrive %0, %1;" ::"r"(1 + r), "r"(AX_SM_THREADS) : "memory");
+  mx = fmx[lane];
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+  // the terms, their f64 prefix sums and running maxima
+  double c[AX_SM_KPT];
+  double run = 0.0;
+  float pmax = 0.0f;
+#pragma unroll
+  for (int i = 0; i < AX_SM_KPT; ++i) {
+    x[i] = x[i] == -INFINITY ? 0.0f : float(exp(double(__fsub_rn(x[i], mx))));
+    run += double(x[i]);
+    c[i] = run;
+    pmax = fmaxf(pmax, x[i]);
+  }
+  reinterpret_cast<float4*>(ps)[t] = make_float4(x[0], x[1], x[2], x[3]);
+  double incl = run;
+  float pm = pmax;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const double v = __shfl_up_sync(0xffffffffu, incl, off);
+    const float q = __shfl_up_sync(0xffffffffu, pm, off);
+    if (lane >= off) {
+      incl += v;
+      pm = fmaxf(pm, q);
     }
-  } else {
-    // warp 0: thread 0 adds round by round, one dependent add per key
-    // (lib.rs:627-635).  A round is 31 blocks of 32 keys; a block's 32 keys
-    // are loaded (as two 16-key halves, eight broadcast 16-byte reads) while
-    // the previous half is added, with no branch inside the loop.
-    float sum = 0.0f;
-    const float4* p4 = reinterpret_cast<const float4*>(ps);
-    for (int r = 0; r < rounds; ++r) {
-      asm volatile("bar.sync %0, %1;" ::"r"(1 + r), "r"(AX_SM_THREADS) : "memory");
-      if (threadIdx.x == 0) {
-        const int j0 = r * AX_SM_ROUND, j1 = min(kr.count, j0 + AX_SM_ROUND);
-        const int n32 = (j1 - j0) / 32;
-        float4 a[4], b[4];
+  }
+  if (lane == 31) {
+    dsum[w] = incl;
+    fpm[w] = pm;
+  }
+  double excl = __shfl_up_sync(0xffffffffu, incl, 1);
+  float pex = __shfl_up_sync(0xffffffffu, pm, 1);
+  if (lane == 0) {
+    excl = 0.0;
+    pex = 0.0f;
+  }
+  __syncthreads();
+  if (w == 0) {
+    const double v = dsum[lane];
+    const float q = fpm[lane];
+    double iv = v;
+    float iq = q;
 #pragma unroll
-        for (int i = 0; i < 4; ++i) a[i] = p4[j0 / 4 + i];
-        for (int blk = 0; blk < n32; ++blk) {
-          const int q = (j0 + 32 * blk) / 4;  // float4 index of the block
+    for (int off = 1; off < 32; off <<= 1) {
+      const double a = __shfl_up_sync(0xffffffffu, iv, off);
+      const float b = __shfl_up_sync(0xffffffffu, iq, off);
+      if (lane >= off) {
+        iv += a;
+        iq = fmaxf(iq, b);
+      }
+    }
+    double ev = __shfl_up_sync(0xffffffffu, iv, 1);
+    float eq = __shfl_up_sync(0xffffffffu, iq, 1);
+    if (lane == 0) {
+      ev = 0.0;
+      eq = 0.0f;
+    }
+    dsum[lane] = ev;
+    fpm[lane] = eq;
+  }
+  __syncthreads();
+  // classify this thread's keys
+  double prev = dsum[w] + excl;
+  float xmax = fmaxf(fpm[w], pex);  // largest term before the key
+  unsigned kk[AX_SM_KPT];
+  bool uns[AX_SM_KPT];
+  int nu = 0;
+  unsigned kl = 0;
 #pragma unroll
-          for (int i = 0; i < 4; ++i) b[i] = p4[q + 4 + i];
+  for (int i = 0; i < AX_SM_KPT; ++i) {
+    const int j = j0 + i;
+    const double cur = dsum[w] + excl + c[i];
+    const double mg = double(j + 2) * 0x1p-23;
+    const double lo = fmax(prev * (1.0 - mg), double(xmax)), hi = cur * (1.0 + mg);
+    const int e = binade_index(lo);
+    bool safe = j > 0 && binade_index(hi) == e;
+    unsigned k = 0;
+    if (safe) {
+      const double r = double(x[i]) * __longlong_as_double((long long)(23 - e + 1023) << 52);  // x / u, exact
+      const double fl = floor(r), fr = r - fl;
+      safe = fr != 0.5;
+      k = unsigned(fl) + (fr > 0.5 ? 1u : 0u);
+    }
+    uns[i] = !safe;
+    kk[i] = safe ? k : 0u;
+    nu += safe ? 0 : 1;
+    kl += kk[i];
+    eb[j] = (signed char)e;
+    prev = cur;
+    xmax = fmaxf(xmax, x[i]);
+  }
+  // positions of the unsafe keys and the k totals before them
+  int ni = nu;
+  unsigned ki = kl;
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            sum = __fadd_rn(sum, a[i].x);
-            sum = __fadd_rn(sum, a[i].y);
-            sum = __fadd_rn(sum, a[i].z);
-            sum = __fadd_rn(sum, a[i].w);
-          }
+  for (int off = 1; off < 32; off <<= 1) {
+    const int a = __shfl_up_sync(0xffffffffu, ni, off);
+    const unsigned b = __shfl_up_sync(0xffffffffu, ki, off);
+    if (lane >= off) {
+      ni += a;
+      ki += b;
+    }
+  }
+  if (lane == 31) {
+    nsum[w] = ni;
+    ksum[w] = ki;
+  }
+  __syncthreads();
+  if (w == 0) {
+    int iv = nsum[lane];
+    unsigned ik = ksum[lane];
 #pragma unroll
-          for (int i = 0; i < 4; ++i) a[i] = p4[q + 8 + i];
+    for (int off = 1; off < 32; off <<= 1) {
+      const int a = __shfl_up_sync(0xffffffffu, iv, off);
+      const unsigned b = __shfl_up_sync(0xffffffffu, ik, off);
+      if (lane >= off) {
+        iv += a;
+        ik += b;
+      }
+    }
+    nsum[lane] = iv - nsum[lane];  // exclusive
+    ksum[lane] = ik - ksum[lane];
+    if (lane == 31) {
+      uk[AX_SM_LIST] = ik;  // the total, read as the end of the last run
+      s_nuns = iv;
+    }
+  }
+  __syncthreads();
+  const int n_uns = s_nuns;
+  {
+    int idx = nsum[w] + ni - nu;
+    unsigned kb = ksum[w] + ki - kl;
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            sum = __fadd_rn(sum, b[i].x);
-            sum = __fadd_rn(sum, b[i].y);
-            sum = __fadd_rn(sum, b[i].z);
-            sum = __fadd_rn(sum, b[i].w);
-          }
+    for (int i = 0; i < AX_SM_KPT; ++i) {
+      if (uns[i]) {
+        if (idx < AX_SM_LIST) {
+          uq[idx] = j0 + i;
+          uk[idx] = kb;
         }
-        for (int j = j0 + 32 * n32; j < j1; ++j) sum = __fadd_rn(sum, ps[j]);
+        ++idx;
       }
+      kb += kk[i];
     }
-    if (threadIdx.x == 0) s_sum = sum;
+  }
+  __syncthreads();
+  if (n_uns <= AX_SM_LIST) {
+    // per unsafe key: its term and the exact value of the safe run after it
+    for (int i = t; i < n_uns; i += AX_SM_THREADS) {
+      const int q = uq[i];
+      const unsigned kend = i + 1 < n_uns ? uk[i + 1] : uk[AX_SM_LIST];
+      const unsigned K = kend - uk[i];
+      xr[i] = make_float2(ps[q], K != 0u ? ldexpf(float(K), int(eb[min(q + 1, 4095)]) - 23) : 0.0f);
+    }
+    __syncthreads();
+    if (t == 0) {
+      float s = 0.0f;
+      for (int i = 0; i < n_uns; ++i) {
+        const float2 v = xr[i];
+        s = __fadd_rn(__fadd_rn(s, v.x), v.y);
+      }
+      s_sum = s;
+    }
+  } else if (t == 0) {
+    float s = 0.0f;
+    for (int j = 0; j < kr.count; ++j) s = __fadd_rn(s, ps[j]);
+    s_sum = s;
   }
   __syncthreads();
   const float sum = s_sum;
   float* r = rprob + (size_t(m) * H + h) * cap;
-  for (int j = int(threadIdx.x); j < kr.count; j += int(blockDim.x)) r[j] = __fdiv_rn(ps[j], sum);
+  for (int j = t; j < kr.count; j += AX_SM_THREADS) r[j] = __fdiv_rn(ps[j], sum);
 }
 
 // One chain warp's pass over a full stage: out += fround(r_j * v_j) key by
