@@ -22,7 +22,7 @@
 //                          4096-term sequential sum (evaluated as integer
 //                          runs inside binades, the same f32 value), the
 //                          divisions;
-//   hc_attx_pv_kernel      grid (KV head x 32-dim slice, groups of 4 query
+//   hc_attx_pv_kernel      grid (KV head x 32-dim slice, groups of 1-4 query
 //                          vectors): one sequential chain per (query, dim)
 //                          over all keys, lane = dim, then the TS f16 cast of
 //                          the output (castF16Rows, layers.ts:982-988).  A
@@ -32,7 +32,7 @@
 //                          (per-key bulk copies where the stage wraps the
 //                          slot ring) and the group's probabilities as one
 //                          bulk copy per query, completion on the stage's
-//                          mbarrier; the four chain warps do nothing but the
+//                          mbarrier; the chain warps do nothing but the
 //                          chain, whose dependent adds bound the kernel.
 // The Q8_K quantization of the cast output for the O projection follows as
 // its own launch.
@@ -56,13 +56,12 @@ constexpr int AX_CH = 64;            // key slots per scores CTA
 constexpr int AX_KSTRIDE = 256 + 4;  // floats per staged K row (conflict-free 16-byte reads)
 constexpr int AX_QL = 4;             // query lanes of the scores CTA (256 threads / 64 keys)
 constexpr int AX_SM_THREADS = 1024;  // softmax CTA
-constexpr int AX_PV_QG = 4;          // query vectors per PV CTA (one chain warp each)
+constexpr int AX_PV_CW_MAX = 4;      // chain warps per PV CTA, at most
 constexpr int AX_PV_TC = 256;        // keys per ring stage
 constexpr int AX_PV_NS = 4;          // ring stages (three stages of copies ahead of the chain)
 constexpr int AX_PV_DS = 32;         // dims per CTA: one per lane
-constexpr int AX_PV_THREADS = 32 * (AX_PV_QG + 1);  // chain warps + the producer warp
-// floats per stage: V [TC][64], probabilities [QG][TC]
-constexpr int AX_PV_STAGE = AX_PV_TC * AX_PV_DS + AX_PV_QG * AX_PV_TC;
+// floats per stage: V [TC][32], probabilities [QG][TC]
+__host__ __device__ constexpr int pv_stage_floats(int qg) { return AX_PV_TC * AX_PV_DS + qg * AX_PV_TC; }
 
 struct KeyRange {
   int count, start, maxpos;
@@ -486,12 +485,17 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
 }
 
 // vmap: the V cache as a 2-D f32 tensor [cap slots][KVH * 256], box [256][32].
-__global__ void __launch_bounds__(AX_PV_THREADS) hc_attx_pv_kernel(const __grid_constant__ CUtensorMap vmap,
+// CW chain warps (one query vector each) share a CTA's V stages; the
+// launcher picks the fewest whose grid fits one CTA per SM.
+template <int CW>
+__global__ void __launch_bounds__(32 * (CW + 1)) hc_attx_pv_kernel(const __grid_constant__ CUtensorMap vmap,
                                                                    const float* __restrict__ rprob,
                                                                    const float* __restrict__ vc,
                                                                    const int32_t* __restrict__ pos, int M, int H,
                                                                    int KVH, int cap, float* __restrict__ out16,
                                                                    int* err) {
+  constexpr int AX_PV_QG = CW;  // query vectors per CTA
+  constexpr int AX_PV_STAGE = pv_stage_floats(AX_PV_QG);
   extern __shared__ __align__(128) float pv_smem[];  // [NS][AX_PV_STAGE]
   __shared__ __align__(8) uint64_t full[AX_PV_NS], empty[AX_PV_NS];
   constexpr int SLICES = 256 / AX_PV_DS;  // dim slices per KV head
@@ -505,14 +509,14 @@ __global__ void __launch_bounds__(AX_PV_THREADS) hc_attx_pv_kernel(const __grid_
   if (threadIdx.x == 0) {
     for (int s = 0; s < AX_PV_NS; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], AX_PV_QG);
+      mbar_init(&empty[s], CW);
     }
   }
   __syncthreads();
   pdl_wait();  // the probabilities (previous launch) and this step's V rows (two launches back)
-  if (warp == AX_PV_QG) {
+  if (warp == CW) {
     // producer: stage c % NS holds keys [256c, 256c + n); it is refilled once
-    // the four chain warps have released it
+    // the chain warps have released it
     int y0 = kr.start;  // slot of the stage's first key
     int issued = 0;
     bool ok = true;
@@ -557,7 +561,7 @@ __global__ void __launch_bounds__(AX_PV_THREADS) hc_attx_pv_kernel(const __grid_
         mbar_wait_parity(&full[c % AX_PV_NS], uint32_t(c / AX_PV_NS) & 1u, nullptr);
     return;
   }
-  // chain warps: query vector qg * 4 + warp, lane = dim ds * 32 + lane
+  // chain warps: query vector qg * QG + warp, lane = dim ds * 32 + lane
   const bool active = warp < nq;
   float acc = 0.0f;
   bool ok = true;
@@ -633,6 +637,22 @@ static cudaError_t encode_v_map(CUtensorMap* map, const float* vc, int KVH, int 
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
+static size_t pv_smem_bytes(int qg) { return sizeof(float) * AX_PV_NS * size_t(pv_stage_floats(qg)); }
+
+template <int CW>
+static cudaError_t pv_set_smem() {
+  return cudaFuncSetAttribute(hc_attx_pv_kernel<CW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              int(pv_smem_bytes(CW)));
+}
+
+template <int CW>
+static cudaError_t pv_launch(int slices, int NQ, cudaStream_t st, const CUtensorMap& vmap, const float* rprob,
+                             const float* vc, const int32_t* pos, int M, int H, int KVH, int cap, float* out16,
+                             int* err) {
+  return pdl_launch_x(hc_attx_pv_kernel<CW>, dim3(slices, (NQ + CW - 1) / CW), dim3(32 * (CW + 1)), pv_smem_bytes(CW),
+                      st, vmap, rprob, vc, pos, M, H, KVH, cap, out16, err);
+}
+
 cudaError_t launch_attention_exact(const float* q, const float* kraw, const float* vraw, const float* qnw,
                                    const float* knw, const double* cos_t, const double* sin_t, double eps, bool own_kv,
                                    float* kc, float* vc, const int32_t* pos, int M, int H, int KVH, int cap,
@@ -640,13 +660,14 @@ cudaError_t launch_attention_exact(const float* q, const float* kraw, const floa
   if (cap % AX_CH != 0 || cap > 4096) return cudaErrorInvalidValue;
   const size_t smem = attx_scores_smem_bytes(M, H, KVH);
   if (smem > ATT_MAX_SMEM) return cudaErrorInvalidValue;
-  constexpr size_t pv_smem = sizeof(float) * AX_PV_NS * AX_PV_STAGE;
   static std::atomic<uint64_t> attr{0};
   const cudaError_t ea = once_per_current_device(attr, [] {
     cudaError_t e = cudaFuncSetAttribute(hc_attx_scores_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          int(ATT_MAX_SMEM));
-    if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(hc_attx_pv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(pv_smem));
+    if (e == cudaSuccess) e = pv_set_smem<1>();
+    if (e == cudaSuccess) e = pv_set_smem<2>();
+    if (e == cudaSuccess) e = pv_set_smem<3>();
+    if (e == cudaSuccess) e = pv_set_smem<4>();
     return e;
   });
   if (ea != cudaSuccess) return ea;
@@ -662,9 +683,17 @@ cudaError_t launch_attention_exact(const float* q, const float* kraw, const floa
   CUtensorMap vmap;
   e = encode_v_map(&vmap, vc, KVH, cap);
   if (e != cudaSuccess) return e;
-  return pdl_launch_x(hc_attx_pv_kernel, dim3(KVH * (256 / AX_PV_DS), (NQ + AX_PV_QG - 1) / AX_PV_QG),
-                      dim3(AX_PV_THREADS), pv_smem,
-                      st, vmap, rprob, vc, pos, M, H, KVH, cap, out16, device_status_word());
+  // the fewest chain warps (query vectors) per CTA whose grid fits one CTA per SM
+  const int slices = KVH * (256 / AX_PV_DS);
+  int cw = 1;
+  while (cw < AX_PV_CW_MAX && slices * ((NQ + cw - 1) / cw) > sm_count()) ++cw;
+  int* err = device_status_word();
+  switch (cw) {
+    case 1: return pv_launch<1>(slices, NQ, st, vmap, rprob, vc, pos, M, H, KVH, cap, out16, err);
+    case 2: return pv_launch<2>(slices, NQ, st, vmap, rprob, vc, pos, M, H, KVH, cap, out16, err);
+    case 3: return pv_launch<3>(slices, NQ, st, vmap, rprob, vc, pos, M, H, KVH, cap, out16, err);
+    default: return pv_launch<4>(slices, NQ, st, vmap, rprob, vc, pos, M, H, KVH, cap, out16, err);
+  }
 }
 
 }  // namespace hc
