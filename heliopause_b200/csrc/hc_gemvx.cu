@@ -26,6 +26,7 @@
 // Activations are read as plane-A/B Q8_K records straight from global
 // memory (every lane reads the same record words; they stay in L1/L2).
 #include <cooperative_groups.h>
+#include <cuda_fp16.h>
 
 #include <cstdlib>
 
@@ -438,6 +439,209 @@ __global__ void __launch_bounds__(GX_THREADS, 1) hc_gemvw_kernel(const __grid_co
     for (int v = 0; v < issued; ++v) mbar_wait_parity(wb + (v % R), uint32_t(v / R) & 1u, nullptr);
 }
 
+// ---- tensor-core lane sums (Q4_K rows of at most 16 blocks, 2..8 columns) ----
+//
+// The warp-per-tile form with the integer lane sums of every column on
+// mma.sync s8 m16n8k32.  The reference's lane l of a block (elements l,
+// l + 8, l + 16, l + 24 of each 32-group) has the integer sum
+//     aux32[l] = sum_g sc_g * dot_g,l       (sc_g: the 6-bit group scale).
+// Split sc_g = 8 * hi_g + lo_g (3 bits each): q * lo_g and q * hi_g are at
+// most 15 * 7 = 105, so the pre-scaled 4-bit values are int8 operands and
+//     aux32[l] = D0 + 8 * D1,  D0 = sum_g dot(q * lo_g, q8), D1 = the same with hi_g,
+// two 32-deep MMAs whose K runs over lane l's four elements of all eight
+// groups (thread t's K slots are groups 2t and 2t + 1: exactly word l of quant
+// pair t, low and high nibbles; the B fragment is the activation record's
+// words of the same groups and lane).  Exact integers, so the f32 part --
+// the reference's nine accumulators per (row, column), advanced per block in
+// block order -- is the warp-per-tile form's, and the outputs are the same
+// bit for bit.  A work item is one 16-row half of a tile (one m16 tile) and
+// every column of the launch, so the weight-side work (unpacking, scaling)
+// is shared by all columns; lane (g = lane / 4, t = lane % 4) holds rows
+// g, g + 8 of the half and columns 2t, 2t + 1 (the m16n8 accumulator layout).
+__device__ __forceinline__ Q4KHeader q4k_header_hw(const uint4 h) {  // f16 by the hardware conversion (exact)
+  Q4KHeader r;
+  r.d = __half2float(__ushort_as_half(static_cast<unsigned short>(h.x & 0xffffu)));
+  r.dmin = __half2float(__ushort_as_half(static_cast<unsigned short>(h.x >> 16)));
+  r.sc_lo = h.y & 0x3f3f3f3fu;
+  r.mn_lo = h.z & 0x3f3f3f3fu;
+  r.sc_hi = (h.w & 0x0f0f0f0fu) | ((h.y >> 2) & 0x30303030u);
+  r.mn_hi = ((h.w >> 4) & 0x0f0f0f0fu) | ((h.z >> 2) & 0x30303030u);
+  return r;
+}
+
+__device__ __forceinline__ void mma_k32_gx(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                           uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
+      : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+}
+
+__device__ __forceinline__ uint32_t u4_word(const uint4& v, int i) {
+  return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
+}
+
+constexpr int GT_MAX_SMEM = 110 * 1024;  // two CTAs per SM
+
+__global__ void __launch_bounds__(GX_THREADS, 2) hc_gemvt_kernel(const __grid_constant__ GemvxParams p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ __align__(8) uint64_t bars[GX_WARPS * GX_MAX_R];
+  __shared__ __align__(8) uint64_t act_bar;
+  const int lane = int(threadIdx.x) & 31, warp = int(threadIdx.x) >> 5;
+  const int g = lane >> 2, t = lane & 3;
+  pdl_trigger();
+  const int R = p.R, nb = p.nb, ncols = p.ncols;
+  const int nitems = 2 * p.total_tiles;  // item = (tile, 16-row half), every column
+  const int gw = warp * int(gridDim.x) + int(blockIdx.x), nw = GX_WARPS * int(gridDim.x);
+  const int nmine = gw < nitems ? (nitems - 1 - gw) / nw + 1 : 0;
+  const int n = nmine * nb;  // this warp's units
+  uint8_t* ring = smem + size_t(warp) * R * p.slot;
+  uint8_t* act_a = smem + size_t(GX_WARPS) * R * p.slot;                       // [ncols][nb][288]
+  uint8_t* act_b = act_a + ((p.planes & 1) ? size_t(ncols) * nb * Q8A_REC : 0);  // written by the prologue only
+  uint64_t* wb = bars + warp * R;
+
+  int is_item = gw, is_b = 0, is_s = 0;
+  auto issue_next = [&]() {
+    const int tile = is_item >> 1;
+    const GemvSeg& sg = p.seg[gx_seg_of(p, tile)];
+    uint64_t* bar = wb + is_s;
+    mbar_expect_tx(bar, uint32_t(Q4K_TILE_BLOCK_BYTES));
+    bulk_copy_g2s(ring + size_t(is_s) * p.slot,
+                  sg.w + (size_t(tile - sg.tile_begin) * nb + is_b) * Q4K_TILE_BLOCK_BYTES,
+                  uint32_t(Q4K_TILE_BLOCK_BYTES), bar);
+    if (++is_b == nb) {
+      is_b = 0;
+      is_item += nw;
+    }
+    if (++is_s == R) is_s = 0;
+  };
+  const int primed = n < R ? n : R;
+  if (lane == 0) {
+    for (int s = 0; s < R; ++s) mbar_init(wb + s, 1);
+    for (int u = 0; u < primed; ++u) issue_next();
+  }
+  __syncwarp();
+  pdl_wait();  // the activation records are written by the previous kernel
+  if (p.pro.mode != GEMV_PRO_NONE) {
+    gx_prologue(p, act_a, act_b, 0, warp, lane);
+    if (threadIdx.x == 0) {
+      mbar_init(&act_bar, 1);
+      mbar_arrive(&act_bar);
+    }
+  } else if (threadIdx.x == 0) {
+    mbar_init(&act_bar, 1);
+    mbar_expect_tx(&act_bar, uint32_t(size_t(ncols) * nb * Q8A_REC));
+    for (int c = 0; c < ncols; ++c) {
+      const size_t rec0 = size_t(p.col0 + c) * nb;
+      bulk_copy_g2s(act_a + size_t(c) * nb * Q8A_REC, p.q.a + rec0 * Q8A_REC, uint32_t(nb * Q8A_REC), &act_bar);
+    }
+  }
+  __syncthreads();
+  bool ok = mbar_wait_parity(&act_bar, 0, p.err);
+  const bool bcol = g < ncols;                                  // B fragment column g
+  const bool ccol0 = 2 * t < ncols, ccol1 = 2 * t + 1 < ncols;  // accumulator columns 2t, 2t + 1
+  int issued = primed, u = 0, rs = 0;
+  uint32_t rph = 0;
+  for (int it = 0; it < nmine; ++it) {
+    const int item = gw + it * nw, tile = item >> 1, r0 = 16 * (item & 1) + g;  // rows r0, r0 + 8
+    const GemvSeg& sg = p.seg[gx_seg_of(p, tile)];
+    LaneChain ch[4];  // pair 2i + cc: row r0 + 8i, column 2t + cc
+#pragma unroll
+    for (int k = 0; k < 4; ++k) ch[k].zero();
+    for (int b = 0; b < nb; ++b, ++u) {
+      if (ok && !mbar_wait_parity_sleep(wb + rs, rph, p.err)) ok = false;
+      if (ok) {
+        const uint8_t* unit = ring + size_t(rs) * p.slot;
+        float dd[2], dm[2];
+        uint32_t mnl[2], mnh[2], s0a[2], s1a[2], s0b[2], s1b[2];
+        uint4 qlo[2], qhi[2];
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+          const int row = r0 + 8 * i;
+          const Q4KHeader hd = q4k_header_hw(*reinterpret_cast<const uint4*>(unit + row * 16));
+          dd[i] = hd.d;
+          dm[i] = hd.dmin;
+          mnl[i] = hd.mn_lo;
+          mnh[i] = hd.mn_hi;
+          const uint32_t sw = t < 2 ? hd.sc_lo : hd.sc_hi, sh = 16u * uint32_t(t & 1);
+          const uint32_t sa = (sw >> sh) & 0xffu, sb = (sw >> (sh + 8u)) & 0xffu;  // groups 2t, 2t + 1
+          s0a[i] = sa & 7u;
+          s1a[i] = sa >> 3;
+          s0b[i] = sb & 7u;
+          s1b[i] = sb >> 3;
+          qlo[i] = *reinterpret_cast<const uint4*>(unit + (1 + 2 * t) * 512 + row * 16);
+          qhi[i] = *reinterpret_cast<const uint4*>(unit + (2 + 2 * t) * 512 + row * 16);
+        }
+        // B: column g's words of groups 2t (lanes 0..7) and 2t + 1
+        uint4 bl0 = make_uint4(0, 0, 0, 0), bl1 = bl0, bh0 = bl0, bh1 = bl0;
+        if (bcol) {
+          const uint8_t* rec = act_a + (size_t(g) * nb + b) * Q8A_REC + 64 * t;
+          bl0 = *reinterpret_cast<const uint4*>(rec);
+          bl1 = *reinterpret_cast<const uint4*>(rec + 16);
+          bh0 = *reinterpret_cast<const uint4*>(rec + 32);
+          bh1 = *reinterpret_cast<const uint4*>(rec + 48);
+        }
+        // per (row, column) pair: d * d8, dmin * d8 and the min sum
+        float pd[4], pm[4];
+        int ms[4];
+#pragma unroll
+        for (int cc = 0; cc < 2; ++cc) {
+          const bool cok = cc == 0 ? ccol0 : ccol1;
+          const uint8_t* rec = act_a + (size_t(cok ? 2 * t + cc : 0) * nb + b) * Q8A_REC;
+          const uint4 bs = *reinterpret_cast<const uint4*>(rec + Q8A_BS);
+          const float d8 = *reinterpret_cast<const float*>(rec + Q8A_D);
+#pragma unroll
+          for (int i = 0; i < 2; ++i) {
+            pd[2 * i + cc] = __fmul_rn(dd[i], d8);
+            pm[2 * i + cc] = __fmul_rn(dm[i], d8);
+            int m = __dp2a_lo(int(bs.x), int(mnl[i]), 0);
+            m = __dp2a_hi(int(bs.y), int(mnl[i]), m);
+            m = __dp2a_lo(int(bs.z), int(mnh[i]), m);
+            ms[2 * i + cc] = __dp2a_hi(int(bs.w), int(mnh[i]), m);
+          }
+        }
+#pragma unroll
+        for (int l = 0; l < 8; ++l) {
+          const uint32_t b0 = u4_word(l < 4 ? bl0 : bl1, l & 3), b1 = u4_word(l < 4 ? bh0 : bh1, l & 3);
+          const uint32_t w0 = u4_word(l < 4 ? qlo[0] : qhi[0], l & 3);
+          const uint32_t w1 = u4_word(l < 4 ? qlo[1] : qhi[1], l & 3);
+          const uint32_t lo0 = w0 & 0x0f0f0f0fu, lo1 = w1 & 0x0f0f0f0fu;
+          const uint32_t hi0 = (w0 >> 4) & 0x0f0f0f0fu, hi1 = (w1 >> 4) & 0x0f0f0f0fu;
+          int d0[4], d1[4];
+          mma_k32_gx(d0, lo0 * s0a[0], lo1 * s0a[1], hi0 * s0b[0], hi1 * s0b[1], b0, b1);
+          mma_k32_gx(d1, lo0 * s1a[0], lo1 * s1a[1], hi0 * s1b[0], hi1 * s1b[1], b0, b1);
+#pragma unroll
+          for (int r = 0; r < 4; ++r)  // r: (row r0 + 8 (r >> 1), column 2t + (r & 1)) = pair r
+            ch[r].s[l] = __fadd_rn(ch[r].s[l], __fmul_rn(pd[r], float(d0[r] + 8 * d1[r])));
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) ch[k].m = __fsub_rn(ch[k].m, __fmul_rn(pm[k], float(ms[k])));
+      }
+      __syncwarp();  // every lane has read the slot: refill it
+      if (u + R < n && ok) {
+        if (lane == 0) issue_next();
+        ++issued;
+      }
+      if (++rs == R) {
+        rs = 0;
+        rph ^= 1u;
+      }
+    }
+    if (ok) {
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const int row = (tile - sg.tile_begin) * TILE + r0 + 8 * i;
+        if (row < sg.rows) {
+          if (ccol0) sg.out[size_t(p.col0 + 2 * t) * sg.rows + row] = ch[2 * i].total(true);
+          if (ccol1) sg.out[size_t(p.col0 + 2 * t + 1) * sg.rows + row] = ch[2 * i + 1].total(true);
+        }
+      }
+    }
+  }
+  if (!ok)
+    for (int v = 0; v < issued; ++v) mbar_wait_parity(wb + (v % R), uint32_t(v / R) & 1u, nullptr);
+}
+
 // ---- relay form (long rows: nb = 8 * NBP blocks) ------------------------------
 //
 // One CTA per (tile, column): warp w owns blocks [w * NBP, (w + 1) * NBP) of
@@ -599,7 +803,7 @@ static char gemvx_form() {
   static int v = -1;
   if (v < 0) {
     const char* e = getenv("HPC_GEMVX_FORM");
-    v = e && (e[0] == 'w' || e[0] == 'r' || e[0] == 'x') ? e[0] : 0;
+    v = e && (e[0] == 'w' || e[0] == 'r' || e[0] == 'x' || e[0] == 't') ? e[0] : 0;
   }
   return char(v);
 }
@@ -696,6 +900,30 @@ int gemvw_plan(GemvxParams& p, int sms, int* grid, bool any_size) {
   return nc <= 1 ? 1 : nc <= 2 ? 2 : nc <= 4 ? 4 : 8;
 }
 
+// Tensor-core lane-sum plan: every segment Q4_K, 2..8 columns, rows of at
+// most GW_MAX_NB blocks, at least 2 tiles per SM (fewer leave most SMs to a
+// single warp: the other forms split those finer); one warp per 16-row half
+// tile; the deepest ring that fits.  Returns the grid size (0: not this form).
+static int gemvt_plan(GemvxParams& p, int sms, bool any_size) {
+  if (p.nb > GW_MAX_NB || p.ncols < 2 || p.ncols > 8) return 0;
+  if (p.total_tiles < 2 * sms && !any_size) return 0;
+  for (int i = 0; i < p.nseg; ++i)
+    if (p.seg[i].type != TYPE_Q4_K) return 0;
+  p.slot = int(Q4K_TILE_BLOCK_BYTES);
+  p.planes = 1;
+  if (p.pro.mode != GEMV_PRO_NONE) {
+    if (p.K != GEMV_PRO_D) return 0;
+    p.planes = 3;
+  }
+  p.C = 1;
+  p.nbc = p.nb;
+  for (p.R = GX_MAX_R; p.R >= 1; --p.R)
+    if (gw_smem_bytes(p) <= size_t(GT_MAX_SMEM)) break;
+  if (p.R < 1) return 0;
+  p.err = device_status_word();
+  return min(2 * sms, 2 * p.total_tiles);
+}
+
 // Relay plan: rows of 16, 32 or 64 blocks, no prologue, every segment one
 // type; the deepest ring (at most the blocks per part) that fits.  Returns
 // the blocks per part (0: not this form).
@@ -762,6 +990,25 @@ static cudaError_t launch_w(const GemvxParams& p, int grid, cudaStream_t st) {
   return cudaLaunchKernelEx(&cfg, hc_gemvw_kernel<NC>, p);
 }
 
+static cudaError_t launch_t(const GemvxParams& p, int grid, cudaStream_t st) {
+  static std::atomic<uint64_t> attr_set{0};
+  const cudaError_t ea = once_per_current_device(attr_set, [] {
+    return cudaFuncSetAttribute(hc_gemvt_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, GT_MAX_SMEM);
+  });
+  if (ea != cudaSuccess) return ea;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(grid));
+  cfg.blockDim = dim3(GX_THREADS);
+  cfg.dynamicSmemBytes = gw_smem_bytes(p);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, hc_gemvt_kernel, p);
+}
+
 template <int NC>
 static cudaError_t launch_x(const GemvxParams& p, int grid, cudaStream_t st) {
   const size_t smem = gx_smem_bytes(p);
@@ -795,6 +1042,15 @@ static cudaError_t launch_x(const GemvxParams& p, int grid, cudaStream_t st) {
 cudaError_t launch_gemvx(GemvxParams& p, cudaStream_t st) {
   if (p.ncols < 1 || p.ncols > GEMVX_MAX_COLS) return cudaErrorInvalidValue;
   const char form = gemvx_form();
+  // 2..8 columns of Q4_K rows: the integer lane sums on the tensor cores
+  if (form == 0 || form == 't') {
+    GemvxParams t = p;
+    const int tgrid = gemvt_plan(t, sm_count(), form == 't');
+    if (tgrid > 0) {
+      p = t;
+      return launch_t(p, tgrid, st);
+    }
+  }
   if (form == 0 || form == 'w') {
     int wgrid = 0;
     const int nc = gemvw_plan(p, sm_count(), &wgrid, form == 'w');

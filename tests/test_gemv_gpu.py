@@ -123,6 +123,10 @@ def _oracle_matmul(oracle, type_id, w, x, k, rows, cols):
     (syn.Q4_K, 256, 7, 3),         # one block, one ragged tile
     (syn.Q6_K, 768, 100, 6),
     (syn.Q4_K, 4096, 65, 7),
+    # exact lane sums on the tensor cores (Q4_K, 2..8 columns, <= 16 blocks)
+    (syn.Q4_K, 2048, 520, 2),
+    (syn.Q4_K, 3840, 33, 6),       # 15 blocks, ragged tile
+    (syn.Q4_K, 512, 4096, 4),
     # tensor-core path (>= 16 columns)
     (syn.Q4_K, 2048, 2048, 64),
     (syn.Q4_K, 768, 100, 70),      # ragged rows and columns
