@@ -440,7 +440,8 @@ class DecodeConfig3:
                 "draft_tokens_per_round": n_spec, "context_start": context, "draft_step_ms": draft_ms,
                 "sampling": {"temperature": opt.temperature, "top_k": opt.top_k, "top_p": opt.top_p, "seed": opt.seed},
                 "note": "config 4: random draft-head weights (acceptance near chance); draft head = hpc_draft_step "
-                        "(f32 dequantized weights, one CUDA graph per step), verify = the fused decoder forward at "
+                        "(dequant-fused matmuls over the head's resident quantized tiles, one CUDA graph per step), "
+                        "verify = the fused decoder forward at "
                         "M=n_spec+1; tok_per_s is the wall clock of the host loop (host-side sampling per draft)"}
 
     @classmethod

@@ -31,6 +31,7 @@
 #include <vector>
 
 #include "../../include/heliocuda.h"
+#include "hc_bulk.cuh"
 #include "hc_common.cuh"
 #include "hc_decmath.cuh"
 #include "hc_internal.h"
@@ -128,7 +129,12 @@ __global__ void __launch_bounds__(256) hc_dqrope_kernel(float* __restrict__ q, c
 // [cap][kvh][hd], causal to *pos, scale 1, f32 query; lib.rs:539-654 as the
 // draft head calls it): split over DA_CHUNK-token slices, local max / sum of
 // f64 exp / sum of p * v per slice, merged by hc_dattn_combine_kernel.
-// Grid (cap / DA_CHUNK, kvh); thread d = dimension.
+// Grid (cap / DA_CHUNK, kvh); the slice's K and V rows are staged in shared
+// memory first (all 16-byte copies in flight at once); thread d = dimension.
+constexpr int DA_KSTRIDE = 256 + 4;  // floats per staged row (16-byte reads by consecutive tokens hit distinct banks)
+__host__ __device__ constexpr size_t dattn_smem_floats(int G) {
+  return size_t(G) * (256 + DA_CHUNK) + 2 * size_t(DA_CHUNK) * DA_KSTRIDE;
+}
 __global__ void __launch_bounds__(256) hc_dattn_partial_kernel(const float* __restrict__ q, const float* __restrict__ kc,
                                                             const float* __restrict__ vc, const int* __restrict__ pos,
                                                             int H, int KVH, float* __restrict__ part_m,
@@ -141,18 +147,28 @@ __global__ void __launch_bounds__(256) hc_dattn_partial_kernel(const float* __re
   const int nt = min(CH, count - t0);
   float* qs = sm;            // [G][HD]
   float* ps = qs + G * HD;   // [G][CH]
+  float* ks = ps + G * CH;   // [CH][DA_KSTRIDE]
+  float* vs = ks + CH * DA_KSTRIDE;
+  for (int i = int(threadIdx.x); i < nt * (HD / 4); i += int(blockDim.x)) {
+    const int t = i / (HD / 4), c4 = i % (HD / 4);
+    const size_t src = (size_t(t0 + t) * KVH + kvh) * HD + 4 * c4;
+    cp_async16(ks + t * DA_KSTRIDE + 4 * c4, kc + src);
+    cp_async16(vs + t * DA_KSTRIDE + 4 * c4, vc + src);
+  }
+  cp_async_commit();
   for (int i = int(threadIdx.x); i < G * HD; i += int(blockDim.x)) qs[i] = q[size_t(kvh) * G * HD + i];
+  cp_async_wait_all();
   __syncthreads();
   for (int pr = int(threadIdx.x); pr < G * CH; pr += int(blockDim.x)) {
     const int g = pr / CH, t = pr % CH;
     float dot = -INFINITY;
     if (t < nt) {
-      const float4* kv = reinterpret_cast<const float4*>(kc + (size_t(t0 + t) * KVH + kvh) * HD);
+      const float4* kv = reinterpret_cast<const float4*>(ks + t * DA_KSTRIDE);
       const float4* qv = reinterpret_cast<const float4*>(qs + g * HD);
       float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll 8
       for (int j = 0; j < HD / 4; ++j) {
-        const float4 a = qv[j], b = __ldg(kv + j);
+        const float4 a = qv[j], b = kv[j];
         acc.x = fmaf(a.x, b.x, acc.x);
         acc.y = fmaf(a.y, b.y, acc.y);
         acc.z = fmaf(a.z, b.z, acc.z);
@@ -187,7 +203,7 @@ __global__ void __launch_bounds__(256) hc_dattn_partial_kernel(const float* __re
   const int d = int(threadIdx.x);
   for (int g = 0; g < G; ++g) {
     float acc = 0.0f;
-    for (int t = 0; t < nt; ++t) acc = fmaf(ps[g * CH + t], __ldg(vc + (size_t(t0 + t) * KVH + kvh) * HD + d), acc);
+    for (int t = 0; t < nt; ++t) acc = fmaf(ps[g * CH + t], vs[t * DA_KSTRIDE + d], acc);
     part_o[((size_t(chunk) * KVH + kvh) * G + g) * HD + d] = acc;
   }
 }
@@ -252,13 +268,101 @@ __device__ __forceinline__ uint64_t dkey(float v, uint32_t id) {
   return (uint64_t(ord) << 32) | uint64_t(0xffffffffu - id);
 }
 
-// Top-k of n <= DT_MAXN entries (values with id = index, or ready keys):
-// bitonic sort of the keys, descending, in one CTA.  *d_k (device) or k.
+// Top-k of n <= DT_MAXN entries (values with id = index, or ready keys), in
+// one CTA, descending.  *d_k (device) or k.  Keys are unique apart from the
+// empty key 0 (ids differ), so for k <= DT_SEL_MAX the k-th largest key is
+// found by an 8-bit radix select (eight histogram passes over the keys held
+// in registers), the keys at or above it are gathered and each is placed by
+// its rank among them; larger k take a bitonic sort of all keys.
+constexpr int DT_KPT = DT_MAXN / DT_THREADS;  // keys per thread
+constexpr int DT_SEL_MAX = 64;
 __global__ void __launch_bounds__(DT_THREADS) hc_dtopk_kernel(const float* __restrict__ vals,
                                                            const uint64_t* __restrict__ keys, int n, int k,
                                                            const int* __restrict__ d_k, int32_t* __restrict__ out_ids,
                                                            float* __restrict__ out_vals) {
   __shared__ uint64_t s[DT_MAXN];
+  __shared__ int hist[256];
+  __shared__ uint64_t s_prefix;
+  __shared__ int s_rank, s_cnt;
+  const int kk = d_k ? *d_k : k;
+  auto emit = [&](int i, uint64_t key) {
+    const uint32_t ord = uint32_t(key >> 32);
+    const uint32_t bits = (ord & 0x80000000u) ? (ord & 0x7fffffffu) : ~ord;
+    out_ids[i] = key ? int32_t(0xffffffffu - uint32_t(key)) : -1;
+    out_vals[i] = key ? __uint_as_float(bits) : -INFINITY;
+  };
+  if (kk <= DT_SEL_MAX && kk < n) {
+    uint64_t v[DT_KPT];
+#pragma unroll
+    for (int j = 0; j < DT_KPT; ++j) {
+      const int i = int(threadIdx.x) + j * DT_THREADS;
+      v[j] = i >= n ? 0ull : (keys ? keys[i] : dkey(vals[i], uint32_t(i)));
+    }
+    if (threadIdx.x == 0) {
+      s_prefix = 0ull;
+      s_rank = kk;  // rank of the wanted key among those matching the prefix
+      s_cnt = 0;
+    }
+    uint64_t mask = 0ull;
+    for (int shift = 56; shift >= 0; shift -= 8) {
+      for (int i = int(threadIdx.x); i < 256; i += DT_THREADS) hist[i] = 0;
+      __syncthreads();
+      const uint64_t prefix = s_prefix;
+#pragma unroll
+      for (int j = 0; j < DT_KPT; ++j)
+        if ((v[j] & mask) == prefix) atomicAdd(&hist[int(v[j] >> shift) & 255], 1);
+      __syncthreads();
+      if (threadIdx.x < 32) {  // warp 0: the digit where the count from the top reaches the rank
+        const int lane = int(threadIdx.x);
+        int c[8], tot = 0;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {  // lane holds digits 255 - 8 lane - q (descending)
+          c[q] = hist[255 - 8 * lane - q];
+          tot += c[q];
+        }
+        int incl = tot;  // inclusive prefix over lanes (higher digits first)
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+          const int y = __shfl_up_sync(0xffffffffu, incl, off);
+          if (lane >= off) incl += y;
+        }
+        const int rank = s_rank;
+        const int before = incl - tot;  // keys with a higher digit, over lower lanes
+        if (before < rank && rank <= incl) {
+          int acc = before, q = 0;
+          while (q < 7 && acc + c[q] < rank) acc += c[q++];
+          s_rank = rank - acc;
+          s_prefix = prefix | (uint64_t(255 - 8 * lane - q) << shift);
+        }
+      }
+      mask |= 0xffull << shift;
+      __syncthreads();
+    }
+    const uint64_t kth = s_prefix;  // the kk-th largest key
+    // gather the non-empty keys at or above it: kk of them, fewer when the
+    // kk-th key is the empty one (the rest of the list is then empty)
+#pragma unroll
+    for (int j = 0; j < DT_KPT; ++j) {
+      const int i = int(threadIdx.x) + j * DT_THREADS;
+      if (i < n && v[j] >= kth && v[j] != 0ull) {
+        const int slot = atomicAdd(&s_cnt, 1);
+        if (slot < DT_SEL_MAX) s[slot] = v[j];
+      }
+    }
+    __syncthreads();
+    const int m = min(s_cnt, DT_SEL_MAX);
+    for (int i = int(threadIdx.x); i < kk; i += DT_THREADS) {
+      if (i >= m) {
+        emit(i, 0ull);
+        continue;
+      }
+      const uint64_t key = s[i];
+      int r = 0;
+      for (int j = 0; j < m; ++j) r += s[j] > key ? 1 : 0;
+      emit(r, key);
+    }
+    return;
+  }
   int np = 1;
   while (np < n) np <<= 1;
   for (int i = int(threadIdx.x); i < np; i += int(blockDim.x))
@@ -280,14 +384,7 @@ __global__ void __launch_bounds__(DT_THREADS) hc_dtopk_kernel(const float* __res
       __syncthreads();
     }
   }
-  const int kk = d_k ? *d_k : k;
-  for (int i = int(threadIdx.x); i < kk; i += int(blockDim.x)) {
-    const uint64_t key = i < n ? s[i] : 0ull;
-    const uint32_t ord = uint32_t(key >> 32);
-    const uint32_t b = (ord & 0x80000000u) ? (ord & 0x7fffffffu) : ~ord;
-    out_ids[i] = key ? int32_t(0xffffffffu - uint32_t(key)) : -1;
-    out_vals[i] = key ? __uint_as_float(b) : -INFINITY;
-  }
+  for (int i = int(threadIdx.x); i < kk; i += int(blockDim.x)) emit(i, i < n ? s[i] : 0ull);
 }
 
 // maskedEmbeddingTopTokens (mtp-assistant-runner.ts:211-242): slot s of the
@@ -295,45 +392,79 @@ __global__ void __launch_bounds__(DT_THREADS) hc_dtopk_kernel(const float* __res
 // embedding row . h -- the row dequantized bit-exactly from its row tile and
 // one sequential f32 chain over the hidden index, as
 // hp_matmul_dequantized_f32 on the gathered rows; ids outside the vocabulary
-// get the empty key.  A warp per slot: per 256-block, eight lanes dequantize
-// the row's block into the warp's shared row buffer, lane 0 walks it.
-constexpr int DS_WARPS = 8;
-__global__ void __launch_bounds__(32 * DS_WARPS) hc_dscores_kernel(const uint8_t* __restrict__ E, int type, int nb,
-                                                                int vocab, const int32_t* __restrict__ ordering,
-                                                                int per, const int32_t* __restrict__ c_ids, int slots,
-                                                                const float* __restrict__ h,
-                                                                uint64_t* __restrict__ keys) {
-  extern __shared__ __align__(16) float ds_smem[];  // h [nb * 256], then [DS_WARPS][256] row blocks
+// get the empty key.  CTA = 32 slots: one chain warp (lane = slot) and four
+// dequant warps that turn 256-block b of the 32 gathered rows into one half
+// of a double buffer while the chain warp walks the other half (one barrier
+// per block); every row's blocks are prefetched into L2 at the start.
+constexpr int DS_DQ_WARPS = 4;
+constexpr int DS_ROW = QK + 4;  // floats per staged row (16-byte reads by lane = slot hit distinct banks)
+__global__ void __launch_bounds__(32 * (1 + DS_DQ_WARPS)) hc_dscores_kernel(
+    const uint8_t* __restrict__ E, int type, int nb, int vocab, const int32_t* __restrict__ ordering, int per,
+    const int32_t* __restrict__ c_ids, int slots, const float* __restrict__ h, uint64_t* __restrict__ keys) {
+  extern __shared__ __align__(16) float ds_smem[];  // h [K], then rows [2][32][DS_ROW]
+  __shared__ int toks[32];
   const int warp = int(threadIdx.x >> 5), lane = int(threadIdx.x & 31);
   const int K = nb * QK;
-  for (int i = int(threadIdx.x); i < K; i += int(blockDim.x)) ds_smem[i] = h[i];
-  __syncthreads();
-  const int slot = int(blockIdx.x) * DS_WARPS + warp;
-  if (slot >= slots) return;
-  const int c = c_ids[slot / per];
-  const int tok = c >= 0 ? ordering[size_t(c) * per + slot % per] : -1;
-  if (tok < 0 || tok >= vocab) {
-    if (lane == 0) keys[slot] = 0ull;
-    return;
+  const int slot0 = int(blockIdx.x) * 32;
+  if (warp == 0) {
+    const int slot = slot0 + lane;
+    int tok = -1;
+    if (slot < slots) {
+      const int c = c_ids[slot / per];
+      tok = c >= 0 ? ordering[size_t(c) * per + slot % per] : -1;
+      if (tok >= vocab) tok = -1;
+    }
+    toks[lane] = tok;
   }
-  float* row = ds_smem + K + warp * QK;
+  float* hs = ds_smem;
+  float* ws = ds_smem + K;
+  for (int i = int(threadIdx.x); i < K; i += int(blockDim.x)) hs[i] = h[i];
+  __syncthreads();
   const size_t ub = type == TYPE_Q4_K ? Q4K_TILE_BLOCK_BYTES : Q6K_TILE_BLOCK_BYTES;
+  const int dt = int(threadIdx.x) - 32;  // dequant thread index (< 0: the chain warp)
+  if (dt >= 0) {
+    // every (row, block): its 16-byte pieces at a 512-byte stride in the tile
+    const int pieces = type == TYPE_Q4_K ? Q4K_CHUNKS : Q6K_CHUNKS;
+    for (int task = dt; task < 32 * nb; task += 32 * DS_DQ_WARPS) {
+      const int r = task & 31, b = task >> 5, tok = toks[r];
+      if (tok < 0) continue;
+      const uint8_t* tb = E + (size_t(tok / TILE) * nb + b) * ub + size_t(tok % TILE) * 16;
+      for (int c = 0; c < pieces; ++c) asm volatile("prefetch.global.L2 [%0];" ::"l"(tb + size_t(c) * 512));
+    }
+  }
+  auto fill = [&](int b, int buf) {
+    float* wb = ws + buf * 32 * DS_ROW;
+    for (int task = dt; task < 32 * 8; task += 32 * DS_DQ_WARPS) {  // (row, 32-element part)
+      const int r = task >> 3, part = task & 7, tok = toks[r];
+      float* o = wb + r * DS_ROW;
+      if (tok < 0) continue;
+      const uint8_t* tb = E + (size_t(tok / TILE) * nb + b) * ub;
+      if (type == TYPE_Q4_K) q4k_dequant_chunk(tb, tok % TILE, part, o);
+      else q6k_dequant_group(tb, tok % TILE, part, o);
+    }
+  };
+  if (dt >= 0) fill(0, 0);
+  __syncthreads();
   float sum = 0.0f;
   for (int b = 0; b < nb; ++b) {
-    const uint8_t* tb = E + (size_t(tok / TILE) * nb + b) * ub;
-    if (lane < 8) {
-      if (type == TYPE_Q4_K) q4k_dequant_chunk(tb, tok % TILE, lane, row);
-      else q6k_dequant_group(tb, tok % TILE, lane, row);
+    const int buf = b & 1;
+    if (warp == 0) {
+      const float4* wr = reinterpret_cast<const float4*>(ws + buf * 32 * DS_ROW + lane * DS_ROW);
+      const float4* xc = reinterpret_cast<const float4*>(hs + b * QK);
+#pragma unroll 8
+      for (int i = 0; i < QK / 4; ++i) {
+        const float4 a = wr[i], v = xc[i];
+        sum = __fadd_rn(sum, __fmul_rn(a.x, v.x));
+        sum = __fadd_rn(sum, __fmul_rn(a.y, v.y));
+        sum = __fadd_rn(sum, __fmul_rn(a.z, v.z));
+        sum = __fadd_rn(sum, __fmul_rn(a.w, v.w));
+      }
+    } else if (b + 1 < nb) {
+      fill(b + 1, buf ^ 1);
     }
-    __syncwarp();
-    if (lane == 0) {
-      const float* hb = ds_smem + b * QK;
-#pragma unroll 16
-      for (int i = 0; i < QK; ++i) sum = __fadd_rn(sum, __fmul_rn(row[i], hb[i]));
-    }
-    __syncwarp();
+    __syncthreads();
   }
-  if (lane == 0) keys[slot] = dkey(sum, uint32_t(tok));
+  if (warp == 0 && slot0 + lane < slots) keys[slot0 + lane] = toks[lane] >= 0 ? dkey(sum, uint32_t(toks[lane])) : 0ull;
 }
 
 // The step's inputs: [embedding ; hidden] into xin, the position and top-k.
@@ -620,7 +751,15 @@ static int draft_enqueue(hpc_draft d, cudaStream_t st) {
     if ((rc = gemv(L.w[HPC_DW_Q], d->a, d->q)) != HPC_OK) return rc;
     hc_dqrope_kernel<<<c.heads, 256, 0, st>>>(d->q, L.n[HPC_DN_Q], c.head_dim, d->d_pos, pairs, theta_scale, c.rms_eps);
     HPC_CK(cudaGetLastError(), "draft q norm / rope");
-    hc_dattn_partial_kernel<<<dim3(chunks, c.kv_heads), 256, size_t(G) * (256 + DA_CHUNK) * 4, st>>>(
+    {
+      static std::atomic<uint64_t> attr{0};
+      const cudaError_t ea = once_per_current_device(attr, [] {
+        return cudaFuncSetAttribute(hc_dattn_partial_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    int(dattn_smem_floats(64) * 4));
+      });
+      HPC_CK(ea, "draft attention attributes");
+    }
+    hc_dattn_partial_kernel<<<dim3(chunks, c.kv_heads), 256, dattn_smem_floats(G) * 4, st>>>(
         d->q, L.kc, L.vc, d->d_pos, c.heads, c.kv_heads, d->pm, d->pl, d->po);
     HPC_CK(cudaGetLastError(), "draft attention");
     hc_dattn_combine_kernel<<<c.heads, 256, 0, st>>>(d->pm, d->pl, d->po, d->d_pos, c.heads, c.kv_heads, d->att);
@@ -641,7 +780,16 @@ static int draft_enqueue(hpc_draft d, cudaStream_t st) {
                                          d->c_vals);
   HPC_CK(cudaGetLastError(), "draft centroid top-k");
   const int slots = c.centroid_top_k * d->per;
-  hc_dscores_kernel<<<(slots + DS_WARPS - 1) / DS_WARPS, 32 * DS_WARPS, size_t(E + DS_WARPS * QK) * 4, st>>>(
+  const size_t ds_bytes = (size_t(E) + 2 * 32 * DS_ROW) * 4;
+  {
+    static std::atomic<uint64_t> attr{0};
+    const cudaError_t ea = once_per_current_device(attr, [] {
+      return cudaFuncSetAttribute(hc_dscores_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  int((8192 + 2 * 32 * DS_ROW) * 4));
+    });
+    HPC_CK(ea, "draft token scores attributes");
+  }
+  hc_dscores_kernel<<<(slots + 31) / 32, 32 * (1 + DS_DQ_WARPS), ds_bytes, st>>>(
       d->embd.w, d->embd.type, d->embd.nb, c.vocab, d->ordering, d->per, d->c_ids, slots, d->h, d->keys);
   HPC_CK(cudaGetLastError(), "draft token scores");
   hc_dtopk_kernel<<<1, DT_THREADS, 0, st>>>(nullptr, d->keys, slots, 0, d->d_k, d->out_ids, d->out_vals);

@@ -7,6 +7,7 @@
 //   y = (d*sc)*(q-32)
 // with every product and difference rounded on its own (__fmul_rn/__fsub_rn),
 // as the Rust code never fuses them.
+#include "hc_bulk.cuh"
 #include "hc_common.cuh"
 #include "hc_kernels.cuh"
 #include "hc_unpack.cuh"
@@ -144,41 +145,73 @@ __global__ void hc_dequant_q6k_kernel(const uint8_t* __restrict__ w, float* __re
 // thread per (row, column) runs the reference's own chain
 // sum = fround(sum + fround(w * x)) in index order (no fused multiply-add,
 // no reassociation), so the result is the reference's bit for bit.
-// CTA = one 32-row tile x NC columns: NC chain warps (lane = row) and four
-// dequant warps.  Per 256-block the dequant warps write the tile's rows
-// (row stride 260 floats: 16-byte reads by lane = row hit distinct banks)
-// and the columns' input slice into one half of a double buffer while the
-// chain warps walk the other half, four elements per pair of 16-byte reads;
-// one CTA barrier per block.  The chain's dependent adds are the bound.
-constexpr int DM_DQ_WARPS = 4;
+// CTA = one 32-row tile x NC columns: NC chain warps (lane = row) and eight
+// dequant warps.  The tile's raw 256-blocks (and, for 16-byte aligned
+// inputs, the columns' input slices) stream through a ring of DM_NS
+// shared-memory slots, one bulk copy each issued DM_NS blocks ahead; per
+// block the dequant warps turn a staged raw block into rows (row stride 260
+// floats: 16-byte reads by lane = row hit distinct banks) in one half of a
+// double buffer while the chain warps walk the other half, four elements per
+// pair of 16-byte reads; one CTA barrier per block.  The chain's dependent
+// adds are the bound.
+constexpr int DM_DQ_WARPS = 8;
 constexpr int DM_ROW = QK + 4;  // floats per staged row
+constexpr int DM_NS = 4;        // raw ring slots
+constexpr size_t DM_RAW = Q6K_TILE_BLOCK_BYTES;  // the larger raw block (16-byte multiple)
+
+__host__ __device__ constexpr size_t dm_slot_bytes(int nc) { return DM_RAW + size_t(nc) * QK * 4; }
 
 template <int NC>
 __global__ void __launch_bounds__(32 * (NC + DM_DQ_WARPS)) hc_dequant_matmul_kernel(
     const uint8_t* __restrict__ w, int type, int nb, int rows, const float* __restrict__ x, int K, int cols,
-    float* __restrict__ out) {
-  extern __shared__ __align__(16) float dm_smem[];  // ws [2][32][DM_ROW], then xs [2][NC][256]
+    float* __restrict__ out, int x_bulk, int* err) {
+  extern __shared__ __align__(16) float dm_smem[];  // ws [2][32][DM_ROW], xs [2][NC][256], raw ring [DM_NS][slot]
+  __shared__ __align__(8) uint64_t full[DM_NS];
   float* ws = dm_smem;
   float* xs = dm_smem + 2 * TILE * DM_ROW;
+  uint8_t* ring = reinterpret_cast<uint8_t*>(xs + 2 * NC * QK);
   const int tile = int(blockIdx.x), col0 = int(blockIdx.y) * NC;
   const int warp = int(threadIdx.x) >> 5, lane = int(threadIdx.x) & 31;
   const int ncols = min(NC, cols - col0);
-  const size_t ub = type == TYPE_Q4_K ? Q4K_TILE_BLOCK_BYTES : Q6K_TILE_BLOCK_BYTES;
+  const uint32_t ub = uint32_t(type == TYPE_Q4_K ? Q4K_TILE_BLOCK_BYTES : Q6K_TILE_BLOCK_BYTES);
   const int dt = int(threadIdx.x) - 32 * NC;  // dequant thread index (< 0: a chain warp)
-  auto fill = [&](int b, int buf) {
-    const uint8_t* tb = w + (size_t(tile) * nb + b) * ub;
+  int issued = 0;
+  auto issue = [&](int b) {  // dequant thread 0: block b into its slot
+    ++issued;
+    const int sl = b % DM_NS;
+    uint8_t* dst = ring + size_t(sl) * dm_slot_bytes(NC);
+    mbar_expect_tx(&full[sl], ub + (x_bulk ? uint32_t(ncols) * QK * 4u : 0u));
+    bulk_copy_g2s(dst, w + (size_t(tile) * nb + b) * ub, ub, &full[sl]);
+    if (x_bulk)
+      for (int c = 0; c < ncols; ++c)
+        bulk_copy_g2s(dst + DM_RAW + size_t(c) * QK * 4, x + size_t(col0 + c) * K + size_t(b) * QK, QK * 4u,
+                      &full[sl]);
+  };
+  bool ok = true;
+  auto fill = [&](int b, int buf) {  // dequant warps: staged block b -> rows and inputs of half `buf`
+    const int sl = b % DM_NS;
+    const uint8_t* raw = ring + size_t(sl) * dm_slot_bytes(NC);
+    if (ok && !mbar_wait_parity(&full[sl], uint32_t(b / DM_NS) & 1u, err)) ok = false;
+    if (!ok) return;
     float* wb = ws + buf * TILE * DM_ROW;
     for (int task = dt; task < TILE * 8; task += 32 * DM_DQ_WARPS) {  // (row, 32-element part)
       const int r = task >> 3, part = task & 7;
-      if (type == TYPE_Q4_K) q4k_dequant_chunk(tb, r, part, wb + r * DM_ROW);
-      else q6k_dequant_group(tb, r, part, wb + r * DM_ROW);
+      if (type == TYPE_Q4_K) q4k_dequant_chunk(raw, r, part, wb + r * DM_ROW);
+      else q6k_dequant_group(raw, r, part, wb + r * DM_ROW);
     }
     float* xb = xs + buf * NC * QK;
+    const float* xr = reinterpret_cast<const float*>(raw + DM_RAW);
     for (int i = dt; i < ncols * QK; i += 32 * DM_DQ_WARPS)
-      xb[i] = x[size_t(col0 + i / QK) * K + size_t(b) * QK + i % QK];
+      xb[i] = x_bulk ? xr[i] : x[size_t(col0 + i / QK) * K + size_t(b) * QK + i % QK];
   };
+  if (dt == 0) {
+    for (int s = 0; s < DM_NS; ++s) mbar_init(&full[s], 1);
+    for (int b = 0; b < nb && b < DM_NS; ++b) issue(b);
+  }
+  __syncthreads();
   if (dt >= 0) fill(0, 0);
   __syncthreads();
+  if (dt == 0 && DM_NS < nb) issue(DM_NS);  // slot 0 is free again
   float sum = 0.0f;
   for (int b = 0; b < nb; ++b) {
     const int buf = b & 1;
@@ -195,27 +228,34 @@ __global__ void __launch_bounds__(32 * (NC + DM_DQ_WARPS)) hc_dequant_matmul_ker
           sum = __fadd_rn(sum, __fmul_rn(a.w, v.w));
         }
       }
-    } else if (b + 1 < nb) {
+    } else if (dt >= 0 && b + 1 < nb) {
       fill(b + 1, buf ^ 1);
     }
-    __syncthreads();  // block b consumed, block b + 1 staged
+    __syncthreads();  // block b consumed, block b + 1 staged, its raw slot free
+    if (dt == 0 && ok && b + 1 + DM_NS < nb) issue(b + 1 + DM_NS);
   }
   const int row = tile * TILE + lane;
   if (warp < ncols && row < rows) out[size_t(col0 + warp) * rows + row] = sum;
+  if (dt == 0 && !ok)  // let the copies in flight land before the CTA exits
+    for (int b = max(0, issued - DM_NS); b < issued; ++b)
+      mbar_wait_parity(&full[b % DM_NS], uint32_t(b / DM_NS) & 1u, nullptr);
 }
 
 template <int NC>
 static cudaError_t launch_dm(int type, const uint8_t* w, int nb, int rows, int rows_pad, const float* x, int K,
                              int cols, float* out, cudaStream_t stream) {
-  constexpr size_t smem = sizeof(float) * (2 * TILE * DM_ROW + 2 * NC * QK);
+  constexpr size_t smem = sizeof(float) * (2 * TILE * DM_ROW + 2 * NC * QK) + DM_NS * dm_slot_bytes(NC);
   static std::atomic<uint64_t> attr{0};
   const cudaError_t ea = once_per_current_device(attr, [] {
     return cudaFuncSetAttribute(hc_dequant_matmul_kernel<NC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 int(smem));
   });
   if (ea != cudaSuccess) return ea;
+  // the input slices go by bulk copy when every slice starts on 16 bytes
+  const int x_bulk = (reinterpret_cast<uintptr_t>(x) & 15) == 0 && (size_t(K) * 4) % 16 == 0;
   const dim3 grid(unsigned(rows_pad / TILE), unsigned((cols + NC - 1) / NC));
-  hc_dequant_matmul_kernel<NC><<<grid, 32 * (NC + DM_DQ_WARPS), smem, stream>>>(w, type, nb, rows, x, K, cols, out);
+  hc_dequant_matmul_kernel<NC><<<grid, 32 * (NC + DM_DQ_WARPS), smem, stream>>>(w, type, nb, rows, x, K, cols, out,
+                                                                               x_bulk, device_status_word());
   return cudaGetLastError();
 }
 
