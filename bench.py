@@ -442,7 +442,8 @@ class DecodeConfig3:
                 "note": "config 4: random draft-head weights (acceptance near chance); draft head = hpc_draft_step "
                         "(dequant-fused matmuls over the head's resident quantized tiles, one CUDA graph per step), "
                         "verify = the fused decoder forward at "
-                        "M=n_spec+1; tok_per_s is the wall clock of the host loop (host-side sampling per draft)"}
+                        "M=n_spec+1; tok_per_s is the wall clock of the host loop (drafts drawn on the device: one host "
+                        "synchronization per round, after the verify)"}
 
     @classmethod
     def cpu_sampler(cls, threads: int):

@@ -89,6 +89,10 @@ def create_deterministic_rng(seed: float) -> Callable[[], float]:
         v ^= (v + _imul(v ^ (v >> 7), v | 61)) & _M32
         return ((v ^ (v >> 14)) & _M32) / 4294967296.0
 
+    # the generator's state before the next draw, for a draw made elsewhere
+    # (the device sampler) from the same stream; the caller then calls rng()
+    # once to advance this copy past it
+    rng.state = lambda: state
     return rng
 
 

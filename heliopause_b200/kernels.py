@@ -309,6 +309,24 @@ def lm_head_topk(handle: CudaQuantizedWeightHandle, hidden, column_count: int, k
     return ids, vals
 
 
+def sample_candidates(ids: torch.Tensor, vals: torch.Tensor, *, top_k: int, top_p: float, temperature: float,
+                      greedy: bool, rng_state: int, token_out: torch.Tensor, table: torch.Tensor | None = None,
+                      scale: float = 1.0, row_out: torch.Tensor | None = None) -> None:
+    """The sampler's token draw on the device (hpc_sample_candidates): ids /
+    vals a sorted candidate list (device int32 / f32), token_out a device
+    int32 slot; with `table` ([rows][hidden] f32) the chosen row * scale goes
+    to row_out.  Nothing is read back (no synchronization)."""
+    if ids.dtype != torch.int32 or vals.dtype != torch.float32 or not ids.is_cuda or not vals.is_cuda:
+        raise CudaKernelError(ERR_TYPE, "sample: candidates must be device int32 ids and f32 values")
+    n = ids.numel()
+    hidden = table.shape[1] if table is not None else 0
+    code = _lib.lib().hpc_sample_candidates(_ptr(ids), _ptr(vals), n, max(1, int(top_k)), float(top_p),
+                                            float(temperature), 1 if greedy else 0, int(rng_state) & 0xFFFFFFFF,
+                                            _ptr(token_out), _ptr(table) if table is not None else None, hidden,
+                                            float(scale), _ptr(row_out) if row_out is not None else None, _stream())
+    assert_cuda_ok(code, "sampleCandidates")
+
+
 def set_matmul_order(exact: bool) -> None:
     """Reference f32 order (default) or the reordered kernels for the matmul
     and LM-head calls (hpc_set_matmul_order)."""

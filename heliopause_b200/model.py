@@ -276,6 +276,27 @@ class CudaDecoderModel:
             return ids_out, vals_out, self.hidden[:n].clone()
         return ids_out, vals_out
 
+    def forward_device(self, ids: torch.Tensor, positions: torch.Tensor, top_k: int, *,
+                       return_hidden: bool = False):
+        """forward() on device int32 token ids and positions (no host copy in
+        either direction): what a device-side sampler feeds the verify."""
+        n = ids.numel()
+        if n != positions.numel() or not 1 <= n <= self.max_tokens:
+            raise hk.CudaKernelError(hk.ERR_SHAPE, f"forward: {n} tokens / {positions.numel()} positions")
+        self._ids[:n].copy_(ids.reshape(-1).to(torch.int32), non_blocking=True)
+        self._pos[:n].copy_(positions.reshape(-1).to(torch.int32), non_blocking=True)
+        st = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+        code = _lib.lib().hpc_model_forward(self._h, C.c_void_p(self._ids.data_ptr()), C.c_void_p(self._pos.data_ptr()),
+                                            n, top_k, C.c_void_p(self.out_ids.data_ptr()),
+                                            C.c_void_p(self.out_vals.data_ptr()),
+                                            C.c_void_p(self.hidden.data_ptr()) if return_hidden else None, st)
+        hk.assert_cuda_ok(code, "modelForward")
+        ids_out = self.out_ids.view(-1)[:n * top_k].view(n, top_k).clone()
+        vals_out = self.out_vals.view(-1)[:n * top_k].view(n, top_k).clone()
+        if return_hidden:
+            return ids_out, vals_out, self.hidden[:n].clone()
+        return ids_out, vals_out
+
     def prefill(self, hidden: torch.Tensor, start: int) -> torch.Tensor:
         """SegmentRunner.runTokensHidden for a prompt: `hidden` [n][hidden]
         (f32, the embedded tokens) at positions start .. start+n-1 through all

@@ -327,23 +327,74 @@ class MtpGenerator:
             hidden = post
         return gen.MtpProposal(drafts, dists)
 
+    def propose_on_device(self, pending: int, ctx: MtpContext, n: int, sampling, rng):
+        """proposeMtpDraft with every draw on the device (hpc_sample_candidates):
+        each draft step's top-k, its token and the next step's input
+        embedding stay on the GPU, so the n steps run without a host
+        synchronization.  Returns the device tokens [n] (int32) and the
+        steps' (ids, logits) device tensors; the host stream `rng` is
+        advanced past the n draws."""
+        kv = [self.t.kv(layer) for layer in self.kv_layers]
+        greedy = gen._greedy(sampling)
+        k = 1 if greedy else sampling.top_k  # mtpDraftTopK (mtp-generation.ts:230-234)
+        toks = torch.empty(n, dtype=torch.int32, device="cuda")
+        emb, hidden = self.embedding(pending), ctx.current_hidden
+        scale = math.sqrt(self.ts.hidden)
+        steps = []
+        for i in range(n):
+            post, ids, logits = self.d.run(emb, hidden, kv, ctx.position, k)
+            ids32 = ids.to(torch.int32)
+            nxt = torch.empty(self.ts.hidden, dtype=torch.float32, device="cuda")
+            hk.sample_candidates(ids32, logits, top_k=k if greedy else sampling.top_k, top_p=sampling.top_p,
+                                 temperature=sampling.temperature if not greedy else 1.0, greedy=greedy,
+                                 rng_state=0 if greedy else rng.state(), token_out=toks[i:i + 1], table=self.embd,
+                                 scale=scale, row_out=nxt)
+            if not greedy:
+                rng()  # this copy of the stream moves past the device's draw
+            steps.append((ids32, logits))
+            emb, hidden = nxt, post
+        return toks, steps
+
     def verify(self, tokens, position: int, top_k: int):
         """verifyMtpDraft: one batched target forward over [pending, d1..dn]
         at positions position.. (webgpu/mtp-target-runner.ts:80-149)."""
         ids, vals, hid = self.t.forward(tokens, [position + i for i in range(len(tokens))], top_k, return_hidden=True)
         return gen.target_verification(ids.cpu().numpy(), vals.cpu().numpy(), self.ts.vocab, position), hid
 
-    def generate(self, first_token: int, ctx: MtpContext, n_tokens: int, n_spec: int, sampling, rng):
+    def verify_device(self, pending: int, toks: torch.Tensor, steps, position: int, top_k: int):
+        """verify() on device draft tokens: the forward reads them where the
+        sampler wrote them; the one read-back of the round brings the
+        target's top-k, the drafts and their distributions together."""
+        n = toks.numel()
+        ids_dev = torch.cat([torch.full((1,), pending, dtype=torch.int32, device="cuda"), toks])
+        pos_dev = torch.arange(position, position + n + 1, dtype=torch.int32, device="cuda")
+        ids, vals, hid = self.t.forward_device(ids_dev, pos_dev, top_k, return_hidden=True)
+        d_ids = torch.stack([s[0] for s in steps]).cpu().tolist()
+        d_vals = torch.stack([s[1] for s in steps]).cpu().tolist()
+        drafts = toks.cpu().tolist()
+        prop = gen.MtpProposal(drafts, [gen.MtpTokenDistribution(list(zip(i, v)), self.d.s.vocab, True)
+                                        for i, v in zip(d_ids, d_vals)])
+        return gen.target_verification(ids.cpu().numpy(), vals.cpu().numpy(), self.ts.vocab, position), hid, prop
+
+    def generate(self, first_token: int, ctx: MtpContext, n_tokens: int, n_spec: int, sampling, rng, *,
+                 device_sampling: bool = True):
         """generateAssistantWithMtp (chat.ts:692-776) without tokenizer and
         stop tokens: `first_token` is the pending token at ctx.position + 1.
-        Returns (tokens, rounds, accepted drafts)."""
+        Returns (tokens, rounds, accepted drafts).  device_sampling: the
+        drafts are drawn on the GPU and fed straight into the verify forward,
+        one host synchronization per round (after the verify); else the host
+        draws each draft (one synchronization per draft)."""
         out, rounds, accepted = [], 0, 0
         pending, pos = first_token, ctx.position + 1
         top_k = self.target_top_k(sampling)
         while len(out) < n_tokens and pos < self.ts.context:
             budget = max(0, min(n_spec, n_tokens - len(out) - 1, self.ts.context - pos - 1))
-            prop = self.propose(pending, ctx, budget, sampling, rng) if budget else gen.MtpProposal([], [])
-            ver, hid = self.verify([pending] + prop.draft_token_ids, pos, top_k)
+            if device_sampling and budget:
+                toks, steps = self.propose_on_device(pending, ctx, budget, sampling, rng)
+                ver, hid, prop = self.verify_device(pending, toks, steps, pos, top_k)
+            else:
+                prop = self.propose(pending, ctx, budget, sampling, rng) if budget else gen.MtpProposal([], [])
+                ver, hid = self.verify([pending] + prop.draft_token_ids, pos, top_k)
             acc = gen.accept_mtp_draft(prop, ver, sampling, rng)
             rounds += 1
             accepted += acc.accepted_draft_length

@@ -227,6 +227,22 @@ int hpc_lm_head_topk_q8(hpc_weight lm_head, const void *d_workspace, size_t work
 int hpc_topk_merge_keys(const uint64_t *d_keys, size_t group_count, size_t column_count, size_t k, float softcap,
                         int32_t *d_ids, float *d_vals, void *stream);
 
+/* One token drawn from a candidate list on the device (replaces the host's
+ * token_sampling_distribution + sample_next_token, generation.ts:85-165, and
+ * the mulberry32-style generator of generation.ts:74-83).  d_ids / d_vals:
+ * n (1..1024) candidates sorted by value descending then id ascending, as the
+ * top-k entry points write them.  Keeps the first top_k, then the top_p
+ * nucleus, then draws from the softmax of value / temperature with the
+ * generator advanced once from rng_state (the caller advances its own copy
+ * of the stream by one draw); greedy != 0 takes the first candidate and
+ * draws nothing.  Writes the token to *d_token and, when d_table != NULL,
+ * d_table[token][0..hidden) * scale (f64 product rounded to f32) to
+ * d_row_out, the next draft step's input embedding.  The exps are the
+ * device's f64 exp. */
+int hpc_sample_candidates(const int32_t *d_ids, const float *d_vals, size_t n, size_t top_k, double top_p,
+                          double temperature, int greedy, uint32_t rng_state, int32_t *d_token, const float *d_table,
+                          size_t hidden, double scale, float *d_row_out, void *stream);
+
 /* ---- LM head + top-k with no allocation inside the call --------------------
  * No reference counterpart: an addition for callers that may not allocate
  * device memory while they serve (all of HBM handed to weights and the KV

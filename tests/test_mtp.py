@@ -275,7 +275,9 @@ def test_mtp_greedy_equals_plain_greedy(gpu_device):
                 g.wrong_at = 0
             first, ctx = g.start(42, start, greedy, gen.create_deterministic_rng(1))
             assert first == plain[0]
-            toks, rounds, acc = g.generate(first, ctx, n, 4, greedy, gen.create_deterministic_rng(1))
+            # the planted proposals replace the host-side proposer
+            toks, rounds, acc = g.generate(first, ctx, n, 4, greedy, gen.create_deterministic_rng(1),
+                                           device_sampling=kind == "draft head")
             assert toks == plain[:n], f"{kind}: {toks} vs {plain[:n]}"
             if kind == "all right":
                 assert rounds == math.ceil(n / 5) and acc == n - rounds
@@ -320,6 +322,65 @@ def test_mtp_sampled_generation_is_deterministic(gpu_device):
     assert runs[0] == runs[1]
     toks, rounds, acc = runs[0]
     assert len(toks) == 20 and 1 <= rounds <= 20 and 0 <= acc <= 20 - rounds
+
+
+@pytest.mark.gpu
+def test_device_sampler_equals_host_sampler(gpu_device):
+    """hpc_sample_candidates against sample_next_token (generation.ts:85-165)
+    on the same candidate lists and generator state: the same token, over
+    list lengths 1..200, ties (id ascending), top-k / top-p / temperature and
+    greedy; the row written for the next step is table[token] * scale."""
+    from heliopause_b200 import kernels as hk
+    g = np.random.default_rng(3)
+    table = torch.from_numpy(g.standard_normal((5000, 64)).astype(np.float32)).cuda()
+    tok = torch.empty(1, dtype=torch.int32, device="cuda")
+    row = torch.empty(64, dtype=torch.float32, device="cuda")
+    for trial in range(300):
+        n = int(g.choice([1, 2, 5, 40, 64, 200]))
+        vals = g.normal(0, float(g.choice([0.5, 2.0, 8.0])), n).astype(np.float32)
+        if trial % 7 == 0 and n > 3:
+            vals[1:3] = vals[0]
+        ids = g.permutation(5000)[:n].astype(np.int32)
+        order = sorted(range(n), key=lambda i: (-float(vals[i]), int(ids[i])))
+        vals, ids = vals[order].copy(), ids[order].copy()
+        top_k = int(g.choice([1, 5, 40, 64, 1000]))
+        top_p = float(g.choice([0.5, 0.9, 0.95, 1.0]))
+        temp = float(g.choice([0.3, 1.0, 1.7]))
+        greedy = trial % 11 == 0
+        opt = gen.resolve_generation_sampling_options(do_sample=not greedy, temperature=temp, top_p=top_p,
+                                                      top_k=top_k, seed=trial)
+        rng = gen.create_deterministic_rng(int(g.integers(0, 2 ** 32)))
+        for _ in range(trial % 3):
+            rng()
+        state = rng.state()
+        host = gen.sample_next_token([gen.Candidate(int(i), float(v)) for i, v in zip(ids, vals)], opt, rng)
+        hk.sample_candidates(torch.from_numpy(ids).cuda(), torch.from_numpy(vals).cuda(), top_k=opt.top_k,
+                             top_p=top_p, temperature=temp, greedy=greedy, rng_state=state, token_out=tok,
+                             table=table, scale=math.sqrt(64), row_out=row)
+        assert int(tok.item()) == host, f"trial {trial}"
+        want = (table[host].double() * math.sqrt(64)).float()
+        assert torch.equal(row, want), f"trial {trial}: row"
+
+
+@pytest.mark.gpu
+def test_mtp_device_sampling_equals_host_sampling(gpu_device):
+    """The drafts drawn on the device (one synchronization per round) give
+    the same generation as the host drawing each draft: same tokens, rounds
+    and accepted drafts from the same seed."""
+    from heliopause_b200.mtp import CudaMtpDraftHead, MtpGenerator
+    head = CudaMtpDraftHead(SMALL_D, SyntheticDraftWeights(SMALL_D, seed=5))
+    opt = gen.resolve_generation_sampling_options(do_sample=True, temperature=1.0, top_k=40, top_p=0.95, seed=99)
+    runs = []
+    for device in (False, True):
+        m, _ = _gpu_target()
+        try:
+            g = MtpGenerator(m, head)
+            rng = gen.create_deterministic_rng(opt.seed)
+            first, ctx = g.start(42, 19, opt, rng)
+            runs.append(g.generate(first, ctx, 24, 4, opt, rng, device_sampling=device))
+        finally:
+            m.close()
+    assert runs[0] == runs[1]
 
 
 @pytest.mark.gpu
