@@ -22,11 +22,11 @@ runner, runner/webgpu/mtp-assistant-runner.ts, computes the same in f32):
 The step runs in the library (hpc_draft_step, csrc/hc_draft.cu: one CUDA
 graph of its own kernels).  All matmuls are f32 products of dequantized
 weights with f32 inputs, as hp_matmul_dequantized_f32 (lib.rs:103-154) / the
-WebGPU F32 matmul do: each matrix is dequantized once by the library's
-bit-exact dequantization into f32 rows.  The norms, RoPE, attention softmax
-(f64 exp, f32 query) and GELU follow the reference's rounding points.
-Summation orders differ from the reference's sequential loops, so outputs
-agree to f32 rounding.
+WebGPU F32 matmul do: every weight element is dequantized bit-exactly from
+the head's resident quantized tiles and each output row is one sequential
+f32 chain in index order.  The norms, RoPE, attention softmax (f64 exp, f32
+query) and GELU follow the reference's rounding points; the norm and
+attention sums run in parallel orders, so those agree to f32 rounding.
 
 The loop (mtp_generate) restates generateAssistantWithMtp
 (packages/engine/src/chat.ts:692-776) with proposeMtpDraft
@@ -35,7 +35,10 @@ constant position, one batched verify of [pending, d1..dn] through
 CudaDecoderModel.forward, acceptance by generation.accept_mtp_draft, and the
 next context from the verify's hidden at the last committed position
 (finalizeMtpVerification; normalizedHiddenSlice,
-webgpu/mtp-target-runner.ts:225-244).
+webgpu/mtp-target-runner.ts:225-244).  By default each draft is drawn on the
+device (hpc_sample_candidates, the host sampler's steps and generator
+stream) and the verify reads the drafts where the sampler wrote them, so a
+round synchronizes with the host once, after the verify.
 """
 from __future__ import annotations
 

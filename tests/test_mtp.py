@@ -18,7 +18,10 @@ decoder C-ABI):
   * MtpGenerator greedy tokens equal plain greedy decoding on the same model
     (draft head drafts, all-right drafts, planted wrong drafts), and the
     oracle's speculative loop where no step is a near-tie;
-  * sampled generation (temperature 1, seeded uniforms) is deterministic.
+  * sampled generation (temperature 1, seeded uniforms) is deterministic;
+  * the device sampler draws the host sampler's token (300 candidate lists),
+    and generation with the drafts drawn on the device equals generation
+    with the host drawing them.
 """
 import math
 
