@@ -664,7 +664,42 @@ __host__ __device__ inline size_t gr_act_bytes(const GemvxParams& p) {
 }
 __host__ __device__ inline size_t gr_smem_bytes(const GemvxParams& p) {
   return size_t(GR_PARTS) * p.R * p.slot + gr_act_bytes(p) + size_t(GR_PARTS) * GX_PROD * sizeof(float) +
-         size_t(GR_PARTS) * (p.nb / GR_PARTS) * GX_PROD * sizeof(float);
+         size_t(GR_PARTS) * (p.nb / (GR_PARTS * p.C)) * GX_PROD * sizeof(float);
+}
+
+// The relay's hop from the last warp of one CTA to the first warp of the
+// next CTA of its cluster: that CTA's relay words are written through
+// distributed shared memory, then each lane arrives on the CTA's hop
+// barrier with release semantics at cluster scope.
+__device__ __forceinline__ void mbar_arrive_remote(uint64_t* bar, int rank) {
+  asm volatile(
+      "{ .reg .b32 ra; mapa.shared::cluster.u32 ra, %0, %1; "
+      "mbarrier.arrive.release.cluster.shared::cluster.b64 _, [ra]; }" ::"r"(smem_u32(bar)),
+      "r"(rank)
+      : "memory");
+}
+// Bounded wait whose completion also acquires what other CTAs of the
+// cluster released before arriving (same bound and status as mbar_wait_parity).
+__device__ __forceinline__ bool mbar_wait_parity_cluster(uint64_t* bar, uint32_t parity, int* err) {
+  unsigned long long t0 = 0;
+  for (int it = 0;; ++it) {
+    uint32_t ok;
+    asm volatile(
+        "{ .reg .pred p; mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3; "
+        "selp.u32 %0, 1, 0, p; }"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(SLEEP_HINT_NS)
+        : "memory");
+    if (ok) return true;
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    if (it == 0) {
+      t0 = t;
+    } else if (t - t0 > WAIT_LIMIT_NS) {
+      if (err) atomicExch(err, DEVICE_ERR_TIMEOUT);
+      return false;
+    }
+  }
 }
 constexpr int GR_MAX_SMEM = 220 * 1024;
 
@@ -676,8 +711,9 @@ __global__ void __launch_bounds__(GX_THREADS, 1) hc_gemvr_kernel(const __grid_co
   __shared__ __align__(8) uint64_t hop[GR_PARTS];
   const int lane = int(threadIdx.x) & 31, warp = int(threadIdx.x) >> 5;
   pdl_trigger();
-  const int R = p.R, nb = p.nb;
-  const int tile = int(blockIdx.x) / p.ncols, c = int(blockIdx.x) - tile * p.ncols;
+  const int R = p.R, nb = p.nb, C = p.C;
+  const int cid = int(blockIdx.x) / C, rank = int(blockIdx.x) - cid * C;  // a cluster of C CTAs per (tile, column)
+  const int tile = cid / p.ncols, c = cid - tile * p.ncols;
   const GemvSeg& sg = p.seg[gx_seg_of(p, tile)];
   const bool q4 = sg.type == TYPE_Q4_K;
   const uint32_t ub = uint32_t(unit_bytes(sg.type));
@@ -689,7 +725,7 @@ __global__ void __launch_bounds__(GX_THREADS, 1) hc_gemvr_kernel(const __grid_co
   float* relay = reinterpret_cast<float*>(act_a + gr_act_bytes(p));  // [8][9][32]
   float* prod = relay + GR_PARTS * GX_PROD + size_t(warp) * NBP * GX_PROD + lane;  // this warp's [NBP][9][32]
   uint64_t* wb = bars + warp * R;
-  const int b0 = warp * NBP;
+  const int b0 = (rank * GR_PARTS + warp) * NBP;
   if (lane == 0) {
     for (int s = 0; s < R; ++s) mbar_init(wb + s, 1);
     for (int k = 0; k < R && k < NBP; ++k) {
@@ -715,6 +751,9 @@ __global__ void __launch_bounds__(GX_THREADS, 1) hc_gemvr_kernel(const __grid_co
     if (p.planes & 2) bulk_copy_g2s(act_b, p.q.b + rec0 * Q8B_REC, uint32_t(nb * Q8B_REC), &act_bar);
   }
   __syncthreads();
+  // the hop barriers are initialized before another CTA of the cluster may
+  // arrive on them (waited for before the relay)
+  if (C > 1) asm volatile("barrier.cluster.arrive.release;" ::: "memory");
   bool ok = mbar_wait_parity(&act_bar, 0, p.err);
   const int ac = acols > 1 ? c : 0;  // this CTA's column among the staged records
   act_a += size_t(ac) * nb * Q8A_REC;
@@ -762,12 +801,15 @@ __global__ void __launch_bounds__(GX_THREADS, 1) hc_gemvr_kernel(const __grid_co
       rph ^= 1u;
     }
   }
-  // the relay: the accumulators after blocks 0 .. b0 - 1 come from warp - 1
+  if (C > 1) asm volatile("barrier.cluster.wait.acquire;" ::: "memory");
+  // the relay: the accumulators after blocks 0 .. b0 - 1 come from the
+  // previous warp (of this CTA, or the last warp of the previous rank)
   float acc[9];
 #pragma unroll
   for (int l = 0; l < 9; ++l) acc[l] = 0.0f;
-  if (warp > 0) {
-    if (ok && !mbar_wait_parity_sleep(&hop[warp], 0, p.err)) ok = false;
+  if (warp > 0 || rank > 0) {
+    if (ok && !(warp == 0 ? mbar_wait_parity_cluster(&hop[0], 0, p.err) : mbar_wait_parity_sleep(&hop[warp], 0, p.err)))
+      ok = false;
 #pragma unroll
     for (int l = 0; l < 9; ++l) acc[l] = relay[(warp * 9 + l) * 32 + lane];
   }
@@ -782,6 +824,11 @@ __global__ void __launch_bounds__(GX_THREADS, 1) hc_gemvr_kernel(const __grid_co
 #pragma unroll
     for (int l = 0; l < 9; ++l) relay[((warp + 1) * 9 + l) * 32 + lane] = acc[l];
     mbar_arrive(&hop[warp + 1]);  // each lane releases its own words
+  } else if (rank + 1 < C) {  // to the first warp of the next rank
+    float* dst = cg::this_cluster().map_shared_rank(relay, rank + 1);
+#pragma unroll
+    for (int l = 0; l < 9; ++l) dst[l * 32 + lane] = acc[l];
+    mbar_arrive_remote(&hop[0], rank + 1);
   } else if (ok) {
     float t = 0.0f;
 #pragma unroll
@@ -792,6 +839,11 @@ __global__ void __launch_bounds__(GX_THREADS, 1) hc_gemvr_kernel(const __grid_co
   }
   if (!ok)
     for (int v = 0; v < issued; ++v) mbar_wait_parity(wb + (v % R), uint32_t(v / R) & 1u, nullptr);
+  // no CTA leaves while another may still write its shared memory
+  if (C > 1) {
+    asm volatile("barrier.cluster.arrive.release;" ::: "memory");
+    asm volatile("barrier.cluster.wait.acquire;" ::: "memory");
+  }
 }
 
 }  // namespace
@@ -927,10 +979,12 @@ static int gemvt_plan(GemvxParams& p, int sms, bool any_size) {
 // Relay plan: rows of 16, 32 or 64 blocks, no prologue, every segment one
 // type; the deepest ring (at most the blocks per part) that fits.  Returns
 // the blocks per part (0: not this form).
-static int gemvr_plan(GemvxParams& p) {
+static int gemvr_plan(GemvxParams& p, int sms) {
   if (p.nb % GR_PARTS != 0) return 0;
   if (p.pro.mode != GEMV_PRO_NONE && p.K != GEMV_PRO_D) return 0;
-  const int nbp = p.nb / GR_PARTS;
+  // a CTA pair per (tile, column) when one CTA each would leave half the SMs idle
+  p.C = p.total_tiles * p.ncols * 2 <= sms && p.nb % (2 * GR_PARTS) == 0 && p.nb / (2 * GR_PARTS) >= 2 ? 2 : 1;
+  const int nbp = p.nb / (GR_PARTS * p.C);
   if (nbp != 1 && nbp != 2 && nbp != 4 && nbp != 8) return 0;
   p.slot = 0;
   p.planes = 0;
@@ -939,8 +993,7 @@ static int gemvr_plan(GemvxParams& p) {
     p.planes |= p.seg[i].type == TYPE_Q4_K ? 1 : 2;
   }
   if (p.pro.mode != GEMV_PRO_NONE) p.planes = 3;  // the prologue writes both planes
-  p.C = 1;
-  p.nbc = p.nb;
+  p.nbc = p.nb / p.C;
   for (p.R = min(GX_MAX_R, nbp); p.R >= 1; --p.R)
     if (gr_smem_bytes(p) <= size_t(GR_MAX_SMEM)) break;
   if (p.R < 1) return 0;
@@ -957,15 +1010,23 @@ static cudaError_t launch_r(const GemvxParams& p, cudaStream_t st) {
   });
   if (ea != cudaSuccess) return ea;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(unsigned(p.total_tiles * p.ncols));
+  cfg.gridDim = dim3(unsigned(p.total_tiles * p.ncols * p.C));
   cfg.blockDim = dim3(GX_THREADS);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
+  int na = 1;
+  if (p.C > 1) {
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = unsigned(p.C);
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    na = 2;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = na;
   return cudaLaunchKernelEx(&cfg, hc_gemvr_kernel<NBP>, p);
 }
 
@@ -1064,7 +1125,7 @@ cudaError_t launch_gemvx(GemvxParams& p, cudaStream_t st) {
   // the relay form serves rows of 16+ blocks (and, pinned, rows of 8)
   if (form == 0 || form == 'r') {
     GemvxParams r = p;
-    const int nbp = form == 'r' || p.nb > GW_MAX_NB ? gemvr_plan(r) : 0;
+    const int nbp = form == 'r' || p.nb > GW_MAX_NB ? gemvr_plan(r, sm_count()) : 0;
     if (nbp == 1) return launch_r<1>(r, st);
     if (nbp == 2) return launch_r<2>(r, st);
     if (nbp == 4) return launch_r<4>(r, st);

@@ -114,7 +114,9 @@ def _oracle_matmul(oracle, type_id, w, x, k, rows, cols):
     (syn.Q4_K, 2048, 40, 3),       # ragged tile
     (syn.Q4_K, 256, 7, 1),         # one block per row
     (syn.Q4_K, 768, 100, 13),      # 3 blocks, > 8 columns
-    (syn.Q6_K, 16384, 2048, 1),    # config 2 down projection (cluster split-K)
+    (syn.Q6_K, 16384, 2048, 1),    # config 2 down projection (relay over a CTA pair)
+    (syn.Q4_K, 16384, 2048, 1),
+    (syn.Q4_K, 8192, 1000, 2),     # 32 blocks: two per warp over the pair, ragged tile
     (syn.Q6_K, 16384, 2048, 8),
     (syn.Q6_K, 2048, 520, 2),
     (syn.Q6_K, 512, 33, 9),
