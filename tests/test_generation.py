@@ -59,6 +59,20 @@ def test_rng_first_draw_and_non_greedy_pick():
                                g.create_deterministic_rng(g.DEFAULT_SAMPLING_SEED)) == 11
 
 
+def test_rng_state_is_the_state_before_the_next_draw():
+    # the device sampler draws from rng.state() and the host copy then calls
+    # rng() once: a generator restarted from that state makes the same draw,
+    # and the stream continues identically
+    rng = g.create_deterministic_rng(g.DEFAULT_SAMPLING_SEED)
+    for _ in range(5):
+        rng()
+    s0 = rng.state()
+    assert 0 <= s0 < 2 ** 32
+    again = g.create_deterministic_rng(s0)
+    assert [rng() for _ in range(8)] == [again() for _ in range(8)]
+    assert rng.state() == again.state() == (s0 + 8 * 0x6D2B79F5) % 2 ** 32
+
+
 def test_top_p_keeps_boundary_token_and_greedy_returns_top1():
     # generation.test.ts:66-81
     cands = _c((10, 3), (11, 2), (12, 1))
