@@ -48,7 +48,7 @@ SIGNATURES = {
     "hpc_lm_head_topk_q8": (_i, [_vp, _vp, _sz, _sz, _sz, _sz, C.c_int32, _vp, _sz, C.c_float, _vp, _vp, _vp, _vp]),
     "hpc_topk_merge_keys": (_i, [_vp, _sz, _sz, _sz, C.c_float, _vp, _vp, _vp]),
     "hpc_sample_candidates": (_i, [_vp, _vp, _sz, _sz, C.c_double, C.c_double, _i, C.c_uint32, _vp, _vp, _sz,
-                                   C.c_double, _vp, _vp]),
+                                   _sz, C.c_double, _vp, _vp]),
     "hpc_model_create": (_i, [_vp, C.POINTER(_vp)]),
     "hpc_model_release": (_i, [_vp]),
     "hpc_model_set_weight": (_i, [_vp, _i, _i, _vp]),

@@ -16,9 +16,10 @@
 // The sums run in the reference's order; the exps are the device's f64 exp,
 // which may differ from the host library's in the last bit, so a draw within
 // ~1e-16 of a cumulative boundary could land on the neighbouring candidate.
-// The chosen token's row of an f32 table times `scale` (f64 product rounded
-// to f32) is written for the next draft step's input, so a chain of draft
-// steps and draws runs without the host.
+// The chosen token's row of an f32 table [table_rows][hidden] times `scale`
+// (f64 product rounded to f32) is written for the next draft step's input,
+// so a chain of draft steps and draws runs without the host; a token outside
+// the table (the empty id -1) leaves the row untouched.
 #include <cmath>
 
 #include "../../include/heliocuda.h"
@@ -43,8 +44,8 @@ __global__ void __launch_bounds__(SMP_MAX) hc_sample_kernel(const int32_t* __res
                                                          const float* __restrict__ vals, int n, int top_k,
                                                          double top_p, double temperature, int greedy,
                                                          uint32_t state, int32_t* __restrict__ out_token,
-                                                         const float* __restrict__ table, int hidden, double scale,
-                                                         float* __restrict__ row_out) {
+                                                         const float* __restrict__ table, int table_rows, int hidden,
+                                                         double scale, float* __restrict__ row_out) {
   __shared__ double e[SMP_MAX];
   __shared__ double s_mx;
   __shared__ int s_keep, s_token;
@@ -119,7 +120,7 @@ __global__ void __launch_bounds__(SMP_MAX) hc_sample_kernel(const int32_t* __res
   __syncthreads();
   const int tok = s_token;
   if (t == 0) *out_token = tok;
-  if (table != nullptr && tok >= 0)
+  if (table != nullptr && tok >= 0 && tok < table_rows)  // ids outside the table are not read
     for (int i = t; i < hidden; i += int(blockDim.x))
       row_out[i] = float(double(table[size_t(tok) * size_t(hidden) + size_t(i)]) * scale);
 }
@@ -131,15 +132,16 @@ extern "C" {
 
 int hpc_sample_candidates(const int32_t* d_ids, const float* d_vals, size_t n, size_t top_k, double top_p,
                           double temperature, int greedy, uint32_t rng_state, int32_t* d_token, const float* d_table,
-                          size_t hidden, double scale, float* d_row_out, void* stream) {
+                          size_t table_rows, size_t hidden, double scale, float* d_row_out, void* stream) {
   if (n < 1 || n > size_t(hc::SMP_MAX) || top_k < 1) return hpc_fail(HPC_ERR_SHAPE, "sample: %zu candidates", n);
   if (!greedy && !(temperature > 0.0)) return hpc_fail(HPC_ERR_ARG, "sample: temperature %g", temperature);
-  if (!d_ids || !d_vals || !d_token || (d_table && (!d_row_out || hidden == 0)))
+  if (!d_ids || !d_vals || !d_token || (d_table && (!d_row_out || hidden == 0 || table_rows == 0)))
     return hpc_fail(HPC_ERR_ARG, "null pointer");
+  if (table_rows > size_t(INT32_MAX) || hidden > size_t(INT32_MAX)) return hpc_fail(HPC_ERR_SHAPE, "sample: table");
   const int threads = greedy ? 256 : hc::SMP_MAX;
   hc::hc_sample_kernel<<<1, threads, 0, static_cast<cudaStream_t>(stream)>>>(
       d_ids, d_vals, int(n), int(top_k > n ? n : top_k), top_p, temperature, greedy, rng_state, d_token, d_table,
-      int(hidden), scale, d_row_out);
+      int(table_rows), int(hidden), scale, d_row_out);
   HPC_CK(cudaGetLastError(), "sample launch");
   return HPC_OK;
 }

@@ -319,11 +319,15 @@ def sample_candidates(ids: torch.Tensor, vals: torch.Tensor, *, top_k: int, top_
     if ids.dtype != torch.int32 or vals.dtype != torch.float32 or not ids.is_cuda or not vals.is_cuda:
         raise CudaKernelError(ERR_TYPE, "sample: candidates must be device int32 ids and f32 values")
     n = ids.numel()
-    hidden = table.shape[1] if table is not None else 0
+    rows, hidden = (table.shape[0], table.shape[1]) if table is not None else (0, 0)
+    if table is not None and (row_out is None or row_out.numel() < hidden or table.dtype != torch.float32
+                              or not table.is_contiguous()):
+        raise CudaKernelError(ERR_SHAPE, "sample: the table must be contiguous f32 and row_out hold a row")
     code = _lib.lib().hpc_sample_candidates(_ptr(ids), _ptr(vals), n, max(1, int(top_k)), float(top_p),
                                             float(temperature), 1 if greedy else 0, int(rng_state) & 0xFFFFFFFF,
-                                            _ptr(token_out), _ptr(table) if table is not None else None, hidden,
-                                            float(scale), _ptr(row_out) if row_out is not None else None, _stream())
+                                            _ptr(token_out), _ptr(table) if table is not None else None, rows,
+                                            hidden, float(scale), _ptr(row_out) if row_out is not None else None,
+                                            _stream())
     assert_cuda_ok(code, "sampleCandidates")
 
 

@@ -235,13 +235,14 @@ int hpc_topk_merge_keys(const uint64_t *d_keys, size_t group_count, size_t colum
  * nucleus, then draws from the softmax of value / temperature with the
  * generator advanced once from rng_state (the caller advances its own copy
  * of the stream by one draw); greedy != 0 takes the first candidate and
- * draws nothing.  Writes the token to *d_token and, when d_table != NULL,
- * d_table[token][0..hidden) * scale (f64 product rounded to f32) to
- * d_row_out, the next draft step's input embedding.  The exps are the
- * device's f64 exp. */
+ * draws nothing.  Writes the token to *d_token and, when d_table != NULL
+ * (f32 [table_rows][hidden]), d_table[token][0..hidden) * scale (f64 product
+ * rounded to f32) to d_row_out, the next draft step's input embedding; a
+ * token outside [0, table_rows) leaves d_row_out untouched.  The exps are
+ * the device's f64 exp. */
 int hpc_sample_candidates(const int32_t *d_ids, const float *d_vals, size_t n, size_t top_k, double top_p,
                           double temperature, int greedy, uint32_t rng_state, int32_t *d_token, const float *d_table,
-                          size_t hidden, double scale, float *d_row_out, void *stream);
+                          size_t table_rows, size_t hidden, double scale, float *d_row_out, void *stream);
 
 /* ---- LM head + top-k with no allocation inside the call --------------------
  * No reference counterpart: an addition for callers that may not allocate

@@ -363,6 +363,13 @@ def test_device_sampler_equals_host_sampler(gpu_device):
         assert int(tok.item()) == host, f"trial {trial}"
         want = (table[host].double() * math.sqrt(64)).float()
         assert torch.equal(row, want), f"trial {trial}: row"
+    # a token outside the table leaves the row as it was
+    small = table[:100].contiguous()
+    row.fill_(7.0)
+    hk.sample_candidates(torch.tensor([4321], dtype=torch.int32, device="cuda"),
+                         torch.tensor([1.0], dtype=torch.float32, device="cuda"), top_k=1, top_p=1.0,
+                         temperature=1.0, greedy=True, rng_state=0, token_out=tok, table=small, scale=1.0, row_out=row)
+    assert int(tok.item()) == 4321 and bool(torch.all(row == 7.0))
 
 
 @pytest.mark.gpu
