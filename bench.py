@@ -313,11 +313,13 @@ class DecodeConfig3:
 
     def kernel_launch_count(self) -> int:
         s = self.shape
-        # M = 1, hidden 2048: the attention and FFN norms run inside the QKV
-        # and gate/up GEMVs (hc_model.cu enqueue_step): QKV, attention (with
-        # QK-norm/RoPE/KV write), combine, O, gate/up, GEGLU, down
-        per_layer = 7
-        return 2 + s.layers * per_layer + 1 + 2  # rope table + embed ... final norm + LM head + merge
+        # M = 1, hidden 2048, the default reference-order step (hc_model.cu
+        # enqueue_step): the attention and FFN norms run inside the QKV and
+        # gate/up GEMVs; per layer QKV, attention scores (with QK-norm / RoPE /
+        # KV write), softmax, p.v, O, gate/up, GEGLU, down -- 285 launches at
+        # 35 layers, as the ncu launch list of one step counts them
+        per_layer = 8
+        return 2 + s.layers * per_layer + 1 + 2  # rope rows + embed ... final norm + LM head + merge
 
     def roofline(self, peak_gbs: float) -> dict:
         """Dominant kernel: the gate/up GEMV (39% of the step's bytes), timed
