@@ -26,7 +26,6 @@
 // Activations are read as plane-A/B Q8_K records straight from global
 // memory (every lane reads the same record words; they stay in L1/L2).
 #include <cooperative_groups.h>
-#include <cuda_fp16.h>
 
 #include <cstdlib>
 
@@ -36,6 +35,7 @@
 #include "hc_exact.cuh"
 #include "hc_gemv_body.cuh"
 #include "hc_kernels.cuh"
+#include "hc_mma.cuh"
 #include "hc_q8.cuh"
 
 namespace cg = cooperative_groups;
@@ -458,25 +458,6 @@ __global__ void __launch_bounds__(GX_THREADS, 1) hc_gemvw_kernel(const __grid_co
 // every column of the launch, so the weight-side work (unpacking, scaling)
 // is shared by all columns; lane (g = lane / 4, t = lane % 4) holds rows
 // g, g + 8 of the half and columns 2t, 2t + 1 (the m16n8 accumulator layout).
-__device__ __forceinline__ Q4KHeader q4k_header_hw(const uint4 h) {  // f16 by the hardware conversion (exact)
-  Q4KHeader r;
-  r.d = __half2float(__ushort_as_half(static_cast<unsigned short>(h.x & 0xffffu)));
-  r.dmin = __half2float(__ushort_as_half(static_cast<unsigned short>(h.x >> 16)));
-  r.sc_lo = h.y & 0x3f3f3f3fu;
-  r.mn_lo = h.z & 0x3f3f3f3fu;
-  r.sc_hi = (h.w & 0x0f0f0f0fu) | ((h.y >> 2) & 0x30303030u);
-  r.mn_hi = ((h.w >> 4) & 0x0f0f0f0fu) | ((h.z >> 2) & 0x30303030u);
-  return r;
-}
-
-__device__ __forceinline__ void mma_k32_gx(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                           uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
-      : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
-}
-
 __device__ __forceinline__ uint32_t u4_word(const uint4& v, int i) {
   return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
 }
@@ -608,8 +589,8 @@ __global__ void __launch_bounds__(GX_THREADS, 2) hc_gemvt_kernel(const __grid_co
           const uint32_t lo0 = w0 & 0x0f0f0f0fu, lo1 = w1 & 0x0f0f0f0fu;
           const uint32_t hi0 = (w0 >> 4) & 0x0f0f0f0fu, hi1 = (w1 >> 4) & 0x0f0f0f0fu;
           int d0[4], d1[4];
-          mma_k32_gx(d0, lo0 * s0a[0], lo1 * s0a[1], hi0 * s0b[0], hi1 * s0b[1], b0, b1);
-          mma_k32_gx(d1, lo0 * s1a[0], lo1 * s1a[1], hi0 * s1b[0], hi1 * s1b[1], b0, b1);
+          mma_k32(d0, lo0 * s0a[0], lo1 * s0a[1], hi0 * s0b[0], hi1 * s0b[1], b0, b1);
+          mma_k32(d1, lo0 * s1a[0], lo1 * s1a[1], hi0 * s1b[0], hi1 * s1b[1], b0, b1);
 #pragma unroll
           for (int r = 0; r < 4; ++r)  // r: (row r0 + 8 (r >> 1), column 2t + (r & 1)) = pair r
             ch[r].s[l] = __fadd_rn(ch[r].s[l], __fmul_rn(pd[r], float(d0[r] + 8 * d1[r])));
